@@ -1,0 +1,148 @@
+// devfns.cuh -- device functions shared by several kernels (header-inline so
+// every caller can inline them; libiq is built without relocatable code).
+#pragma once
+#include "layout.cuh"
+
+namespace iq {
+
+// Deterministic CTA-wide sum for 256 threads (fixed tree order).
+__device__ __forceinline__ float block_sum_256(float v) {
+  __shared__ float red[8];
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+  const int warp = threadIdx.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  float t = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; i++) t = __fadd_rn(t, red[i]);
+  return t;
+}
+
+// Element `e` of a device-layout row, decoded as candle's to_float does
+// (d*sc first, then *q, then -dmin*m: two roundings, never fused).
+__device__ __forceinline__ float dev_weight(int dt, const uint8_t* row, int nb, int e) {
+  switch (dt) {
+    case Q4_K:
+    case Q5_K: {
+      const int BB = dt == Q4_K ? 144 : 176;
+      const int b = e / 256, i = e % 256;
+      const uint8_t* blk = row + (int64_t)b * BB;
+      int sc[8], mn[8];
+      unpack_k_scales(blk + 4, sc, mn);
+      const int j = i / 64, w = i % 64, hi = w / 32, ii = w % 32;
+      const uint8_t* qs = blk + (dt == Q4_K ? 16 : 48);
+      int q = (qs[q4k_qs_perm(32 * j + ii)] >> (4 * hi)) & 15;
+      if (dt == Q5_K) q |= ((blk[16 + q5k_qh_perm(ii)] >> (2 * j + hi)) & 1) << 4;
+      const int s = 2 * j + hi;
+      const float d = h2f(*reinterpret_cast<const uint16_t*>(blk));
+      const float dmin = h2f(*reinterpret_cast<const uint16_t*>(blk + 2));
+      const float d1 = __fmul_rn(d, (float)sc[s]), m1 = __fmul_rn(dmin, (float)mn[s]);
+      return __fsub_rn(__fmul_rn(d1, (float)q), m1);
+    }
+    case Q6_K: {
+      const int b = e / 256, i = e % 256;
+      const uint8_t* blk = row + (int64_t)b * 208;
+      const int half = i / 128, l = i % 128;
+      const int qli = half * 64 + (l % 64), qhi = half * 32 + (l % 32);
+      int nib = (blk[q6k_ql_perm(qli)] >> (4 * (l / 64))) & 15;
+      int hb = (blk[128 + q6k_qh_perm(qhi)] >> (2 * (l / 32))) & 3;
+      const int q = (nib | (hb << 4)) - 32;
+      const float d = h2f(*reinterpret_cast<const uint16_t*>(row + (int64_t)nb * 208 + 2 * b));
+      const float sc = (float)reinterpret_cast<const int8_t*>(blk + 192)[i / 16];
+      return __fmul_rn(__fmul_rn(d, sc), (float)q);
+    }
+    case Q8_0: {
+      const int b = e / 32, i = e % 32;
+      const int8_t q = reinterpret_cast<const int8_t*>(row)[(int64_t)(b / 4) * 128 + q80_perm(b % 4, i)];
+      const float d = h2f(*reinterpret_cast<const uint16_t*>(row + (int64_t)nb * 32 + 2 * b));
+      return __fmul_rn((float)q, d);
+    }
+    case F32: return reinterpret_cast<const float*>(row)[e];
+    default: return __half2float(reinterpret_cast<const __half*>(row)[e]);
+  }
+}
+
+// ---------------------------------------------------------------- quantizers
+// One warp per Q8_K block.  Lane l = tig*8 + s holds elements
+// 32s + 16h + tig*4 + e (h, e in order), which is exactly the 8 contiguous
+// bytes it writes to the permuted layout.  Semantics: candle
+// BlockQ8K::from_float (first value of largest magnitude sets the scale).
+__device__ __forceinline__ void quant_q8k_block_warp(const float* x, uint8_t* act_row, int nb, int b, int lane) {
+  const int s = lane & 7, tig = lane >> 3;
+  float v[8];
+#pragma unroll
+  for (int h = 0; h < 2; h++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) v[h * 4 + e] = x[b * 256 + 32 * s + 16 * h + tig * 4 + e];
+  float amax = 0.f, vmax = 0.f;
+  int imax = 1 << 30;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const float a = fabsf(v[i]);
+    if (amax < a) { amax = a; vmax = v[i]; imax = 32 * s + 16 * (i / 4) + tig * 4 + (i % 4); }
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    float oa = __shfl_xor_sync(0xffffffffu, amax, m);
+    float ov = __shfl_xor_sync(0xffffffffu, vmax, m);
+    int oi = __shfl_xor_sync(0xffffffffu, imax, m);
+    if (oa > amax || (oa == amax && oi < imax)) { amax = oa; vmax = ov; imax = oi; }
+  }
+  int8_t q[8];
+  float d = 0.f;
+  if (amax != 0.f) {
+    const float iscale = __fdiv_rn(-128.f, vmax);
+#pragma unroll
+    for (int i = 0; i < 8; i++) q[i] = (int8_t)fminf(roundf(__fmul_rn(iscale, v[i])), 127.f);
+    d = __fdiv_rn(1.f, iscale);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; i++) q[i] = 0;
+  }
+  int sum[2] = {0, 0};
+#pragma unroll
+  for (int i = 0; i < 8; i++) sum[i / 4] += q[i];
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 8);
+    sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 16);
+  }
+  uint2 packed;
+  packed.x = (uint32_t)(uint8_t)q[0] | ((uint32_t)(uint8_t)q[1] << 8) | ((uint32_t)(uint8_t)q[2] << 16) |
+             ((uint32_t)(uint8_t)q[3] << 24);
+  packed.y = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) | ((uint32_t)(uint8_t)q[6] << 16) |
+             ((uint32_t)(uint8_t)q[7] << 24);
+  *reinterpret_cast<uint2*>(act_row + (int64_t)b * 256 + tig * 64 + s * 8) = packed;
+  int16_t* bs = reinterpret_cast<int16_t*>(act_row + (int64_t)nb * 260 + b * 32);
+  if (tig == 0) { bs[2 * s] = (int16_t)sum[0]; bs[2 * s + 1] = (int16_t)sum[1]; }
+  if (lane == 0) reinterpret_cast<float*>(act_row + (int64_t)nb * 256)[b] = d;
+}
+
+// One warp per group of four Q8_0 blocks.  Lane l = tig*8 + bb*2 + h holds
+// the 4 elements it writes at byte 4l of the group.  Semantics: candle
+// BlockQ8_0::from_float (d = amax/127 kept as f16; q from the f32 d).
+__device__ __forceinline__ void quant_q80_group_warp(const float* x, uint8_t* act_row, int nb, int g, int lane) {
+  const int tig = lane >> 3, bb = (lane & 7) >> 1, h = lane & 1;
+  const int base = 32 * (4 * g + bb) + 16 * h + tig * 4;
+  float v[4];
+#pragma unroll
+  for (int e = 0; e < 4; e++) v[e] = x[base + e];
+  float amax = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; e++) amax = fmaxf(amax, fabsf(v[e]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 8));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 16));
+  const float d = __fdiv_rn(amax, 127.f);
+  const float id = d != 0.f ? __fdiv_rn(1.f, d) : 0.f;
+  uint32_t packed = 0;
+#pragma unroll
+  for (int e = 0; e < 4; e++) packed |= (uint32_t)(uint8_t)(int8_t)roundf(__fmul_rn(v[e], id)) << (8 * e);
+  *reinterpret_cast<uint32_t*>(act_row + (int64_t)g * 128 + lane * 4) = packed;
+  if (tig == 0 && h == 0)
+    reinterpret_cast<float*>(act_row + (int64_t)nb * 32)[4 * g + bb] = __half2float(__float2half_rn(d));
+}
+
+}  // namespace iq

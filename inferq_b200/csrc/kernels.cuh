@@ -1,0 +1,32 @@
+// kernels.cuh -- declarations shared across the .cu files of libiq.
+#pragma once
+#include <algorithm>
+#include "iq_common.cuh"
+#include "qmv.cuh"
+
+namespace iq {
+
+struct PrepArgs {
+  const float* x;        // [rows][ldx]
+  int ldx;
+  int cols;
+  const float* norm_w;   // optional RMSNorm weight [cols]
+  float eps;
+  float inv_cols;
+  float* xn_out;         // optional normalized f32 rows
+  int ldxn;
+  uint8_t* q8k;          // optional Q8_K activation rows
+  uint8_t* q80;          // optional Q8_0 activation rows
+};
+
+
+cudaError_t gguf_to_device(int dt, const uint8_t* src, uint8_t* dst, int64_t rows, int cols, cudaStream_t st);
+cudaError_t dequant_rows(int dt, const uint8_t* w, int64_t row_bytes, int cols, const int32_t* ids,
+                         int64_t rows, float* out, cudaStream_t st);
+cudaError_t prep_rows(const PrepArgs& a, int rows, cudaStream_t st, bool pdl);
+
+// f32 matrix rows (router): y[i*ld + r] = dot(w[r], x[i]); fixed lane order.
+cudaError_t f32_matvec(const float* w, int rows, int cols, const float* x, int ldx, int k, float* y,
+                       int ldy, cudaStream_t st, bool pdl);
+
+}  // namespace iq

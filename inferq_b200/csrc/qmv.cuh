@@ -1,0 +1,64 @@
+// qmv.cuh -- skinny quantized matrix x multi-row product (k <= 8 input rows).
+//
+// Replaces the reference's fused multi-row kernels (src/qgemm.rs:175-397,
+// dispatched by QuantizedMatrix::forward / forward_rows, src/gguf.rs:406-456).
+//
+// One launch runs a table of jobs.  A job is one weight matrix (or a row
+// range of one) against up to eight quantized input rows.  A CTA of eight
+// warps owns (8 / ksplit) tiles of 16 weight rows; the ksplit warps of a tile
+// each take a contiguous chunk of the row's blocks.  Integer sub-block dot
+// products run on the tensor cores (int8 mma.sync, exact int32); each warp
+// then folds one f32 FMA per block into its chunk partial, and the chunk
+// partials are added left to right.  ksplit depends only on the matrix
+// shape, so an output row never depends on how many input rows ran with it.
+#pragma once
+#include "iq_common.cuh"
+
+namespace iq {
+
+enum QmvEpilogue : int {
+  kEpiStore = 0,     // out = y
+  kEpiResidual = 1,  // out = resid + y   (resid may alias out)
+};
+
+struct QmvJob {
+  const uint8_t* w;      // device-layout row 0
+  const uint8_t* act;    // quantized activation rows (Q8_K or Q8_0 layout)
+  float* out;
+  const float* resid;
+  int64_t w_row_bytes;
+  int act_row_bytes;
+  int out_ld;
+  int dtype, rows, cols, ksplit;
+  int n;                 // input rows used, 1..8
+  int tile0;             // first global tile of this job
+  int epi;
+  int8_t rowmap[8];      // activation row of input column i
+  int16_t outrow[8];     // output row (of out) of input column i
+};
+
+// Rows one CTA covers for a job.
+__host__ __device__ inline int qmv_rows_per_cta(int ksplit) { return 16 * (8 / ksplit); }
+__host__ __device__ inline int qmv_units(int dt, int cols) {
+  return dt == Q8_0 ? cols / 128 : cols / 256;
+}
+
+// The chunk count of a matrix: a function of its shape only.
+inline int qmv_ksplit(int dt, int64_t rows, int64_t cols) {
+  int units = qmv_units(dt, (int)cols);
+  int ks = 1;
+  while (ks < 8 && units % (ks * 2) == 0 && (rows / 16) * ks < 148 * 32) ks *= 2;
+  return ks;
+}
+inline int qmv_tiles(const QmvJob& j) {
+  return (int)ceil_div(j.rows, qmv_rows_per_cta(j.ksplit));
+}
+
+// Launch `ntiles` CTAs over `jobs` (device memory, sorted by tile0).
+// When `dyn_count` is non-null the job count is read on the device after the
+// programmatic-dependency wait (jobs written by the previous kernel), and
+// CTAs past the last job's tiles exit.
+cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int ntiles,
+                       cudaStream_t stream, bool pdl);
+
+}  // namespace iq

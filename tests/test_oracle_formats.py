@@ -1,0 +1,68 @@
+"""The CPU oracle against golden vectors (gguf-py) and the reference's own
+known-answer semantics for block decode and activation quantization."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+from inferq_b200 import quants as Q
+
+G = np.load(Path(__file__).parent / "golden" / "formats.npz")
+
+
+@pytest.mark.parametrize("dt", [Q.Q4_K, Q.Q5_K, Q.Q6_K, Q.Q8_0])
+def test_block_decode_is_bit_exact_against_gguf_py(dt):
+    name = Q.NAMES[dt]
+    blocks, ref = G[f"{name}_bytes"], G[f"{name}_f32"]
+    got = oracle.dequant(dt, blocks, *ref.shape)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_q8_0_activation_quantization_matches_gguf_py():
+    got = oracle.quant_q80(G["act_f32"])
+    assert np.array_equal(got, G["act_q8_0"].ravel())
+
+
+def test_q8k_quantization_follows_candle_from_float():
+    # iscale = -128/max of the largest-magnitude value; that value maps to -128.
+    x = np.linspace(-1.0, 0.5, 256, dtype=np.float32)
+    blk = oracle.quant_q8k(x)
+    d = blk[:4].view(np.float32)[0]
+    qs = blk[4:260].view(np.int8)
+    bs = blk[260:292].view(np.int16)
+    assert qs[0] == -128 * np.sign(x[0]) * -1 or qs[0] == -128
+    assert d == np.float32(1.0) / (np.float32(-128.0) / np.float32(-1.0))
+    assert np.array_equal(bs, qs.astype(np.int32).reshape(16, 16).sum(1).astype(np.int16))
+    # first occurrence wins on equal magnitude: +1 before -1 gives d < 0
+    y = np.zeros(256, np.float32)
+    y[3], y[9] = 1.0, -1.0
+    blk = oracle.quant_q8k(y)
+    assert blk[:4].view(np.float32)[0] < 0 and blk[4 + 3].view(np.int8) == -128
+    assert blk[4 + 9].view(np.int8) == 127  # +128 capped at 127
+    # an all-zero block
+    z = oracle.quant_q8k(np.zeros(256, np.float32))
+    assert not z.any()
+
+
+@pytest.mark.parametrize("dt,cols", [(Q.Q4_K, 512), (Q.Q5_K, 512), (Q.Q6_K, 768), (Q.Q8_0, 256)])
+def test_reference_and_device_orders_agree_to_f32_rounding(dt, cols):
+    import torch
+    torch.manual_seed(dt)
+    w = Q.encode(torch.randn(24, cols) * 0.02, dt).numpy()
+    x = np.random.default_rng(dt).standard_normal((3, cols)).astype(np.float32)
+    a = oracle.qmatvec(dt, w, 24, cols, x, order=0)
+    b = oracle.qmatvec(dt, w, 24, cols, x, order=1, ksplit=2 if dt != Q.Q8_0 else 1)
+    deq = oracle.dequant(dt, w, 24, cols)
+    exact = x.astype(np.float64) @ deq.astype(np.float64).T
+    scale = np.abs(x).max() * np.abs(deq).sum(1).max()
+    assert np.abs(a - b).max() <= 1e-5 * scale
+    # the reference's own tolerance vs f32 matmul of the dequantized matrix
+    # (src/gguf.rs:1741-1775 direct_matrix_matches_its_dequantized_reference)
+    assert np.abs(a - exact).max() < 2e-2
+
+
+def test_argmax_takes_the_last_max_and_skips_non_finite():
+    assert oracle.argmax(np.array([1, 3, 3, 2], np.float32)) == 2
+    assert oracle.argmax(np.array([np.nan, 1, np.inf, -np.inf], np.float32)) == 1
+    assert oracle.argmax(np.array([np.nan], np.float32)) == -1
