@@ -87,6 +87,108 @@ int iq_qgemv_ksplit(int dtype, int64_t rows, int64_t cols);
  * (src/gguf.rs:288-290). */
 int iq_matrix_dequantize(const iq_matrix* m, const int32_t* ids, int64_t n, float* out);
 
+
+/* ------------------------------------------------------------------ */
+/* Model level: the verify pass, greedy accept and rollback            */
+/* (QuantizedModel / QuantizedModelState, src/qwen/quantized_model.rs). */
+/* ------------------------------------------------------------------ */
+
+/* The fields of Qwen3NextConfig (src/config.rs:40-93) the pass reads. */
+typedef struct iq_config {
+  int32_t hidden_size;
+  int32_t num_hidden_layers;
+  int32_t vocab_size;
+  int32_t num_attention_heads;
+  int32_t num_key_value_heads;
+  int32_t head_dim;
+  int32_t rotary_dim;               /* head_dim * partial_rotary_factor (config.rs:253-255) */
+  int32_t linear_num_key_heads;
+  int32_t linear_num_value_heads;
+  int32_t linear_key_head_dim;
+  int32_t linear_value_head_dim;
+  int32_t linear_conv_kernel_dim;
+  int32_t num_experts;
+  int32_t num_experts_per_tok;
+  int32_t moe_intermediate_size;
+  int32_t shared_expert_intermediate_size;
+  int32_t full_attention_interval;  /* layer l is full attention iff (l+1) % interval == 0 */
+  int32_t mtp_num_hidden_layers;    /* 0 or 1 */
+  int32_t norm_topk_prob;
+  int32_t value_heads_tiled;        /* 1 for model_type qwen3_5_moe_text (TiledByRepeat) */
+  int32_t max_position_embeddings;
+  float rms_norm_eps;
+  double rope_theta;
+} iq_config;
+
+/* One GGUF tensor: its GGUF name (e.g. "blk.3.attn_qkv.weight"), dtype,
+ * row-major shape (outermost first, as candle reports it) and bytes. */
+typedef struct iq_tensor_view {
+  const char* name;
+  int32_t dtype;
+  int32_t ndim;
+  int64_t shape[4];
+  const void* data;
+  int32_t location; /* IQ_HOST or IQ_DEVICE */
+} iq_tensor_view;
+
+typedef struct iq_model iq_model;
+typedef struct iq_state iq_state;
+
+/* Upload every tensor the pass needs to the current device (all experts
+ * resident in HBM).  Replaces QuantizedModel::load (quantized_model.rs:511-564)
+ * with the expert cache of src/residency.rs made fully resident.  Tensor
+ * names and shape checks follow the reference's loaders; a missing or
+ * misshapen tensor fails with its name in iq_last_error(). */
+int iq_model_create(const iq_tensor_view* tensors, int n, const iq_config* cfg, iq_model** out);
+/* Expert-parallel variant: this rank keeps experts
+ * [rank*E/world, (rank+1)*E/world); dense, DeltaNet and attention weights
+ * are replicated.  `nccl_comm` is an ncclComm_t of `world` ranks (one per
+ * GPU) used to all-gather expert outputs after every MoE layer. */
+int iq_model_create_ep(const iq_tensor_view* tensors, int n, const iq_config* cfg, int rank, int world,
+                       void* nccl_comm, iq_model** out);
+void iq_model_destroy(iq_model* m);
+int iq_model_weight_bytes(const iq_model* m, int64_t* bytes);
+
+/* Decode state: per-layer KV cache (f32 [pos][kv_head][head_dim]) and
+ * DeltaNet conv/recurrent state, double-buffered for rollback. */
+int iq_state_create(iq_model* m, int64_t max_positions, iq_state** out);
+void iq_state_destroy(iq_state* s);
+int iq_state_reset(iq_state* s);
+int iq_state_position(const iq_state* s, int64_t* position);
+/* The cudaStream_t every pass of this state is enqueued on. */
+int iq_state_stream(const iq_state* s, void** stream);
+
+/* Evaluate `rows` tokens at the state's position and commit all of them
+ * (QuantizedModel::forward_detailed, quantized_model.rs:599-621; prefill
+ * splits into passes of at most 8 rows).  Outputs are host buffers or NULL:
+ * logits [rows][vocab], normalized hidden [rows][hidden], argmax [rows]
+ * (ties to the last index, sampling.rs:104-112).  The pre-pass state of the
+ * last pass is kept, so iq_rollback may follow. */
+int iq_forward(iq_state* s, const uint32_t* tokens, int rows, float* logits, float* hidden, int32_t* argmax);
+
+typedef struct iq_verify_result {
+  int32_t accepted;       /* drafts accepted (accepted_draft_prefix, runtime.rs:2225) */
+  int32_t authoritative;  /* argmax of row `accepted` */
+  int32_t committed;      /* rows kept: accepted + 1 */
+} iq_verify_result;
+
+/* One speculative verification pass: tokens = [seed, draft_1..draft_{rows-1}],
+ * rows <= 8.  Runs the rows (verify_rows, runtime.rs:2102-2114), takes the
+ * greedy argmax of every row on the device, accepts the longest matching
+ * draft prefix, rolls the DeltaNet state back to the committed boundary and
+ * truncates the KV cache (QuantizedModelState::rollback,
+ * quantized_model.rs:177-204) -- all before the single host synchronization.
+ * logits [rows][vocab] / hidden [rows][hidden] are optional host outputs. */
+int iq_verify(iq_state* s, const uint32_t* tokens, int rows, iq_verify_result* out, float* logits, float* hidden);
+
+/* Roll the last iq_forward pass back to its first `committed_rows` rows
+ * (QuantizedModelState::rollback).  committed_rows < rows of that pass. */
+int iq_rollback(iq_state* s, int committed_rows);
+
+/* Distinct experts each MoE layer ran in the last pass (one int per layer);
+ * the measured expert union that sets the pass's algorithmic bytes. */
+int iq_state_union_sizes(const iq_state* s, int32_t* per_layer);
+
 #ifdef __cplusplus
 }
 #endif

@@ -10,6 +10,10 @@ struct iq_matrix {
   int64_t rows, cols, row_bytes;
   std::shared_ptr<iq::DevBuf> storage;
   const uint8_t* base;
+  // Device copy of the last job table this matrix launched, reused while the
+  // call's buffers and row count stay the same.
+  std::shared_ptr<iq::DevBuf> job_cache = std::make_shared<iq::DevBuf>();
+  iq::QmvJob last_job = {};
 };
 
 namespace iq {
@@ -83,7 +87,6 @@ int matrix_forward_dev(const iq_matrix* m, const float* x, int k, float* y, cuda
   const bool kq = m->dtype != Q8_0;
   const int64_t arb = kq ? act_row_bytes_q8k(m->cols) : act_row_bytes_q80(m->cols);
   IQ_CUDA(g_scratch.act.reserve((size_t)(arb * 8)));
-  IQ_CUDA(g_scratch.jobs.reserve(sizeof(QmvJob)));
   PrepArgs pa = {};
   pa.x = x;
   pa.ldx = (int)m->cols;
@@ -92,7 +95,8 @@ int matrix_forward_dev(const iq_matrix* m, const float* x, int k, float* y, cuda
   if (kq) pa.q8k = g_scratch.act.as<uint8_t>();
   else pa.q80 = g_scratch.act.as<uint8_t>();
   IQ_CUDA(prep_rows(pa, k, st, false));
-  QmvJob j = {};
+  QmvJob j;
+  memset(&j, 0, sizeof j);
   j.w = m->base;
   j.act = g_scratch.act.as<uint8_t>();
   j.out = y;
@@ -106,9 +110,14 @@ int matrix_forward_dev(const iq_matrix* m, const float* x, int k, float* y, cuda
   j.n = k;
   j.tile0 = 0;
   j.epi = kEpiStore;
-  for (int i = 0; i < 8; i++) { j.rowmap[i] = (int8_t)(i < k ? i : 0); j.outrow[i] = (int16_t)i; }
-  IQ_CUDA(cudaMemcpyAsync(g_scratch.jobs.p, &j, sizeof j, cudaMemcpyHostToDevice, st));
-  IQ_CUDA(qmv_launch(g_scratch.jobs.as<QmvJob>(), 1, nullptr, qmv_tiles(j), st, false));
+  for (int i = 0; i < 8; i++) { j.rowmap[i] = (uint8_t)(i < k ? i : 0); j.outrow[i] = (int16_t)i; }
+  iq_matrix* mm = const_cast<iq_matrix*>(m);
+  if (!mm->job_cache->p || memcmp(&mm->last_job, &j, sizeof j) != 0) {
+    IQ_CUDA(mm->job_cache->reserve(sizeof(QmvJob)));
+    IQ_CUDA(cudaMemcpyAsync(mm->job_cache->p, &j, sizeof j, cudaMemcpyHostToDevice, st));
+    mm->last_job = j;
+  }
+  IQ_CUDA(qmv_launch(mm->job_cache->as<QmvJob>(), 1, nullptr, qmv_tiles(j), (int)(arb * k), st, false));
   return IQ_OK;
 }
 
@@ -148,6 +157,8 @@ int iq_matrix_leading_rows(const iq_matrix* m, int64_t rows, iq_matrix** out) {
            (long long)rows, (long long)m->rows);
   auto* r = new iq_matrix(*m);
   r->rows = rows;
+  r->job_cache = std::make_shared<DevBuf>();
+  r->last_job = {};
   *out = r;
   return IQ_OK;
 }

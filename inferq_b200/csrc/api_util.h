@@ -36,6 +36,15 @@ struct DevBuf {
   DevBuf() = default;
   DevBuf(const DevBuf&) = delete;
   DevBuf& operator=(const DevBuf&) = delete;
+  DevBuf(DevBuf&& o) noexcept : p(o.p), bytes(o.bytes) { o.p = nullptr; o.bytes = 0; }
+  DevBuf& operator=(DevBuf&& o) noexcept {
+    if (this != &o) {
+      release();
+      p = o.p; bytes = o.bytes;
+      o.p = nullptr; o.bytes = 0;
+    }
+    return *this;
+  }
   ~DevBuf() { release(); }
   void release() {
     if (p) cudaFree(p);

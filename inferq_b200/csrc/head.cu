@@ -1,0 +1,168 @@
+// head.cu -- token embedding, greedy argmax over the LM-head logits, the
+// on-device speculative accept, and the end-of-pass commit.
+//
+// argmax restates src/sampling.rs:104-112: non-finite logits are skipped and
+// ties resolve to the LAST maximal index (Iterator::max_by).  The accept
+// restates src/runtime.rs:2225-2236 (accepted_draft_prefix) and :1753-1755:
+// the longest prefix of drafts equal to the argmax of the row before them,
+// then the authoritative token = argmax of row `accepted`.
+// The MTP confidence of row 0 restates top1_with_scores (:2245-2265): the
+// top-1/top-2 logit margin and p(top1) = 1 / sum(exp(l - peak)).
+#include "model_kernels.cuh"
+#include "devfns.cuh"
+
+namespace iq {
+namespace {
+
+__global__ void __launch_bounds__(256) embed_kernel(int dt, const uint8_t* __restrict__ w, int64_t row_bytes,
+                                                    int cols, const int32_t* __restrict__ tokens, float* out,
+                                                    int out_ld) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  const uint8_t* row = w + (int64_t)tokens[t] * row_bytes;
+  const int nb = cols / gguf_block_elems(dt);
+  for (int e = threadIdx.x; e < cols; e += blockDim.x) out[(int64_t)t * out_ld + e] = dev_weight(dt, row, nb, e);
+}
+
+struct Best {
+  float v;    // best value (-inf when nothing finite)
+  int i;      // its index (-1 when none)
+  float v2;   // best value at any other index
+  float se;   // sum over finite values of exp(l - v)
+};
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+  return v > bv || (v == bv && i > bi);
+}
+
+__device__ __forceinline__ Best merge(Best a, Best b, bool scores) {
+  Best r;
+  if (b.i >= 0 && (a.i < 0 || better(b.v, b.i, a.v, a.i))) {
+    r.v = b.v; r.i = b.i;
+    r.v2 = fmaxf(b.v2, a.v);
+  } else {
+    r.v = a.v; r.i = a.i;
+    r.v2 = fmaxf(a.v2, b.i >= 0 ? b.v : -INFINITY);
+  }
+  if (scores) {
+    const float ea = a.i >= 0 ? __fmul_rn(a.se, expf(a.v - r.v)) : 0.f;
+    const float eb = b.i >= 0 ? __fmul_rn(b.se, expf(b.v - r.v)) : 0.f;
+    r.se = __fadd_rn(ea, eb);
+  } else {
+    r.se = 0.f;
+  }
+  return r;
+}
+
+__device__ Best block_best(Best b, bool scores) {
+  __shared__ Best red[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    Best x;
+    x.v = __shfl_xor_sync(0xffffffffu, b.v, o);
+    x.i = __shfl_xor_sync(0xffffffffu, b.i, o);
+    x.v2 = __shfl_xor_sync(0xffffffffu, b.v2, o);
+    x.se = __shfl_xor_sync(0xffffffffu, b.se, o);
+    b = (lane & o) ? merge(x, b, scores) : merge(b, x, scores);
+  }
+  __syncthreads();
+  if (lane == 0) red[warp] = b;
+  __syncthreads();
+  Best r = red[0];
+  for (int w = 1; w < 8; w++) r = merge(r, red[w], scores);
+  return r;
+}
+
+// grid (rows, nparts): each CTA reduces a contiguous slice of one row.
+__global__ void __launch_bounds__(256) argmax_part_kernel(HeadArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x, part = blockIdx.y;
+  const bool scores = a.scores != nullptr && t == 0;
+  const int64_t per = (a.vocab + a.nparts - 1) / a.nparts;
+  const int64_t lo = part * per, hi = lo + per < a.vocab ? lo + per : (int64_t)a.vocab;
+  const float* l = a.logits + (int64_t)t * a.logits_ld;
+  Best b = {-INFINITY, -1, -INFINITY, 0.f};
+  for (int64_t i = lo + threadIdx.x; i < hi; i += 256) {
+    const float v = l[i];
+    if (!isfinite(v)) continue;
+    Best x = {v, (int)i, -INFINITY, 1.f};
+    b = merge(b, x, scores);
+  }
+  b = block_best(b, scores);
+  if (threadIdx.x == 0) {
+    a.part_val[(t * a.nparts + part) * 3 + 0] = b.v;
+    a.part_val[(t * a.nparts + part) * 3 + 1] = b.v2;
+    a.part_val[(t * a.nparts + part) * 3 + 2] = b.se;
+    a.part_idx[t * a.nparts + part] = b.i;
+  }
+}
+
+// One CTA: final argmax per row, then accept and the authoritative token.
+__global__ void __launch_bounds__(256) accept_kernel(HeadArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int am[8];
+  for (int t = 0; t < a.rows; t++) {
+    const bool scores = a.scores != nullptr && t == 0;
+    Best b = {-INFINITY, -1, -INFINITY, 0.f};
+    for (int p = threadIdx.x; p < a.nparts; p += 256) {
+      Best x;
+      x.v = a.part_val[(t * a.nparts + p) * 3 + 0];
+      x.v2 = a.part_val[(t * a.nparts + p) * 3 + 1];
+      x.se = a.part_val[(t * a.nparts + p) * 3 + 2];
+      x.i = a.part_idx[t * a.nparts + p];
+      b = merge(b, x, scores);
+    }
+    b = block_best(b, scores);
+    if (threadIdx.x == 0) {
+      am[t] = b.i;
+      a.argmax[t] = b.i;
+      if (scores) {
+        a.scores[0] = b.v - b.v2;
+        a.scores[1] = __fdiv_rn(1.f, b.se);
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    int accepted = 0;
+    if (a.verify)
+      while (accepted + 1 < a.rows && am[accepted] == a.tokens[accepted + 1]) accepted++;
+    const int last = a.verify ? accepted : a.rows - 1;
+    a.result[0] = accepted;
+    a.result[1] = am[last];
+    a.result[2] = a.verify ? accepted + 1 : a.rows;
+  }
+}
+
+__global__ void commit_kernel(int* sel, int* pos, const int* result) {
+  pdl_wait();
+  pdl_trigger();
+  *sel ^= 1;
+  *pos += result[2];
+}
+
+}  // namespace
+
+cudaError_t embed_launch(int dt, const uint8_t* w, int64_t row_bytes, int cols, const int32_t* tokens, int rows,
+                         float* out, int out_ld, cudaStream_t st, bool pdl) {
+  return launch_pdl(embed_kernel, dim3(rows), dim3(256), 0, st, pdl, dt, w, row_bytes, cols, tokens, out, out_ld);
+}
+
+cudaError_t argmax_launch(const HeadArgs& a, cudaStream_t st, bool pdl) {
+  return launch_pdl(argmax_part_kernel, dim3(a.rows, a.nparts), dim3(256), 0, st, pdl, a);
+}
+
+cudaError_t accept_launch(const HeadArgs& a, cudaStream_t st, bool pdl) {
+  if (a.rows > 8) return cudaErrorInvalidValue;
+  return launch_pdl(accept_kernel, dim3(1), dim3(256), 0, st, pdl, a);
+}
+
+cudaError_t commit_launch(int* sel, int* pos, const int* result, cudaStream_t st, bool pdl) {
+  return launch_pdl(commit_kernel, dim3(1), dim3(1), 0, st, pdl, sel, pos, result);
+}
+
+}  // namespace iq

@@ -17,6 +17,8 @@ struct PrepArgs {
   int ldxn;
   uint8_t* q8k;          // optional Q8_K activation rows
   uint8_t* q80;          // optional Q8_0 activation rows
+  int q8k_stride;        // row strides in bytes (0: packed for `cols`)
+  int q80_stride;
 };
 
 

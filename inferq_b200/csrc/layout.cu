@@ -98,12 +98,12 @@ __global__ void __launch_bounds__(256) prep_rows_kernel(PrepArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (a.q8k) {
     const int nb = cols / 256;
-    uint8_t* ar = a.q8k + (int64_t)row * act_row_bytes_q8k(cols);
+    uint8_t* ar = a.q8k + (int64_t)row * (a.q8k_stride ? a.q8k_stride : act_row_bytes_q8k(cols));
     for (int b = warp; b < nb; b += 8) quant_q8k_block_warp(xs, ar, nb, b, lane);
   }
   if (a.q80) {
     const int nb = cols / 32;
-    uint8_t* ar = a.q80 + (int64_t)row * act_row_bytes_q80(cols);
+    uint8_t* ar = a.q80 + (int64_t)row * (a.q80_stride ? a.q80_stride : act_row_bytes_q80(cols));
     for (int g = warp; g < nb / 4; g += 8) quant_q80_group_warp(xs, ar, nb, g, lane);
   }
 }

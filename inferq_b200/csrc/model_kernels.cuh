@@ -1,0 +1,171 @@
+// model_kernels.cuh -- argument blocks and launchers of the layer kernels.
+#pragma once
+#include "kernels.cuh"
+
+namespace iq {
+
+// ----------------------------------------------------------------- DeltaNet
+struct DeltaNetLayer {
+  float* conv_state[2];   // [conv_dim][K-1], double-buffered by `sel`
+  float* rec_state[2];    // [nv][dk][dv]
+  const float* conv_w;    // [conv_dim][K]
+  const float* ssm_a;     // [nv]  (already -exp(A_log))
+  const float* dt_bias;   // [nv]
+};
+
+struct DeltaNetArgs {
+  const DeltaNetLayer* layers;  // device array, gridDim.y entries
+  const float* qkv;             // projections [rows][qkv_ld] (first conv_dim cols)
+  int qkv_ld;
+  const float* ba;              // beta/alpha projections [rows][ba_ld]
+  int ba_ld;
+  float* out;                   // recurrent outputs [rows][out_ld]
+  int out_ld;
+  int rows;
+  int nk, nv, dk, dv, conv_k;
+  int tiled_heads;              // value head layout: 1 TiledByRepeat, 0 GroupedByKeyHead
+  int ba_interleaved;           // 1: ssm_ba per key head, 0: beta rows then alpha rows
+  const int* sel;               // device: which state buffer is current
+  const int* committed;         // device: rows to replay (replay mode)
+  int replay;
+};
+cudaError_t deltanet_launch(const DeltaNetArgs& a, int nlayers, cudaStream_t st, bool pdl);
+
+struct GatedNormArgs {
+  const float* o;  int o_ld;
+  const float* z;  int z_ld;
+  const float* w;  // [dv]
+  int heads, dv;
+  float eps, inv_dv;
+  uint8_t* q8k;
+  uint8_t* q80;
+  int q8k_stride, q80_stride;  // activation row strides in bytes
+};
+cudaError_t gated_norm_launch(const GatedNormArgs& a, int rows, cudaStream_t st, bool pdl);
+
+// ---------------------------------------------------------------- attention
+struct AttnArgs {
+  const float* qg;  int qg_ld;   // [rows][nh][2*hd] (q then gate per head)
+  const float* kp;  int kp_ld;   // [rows][nkv*hd]
+  const float* vp;  int vp_ld;
+  const float* q_norm;           // [hd]
+  const float* k_norm;           // [hd]
+  float* kcache;                 // [max_pos][nkv][hd]
+  float* vcache;
+  float* qbuf;                   // [rows][nh][hd]  normalized + roped queries
+  float* part;                   // split-K partials
+  float* out;  int out_ld;       // [rows][nh*hd]
+  int rows, nh, nkv, hd, rotary_dim;
+  double theta;
+  float eps;
+  const int* pos;                // device: position of row 0
+  int chunk_ctas;                // CTAs per (kv head, query group) walking the chunks
+};
+// Positions per split of the scan.  Chunk c always covers absolute positions
+// [c*kAttnChunk, (c+1)*kAttnChunk), and a row combines its chunks in order, so
+// a row's output depends only on its own context, never on the pass it ran in.
+constexpr int kAttnChunk = 64;
+cudaError_t attn_prep_launch(const AttnArgs& a, cudaStream_t st, bool pdl);
+cudaError_t attn_scan_launch(const AttnArgs& a, cudaStream_t st, bool pdl);
+cudaError_t attn_combine_launch(const AttnArgs& a, cudaStream_t st, bool pdl);
+
+// ---------------------------------------------------------------------- MoE
+// Per-layer constants of the routed and shared experts (device layout).
+struct MoeRouteStatic {
+  const uint8_t* gate; const uint8_t* up; const uint8_t* down;  // expert-stacked, resident experts only
+  int64_t gate_stride, up_stride, down_stride;                 // bytes per expert
+  int64_t gate_row_bytes, down_row_bytes;
+  int gate_dt, down_dt;
+  int ks_gate, ks_down, tiles_gate, tiles_down;
+  const uint8_t* sh_gate; const uint8_t* sh_up; const uint8_t* sh_down;
+  int64_t sh_gate_row_bytes, sh_down_row_bytes;
+  int sh_gate_dt, sh_down_dt;
+  int ks_sh_gate, ks_sh_down, tiles_sh_gate;
+  int with_shared;
+  int expert_lo, expert_hi;  // experts resident on this rank: [lo, hi)
+};
+
+struct MoeRouteArgs {
+  const float* logits;  int logits_ld;  // [rows][E (+1 shared selector)]
+  int rows, experts, topk, norm_topk;
+  int hidden, ffn, sh_ffn;
+  // outputs
+  int* route_expert;     // [rows][topk]
+  float* route_weight;   // [rows][topk]
+  QmvJob* gu_jobs;       // gate/up job table
+  int* gu_count;
+  QmvJob* down_jobs;
+  int* down_count;
+  int* union_size;       // number of distinct experts (stat)
+  int* union_list;       // [experts] distinct experts, ascending
+  // buffers the jobs point at
+  const uint8_t* act_in8k; int act_in8k_bytes;  // normalized hidden rows, Q8_K layout
+  const uint8_t* act_in80; int act_in80_bytes;  // the same rows, Q8_0 layout
+  float* gu_out;                               // [slot][2*ffn_max]
+  int gu_ld;
+  const uint8_t* act_mid; int act_mid_bytes;   // silu(g)*u rows per slot, in the down matrix's layout
+  float* y;  int y_ld;                         // [slot][hidden]
+};
+cudaError_t moe_route_launch(const MoeRouteArgs& a, const MoeRouteStatic& s, cudaStream_t st, bool pdl);
+
+struct MoeActArgs {
+  const float* gu; int gu_ld;  // [slot][gate ffn | up ffn]
+  int ffn, sh_ffn;
+  int rows, topk;
+  const int* route_expert;     // slots whose expert is not resident are skipped
+  int expert_lo, expert_hi;
+  uint8_t* act; int act_bytes;  // rows per slot
+  int down_q80, sh_down_q80;    // 1: quantize to Q8_0 (Q8_0 down matrix), else Q8_K
+};
+cudaError_t moe_act_launch(const MoeActArgs& a, cudaStream_t st, bool pdl);
+
+struct MoeCombineArgs {
+  const float* y; int y_ld;     // [slot][hidden]: routed slots row*topk+route, shared at rows*topk+row
+  const float* route_weight;
+  const float* logits; int logits_ld;  // shared selector logit at column `experts`
+  int experts;
+  float* hidden; int hidden_ld;
+  int rows, topk, dim;
+};
+cudaError_t moe_combine_launch(const MoeCombineArgs& a, cudaStream_t st, bool pdl);
+
+// -------------------------------------------------------- embed / head / accept
+cudaError_t embed_launch(int dt, const uint8_t* w, int64_t row_bytes, int cols, const int32_t* tokens, int rows,
+                         float* out, int out_ld, cudaStream_t st, bool pdl);
+
+struct HeadArgs {
+  const float* logits; int logits_ld;  // [rows][vocab]
+  int rows, vocab;
+  float* part_val; int* part_idx;      // [rows][nparts]
+  int nparts;
+  int* argmax;                          // [rows]
+  // speculative accept (verify mode)
+  const int32_t* tokens;                // [rows]: seed then drafts
+  int verify;                           // 1: accept the longest matching draft prefix
+  int* result;                          // [0]=accepted [1]=authoritative [2]=committed rows
+  // MTP scores of row 0: margin and top-1 probability
+  float* scores;                        // [2] or null
+};
+cudaError_t argmax_launch(const HeadArgs& a, cudaStream_t st, bool pdl);
+cudaError_t accept_launch(const HeadArgs& a, cudaStream_t st, bool pdl);
+
+// sel ^= 1; pos += committed  (after any replay)
+cudaError_t commit_launch(int* sel, int* pos, const int* result, cudaStream_t st, bool pdl);
+
+template <class K, class... Args>
+inline cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+}  // namespace iq

@@ -1,0 +1,741 @@
+// model_run.cu -- decode state, the k-row pass, verify/accept/rollback.
+//
+// One pass (QuantizedModel::forward_inner, src/qwen/quantized_model.rs:654-752):
+//   embed -> per layer { RMSNorm -> DeltaNet | gated attention -> residual
+//                        -> RMSNorm -> MoE -> residual }
+//   -> final RMSNorm -> LM head -> argmax -> accept -> replay/commit
+// Every launch is enqueued on the state's stream with programmatic dependent
+// launch, and the whole pass is captured once per row count into a CUDA graph.
+#include <algorithm>
+#include <cstring>
+#include "model.h"
+
+namespace iq {
+
+constexpr int kMaxK = 8;
+constexpr int kArgmaxParts = 128;
+
+struct QmvRec {
+  int job = 0;    // index of the first job in the state's job table for this k
+  int njobs = 0;
+  int ntiles = 0;
+  int smem = 0;
+};
+
+struct LayerRec {
+  QmvRec proj, out, router;
+};
+
+struct KPlan {
+  std::vector<LayerRec> layers;
+  QmvRec lm_head;
+};
+
+}  // namespace iq
+
+struct iq_state {
+  iq_model* m = nullptr;
+  int64_t max_pos = 0;
+  int64_t position = 0;  // host mirror of d_ctrl[0]
+  int last_rows = 0;     // rows of the last iq_forward pass (rollback bound)
+  bool can_rollback = false;
+  cudaStream_t st = nullptr;
+  // control words: [0]=pos [1]=sel [2..5]=result
+  iq::DevBuf ctrl;
+  int* h_result = nullptr;   // pinned [4]
+  int32_t* h_tokens = nullptr;  // pinned [8]
+  iq::DevBuf tokens;
+  // DeltaNet
+  std::vector<iq::DevBuf> conv, rec;  // 2 per linear layer
+  std::vector<iq::DevBuf> dn_qkv, dn_ba;  // per linear layer pass projections
+  iq::DevBuf dn_layers;  // DeltaNetLayer[n_linear]
+  // attention
+  std::vector<iq::DevBuf> kc, vc;
+  // scratch
+  iq::DevBuf hidden, xn, act8k, act80, z, dn_out, qg, kp, vp, qbuf, part, attn_out;
+  iq::DevBuf logits_moe, route_e, route_w, gu_jobs, down_jobs, counts, union_list, gu_out, act_mid, y;
+  iq::DevBuf logits, pval, pidx, argmax, scores;
+  int64_t act8k_bytes = 0, act80_bytes = 0, act_mid_bytes = 0;
+  int gu_ld = 0;
+  int max_chunks = 0;
+  // job tables for k = 1..8
+  iq::DevBuf jobs;
+  std::vector<iq::KPlan> plans;  // index k-1
+  int* union_dev = nullptr;      // counts + 4*layer + 2
+  ~iq_state() {
+    if (h_result) cudaFreeHost(h_result);
+    if (h_tokens) cudaFreeHost(h_tokens);
+    if (st) cudaStreamDestroy(st);
+  }
+};
+
+namespace iq {
+namespace {
+
+#define TRY(x)              \
+  do {                      \
+    int _rc = (x);          \
+    if (_rc) return _rc;    \
+  } while (0)
+
+int64_t arb_for(int dt, int64_t cols) { return dt == Q8_0 ? act_row_bytes_q80(cols) : act_row_bytes_q8k(cols); }
+
+QmvJob make_job(const Weight& w, const uint8_t* act, int64_t arb, float* out, int out_ld, int k, int epi,
+                const float* resid) {
+  QmvJob j;
+  memset(&j, 0, sizeof j);
+  j.w = w.p();
+  j.act = act;
+  j.out = out;
+  j.resid = resid;
+  j.w_row_bytes = w.row_bytes;
+  j.act_row_bytes = (int)arb;
+  j.out_ld = out_ld;
+  j.dtype = w.dt;
+  j.rows = (int)w.rows;
+  j.cols = (int)w.cols;
+  j.ksplit = qmv_ksplit(w.dt, w.rows, w.cols);
+  j.n = k;
+  j.epi = epi;
+  for (int i = 0; i < 8; i++) {
+    j.rowmap[i] = (uint8_t)(i < k ? i : 0);
+    j.outrow[i] = (int16_t)i;
+  }
+  return j;
+}
+
+// Append a multi-job launch to `table`, assigning tile0 prefixes.
+QmvRec add_launch(std::vector<QmvJob>& table, std::vector<QmvJob> jobs) {
+  QmvRec r;
+  r.job = (int)table.size();
+  r.njobs = (int)jobs.size();
+  int tiles = 0, smem = 0;
+  for (auto& j : jobs) {
+    j.tile0 = tiles;
+    tiles += qmv_tiles(j);
+    smem = std::max(smem, j.n * j.act_row_bytes);
+    table.push_back(j);
+  }
+  r.ntiles = tiles;
+  r.smem = smem;
+  return r;
+}
+
+struct Ctx {
+  iq_state* s;
+  iq_model* m;
+  const iq_config& c;
+  cudaStream_t st;
+  bool pdl = true;
+  Ctx(iq_state* s_) : s(s_), m(s_->m), c(s_->m->cfg), st(s_->st) {}
+  int* pos() const { return s->ctrl.as<int>(); }
+  int* sel() const { return s->ctrl.as<int>() + 1; }
+  int* result() const { return s->ctrl.as<int>() + 2; }
+  const uint8_t* act(int dt) const { return dt == Q8_0 ? s->act80.as<uint8_t>() : s->act8k.as<uint8_t>(); }
+  int64_t arb(int dt) const { return dt == Q8_0 ? s->act80_bytes : s->act8k_bytes; }
+};
+
+bool needs(int dt, bool q80) { return dt >= 0 && (q80 ? dt == Q8_0 : dt != Q8_0 && dt != F32); }
+
+int prep(Ctx& x, const float* in, int ld, int cols, const float* norm, int k, bool q8k, bool q80, float* xn) {
+  PrepArgs a = {};
+  a.x = in;
+  a.ldx = ld;
+  a.cols = cols;
+  a.norm_w = norm;
+  a.eps = x.c.rms_norm_eps;
+  a.inv_cols = (float)(1.0 / (double)cols);
+  a.xn_out = xn;
+  a.ldxn = cols;
+  a.q8k = q8k ? x.s->act8k.as<uint8_t>() : nullptr;
+  a.q80 = q80 ? x.s->act80.as<uint8_t>() : nullptr;
+  a.q8k_stride = (int)x.s->act8k_bytes;
+  a.q80_stride = (int)x.s->act80_bytes;
+  IQ_CUDA(prep_rows(a, k, x.st, x.pdl));
+  return IQ_OK;
+}
+
+int qmv(Ctx& x, const QmvRec& r) {
+  IQ_CUDA(qmv_launch(x.s->jobs.as<QmvJob>() + r.job, r.njobs, nullptr, r.ntiles, r.smem, x.st, x.pdl));
+  return IQ_OK;
+}
+
+// ------------------------------------------------------------ plan building
+int build_plans(iq_state* s) {
+  iq_model* m = s->m;
+  const iq_config& c = m->cfg;
+  const int H = c.hidden_size;
+  const int vdim = c.linear_num_value_heads * c.linear_value_head_dim;
+  const int conv_dim = 2 * c.linear_num_key_heads * c.linear_key_head_dim + vdim;
+  const int nhd = c.num_attention_heads * c.head_dim;
+  std::vector<QmvJob> table;
+  s->plans.assign(kMaxK, KPlan());
+  float* hidden = s->hidden.as<float>();
+  for (int k = 1; k <= kMaxK; k++) {
+    KPlan& P = s->plans[k - 1];
+    P.layers.resize(c.num_hidden_layers);
+    int li = 0;
+    for (int l = 0; l < c.num_hidden_layers; l++) {
+      const Layer& L = m->layers[l];
+      LayerRec& R = P.layers[l];
+      auto J = [&](const Weight& w, float* out, int ld, int epi = kEpiStore) {
+        return make_job(w, w.dt == Q8_0 ? s->act80.as<uint8_t>() : s->act8k.as<uint8_t>(),
+                        w.dt == Q8_0 ? s->act80_bytes : s->act8k_bytes, out, ld, k, epi, out);
+      };
+      if (L.type == kLinear) {
+        std::vector<QmvJob> js;
+        js.push_back(J(L.dn.qkv, s->dn_qkv[li].as<float>(), conv_dim));
+        js.push_back(J(L.dn.z, s->z.as<float>(), vdim));
+        if (L.dn.ba_fused) {
+          js.push_back(J(L.dn.ba, s->dn_ba[li].as<float>(), 2 * c.linear_num_value_heads));
+        } else {
+          js.push_back(J(L.dn.beta, s->dn_ba[li].as<float>(), 2 * c.linear_num_value_heads));
+          js.push_back(J(L.dn.alpha, s->dn_ba[li].as<float>() + c.linear_num_value_heads, 2 * c.linear_num_value_heads));
+        }
+        R.proj = add_launch(table, js);
+        R.out = add_launch(table, {J(L.dn.out, hidden, H, kEpiResidual)});
+        li++;
+      } else {
+        R.proj = add_launch(table, {J(L.at.q, s->qg.as<float>(), 2 * nhd),
+                                    J(L.at.k, s->kp.as<float>(), c.num_key_value_heads * c.head_dim),
+                                    J(L.at.v, s->vp.as<float>(), c.num_key_value_heads * c.head_dim)});
+        R.out = add_launch(table, {J(L.at.o, hidden, H, kEpiResidual)});
+      }
+      if (L.moe.router.present())
+        R.router = add_launch(table, {J(L.moe.router, s->logits_moe.as<float>(), c.num_experts + 1)});
+    }
+    P.lm_head = add_launch(table, {make_job(m->lm_head, m->lm_head.dt == Q8_0 ? s->act80.as<uint8_t>() : s->act8k.as<uint8_t>(),
+                                            m->lm_head.dt == Q8_0 ? s->act80_bytes : s->act8k_bytes,
+                                            s->logits.as<float>(), c.vocab_size, k, kEpiStore, nullptr)});
+  }
+  IQ_CUDA(s->jobs.reserve(table.size() * sizeof(QmvJob)));
+  IQ_CUDA(cudaMemcpy(s->jobs.p, table.data(), table.size() * sizeof(QmvJob), cudaMemcpyHostToDevice));
+  return IQ_OK;
+}
+
+// ------------------------------------------------------------------- layers
+int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
+  iq_state* s = x.s;
+  const iq_config& c = x.c;
+  const MoeWeights& W = L.moe;
+  const int H = c.hidden_size, E = c.num_experts;
+  const bool q8k = needs(W.gate.dt, false) || needs(W.sh_gate.dt, false) || needs(W.router.dt, false);
+  const bool q80 = needs(W.gate.dt, true) || needs(W.sh_gate.dt, true) || needs(W.router.dt, true);
+  TRY(prep(x, s->hidden.as<float>(), H, H, L.post_norm.p(), k, q8k, q80, s->xn.as<float>()));
+  float* lg = s->logits_moe.as<float>();
+  if (W.router.present()) {
+    TRY(qmv(x, R.router));
+    IQ_CUDA(f32_matvec(W.selector.p(), 1, H, s->xn.as<float>(), H, k, lg + E, E + 1, x.st, x.pdl));
+  } else {
+    IQ_CUDA(f32_matvec(W.router_sel.p(), E + 1, H, s->xn.as<float>(), H, k, lg, E + 1, x.st, x.pdl));
+  }
+  MoeRouteArgs a = {};
+  a.logits = lg;
+  a.logits_ld = E + 1;
+  a.rows = k;
+  a.experts = E;
+  a.topk = c.num_experts_per_tok;
+  a.norm_topk = c.norm_topk_prob;
+  a.hidden = H;
+  a.ffn = c.moe_intermediate_size;
+  a.sh_ffn = c.shared_expert_intermediate_size;
+  a.route_expert = s->route_e.as<int>();
+  a.route_weight = s->route_w.as<float>();
+  a.gu_jobs = s->gu_jobs.as<QmvJob>();
+  a.down_jobs = s->down_jobs.as<QmvJob>();
+  int* cnt = s->counts.as<int>();
+  a.gu_count = cnt;
+  a.down_count = cnt + 1;
+  a.union_size = cnt + 4 + layer_index;
+  a.union_list = s->union_list.as<int>();
+  a.act_in8k = s->act8k.as<uint8_t>();
+  a.act_in8k_bytes = (int)s->act8k_bytes;
+  a.act_in80 = s->act80.as<uint8_t>();
+  a.act_in80_bytes = (int)s->act80_bytes;
+  a.gu_out = s->gu_out.as<float>();
+  a.gu_ld = s->gu_ld;
+  a.act_mid = s->act_mid.as<uint8_t>();
+  a.act_mid_bytes = (int)s->act_mid_bytes;
+  a.y = s->y.as<float>();
+  a.y_ld = H;
+  MoeRouteStatic t = {};
+  const int F = c.moe_intermediate_size, Fs = c.shared_expert_intermediate_size;
+  t.gate = W.gate.p();
+  t.up = W.up.p();
+  t.down = W.down.p();
+  t.gate_stride = (int64_t)F * W.gate.row_bytes;
+  t.up_stride = (int64_t)F * W.up.row_bytes;
+  t.down_stride = (int64_t)H * W.down.row_bytes;
+  t.gate_row_bytes = W.gate.row_bytes;
+  t.down_row_bytes = W.down.row_bytes;
+  t.gate_dt = W.gate.dt;
+  t.down_dt = W.down.dt;
+  t.ks_gate = qmv_ksplit(W.gate.dt, F, H);
+  t.ks_down = qmv_ksplit(W.down.dt, H, F);
+  t.tiles_gate = (int)ceil_div(F, qmv_rows_per_cta(t.ks_gate));
+  t.tiles_down = (int)ceil_div(H, qmv_rows_per_cta(t.ks_down));
+  t.sh_gate = W.sh_gate.p();
+  t.sh_up = W.sh_up.p();
+  t.sh_down = W.sh_down.p();
+  t.sh_gate_row_bytes = W.sh_gate.row_bytes;
+  t.sh_down_row_bytes = W.sh_down.row_bytes;
+  t.sh_gate_dt = W.sh_gate.dt;
+  t.sh_down_dt = W.sh_down.dt;
+  t.ks_sh_gate = qmv_ksplit(W.sh_gate.dt, Fs, H);
+  t.ks_sh_down = qmv_ksplit(W.sh_down.dt, H, Fs);
+  t.tiles_sh_gate = (int)ceil_div(Fs, qmv_rows_per_cta(t.ks_sh_gate));
+  t.with_shared = 1;
+  t.expert_lo = W.expert_lo;
+  t.expert_hi = W.expert_hi;
+  IQ_CUDA(moe_route_launch(a, t, x.st, x.pdl));
+  // upper bounds on the dynamic job tables' tiles
+  const int max_union = std::min(W.expert_hi - W.expert_lo, k * c.num_experts_per_tok);
+  const int gu_tiles = 2 * max_union * t.tiles_gate + 2 * t.tiles_sh_gate;
+  const int tiles_sh_down = (int)ceil_div(H, qmv_rows_per_cta(t.ks_sh_down));
+  const int down_tiles = max_union * t.tiles_down + tiles_sh_down;
+  const int gu_smem = k * (int)std::max(s->act8k_bytes, s->act80_bytes);
+  IQ_CUDA(qmv_launch(a.gu_jobs, 0, a.gu_count, gu_tiles, gu_smem, x.st, x.pdl));
+  MoeActArgs b = {};
+  b.gu = a.gu_out;
+  b.gu_ld = a.gu_ld;
+  b.ffn = F;
+  b.sh_ffn = Fs;
+  b.rows = k;
+  b.topk = c.num_experts_per_tok;
+  b.route_expert = a.route_expert;
+  b.expert_lo = W.expert_lo;
+  b.expert_hi = W.expert_hi;
+  b.act = s->act_mid.as<uint8_t>();
+  b.act_bytes = (int)s->act_mid_bytes;
+  b.down_q80 = W.down.dt == Q8_0;
+  b.sh_down_q80 = W.sh_down.dt == Q8_0;
+  IQ_CUDA(moe_act_launch(b, x.st, x.pdl));
+  IQ_CUDA(qmv_launch(a.down_jobs, 0, a.down_count, down_tiles, 8 * (int)s->act_mid_bytes, x.st, x.pdl));
+  // expert parallelism: the all-gather of y happens here (model_ep.cu)
+  MoeCombineArgs cb = {};
+  cb.y = a.y;
+  cb.y_ld = H;
+  cb.route_weight = a.route_weight;
+  cb.logits = lg;
+  cb.logits_ld = E + 1;
+  cb.experts = E;
+  cb.hidden = s->hidden.as<float>();
+  cb.hidden_ld = H;
+  cb.rows = k;
+  cb.topk = c.num_experts_per_tok;
+  cb.dim = H;
+  IQ_CUDA(moe_combine_launch(cb, x.st, x.pdl));
+  return IQ_OK;
+}
+
+int run_delta(Ctx& x, const Layer& L, const LayerRec& R, int k, int li) {
+  iq_state* s = x.s;
+  const iq_config& c = x.c;
+  const DeltaWeights& D = L.dn;
+  const int H = c.hidden_size;
+  const int vdim = c.linear_num_value_heads * c.linear_value_head_dim;
+  const int conv_dim = 2 * c.linear_num_key_heads * c.linear_key_head_dim + vdim;
+  const int bdt = D.ba_fused ? D.ba.dt : D.beta.dt;
+  const bool q8k = needs(D.qkv.dt, false) || needs(D.z.dt, false) || needs(bdt, false);
+  const bool q80 = needs(D.qkv.dt, true) || needs(D.z.dt, true) || needs(bdt, true);
+  TRY(prep(x, s->hidden.as<float>(), H, H, L.attn_norm.p(), k, q8k, q80, nullptr));
+  TRY(qmv(x, R.proj));
+  DeltaNetArgs a = {};
+  a.layers = s->dn_layers.as<DeltaNetLayer>() + li;
+  a.qkv = s->dn_qkv[li].as<float>();
+  a.qkv_ld = conv_dim;
+  a.ba = s->dn_ba[li].as<float>();
+  a.ba_ld = 2 * c.linear_num_value_heads;
+  a.out = s->dn_out.as<float>();
+  a.out_ld = vdim;
+  a.rows = k;
+  a.nk = c.linear_num_key_heads;
+  a.nv = c.linear_num_value_heads;
+  a.dk = c.linear_key_head_dim;
+  a.dv = c.linear_value_head_dim;
+  a.conv_k = c.linear_conv_kernel_dim;
+  a.tiled_heads = c.value_heads_tiled;
+  a.ba_interleaved = D.ba_fused;
+  a.sel = x.sel();
+  a.committed = x.result() + 2;
+  a.replay = 0;
+  IQ_CUDA(deltanet_launch(a, 1, x.st, x.pdl));
+  GatedNormArgs g = {};
+  g.o = s->dn_out.as<float>();
+  g.o_ld = vdim;
+  g.z = s->z.as<float>();
+  g.z_ld = vdim;
+  g.w = D.norm.p();
+  g.heads = c.linear_num_value_heads;
+  g.dv = c.linear_value_head_dim;
+  g.eps = c.rms_norm_eps;
+  g.inv_dv = (float)(1.0 / c.linear_value_head_dim);
+  g.q8k = D.out.dt == Q8_0 ? nullptr : s->act8k.as<uint8_t>();
+  g.q80 = D.out.dt == Q8_0 ? s->act80.as<uint8_t>() : nullptr;
+  g.q8k_stride = (int)s->act8k_bytes;
+  g.q80_stride = (int)s->act80_bytes;
+  IQ_CUDA(gated_norm_launch(g, k, x.st, x.pdl));
+  TRY(qmv(x, R.out));
+  return IQ_OK;
+}
+
+int run_attention(Ctx& x, const Layer& L, const LayerRec& R, int k, int fi) {
+  iq_state* s = x.s;
+  const iq_config& c = x.c;
+  const AttnWeights& A = L.at;
+  const int H = c.hidden_size;
+  const int nhd = c.num_attention_heads * c.head_dim;
+  const bool q8k = needs(A.q.dt, false) || needs(A.k.dt, false) || needs(A.v.dt, false);
+  const bool q80 = needs(A.q.dt, true) || needs(A.k.dt, true) || needs(A.v.dt, true);
+  TRY(prep(x, s->hidden.as<float>(), H, H, L.attn_norm.p(), k, q8k, q80, nullptr));
+  TRY(qmv(x, R.proj));
+  AttnArgs a = {};
+  a.qg = s->qg.as<float>();
+  a.qg_ld = 2 * nhd;
+  a.kp = s->kp.as<float>();
+  a.kp_ld = c.num_key_value_heads * c.head_dim;
+  a.vp = s->vp.as<float>();
+  a.vp_ld = a.kp_ld;
+  a.q_norm = A.q_norm.p();
+  a.k_norm = A.k_norm.p();
+  a.kcache = s->kc[fi].as<float>();
+  a.vcache = s->vc[fi].as<float>();
+  a.qbuf = s->qbuf.as<float>();
+  a.part = s->part.as<float>();
+  a.out = s->attn_out.as<float>();
+  a.out_ld = nhd;
+  a.rows = k;
+  a.nh = c.num_attention_heads;
+  a.nkv = c.num_key_value_heads;
+  a.hd = c.head_dim;
+  a.rotary_dim = c.rotary_dim;
+  a.theta = c.rope_theta;
+  a.eps = c.rms_norm_eps;
+  a.pos = x.pos();
+  a.chunk_ctas = 16;
+  IQ_CUDA(attn_prep_launch(a, x.st, x.pdl));
+  IQ_CUDA(attn_scan_launch(a, x.st, x.pdl));
+  IQ_CUDA(attn_combine_launch(a, x.st, x.pdl));
+  TRY(prep(x, s->attn_out.as<float>(), nhd, nhd, nullptr, k, needs(A.o.dt, false), needs(A.o.dt, true), nullptr));
+  TRY(qmv(x, R.out));
+  return IQ_OK;
+}
+
+__global__ void rollback_prep_kernel(int* ctrl, int rows, int committed) {
+  ctrl[1] ^= 1;                   // the pass input becomes current again
+  ctrl[0] -= rows - committed;    // truncate the KV positions
+  ctrl[4] = committed;            // rows the replay keeps
+}
+__global__ void flip_kernel(int* ctrl) { ctrl[1] ^= 1; }
+
+int replay_all(Ctx& x, int k) {
+  iq_state* s = x.s;
+  const iq_config& c = x.c;
+  if (x.m->n_linear == 0) return IQ_OK;
+  const int vdim = c.linear_num_value_heads * c.linear_value_head_dim;
+  const int conv_dim = 2 * c.linear_num_key_heads * c.linear_key_head_dim + vdim;
+  // one launch per layer keeps each layer's projection pointers simple
+  for (int li = 0; li < x.m->n_linear; li++) {
+    DeltaNetArgs a = {};
+    a.layers = s->dn_layers.as<DeltaNetLayer>() + li;
+    a.qkv = s->dn_qkv[li].as<float>();
+    a.qkv_ld = conv_dim;
+    a.ba = s->dn_ba[li].as<float>();
+    a.ba_ld = 2 * c.linear_num_value_heads;
+    a.out = nullptr;
+    a.rows = k;
+    a.nk = c.linear_num_key_heads;
+    a.nv = c.linear_num_value_heads;
+    a.dk = c.linear_key_head_dim;
+    a.dv = c.linear_value_head_dim;
+    a.conv_k = c.linear_conv_kernel_dim;
+    a.tiled_heads = c.value_heads_tiled;
+    const Layer* L = nullptr;
+    int seen = 0;
+    for (const Layer& ly : x.m->layers)
+      if (ly.type == kLinear && seen++ == li) { L = &ly; break; }
+    a.ba_interleaved = L->dn.ba_fused;
+    a.sel = x.sel();
+    a.committed = x.result() + 2;
+    a.replay = 1;
+    IQ_CUDA(deltanet_launch(a, 1, x.st, x.pdl));
+  }
+  return IQ_OK;
+}
+
+// The pass body shared by forward and verify.
+int run_pass(iq_state* s, int k, bool verify) {
+  Ctx x(s);
+  iq_model* m = s->m;
+  const iq_config& c = m->cfg;
+  const KPlan& P = s->plans[k - 1];
+  const int H = c.hidden_size;
+  IQ_CUDA(cudaMemcpyAsync(s->tokens.p, s->h_tokens, k * sizeof(int32_t), cudaMemcpyHostToDevice, x.st));
+  IQ_CUDA(embed_launch(m->embed.dt, m->embed.p(), m->embed.row_bytes, H, s->tokens.as<int32_t>(), k,
+                       s->hidden.as<float>(), H, x.st, x.pdl));
+  int li = 0, fi = 0;
+  for (int l = 0; l < c.num_hidden_layers; l++) {
+    const Layer& L = m->layers[l];
+    if (L.type == kLinear) TRY(run_delta(x, L, P.layers[l], k, li++));
+    else TRY(run_attention(x, L, P.layers[l], k, fi++));
+    TRY(run_moe(x, L, P.layers[l], k, l));
+  }
+  TRY(prep(x, s->hidden.as<float>(), H, H, m->out_norm.p(), k, needs(m->lm_head.dt, false),
+           needs(m->lm_head.dt, true), s->xn.as<float>()));
+  TRY(qmv(x, P.lm_head));
+  HeadArgs h = {};
+  h.logits = s->logits.as<float>();
+  h.logits_ld = c.vocab_size;
+  h.rows = k;
+  h.vocab = c.vocab_size;
+  h.part_val = s->pval.as<float>();
+  h.part_idx = s->pidx.as<int>();
+  h.nparts = kArgmaxParts;
+  h.argmax = s->argmax.as<int>();
+  h.tokens = s->tokens.as<int32_t>();
+  h.verify = verify ? 1 : 0;
+  h.result = x.result();
+  h.scores = nullptr;
+  IQ_CUDA(argmax_launch(h, x.st, x.pdl));
+  IQ_CUDA(accept_launch(h, x.st, x.pdl));
+  if (verify) TRY(replay_all(x, k));
+  IQ_CUDA(commit_launch(x.sel(), x.pos(), x.result(), x.st, x.pdl));
+  IQ_CUDA(cudaMemcpyAsync(s->h_result, x.result(), 4 * sizeof(int), cudaMemcpyDeviceToHost, x.st));
+  return IQ_OK;
+}
+
+int alloc_state(iq_state* s) {
+  iq_model* m = s->m;
+  const iq_config& c = m->cfg;
+  const int K = kMaxK;
+  const int64_t H = c.hidden_size;
+  const int64_t vdim = (int64_t)c.linear_num_value_heads * c.linear_value_head_dim;
+  const int64_t conv_dim = 2 * (int64_t)c.linear_num_key_heads * c.linear_key_head_dim + vdim;
+  const int64_t nhd = (int64_t)c.num_attention_heads * c.head_dim;
+  const int64_t kvd = (int64_t)c.num_key_value_heads * c.head_dim;
+  const int64_t E = c.num_experts, topk = c.num_experts_per_tok;
+  const int64_t F = c.moe_intermediate_size, Fs = c.shared_expert_intermediate_size;
+  IQ_CUDA(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+  IQ_CUDA(cudaMallocHost(&s->h_result, 4 * sizeof(int)));
+  IQ_CUDA(cudaMallocHost(&s->h_tokens, kMaxK * sizeof(int32_t)));
+  IQ_CUDA(s->ctrl.reserve(8 * sizeof(int)));
+  IQ_CUDA(cudaMemset(s->ctrl.p, 0, 8 * sizeof(int)));
+  IQ_CUDA(s->tokens.reserve(kMaxK * sizeof(int32_t)));
+  const int64_t K_conv = c.linear_conv_kernel_dim - 1;
+  std::vector<DeltaNetLayer> dl;
+  s->conv.resize(2 * m->n_linear);
+  s->rec.resize(2 * m->n_linear);
+  s->dn_qkv.resize(m->n_linear);
+  s->dn_ba.resize(m->n_linear);
+  int li = 0;
+  for (const Layer& L : m->layers) {
+    if (L.type != kLinear) continue;
+    DeltaNetLayer d = {};
+    for (int b = 0; b < 2; b++) {
+      IQ_CUDA(s->conv[2 * li + b].reserve(std::max<int64_t>(1, conv_dim * K_conv) * 4));
+      IQ_CUDA(s->rec[2 * li + b].reserve((size_t)c.linear_num_value_heads * c.linear_key_head_dim *
+                                         c.linear_value_head_dim * 4));
+      d.conv_state[b] = s->conv[2 * li + b].as<float>();
+      d.rec_state[b] = s->rec[2 * li + b].as<float>();
+    }
+    d.conv_w = L.dn.conv_w.p();
+    d.ssm_a = L.dn.ssm_a.p();
+    d.dt_bias = L.dn.dt_bias.p();
+    IQ_CUDA(s->dn_qkv[li].reserve((size_t)(K * conv_dim * 4)));
+    IQ_CUDA(s->dn_ba[li].reserve((size_t)(K * 2 * c.linear_num_value_heads * 4)));
+    dl.push_back(d);
+    li++;
+  }
+  if (!dl.empty()) {
+    IQ_CUDA(s->dn_layers.reserve(dl.size() * sizeof(DeltaNetLayer)));
+    IQ_CUDA(cudaMemcpy(s->dn_layers.p, dl.data(), dl.size() * sizeof(DeltaNetLayer), cudaMemcpyHostToDevice));
+  }
+  s->kc.resize(m->n_full + (m->has_mtp ? 1 : 0));
+  s->vc.resize(s->kc.size());
+  for (size_t i = 0; i < s->kc.size(); i++) {
+    IQ_CUDA(s->kc[i].reserve((size_t)(s->max_pos * kvd * 4)));
+    IQ_CUDA(s->vc[i].reserve((size_t)(s->max_pos * kvd * 4)));
+  }
+  const int64_t maxcols = std::max({H, vdim, nhd, 2 * H});
+  s->act8k_bytes = act_row_bytes_q8k(maxcols);
+  s->act80_bytes = act_row_bytes_q80(maxcols);
+  IQ_CUDA(s->hidden.reserve(K * H * 4));
+  IQ_CUDA(s->xn.reserve(K * H * 4));
+  IQ_CUDA(s->act8k.reserve(K * s->act8k_bytes));
+  IQ_CUDA(s->act80.reserve(K * s->act80_bytes));
+  IQ_CUDA(s->z.reserve(K * std::max<int64_t>(vdim, 1) * 4));
+  IQ_CUDA(s->dn_out.reserve(K * std::max<int64_t>(vdim, 1) * 4));
+  IQ_CUDA(s->qg.reserve(K * 2 * nhd * 4));
+  IQ_CUDA(s->kp.reserve(K * kvd * 4));
+  IQ_CUDA(s->vp.reserve(K * kvd * 4));
+  IQ_CUDA(s->qbuf.reserve(K * nhd * 4));
+  IQ_CUDA(s->attn_out.reserve(K * nhd * 4));
+  s->max_chunks = (int)ceil_div(s->max_pos + kMaxK, kAttnChunk);
+  IQ_CUDA(s->part.reserve((size_t)K * c.num_attention_heads * s->max_chunks * (c.head_dim + 2) * 4));
+  const int64_t slots = K * topk + K;
+  IQ_CUDA(s->logits_moe.reserve(K * (E + 1) * 4));
+  IQ_CUDA(s->route_e.reserve(K * topk * 4));
+  IQ_CUDA(s->route_w.reserve(K * topk * 4));
+  IQ_CUDA(s->gu_jobs.reserve((2 * E + 2) * sizeof(QmvJob)));
+  IQ_CUDA(s->down_jobs.reserve((E + 1) * sizeof(QmvJob)));
+  IQ_CUDA(s->counts.reserve((4 + c.num_hidden_layers + 2) * 4));
+  IQ_CUDA(cudaMemset(s->counts.p, 0, (4 + c.num_hidden_layers + 2) * 4));
+  IQ_CUDA(s->union_list.reserve(E * 4));
+  s->gu_ld = (int)(2 * std::max(F, Fs));
+  IQ_CUDA(s->gu_out.reserve(slots * s->gu_ld * 4));
+  s->act_mid_bytes = std::max(act_row_bytes_q8k(std::max(F, Fs)), act_row_bytes_q80(std::max(F, Fs)));
+  IQ_CUDA(s->act_mid.reserve(slots * s->act_mid_bytes));
+  IQ_CUDA(s->y.reserve(slots * H * 4));
+  IQ_CUDA(s->logits.reserve((size_t)K * c.vocab_size * 4));
+  IQ_CUDA(s->pval.reserve(K * kArgmaxParts * 3 * 4));
+  IQ_CUDA(s->pidx.reserve(K * kArgmaxParts * 4));
+  IQ_CUDA(s->argmax.reserve(K * 4));
+  IQ_CUDA(s->scores.reserve(4 * 4));
+  return build_plans(s);
+}
+
+int reset_state(iq_state* s) {
+  for (auto& b : s->conv) IQ_CUDA(cudaMemsetAsync(b.p, 0, b.bytes, s->st));
+  for (auto& b : s->rec) IQ_CUDA(cudaMemsetAsync(b.p, 0, b.bytes, s->st));
+  IQ_CUDA(cudaMemsetAsync(s->ctrl.p, 0, 8 * sizeof(int), s->st));
+  IQ_CUDA(cudaStreamSynchronize(s->st));
+  s->position = 0;
+  s->can_rollback = false;
+  return IQ_OK;
+}
+
+int copy_out(iq_state* s, int k, int row0, float* logits, float* hidden, int32_t* argmax) {
+  const iq_config& c = s->m->cfg;
+  if (logits)
+    IQ_CUDA(cudaMemcpyAsync(logits + (int64_t)row0 * c.vocab_size, s->logits.p, (size_t)k * c.vocab_size * 4,
+                            cudaMemcpyDeviceToHost, s->st));
+  if (hidden)
+    IQ_CUDA(cudaMemcpyAsync(hidden + (int64_t)row0 * c.hidden_size, s->xn.p, (size_t)k * c.hidden_size * 4,
+                            cudaMemcpyDeviceToHost, s->st));
+  if (argmax)
+    IQ_CUDA(cudaMemcpyAsync(argmax + row0, s->argmax.p, (size_t)k * 4, cudaMemcpyDeviceToHost, s->st));
+  return IQ_OK;
+}
+
+}  // namespace
+}  // namespace iq
+
+using namespace iq;
+
+extern "C" {
+
+int iq_state_create(iq_model* m, int64_t max_positions, iq_state** out) {
+  clear_error();
+  IQ_CHECK(m && out, IQ_EINVAL, "iq_state_create: null argument");
+  IQ_CHECK(max_positions > 0 && max_positions <= m->cfg.max_position_embeddings, IQ_EINVAL,
+           "max_positions %lld outside 1..%d", (long long)max_positions, m->cfg.max_position_embeddings);
+  std::unique_ptr<iq_state> s(new iq_state);
+  s->m = m;
+  s->max_pos = max_positions;
+  int rc = alloc_state(s.get());
+  if (rc) return rc;
+  rc = reset_state(s.get());
+  if (rc) return rc;
+  *out = s.release();
+  return IQ_OK;
+}
+
+void iq_state_destroy(iq_state* s) {
+  if (s && s->st) cudaStreamSynchronize(s->st);
+  delete s;
+}
+
+int iq_state_reset(iq_state* s) {
+  clear_error();
+  IQ_CHECK(s, IQ_EINVAL, "iq_state_reset: null state");
+  return reset_state(s);
+}
+
+int iq_state_position(const iq_state* s, int64_t* position) {
+  IQ_CHECK(s && position, IQ_EINVAL, "iq_state_position: null argument");
+  *position = s->position;
+  return IQ_OK;
+}
+
+int iq_state_stream(const iq_state* s, void** stream) {
+  IQ_CHECK(s && stream, IQ_EINVAL, "iq_state_stream: null argument");
+  *stream = s->st;
+  return IQ_OK;
+}
+
+int iq_forward(iq_state* s, const uint32_t* tokens, int rows, float* logits, float* hidden, int32_t* argmax) {
+  clear_error();
+  IQ_CHECK(s && tokens, IQ_EINVAL, "iq_forward: null argument");
+  IQ_CHECK(rows >= 1, IQ_EINVAL, "forward requires at least one token");
+  IQ_CHECK(s->position + rows <= s->max_pos, IQ_EINVAL, "sequence exceeds the state's %lld positions",
+           (long long)s->max_pos);
+  const int V = s->m->cfg.vocab_size;
+  for (int i = 0; i < rows; i++)
+    IQ_CHECK(tokens[i] < (uint32_t)V, IQ_EINVAL, "token %u outside the vocabulary of %d", tokens[i], V);
+  for (int r0 = 0; r0 < rows; r0 += kMaxK) {
+    const int k = std::min(kMaxK, rows - r0);
+    IQ_CUDA(cudaStreamSynchronize(s->st));  // h_tokens is reused
+    for (int i = 0; i < k; i++) s->h_tokens[i] = (int32_t)tokens[r0 + i];
+    int rc = run_pass(s, k, false);
+    if (rc) return rc;
+    rc = copy_out(s, k, r0, logits, hidden, argmax);
+    if (rc) return rc;
+    s->position += k;
+    s->last_rows = k;
+  }
+  IQ_CUDA(cudaStreamSynchronize(s->st));
+  s->can_rollback = true;
+  return IQ_OK;
+}
+
+int iq_verify(iq_state* s, const uint32_t* tokens, int rows, iq_verify_result* out, float* logits, float* hidden) {
+  clear_error();
+  IQ_CHECK(s && tokens && out, IQ_EINVAL, "iq_verify: null argument");
+  IQ_CHECK(rows >= 1 && rows <= kMaxK, IQ_EINVAL, "verify takes 1..%d rows, got %d", kMaxK, rows);
+  IQ_CHECK(s->position + rows <= s->max_pos, IQ_EINVAL, "sequence exceeds the state's %lld positions",
+           (long long)s->max_pos);
+  const int V = s->m->cfg.vocab_size;
+  for (int i = 0; i < rows; i++)
+    IQ_CHECK(tokens[i] < (uint32_t)V, IQ_EINVAL, "token %u outside the vocabulary of %d", tokens[i], V);
+  IQ_CUDA(cudaStreamSynchronize(s->st));
+  for (int i = 0; i < rows; i++) s->h_tokens[i] = (int32_t)tokens[i];
+  int rc = run_pass(s, rows, true);
+  if (rc) return rc;
+  rc = copy_out(s, rows, 0, logits, hidden, nullptr);
+  if (rc) return rc;
+  IQ_CUDA(cudaStreamSynchronize(s->st));
+  out->accepted = s->h_result[0];
+  out->authoritative = s->h_result[1];
+  out->committed = s->h_result[2];
+  s->position += out->committed;
+  s->can_rollback = false;
+  return IQ_OK;
+}
+
+int iq_rollback(iq_state* s, int committed_rows) {
+  clear_error();
+  IQ_CHECK(s, IQ_EINVAL, "iq_rollback: null state");
+  IQ_CHECK(s->can_rollback, IQ_ESTATE, "no forward pass to roll back");
+  IQ_CHECK(committed_rows >= 0 && committed_rows < s->last_rows, IQ_EINVAL,
+           "cannot roll back to %d of %d committed rows", committed_rows, s->last_rows);
+  Ctx x(s);
+  rollback_prep_kernel<<<1, 1, 0, s->st>>>(s->ctrl.as<int>(), s->last_rows, committed_rows);
+  IQ_CUDA(cudaGetLastError());
+  int rc = replay_all(x, s->last_rows);
+  if (rc) return rc;
+  flip_kernel<<<1, 1, 0, s->st>>>(s->ctrl.as<int>());
+  IQ_CUDA(cudaGetLastError());
+  IQ_CUDA(cudaStreamSynchronize(s->st));
+  s->position -= s->last_rows - committed_rows;
+  s->can_rollback = false;
+  return IQ_OK;
+}
+
+int iq_state_union_sizes(const iq_state* s, int32_t* per_layer) {
+  IQ_CHECK(s && per_layer, IQ_EINVAL, "iq_state_union_sizes: null argument");
+  IQ_CUDA(cudaStreamSynchronize(s->st));
+  IQ_CUDA(cudaMemcpy(per_layer, s->counts.as<int>() + 4, s->m->cfg.num_hidden_layers * 4, cudaMemcpyDeviceToHost));
+  return IQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,262 @@
+// moe.cu -- router softmax/top-k, expert-union job tables, SwiGLU activation
+// and the ordered combine of the sparse MoE block.
+//
+// Restates src/qwen/moe.rs:21-54 (softmax over the router logits, top-k by
+// probability, renormalised weights) and src/qwen/quantized_moe.rs:237-460
+// (grouped-by-expert execution: each distinct expert's weights are read once
+// for every row routed to it; silu(g)*u with g/(1+exp(-g)); weighted sum in
+// row -> route order, multiply then add; shared expert times
+// sigmoid(x . selector) added after the routed sum).
+#include "model_kernels.cuh"
+#include "devfns.cuh"
+
+namespace iq {
+namespace {
+
+constexpr int kMaxRows = 8;
+constexpr int kMaxExperts = 1024;
+
+__device__ __forceinline__ void set_job(QmvJob& j, const uint8_t* w, int64_t w_row_bytes, int dt, int rows, int cols,
+                                        int ks, const uint8_t* act, int act_bytes, float* out, int out_ld, int n,
+                                        int tile0) {
+  j.w = w;
+  j.act = act;
+  j.out = out;
+  j.resid = nullptr;
+  j.w_row_bytes = w_row_bytes;
+  j.act_row_bytes = act_bytes;
+  j.out_ld = out_ld;
+  j.dtype = dt;
+  j.rows = rows;
+  j.cols = cols;
+  j.ksplit = ks;
+  j.n = n;
+  j.tile0 = tile0;
+  j.epi = kEpiStore;
+}
+
+// One CTA.  Warp t < rows routes row t; then every thread e examines expert
+// e (and e + 256, ...) and, if it is in the union and resident, writes that
+// expert's gate, up and down jobs at its rank in the ascending union.
+__global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRouteStatic s) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int sel_e[kMaxRows][16];
+  __shared__ float sel_w[kMaxRows][16];
+  __shared__ unsigned used[kMaxExperts / 32];
+  __shared__ int scan[256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = a.experts;
+  for (int i = threadIdx.x; i < kMaxExperts / 32; i += 256) used[i] = 0;
+  __syncthreads();
+  if (warp < a.rows) {
+    const float* lg = a.logits + (int64_t)warp * a.logits_ld;
+    float mx = -INFINITY;
+    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float den = 0.f;
+    for (int e = lane; e < E; e += 32) den = __fadd_rn(den, expf(lg[e] - mx));
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) den = __fadd_rn(den, __shfl_xor_sync(0xffffffffu, den, o));
+    // top-k by probability; equal probabilities rank the lower expert first
+    for (int r = 0; r < a.topk; r++) {
+      float best = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int e = lane; e < E; e += 32) {
+        bool tk = false;
+        for (int q = 0; q < r; q++) tk |= sel_e[warp][q] == e;
+        if (tk) continue;
+        const float p = __fdiv_rn(expf(lg[e] - mx), den);
+        if (p > best || (p == best && e < bi)) { best = p; bi = e; }
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+      }
+      if (lane == 0) { sel_e[warp][r] = bi; sel_w[warp][r] = best; }
+      __syncwarp();
+    }
+    if (lane == 0) {
+      float sum = 0.f;
+      for (int r = 0; r < a.topk; r++) sum = __fadd_rn(sum, sel_w[warp][r]);
+      for (int r = 0; r < a.topk; r++) {
+        const float w = a.norm_topk ? __fdiv_rn(sel_w[warp][r], sum) : sel_w[warp][r];
+        a.route_expert[warp * a.topk + r] = sel_e[warp][r];
+        a.route_weight[warp * a.topk + r] = w;
+        atomicOr(&used[sel_e[warp][r] / 32], 1u << (sel_e[warp][r] % 32));
+      }
+    }
+  }
+  __syncthreads();
+  // rank of each used+resident expert in the ascending union
+  const int per = (E + 255) / 256;  // experts per thread, contiguous
+  int mine = 0;
+  for (int q = 0; q < per; q++) {
+    const int e = threadIdx.x * per + q;
+    if (e < E && ((used[e / 32] >> (e % 32)) & 1)) mine++;
+  }
+  scan[threadIdx.x] = mine;
+  __syncthreads();
+  for (int o = 1; o < 256; o <<= 1) {
+    const int v = threadIdx.x >= o ? scan[threadIdx.x - o] : 0;
+    __syncthreads();
+    scan[threadIdx.x] += v;
+    __syncthreads();
+  }
+  int rank = scan[threadIdx.x] - mine;  // exclusive prefix: union index of my first expert
+  const int total_union = scan[255];
+  int res_rank = 0;  // resident union rank (jobs exist only for resident experts)
+  {
+    // count resident union experts before mine: recompute with a second scan
+    int rmine = 0;
+    for (int q = 0; q < per; q++) {
+      const int e = threadIdx.x * per + q;
+      if (e < E && ((used[e / 32] >> (e % 32)) & 1) && e >= s.expert_lo && e < s.expert_hi) rmine++;
+    }
+    __syncthreads();
+    scan[threadIdx.x] = rmine;
+    __syncthreads();
+    for (int o = 1; o < 256; o <<= 1) {
+      const int v = threadIdx.x >= o ? scan[threadIdx.x - o] : 0;
+      __syncthreads();
+      scan[threadIdx.x] += v;
+      __syncthreads();
+    }
+    res_rank = scan[threadIdx.x] - rmine;
+  }
+  const int n_res = scan[255];
+  const int slots_routed = a.rows * a.topk;
+  for (int q = 0; q < per; q++) {
+    const int e = threadIdx.x * per + q;
+    if (!(e < E && ((used[e / 32] >> (e % 32)) & 1))) continue;
+    a.union_list[rank++] = e;
+    if (e < s.expert_lo || e >= s.expert_hi) continue;
+    const int le = e - s.expert_lo;
+    QmvJob gj, uj, dj;
+    const int ri = res_rank++;
+    const bool q80 = s.gate_dt == Q8_0;
+    const uint8_t* ain = q80 ? a.act_in80 : a.act_in8k;
+    const int ab = q80 ? a.act_in80_bytes : a.act_in8k_bytes;
+    set_job(gj, s.gate + le * s.gate_stride, s.gate_row_bytes, s.gate_dt, a.ffn, a.hidden, s.ks_gate, ain, ab,
+            a.gu_out, a.gu_ld, 0, 2 * ri * s.tiles_gate);
+    set_job(uj, s.up + le * s.up_stride, s.gate_row_bytes, s.gate_dt, a.ffn, a.hidden, s.ks_gate, ain, ab,
+            a.gu_out + a.ffn, a.gu_ld, 0, (2 * ri + 1) * s.tiles_gate);
+    set_job(dj, s.down + le * s.down_stride, s.down_row_bytes, s.down_dt, a.hidden, a.ffn, s.ks_down, a.act_mid,
+            a.act_mid_bytes, a.y, a.y_ld, 0, ri * s.tiles_down);
+    int n = 0;
+    for (int t = 0; t < a.rows; t++)
+      for (int r = 0; r < a.topk; r++)
+        if (a.route_expert[t * a.topk + r] == e) {
+          const int slot = t * a.topk + r;
+          gj.rowmap[n] = uj.rowmap[n] = (uint8_t)t;
+          gj.outrow[n] = uj.outrow[n] = (int16_t)slot;
+          dj.rowmap[n] = (uint8_t)slot;
+          dj.outrow[n] = (int16_t)slot;
+          n++;
+        }
+    gj.n = uj.n = dj.n = n;
+    a.gu_jobs[2 * ri] = gj;
+    a.gu_jobs[2 * ri + 1] = uj;
+    a.down_jobs[ri] = dj;
+  }
+  if (threadIdx.x == 0) {
+    // shared expert: every row, slots rows*topk + t
+    QmvJob gj, uj, dj;
+    const bool q80 = s.sh_gate_dt == Q8_0;
+    const uint8_t* ain = q80 ? a.act_in80 : a.act_in8k;
+    const int ab = q80 ? a.act_in80_bytes : a.act_in8k_bytes;
+    set_job(gj, s.sh_gate, s.sh_gate_row_bytes, s.sh_gate_dt, a.sh_ffn, a.hidden, s.ks_sh_gate, ain, ab, a.gu_out,
+            a.gu_ld, a.rows, 2 * n_res * s.tiles_gate);
+    set_job(uj, s.sh_up, s.sh_gate_row_bytes, s.sh_gate_dt, a.sh_ffn, a.hidden, s.ks_sh_gate, ain, ab,
+            a.gu_out + a.sh_ffn, a.gu_ld, a.rows, 2 * n_res * s.tiles_gate + s.tiles_sh_gate);
+    set_job(dj, s.sh_down, s.sh_down_row_bytes, s.sh_down_dt, a.hidden, a.sh_ffn, s.ks_sh_down, a.act_mid,
+            a.act_mid_bytes, a.y, a.y_ld, a.rows, n_res * s.tiles_down);
+    for (int t = 0; t < a.rows; t++) {
+      gj.rowmap[t] = uj.rowmap[t] = (uint8_t)t;
+      gj.outrow[t] = uj.outrow[t] = (int16_t)(slots_routed + t);
+      dj.rowmap[t] = (uint8_t)(slots_routed + t);
+      dj.outrow[t] = (int16_t)(slots_routed + t);
+    }
+    a.gu_jobs[2 * n_res] = gj;
+    a.gu_jobs[2 * n_res + 1] = uj;
+    a.down_jobs[n_res] = dj;
+    *a.gu_count = s.with_shared ? 2 * n_res + 2 : 2 * n_res;
+    *a.down_count = s.with_shared ? n_res + 1 : n_res;
+    *a.union_size = total_union;
+  }
+}
+
+// One CTA per slot: silu(gate) * up (candle's elementwise silu,
+// g / (1 + exp(-g))), quantized to Q8_K for the down projection.
+__global__ void __launch_bounds__(256) moe_act_kernel(MoeActArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ float xs[];
+  const int slot = blockIdx.x;
+  const int routed = a.rows * a.topk;
+  if (slot >= routed + a.rows) return;
+  int ffn = a.sh_ffn;
+  bool q80 = a.sh_down_q80;
+  if (slot < routed) {
+    const int e = a.route_expert[slot];
+    if (e < a.expert_lo || e >= a.expert_hi) return;
+    ffn = a.ffn;
+    q80 = a.down_q80;
+  }
+  const float* g = a.gu + (int64_t)slot * a.gu_ld;
+  for (int i = threadIdx.x; i < ffn; i += 256) {
+    const float gv = g[i];
+    xs[i] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.f, expf(-gv))), g[ffn + i]);
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* ar = a.act + (int64_t)slot * a.act_bytes;
+  if (q80) {
+    const int nb = ffn / 32;
+    for (int g = warp; g < nb / 4; g += 8) quant_q80_group_warp(xs, ar, nb, g, lane);
+  } else {
+    const int nb = ffn / 256;
+    for (int b = warp; b < nb; b += 8) quant_q8k_block_warp(xs, ar, nb, b, lane);
+  }
+}
+
+// One CTA per row: hidden += (sum_route y*w) + shared * sigmoid(selector).
+__global__ void __launch_bounds__(256) moe_combine_kernel(MoeCombineArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  const float sl = a.logits[(int64_t)t * a.logits_ld + a.experts];
+  const float selector = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-sl)));
+  const float* ysh = a.y + (int64_t)(a.rows * a.topk + t) * a.y_ld;
+  for (int i = threadIdx.x; i < a.dim; i += 256) {
+    float r = 0.f;
+    for (int q = 0; q < a.topk; q++) {
+      const float w = a.route_weight[t * a.topk + q];
+      r = __fadd_rn(r, __fmul_rn(a.y[(int64_t)(t * a.topk + q) * a.y_ld + i], w));
+    }
+    const float moe = __fadd_rn(r, __fmul_rn(ysh[i], selector));
+    float* h = a.hidden + (int64_t)t * a.hidden_ld + i;
+    *h = __fadd_rn(*h, moe);
+  }
+}
+
+}  // namespace
+
+cudaError_t moe_route_launch(const MoeRouteArgs& a, const MoeRouteStatic& s, cudaStream_t st, bool pdl) {
+  if (a.rows > kMaxRows || a.experts > kMaxExperts || a.topk > 16) return cudaErrorInvalidValue;
+  return launch_pdl(moe_route_kernel, dim3(1), dim3(256), 0, st, pdl, a, s);
+}
+
+cudaError_t moe_act_launch(const MoeActArgs& a, cudaStream_t st, bool pdl) {
+  const int ffn = a.ffn > a.sh_ffn ? a.ffn : a.sh_ffn;
+  return launch_pdl(moe_act_kernel, dim3(a.rows * a.topk + a.rows), dim3(256), ffn * sizeof(float), st, pdl, a);
+}
+
+cudaError_t moe_combine_launch(const MoeCombineArgs& a, cudaStream_t st, bool pdl) {
+  return launch_pdl(moe_combine_kernel, dim3(a.rows), dim3(256), 0, st, pdl, a);
+}
+
+}  // namespace iq

@@ -2,6 +2,10 @@
 #include "qmv.cuh"
 #include "layout.cuh"
 
+#ifndef QMV_MIN_BLOCKS
+#define QMV_MIN_BLOCKS 2
+#endif
+
 namespace iq {
 namespace {
 
@@ -19,51 +23,86 @@ struct ActCols {  // the two C-fragment columns of this thread
   const uint8_t* c[2];
 };
 
+__device__ __forceinline__ void load_act(uint4 (&bw)[4], const uint8_t* bact, int b, int tig) {
+  if (bact) {
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      bw[i] = *reinterpret_cast<const uint4*>(bact + (int64_t)b * 256 + tig * 64 + i * 16);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; i++) bw[i] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Software pipeline over a chunk: the weights of block b+1 are in flight
+// while block b is computed.  The first block's weights are requested before
+// the programmatic-dependency wait (weights never depend on the previous
+// kernel; the activations do).
+template <class Ops, class Stage>
+__device__ __forceinline__ void run_chunk(const Ops& ops, int b0, int b1, bool live, Stage& stage, Frag& f) {
+  typename Ops::Regs cur;
+  if (live) cur = ops.load(b0);
+  stage();  // every thread: wait for the producer kernel, stage activations
+  if (!live) return;
+  for (int b = b0; b < b1; b++) {
+    typename Ops::Regs nxt;
+    if (b + 1 < b1) nxt = ops.load(b + 1);
+    ops.compute(cur, b, f);
+    cur = nxt;
+  }
+}
+
 // ---------------------------------------------------------------- Q4_K / Q5_K
 template <int DT>
-__device__ __forceinline__ void chunk_q45(const QmvJob& jb, const uint8_t* wa, const uint8_t* wb,
-                                         const uint8_t* bact, ActCols ac, int nb, int b0, int b1,
-                                         int tig, Frag& f) {
-  constexpr int BB = DT == Q4_K ? 144 : 176;
-  constexpr int QS = DT == Q4_K ? 16 : 48;
-  for (int b = b0; b < b1; b++) {
+struct OpsQ45 {
+  static constexpr int BB = DT == Q4_K ? 144 : 176;
+  static constexpr int QS = DT == Q4_K ? 16 : 48;
+  struct Regs {
+    uint4 ha, hb, qa0, qa1, qb0, qb1;
+    uint2 hha, hhb;
+  };
+  const uint8_t *wa, *wb, *bact;
+  ActCols ac;
+  int nb, tig;
+  __device__ __forceinline__ Regs load(int b) const {
+    Regs r;
     const uint8_t* ba = wa + (int64_t)b * BB;
     const uint8_t* bb = wb + (int64_t)b * BB;
-    uint4 ha = ld_stream(ba), hb = ld_stream(bb);
-    uint4 qa0 = ld_stream(ba + QS + tig * 32), qa1 = ld_stream(ba + QS + tig * 32 + 16);
-    uint4 qb0 = ld_stream(bb + QS + tig * 32), qb1 = ld_stream(bb + QS + tig * 32 + 16);
-    uint2 hha = make_uint2(0, 0), hhb = make_uint2(0, 0);
+    r.ha = ld_stream(ba);
+    r.hb = ld_stream(bb);
+    r.qa0 = ld_stream(ba + QS + tig * 32);
+    r.qa1 = ld_stream(ba + QS + tig * 32 + 16);
+    r.qb0 = ld_stream(bb + QS + tig * 32);
+    r.qb1 = ld_stream(bb + QS + tig * 32 + 16);
     if (DT == Q5_K) {
-      hha = *reinterpret_cast<const uint2*>(ba + 16 + tig * 8);
-      hhb = *reinterpret_cast<const uint2*>(bb + 16 + tig * 8);
-    }
-    uint4 bw[4];
-    if (bact) {
-#pragma unroll
-      for (int i = 0; i < 4; i++)
-        bw[i] = *reinterpret_cast<const uint4*>(bact + (int64_t)b * 256 + tig * 64 + i * 16);
+      r.hha = *reinterpret_cast<const uint2*>(ba + 16 + tig * 8);
+      r.hhb = *reinterpret_cast<const uint2*>(bb + 16 + tig * 8);
     } else {
-#pragma unroll
-      for (int i = 0; i < 4; i++) bw[i] = make_uint4(0, 0, 0, 0);
+      r.hha = r.hhb = make_uint2(0, 0);
     }
+    return r;
+  }
+  __device__ __forceinline__ void compute(const Regs& r, int b, Frag& f) const {
+    uint4 bw[4];
+    load_act(bw, bact, b, tig);
     int scA[8], mnA[8], scB[8], mnB[8];
-    unpack_k_scales(reinterpret_cast<const uint8_t*>(&ha) + 4, scA, mnA);
-    unpack_k_scales(reinterpret_cast<const uint8_t*>(&hb) + 4, scB, mnB);
+    unpack_k_scales(reinterpret_cast<const uint8_t*>(&r.ha) + 4, scA, mnA);
+    unpack_k_scales(reinterpret_cast<const uint8_t*>(&r.hb) + 4, scB, mnB);
     int isum[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int s = 0; s < 8; s++) {
       const int j = s / 2, hi = s & 1;
-      const uint4& qa = j < 2 ? qa0 : qa1;
-      const uint4& qb = j < 2 ? qb0 : qb1;
+      const uint4& qa = j < 2 ? r.qa0 : r.qa1;
+      const uint4& qb = j < 2 ? r.qb0 : r.qb1;
       uint32_t wa0 = w32(qa, (j % 2) * 2), wa1 = w32(qa, (j % 2) * 2 + 1);
       uint32_t wb0 = w32(qb, (j % 2) * 2), wb1 = w32(qb, (j % 2) * 2 + 1);
       uint32_t a0 = (wa0 >> (4 * hi)) & 0x0F0F0F0Fu, a2 = (wa1 >> (4 * hi)) & 0x0F0F0F0Fu;
       uint32_t a1 = (wb0 >> (4 * hi)) & 0x0F0F0F0Fu, a3 = (wb1 >> (4 * hi)) & 0x0F0F0F0Fu;
       if (DT == Q5_K) {
-        a0 |= ((hha.x >> s) & 0x01010101u) << 4;
-        a2 |= ((hha.y >> s) & 0x01010101u) << 4;
-        a1 |= ((hhb.x >> s) & 0x01010101u) << 4;
-        a3 |= ((hhb.y >> s) & 0x01010101u) << 4;
+        a0 |= ((r.hha.x >> s) & 0x01010101u) << 4;
+        a2 |= ((r.hha.y >> s) & 0x01010101u) << 4;
+        a1 |= ((r.hhb.x >> s) & 0x01010101u) << 4;
+        a3 |= ((r.hhb.y >> s) & 0x01010101u) << 4;
       }
       int p[4] = {0, 0, 0, 0};
       mma_u8s8_k32(p, a0, a1, a2, a3, w32(bw[s / 2], (s % 2) * 2), w32(bw[s / 2], (s % 2) * 2 + 1));
@@ -72,8 +111,8 @@ __device__ __forceinline__ void chunk_q45(const QmvJob& jb, const uint8_t* wa, c
       isum[2] += scB[s] * p[2];
       isum[3] += scB[s] * p[3];
     }
-    const float wdA = h2f(ha.x & 0xffff), wdminA = h2f(ha.x >> 16);
-    const float wdB = h2f(hb.x & 0xffff), wdminB = h2f(hb.x >> 16);
+    const float wdA = h2f(r.ha.x & 0xffff), wdminA = h2f(r.ha.x >> 16);
+    const float wdB = h2f(r.hb.x & 0xffff), wdminB = h2f(r.hb.x >> 16);
 #pragma unroll
     for (int c = 0; c < 2; c++) {
       float yd = 0.f;
@@ -94,7 +133,7 @@ __device__ __forceinline__ void chunk_q45(const QmvJob& jb, const uint8_t* wa, c
       f.accm[2 + c] = fmaf(__fmul_rn(yd, wdminB), __int2float_rn(msB), f.accm[2 + c]);
     }
   }
-}
+};
 
 // ---------------------------------------------------------------------- Q6_K
 __device__ __forceinline__ uint32_t q6_a(uint32_t qlw, uint32_t qhw, int q) {
@@ -105,36 +144,43 @@ __device__ __forceinline__ uint32_t q6_a(uint32_t qlw, uint32_t qhw, int q) {
   return (nib | hb) ^ 0x80808080u;
 }
 
-__device__ __forceinline__ void chunk_q6(const uint8_t* wa, const uint8_t* wb, const uint8_t* bact,
-                                         ActCols ac, int nb, int b0, int b1, int tig, Frag& f) {
-  const uint8_t* dA = wa + (int64_t)nb * 208;
-  const uint8_t* dB = wb + (int64_t)nb * 208;
-  for (int b = b0; b < b1; b++) {
+struct OpsQ6 {
+  struct Regs {
+    uint4 la0, la1, lb0, lb1, hA, hB, sA, sB;
+    uint16_t dA, dB;
+  };
+  const uint8_t *wa, *wb, *bact;
+  ActCols ac;
+  int nb, tig;
+  __device__ __forceinline__ Regs load(int b) const {
+    Regs r;
     const uint8_t* ba = wa + (int64_t)b * 208;
     const uint8_t* bb = wb + (int64_t)b * 208;
-    uint4 la0 = ld_stream(ba + tig * 32), la1 = ld_stream(ba + tig * 32 + 16);
-    uint4 lb0 = ld_stream(bb + tig * 32), lb1 = ld_stream(bb + tig * 32 + 16);
-    uint4 hA = ld_stream(ba + 128 + tig * 16), hB = ld_stream(bb + 128 + tig * 16);
-    uint4 sA = ld_stream(ba + 192), sB = ld_stream(bb + 192);
+    r.la0 = ld_stream(ba + tig * 32);
+    r.la1 = ld_stream(ba + tig * 32 + 16);
+    r.lb0 = ld_stream(bb + tig * 32);
+    r.lb1 = ld_stream(bb + tig * 32 + 16);
+    r.hA = ld_stream(ba + 128 + tig * 16);
+    r.hB = ld_stream(bb + 128 + tig * 16);
+    r.sA = ld_stream(ba + 192);
+    r.sB = ld_stream(bb + 192);
+    r.dA = *reinterpret_cast<const uint16_t*>(wa + (int64_t)nb * 208 + 2 * b);
+    r.dB = *reinterpret_cast<const uint16_t*>(wb + (int64_t)nb * 208 + 2 * b);
+    return r;
+  }
+  __device__ __forceinline__ void compute(const Regs& r, int b, Frag& f) const {
     uint4 bw[4];
-    if (bact) {
-#pragma unroll
-      for (int i = 0; i < 4; i++)
-        bw[i] = *reinterpret_cast<const uint4*>(bact + (int64_t)b * 256 + tig * 64 + i * 16);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 4; i++) bw[i] = make_uint4(0, 0, 0, 0);
-    }
-    const int8_t* scA = reinterpret_cast<const int8_t*>(&sA);
-    const int8_t* scB = reinterpret_cast<const int8_t*>(&sB);
+    load_act(bw, bact, b, tig);
+    const int8_t* scA = reinterpret_cast<const int8_t*>(&r.sA);
+    const int8_t* scB = reinterpret_cast<const int8_t*>(&r.sB);
     int isum[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int s16 = 0; s16 < 16; s16++) {
       const int half = s16 / 8, q = s16 % 8, c = q % 4, c2 = q % 2;
-      const uint4& la = half ? la1 : la0;
-      const uint4& lb = half ? lb1 : lb0;
-      uint32_t a0 = q6_a(w32(la, c), w32(hA, half * 2 + c2), q);
-      uint32_t a1 = q6_a(w32(lb, c), w32(hB, half * 2 + c2), q);
+      const uint4& la = half ? r.la1 : r.la0;
+      const uint4& lb = half ? r.lb1 : r.lb0;
+      uint32_t a0 = q6_a(w32(la, c), w32(r.hA, half * 2 + c2), q);
+      uint32_t a1 = q6_a(w32(lb, c), w32(r.hB, half * 2 + c2), q);
       int p[4] = {0, 0, 0, 0};
       mma_s8s8_k16(p, a0, a1, w32(bw[s16 / 4], s16 % 4));
       isum[0] += scA[s16] * p[0];
@@ -142,8 +188,7 @@ __device__ __forceinline__ void chunk_q6(const uint8_t* wa, const uint8_t* wb, c
       isum[2] += scB[s16] * p[2];
       isum[3] += scB[s16] * p[3];
     }
-    const float wdA = h2f(*reinterpret_cast<const uint16_t*>(dA + 2 * b));
-    const float wdB = h2f(*reinterpret_cast<const uint16_t*>(dB + 2 * b));
+    const float wdA = h2f(r.dA), wdB = h2f(r.dB);
 #pragma unroll
     for (int c = 0; c < 2; c++) {
       float yd = ac.c[c] ? *reinterpret_cast<const float*>(ac.c[c] + (int64_t)nb * 256 + b * 4) : 0.f;
@@ -151,18 +196,28 @@ __device__ __forceinline__ void chunk_q6(const uint8_t* wa, const uint8_t* wb, c
       f.acc[2 + c] = fmaf(__fmul_rn(yd, wdB), __int2float_rn(isum[2 + c] >> 2), f.acc[2 + c]);
     }
   }
-}
+};
 
 // ---------------------------------------------------------------------- Q8_0
-__device__ __forceinline__ void chunk_q80(const uint8_t* wa, const uint8_t* wb, const uint8_t* bact,
-                                          ActCols ac, int nb, int u0, int u1, int tig, Frag& f) {
-  const uint8_t* dA = wa + (int64_t)nb * 32;
-  const uint8_t* dB = wb + (int64_t)nb * 32;
-  for (int g = u0; g < u1; g++) {
-    uint4 qa0 = ld_stream(wa + (int64_t)g * 128 + tig * 32), qa1 = ld_stream(wa + (int64_t)g * 128 + tig * 32 + 16);
-    uint4 qb0 = ld_stream(wb + (int64_t)g * 128 + tig * 32), qb1 = ld_stream(wb + (int64_t)g * 128 + tig * 32 + 16);
-    uint2 dwa = *reinterpret_cast<const uint2*>(dA + 8 * g);
-    uint2 dwb = *reinterpret_cast<const uint2*>(dB + 8 * g);
+struct OpsQ80 {
+  struct Regs {
+    uint4 qa0, qa1, qb0, qb1;
+    uint2 dwa, dwb;
+  };
+  const uint8_t *wa, *wb, *bact;
+  ActCols ac;
+  int nb, tig;
+  __device__ __forceinline__ Regs load(int g) const {
+    Regs r;
+    r.qa0 = ld_stream(wa + (int64_t)g * 128 + tig * 32);
+    r.qa1 = ld_stream(wa + (int64_t)g * 128 + tig * 32 + 16);
+    r.qb0 = ld_stream(wb + (int64_t)g * 128 + tig * 32);
+    r.qb1 = ld_stream(wb + (int64_t)g * 128 + tig * 32 + 16);
+    r.dwa = *reinterpret_cast<const uint2*>(wa + (int64_t)nb * 32 + 8 * g);
+    r.dwb = *reinterpret_cast<const uint2*>(wb + (int64_t)nb * 32 + 8 * g);
+    return r;
+  }
+  __device__ __forceinline__ void compute(const Regs& r, int g, Frag& f) const {
     uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
     if (bact) {
       x0 = *reinterpret_cast<const uint4*>(bact + (int64_t)g * 128 + tig * 32);
@@ -175,13 +230,13 @@ __device__ __forceinline__ void chunk_q80(const uint8_t* wa, const uint8_t* wb, 
                       : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int bb = 0; bb < 4; bb++) {
-      const uint4& qa = bb < 2 ? qa0 : qa1;
-      const uint4& qb = bb < 2 ? qb0 : qb1;
+      const uint4& qa = bb < 2 ? r.qa0 : r.qa1;
+      const uint4& qb = bb < 2 ? r.qb0 : r.qb1;
       const uint4& xx = bb < 2 ? x0 : x1;
       const int o = (bb % 2) * 2;
       int p[4] = {0, 0, 0, 0};
       mma_s8s8_k32(p, w32(qa, o), w32(qb, o), w32(qa, o + 1), w32(qb, o + 1), w32(xx, o), w32(xx, o + 1));
-      const uint32_t hwa = bb < 2 ? dwa.x : dwa.y, hwb = bb < 2 ? dwb.x : dwb.y;
+      const uint32_t hwa = bb < 2 ? r.dwa.x : r.dwa.y, hwb = bb < 2 ? r.dwb.x : r.dwb.y;
       const float wdA = h2f((bb & 1) ? hwa >> 16 : hwa & 0xffff);
       const float wdB = h2f((bb & 1) ? hwb >> 16 : hwb & 0xffff);
 #pragma unroll
@@ -192,11 +247,12 @@ __device__ __forceinline__ void chunk_q80(const uint8_t* wa, const uint8_t* wb, 
       }
     }
   }
-}
+};
 
-__global__ void __launch_bounds__(256) qmv_kernel(const QmvJob* __restrict__ jobs, int njobs,
-                                                  const int* __restrict__ dyn_count) {
+__global__ void __launch_bounds__(256, QMV_MIN_BLOCKS) qmv_kernel(const QmvJob* __restrict__ jobs, int njobs,
+                                                                  const int* __restrict__ dyn_count) {
   __shared__ float part[8][32][4];
+  extern __shared__ __align__(16) uint8_t act_smem[];
   if (dyn_count) {
     pdl_wait();
     njobs = *dyn_count;
@@ -204,7 +260,10 @@ __global__ void __launch_bounds__(256) qmv_kernel(const QmvJob* __restrict__ job
   const int tile = blockIdx.x;
   // locate the job: the last one with tile0 <= tile
   int lo = 0, hi = njobs - 1;
-  if (njobs <= 0) return;
+  if (njobs <= 0) {
+    pdl_wait();  // every CTA waits once, so completion order stays transitive
+    return;
+  }
   while (lo < hi) {
     int mid = (lo + hi + 1) >> 1;
     if (jobs[mid].tile0 <= tile) lo = mid; else hi = mid - 1;
@@ -212,7 +271,10 @@ __global__ void __launch_bounds__(256) qmv_kernel(const QmvJob* __restrict__ job
   const QmvJob& jb = jobs[lo];
   const int ks = jb.ksplit;
   const int local = tile - jb.tile0;
-  if (local * qmv_rows_per_cta(ks) >= jb.rows) return;  // past the job table's end
+  if (local * qmv_rows_per_cta(ks) >= jb.rows) {  // past the job table's end
+    pdl_wait();
+    return;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
   const int rt = warp / ks, chunk = warp % ks;
@@ -222,29 +284,38 @@ __global__ void __launch_bounds__(256) qmv_kernel(const QmvJob* __restrict__ job
   const int nb = jb.cols / gguf_block_elems(dt);
   const int units = qmv_units(dt, jb.cols);
   const int u0 = chunk * units / ks, u1 = (chunk + 1) * units / ks;
-
-  if (!dyn_count) pdl_wait();  // activations come from the previous kernel
-  pdl_trigger();
+  const int arb = jb.act_row_bytes;
+  const int n = jb.n;
 
   Frag f;
 #pragma unroll
   for (int i = 0; i < 4; i++) { f.acc[i] = 0.f; f.accm[i] = 0.f; }
-  if (warp_live) {
-    const int ra = min(row0 + gid, jb.rows - 1), rb = min(row0 + gid + 8, jb.rows - 1);
-    const uint8_t* wa = jb.w + (int64_t)ra * jb.w_row_bytes;
-    const uint8_t* wb = jb.w + (int64_t)rb * jb.w_row_bytes;
-    const uint8_t* bact = gid < jb.n ? jb.act + (int64_t)jb.rowmap[gid] * jb.act_row_bytes : nullptr;
-    ActCols ac;
-    ac.c[0] = 2 * tig < jb.n ? jb.act + (int64_t)jb.rowmap[2 * tig] * jb.act_row_bytes : nullptr;
-    ac.c[1] = 2 * tig + 1 < jb.n ? jb.act + (int64_t)jb.rowmap[2 * tig + 1] * jb.act_row_bytes : nullptr;
-    switch (dt) {
-      case Q4_K: chunk_q45<Q4_K>(jb, wa, wb, bact, ac, nb, u0, u1, tig, f); break;
-      case Q5_K: chunk_q45<Q5_K>(jb, wa, wb, bact, ac, nb, u0, u1, tig, f); break;
-      case Q6_K: chunk_q6(wa, wb, bact, ac, nb, u0, u1, tig, f); break;
-      case Q8_0: chunk_q80(wa, wb, bact, ac, nb, u0, u1, tig, f); break;
-      default: break;
+  const int ra = min(row0 + gid, jb.rows - 1), rb = min(row0 + gid + 8, jb.rows - 1);
+  const uint8_t* wa = jb.w + (int64_t)ra * jb.w_row_bytes;
+  const uint8_t* wb = jb.w + (int64_t)rb * jb.w_row_bytes;
+  // The activation rows this job reads, staged once per CTA after the wait.
+  auto stage = [&]() {
+    pdl_wait();
+    const int words = arb / 16;
+    for (int i = threadIdx.x; i < n * words; i += 256) {
+      const int r = i / words, w = i % words;
+      reinterpret_cast<uint4*>(act_smem)[i] =
+          *reinterpret_cast<const uint4*>(jb.act + (int64_t)jb.rowmap[r] * arb + 16 * w);
     }
+    __syncthreads();
+  };
+  const uint8_t* bact = gid < n ? act_smem + gid * arb : nullptr;
+  ActCols ac;
+  ac.c[0] = 2 * tig < n ? act_smem + 2 * tig * arb : nullptr;
+  ac.c[1] = 2 * tig + 1 < n ? act_smem + (2 * tig + 1) * arb : nullptr;
+  const bool live = warp_live && u0 < u1;
+  switch (dt) {
+    case Q4_K: run_chunk(OpsQ45<Q4_K>{wa, wb, bact, ac, nb, tig}, u0, u1, live, stage, f); break;
+    case Q5_K: run_chunk(OpsQ45<Q5_K>{wa, wb, bact, ac, nb, tig}, u0, u1, live, stage, f); break;
+    case Q6_K: run_chunk(OpsQ6{wa, wb, bact, ac, nb, tig}, u0, u1, live, stage, f); break;
+    default: run_chunk(OpsQ80{wa, wb, bact, ac, nb, tig}, u0, u1, live, stage, f); break;
   }
+  pdl_trigger();
   const bool has_min = dt == Q4_K || dt == Q5_K;
 #pragma unroll
   for (int i = 0; i < 4; i++) part[warp][lane][i] = has_min ? __fsub_rn(f.acc[i], f.accm[i]) : f.acc[i];
@@ -260,7 +331,7 @@ __global__ void __launch_bounds__(256) qmv_kernel(const QmvJob* __restrict__ job
   for (int i = 0; i < 4; i++) {
     const int row = row0 + gid + (i >= 2 ? 8 : 0);
     const int col = 2 * tig + (i & 1);
-    if (row >= jb.rows || col >= jb.n) continue;
+    if (row >= jb.rows || col >= n) continue;
     const int64_t o = (int64_t)jb.outrow[col] * jb.out_ld + row;
     float v = y[i];
     if (jb.epi == kEpiResidual) v = __fadd_rn(jb.resid[o], v);
@@ -270,12 +341,18 @@ __global__ void __launch_bounds__(256) qmv_kernel(const QmvJob* __restrict__ job
 
 }  // namespace
 
-cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int ntiles,
+cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int ntiles, int smem_bytes,
                        cudaStream_t stream, bool pdl) {
   if (ntiles <= 0) return cudaSuccess;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(qmv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kQmvMaxActSmem);
+    configured = true;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ntiles);
   cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -33,7 +33,7 @@ struct QmvJob {
   int n;                 // input rows used, 1..8
   int tile0;             // first global tile of this job
   int epi;
-  int8_t rowmap[8];      // activation row of input column i
+  uint8_t rowmap[8];     // activation row of input column i
   int16_t outrow[8];     // output row (of out) of input column i
 };
 
@@ -58,7 +58,9 @@ inline int qmv_tiles(const QmvJob& j) {
 // When `dyn_count` is non-null the job count is read on the device after the
 // programmatic-dependency wait (jobs written by the previous kernel), and
 // CTAs past the last job's tiles exit.
-cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int ntiles,
+// `smem_bytes` must cover n * act_row_bytes of every job in the table.
+constexpr int kQmvMaxActSmem = 64 * 1024;
+cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int ntiles, int smem_bytes,
                        cudaStream_t stream, bool pdl);
 
 }  // namespace iq
