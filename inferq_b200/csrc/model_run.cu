@@ -62,7 +62,13 @@ struct iq_state {
   iq::DevBuf jobs;
   std::vector<iq::KPlan> plans;  // index k-1
   int* union_dev = nullptr;      // counts + 4*layer + 2
+  // one captured graph per (mode, rows): [verify][k-1]
+  cudaGraphExec_t graphs[2][8] = {};
+  int eager_runs[2][8] = {};
   ~iq_state() {
+    for (auto& row : graphs)
+      for (auto& g : row)
+        if (g) cudaGraphExecDestroy(g);
     if (h_result) cudaFreeHost(h_result);
     if (h_tokens) cudaFreeHost(h_tokens);
     if (st) cudaStreamDestroy(st);
@@ -504,6 +510,31 @@ int run_pass(iq_state* s, int k, bool verify) {
   return IQ_OK;
 }
 
+// Run a pass through its CUDA graph: the first call of each (mode, rows)
+// runs eagerly (so lazily configured kernel attributes are set outside any
+// capture), the second captures the launch sequence, later calls replay it.
+int run_pass_graph(iq_state* s, int k, bool verify) {
+  const int v = verify ? 1 : 0;
+  cudaGraphExec_t& ge = s->graphs[v][k - 1];
+  if (!ge) {
+    if (s->eager_runs[v][k - 1]++ == 0) return run_pass(s, k, verify);
+    cudaGraph_t g = nullptr;
+    IQ_CUDA(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+    int rc = run_pass(s, k, verify);
+    cudaError_t e = cudaStreamEndCapture(s->st, &g);
+    if (rc) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    IQ_CUDA(e);
+    e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    IQ_CUDA(e);
+  }
+  IQ_CUDA(cudaGraphLaunch(ge, s->st));
+  return IQ_OK;
+}
+
 int alloc_state(iq_state* s) {
   iq_model* m = s->m;
   const iq_config& c = m->cfg;
@@ -676,7 +707,7 @@ int iq_forward(iq_state* s, const uint32_t* tokens, int rows, float* logits, flo
     const int k = std::min(kMaxK, rows - r0);
     IQ_CUDA(cudaStreamSynchronize(s->st));  // h_tokens is reused
     for (int i = 0; i < k; i++) s->h_tokens[i] = (int32_t)tokens[r0 + i];
-    int rc = run_pass(s, k, false);
+    int rc = run_pass_graph(s, k, false);
     if (rc) return rc;
     rc = copy_out(s, k, r0, logits, hidden, argmax);
     if (rc) return rc;
@@ -699,7 +730,7 @@ int iq_verify(iq_state* s, const uint32_t* tokens, int rows, iq_verify_result* o
     IQ_CHECK(tokens[i] < (uint32_t)V, IQ_EINVAL, "token %u outside the vocabulary of %d", tokens[i], V);
   IQ_CUDA(cudaStreamSynchronize(s->st));
   for (int i = 0; i < rows; i++) s->h_tokens[i] = (int32_t)tokens[i];
-  int rc = run_pass(s, rows, true);
+  int rc = run_pass_graph(s, rows, true);
   if (rc) return rc;
   rc = copy_out(s, rows, 0, logits, hidden, nullptr);
   if (rc) return rc;
