@@ -189,6 +189,18 @@ int iq_rollback(iq_state* s, int committed_rows);
  * the measured expert union that sets the pass's algorithmic bytes. */
 int iq_state_union_sizes(const iq_state* s, int32_t* per_layer);
 
+/* Routed experts of the last pass: [layer][row][top_k], `rows` = that
+ * pass's rows (the routes of QuantizedMoeOutput, quantized_moe.rs:227-281). */
+int iq_state_routes(const iq_state* s, int rows, int32_t* experts);
+
+/* Stage timers (the reference threads wall-clock stage timers through every
+ * layer, QuantizedForwardTimings, quantized_model.rs:305-401).  With
+ * profiling on, passes run without graphs or programmatic overlap and every
+ * stage is bracketed by CUDA events.  iq_state_profile writes
+ * "stage count total_us" lines into buf and returns their length. */
+int iq_state_set_profiling(iq_state* s, int on);
+int iq_state_profile(const iq_state* s, char* buf, int len);
+
 #ifdef __cplusplus
 }
 #endif

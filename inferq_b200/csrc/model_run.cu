@@ -8,6 +8,7 @@
 // launch, and the whole pass is captured once per row count into a CUDA graph.
 #include <algorithm>
 #include <cstring>
+#include <string>
 #include "model.h"
 
 namespace iq {
@@ -62,6 +63,10 @@ struct iq_state {
   iq::DevBuf jobs;
   std::vector<iq::KPlan> plans;  // index k-1
   int* union_dev = nullptr;      // counts + 4*layer + 2
+  // stage profiling (iq_state_set_profiling): events and accumulated times
+  bool profiling = false;
+  std::vector<std::pair<std::string, cudaEvent_t>> marks;
+  std::vector<std::pair<std::string, std::pair<int, double>>> prof;
   // one captured graph per (mode, rows): [verify][k-1]
   cudaGraphExec_t graphs[2][8] = {};
   int eager_runs[2][8] = {};
@@ -132,8 +137,16 @@ struct Ctx {
   iq_model* m;
   const iq_config& c;
   cudaStream_t st;
-  bool pdl = true;
-  Ctx(iq_state* s_) : s(s_), m(s_->m), c(s_->m->cfg), st(s_->st) {}
+  bool pdl;
+  Ctx(iq_state* s_) : s(s_), m(s_->m), c(s_->m->cfg), st(s_->st), pdl(!s_->profiling) {}
+  // Stage timer: under profiling every stage is bracketed by CUDA events.
+  void mark(const char* name) {
+    if (!s->profiling) return;
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    cudaEventRecord(e, st);
+    s->marks.emplace_back(name, e);
+  }
   int* pos() const { return s->ctrl.as<int>(); }
   int* sel() const { return s->ctrl.as<int>() + 1; }
   int* result() const { return s->ctrl.as<int>() + 2; }
@@ -228,12 +241,16 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   const bool q8k = needs(W.gate.dt, false) || needs(W.sh_gate.dt, false) || needs(W.router.dt, false);
   const bool q80 = needs(W.gate.dt, true) || needs(W.sh_gate.dt, true) || needs(W.router.dt, true);
   TRY(prep(x, s->hidden.as<float>(), H, H, L.post_norm.p(), k, q8k, q80, s->xn.as<float>()));
+  x.mark("moe.prep");
   float* lg = s->logits_moe.as<float>();
   if (W.router.present()) {
     TRY(qmv(x, R.router));
+  x.mark("moe.router");
     IQ_CUDA(f32_matvec(W.selector.p(), 1, H, s->xn.as<float>(), H, k, lg + E, E + 1, x.st, x.pdl));
+  x.mark("moe.router");
   } else {
     IQ_CUDA(f32_matvec(W.router_sel.p(), E + 1, H, s->xn.as<float>(), H, k, lg, E + 1, x.st, x.pdl));
+  x.mark("moe.router");
   }
   MoeRouteArgs a = {};
   a.logits = lg;
@@ -245,7 +262,7 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   a.hidden = H;
   a.ffn = c.moe_intermediate_size;
   a.sh_ffn = c.shared_expert_intermediate_size;
-  a.route_expert = s->route_e.as<int>();
+  a.route_expert = s->route_e.as<int>() + (int64_t)layer_index * kMaxK * c.num_experts_per_tok;
   a.route_weight = s->route_w.as<float>();
   a.gu_jobs = s->gu_jobs.as<QmvJob>();
   a.down_jobs = s->down_jobs.as<QmvJob>();
@@ -294,6 +311,7 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   t.expert_lo = W.expert_lo;
   t.expert_hi = W.expert_hi;
   IQ_CUDA(moe_route_launch(a, t, x.st, x.pdl));
+  x.mark("moe.route");
   // upper bounds on the dynamic job tables' tiles
   const int max_union = std::min(W.expert_hi - W.expert_lo, k * c.num_experts_per_tok);
   const int gu_tiles = 2 * max_union * t.tiles_gate + 2 * t.tiles_sh_gate;
@@ -301,6 +319,7 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   const int down_tiles = max_union * t.tiles_down + tiles_sh_down;
   const int gu_smem = k * (int)std::max(s->act8k_bytes, s->act80_bytes);
   IQ_CUDA(qmv_launch(a.gu_jobs, 0, a.gu_count, gu_tiles, gu_smem, x.st, x.pdl));
+  x.mark("moe.gate_up");
   MoeActArgs b = {};
   b.gu = a.gu_out;
   b.gu_ld = a.gu_ld;
@@ -316,7 +335,9 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   b.down_q80 = W.down.dt == Q8_0;
   b.sh_down_q80 = W.sh_down.dt == Q8_0;
   IQ_CUDA(moe_act_launch(b, x.st, x.pdl));
+  x.mark("moe.act");
   IQ_CUDA(qmv_launch(a.down_jobs, 0, a.down_count, down_tiles, 8 * (int)s->act_mid_bytes, x.st, x.pdl));
+  x.mark("moe.down");
   // expert parallelism: the all-gather of y happens here (model_ep.cu)
   MoeCombineArgs cb = {};
   cb.y = a.y;
@@ -331,6 +352,7 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   cb.topk = c.num_experts_per_tok;
   cb.dim = H;
   IQ_CUDA(moe_combine_launch(cb, x.st, x.pdl));
+  x.mark("moe.combine");
   return IQ_OK;
 }
 
@@ -345,7 +367,9 @@ int run_delta(Ctx& x, const Layer& L, const LayerRec& R, int k, int li) {
   const bool q8k = needs(D.qkv.dt, false) || needs(D.z.dt, false) || needs(bdt, false);
   const bool q80 = needs(D.qkv.dt, true) || needs(D.z.dt, true) || needs(bdt, true);
   TRY(prep(x, s->hidden.as<float>(), H, H, L.attn_norm.p(), k, q8k, q80, nullptr));
+  x.mark("dn.prep");
   TRY(qmv(x, R.proj));
+  x.mark("dn.proj");
   DeltaNetArgs a = {};
   a.layers = s->dn_layers.as<DeltaNetLayer>() + li;
   a.qkv = s->dn_qkv[li].as<float>();
@@ -366,6 +390,7 @@ int run_delta(Ctx& x, const Layer& L, const LayerRec& R, int k, int li) {
   a.committed = x.result() + 2;
   a.replay = 0;
   IQ_CUDA(deltanet_launch(a, 1, x.st, x.pdl));
+  x.mark("dn.recurrence");
   GatedNormArgs g = {};
   g.o = s->dn_out.as<float>();
   g.o_ld = vdim;
@@ -381,7 +406,9 @@ int run_delta(Ctx& x, const Layer& L, const LayerRec& R, int k, int li) {
   g.q8k_stride = (int)s->act8k_bytes;
   g.q80_stride = (int)s->act80_bytes;
   IQ_CUDA(gated_norm_launch(g, k, x.st, x.pdl));
+  x.mark("dn.gated_norm");
   TRY(qmv(x, R.out));
+  x.mark("dn.out");
   return IQ_OK;
 }
 
@@ -394,7 +421,9 @@ int run_attention(Ctx& x, const Layer& L, const LayerRec& R, int k, int fi) {
   const bool q8k = needs(A.q.dt, false) || needs(A.k.dt, false) || needs(A.v.dt, false);
   const bool q80 = needs(A.q.dt, true) || needs(A.k.dt, true) || needs(A.v.dt, true);
   TRY(prep(x, s->hidden.as<float>(), H, H, L.attn_norm.p(), k, q8k, q80, nullptr));
+  x.mark("attn.prep_norm");
   TRY(qmv(x, R.proj));
+  x.mark("attn.proj");
   AttnArgs a = {};
   a.qg = s->qg.as<float>();
   a.qg_ld = 2 * nhd;
@@ -420,10 +449,15 @@ int run_attention(Ctx& x, const Layer& L, const LayerRec& R, int k, int fi) {
   a.pos = x.pos();
   a.chunk_ctas = 16;
   IQ_CUDA(attn_prep_launch(a, x.st, x.pdl));
+  x.mark("attn.prep");
   IQ_CUDA(attn_scan_launch(a, x.st, x.pdl));
+  x.mark("attn.scan");
   IQ_CUDA(attn_combine_launch(a, x.st, x.pdl));
+  x.mark("attn.combine");
   TRY(prep(x, s->attn_out.as<float>(), nhd, nhd, nullptr, k, needs(A.o.dt, false), needs(A.o.dt, true), nullptr));
+  x.mark("attn.out_prep");
   TRY(qmv(x, R.out));
+  x.mark("attn.out");
   return IQ_OK;
 }
 
@@ -465,6 +499,7 @@ int replay_all(Ctx& x, int k) {
     a.committed = x.result() + 2;
     a.replay = 1;
     IQ_CUDA(deltanet_launch(a, 1, x.st, x.pdl));
+  x.mark("dn.recurrence");
   }
   return IQ_OK;
 }
@@ -479,6 +514,7 @@ int run_pass(iq_state* s, int k, bool verify) {
   IQ_CUDA(cudaMemcpyAsync(s->tokens.p, s->h_tokens, k * sizeof(int32_t), cudaMemcpyHostToDevice, x.st));
   IQ_CUDA(embed_launch(m->embed.dt, m->embed.p(), m->embed.row_bytes, H, s->tokens.as<int32_t>(), k,
                        s->hidden.as<float>(), H, x.st, x.pdl));
+  x.mark("embed");
   int li = 0, fi = 0;
   for (int l = 0; l < c.num_hidden_layers; l++) {
     const Layer& L = m->layers[l];
@@ -488,7 +524,9 @@ int run_pass(iq_state* s, int k, bool verify) {
   }
   TRY(prep(x, s->hidden.as<float>(), H, H, m->out_norm.p(), k, needs(m->lm_head.dt, false),
            needs(m->lm_head.dt, true), s->xn.as<float>()));
+  x.mark("head.prep");
   TRY(qmv(x, P.lm_head));
+  x.mark("head.lm_head");
   HeadArgs h = {};
   h.logits = s->logits.as<float>();
   h.logits_ld = c.vocab_size;
@@ -503,9 +541,13 @@ int run_pass(iq_state* s, int k, bool verify) {
   h.result = x.result();
   h.scores = nullptr;
   IQ_CUDA(argmax_launch(h, x.st, x.pdl));
+  x.mark("head.argmax");
   IQ_CUDA(accept_launch(h, x.st, x.pdl));
+  x.mark("head.accept");
   if (verify) TRY(replay_all(x, k));
+  x.mark("head.replay");
   IQ_CUDA(commit_launch(x.sel(), x.pos(), x.result(), x.st, x.pdl));
+  x.mark("head.commit");
   IQ_CUDA(cudaMemcpyAsync(s->h_result, x.result(), 4 * sizeof(int), cudaMemcpyDeviceToHost, x.st));
   return IQ_OK;
 }
@@ -514,6 +556,11 @@ int run_pass(iq_state* s, int k, bool verify) {
 // runs eagerly (so lazily configured kernel attributes are set outside any
 // capture), the second captures the launch sequence, later calls replay it.
 int run_pass_graph(iq_state* s, int k, bool verify) {
+  if (s->profiling) {
+    Ctx x(s);
+    x.mark("start");
+    return run_pass(s, k, verify);
+  }
   const int v = verify ? 1 : 0;
   cudaGraphExec_t& ge = s->graphs[v][k - 1];
   if (!ge) {
@@ -533,6 +580,20 @@ int run_pass_graph(iq_state* s, int k, bool verify) {
   }
   IQ_CUDA(cudaGraphLaunch(ge, s->st));
   return IQ_OK;
+}
+
+// Fold the recorded stage events into per-stage totals (call after a sync).
+void collect_marks(iq_state* s) {
+  for (size_t i = 1; i < s->marks.size(); i++) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, s->marks[i - 1].second, s->marks[i].second);
+    const std::string& name = s->marks[i].first == "start" ? std::string("host.gap") : s->marks[i].first;
+    auto it = std::find_if(s->prof.begin(), s->prof.end(), [&](auto& p) { return p.first == name; });
+    if (it == s->prof.end()) s->prof.push_back({name, {1, ms * 1000.0}});
+    else { it->second.first++; it->second.second += ms * 1000.0; }
+  }
+  for (auto& m : s->marks) cudaEventDestroy(m.second);
+  s->marks.clear();
 }
 
 int alloc_state(iq_state* s) {
@@ -605,7 +666,7 @@ int alloc_state(iq_state* s) {
   IQ_CUDA(s->part.reserve((size_t)K * c.num_attention_heads * s->max_chunks * (c.head_dim + 2) * 4));
   const int64_t slots = K * topk + K;
   IQ_CUDA(s->logits_moe.reserve(K * (E + 1) * 4));
-  IQ_CUDA(s->route_e.reserve(K * topk * 4));
+  IQ_CUDA(s->route_e.reserve((c.num_hidden_layers + 1) * K * topk * 4));
   IQ_CUDA(s->route_w.reserve(K * topk * 4));
   IQ_CUDA(s->gu_jobs.reserve((2 * E + 2) * sizeof(QmvJob)));
   IQ_CUDA(s->down_jobs.reserve((E + 1) * sizeof(QmvJob)));
@@ -715,6 +776,7 @@ int iq_forward(iq_state* s, const uint32_t* tokens, int rows, float* logits, flo
     s->last_rows = k;
   }
   IQ_CUDA(cudaStreamSynchronize(s->st));
+  if (s->profiling) collect_marks(s);
   s->can_rollback = true;
   return IQ_OK;
 }
@@ -735,6 +797,7 @@ int iq_verify(iq_state* s, const uint32_t* tokens, int rows, iq_verify_result* o
   rc = copy_out(s, rows, 0, logits, hidden, nullptr);
   if (rc) return rc;
   IQ_CUDA(cudaStreamSynchronize(s->st));
+  if (s->profiling) collect_marks(s);
   out->accepted = s->h_result[0];
   out->authoritative = s->h_result[1];
   out->committed = s->h_result[2];
@@ -766,6 +829,40 @@ int iq_state_union_sizes(const iq_state* s, int32_t* per_layer) {
   IQ_CHECK(s && per_layer, IQ_EINVAL, "iq_state_union_sizes: null argument");
   IQ_CUDA(cudaStreamSynchronize(s->st));
   IQ_CUDA(cudaMemcpy(per_layer, s->counts.as<int>() + 4, s->m->cfg.num_hidden_layers * 4, cudaMemcpyDeviceToHost));
+  return IQ_OK;
+}
+
+int iq_state_set_profiling(iq_state* s, int on) {
+  IQ_CHECK(s, IQ_EINVAL, "iq_state_set_profiling: null state");
+  IQ_CUDA(cudaStreamSynchronize(s->st));
+  for (auto& m : s->marks) cudaEventDestroy(m.second);
+  s->marks.clear();
+  s->prof.clear();
+  s->profiling = on != 0;
+  return IQ_OK;
+}
+
+int iq_state_profile(const iq_state* s, char* buf, int len) {
+  IQ_CHECK(s && buf && len > 0, IQ_EINVAL, "iq_state_profile: null argument");
+  std::string out;
+  char line[256];
+  for (auto& p : s->prof) {
+    snprintf(line, sizeof line, "%s %d %.3f\n", p.first.c_str(), p.second.first, p.second.second);
+    out += line;
+  }
+  snprintf(buf, (size_t)len, "%s", out.c_str());
+  return (int)out.size();
+}
+
+int iq_state_routes(const iq_state* s, int rows, int32_t* experts) {
+  IQ_CHECK(s && experts, IQ_EINVAL, "iq_state_routes: null argument");
+  IQ_CHECK(rows >= 1 && rows <= kMaxK, IQ_EINVAL, "rows must be 1..%d", kMaxK);
+  const iq_config& c = s->m->cfg;
+  IQ_CUDA(cudaStreamSynchronize(s->st));
+  for (int l = 0; l < c.num_hidden_layers; l++)
+    IQ_CUDA(cudaMemcpy(experts + (int64_t)l * rows * c.num_experts_per_tok,
+                       s->route_e.as<int>() + (int64_t)l * kMaxK * c.num_experts_per_tok,
+                       (size_t)rows * c.num_experts_per_tok * 4, cudaMemcpyDeviceToHost));
   return IQ_OK;
 }
 

@@ -51,6 +51,9 @@ def _declare(L):
         "iq_verify": (ctypes.c_int, [P, P, ctypes.c_int, ctypes.POINTER(IqVerifyResult), P, P]),
         "iq_rollback": (ctypes.c_int, [P, ctypes.c_int]),
         "iq_state_union_sizes": (ctypes.c_int, [P, P]),
+        "iq_state_routes": (ctypes.c_int, [P, ctypes.c_int, P]),
+        "iq_state_set_profiling": (ctypes.c_int, [P, ctypes.c_int]),
+        "iq_state_profile": (ctypes.c_int, [P, ctypes.c_char_p, ctypes.c_int]),
     }
     for n, (r, a) in sig.items():
         f = getattr(L, n)
@@ -160,6 +163,24 @@ class State:
     def union_sizes(self) -> np.ndarray:
         out = np.zeros(self.model.cfg.num_hidden_layers, np.int32)
         _lib.check(lib().iq_state_union_sizes(self._h, out.ctypes.data))
+        return out
+
+    def routes(self, rows: int) -> np.ndarray:
+        c = self.model.cfg
+        out = np.zeros((c.num_hidden_layers, rows, c.num_experts_per_tok), np.int32)
+        _lib.check(lib().iq_state_routes(self._h, rows, out.ctypes.data))
+        return out
+
+    def set_profiling(self, on: bool):
+        _lib.check(lib().iq_state_set_profiling(self._h, int(on)))
+
+    def profile(self) -> dict:
+        buf = ctypes.create_string_buffer(1 << 16)
+        _lib.check(lib().iq_state_profile(self._h, buf, len(buf)))
+        out = {}
+        for line in buf.value.decode().splitlines():
+            name, cnt, us = line.split()
+            out[name] = (int(cnt), float(us))
         return out
 
     def __del__(self):

@@ -1,0 +1,563 @@
+/*
+ * iq_oracle_model.c -- CPU restatement of the reference's quantized model
+ * forward pass, one row at a time.
+ *
+ * TEST INFRASTRUCTURE ONLY (see iq_oracle.h).  Built with -ffp-contract=off.
+ *
+ * Follows, file by file (paths in the ybrs/inferq tree):
+ *   src/qwen/quantized_model.rs:654-752   forward_inner (embed, layers, final norm, LM head)
+ *   src/qwen/quantized_layer.rs:101-236   layer wrappers, gguf_rms_norm
+ *   src/qwen/quantized_deltanet.rs:517-759 DeltaNet mixer (conv, L2 norm, beta/alpha, gated norm)
+ *   src/qwen/deltanet.rs:122-217          recurrent delta rule
+ *   src/qwen/quantized_attention.rs:155-178, 409-589, 833-851  gated attention
+ *   src/qwen/moe.rs:21-54                 softmax top-k routing
+ *   src/qwen/quantized_moe.rs:237-460     routed + shared experts, ordered accumulation
+ *   src/qwen/quantized_mtp.rs:175-227     MTP predictor block
+ * Every projection goes through or_qmatvec in the reference lane order.
+ * A multi-row pass of the reference equals its rows run one at a time
+ * (per-row matmuls, serial recurrence, causal attention), so the oracle
+ * evaluates one row per step.
+ */
+#include "iq_oracle.h"
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+typedef struct or_config {
+    int32_t hidden_size, num_hidden_layers, vocab_size;
+    int32_t num_attention_heads, num_key_value_heads, head_dim, rotary_dim;
+    int32_t linear_num_key_heads, linear_num_value_heads, linear_key_head_dim, linear_value_head_dim;
+    int32_t linear_conv_kernel_dim;
+    int32_t num_experts, num_experts_per_tok, moe_intermediate_size, shared_expert_intermediate_size;
+    int32_t full_attention_interval, mtp_num_hidden_layers, norm_topk_prob, value_heads_tiled;
+    int32_t max_position_embeddings;
+    float rms_norm_eps;
+    double rope_theta;
+} or_config;
+
+typedef struct or_tensor {
+    const char* name;
+    int32_t dtype;
+    int32_t ndim;
+    int64_t shape[4];
+    const void* data;
+    int32_t location;
+} or_tensor;
+
+typedef struct { int dt; int64_t rows, cols; const uint8_t* p; } mat_t;
+
+typedef struct {
+    int full;
+    const float *attn_norm, *post_norm;
+    /* DeltaNet */
+    mat_t qkv, z, ba, beta, alpha, out;
+    int ba_fused;
+    const float *conv_w, *ssm_a, *dt_bias, *ssm_norm;
+    /* attention */
+    mat_t q, k, v, o;
+    const float *q_norm, *k_norm;
+    /* MoE */
+    mat_t router, gate, up, down, sh_gate, sh_up, sh_down;
+    const float* selector;
+} layer_t;
+
+typedef struct or_model {
+    or_config c;
+    mat_t embed, lm_head;
+    const float* out_norm;
+    layer_t* layers;
+    int has_mtp;
+    layer_t mtp;
+    const float *enorm, *hnorm, *head_norm;
+    mat_t eh_proj;
+} or_model;
+
+typedef struct {
+    float* conv;  /* [conv_dim][K-1] */
+    float* rec;   /* [nv][dk][dv] */
+    float* keys;  /* [max_pos][nkv][hd] */
+    float* values;
+} lstate_t;
+
+typedef struct or_state {
+    int64_t position, max_pos;
+    int nlayers;
+    lstate_t* l;
+    lstate_t mtp;
+    int64_t mtp_position;
+} or_state;
+
+/* --------------------------------------------------------------- helpers */
+static const or_tensor* find(const or_tensor* t, int n, const char* name) {
+    for (int i = 0; i < n; i++)
+        if (!strcmp(t[i].name, name)) return &t[i];
+    return NULL;
+}
+static int getmat(const or_tensor* t, int n, const char* name, mat_t* m) {
+    const or_tensor* x = find(t, n, name);
+    if (!x) return -1;
+    m->dt = x->dtype;
+    m->cols = x->shape[x->ndim - 1];
+    m->rows = 1;
+    for (int i = 0; i < x->ndim - 1; i++) m->rows *= x->shape[i];
+    m->p = (const uint8_t*)x->data;
+    return 0;
+}
+static const float* getvec(const or_tensor* t, int n, const char* name) {
+    const or_tensor* x = find(t, n, name);
+    return x ? (const float*)x->data : NULL;
+}
+
+/* Accumulation order of every projection: 0 = the reference's AVX2 lane
+ * order (default), 1 = the device's block-chunk order (a diagnostic that
+ * isolates f32-order effects from everything else). */
+static int g_order = 0;
+void or_set_gemv_order(int order) { g_order = order; }
+
+/* The device's chunk count for a matrix shape (a function of shape only). */
+static int device_ksplit(int dt, int64_t rows, int64_t cols) {
+    if (dt == OR_F32) return 1;
+    int units = (int)(dt == OR_Q8_0 ? cols / 128 : cols / 256);
+    int ks = 1;
+    while (ks < 8 && units % (ks * 2) == 0 && (rows / 16) * ks < 148 * 32) ks *= 2;
+    return ks;
+}
+
+/* y[rows] = W x  (one input row) */
+static void matvec_n(const mat_t* m, const uint8_t* p, int64_t n, const float* x, float* y) {
+    or_qmatvec(m->dt, p, n, m->cols, x, 1, y, g_order, g_order ? device_ksplit(m->dt, n, m->cols) : 1);
+}
+static void matvec(const mat_t* m, const float* x, float* y) { matvec_n(m, m->p, m->rows, x, y); }
+/* rows [r0, r0+n) of a stacked matrix */
+static void matvec_rows(const mat_t* m, int64_t r0, int64_t n, const float* x, float* y) {
+    matvec_n(m, m->p + r0 * or_row_bytes(m->dt, m->cols), n, x, y);
+}
+
+static float sigmoid_ref(float v) { return 1.f / (1.f + expf(-v)); }
+static float softplus_ref(float v) { return v > 20.f ? v : v < -20.f ? expf(v) : log1pf(expf(v)); }
+
+/* gguf_rms_norm (quantized_layer.rs:230-236): x / sqrt(mean(x^2) + eps) * w */
+static void rms_norm(const float* x, const float* w, int n, float eps, float* out) {
+    float ss = 0.f;
+    for (int i = 0; i < n; i++) ss += x[i] * x[i];
+    float var = ss * (float)(1.0 / (double)n);
+    float den = sqrtf(var + eps);
+    for (int i = 0; i < n; i++) out[i] = (x[i] / den) * w[i];
+}
+
+/* ------------------------------------------------------------- creation */
+#define REQ(x) do { if (!(x)) { free(m->layers); free(m); return NULL; } } while (0)
+
+static int load_moe(const or_tensor* t, int n, const char* p, layer_t* L) {
+    char b[256];
+    snprintf(b, sizeof b, "%s.ffn_gate_inp.weight", p); if (getmat(t, n, b, &L->router)) return -1;
+    snprintf(b, sizeof b, "%s.ffn_gate_exps.weight", p); if (getmat(t, n, b, &L->gate)) return -1;
+    snprintf(b, sizeof b, "%s.ffn_up_exps.weight", p); if (getmat(t, n, b, &L->up)) return -1;
+    snprintf(b, sizeof b, "%s.ffn_down_exps.weight", p); if (getmat(t, n, b, &L->down)) return -1;
+    snprintf(b, sizeof b, "%s.ffn_gate_shexp.weight", p); if (getmat(t, n, b, &L->sh_gate)) return -1;
+    snprintf(b, sizeof b, "%s.ffn_up_shexp.weight", p); if (getmat(t, n, b, &L->sh_up)) return -1;
+    snprintf(b, sizeof b, "%s.ffn_down_shexp.weight", p); if (getmat(t, n, b, &L->sh_down)) return -1;
+    snprintf(b, sizeof b, "%s.ffn_gate_inp_shexp.weight", p); if (!(L->selector = getvec(t, n, b))) return -1;
+    return 0;
+}
+static int load_attn(const or_tensor* t, int n, const char* p, layer_t* L) {
+    char b[256];
+    L->full = 1;
+    snprintf(b, sizeof b, "%s.attn_q.weight", p); if (getmat(t, n, b, &L->q)) return -1;
+    snprintf(b, sizeof b, "%s.attn_k.weight", p); if (getmat(t, n, b, &L->k)) return -1;
+    snprintf(b, sizeof b, "%s.attn_v.weight", p); if (getmat(t, n, b, &L->v)) return -1;
+    snprintf(b, sizeof b, "%s.attn_output.weight", p); if (getmat(t, n, b, &L->o)) return -1;
+    snprintf(b, sizeof b, "%s.attn_q_norm.weight", p); if (!(L->q_norm = getvec(t, n, b))) return -1;
+    snprintf(b, sizeof b, "%s.attn_k_norm.weight", p); if (!(L->k_norm = getvec(t, n, b))) return -1;
+    return 0;
+}
+static int load_norms(const or_tensor* t, int n, const char* p, layer_t* L) {
+    char b[256];
+    snprintf(b, sizeof b, "%s.attn_norm.weight", p); if (!(L->attn_norm = getvec(t, n, b))) return -1;
+    snprintf(b, sizeof b, "%s.post_attention_norm.weight", p); if (!(L->post_norm = getvec(t, n, b))) return -1;
+    return 0;
+}
+
+or_model* or_model_create(const or_config* c, const or_tensor* t, int n) {
+    or_model* m = (or_model*)calloc(1, sizeof(or_model));
+    m->c = *c;
+    m->layers = (layer_t*)calloc((size_t)c->num_hidden_layers, sizeof(layer_t));
+    REQ(!getmat(t, n, "token_embd.weight", &m->embed));
+    REQ(!getmat(t, n, "output.weight", &m->lm_head));
+    REQ(m->out_norm = getvec(t, n, "output_norm.weight"));
+    char p[64], b[256];
+    for (int l = 0; l < c->num_hidden_layers; l++) {
+        layer_t* L = &m->layers[l];
+        snprintf(p, sizeof p, "blk.%d", l);
+        REQ(!load_norms(t, n, p, L));
+        if ((l + 1) % c->full_attention_interval == 0) {
+            REQ(!load_attn(t, n, p, L));
+        } else {
+            snprintf(b, sizeof b, "%s.attn_qkv.weight", p); REQ(!getmat(t, n, b, &L->qkv));
+            snprintf(b, sizeof b, "%s.attn_gate.weight", p); REQ(!getmat(t, n, b, &L->z));
+            snprintf(b, sizeof b, "%s.ssm_ba.weight", p);
+            if (!getmat(t, n, b, &L->ba)) L->ba_fused = 1;
+            else {
+                snprintf(b, sizeof b, "%s.ssm_beta.weight", p); REQ(!getmat(t, n, b, &L->beta));
+                snprintf(b, sizeof b, "%s.ssm_alpha.weight", p); REQ(!getmat(t, n, b, &L->alpha));
+            }
+            snprintf(b, sizeof b, "%s.ssm_out.weight", p); REQ(!getmat(t, n, b, &L->out));
+            snprintf(b, sizeof b, "%s.ssm_conv1d.weight", p); REQ(L->conv_w = getvec(t, n, b));
+            snprintf(b, sizeof b, "%s.ssm_a", p); REQ(L->ssm_a = getvec(t, n, b));
+            snprintf(b, sizeof b, "%s.ssm_dt.bias", p); REQ(L->dt_bias = getvec(t, n, b));
+            snprintf(b, sizeof b, "%s.ssm_norm.weight", p); REQ(L->ssm_norm = getvec(t, n, b));
+        }
+        REQ(!load_moe(t, n, p, L));
+    }
+    if (c->mtp_num_hidden_layers == 1) {
+        m->has_mtp = 1;
+        snprintf(p, sizeof p, "blk.%d", c->num_hidden_layers);
+        REQ(!load_norms(t, n, p, &m->mtp));
+        REQ(!load_attn(t, n, p, &m->mtp));
+        REQ(!load_moe(t, n, p, &m->mtp));
+        snprintf(b, sizeof b, "%s.nextn.enorm.weight", p); REQ(m->enorm = getvec(t, n, b));
+        snprintf(b, sizeof b, "%s.nextn.hnorm.weight", p); REQ(m->hnorm = getvec(t, n, b));
+        snprintf(b, sizeof b, "%s.nextn.shared_head_norm.weight", p); REQ(m->head_norm = getvec(t, n, b));
+        snprintf(b, sizeof b, "%s.nextn.eh_proj.weight", p); REQ(!getmat(t, n, b, &m->eh_proj));
+    }
+    return m;
+}
+
+void or_model_destroy(or_model* m) {
+    if (!m) return;
+    free(m->layers);
+    free(m);
+}
+
+static void lstate_alloc(const or_config* c, int full, int64_t max_pos, lstate_t* s) {
+    memset(s, 0, sizeof *s);
+    if (full) {
+        size_t kv = (size_t)max_pos * c->num_key_value_heads * c->head_dim;
+        s->keys = (float*)calloc(kv, 4);
+        s->values = (float*)calloc(kv, 4);
+    } else {
+        int64_t conv_dim = 2 * (int64_t)c->linear_num_key_heads * c->linear_key_head_dim +
+                           (int64_t)c->linear_num_value_heads * c->linear_value_head_dim;
+        s->conv = (float*)calloc((size_t)(conv_dim * (c->linear_conv_kernel_dim - 1) + 1), 4);
+        s->rec = (float*)calloc((size_t)c->linear_num_value_heads * c->linear_key_head_dim * c->linear_value_head_dim, 4);
+    }
+}
+static void lstate_free(lstate_t* s) { free(s->conv); free(s->rec); free(s->keys); free(s->values); }
+
+or_state* or_state_create(const or_model* m, int64_t max_pos) {
+    or_state* s = (or_state*)calloc(1, sizeof(or_state));
+    s->max_pos = max_pos;
+    s->nlayers = m->c.num_hidden_layers;
+    s->l = (lstate_t*)calloc((size_t)s->nlayers, sizeof(lstate_t));
+    for (int i = 0; i < s->nlayers; i++) lstate_alloc(&m->c, m->layers[i].full, max_pos, &s->l[i]);
+    if (m->has_mtp) lstate_alloc(&m->c, 1, max_pos, &s->mtp);
+    return s;
+}
+
+void or_state_destroy(or_state* s) {
+    if (!s) return;
+    for (int i = 0; i < s->nlayers; i++) lstate_free(&s->l[i]);
+    lstate_free(&s->mtp);
+    free(s->l);
+    free(s);
+}
+
+/* Deep copy (the snapshot a rollback restores). */
+void or_state_copy(const or_model* m, or_state* dst, const or_state* src) {
+    const or_config* c = &m->c;
+    int64_t conv_dim = 2 * (int64_t)c->linear_num_key_heads * c->linear_key_head_dim +
+                       (int64_t)c->linear_num_value_heads * c->linear_value_head_dim;
+    size_t kv = (size_t)src->max_pos * c->num_key_value_heads * c->head_dim;
+    size_t rec = (size_t)c->linear_num_value_heads * c->linear_key_head_dim * c->linear_value_head_dim;
+    for (int i = 0; i < src->nlayers; i++) {
+        if (m->layers[i].full) {
+            memcpy(dst->l[i].keys, src->l[i].keys, kv * 4);
+            memcpy(dst->l[i].values, src->l[i].values, kv * 4);
+        } else {
+            memcpy(dst->l[i].conv, src->l[i].conv, (size_t)(conv_dim * (c->linear_conv_kernel_dim - 1) + 1) * 4);
+            memcpy(dst->l[i].rec, src->l[i].rec, rec * 4);
+        }
+    }
+    if (m->has_mtp) {
+        memcpy(dst->mtp.keys, src->mtp.keys, kv * 4);
+        memcpy(dst->mtp.values, src->mtp.values, kv * 4);
+    }
+    dst->position = src->position;
+    dst->mtp_position = src->mtp_position;
+}
+
+int64_t or_state_position(const or_state* s) { return s->position; }
+
+/* ------------------------------------------------------------ DeltaNet */
+static void delta_row(const or_model* m, const layer_t* L, lstate_t* st, const float* x, float* out) {
+    const or_config* c = &m->c;
+    const int nk = c->linear_num_key_heads, nv = c->linear_num_value_heads;
+    const int dk = c->linear_key_head_dim, dv = c->linear_value_head_dim, K = c->linear_conv_kernel_dim;
+    const int kd = nk * dk, vd = nv * dv, conv_dim = 2 * kd + vd, ratio = nv / nk;
+    float* proj = (float*)malloc((size_t)conv_dim * 4);
+    float* z = (float*)malloc((size_t)vd * 4);
+    float* ba = (float*)malloc((size_t)2 * nv * 4);
+    float* cv = (float*)malloc((size_t)conv_dim * 4);
+    float* qr = (float*)malloc((size_t)nv * dk * 4);
+    float* kr = (float*)malloc((size_t)nv * dk * 4);
+    float* o = (float*)malloc((size_t)vd * 4);
+    float* g = (float*)malloc((size_t)vd * 4);
+    matvec(&L->qkv, x, proj);
+    matvec(&L->z, x, z);
+    if (L->ba_fused) matvec(&L->ba, x, ba);
+    else { matvec(&L->beta, x, ba); matvec(&L->alpha, x, ba + nv); }
+    /* causal depthwise conv step + SiLU (quantized_deltanet.rs:733-759) */
+    for (int ch = 0; ch < conv_dim; ch++) {
+        const float* w = L->conv_w + (int64_t)ch * K;
+        float* hist = st->conv + (int64_t)ch * (K - 1);
+        float sum = w[K - 1] * proj[ch];
+        for (int tap = 0; tap < K - 1; tap++) sum += w[tap] * hist[tap];
+        cv[ch] = sum * sigmoid_ref(sum);
+        for (int tap = 0; tap + 1 < K - 1; tap++) hist[tap] = hist[tap + 1];
+        if (K > 1) hist[K - 2] = proj[ch];
+    }
+    float* q = cv; float* k = cv + kd; const float* v = cv + 2 * kd;
+    for (int kh = 0; kh < nk; kh++) {
+        for (int which = 0; which < 2; which++) {  /* normalize (:724-731) */
+            float* a = (which ? k : q) + kh * dk;
+            float ss = 0.f;
+            for (int i = 0; i < dk; i++) ss += a[i] * a[i];
+            float scale = 1.f / sqrtf(ss + 1e-6f);
+            for (int i = 0; i < dk; i++) a[i] *= scale;
+        }
+    }
+    float q_scale = 1.f / sqrtf((float)dk);
+    for (int kh = 0; kh < nk; kh++)
+        for (int rep = 0; rep < ratio; rep++) {
+            int vh = c->value_heads_tiled ? rep * nk + kh : kh * ratio + rep;
+            memcpy(qr + vh * dk, q + kh * dk, (size_t)dk * 4);
+            memcpy(kr + vh * dk, k + kh * dk, (size_t)dk * 4);
+            float b, al;
+            if (L->ba_fused) { int base = kh * 2 * ratio; b = ba[base + rep]; al = ba[base + ratio + rep]; }
+            else { b = ba[vh]; al = ba[nv + vh]; }
+            float beta = sigmoid_ref(b);
+            float gdec = L->ssm_a[vh] * softplus_ref(al + L->dt_bias[vh]);
+            /* delta_head_step (deltanet.rs:170-217) */
+            float* S = st->rec + (int64_t)vh * dk * dv;
+            const float* kk = kr + vh * dk; const float* qq = qr + vh * dk; const float* vv = v + vh * dv;
+            float decay = expf(gdec);
+            for (int i = 0; i < dk * dv; i++) S[i] *= decay;
+            float* out_h = o + vh * dv;
+            for (int j = 0; j < dv; j++) out_h[j] = 0.f;
+            for (int i = 0; i < dk; i++) for (int j = 0; j < dv; j++) out_h[j] += S[i * dv + j] * kk[i];
+            for (int j = 0; j < dv; j++) out_h[j] = (vv[j] - out_h[j]) * beta;
+            for (int i = 0; i < dk; i++) for (int j = 0; j < dv; j++) S[i * dv + j] += kk[i] * out_h[j];
+            for (int j = 0; j < dv; j++) out_h[j] = 0.f;
+            for (int i = 0; i < dk; i++) for (int j = 0; j < dv; j++) out_h[j] += S[i * dv + j] * qq[i] * q_scale;
+        }
+    /* rms_norm_gated (norm.rs:16-25) per value head */
+    for (int vh = 0; vh < nv; vh++) {
+        const float* oh = o + vh * dv;
+        float ss = 0.f;
+        for (int j = 0; j < dv; j++) ss += oh[j] * oh[j];
+        float den = sqrtf(ss * (float)(1.0 / dv) + c->rms_norm_eps);
+        for (int j = 0; j < dv; j++) {
+            float zz = z[vh * dv + j];
+            float silu = zz / (1.f + expf(-zz));
+            g[vh * dv + j] = ((oh[j] / den) * L->ssm_norm[j]) * silu;
+        }
+    }
+    matvec(&L->out, g, out);
+    free(proj); free(z); free(ba); free(cv); free(qr); free(kr); free(o); free(g);
+}
+
+/* ----------------------------------------------------------- attention */
+static float dot8(const float* a, const float* b, int n) {  /* quantized_attention.rs:155-178 */
+    float lanes[8] = {0};
+    int full = n / 8 * 8;
+    for (int i = 0; i < full; i += 8)
+        for (int l = 0; l < 8; l++) lanes[l] += a[i + l] * b[i + l];
+    float total = 0.f;
+    for (int i = full; i < n; i++) total += a[i] * b[i];
+    for (int l = 0; l < 8; l++) total += lanes[l];
+    return total;
+}
+static void converted_norm(float* v, const float* w, int n, float eps) {  /* :833-839 */
+    float ss = 0.f;
+    for (int i = 0; i < n; i++) ss += v[i] * v[i];
+    float var = ss / (float)n;
+    float scale = 1.f / sqrtf(var + eps);
+    for (int i = 0; i < n; i++) v[i] = v[i] * scale * w[i];
+}
+static void apply_rope(float* v, int64_t pos, int rd, double theta) {  /* :841-851 */
+    int half = rd / 2;
+    float orig[512];
+    memcpy(orig, v, (size_t)rd * 4);
+    for (int i = 0; i < half; i++) {
+        double freq = 1.0 / pow(theta, (double)(2 * i) / (double)rd);
+        double ang = (double)pos * freq;
+        float s = (float)sin(ang), cs = (float)cos(ang);
+        v[i] = orig[i] * cs - orig[half + i] * s;
+        v[half + i] = orig[half + i] * cs + orig[i] * s;
+    }
+}
+
+static void attn_row(const or_model* m, const layer_t* L, lstate_t* st, int64_t pos, const float* x, float* out) {
+    const or_config* c = &m->c;
+    const int nh = c->num_attention_heads, nkv = c->num_key_value_heads, hd = c->head_dim;
+    const int G = nh / nkv;
+    float* qg = (float*)malloc((size_t)nh * 2 * hd * 4);
+    float* kv = (float*)malloc((size_t)nkv * hd * 4);
+    float* vv = (float*)malloc((size_t)nkv * hd * 4);
+    float* res = (float*)malloc((size_t)nh * hd * 4);
+    float* scores = (float*)malloc((size_t)(pos + 1) * 4);
+    matvec(&L->q, x, qg);
+    matvec(&L->k, x, kv);
+    matvec(&L->v, x, vv);
+    for (int h = 0; h < nkv; h++) {
+        converted_norm(kv + h * hd, L->k_norm, hd, c->rms_norm_eps);
+        apply_rope(kv + h * hd, pos, c->rotary_dim, c->rope_theta);
+    }
+    memcpy(st->keys + pos * nkv * hd, kv, (size_t)nkv * hd * 4);
+    memcpy(st->values + pos * nkv * hd, vv, (size_t)nkv * hd * 4);
+    float scale = 1.f / sqrtf((float)hd);
+    for (int h = 0; h < nh; h++) {
+        float* q = qg + h * 2 * hd;
+        const float* gate = q + hd;
+        converted_norm(q, L->q_norm, hd, c->rms_norm_eps);
+        apply_rope(q, pos, c->rotary_dim, c->rope_theta);
+        int kvh = h / G;
+        float mx = -INFINITY;
+        for (int64_t p = 0; p <= pos; p++) {
+            scores[p] = dot8(q, st->keys + (p * nkv + kvh) * hd, hd) * scale;
+            if (scores[p] > mx) mx = scores[p];
+        }
+        float den = 0.f;
+        for (int64_t p = 0; p <= pos; p++) { scores[p] = expf(scores[p] - mx); den += scores[p]; }
+        float* o = res + h * hd;
+        for (int d = 0; d < hd; d++) o[d] = 0.f;
+        for (int64_t p = 0; p <= pos; p++) {
+            float prob = scores[p] / den;
+            const float* vr = st->values + (p * nkv + kvh) * hd;
+            for (int d = 0; d < hd; d++) o[d] += prob * vr[d];
+        }
+        for (int d = 0; d < hd; d++) o[d] *= sigmoid_ref(gate[d]);
+    }
+    matvec(&L->o, res, out);
+    free(qg); free(kv); free(vv); free(res); free(scores);
+}
+
+/* ----------------------------------------------------------------- MoE */
+static void moe_row(const or_model* m, const layer_t* L, const float* x, float* out, int* experts_out) {
+    const or_config* c = &m->c;
+    const int E = c->num_experts, H = c->hidden_size, F = c->moe_intermediate_size;
+    const int Fs = c->shared_expert_intermediate_size, topk = c->num_experts_per_tok;
+    float* lg = (float*)malloc((size_t)E * 4);
+    float* pr = (float*)malloc((size_t)E * 4);
+    int* rank = (int*)malloc((size_t)E * sizeof(int));
+    float* g = (float*)malloc((size_t)(F > Fs ? F : Fs) * 4);
+    float* u = (float*)malloc((size_t)(F > Fs ? F : Fs) * 4);
+    float* y = (float*)malloc((size_t)H * 4);
+    matvec(&L->router, x, lg);
+    float mx = -INFINITY;
+    for (int e = 0; e < E; e++) mx = fmaxf(mx, lg[e]);
+    float den = 0.f;
+    for (int e = 0; e < E; e++) den += expf(lg[e] - mx);
+    for (int e = 0; e < E; e++) pr[e] = expf(lg[e] - mx) / den;
+    /* top-k by probability; equal probabilities rank the lower expert first */
+    for (int e = 0; e < E; e++) rank[e] = e;
+    for (int r = 0; r < topk; r++) {
+        int best = r;
+        for (int i = r + 1; i < E; i++)
+            if (pr[rank[i]] > pr[rank[best]] || (pr[rank[i]] == pr[rank[best]] && rank[i] < rank[best])) best = i;
+        int t = rank[r]; rank[r] = rank[best]; rank[best] = t;
+    }
+    float w[16], sum = 0.f;
+    for (int r = 0; r < topk; r++) { w[r] = pr[rank[r]]; sum += w[r]; }
+    if (c->norm_topk_prob) for (int r = 0; r < topk; r++) w[r] /= sum;
+    for (int i = 0; i < H; i++) out[i] = 0.f;
+    for (int r = 0; r < topk; r++) {
+        int e = rank[r];
+        if (experts_out) experts_out[r] = e;
+        matvec_rows(&L->gate, (int64_t)e * F, F, x, g);
+        matvec_rows(&L->up, (int64_t)e * F, F, x, u);
+        for (int i = 0; i < F; i++) g[i] = (g[i] / (1.f + expf(-g[i]))) * u[i];
+        matvec_rows(&L->down, (int64_t)e * H, H, g, y);
+        for (int i = 0; i < H; i++) out[i] += y[i] * w[r];
+    }
+    matvec(&L->sh_gate, x, g);
+    matvec(&L->sh_up, x, u);
+    for (int i = 0; i < Fs; i++) g[i] = (g[i] / (1.f + expf(-g[i]))) * u[i];
+    matvec(&L->sh_down, g, y);
+    float sel = 0.f;
+    for (int i = 0; i < H; i++) sel += x[i] * L->selector[i];
+    sel = 1.f / (1.f + expf(-sel));
+    for (int i = 0; i < H; i++) out[i] = out[i] + y[i] * sel;
+    free(lg); free(pr); free(rank); free(g); free(u); free(y);
+}
+
+/* One decoder layer on one row, in place (quantized_layer.rs:101-225). */
+static void layer_row(const or_model* m, const layer_t* L, lstate_t* st, int64_t pos, float* h, int* experts) {
+    const int H = m->c.hidden_size;
+    float* xn = (float*)malloc((size_t)H * 4);
+    float* mix = (float*)malloc((size_t)H * 4);
+    rms_norm(h, L->attn_norm, H, m->c.rms_norm_eps, xn);
+    if (L->full) attn_row(m, L, st, pos, xn, mix);
+    else delta_row(m, L, st, xn, mix);
+    for (int i = 0; i < H; i++) h[i] = h[i] + mix[i];
+    rms_norm(h, L->post_norm, H, m->c.rms_norm_eps, xn);
+    moe_row(m, L, xn, mix, experts);
+    for (int i = 0; i < H; i++) h[i] = h[i] + mix[i];
+    free(xn); free(mix);
+}
+
+/* Evaluate `rows` tokens (QuantizedModel::forward_detailed).  logits
+ * [rows][vocab] and hidden [rows][hidden] (final-normed) may be NULL.
+ * experts, when non-NULL, receives [rows][layers][topk] routed experts. */
+int or_forward(const or_model* m, or_state* s, const uint32_t* tokens, int rows, float* logits, float* hidden,
+               int32_t* experts) {
+    const or_config* c = &m->c;
+    const int H = c->hidden_size;
+    if (s->position + rows > s->max_pos) return -1;
+    float* h = (float*)malloc((size_t)H * 4);
+    float* hn = (float*)malloc((size_t)H * 4);
+    for (int r = 0; r < rows; r++) {
+        if (tokens[r] >= (uint32_t)c->vocab_size) { free(h); free(hn); return -2; }
+        or_dequant_rows(m->embed.dt, m->embed.p + (int64_t)tokens[r] * or_row_bytes(m->embed.dt, H), 1, H, h);
+        for (int l = 0; l < c->num_hidden_layers; l++) {
+            int ex[16];
+            layer_row(m, &m->layers[l], &s->l[l], s->position, h, ex);
+            if (experts)
+                for (int i = 0; i < c->num_experts_per_tok; i++)
+                    experts[((int64_t)r * c->num_hidden_layers + l) * c->num_experts_per_tok + i] = ex[i];
+        }
+        rms_norm(h, m->out_norm, H, c->rms_norm_eps, hn);
+        if (hidden) memcpy(hidden + (int64_t)r * H, hn, (size_t)H * 4);
+        if (logits) matvec(&m->lm_head, hn, logits + (int64_t)r * c->vocab_size);
+        s->position++;
+    }
+    free(h); free(hn);
+    return 0;
+}
+
+/* One MTP predictor step (quantized_mtp.rs:175-227): token + previous
+ * hidden row -> next hidden row and logits over the first head_rows rows
+ * of the LM head (0 = no logits). */
+int or_mtp_forward(const or_model* m, or_state* s, uint32_t token, const float* hidden_in, int64_t head_rows,
+                   float* logits, float* hidden_out) {
+    const or_config* c = &m->c;
+    const int H = c->hidden_size;
+    if (!m->has_mtp) return -1;
+    float* e = (float*)malloc((size_t)2 * H * 4);
+    float* tmp = (float*)malloc((size_t)H * 4);
+    float* h = (float*)malloc((size_t)H * 4);
+    or_dequant_rows(m->embed.dt, m->embed.p + (int64_t)token * or_row_bytes(m->embed.dt, H), 1, H, tmp);
+    rms_norm(tmp, m->enorm, H, c->rms_norm_eps, e);
+    rms_norm(hidden_in, m->hnorm, H, c->rms_norm_eps, e + H);
+    matvec(&m->eh_proj, e, h);
+    layer_row(m, &m->mtp, &s->mtp, s->mtp_position, h, NULL);
+    rms_norm(h, m->head_norm, H, c->rms_norm_eps, tmp);
+    if (hidden_out) memcpy(hidden_out, tmp, (size_t)H * 4);
+    if (logits && head_rows > 0) matvec_n(&m->lm_head, m->lm_head.p, head_rows, tmp, logits);
+    s->mtp_position++;
+    free(e); free(tmp); free(h);
+    return 0;
+}
+
+void or_state_set_mtp_position(or_state* s, int64_t p) { s->mtp_position = p; }

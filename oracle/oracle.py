@@ -76,6 +76,102 @@ def qmatvec(dtype: int, w: np.ndarray, rows: int, cols: int, x: np.ndarray, *, o
     return y
 
 
+def set_gemv_order(order: int) -> None:
+    """0: reference lane order (default); 1: device chunk order (diagnostic)."""
+    lib().or_set_gemv_order(order)
+
+
 def argmax(v: np.ndarray) -> int:
     v = np.ascontiguousarray(v, np.float32)
     return int(lib().or_argmax(_p(v), len(v)))
+
+
+# ------------------------------------------------------------------ model
+class OracleModel:
+    """The CPU restatement of the reference model over host tensors.
+
+    ``tensors`` are inferq_b200.synth.Tensor objects (CPU); the config is a
+    synth.Config.  Rows are evaluated one at a time in the reference's own
+    arithmetic order (see iq_oracle_model.c).
+    """
+
+    def __init__(self, cfg, tensors):
+        from inferq_b200.model import IqConfig, IqTensorView, iq_config
+        L = lib()
+        P = ctypes.c_void_p
+        L.or_model_create.restype = P
+        L.or_model_create.argtypes = [P, P, ctypes.c_int]
+        L.or_model_destroy.argtypes = [P]
+        L.or_state_create.restype = P
+        L.or_state_create.argtypes = [P, ctypes.c_int64]
+        L.or_state_destroy.argtypes = [P]
+        L.or_state_copy.argtypes = [P, P, P]
+        L.or_forward.argtypes = [P, P, P, ctypes.c_int, P, P, P]
+        L.or_mtp_forward.argtypes = [P, P, ctypes.c_uint32, P, ctypes.c_int64, P, P]
+        L.or_state_set_mtp_position.argtypes = [P, ctypes.c_int64]
+        self.cfg = cfg
+        self._keep = []
+        views = []
+        for t in tensors:
+            d = t.data.detach().cpu().contiguous()
+            self._keep.append(d)
+            v = IqTensorView()
+            nm = t.name.encode()
+            self._keep.append(nm)
+            v.name = nm
+            v.dtype = t.dtype
+            v.ndim = len(t.shape)
+            for i, s in enumerate(t.shape):
+                v.shape[i] = s
+            v.data = d.data_ptr()
+            v.location = 0
+            views.append(v)
+        self._views = (IqTensorView * len(views))(*views)
+        self._cfg = iq_config(cfg)
+        self._h = L.or_model_create(ctypes.byref(self._cfg), self._views, len(views))
+        assert self._h, "oracle model creation failed (missing tensor)"
+
+    def state(self, max_pos: int) -> "OracleState":
+        return OracleState(self, max_pos)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().or_model_destroy(self._h)
+            self._h = None
+
+
+class OracleState:
+    def __init__(self, model: OracleModel, max_pos: int):
+        self.model = model
+        self.max_pos = max_pos
+        self._h = lib().or_state_create(model._h, max_pos)
+
+    def forward(self, tokens, *, logits=True, hidden=False, experts=False):
+        c = self.model.cfg
+        tok = np.ascontiguousarray(tokens, dtype=np.uint32)
+        n = len(tok)
+        lg = np.empty((n, c.vocab_size), np.float32) if logits else None
+        hd = np.empty((n, c.hidden_size), np.float32) if hidden else None
+        ex = np.empty((n, c.num_hidden_layers, c.num_experts_per_tok), np.int32) if experts else None
+        rc = lib().or_forward(self.model._h, self._h, _p(tok), n, None if lg is None else _p(lg),
+                              None if hd is None else _p(hd), None if ex is None else _p(ex))
+        assert rc == 0, rc
+        return lg, hd, ex
+
+    def mtp(self, token: int, hidden_in: np.ndarray, head_rows: int):
+        c = self.model.cfg
+        h = np.ascontiguousarray(hidden_in, np.float32)
+        lg = np.empty(head_rows, np.float32) if head_rows else None
+        out = np.empty(c.hidden_size, np.float32)
+        rc = lib().or_mtp_forward(self.model._h, self._h, token, _p(h), head_rows,
+                                  None if lg is None else _p(lg), _p(out))
+        assert rc == 0, rc
+        return lg, out
+
+    def copy_from(self, other: "OracleState"):
+        lib().or_state_copy(self.model._h, self._h, other._h)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().or_state_destroy(self._h)
+            self._h = None
