@@ -199,6 +199,8 @@ int iq_state_routes(const iq_state* s, int rows, int32_t* experts);
  * stage is bracketed by CUDA events.  iq_state_profile writes
  * "stage count total_us" lines into buf and returns their length. */
 int iq_state_set_profiling(iq_state* s, int on);
+/* Kernels this state has launched so far (graph replays included). */
+int iq_state_launch_count(const iq_state* s, int64_t* count);
 int iq_state_profile(const iq_state* s, char* buf, int len);
 
 #ifdef __cplusplus

@@ -65,6 +65,8 @@ struct iq_state {
   int* union_dev = nullptr;      // counts + 4*layer + 2
   // stage profiling (iq_state_set_profiling): events and accumulated times
   bool profiling = false;
+  int64_t launch_count = 0;  // kernels enqueued by passes (graph replays count theirs too)
+  int graph_launches[2][8] = {};
   std::vector<std::pair<std::string, cudaEvent_t>> marks;
   std::vector<std::pair<std::string, std::pair<int, double>>> prof;
   // one captured graph per (mode, rows): [verify][k-1]
@@ -170,11 +172,13 @@ int prep(Ctx& x, const float* in, int ld, int cols, const float* norm, int k, bo
   a.q80 = q80 ? x.s->act80.as<uint8_t>() : nullptr;
   a.q8k_stride = (int)x.s->act8k_bytes;
   a.q80_stride = (int)x.s->act80_bytes;
+  ++x.s->launch_count;
   IQ_CUDA(prep_rows(a, k, x.st, x.pdl));
   return IQ_OK;
 }
 
 int qmv(Ctx& x, const QmvRec& r) {
+  ++x.s->launch_count;
   IQ_CUDA(qmv_launch(x.s->jobs.as<QmvJob>() + r.job, r.njobs, nullptr, r.ntiles, r.smem, x.st, x.pdl));
   return IQ_OK;
 }
@@ -246,9 +250,11 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   if (W.router.present()) {
     TRY(qmv(x, R.router));
   x.mark("moe.router");
+    ++x.s->launch_count;
     IQ_CUDA(f32_matvec(W.selector.p(), 1, H, s->xn.as<float>(), H, k, lg + E, E + 1, x.st, x.pdl));
   x.mark("moe.router");
   } else {
+    ++x.s->launch_count;
     IQ_CUDA(f32_matvec(W.router_sel.p(), E + 1, H, s->xn.as<float>(), H, k, lg, E + 1, x.st, x.pdl));
   x.mark("moe.router");
   }
@@ -310,6 +316,7 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   t.with_shared = 1;
   t.expert_lo = W.expert_lo;
   t.expert_hi = W.expert_hi;
+  ++x.s->launch_count;
   IQ_CUDA(moe_route_launch(a, t, x.st, x.pdl));
   x.mark("moe.route");
   // upper bounds on the dynamic job tables' tiles
@@ -318,6 +325,7 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   const int tiles_sh_down = (int)ceil_div(H, qmv_rows_per_cta(t.ks_sh_down));
   const int down_tiles = max_union * t.tiles_down + tiles_sh_down;
   const int gu_smem = k * (int)std::max(s->act8k_bytes, s->act80_bytes);
+  ++x.s->launch_count;
   IQ_CUDA(qmv_launch(a.gu_jobs, 0, a.gu_count, gu_tiles, gu_smem, x.st, x.pdl));
   x.mark("moe.gate_up");
   MoeActArgs b = {};
@@ -334,8 +342,10 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   b.act_bytes = (int)s->act_mid_bytes;
   b.down_q80 = W.down.dt == Q8_0;
   b.sh_down_q80 = W.sh_down.dt == Q8_0;
+  ++x.s->launch_count;
   IQ_CUDA(moe_act_launch(b, x.st, x.pdl));
   x.mark("moe.act");
+  ++x.s->launch_count;
   IQ_CUDA(qmv_launch(a.down_jobs, 0, a.down_count, down_tiles, 8 * (int)s->act_mid_bytes, x.st, x.pdl));
   x.mark("moe.down");
   // expert parallelism: the all-gather of y happens here (model_ep.cu)
@@ -351,6 +361,7 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   cb.rows = k;
   cb.topk = c.num_experts_per_tok;
   cb.dim = H;
+  ++x.s->launch_count;
   IQ_CUDA(moe_combine_launch(cb, x.st, x.pdl));
   x.mark("moe.combine");
   return IQ_OK;
@@ -389,6 +400,7 @@ int run_delta(Ctx& x, const Layer& L, const LayerRec& R, int k, int li) {
   a.sel = x.sel();
   a.committed = x.result() + 2;
   a.replay = 0;
+  ++x.s->launch_count;
   IQ_CUDA(deltanet_launch(a, 1, x.st, x.pdl));
   x.mark("dn.recurrence");
   GatedNormArgs g = {};
@@ -405,6 +417,7 @@ int run_delta(Ctx& x, const Layer& L, const LayerRec& R, int k, int li) {
   g.q80 = D.out.dt == Q8_0 ? s->act80.as<uint8_t>() : nullptr;
   g.q8k_stride = (int)s->act8k_bytes;
   g.q80_stride = (int)s->act80_bytes;
+  ++x.s->launch_count;
   IQ_CUDA(gated_norm_launch(g, k, x.st, x.pdl));
   x.mark("dn.gated_norm");
   TRY(qmv(x, R.out));
@@ -448,10 +461,13 @@ int run_attention(Ctx& x, const Layer& L, const LayerRec& R, int k, int fi) {
   a.eps = c.rms_norm_eps;
   a.pos = x.pos();
   a.chunk_ctas = 16;
+  ++x.s->launch_count;
   IQ_CUDA(attn_prep_launch(a, x.st, x.pdl));
   x.mark("attn.prep");
+  ++x.s->launch_count;
   IQ_CUDA(attn_scan_launch(a, x.st, x.pdl));
   x.mark("attn.scan");
+  ++x.s->launch_count;
   IQ_CUDA(attn_combine_launch(a, x.st, x.pdl));
   x.mark("attn.combine");
   TRY(prep(x, s->attn_out.as<float>(), nhd, nhd, nullptr, k, needs(A.o.dt, false), needs(A.o.dt, true), nullptr));
@@ -498,6 +514,7 @@ int replay_all(Ctx& x, int k) {
     a.sel = x.sel();
     a.committed = x.result() + 2;
     a.replay = 1;
+    ++x.s->launch_count;
     IQ_CUDA(deltanet_launch(a, 1, x.st, x.pdl));
   x.mark("dn.recurrence");
   }
@@ -512,6 +529,7 @@ int run_pass(iq_state* s, int k, bool verify) {
   const KPlan& P = s->plans[k - 1];
   const int H = c.hidden_size;
   IQ_CUDA(cudaMemcpyAsync(s->tokens.p, s->h_tokens, k * sizeof(int32_t), cudaMemcpyHostToDevice, x.st));
+  ++s->launch_count;
   IQ_CUDA(embed_launch(m->embed.dt, m->embed.p(), m->embed.row_bytes, H, s->tokens.as<int32_t>(), k,
                        s->hidden.as<float>(), H, x.st, x.pdl));
   x.mark("embed");
@@ -540,12 +558,15 @@ int run_pass(iq_state* s, int k, bool verify) {
   h.verify = verify ? 1 : 0;
   h.result = x.result();
   h.scores = nullptr;
+  ++x.s->launch_count;
   IQ_CUDA(argmax_launch(h, x.st, x.pdl));
   x.mark("head.argmax");
+  ++x.s->launch_count;
   IQ_CUDA(accept_launch(h, x.st, x.pdl));
   x.mark("head.accept");
   if (verify) TRY(replay_all(x, k));
   x.mark("head.replay");
+  ++x.s->launch_count;
   IQ_CUDA(commit_launch(x.sel(), x.pos(), x.result(), x.st, x.pdl));
   x.mark("head.commit");
   IQ_CUDA(cudaMemcpyAsync(s->h_result, x.result(), 4 * sizeof(int), cudaMemcpyDeviceToHost, x.st));
@@ -567,7 +588,10 @@ int run_pass_graph(iq_state* s, int k, bool verify) {
     if (s->eager_runs[v][k - 1]++ == 0) return run_pass(s, k, verify);
     cudaGraph_t g = nullptr;
     IQ_CUDA(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+    const int64_t before = s->launch_count;
     int rc = run_pass(s, k, verify);
+    s->graph_launches[v][k - 1] = (int)(s->launch_count - before);
+    s->launch_count = before;
     cudaError_t e = cudaStreamEndCapture(s->st, &g);
     if (rc) {
       if (g) cudaGraphDestroy(g);
@@ -579,6 +603,7 @@ int run_pass_graph(iq_state* s, int k, bool verify) {
     IQ_CUDA(e);
   }
   IQ_CUDA(cudaGraphLaunch(ge, s->st));
+  s->launch_count += s->graph_launches[v][k - 1];
   return IQ_OK;
 }
 
@@ -863,6 +888,12 @@ int iq_state_routes(const iq_state* s, int rows, int32_t* experts) {
     IQ_CUDA(cudaMemcpy(experts + (int64_t)l * rows * c.num_experts_per_tok,
                        s->route_e.as<int>() + (int64_t)l * kMaxK * c.num_experts_per_tok,
                        (size_t)rows * c.num_experts_per_tok * 4, cudaMemcpyDeviceToHost));
+  return IQ_OK;
+}
+
+int iq_state_launch_count(const iq_state* s, int64_t* count) {
+  IQ_CHECK(s && count, IQ_EINVAL, "iq_state_launch_count: null argument");
+  *count = s->launch_count;
   return IQ_OK;
 }
 

@@ -51,6 +51,7 @@ def _declare(L):
         "iq_verify": (ctypes.c_int, [P, P, ctypes.c_int, ctypes.POINTER(IqVerifyResult), P, P]),
         "iq_rollback": (ctypes.c_int, [P, ctypes.c_int]),
         "iq_state_union_sizes": (ctypes.c_int, [P, P]),
+        "iq_state_launch_count": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_int64)]),
         "iq_state_routes": (ctypes.c_int, [P, ctypes.c_int, P]),
         "iq_state_set_profiling": (ctypes.c_int, [P, ctypes.c_int]),
         "iq_state_profile": (ctypes.c_int, [P, ctypes.c_char_p, ctypes.c_int]),
@@ -164,6 +165,16 @@ class State:
         out = np.zeros(self.model.cfg.num_hidden_layers, np.int32)
         _lib.check(lib().iq_state_union_sizes(self._h, out.ctypes.data))
         return out
+
+    def launch_count(self) -> int:
+        v = ctypes.c_int64()
+        _lib.check(lib().iq_state_launch_count(self._h, ctypes.byref(v)))
+        return v.value
+
+    def stream(self) -> int:
+        v = P()
+        _lib.check(lib().iq_state_stream(self._h, ctypes.byref(v)))
+        return v.value or 0
 
     def routes(self, rows: int) -> np.ndarray:
         c = self.model.cfg

@@ -172,8 +172,11 @@ def test_35b_widths_match_the_oracle(cuda):
     tensors = list(synth.generate(cfg, seed=2, device="cuda"))
     model = Model(cfg, tensors)
     om = oracle.OracleModel(cfg, tensors)
-    st, ost = State(model, 64), om.state(64)
     prompt = [3, 77]
-    _, lg, _ = st.forward(prompt, logits=True)
-    olg, _, _ = ost.forward(prompt)
-    assert np.abs(lg - olg).max() <= TOL
+    _, lg, _ = State(model, 64).forward(prompt, logits=True)
+    ref, _ = _oracle_logits(om, prompt, 0)
+    dev, _ = _oracle_logits(om, prompt, 1)
+    # DeltaNet's gated RMSNorm of a near-zero early recurrent output amplifies
+    # last-bit differences; the oracle's two orders bound that noise.
+    noise = np.abs(ref - dev).max()
+    assert np.abs(lg - ref).max() <= max(TOL, 2 * noise), (np.abs(lg - ref).max(), noise)
