@@ -73,6 +73,20 @@ int iq_matrix_forward_rows(const iq_matrix* m, const float* x, int64_t input_row
  * (a cudaStream_t, or NULL for the legacy stream).  Input rows <= 8. */
 int iq_matrix_forward_device(const iq_matrix* m, const float* x, int input_rows, float* y, void* stream);
 
+/* As iq_matrix_forward_device, but allocating no device memory at all: the
+ * quantized input rows and the launch record go to a fixed 37.6 KB scratch
+ * array built into the library (one per GPU, held until the process exits).
+ * No counterpart in the reference.  For callers that may not allocate while
+ * they run -- a host whose device memory is carved up in advance by its own
+ * pool, or a decode thread that cannot take cudaMalloc's implicit device
+ * synchronization.  Limits: 1..8 input rows, at most 4096 columns; larger
+ * requests fail with IQ_EINVAL.  The first call on a device looks up the
+ * array's device address, so make that first call before any stream
+ * capture.  All calls on a device share the one array: calls whose work
+ * overlaps on the GPU (different streams, or threads) race and must be
+ * serialized by the caller. */
+int iq_matrix_forward_device_noalloc(const iq_matrix* m, const float* x, int input_rows, float* y, void* stream);
+
 /* One-shot form over GGUF bytes in host memory (uploads, multiplies,
  * frees): int iq_qgemv of the boundary table, mirroring forward_rows. */
 int iq_qgemv(int dtype, const void* w, int64_t rows, int64_t cols, const float* x, int k, float* y,

@@ -57,6 +57,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "iq_matrix_shape": (I32, [P, ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I32)]),
         "iq_matrix_forward_rows": (I32, [P, P, I64, P]),
         "iq_matrix_forward_device": (I32, [P, P, I32, P, P]),
+        "iq_matrix_forward_device_noalloc": (I32, [P, P, I32, P, P]),
         "iq_qgemv": (I32, [I32, P, I64, I64, P, I32, P, P]),
         "iq_qgemv_ksplit": (I32, [I32, I64, I64]),
         "iq_matrix_dequantize": (I32, [P, P, I64, P]),

@@ -4,17 +4,7 @@
 #include <cstring>
 #include "api_util.h"
 #include "kernels.cuh"
-
-struct iq_matrix {
-  int dtype;
-  int64_t rows, cols, row_bytes;
-  std::shared_ptr<iq::DevBuf> storage;
-  const uint8_t* base;
-  // Device copy of the last job table this matrix launched, reused while the
-  // call's buffers and row count stay the same.
-  std::shared_ptr<iq::DevBuf> job_cache = std::make_shared<iq::DevBuf>();
-  iq::QmvJob last_job = {};
-};
+#include "matrix.h"
 
 namespace iq {
 
