@@ -98,6 +98,7 @@ int matrix_forward_dev(const iq_matrix* m, const float* x, int k, float* y, cuda
   j.cols = (int)m->cols;
   j.ksplit = qmv_ksplit(m->dtype, m->rows, m->cols);
   j.n = k;
+  j.act_nrows = k;
   j.tile0 = 0;
   j.epi = kEpiStore;
   for (int i = 0; i < 8; i++) { j.rowmap[i] = (uint8_t)(i < k ? i : 0); j.outrow[i] = (int16_t)i; }

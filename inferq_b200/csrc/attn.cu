@@ -7,7 +7,7 @@
 // sigmoid(gate).
 //
 // The scan is split over fixed position chunks of kAttnChunk: chunk c covers
-// absolute positions [c*64, c*64+64) for every pass, each chunk keeps an
+// absolute positions [c*32, c*32+32) for every pass, each chunk keeps an
 // online-softmax partial per query, and a row merges its chunks in order.
 // A row's output therefore depends only on its own context length.
 #include "model_kernels.cuh"
@@ -74,61 +74,82 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(AttnArgs a) {
   }
 }
 
-// grid (nkv, query groups of 8, chunk_ctas).  Warp w owns query
-// q = group*8 + w (q = t*G + g over the rows and the G query heads of this kv
-// head); lane l holds dims [l*D, l*D+D) with D = hd/32.  Each CTA walks chunks
-// c = blockIdx.z, +chunk_ctas, ... and writes one partial {m, l, acc[hd]}.
+// grid (nkv, chunks): CTA (h, c) stages K and V of positions
+// [c*32, c*32+32) of kv head h in shared memory, then every warp takes the
+// queries q = t*G + g of this kv head in turn: lane p scores position p,
+// the warp forms the chunk's softmax partial {m, l} with butterflies, and
+// lane l accumulates dims [l*D, l*D+D) of sum_p e_p V[p].  A chunk's partial
+// depends only on the query and the positions inside it.
 template <int D>
 __global__ void __launch_bounds__(256) attn_scan_kernel(AttnArgs a) {
   pdl_wait();
   pdl_trigger();
-  const int kvh = blockIdx.x;
+  constexpr int HD = 32 * D;
+  extern __shared__ float sm[];
+  float* Ks = sm;                       // [32][HD + 1]
+  float* Vs = Ks + 32 * (HD + 1);       // [32][HD]
+  float* Qs = Vs + 32 * HD;             // [8 warps][HD]
+  const int kvh = blockIdx.x, c = blockIdx.y;
   const int G = a.nh / a.nkv;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q = blockIdx.y * 8 + warp;
-  const int nq = a.rows * G;
-  if (q >= nq) return;
-  const int t = q / G, g = q % G;
-  const int h = kvh * G + g;
   const int pos0 = *a.pos;
-  const int attend = pos0 + t + 1;  // positions 0 .. pos0+t
-  const int nchunks = (attend + kAttnChunk - 1) / kAttnChunk;
-  const float scale = __fdiv_rn(1.f, sqrtf((float)a.hd));
-  float qv[D];
-  const float* qsrc = a.qbuf + ((int64_t)t * a.nh + h) * a.hd + lane * D;
+  const int last = pos0 + a.rows - 1;   // last position any row attends to
+  const int p0 = c * kAttnChunk;
+  if (p0 > last) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // stage K (padded rows) and V of the chunk
+  for (int i = threadIdx.x; i < 32 * HD / 4; i += 256) {
+    const int p = i / (HD / 4), d4 = i % (HD / 4);
+    const int pp = min(p0 + p, last);
+    const float4 kv = *reinterpret_cast<const float4*>(a.kcache + ((int64_t)pp * a.nkv + kvh) * HD + 4 * d4);
+    const float4 vv = *reinterpret_cast<const float4*>(a.vcache + ((int64_t)pp * a.nkv + kvh) * HD + 4 * d4);
+    float* kr = Ks + p * (HD + 1) + 4 * d4;
+    kr[0] = kv.x; kr[1] = kv.y; kr[2] = kv.z; kr[3] = kv.w;
+    *reinterpret_cast<float4*>(Vs + p * HD + 4 * d4) = vv;
+  }
+  __syncthreads();
+  const float scale = __fdiv_rn(1.f, sqrtf((float)HD));
+  const int nchunks_total = (last + kAttnChunk) / kAttnChunk;
+  float* qs = Qs + warp * HD;
+  for (int q = warp; q < a.rows * G; q += 8) {
+    const int t = q / G, g = q % G, h = kvh * G + g;
+    const int attend_last = pos0 + t;
+    if (p0 > attend_last) continue;  // this chunk is entirely in row t's future
+    const float* qsrc = a.qbuf + ((int64_t)t * a.nh + h) * HD;
 #pragma unroll
-  for (int d = 0; d < D; d++) qv[d] = qsrc[d];
-  const int max_chunks = (pos0 + a.rows + kAttnChunk - 1) / kAttnChunk;
-  for (int c = blockIdx.z; c < max_chunks; c += gridDim.z) {
-    float* part = a.part + (((int64_t)t * a.nh + h) * max_chunks + c) * (a.hd + 2);
-    if (c >= nchunks) {
-      if (lane == 0) { part[0] = -INFINITY; part[1] = 0.f; }
-      continue;
+    for (int d = 0; d < D; d++) qs[lane * D + d] = qsrc[lane * D + d];
+    __syncwarp();
+    const float* kr = Ks + lane * (HD + 1);
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll 8
+    for (int d = 0; d < HD; d += 4) {
+      s0 = fmaf(qs[d], kr[d], s0);
+      s1 = fmaf(qs[d + 1], kr[d + 1], s1);
+      s2 = fmaf(qs[d + 2], kr[d + 2], s2);
+      s3 = fmaf(qs[d + 3], kr[d + 3], s3);
     }
-    const int p0 = c * kAttnChunk, p1 = min(attend, p0 + kAttnChunk);
-    float m = -INFINITY, l = 0.f, acc[D];
+    const bool valid = p0 + lane <= attend_last;
+    float sc = valid ? __fmul_rn(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)), scale) : -INFINITY;
+    float m = sc;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float e = valid ? expf(sc - m) : 0.f;
+    float l = e;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
+    float acc[D];
 #pragma unroll
     for (int d = 0; d < D; d++) acc[d] = 0.f;
-    for (int p = p0; p < p1; p++) {
-      const float* kr = a.kcache + ((int64_t)p * a.nkv + kvh) * a.hd + lane * D;
-      float s = 0.f;
+    for (int p = 0; p < 32; p++) {
+      const float ep = __shfl_sync(0xffffffffu, e, p);
+      const float* vr = Vs + p * HD + lane * D;
 #pragma unroll
-      for (int d = 0; d < D; d++) s = fmaf(qv[d], kr[d], s);
-#pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-      s = __fmul_rn(s, scale);
-      const float mn = fmaxf(m, s);
-      const float corr = expf(m - mn);
-      const float e = expf(s - mn);
-      l = fmaf(l, corr, e);
-      const float* vr = a.vcache + ((int64_t)p * a.nkv + kvh) * a.hd + lane * D;
-#pragma unroll
-      for (int d = 0; d < D; d++) acc[d] = fmaf(acc[d], corr, __fmul_rn(e, vr[d]));
-      m = mn;
+      for (int d = 0; d < D; d++) acc[d] = fmaf(ep, vr[d], acc[d]);
     }
+    float* part = a.part + (((int64_t)t * a.nh + h) * nchunks_total + c) * (HD + 2);
     if (lane == 0) { part[0] = m; part[1] = l; }
 #pragma unroll
     for (int d = 0; d < D; d++) part[2 + lane * D + d] = acc[d];
+    __syncwarp();
   }
 }
 
@@ -139,8 +160,8 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a) {
   const int t = blockIdx.x / a.nh, h = blockIdx.x % a.nh;
   const int pos0 = *a.pos;
   const int nchunks = (pos0 + t + 1 + kAttnChunk - 1) / kAttnChunk;
-  const int max_chunks = (pos0 + a.rows + kAttnChunk - 1) / kAttnChunk;
-  const float* part = a.part + ((int64_t)t * a.nh + h) * max_chunks * (a.hd + 2);
+  const int nchunks_total = (pos0 + a.rows - 1 + kAttnChunk) / kAttnChunk;
+  const float* part = a.part + ((int64_t)t * a.nh + h) * nchunks_total * (a.hd + 2);
   float M = -INFINITY;
   for (int c = 0; c < nchunks; c++) M = fmaxf(M, part[c * (a.hd + 2)]);
   const int i = threadIdx.x;
@@ -157,6 +178,16 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a) {
   a.out[(int64_t)t * a.out_ld + (int64_t)h * a.hd + i] = __fmul_rn(o, sigmoidf_ref(gate));
 }
 
+template <int D>
+cudaError_t launch_scan(dim3 grid, size_t smem, cudaStream_t st, bool pdl, const AttnArgs& a) {
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(attn_scan_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, 80 * 1024);
+    configured = true;
+  }
+  return launch_pdl(attn_scan_kernel<D>, grid, dim3(256), smem, st, pdl, a);
+}
+
 }  // namespace
 
 cudaError_t attn_prep_launch(const AttnArgs& a, cudaStream_t st, bool pdl) {
@@ -164,12 +195,12 @@ cudaError_t attn_prep_launch(const AttnArgs& a, cudaStream_t st, bool pdl) {
 }
 
 cudaError_t attn_scan_launch(const AttnArgs& a, cudaStream_t st, bool pdl) {
-  const int G = a.nh / a.nkv;
-  dim3 grid(a.nkv, (unsigned)ceil_div(a.rows * G, 8), a.chunk_ctas);
+  dim3 grid(a.nkv, a.chunk_ctas);
+  const size_t smem = (size_t)(32 * (a.hd + 1) + 32 * a.hd + 8 * a.hd) * sizeof(float);
   switch (a.hd / 32) {
-    case 2: return launch_pdl(attn_scan_kernel<2>, grid, dim3(256), 0, st, pdl, a);
-    case 4: return launch_pdl(attn_scan_kernel<4>, grid, dim3(256), 0, st, pdl, a);
-    case 8: return launch_pdl(attn_scan_kernel<8>, grid, dim3(256), 0, st, pdl, a);
+    case 2: return launch_scan<2>(grid, smem, st, pdl, a);
+    case 4: return launch_scan<4>(grid, smem, st, pdl, a);
+    case 8: return launch_scan<8>(grid, smem, st, pdl, a);
     default: return cudaErrorInvalidValue;
   }
 }

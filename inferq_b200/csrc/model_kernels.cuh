@@ -59,12 +59,12 @@ struct AttnArgs {
   double theta;
   float eps;
   const int* pos;                // device: position of row 0
-  int chunk_ctas;                // CTAs per (kv head, query group) walking the chunks
+  int chunk_ctas;                // chunks the grid covers: ceil(max positions / kAttnChunk)
 };
 // Positions per split of the scan.  Chunk c always covers absolute positions
 // [c*kAttnChunk, (c+1)*kAttnChunk), and a row combines its chunks in order, so
 // a row's output depends only on its own context, never on the pass it ran in.
-constexpr int kAttnChunk = 64;
+constexpr int kAttnChunk = 32;
 cudaError_t attn_prep_launch(const AttnArgs& a, cudaStream_t st, bool pdl);
 cudaError_t attn_scan_launch(const AttnArgs& a, cudaStream_t st, bool pdl);
 cudaError_t attn_combine_launch(const AttnArgs& a, cudaStream_t st, bool pdl);

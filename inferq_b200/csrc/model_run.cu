@@ -8,6 +8,7 @@
 // launch, and the whole pass is captured once per row count into a CUDA graph.
 #include <algorithm>
 #include <cstring>
+#include <cstdlib>
 #include <string>
 #include "model.h"
 
@@ -109,6 +110,7 @@ QmvJob make_job(const Weight& w, const uint8_t* act, int64_t arb, float* out, in
   j.cols = (int)w.cols;
   j.ksplit = qmv_ksplit(w.dt, w.rows, w.cols);
   j.n = k;
+  j.act_nrows = k;
   j.epi = epi;
   for (int i = 0; i < 8; i++) {
     j.rowmap[i] = (uint8_t)(i < k ? i : 0);
@@ -140,7 +142,9 @@ struct Ctx {
   const iq_config& c;
   cudaStream_t st;
   bool pdl;
-  Ctx(iq_state* s_) : s(s_), m(s_->m), c(s_->m->cfg), st(s_->st), pdl(!s_->profiling) {}
+  // IQ_NO_PDL=1 turns programmatic dependent launch off (kernel timing,
+  // debugging); results are identical either way.
+  Ctx(iq_state* s_) : s(s_), m(s_->m), c(s_->m->cfg), st(s_->st), pdl(!s_->profiling && !getenv("IQ_NO_PDL")) {}
   // Stage timer: under profiling every stage is bracketed by CUDA events.
   void mark(const char* name) {
     if (!s->profiling) return;
@@ -299,8 +303,8 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   t.down_row_bytes = W.down.row_bytes;
   t.gate_dt = W.gate.dt;
   t.down_dt = W.down.dt;
-  t.ks_gate = qmv_ksplit(W.gate.dt, F, H);
-  t.ks_down = qmv_ksplit(W.down.dt, H, F);
+  t.ks_gate = qmv_ksplit(W.gate.dt, F, H, true);
+  t.ks_down = qmv_ksplit(W.down.dt, H, F, true);
   t.tiles_gate = (int)ceil_div(F, qmv_rows_per_cta(t.ks_gate));
   t.tiles_down = (int)ceil_div(H, qmv_rows_per_cta(t.ks_down));
   t.sh_gate = W.sh_gate.p();
@@ -310,8 +314,8 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   t.sh_down_row_bytes = W.sh_down.row_bytes;
   t.sh_gate_dt = W.sh_gate.dt;
   t.sh_down_dt = W.sh_down.dt;
-  t.ks_sh_gate = qmv_ksplit(W.sh_gate.dt, Fs, H);
-  t.ks_sh_down = qmv_ksplit(W.sh_down.dt, H, Fs);
+  t.ks_sh_gate = qmv_ksplit(W.sh_gate.dt, Fs, H, true);
+  t.ks_sh_down = qmv_ksplit(W.sh_down.dt, H, Fs, true);
   t.tiles_sh_gate = (int)ceil_div(Fs, qmv_rows_per_cta(t.ks_sh_gate));
   t.with_shared = 1;
   t.expert_lo = W.expert_lo;
@@ -346,7 +350,7 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   IQ_CUDA(moe_act_launch(b, x.st, x.pdl));
   x.mark("moe.act");
   ++x.s->launch_count;
-  IQ_CUDA(qmv_launch(a.down_jobs, 0, a.down_count, down_tiles, 8 * (int)s->act_mid_bytes, x.st, x.pdl));
+  IQ_CUDA(qmv_launch(a.down_jobs, 0, a.down_count, down_tiles, (k * c.num_experts_per_tok + k) * (int)s->act_mid_bytes, x.st, x.pdl));
   x.mark("moe.down");
   // expert parallelism: the all-gather of y happens here (model_ep.cu)
   MoeCombineArgs cb = {};
@@ -460,7 +464,7 @@ int run_attention(Ctx& x, const Layer& L, const LayerRec& R, int k, int fi) {
   a.theta = c.rope_theta;
   a.eps = c.rms_norm_eps;
   a.pos = x.pos();
-  a.chunk_ctas = 16;
+  a.chunk_ctas = s->max_chunks;
   ++x.s->launch_count;
   IQ_CUDA(attn_prep_launch(a, x.st, x.pdl));
   x.mark("attn.prep");
@@ -670,8 +674,8 @@ int alloc_state(iq_state* s) {
   s->kc.resize(m->n_full + (m->has_mtp ? 1 : 0));
   s->vc.resize(s->kc.size());
   for (size_t i = 0; i < s->kc.size(); i++) {
-    IQ_CUDA(s->kc[i].reserve((size_t)(s->max_pos * kvd * 4)));
-    IQ_CUDA(s->vc[i].reserve((size_t)(s->max_pos * kvd * 4)));
+    IQ_CUDA(s->kc[i].reserve((size_t)(align_up(s->max_pos + kMaxK, kAttnChunk) * kvd * 4)));
+    IQ_CUDA(s->vc[i].reserve((size_t)(align_up(s->max_pos + kMaxK, kAttnChunk) * kvd * 4)));
   }
   const int64_t maxcols = std::max({H, vdim, nhd, 2 * H});
   s->act8k_bytes = act_row_bytes_q8k(maxcols);

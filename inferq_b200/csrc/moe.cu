@@ -18,7 +18,7 @@ constexpr int kMaxExperts = 1024;
 
 __device__ __forceinline__ void set_job(QmvJob& j, const uint8_t* w, int64_t w_row_bytes, int dt, int rows, int cols,
                                         int ks, const uint8_t* act, int act_bytes, float* out, int out_ld, int n,
-                                        int tile0) {
+                                        int tile0, int act_nrows) {
   j.w = w;
   j.act = act;
   j.out = out;
@@ -32,43 +32,56 @@ __device__ __forceinline__ void set_job(QmvJob& j, const uint8_t* w, int64_t w_r
   j.ksplit = ks;
   j.n = n;
   j.tile0 = tile0;
+  j.act_nrows = act_nrows;
   j.epi = kEpiStore;
 }
 
-// One CTA.  Warp t < rows routes row t; then every thread e examines expert
-// e (and e + 256, ...) and, if it is in the union and resident, writes that
-// expert's gate, up and down jobs at its rank in the ascending union.
+// One CTA.  Warp t < rows routes row t with its probabilities in registers
+// (lane l holds experts l, l+32, ...): top-k by repeated warp arg-max, equal
+// probabilities ranking the lower expert first.  Then thread e owns experts
+// [e*per, e*per+per), finds their rank in the ascending union with warp
+// ballots, and writes the gate, up and down jobs of its resident ones.
 __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRouteStatic s) {
   pdl_wait();
   pdl_trigger();
+  constexpr int kPerLane = kMaxExperts / 32;
   __shared__ int sel_e[kMaxRows][16];
   __shared__ float sel_w[kMaxRows][16];
   __shared__ unsigned used[kMaxExperts / 32];
-  __shared__ int scan[256];
+  __shared__ int wcount[2][8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = a.experts;
   for (int i = threadIdx.x; i < kMaxExperts / 32; i += 256) used[i] = 0;
   __syncthreads();
   if (warp < a.rows) {
     const float* lg = a.logits + (int64_t)warp * a.logits_ld;
+    float p[kPerLane];
     float mx = -INFINITY;
-    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+#pragma unroll
+    for (int i = 0; i < kPerLane; i++) {
+      const int e = lane + 32 * i;
+      p[i] = e < E ? lg[e] : -INFINITY;
+      mx = fmaxf(mx, p[i]);
+    }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float den = 0.f;
-    for (int e = lane; e < E; e += 32) den = __fadd_rn(den, expf(lg[e] - mx));
+#pragma unroll
+    for (int i = 0; i < kPerLane; i++) {
+      p[i] = lane + 32 * i < E ? expf(p[i] - mx) : 0.f;
+      den = __fadd_rn(den, p[i]);
+    }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) den = __fadd_rn(den, __shfl_xor_sync(0xffffffffu, den, o));
-    // top-k by probability; equal probabilities rank the lower expert first
+#pragma unroll
+    for (int i = 0; i < kPerLane; i++) p[i] = lane + 32 * i < E ? __fdiv_rn(p[i], den) : -1.f;
     for (int r = 0; r < a.topk; r++) {
-      float best = -INFINITY;
+      float best = -1.f;
       int bi = 0x7fffffff;
-      for (int e = lane; e < E; e += 32) {
-        bool tk = false;
-        for (int q = 0; q < r; q++) tk |= sel_e[warp][q] == e;
-        if (tk) continue;
-        const float p = __fdiv_rn(expf(lg[e] - mx), den);
-        if (p > best || (p == best && e < bi)) { best = p; bi = e; }
+#pragma unroll
+      for (int i = 0; i < kPerLane; i++) {
+        const int e = lane + 32 * i;
+        if (p[i] > best) { best = p[i]; bi = e; }  // ascending e: ties keep the lower
       }
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1) {
@@ -76,14 +89,18 @@ __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRoute
         const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
         if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
       }
+#pragma unroll
+      for (int i = 0; i < kPerLane; i++)
+        if (lane + 32 * i == bi) p[i] = -1.f;
       if (lane == 0) { sel_e[warp][r] = bi; sel_w[warp][r] = best; }
-      __syncwarp();
     }
+    __syncwarp();
     if (lane == 0) {
       float sum = 0.f;
       for (int r = 0; r < a.topk; r++) sum = __fadd_rn(sum, sel_w[warp][r]);
       for (int r = 0; r < a.topk; r++) {
         const float w = a.norm_topk ? __fdiv_rn(sel_w[warp][r], sum) : sel_w[warp][r];
+        sel_w[warp][r] = w;
         a.route_expert[warp * a.topk + r] = sel_e[warp][r];
         a.route_weight[warp * a.topk + r] = w;
         atomicOr(&used[sel_e[warp][r] / 32], 1u << (sel_e[warp][r] % 32));
@@ -91,43 +108,32 @@ __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRoute
     }
   }
   __syncthreads();
-  // rank of each used+resident expert in the ascending union
-  const int per = (E + 255) / 256;  // experts per thread, contiguous
-  int mine = 0;
+  // union ranks: thread-contiguous experts, warp ballots, then warp prefix
+  const int per = (E + 255) / 256;
+  int mine = 0, rmine = 0;
   for (int q = 0; q < per; q++) {
     const int e = threadIdx.x * per + q;
-    if (e < E && ((used[e / 32] >> (e % 32)) & 1)) mine++;
+    if (e < E && ((used[e / 32] >> (e % 32)) & 1)) {
+      mine++;
+      if (e >= s.expert_lo && e < s.expert_hi) rmine++;
+    }
   }
-  scan[threadIdx.x] = mine;
+  int inc = mine, rinc = rmine;  // inclusive warp scans
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, inc, o), rv = __shfl_up_sync(0xffffffffu, rinc, o);
+    if (lane >= o) { inc += v; rinc += rv; }
+  }
+  if (lane == 31) { wcount[0][warp] = inc; wcount[1][warp] = rinc; }
   __syncthreads();
-  for (int o = 1; o < 256; o <<= 1) {
-    const int v = threadIdx.x >= o ? scan[threadIdx.x - o] : 0;
-    __syncthreads();
-    scan[threadIdx.x] += v;
-    __syncthreads();
+  int base = 0, rbase = 0, total_union = 0, n_res = 0;
+  for (int w = 0; w < 8; w++) {
+    if (w < warp) { base += wcount[0][w]; rbase += wcount[1][w]; }
+    total_union += wcount[0][w];
+    n_res += wcount[1][w];
   }
-  int rank = scan[threadIdx.x] - mine;  // exclusive prefix: union index of my first expert
-  const int total_union = scan[255];
-  int res_rank = 0;  // resident union rank (jobs exist only for resident experts)
-  {
-    // count resident union experts before mine: recompute with a second scan
-    int rmine = 0;
-    for (int q = 0; q < per; q++) {
-      const int e = threadIdx.x * per + q;
-      if (e < E && ((used[e / 32] >> (e % 32)) & 1) && e >= s.expert_lo && e < s.expert_hi) rmine++;
-    }
-    __syncthreads();
-    scan[threadIdx.x] = rmine;
-    __syncthreads();
-    for (int o = 1; o < 256; o <<= 1) {
-      const int v = threadIdx.x >= o ? scan[threadIdx.x - o] : 0;
-      __syncthreads();
-      scan[threadIdx.x] += v;
-      __syncthreads();
-    }
-    res_rank = scan[threadIdx.x] - rmine;
-  }
-  const int n_res = scan[255];
+  int rank = base + inc - mine;
+  int res_rank = rbase + rinc - rmine;
   const int slots_routed = a.rows * a.topk;
   for (int q = 0; q < per; q++) {
     const int e = threadIdx.x * per + q;
@@ -141,15 +147,15 @@ __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRoute
     const uint8_t* ain = q80 ? a.act_in80 : a.act_in8k;
     const int ab = q80 ? a.act_in80_bytes : a.act_in8k_bytes;
     set_job(gj, s.gate + le * s.gate_stride, s.gate_row_bytes, s.gate_dt, a.ffn, a.hidden, s.ks_gate, ain, ab,
-            a.gu_out, a.gu_ld, 0, 2 * ri * s.tiles_gate);
+            a.gu_out, a.gu_ld, 0, 2 * ri * s.tiles_gate, a.rows);
     set_job(uj, s.up + le * s.up_stride, s.gate_row_bytes, s.gate_dt, a.ffn, a.hidden, s.ks_gate, ain, ab,
-            a.gu_out + a.ffn, a.gu_ld, 0, (2 * ri + 1) * s.tiles_gate);
+            a.gu_out + a.ffn, a.gu_ld, 0, (2 * ri + 1) * s.tiles_gate, a.rows);
     set_job(dj, s.down + le * s.down_stride, s.down_row_bytes, s.down_dt, a.hidden, a.ffn, s.ks_down, a.act_mid,
-            a.act_mid_bytes, a.y, a.y_ld, 0, ri * s.tiles_down);
+            a.act_mid_bytes, a.y, a.y_ld, 0, ri * s.tiles_down, slots_routed + a.rows);
     int n = 0;
     for (int t = 0; t < a.rows; t++)
       for (int r = 0; r < a.topk; r++)
-        if (a.route_expert[t * a.topk + r] == e) {
+        if (sel_e[t][r] == e) {
           const int slot = t * a.topk + r;
           gj.rowmap[n] = uj.rowmap[n] = (uint8_t)t;
           gj.outrow[n] = uj.outrow[n] = (int16_t)slot;
@@ -169,11 +175,11 @@ __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRoute
     const uint8_t* ain = q80 ? a.act_in80 : a.act_in8k;
     const int ab = q80 ? a.act_in80_bytes : a.act_in8k_bytes;
     set_job(gj, s.sh_gate, s.sh_gate_row_bytes, s.sh_gate_dt, a.sh_ffn, a.hidden, s.ks_sh_gate, ain, ab, a.gu_out,
-            a.gu_ld, a.rows, 2 * n_res * s.tiles_gate);
+            a.gu_ld, a.rows, 2 * n_res * s.tiles_gate, a.rows);
     set_job(uj, s.sh_up, s.sh_gate_row_bytes, s.sh_gate_dt, a.sh_ffn, a.hidden, s.ks_sh_gate, ain, ab,
-            a.gu_out + a.sh_ffn, a.gu_ld, a.rows, 2 * n_res * s.tiles_gate + s.tiles_sh_gate);
+            a.gu_out + a.sh_ffn, a.gu_ld, a.rows, 2 * n_res * s.tiles_gate + s.tiles_sh_gate, a.rows);
     set_job(dj, s.sh_down, s.sh_down_row_bytes, s.sh_down_dt, a.hidden, a.sh_ffn, s.ks_sh_down, a.act_mid,
-            a.act_mid_bytes, a.y, a.y_ld, a.rows, n_res * s.tiles_down);
+            a.act_mid_bytes, a.y, a.y_ld, a.rows, n_res * s.tiles_down, slots_routed + a.rows);
     for (int t = 0; t < a.rows; t++) {
       gj.rowmap[t] = uj.rowmap[t] = (uint8_t)t;
       gj.outrow[t] = uj.outrow[t] = (int16_t)(slots_routed + t);

@@ -95,6 +95,7 @@ extern "C" int iq_matrix_forward_device_noalloc(const iq_matrix* m, const float*
   j.cols = (int)m->cols;
   j.ksplit = qmv_ksplit(m->dtype, m->rows, m->cols);
   j.n = input_rows;
+  j.act_nrows = input_rows;
   j.epi = kEpiStore;
   for (int i = 0; i < 8; i++) {
     j.rowmap[i] = (uint8_t)(i < input_rows ? i : 0);

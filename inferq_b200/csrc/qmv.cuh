@@ -31,6 +31,7 @@ struct QmvJob {
   int out_ld;
   int dtype, rows, cols, ksplit;
   int n;                 // input rows used, 1..8
+  int act_nrows;         // rows of `act` staged into shared memory (> every rowmap entry)
   int tile0;             // first global tile of this job
   int epi;
   uint8_t rowmap[8];     // activation row of input column i
@@ -43,11 +44,15 @@ __host__ __device__ inline int qmv_units(int dt, int cols) {
   return dt == Q8_0 ? cols / 128 : cols / 256;
 }
 
-// The chunk count of a matrix: a function of its shape only.
-inline int qmv_ksplit(int dt, int64_t rows, int64_t cols) {
+// The chunk count of a matrix: a function of its shape only (never of the
+// number of input rows), so a row's f32 accumulation order is fixed.
+// Expert matrices (`expert`: one of many small matrices in the same launch)
+// split less, so each warp streams several blocks.
+inline int qmv_ksplit(int dt, int64_t rows, int64_t cols, bool expert = false) {
   int units = qmv_units(dt, (int)cols);
+  const int64_t target = expert ? 64 : 148 * 32;
   int ks = 1;
-  while (ks < 8 && units % (ks * 2) == 0 && (rows / 16) * ks < 148 * 32) ks *= 2;
+  while (ks < 8 && units % (ks * 2) == 0 && (rows / 16) * ks < target) ks *= 2;
   return ks;
 }
 inline int qmv_tiles(const QmvJob& j) {

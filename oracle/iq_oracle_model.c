@@ -116,22 +116,25 @@ static int g_order = 0;
 void or_set_gemv_order(int order) { g_order = order; }
 
 /* The device's chunk count for a matrix shape (a function of shape only). */
-static int device_ksplit(int dt, int64_t rows, int64_t cols) {
+static int device_ksplit(int dt, int64_t rows, int64_t cols, int expert) {
     if (dt == OR_F32) return 1;
     int units = (int)(dt == OR_Q8_0 ? cols / 128 : cols / 256);
+    int64_t target = expert ? 64 : 148 * 32;
     int ks = 1;
-    while (ks < 8 && units % (ks * 2) == 0 && (rows / 16) * ks < 148 * 32) ks *= 2;
+    while (ks < 8 && units % (ks * 2) == 0 && (rows / 16) * ks < target) ks *= 2;
     return ks;
 }
 
 /* y[rows] = W x  (one input row) */
-static void matvec_n(const mat_t* m, const uint8_t* p, int64_t n, const float* x, float* y) {
-    or_qmatvec(m->dt, p, n, m->cols, x, 1, y, g_order, g_order ? device_ksplit(m->dt, n, m->cols) : 1);
+static void matvec_n(const mat_t* m, const uint8_t* p, int64_t n, const float* x, float* y, int expert) {
+    or_qmatvec(m->dt, p, n, m->cols, x, 1, y, g_order, g_order ? device_ksplit(m->dt, n, m->cols, expert) : 1);
 }
-static void matvec(const mat_t* m, const float* x, float* y) { matvec_n(m, m->p, m->rows, x, y); }
-/* rows [r0, r0+n) of a stacked matrix */
+static void matvec(const mat_t* m, const float* x, float* y) { matvec_n(m, m->p, m->rows, x, y, 0); }
+/* an expert-class matrix (routed or shared expert) */
+static void matvec_e(const mat_t* m, const float* x, float* y) { matvec_n(m, m->p, m->rows, x, y, 1); }
+/* rows [r0, r0+n) of a stacked expert matrix */
 static void matvec_rows(const mat_t* m, int64_t r0, int64_t n, const float* x, float* y) {
-    matvec_n(m, m->p + r0 * or_row_bytes(m->dt, m->cols), n, x, y);
+    matvec_n(m, m->p + r0 * or_row_bytes(m->dt, m->cols), n, x, y, 1);
 }
 
 static float sigmoid_ref(float v) { return 1.f / (1.f + expf(-v)); }
@@ -481,10 +484,10 @@ static void moe_row(const or_model* m, const layer_t* L, const float* x, float* 
         matvec_rows(&L->down, (int64_t)e * H, H, g, y);
         for (int i = 0; i < H; i++) out[i] += y[i] * w[r];
     }
-    matvec(&L->sh_gate, x, g);
-    matvec(&L->sh_up, x, u);
+    matvec_e(&L->sh_gate, x, g);
+    matvec_e(&L->sh_up, x, u);
     for (int i = 0; i < Fs; i++) g[i] = (g[i] / (1.f + expf(-g[i]))) * u[i];
-    matvec(&L->sh_down, g, y);
+    matvec_e(&L->sh_down, g, y);
     float sel = 0.f;
     for (int i = 0; i < H; i++) sel += x[i] * L->selector[i];
     sel = 1.f / (1.f + expf(-sel));
@@ -554,7 +557,7 @@ int or_mtp_forward(const or_model* m, or_state* s, uint32_t token, const float* 
     layer_row(m, &m->mtp, &s->mtp, s->mtp_position, h, NULL);
     rms_norm(h, m->head_norm, H, c->rms_norm_eps, tmp);
     if (hidden_out) memcpy(hidden_out, tmp, (size_t)H * 4);
-    if (logits && head_rows > 0) matvec_n(&m->lm_head, m->lm_head.p, head_rows, tmp, logits);
+    if (logits && head_rows > 0) matvec_n(&m->lm_head, m->lm_head.p, head_rows, tmp, logits, 0);
     s->mtp_position++;
     free(e); free(tmp); free(h);
     return 0;
