@@ -9,7 +9,8 @@ namespace {
 
 __global__ void __launch_bounds__(256) f32_matvec_kernel(const float* __restrict__ w, int rows, int cols,
                                                          const float* __restrict__ x, int ldx, int k,
-                                                         float* __restrict__ y, int ldy) {
+                                                         float* __restrict__ y, int ldy, const float* norm_w,
+                                                         float eps, float inv_cols) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ float4 xs4[];  // [k][cols/4]
@@ -19,6 +20,23 @@ __global__ void __launch_bounds__(256) f32_matvec_kernel(const float* __restrict
     xs4[i] = *reinterpret_cast<const float4*>(x + (int64_t)r * ldx + 4 * c);
   }
   __syncthreads();
+  if (norm_w) {  // GGUF RMSNorm of the staged rows (same order as the GEMV prologue)
+    __shared__ float den[8];
+    const float* xs = reinterpret_cast<const float*>(xs4);
+    const int wp = threadIdx.x >> 5, ln = threadIdx.x & 31;
+    if (wp < k) {
+      float ss = 0.f;
+      for (int i = ln; i < cols; i += 32) ss = fmaf(xs[wp * cols + i], xs[wp * cols + i], ss);
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      if (ln == 0) den[wp] = sqrtf(__fadd_rn(__fmul_rn(ss, inv_cols), eps));
+    }
+    __syncthreads();
+    float* xw = reinterpret_cast<float*>(xs4);
+    for (int i = threadIdx.x; i < k * cols; i += 256)
+      xw[i] = __fmul_rn(__fdiv_rn(xw[i], den[i / cols]), norm_w[i % cols]);
+    __syncthreads();
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * 8 + warp;
   if (r >= rows) return;
@@ -60,7 +78,7 @@ __global__ void __launch_bounds__(256) f32_matvec_kernel(const float* __restrict
 }  // namespace
 
 cudaError_t f32_matvec(const float* w, int rows, int cols, const float* x, int ldx, int k, float* y, int ldy,
-                       cudaStream_t st, bool pdl) {
+                       cudaStream_t st, bool pdl, const float* norm_w, float eps) {
   if (cols % 4 || cols > 4096 || k < 1 || k > 8) return cudaErrorInvalidValue;
   static bool configured = false;
   if (!configured) {
@@ -77,7 +95,8 @@ cudaError_t f32_matvec(const float* w, int rows, int cols, const float* x, int l
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, f32_matvec_kernel, w, rows, cols, x, ldx, k, y, ldy);
+  return cudaLaunchKernelEx(&cfg, f32_matvec_kernel, w, rows, cols, x, ldx, k, y, ldy, norm_w, eps,
+                            (float)(1.0 / (double)cols));
 }
 
 }  // namespace iq

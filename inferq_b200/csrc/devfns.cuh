@@ -44,11 +44,7 @@ __device__ __forceinline__ float dev_weight(int dt, const uint8_t* row, int nb, 
     case Q6_K: {
       const int b = e / 256, i = e % 256;
       const uint8_t* blk = row + (int64_t)b * 208;
-      const int half = i / 128, l = i % 128;
-      const int qli = half * 64 + (l % 64), qhi = half * 32 + (l % 32);
-      int nib = (blk[q6k_ql_perm(qli)] >> (4 * (l / 64))) & 15;
-      int hb = (blk[128 + q6k_qh_perm(qhi)] >> (2 * (l / 32))) & 3;
-      const int q = (nib | (hb << 4)) - 32;
+      const int q = q6k_dev_value(blk, i) - 32;
       const float d = h2f(*reinterpret_cast<const uint16_t*>(row + (int64_t)nb * 208 + 2 * b));
       const float sc = (float)reinterpret_cast<const int8_t*>(blk + 192)[i / 16];
       return __fmul_rn(__fmul_rn(d, sc), (float)q);
@@ -69,13 +65,11 @@ __device__ __forceinline__ float dev_weight(int dt, const uint8_t* row, int nb, 
 // 32s + 16h + tig*4 + e (h, e in order), which is exactly the 8 contiguous
 // bytes it writes to the permuted layout.  Semantics: candle
 // BlockQ8K::from_float (first value of largest magnitude sets the scale).
-__device__ __forceinline__ void quant_q8k_block_warp(const float* x, uint8_t* act_row, int nb, int b, int lane) {
+// v[4h + e] is element 32s + 16h + 4tig + e of block b (s = lane & 7,
+// tig = lane >> 3): two runs of four contiguous floats.
+__device__ __forceinline__ void quant_q8k_block_warp_v(const float (&v)[8], uint8_t* act_row, int nb, int b,
+                                                       int lane) {
   const int s = lane & 7, tig = lane >> 3;
-  float v[8];
-#pragma unroll
-  for (int h = 0; h < 2; h++)
-#pragma unroll
-    for (int e = 0; e < 4; e++) v[h * 4 + e] = x[b * 256 + 32 * s + 16 * h + tig * 4 + e];
   float amax = 0.f, vmax = 0.f;
   int imax = 1 << 30;
 #pragma unroll
@@ -115,20 +109,21 @@ __device__ __forceinline__ void quant_q8k_block_warp(const float* x, uint8_t* ac
   packed.y = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) | ((uint32_t)(uint8_t)q[6] << 16) |
              ((uint32_t)(uint8_t)q[7] << 24);
   *reinterpret_cast<uint2*>(act_row + (int64_t)b * 256 + tig * 64 + s * 8) = packed;
-  int16_t* bs = reinterpret_cast<int16_t*>(act_row + (int64_t)nb * 260 + b * 32);
-  if (tig == 0) { bs[2 * s] = (int16_t)sum[0]; bs[2 * s + 1] = (int16_t)sum[1]; }
+  int16_t* bs = reinterpret_cast<int16_t*>(act_row + q8k_bs_offset(nb) + b * 16);
+  if (tig == 0) bs[s] = (int16_t)(sum[0] + sum[1]);
   if (lane == 0) reinterpret_cast<float*>(act_row + (int64_t)nb * 256)[b] = d;
 }
 
 // One warp per group of four Q8_0 blocks.  Lane l = tig*8 + bb*2 + h holds
 // the 4 elements it writes at byte 4l of the group.  Semantics: candle
 // BlockQ8_0::from_float (d = amax/127 kept as f16; q from the f32 d).
-__device__ __forceinline__ void quant_q80_group_warp(const float* x, uint8_t* act_row, int nb, int g, int lane) {
+// v[e] is element q80_lane_base(g, lane) + e: four contiguous floats.
+__device__ __forceinline__ int q80_lane_base(int g, int lane) {
+  return 32 * (4 * g + ((lane & 7) >> 1)) + 16 * (lane & 1) + (lane >> 3) * 4;
+}
+__device__ __forceinline__ void quant_q80_group_warp_v(const float (&v)[4], uint8_t* act_row, int nb, int g,
+                                                       int lane) {
   const int tig = lane >> 3, bb = (lane & 7) >> 1, h = lane & 1;
-  const int base = 32 * (4 * g + bb) + 16 * h + tig * 4;
-  float v[4];
-#pragma unroll
-  for (int e = 0; e < 4; e++) v[e] = x[base + e];
   float amax = 0.f;
 #pragma unroll
   for (int e = 0; e < 4; e++) amax = fmaxf(amax, fabsf(v[e]));
@@ -143,6 +138,23 @@ __device__ __forceinline__ void quant_q80_group_warp(const float* x, uint8_t* ac
   *reinterpret_cast<uint32_t*>(act_row + (int64_t)g * 128 + lane * 4) = packed;
   if (tig == 0 && h == 0)
     reinterpret_cast<float*>(act_row + (int64_t)nb * 32)[4 * g + bb] = __half2float(__float2half_rn(d));
+}
+
+__device__ __forceinline__ void quant_q8k_block_warp(const float* x, uint8_t* act_row, int nb, int b, int lane) {
+  const int s = lane & 7, tig = lane >> 3;
+  float v[8];
+#pragma unroll
+  for (int h = 0; h < 2; h++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) v[h * 4 + e] = x[b * 256 + 32 * s + 16 * h + tig * 4 + e];
+  quant_q8k_block_warp_v(v, act_row, nb, b, lane);
+}
+__device__ __forceinline__ void quant_q80_group_warp(const float* x, uint8_t* act_row, int nb, int g, int lane) {
+  const int base = q80_lane_base(g, lane);
+  float v[4];
+#pragma unroll
+  for (int e = 0; e < 4; e++) v[e] = x[base + e];
+  quant_q80_group_warp_v(v, act_row, nb, g, lane);
 }
 
 }  // namespace iq

@@ -44,9 +44,12 @@ __host__ __device__ inline int64_t dev_row_bytes(int dt, int64_t cols) {
 }
 // Quantized-activation row bytes: Q8_K {qs[256] permuted, f32 d, i16 bsums[16]}
 // as three planes; Q8_0 {qs[32] permuted, f32 d} as two planes.
+// Q8_K activation row: nb x 256 quants, nb f32 d (padded to 16 B), then
+// nb x 16 B of eight i16 sums of 32 quants.
+__host__ __device__ inline int64_t q8k_bs_offset(int64_t nb) { return nb * 256 + align_up(nb * 4, 16); }
 __host__ __device__ inline int64_t act_row_bytes_q8k(int64_t cols) {
   int64_t nb = cols / 256;
-  return align_up(nb * 256 + nb * 4 + nb * 32, 16);
+  return q8k_bs_offset(nb) + nb * 16;
 }
 __host__ __device__ inline int64_t act_row_bytes_q80(int64_t cols) {
   int64_t nb = cols / 32;

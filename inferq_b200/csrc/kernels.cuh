@@ -28,7 +28,8 @@ cudaError_t dequant_rows(int dt, const uint8_t* w, int64_t row_bytes, int cols, 
 cudaError_t prep_rows(const PrepArgs& a, int rows, cudaStream_t st, bool pdl);
 
 // f32 matrix rows (router): y[i*ld + r] = dot(w[r], x[i]); fixed lane order.
+// With norm_w set, the input rows are first RMS-normalized (GGUF RMSNorm).
 cudaError_t f32_matvec(const float* w, int rows, int cols, const float* x, int ldx, int k, float* y,
-                       int ldy, cudaStream_t st, bool pdl);
+                       int ldy, cudaStream_t st, bool pdl, const float* norm_w = nullptr, float eps = 0.f);
 
 }  // namespace iq

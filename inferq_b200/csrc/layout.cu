@@ -32,8 +32,14 @@ __global__ void gguf_to_dev_kernel(int dt, const uint8_t* __restrict__ src, uint
       } break;
       case Q6_K: {
         uint8_t* o = d + (int64_t)b * 208;
-        for (int i = 0; i < 128; i++) o[q6k_ql_perm(i)] = s[i];
-        for (int i = 0; i < 64; i++) o[128 + q6k_qh_perm(i)] = s[128 + i];
+        for (int tig = 0; tig < 4; tig++)
+          for (int g = 0; g < 4; g++)
+            for (int e = 0; e < 4; e++) {
+              const int v3 = q6k_value(s, 16 * (4 * g + 3) + 4 * tig + e);
+              for (int j = 0; j < 3; j++)
+                o[tig * 48 + g * 12 + 4 * j + e] =
+                    (uint8_t)((q6k_value(s, 16 * (4 * g + j) + 4 * tig + e) << 2) | ((v3 >> (2 * j)) & 3));
+            }
         for (int i = 0; i < 16; i++) o[192 + i] = s[192 + i];
         d[(int64_t)nb * 208 + 2 * b] = s[208];
         d[(int64_t)nb * 208 + 2 * b + 1] = s[209];

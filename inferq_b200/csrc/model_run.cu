@@ -144,7 +144,14 @@ struct Ctx {
   bool pdl;
   // IQ_NO_PDL=1 turns programmatic dependent launch off (kernel timing,
   // debugging); results are identical either way.
-  Ctx(iq_state* s_) : s(s_), m(s_->m), c(s_->m->cfg), st(s_->st), pdl(!s_->profiling && !getenv("IQ_NO_PDL")) {}
+  // IQ_FUSE=1 computes the norm / quantization that precedes a projection
+  // inside every CTA of the GEMV (a prologue) instead of as its own kernel.
+  // Results are identical; the separate kernel is faster on B200 (each CTA
+  // of the fused form waits on a chain of L2 round trips before streaming).
+  bool fuse;
+  Ctx(iq_state* s_)
+      : s(s_), m(s_->m), c(s_->m->cfg), st(s_->st), pdl(!s_->profiling && !getenv("IQ_NO_PDL")),
+        fuse(getenv("IQ_FUSE") != nullptr) {}
   // Stage timer: under profiling every stage is bracketed by CUDA events.
   void mark(const char* name) {
     if (!s->profiling) return;
@@ -181,10 +188,61 @@ int prep(Ctx& x, const float* in, int ld, int cols, const float* norm, int k, bo
   return IQ_OK;
 }
 
-int qmv(Ctx& x, const QmvRec& r) {
+// The activation rows a prologue describes, produced by a separate kernel
+// (unfused mode; the GEMV then stages them from global memory).
+int pre(Ctx& x, const QmvPrologue& p) {
+  if (p.mode == kProGated) {
+    GatedNormArgs g = {};
+    g.o = p.x;
+    g.o_ld = p.ldx;
+    g.z = p.z;
+    g.z_ld = p.ldz;
+    g.w = p.w;
+    g.heads = p.heads;
+    g.dv = p.dv;
+    g.eps = p.eps;
+    g.inv_dv = p.inv_n;
+    g.q8k = p.want8k ? x.s->act8k.as<uint8_t>() : nullptr;
+    g.q80 = p.want80 ? x.s->act80.as<uint8_t>() : nullptr;
+    g.q8k_stride = (int)x.s->act8k_bytes;
+    g.q80_stride = (int)x.s->act80_bytes;
+    ++x.s->launch_count;
+    IQ_CUDA(gated_norm_launch(g, p.rows, x.st, x.pdl));
+    return IQ_OK;
+  }
+  return prep(x, p.x, p.ldx, p.cols, p.mode == kProRmsNorm ? p.w : nullptr, p.rows, p.want8k, p.want80, p.xn_out);
+}
+
+int qmv(Ctx& x, const QmvRec& r, const QmvPrologue* pro = nullptr) {
+  if (pro && !x.fuse) {
+    TRY(pre(x, *pro));
+    pro = nullptr;
+  }
   ++x.s->launch_count;
-  IQ_CUDA(qmv_launch(x.s->jobs.as<QmvJob>() + r.job, r.njobs, nullptr, r.ntiles, r.smem, x.st, x.pdl));
+  IQ_CUDA(qmv_launch(x.s->jobs.as<QmvJob>() + r.job, r.njobs, nullptr, r.ntiles, r.smem, x.st, x.pdl, pro));
   return IQ_OK;
+}
+
+// Prologue that RMS-normalizes (or, norm == null, just quantizes) `k` f32
+// rows of `cols` into the layouts the launch's matrices need.
+QmvPrologue row_pro(Ctx& x, const float* in, int ld, int cols, const float* norm, int k, bool q8k, bool q80,
+                    float* xn = nullptr) {
+  QmvPrologue p = {};
+  p.mode = norm ? kProRmsNorm : kProQuant;
+  p.rows = k;
+  p.cols = cols;
+  p.x = in;
+  p.ldx = ld;
+  p.w = norm;
+  p.eps = x.c.rms_norm_eps;
+  p.inv_n = (float)(1.0 / (double)cols);
+  p.want8k = q8k;
+  p.want80 = q80;
+  p.stride8k = (int)act_row_bytes_q8k(cols);
+  p.stride80 = (int)act_row_bytes_q80(cols);
+  p.xn_out = xn;
+  p.ldxn = cols;
+  return p;
 }
 
 // ------------------------------------------------------------ plan building
@@ -248,19 +306,26 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   const int H = c.hidden_size, E = c.num_experts;
   const bool q8k = needs(W.gate.dt, false) || needs(W.sh_gate.dt, false) || needs(W.router.dt, false);
   const bool q80 = needs(W.gate.dt, true) || needs(W.sh_gate.dt, true) || needs(W.router.dt, true);
-  TRY(prep(x, s->hidden.as<float>(), H, H, L.post_norm.p(), k, q8k, q80, s->xn.as<float>()));
-  x.mark("moe.prep");
+  const QmvPrologue in_pro =
+      row_pro(x, s->hidden.as<float>(), H, H, L.post_norm.p(), k, q8k, q80, x.fuse ? nullptr : s->xn.as<float>());
+  if (!x.fuse) TRY(pre(x, in_pro));
+  const QmvPrologue* gp = x.fuse ? &in_pro : nullptr;
+  // the f32 router normalizes the hidden rows itself when fused
+  const float* rin = x.fuse ? s->hidden.as<float>() : s->xn.as<float>();
+  const float* rnorm = x.fuse ? L.post_norm.p() : nullptr;
   float* lg = s->logits_moe.as<float>();
   if (W.router.present()) {
-    TRY(qmv(x, R.router));
-  x.mark("moe.router");
     ++x.s->launch_count;
-    IQ_CUDA(f32_matvec(W.selector.p(), 1, H, s->xn.as<float>(), H, k, lg + E, E + 1, x.st, x.pdl));
-  x.mark("moe.router");
+    IQ_CUDA(qmv_launch(x.s->jobs.as<QmvJob>() + R.router.job, R.router.njobs, nullptr, R.router.ntiles, R.router.smem,
+                       x.st, x.pdl, gp));
+    x.mark("moe.router");
+    ++x.s->launch_count;
+    IQ_CUDA(f32_matvec(W.selector.p(), 1, H, rin, H, k, lg + E, E + 1, x.st, x.pdl, rnorm, c.rms_norm_eps));
+    x.mark("moe.router");
   } else {
     ++x.s->launch_count;
-    IQ_CUDA(f32_matvec(W.router_sel.p(), E + 1, H, s->xn.as<float>(), H, k, lg, E + 1, x.st, x.pdl));
-  x.mark("moe.router");
+    IQ_CUDA(f32_matvec(W.router_sel.p(), E + 1, H, rin, H, k, lg, E + 1, x.st, x.pdl, rnorm, c.rms_norm_eps));
+    x.mark("moe.router");
   }
   MoeRouteArgs a = {};
   a.logits = lg;
@@ -330,7 +395,7 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   const int down_tiles = max_union * t.tiles_down + tiles_sh_down;
   const int gu_smem = k * (int)std::max(s->act8k_bytes, s->act80_bytes);
   ++x.s->launch_count;
-  IQ_CUDA(qmv_launch(a.gu_jobs, 0, a.gu_count, gu_tiles, gu_smem, x.st, x.pdl));
+  IQ_CUDA(qmv_launch(a.gu_jobs, 0, a.gu_count, gu_tiles, gu_smem, x.st, x.pdl, gp));
   x.mark("moe.gate_up");
   MoeActArgs b = {};
   b.gu = a.gu_out;
@@ -350,7 +415,8 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   IQ_CUDA(moe_act_launch(b, x.st, x.pdl));
   x.mark("moe.act");
   ++x.s->launch_count;
-  IQ_CUDA(qmv_launch(a.down_jobs, 0, a.down_count, down_tiles, (k * c.num_experts_per_tok + k) * (int)s->act_mid_bytes, x.st, x.pdl));
+  IQ_CUDA(qmv_launch(a.down_jobs, 0, a.down_count, down_tiles, (k * c.num_experts_per_tok + k) * (int)s->act_mid_bytes,
+                     x.st, x.pdl));
   x.mark("moe.down");
   // expert parallelism: the all-gather of y happens here (model_ep.cu)
   MoeCombineArgs cb = {};
@@ -381,9 +447,8 @@ int run_delta(Ctx& x, const Layer& L, const LayerRec& R, int k, int li) {
   const int bdt = D.ba_fused ? D.ba.dt : D.beta.dt;
   const bool q8k = needs(D.qkv.dt, false) || needs(D.z.dt, false) || needs(bdt, false);
   const bool q80 = needs(D.qkv.dt, true) || needs(D.z.dt, true) || needs(bdt, true);
-  TRY(prep(x, s->hidden.as<float>(), H, H, L.attn_norm.p(), k, q8k, q80, nullptr));
-  x.mark("dn.prep");
-  TRY(qmv(x, R.proj));
+  const QmvPrologue in_pro = row_pro(x, s->hidden.as<float>(), H, H, L.attn_norm.p(), k, q8k, q80);
+  TRY(qmv(x, R.proj, &in_pro));
   x.mark("dn.proj");
   DeltaNetArgs a = {};
   a.layers = s->dn_layers.as<DeltaNetLayer>() + li;
@@ -421,10 +486,24 @@ int run_delta(Ctx& x, const Layer& L, const LayerRec& R, int k, int li) {
   g.q80 = D.out.dt == Q8_0 ? s->act80.as<uint8_t>() : nullptr;
   g.q8k_stride = (int)s->act8k_bytes;
   g.q80_stride = (int)s->act80_bytes;
-  ++x.s->launch_count;
-  IQ_CUDA(gated_norm_launch(g, k, x.st, x.pdl));
-  x.mark("dn.gated_norm");
-  TRY(qmv(x, R.out));
+  QmvPrologue gp = {};
+  gp.mode = kProGated;
+  gp.rows = k;
+  gp.cols = vdim;
+  gp.x = g.o;
+  gp.ldx = g.o_ld;
+  gp.z = g.z;
+  gp.ldz = g.z_ld;
+  gp.w = g.w;
+  gp.heads = g.heads;
+  gp.dv = g.dv;
+  gp.eps = g.eps;
+  gp.inv_n = g.inv_dv;
+  gp.want8k = D.out.dt != Q8_0;
+  gp.want80 = D.out.dt == Q8_0;
+  gp.stride8k = (int)act_row_bytes_q8k(vdim);
+  gp.stride80 = (int)act_row_bytes_q80(vdim);
+  TRY(qmv(x, R.out, &gp));
   x.mark("dn.out");
   return IQ_OK;
 }
@@ -437,9 +516,8 @@ int run_attention(Ctx& x, const Layer& L, const LayerRec& R, int k, int fi) {
   const int nhd = c.num_attention_heads * c.head_dim;
   const bool q8k = needs(A.q.dt, false) || needs(A.k.dt, false) || needs(A.v.dt, false);
   const bool q80 = needs(A.q.dt, true) || needs(A.k.dt, true) || needs(A.v.dt, true);
-  TRY(prep(x, s->hidden.as<float>(), H, H, L.attn_norm.p(), k, q8k, q80, nullptr));
-  x.mark("attn.prep_norm");
-  TRY(qmv(x, R.proj));
+  const QmvPrologue in_pro = row_pro(x, s->hidden.as<float>(), H, H, L.attn_norm.p(), k, q8k, q80);
+  TRY(qmv(x, R.proj, &in_pro));
   x.mark("attn.proj");
   AttnArgs a = {};
   a.qg = s->qg.as<float>();
@@ -474,9 +552,9 @@ int run_attention(Ctx& x, const Layer& L, const LayerRec& R, int k, int fi) {
   ++x.s->launch_count;
   IQ_CUDA(attn_combine_launch(a, x.st, x.pdl));
   x.mark("attn.combine");
-  TRY(prep(x, s->attn_out.as<float>(), nhd, nhd, nullptr, k, needs(A.o.dt, false), needs(A.o.dt, true), nullptr));
-  x.mark("attn.out_prep");
-  TRY(qmv(x, R.out));
+  const QmvPrologue out_pro = row_pro(x, s->attn_out.as<float>(), nhd, nhd, nullptr, k, needs(A.o.dt, false),
+                                     needs(A.o.dt, true));
+  TRY(qmv(x, R.out, &out_pro));
   x.mark("attn.out");
   return IQ_OK;
 }
@@ -544,10 +622,9 @@ int run_pass(iq_state* s, int k, bool verify) {
     else TRY(run_attention(x, L, P.layers[l], k, fi++));
     TRY(run_moe(x, L, P.layers[l], k, l));
   }
-  TRY(prep(x, s->hidden.as<float>(), H, H, m->out_norm.p(), k, needs(m->lm_head.dt, false),
-           needs(m->lm_head.dt, true), s->xn.as<float>()));
-  x.mark("head.prep");
-  TRY(qmv(x, P.lm_head));
+  const QmvPrologue head_pro = row_pro(x, s->hidden.as<float>(), H, H, m->out_norm.p(), k,
+                                      needs(m->lm_head.dt, false), needs(m->lm_head.dt, true), s->xn.as<float>());
+  TRY(qmv(x, P.lm_head, &head_pro));
   x.mark("head.lm_head");
   HeadArgs h = {};
   h.logits = s->logits.as<float>();

@@ -38,8 +38,11 @@ struct QmvJob {
   int16_t outrow[8];     // output row (of out) of input column i
 };
 
+// Two persistent CTAs per SM; each of their warps streams 16 weight rows.
+constexpr int kQmvWarps = 8;
+constexpr int kQmvThreads = 32 * kQmvWarps;
 // Rows one CTA covers for a job.
-__host__ __device__ inline int qmv_rows_per_cta(int ksplit) { return 16 * (8 / ksplit); }
+__host__ __device__ inline int qmv_rows_per_cta(int ksplit) { return 16 * (kQmvWarps / ksplit); }
 __host__ __device__ inline int qmv_units(int dt, int cols) {
   return dt == Q8_0 ? cols / 128 : cols / 256;
 }
@@ -59,6 +62,34 @@ inline int qmv_tiles(const QmvJob& j) {
   return (int)ceil_div(j.rows, qmv_rows_per_cta(j.ksplit));
 }
 
+// How the activation rows of a launch are produced in shared memory.
+// kProNone stages job.act from global memory; the other modes compute the
+// rows in every CTA from f32 inputs and quantize them straight into shared
+// memory, fusing the norm / gate that precedes the projection.
+enum QmvProMode : int {
+  kProNone = 0,
+  kProRmsNorm = 1,  // x / sqrt(mean(x^2) + eps) * w         (GGUF RMSNorm)
+  kProGated = 2,    // per head: x / sqrt(mean(x^2) + eps) * w * silu(z)
+  kProQuant = 3,    // x as is
+};
+
+struct QmvPrologue {
+  int mode;
+  int rows;          // activation rows produced (<= 8)
+  int cols;          // elements per row (a multiple of 256)
+  const float* x;    // [rows][ldx] (Gated: the recurrent output o)
+  int ldx;
+  const float* w;    // RmsNorm: [cols]; Gated: [dv]
+  const float* z;    // Gated: [rows][ldz]
+  int ldz;
+  int heads, dv;     // Gated
+  float eps, inv_n;  // inv_n = 1/cols (RmsNorm) or 1/dv (Gated)
+  int want8k, want80;  // layouts to produce
+  int stride8k, stride80;  // shared-memory row strides of the two layouts
+  float* xn_out;     // RmsNorm: CTA 0 also writes the normalized rows here (or null)
+  int ldxn;
+};
+
 // Launch `ntiles` CTAs over `jobs` (device memory, sorted by tile0).
 // When `dyn_count` is non-null the job count is read on the device after the
 // programmatic-dependency wait (jobs written by the previous kernel), and
@@ -66,6 +97,12 @@ inline int qmv_tiles(const QmvJob& j) {
 // `smem_bytes` must cover n * act_row_bytes of every job in the table.
 constexpr int kQmvMaxActSmem = 64 * 1024;
 cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int ntiles, int smem_bytes,
-                       cudaStream_t stream, bool pdl);
+                       cudaStream_t stream, bool pdl, const QmvPrologue* pro = nullptr);
+// Norm statistics a prologue keeps (rows, or rows x heads for Gated).
+constexpr int kProMaxDen = 512;
+// Shared memory a prologue launch needs.
+inline int qmv_prologue_smem(const QmvPrologue& p) {
+  return p.rows * (p.want8k ? p.stride8k : 0) + p.rows * (p.want80 ? p.stride80 : 0);
+}
 
 }  // namespace iq
