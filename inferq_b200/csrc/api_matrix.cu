@@ -77,6 +77,11 @@ int matrix_forward_dev(const iq_matrix* m, const float* x, int k, float* y, cuda
   const bool kq = m->dtype != Q8_0;
   const int64_t arb = kq ? act_row_bytes_q8k(m->cols) : act_row_bytes_q80(m->cols);
   IQ_CUDA(g_scratch.act.reserve((size_t)(arb * 8)));
+  if ((uintptr_t)x & 15) {  // the quantizer reads 16-byte vectors
+    IQ_CUDA(g_scratch.x.reserve((size_t)(m->cols * k * sizeof(float))));
+    IQ_CUDA(cudaMemcpyAsync(g_scratch.x.p, x, (size_t)(m->cols * k * sizeof(float)), cudaMemcpyDeviceToDevice, st));
+    x = g_scratch.x.as<float>();
+  }
   PrepArgs pa = {};
   pa.x = x;
   pa.ldx = (int)m->cols;

@@ -182,38 +182,52 @@ __global__ void __launch_bounds__(256) deltanet_kernel(DeltaNetArgs a) {
 // Gated RMSNorm of every value head (src/qwen/norm.rs:16-25:
 // x / sqrt(mean(x^2) + eps) * w * silu(z)), then quantization of the row for
 // the output projection.  One CTA per row; warp w normalizes heads w, w+8, ...
+template <int MAXB>
 __global__ void __launch_bounds__(256) gated_norm_kernel(GatedNormArgs a) {
   pdl_wait();
   pdl_trigger();
-  extern __shared__ float xs[];
+  extern __shared__ __align__(16) float xs[];
   const int row = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cols = a.heads * a.dv, nb = cols / 256;
   const float* o = a.o + (int64_t)row * a.o_ld;
   const float* z = a.z + (int64_t)row * a.z_ld;
-  for (int h = warp; h < a.heads; h += 8) {
-    float ss = 0.f;
-    for (int i = lane; i < a.dv; i += 32) ss = fmaf(o[h * a.dv + i], o[h * a.dv + i], ss);
+  // a lane's elements of block b lie in one head (dv >= 32): 32s .. 32s+31
+  float v[MAXB][8], zv[MAXB][8], wv[MAXB][8];
 #pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, m));
-    const float den = sqrtf(__fadd_rn(__fmul_rn(ss, a.inv_dv), a.eps));
-    for (int i = lane; i < a.dv; i += 32) {
-      const float zv = z[h * a.dv + i];
-      const float silu = __fdiv_rn(zv, __fadd_rn(1.f, expf(-zv)));
-      xs[h * a.dv + i] = __fmul_rn(__fmul_rn(__fdiv_rn(o[h * a.dv + i], den), a.w[i]), silu);
+  for (int j = 0; j < MAXB; j++) {
+    const int b = warp + 8 * j;
+    if (b < nb) {
+      ld_q8k_lane(o, b, lane, v[j]);
+      ld_q8k_lane(z, b, lane, zv[j]);
+      const int e0 = b * 256 + 32 * (lane & 7);
+      const float* wp = a.w + (e0 % a.dv) + 4 * (lane >> 3);
+      const float4 w0 = *reinterpret_cast<const float4*>(wp), w1 = *reinterpret_cast<const float4*>(wp + 16);
+      wv[j][0] = w0.x; wv[j][1] = w0.y; wv[j][2] = w0.z; wv[j][3] = w0.w;
+      wv[j][4] = w1.x; wv[j][5] = w1.y; wv[j][6] = w1.z; wv[j][7] = w1.w;
     }
   }
-  __syncthreads();
-  const int cols = a.heads * a.dv;
-  if (a.q8k) {
-    const int nb = cols / 256;
-    uint8_t* ar = a.q8k + (int64_t)row * a.q8k_stride;
-    for (int b = warp; b < nb; b += 8) quant_q8k_block_warp(xs, ar, nb, b, lane);
+  // per head: sum of squares over the lanes of the head (s bits below
+  // log2(dv/32), and the tig bits), then x / sqrt(mean + eps) * w * silu(z)
+  const int smask = a.dv / 32 - 1;
+#pragma unroll
+  for (int j = 0; j < MAXB; j++) {
+    if (warp + 8 * j >= nb) continue;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) ss = fmaf(v[j][i], v[j][i], ss);
+    for (int m = 1; m <= smask; m <<= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, m));
+    ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, 8));
+    ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, 16));
+    const float den = sqrtf(__fadd_rn(__fmul_rn(ss, a.inv_dv), a.eps));
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float silu = __fdiv_rn(zv[j][i], __fadd_rn(1.f, expf(-zv[j][i])));
+      v[j][i] = __fmul_rn(__fmul_rn(__fdiv_rn(v[j][i], den), wv[j][i]), silu);
+    }
   }
-  if (a.q80) {
-    const int nb = cols / 32;
-    uint8_t* ar = a.q80 + (int64_t)row * a.q80_stride;
-    for (int g = warp; g < nb / 4; g += 8) quant_q80_group_warp(xs, ar, nb, g, lane);
-  }
+  finish_row<MAXB>(v, nb, cols, a.q8k ? a.q8k + (int64_t)row * a.q8k_stride : nullptr,
+                   a.q80 ? a.q80 + (int64_t)row * a.q80_stride : nullptr, nullptr, xs);
 }
 
 }  // namespace
@@ -235,14 +249,22 @@ cudaError_t gated_norm_launch(const GatedNormArgs& a, int rows, cudaStream_t st,
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(rows);
   cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = a.heads * a.dv * sizeof(float);
+  const int cols = a.heads * a.dv, nb = cols / 256;
+  // lanes own 32 contiguous elements of one head; Q8_K rows need 256-blocks
+  if (a.dv < 32 || a.dv > 256 || (a.dv & (a.dv - 1)) || cols % 256 || a.o_ld % 4 || a.z_ld % 4 ||
+      ((uintptr_t)a.o | (uintptr_t)a.z | (uintptr_t)a.w) & 15)
+    return cudaErrorInvalidValue;
+  cfg.dynamicSmemBytes = a.q80 ? cols * sizeof(float) : 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gated_norm_kernel, a);
+  if (nb <= 8) return cudaLaunchKernelEx(&cfg, gated_norm_kernel<1>, a);
+  if (nb <= 16) return cudaLaunchKernelEx(&cfg, gated_norm_kernel<2>, a);
+  if (nb <= 32) return cudaLaunchKernelEx(&cfg, gated_norm_kernel<4>, a);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace iq

@@ -157,4 +157,66 @@ __device__ __forceinline__ void quant_q80_group_warp(const float* x, uint8_t* ac
   quant_q80_group_warp_v(v, act_row, nb, g, lane);
 }
 
+// ------------------------------------------------- row transforms (one CTA per row)
+// Warp w of a 256-thread CTA owns the Q8_K blocks b = w + 8j (j < MAXB) of a
+// row and keeps their elements in registers: lane l holds element
+// b*256 + q8k_lane_pos(l, i) in v[j][i], i.e. the order quant_q8k_block_warp_v
+// consumes, loaded as two 16-byte vectors.
+__device__ __forceinline__ int q8k_lane_pos(int lane, int i) {
+  return 32 * (lane & 7) + 16 * (i / 4) + 4 * (lane >> 3) + (i % 4);
+}
+__device__ __forceinline__ void ld_q8k_lane(const float* row, int b, int lane, float (&v)[8], int cols = 1 << 30) {
+  if (b * 256 + 32 * (lane & 7) >= cols) {  // a trailing half block (cols % 256 == 128)
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = 0.f;
+    return;
+  }
+  const float* p = row + b * 256 + 32 * (lane & 7) + 4 * (lane >> 3);
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 c = *reinterpret_cast<const float4*>(p + 16);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+}
+// Deterministic CTA-wide sum of one value per thread (256 threads): lane
+// tree, then the eight warp partials in warp order.
+__device__ __forceinline__ float cta_sum256(float v, float* red8) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+  if ((threadIdx.x & 31) == 0) red8[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = red8[0];
+#pragma unroll
+  for (int i = 1; i < 8; i++) t = __fadd_rn(t, red8[i]);
+  return t;
+}
+// Write a row held as above (nb = ceil(cols / 256) blocks, cols a multiple of
+// 128): Q8_K straight from registers (cols a multiple of 256); the Q8_0
+// layout and the f32 copy go through the shared row `xs` (cols floats).
+template <int MAXB>
+__device__ __forceinline__ void finish_row(const float (&v)[MAXB][8], int nb, int cols, uint8_t* q8k, uint8_t* q80,
+                                           float* xn, float* xs) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (q8k) {
+#pragma unroll
+    for (int j = 0; j < MAXB; j++)
+      if (warp + 8 * j < nb) quant_q8k_block_warp_v(v[j], q8k, nb, warp + 8 * j, lane);
+  }
+  if (!q80 && !xn) return;
+#pragma unroll
+  for (int j = 0; j < MAXB; j++) {
+    const int b = warp + 8 * j;
+    if (b < nb && b * 256 + 32 * (lane & 7) < cols) {
+      float* p = xs + b * 256 + 32 * (lane & 7) + 4 * (lane >> 3);
+      *reinterpret_cast<float4*>(p) = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+      *reinterpret_cast<float4*>(p + 16) = make_float4(v[j][4], v[j][5], v[j][6], v[j][7]);
+    }
+  }
+  __syncthreads();
+  if (q80)
+    for (int g = warp; g < cols / 128; g += 8) quant_q80_group_warp(xs, q80, cols / 32, g, lane);
+  if (xn)
+    for (int i = 4 * threadIdx.x; i < cols; i += 1024)
+      *reinterpret_cast<float4*>(xn + i) = *reinterpret_cast<const float4*>(xs + i);
+}
+
 }  // namespace iq

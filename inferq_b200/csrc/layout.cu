@@ -79,39 +79,42 @@ namespace {
 
 // One CTA per input row: optional GGUF RMSNorm (x / sqrt(mean(x^2)+eps) * w,
 // src/qwen/quantized_layer.rs:230-236), then quantization to the requested
-// activation layouts, and optionally the normalized f32 row itself.
+// activation layouts, and optionally the normalized f32 row itself.  Every
+// load of the row (and of the norm weight) is issued before the reduction.
+template <int MAXB>
 __global__ void __launch_bounds__(256) prep_rows_kernel(PrepArgs a) {
   pdl_wait();
   pdl_trigger();
-  extern __shared__ float xs[];
+  extern __shared__ __align__(16) float xs[];
+  __shared__ float red[8];
   const int row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* x = a.x + (int64_t)row * a.ldx;
-  const int cols = a.cols;
+  const int nb = (a.cols + 255) / 256;
+  float v[MAXB][8], w[MAXB][8];
+#pragma unroll
+  for (int j = 0; j < MAXB; j++)
+    if (warp + 8 * j < nb) {
+      ld_q8k_lane(x, warp + 8 * j, lane, v[j], a.cols);
+      if (a.norm_w) ld_q8k_lane(a.norm_w, warp + 8 * j, lane, w[j], a.cols);
+    }
   if (a.norm_w) {
     float ss = 0.f;
-    for (int i = threadIdx.x; i < cols; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
-    ss = block_sum_256(ss);
-    const float var = __fmul_rn(ss, a.inv_cols);
-    const float den = sqrtf(__fadd_rn(var, a.eps));
-    for (int i = threadIdx.x; i < cols; i += blockDim.x)
-      xs[i] = __fmul_rn(__fdiv_rn(x[i], den), a.norm_w[i]);
-  } else {
-    for (int i = threadIdx.x; i < cols; i += blockDim.x) xs[i] = x[i];
+#pragma unroll
+    for (int j = 0; j < MAXB; j++)
+      if (warp + 8 * j < nb)
+#pragma unroll
+        for (int i = 0; i < 8; i++) ss = fmaf(v[j][i], v[j][i], ss);
+    ss = cta_sum256(ss, red);
+    const float den = sqrtf(__fadd_rn(__fmul_rn(ss, a.inv_cols), a.eps));
+#pragma unroll
+    for (int j = 0; j < MAXB; j++)
+#pragma unroll
+      for (int i = 0; i < 8; i++) v[j][i] = __fmul_rn(__fdiv_rn(v[j][i], den), w[j][i]);
   }
-  __syncthreads();
-  if (a.xn_out)
-    for (int i = threadIdx.x; i < cols; i += blockDim.x) a.xn_out[(int64_t)row * a.ldxn + i] = xs[i];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (a.q8k) {
-    const int nb = cols / 256;
-    uint8_t* ar = a.q8k + (int64_t)row * (a.q8k_stride ? a.q8k_stride : act_row_bytes_q8k(cols));
-    for (int b = warp; b < nb; b += 8) quant_q8k_block_warp(xs, ar, nb, b, lane);
-  }
-  if (a.q80) {
-    const int nb = cols / 32;
-    uint8_t* ar = a.q80 + (int64_t)row * (a.q80_stride ? a.q80_stride : act_row_bytes_q80(cols));
-    for (int g = warp; g < nb / 4; g += 8) quant_q80_group_warp(xs, ar, nb, g, lane);
-  }
+  uint8_t* q8k = a.q8k ? a.q8k + (int64_t)row * (a.q8k_stride ? a.q8k_stride : act_row_bytes_q8k(a.cols)) : nullptr;
+  uint8_t* q80 = a.q80 ? a.q80 + (int64_t)row * (a.q80_stride ? a.q80_stride : act_row_bytes_q80(a.cols)) : nullptr;
+  finish_row<MAXB>(v, nb, a.cols, q8k, q80, a.xn_out ? a.xn_out + (int64_t)row * a.ldxn : nullptr, xs);
 }
 
 }  // namespace
@@ -136,14 +139,24 @@ cudaError_t prep_rows(const PrepArgs& a, int rows, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(rows);
   cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = a.cols * sizeof(float);
+  cfg.dynamicSmemBytes = (a.q80 || a.xn_out) ? a.cols * sizeof(float) : 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, prep_rows_kernel, a);
+  // 16-byte row vectors: Q8_K rows of 256-element blocks, Q8_0 / f32 rows of 128
+  const int nb = (a.cols + 255) / 256;
+  auto a16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+  if (a.cols % (a.q8k ? 256 : 128) || a.ldx % 4 || !a16(a.x) || (a.norm_w && !a16(a.norm_w)) ||
+      (a.xn_out && (a.ldxn % 4 || !a16(a.xn_out))))
+    return cudaErrorInvalidValue;
+  if (nb <= 8) return cudaLaunchKernelEx(&cfg, prep_rows_kernel<1>, a);
+  if (nb <= 16) return cudaLaunchKernelEx(&cfg, prep_rows_kernel<2>, a);
+  if (nb <= 32) return cudaLaunchKernelEx(&cfg, prep_rows_kernel<4>, a);
+  if (nb <= 64) return cudaLaunchKernelEx(&cfg, prep_rows_kernel<8>, a);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace iq

@@ -7,6 +7,7 @@
 // for every row routed to it; silu(g)*u with g/(1+exp(-g)); weighted sum in
 // row -> route order, multiply then add; shared expert times
 // sigmoid(x . selector) added after the routed sum).
+#include <cstddef>
 #include "model_kernels.cuh"
 #include "devfns.cuh"
 
@@ -16,24 +17,36 @@ namespace {
 constexpr int kMaxRows = 8;
 constexpr int kMaxExperts = 1024;
 
-__device__ __forceinline__ void set_job(QmvJob& j, const uint8_t* w, int64_t w_row_bytes, int dt, int rows, int cols,
+static_assert(offsetof(QmvJob, rowmap) % 8 == 0 && offsetof(QmvJob, outrow) % 8 == 0, "packed job maps");
+
+// Write a job record straight to global memory (no local-memory staging):
+// rowmap / outrow arrive packed, 8 bytes / 2 x 8 bytes.
+__device__ __forceinline__ void put_job(QmvJob* j, const uint8_t* w, int64_t w_row_bytes, int dt, int rows, int cols,
                                         int ks, const uint8_t* act, int act_bytes, float* out, int out_ld, int n,
-                                        int tile0, int act_nrows) {
-  j.w = w;
-  j.act = act;
-  j.out = out;
-  j.resid = nullptr;
-  j.w_row_bytes = w_row_bytes;
-  j.act_row_bytes = act_bytes;
-  j.out_ld = out_ld;
-  j.dtype = dt;
-  j.rows = rows;
-  j.cols = cols;
-  j.ksplit = ks;
-  j.n = n;
-  j.tile0 = tile0;
-  j.act_nrows = act_nrows;
-  j.epi = kEpiStore;
+                                        int tile0, int act_nrows, uint64_t rowmap, uint64_t out_lo, uint64_t out_hi) {
+  j->w = w;
+  j->act = act;
+  j->out = out;
+  j->resid = nullptr;
+  j->w_row_bytes = w_row_bytes;
+  j->act_row_bytes = act_bytes;
+  j->out_ld = out_ld;
+  j->dtype = dt;
+  j->rows = rows;
+  j->cols = cols;
+  j->ksplit = ks;
+  j->n = n;
+  j->tile0 = tile0;
+  j->act_nrows = act_nrows;
+  j->epi = kEpiStore;
+  *reinterpret_cast<uint64_t*>(j->rowmap) = rowmap;
+  reinterpret_cast<uint64_t*>(j->outrow)[0] = out_lo;
+  reinterpret_cast<uint64_t*>(j->outrow)[1] = out_hi;
+}
+__device__ __forceinline__ void pack_out(uint64_t& lo, uint64_t& hi, int n, int v) {
+  const uint64_t x = (uint64_t)(uint16_t)v;
+  if (n < 4) lo |= x << (16 * n);
+  else hi |= x << (16 * (n - 4));
 }
 
 // One CTA.  Warp t < rows routes row t with its probabilities in registers
@@ -141,54 +154,48 @@ __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRoute
     a.union_list[rank++] = e;
     if (e < s.expert_lo || e >= s.expert_hi) continue;
     const int le = e - s.expert_lo;
-    QmvJob gj, uj, dj;
     const int ri = res_rank++;
     const bool q80 = s.gate_dt == Q8_0;
     const uint8_t* ain = q80 ? a.act_in80 : a.act_in8k;
     const int ab = q80 ? a.act_in80_bytes : a.act_in8k_bytes;
-    set_job(gj, s.gate + le * s.gate_stride, s.gate_row_bytes, s.gate_dt, a.ffn, a.hidden, s.ks_gate, ain, ab,
-            a.gu_out, a.gu_ld, 0, 2 * ri * s.tiles_gate, a.rows);
-    set_job(uj, s.up + le * s.up_stride, s.gate_row_bytes, s.gate_dt, a.ffn, a.hidden, s.ks_gate, ain, ab,
-            a.gu_out + a.ffn, a.gu_ld, 0, (2 * ri + 1) * s.tiles_gate, a.rows);
-    set_job(dj, s.down + le * s.down_stride, s.down_row_bytes, s.down_dt, a.hidden, a.ffn, s.ks_down, a.act_mid,
-            a.act_mid_bytes, a.y, a.y_ld, 0, ri * s.tiles_down, slots_routed + a.rows);
+    uint64_t gmap = 0, dmap = 0, olo = 0, ohi = 0;
     int n = 0;
     for (int t = 0; t < a.rows; t++)
       for (int r = 0; r < a.topk; r++)
         if (sel_e[t][r] == e) {
           const int slot = t * a.topk + r;
-          gj.rowmap[n] = uj.rowmap[n] = (uint8_t)t;
-          gj.outrow[n] = uj.outrow[n] = (int16_t)slot;
-          dj.rowmap[n] = (uint8_t)slot;
-          dj.outrow[n] = (int16_t)slot;
+          gmap |= (uint64_t)t << (8 * n);
+          dmap |= (uint64_t)slot << (8 * n);
+          pack_out(olo, ohi, n, slot);
           n++;
         }
-    gj.n = uj.n = dj.n = n;
-    a.gu_jobs[2 * ri] = gj;
-    a.gu_jobs[2 * ri + 1] = uj;
-    a.down_jobs[ri] = dj;
+    put_job(&a.gu_jobs[2 * ri], s.gate + le * s.gate_stride, s.gate_row_bytes, s.gate_dt, a.ffn, a.hidden,
+            s.ks_gate, ain, ab, a.gu_out, a.gu_ld, n, 2 * ri * s.tiles_gate, a.rows, gmap, olo, ohi);
+    put_job(&a.gu_jobs[2 * ri + 1], s.up + le * s.up_stride, s.gate_row_bytes, s.gate_dt, a.ffn, a.hidden,
+            s.ks_gate, ain, ab, a.gu_out + a.ffn, a.gu_ld, n, (2 * ri + 1) * s.tiles_gate, a.rows, gmap, olo, ohi);
+    put_job(&a.down_jobs[ri], s.down + le * s.down_stride, s.down_row_bytes, s.down_dt, a.hidden, a.ffn,
+            s.ks_down, a.act_mid, a.act_mid_bytes, a.y, a.y_ld, n, ri * s.tiles_down, slots_routed + a.rows, dmap,
+            olo, ohi);
   }
   if (threadIdx.x == 0) {
     // shared expert: every row, slots rows*topk + t
-    QmvJob gj, uj, dj;
     const bool q80 = s.sh_gate_dt == Q8_0;
     const uint8_t* ain = q80 ? a.act_in80 : a.act_in8k;
     const int ab = q80 ? a.act_in80_bytes : a.act_in8k_bytes;
-    set_job(gj, s.sh_gate, s.sh_gate_row_bytes, s.sh_gate_dt, a.sh_ffn, a.hidden, s.ks_sh_gate, ain, ab, a.gu_out,
-            a.gu_ld, a.rows, 2 * n_res * s.tiles_gate, a.rows);
-    set_job(uj, s.sh_up, s.sh_gate_row_bytes, s.sh_gate_dt, a.sh_ffn, a.hidden, s.ks_sh_gate, ain, ab,
-            a.gu_out + a.sh_ffn, a.gu_ld, a.rows, 2 * n_res * s.tiles_gate + s.tiles_sh_gate, a.rows);
-    set_job(dj, s.sh_down, s.sh_down_row_bytes, s.sh_down_dt, a.hidden, a.sh_ffn, s.ks_sh_down, a.act_mid,
-            a.act_mid_bytes, a.y, a.y_ld, a.rows, n_res * s.tiles_down, slots_routed + a.rows);
+    uint64_t gmap = 0, dmap = 0, olo = 0, ohi = 0;
     for (int t = 0; t < a.rows; t++) {
-      gj.rowmap[t] = uj.rowmap[t] = (uint8_t)t;
-      gj.outrow[t] = uj.outrow[t] = (int16_t)(slots_routed + t);
-      dj.rowmap[t] = (uint8_t)(slots_routed + t);
-      dj.outrow[t] = (int16_t)(slots_routed + t);
+      gmap |= (uint64_t)t << (8 * t);
+      dmap |= (uint64_t)(slots_routed + t) << (8 * t);
+      pack_out(olo, ohi, t, slots_routed + t);
     }
-    a.gu_jobs[2 * n_res] = gj;
-    a.gu_jobs[2 * n_res + 1] = uj;
-    a.down_jobs[n_res] = dj;
+    put_job(&a.gu_jobs[2 * n_res], s.sh_gate, s.sh_gate_row_bytes, s.sh_gate_dt, a.sh_ffn, a.hidden, s.ks_sh_gate,
+            ain, ab, a.gu_out, a.gu_ld, a.rows, 2 * n_res * s.tiles_gate, a.rows, gmap, olo, ohi);
+    put_job(&a.gu_jobs[2 * n_res + 1], s.sh_up, s.sh_gate_row_bytes, s.sh_gate_dt, a.sh_ffn, a.hidden,
+            s.ks_sh_gate, ain, ab, a.gu_out + a.sh_ffn, a.gu_ld, a.rows, 2 * n_res * s.tiles_gate + s.tiles_sh_gate,
+            a.rows, gmap, olo, ohi);
+    put_job(&a.down_jobs[n_res], s.sh_down, s.sh_down_row_bytes, s.sh_down_dt, a.hidden, a.sh_ffn, s.ks_sh_down,
+            a.act_mid, a.act_mid_bytes, a.y, a.y_ld, a.rows, n_res * s.tiles_down, slots_routed + a.rows, dmap, olo,
+            ohi);
     *a.gu_count = s.with_shared ? 2 * n_res + 2 : 2 * n_res;
     *a.down_count = s.with_shared ? n_res + 1 : n_res;
     *a.union_size = total_union;
@@ -196,11 +203,12 @@ __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRoute
 }
 
 // One CTA per slot: silu(gate) * up (candle's elementwise silu,
-// g / (1 + exp(-g))), quantized to Q8_K for the down projection.
+// g / (1 + exp(-g))), quantized for the down projection.
+template <int MAXB>
 __global__ void __launch_bounds__(256) moe_act_kernel(MoeActArgs a) {
   pdl_wait();
   pdl_trigger();
-  extern __shared__ float xs[];
+  extern __shared__ __align__(16) float xs[];
   const int slot = blockIdx.x;
   const int routed = a.rows * a.topk;
   if (slot >= routed + a.rows) return;
@@ -212,41 +220,61 @@ __global__ void __launch_bounds__(256) moe_act_kernel(MoeActArgs a) {
     ffn = a.ffn;
     q80 = a.down_q80;
   }
-  const float* g = a.gu + (int64_t)slot * a.gu_ld;
-  for (int i = threadIdx.x; i < ffn; i += 256) {
-    const float gv = g[i];
-    xs[i] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.f, expf(-gv))), g[ffn + i]);
-  }
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = (ffn + 255) / 256;
+  const float* g = a.gu + (int64_t)slot * a.gu_ld;
+  float v[MAXB][8], u[MAXB][8];
+#pragma unroll
+  for (int j = 0; j < MAXB; j++)
+    if (warp + 8 * j < nb) {
+      ld_q8k_lane(g, warp + 8 * j, lane, v[j], ffn);
+      ld_q8k_lane(g + ffn, warp + 8 * j, lane, u[j], ffn);
+    }
+#pragma unroll
+  for (int j = 0; j < MAXB; j++)
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[j][i] = __fmul_rn(__fdiv_rn(v[j][i], __fadd_rn(1.f, expf(-v[j][i]))), u[j][i]);
   uint8_t* ar = a.act + (int64_t)slot * a.act_bytes;
-  if (q80) {
-    const int nb = ffn / 32;
-    for (int g = warp; g < nb / 4; g += 8) quant_q80_group_warp(xs, ar, nb, g, lane);
-  } else {
-    const int nb = ffn / 256;
-    for (int b = warp; b < nb; b += 8) quant_q8k_block_warp(xs, ar, nb, b, lane);
-  }
+  finish_row<MAXB>(v, nb, ffn, q80 ? nullptr : ar, q80 ? ar : nullptr, nullptr, xs);
 }
 
-// One CTA per row: hidden += (sum_route y*w) + shared * sigmoid(selector).
+// hidden += (sum_route y*w) + shared * sigmoid(selector); one thread per four
+// consecutive columns of a row, every load issued before the sums.
 __global__ void __launch_bounds__(256) moe_combine_kernel(MoeCombineArgs a) {
   pdl_wait();
   pdl_trigger();
-  const int t = blockIdx.x;
+  constexpr int kMaxTopk = 16;
+  const int t = blockIdx.y;
+  const int i = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (i >= a.dim) return;
   const float sl = a.logits[(int64_t)t * a.logits_ld + a.experts];
-  const float selector = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-sl)));
-  const float* ysh = a.y + (int64_t)(a.rows * a.topk + t) * a.y_ld;
-  for (int i = threadIdx.x; i < a.dim; i += 256) {
-    float r = 0.f;
-    for (int q = 0; q < a.topk; q++) {
-      const float w = a.route_weight[t * a.topk + q];
-      r = __fadd_rn(r, __fmul_rn(a.y[(int64_t)(t * a.topk + q) * a.y_ld + i], w));
+  float w[kMaxTopk];
+  float4 y[kMaxTopk];
+#pragma unroll
+  for (int q = 0; q < kMaxTopk; q++)
+    if (q < a.topk) {
+      w[q] = a.route_weight[t * a.topk + q];
+      y[q] = *reinterpret_cast<const float4*>(a.y + (int64_t)(t * a.topk + q) * a.y_ld + i);
     }
-    const float moe = __fadd_rn(r, __fmul_rn(ysh[i], selector));
-    float* h = a.hidden + (int64_t)t * a.hidden_ld + i;
-    *h = __fadd_rn(*h, moe);
-  }
+  const float4 ysh = *reinterpret_cast<const float4*>(a.y + (int64_t)(a.rows * a.topk + t) * a.y_ld + i);
+  float4* hp = reinterpret_cast<float4*>(a.hidden + (int64_t)t * a.hidden_ld + i);
+  const float4 h = *hp;
+  const float selector = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-sl)));
+  float r[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int q = 0; q < kMaxTopk; q++)
+    if (q < a.topk) {
+      r[0] = __fadd_rn(r[0], __fmul_rn(y[q].x, w[q]));
+      r[1] = __fadd_rn(r[1], __fmul_rn(y[q].y, w[q]));
+      r[2] = __fadd_rn(r[2], __fmul_rn(y[q].z, w[q]));
+      r[3] = __fadd_rn(r[3], __fmul_rn(y[q].w, w[q]));
+    }
+  float4 o;
+  o.x = __fadd_rn(h.x, __fadd_rn(r[0], __fmul_rn(ysh.x, selector)));
+  o.y = __fadd_rn(h.y, __fadd_rn(r[1], __fmul_rn(ysh.y, selector)));
+  o.z = __fadd_rn(h.z, __fadd_rn(r[2], __fmul_rn(ysh.z, selector)));
+  o.w = __fadd_rn(h.w, __fadd_rn(r[3], __fmul_rn(ysh.w, selector)));
+  *hp = o;
 }
 
 }  // namespace
@@ -258,11 +286,22 @@ cudaError_t moe_route_launch(const MoeRouteArgs& a, const MoeRouteStatic& s, cud
 
 cudaError_t moe_act_launch(const MoeActArgs& a, cudaStream_t st, bool pdl) {
   const int ffn = a.ffn > a.sh_ffn ? a.ffn : a.sh_ffn;
-  return launch_pdl(moe_act_kernel, dim3(a.rows * a.topk + a.rows), dim3(256), ffn * sizeof(float), st, pdl, a);
+  const bool any80 = a.down_q80 || a.sh_down_q80;
+  if (a.ffn % (a.down_q80 ? 128 : 256) || a.sh_ffn % (a.sh_down_q80 ? 128 : 256) || a.gu_ld % 4)
+    return cudaErrorInvalidValue;
+  const dim3 grid(a.rows * a.topk + a.rows);
+  const size_t smem = any80 ? ffn * sizeof(float) : 0;
+  const int nb = (ffn + 255) / 256;
+  if (nb <= 8) return launch_pdl(moe_act_kernel<1>, grid, dim3(256), smem, st, pdl, a);
+  if (nb <= 16) return launch_pdl(moe_act_kernel<2>, grid, dim3(256), smem, st, pdl, a);
+  if (nb <= 32) return launch_pdl(moe_act_kernel<4>, grid, dim3(256), smem, st, pdl, a);
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t moe_combine_launch(const MoeCombineArgs& a, cudaStream_t st, bool pdl) {
-  return launch_pdl(moe_combine_kernel, dim3(a.rows), dim3(256), 0, st, pdl, a);
+  if (a.topk > 16 || a.dim % 4 || a.y_ld % 4 || a.hidden_ld % 4) return cudaErrorInvalidValue;
+  const dim3 grid((unsigned)ceil_div(a.dim / 4, 128), a.rows);
+  return launch_pdl(moe_combine_kernel, grid, dim3(128), 0, st, pdl, a);
 }
 
 }  // namespace iq
