@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(256) attn_scan_kernel(AttnArgs a) {
   extern __shared__ float sm[];
   float* Ks = sm;                       // [32][HD + 1]
   float* Vs = Ks + 32 * (HD + 1);       // [32][HD]
-  float* Qs = Vs + 32 * HD;             // [8 warps][HD]
+  float* Qs = Vs + 32 * HD;             // [rows * G][HD]: this KV head's query rows
   const int kvh = blockIdx.x, c = blockIdx.y;
   const int G = a.nh / a.nkv;
   const int pos0 = *a.pos;
@@ -106,18 +106,22 @@ __global__ void __launch_bounds__(256) attn_scan_kernel(AttnArgs a) {
     kr[0] = kv.x; kr[1] = kv.y; kr[2] = kv.z; kr[3] = kv.w;
     *reinterpret_cast<float4*>(Vs + p * HD + 4 * d4) = vv;
   }
+  const int nq = a.rows * G;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < nq * HD / 4; i += 256) {
+    const int q = i / (HD / 4), d4 = i % (HD / 4);
+    const int t = q / G, h = kvh * G + q % G;
+    *reinterpret_cast<float4*>(Qs + q * HD + 4 * d4) =
+        *reinterpret_cast<const float4*>(a.qbuf + ((int64_t)t * a.nh + h) * HD + 4 * d4);
+  }
   __syncthreads();
   const float scale = __fdiv_rn(1.f, sqrtf((float)HD));
   const int nchunks_total = (last + kAttnChunk) / kAttnChunk;
-  float* qs = Qs + warp * HD;
-  for (int q = warp; q < a.rows * G; q += 8) {
+  for (int q = warp; q < nq; q += 8) {
     const int t = q / G, g = q % G, h = kvh * G + g;
     const int attend_last = pos0 + t;
     if (p0 > attend_last) continue;  // this chunk is entirely in row t's future
-    const float* qsrc = a.qbuf + ((int64_t)t * a.nh + h) * HD;
-#pragma unroll
-    for (int d = 0; d < D; d++) qs[lane * D + d] = qsrc[lane * D + d];
-    __syncwarp();
+    const float* qs = Qs + q * HD;
     const float* kr = Ks + lane * (HD + 1);
     float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll 8
@@ -141,15 +145,14 @@ __global__ void __launch_bounds__(256) attn_scan_kernel(AttnArgs a) {
     for (int d = 0; d < D; d++) acc[d] = 0.f;
     for (int p = 0; p < 32; p++) {
       const float ep = __shfl_sync(0xffffffffu, e, p);
-      const float* vr = Vs + p * HD + lane * D;
+      const float* vr = Vs + p * HD + lane;
 #pragma unroll
-      for (int d = 0; d < D; d++) acc[d] = fmaf(ep, vr[d], acc[d]);
+      for (int d = 0; d < D; d++) acc[d] = fmaf(ep, vr[32 * d], acc[d]);
     }
     float* part = a.part + (((int64_t)t * a.nh + h) * nchunks_total + c) * (HD + 2);
     if (lane == 0) { part[0] = m; part[1] = l; }
 #pragma unroll
-    for (int d = 0; d < D; d++) part[2 + lane * D + d] = acc[d];
-    __syncwarp();
+    for (int d = 0; d < D; d++) part[2 + 32 * d + lane] = acc[d];
   }
 }
 
@@ -163,10 +166,12 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a) {
   const int nchunks_total = (pos0 + a.rows - 1 + kAttnChunk) / kAttnChunk;
   const float* part = a.part + ((int64_t)t * a.nh + h) * nchunks_total * (a.hd + 2);
   float M = -INFINITY;
+#pragma unroll 8
   for (int c = 0; c < nchunks; c++) M = fmaxf(M, part[c * (a.hd + 2)]);
   const int i = threadIdx.x;
   if (i >= a.hd) return;
   float L = 0.f, o = 0.f;
+#pragma unroll 8
   for (int c = 0; c < nchunks; c++) {
     const float* pc = part + c * (a.hd + 2);
     const float w = expf(pc[0] - M);
@@ -182,7 +187,7 @@ template <int D>
 cudaError_t launch_scan(dim3 grid, size_t smem, cudaStream_t st, bool pdl, const AttnArgs& a) {
   static bool configured = false;
   if (!configured) {
-    cudaFuncSetAttribute(attn_scan_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, 80 * 1024);
+    cudaFuncSetAttribute(attn_scan_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     configured = true;
   }
   return launch_pdl(attn_scan_kernel<D>, grid, dim3(256), smem, st, pdl, a);
@@ -196,7 +201,8 @@ cudaError_t attn_prep_launch(const AttnArgs& a, cudaStream_t st, bool pdl) {
 
 cudaError_t attn_scan_launch(const AttnArgs& a, cudaStream_t st, bool pdl) {
   dim3 grid(a.nkv, a.chunk_ctas);
-  const size_t smem = (size_t)(32 * (a.hd + 1) + 32 * a.hd + 8 * a.hd) * sizeof(float);
+  const size_t smem = (size_t)(32 * (a.hd + 1) + 32 * a.hd + a.rows * (a.nh / a.nkv) * a.hd) * sizeof(float);
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
   switch (a.hd / 32) {
     case 2: return launch_scan<2>(grid, smem, st, pdl, a);
     case 4: return launch_scan<4>(grid, smem, st, pdl, a);

@@ -7,16 +7,17 @@
 // delta = (v - pred) * beta; S += k delta^T; o = S^T q / sqrt(dk)).
 //
 // Grid: one CTA per (value head, 32-column slice of the value dimension).
-// The delta rule is separable over value columns, so a slice's 128 x 32
-// state block lives in registers for the whole pass (8 warps x 16 key rows,
-// lane = column) and is read and written exactly once.  Rows are processed
-// serially inside the CTA, so a row's result never depends on how many rows
-// the pass holds.
+// The delta rule is separable over value columns, so a slice's dk x 32 state
+// block lives in registers for the whole pass: warp w owns columns 4w..4w+3,
+// lane = (column, group of dk/8 key rows), and the sums over key rows are
+// shuffles inside the warp.  The conv outputs of a row are shared through a
+// double-buffered shared row, so a row costs one CTA barrier.  Rows are
+// processed serially inside the CTA, so a row's result never depends on how
+// many rows the pass holds.
 //
-// Rollback: the pass reads state buffer `sel` and writes buffer `1-sel`.
-// A pass that commits only c < k rows is rolled back by running the same
-// kernel again over the first c rows of the same projections (replay mode),
-// which reproduces bit for bit the state c sequential rows would leave.
+// Rollback: the state lives in a ring of kStateRing buffers.  A pass reads
+// buffer `cur` and writes the state after its row t to buffer cur+1+t, so
+// committing c rows (any c <= rows) only moves `cur` by c.
 #include "kernels.cuh"
 #include "model_kernels.cuh"
 #include "devfns.cuh"
@@ -32,17 +33,9 @@ __device__ __forceinline__ float softplus_ref(float v) {
   return log1pf(expf(v));
 }
 
-// Fixed-order sum across the 8 warps of a column: red[warp][lane].
-__device__ __forceinline__ float warp8_col_sum(float v, float (*red)[33], int warp, int lane) {
-  red[warp][lane] = v;
-  __syncthreads();
-  float s = red[0][lane];
-#pragma unroll
-  for (int w = 1; w < 8; w++) s = __fadd_rn(s, red[w][lane]);
-  __syncthreads();
-  return s;
-}
+constexpr int kMaxRowsDn = 8;
 
+template <int K>  // conv kernel width
 __global__ void __launch_bounds__(256) deltanet_kernel(DeltaNetArgs a) {
   pdl_wait();
   pdl_trigger();
@@ -56,126 +49,138 @@ __global__ void __launch_bounds__(256) deltanet_kernel(DeltaNetArgs a) {
   const int rep = a.tiled_heads ? vh / a.nk : vh % ratio;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int key_dim = a.nk * a.dk;
-  const int conv_dim = 2 * key_dim + a.nv * a.dv;
-  const int K = a.conv_k;  // conv kernel width (<= 4)
-  const int rows_i = a.dk / 8;  // key rows per warp
-  const int j = slice * 32 + lane;  // value column
-  const int sel = *a.sel;
-  const int rows = a.replay ? *a.committed : a.rows;
-  if (a.replay && rows >= a.rows) return;  // a fully accepted pass needs no replay
+  const int rows_i = a.dk / 8;   // key rows per lane
+  const int c4 = lane & 3, rg = lane >> 2;
+  const int j = slice * 32 + 4 * warp + c4;  // value column of this lane
+  const int kr0 = rg * rows_i;               // first key row of this lane
+  const int cur = *a.cur;
+  const int rows = a.rows;
 
-  __shared__ float qk[2][256];  // normalized q, k of this key head (dk <= 256)
-  __shared__ float red[8][33];
-  __shared__ float bg[2];
-  // conv channels this CTA computes: q and k of key head kh, and its v columns
+  // per row t (double-buffered by t & 1): conv outputs q | k | v(32 columns)
+  __shared__ float qkv[2][2 * 128 + 32];
+  __shared__ float bg[2][2];
   const int nqk = 2 * a.dk;
   const int nch = nqk + 32;
-  // channel id -> global conv channel
   auto chan = [&](int c) {
     if (c < a.dk) return kh * a.dk + c;
     if (c < nqk) return key_dim + kh * a.dk + (c - a.dk);
     return 2 * key_dim + vh * a.dv + slice * 32 + (c - nqk);
   };
-  // conv history (K-1 taps) of this thread's channels in registers:
-  // thread t owns channels t and t+256 (nch <= 512 covers dk <= 240).
-  float hist[2][3];
-  const float* cin = L.conv_state[sel];
+  // every input of the pass, requested before any arithmetic and parked in
+  // shared memory: thread t owns conv channels t and t+256; thread 0 also
+  // reads beta/alpha
+  __shared__ float xin_s[kMaxRowsDn][2 * 128 + 32];
+  __shared__ float ba_s[kMaxRowsDn][2];
+  float cw[2][4], hist[2][3];
+  const float* cin = L.conv_state[cur];
+  {
+    float xin[kMaxRowsDn][2];
 #pragma unroll
-  for (int u = 0; u < 2; u++) {
-    const int c = threadIdx.x + 256 * u;
+    for (int u = 0; u < 2; u++) {
+      const int c = threadIdx.x + 256 * u;
+      const bool own = c < nch;
+      const int g = own ? chan(c) : 0;
 #pragma unroll
-    for (int tp = 0; tp < 3; tp++) hist[u][tp] = (c < nch && tp < K - 1) ? cin[(int64_t)chan(c) * (K - 1) + tp] : 0.f;
+      for (int t = 0; t < kMaxRowsDn; t++) xin[t][u] = (own && t < rows) ? a.qkv[(int64_t)t * a.qkv_ld + g] : 0.f;
+#pragma unroll
+      for (int tp = 0; tp < 4; tp++) cw[u][tp] = (own && tp < K) ? L.conv_w[(int64_t)g * K + tp] : 0.f;
+#pragma unroll
+      for (int tp = 0; tp < 3; tp++) hist[u][tp] = (own && tp < K - 1) ? cin[(int64_t)g * (K - 1) + tp] : 0.f;
+    }
+    if (threadIdx.x < 2 * kMaxRowsDn) {
+      const int t = threadIdx.x >> 1;
+      int idx = (threadIdx.x & 1) ? a.nv + vh : vh;
+      if (a.ba_interleaved) idx = kh * 2 * ratio + ((threadIdx.x & 1) ? ratio : 0) + rep;
+      if (t < rows) ba_s[t][threadIdx.x & 1] = a.ba[(int64_t)t * a.ba_ld + idx];
+    }
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const int c = threadIdx.x + 256 * u;
+      if (c < nch)
+#pragma unroll
+        for (int t = 0; t < kMaxRowsDn; t++) xin_s[t][c] = xin[t][u];
+    }
   }
-  // state block
+  const float ssm_a = L.ssm_a[vh], dt_bias = L.dt_bias[vh];
   float S[16];
-  const float* sin_ = L.rec_state[sel] + (int64_t)vh * a.dk * a.dv;
+  const float* sin_ = L.rec_state[cur] + (int64_t)vh * a.dk * a.dv;
 #pragma unroll
-  for (int r = 0; r < 16; r++) S[r] = r < rows_i ? sin_[(int64_t)(warp * rows_i + r) * a.dv + j] : 0.f;
+  for (int r = 0; r < 16; r++) S[r] = r < rows_i ? sin_[(int64_t)(kr0 + r) * a.dv + j] : 0.f;
   const float qscale = __fdiv_rn(1.f, sqrtf((float)a.dk));
+  const bool qk_writer = rep == 0 && slice == 0;
+  __syncthreads();  // ba_s is written by threads 0..15 and read by thread 0
 
   for (int t = 0; t < rows; t++) {
-    const float* proj = a.qkv + (int64_t)t * a.qkv_ld;
-    float vcol = 0.f;
+    const int buf = t & 1;
+    const int snap = (cur + 1 + t) % kStateRing;
     // causal depthwise conv + SiLU (src/qwen/quantized_deltanet.rs:733-759)
 #pragma unroll
     for (int u = 0; u < 2; u++) {
       const int c = threadIdx.x + 256 * u;
       if (c < nch) {
-        const int g = chan(c);
-        const float* w = L.conv_w + (int64_t)g * K;
-        const float x = proj[g];
-        float sum = __fmul_rn(w[K - 1], x);
-        for (int tp = 0; tp < K - 1; tp++) sum = __fadd_rn(sum, __fmul_rn(w[tp], hist[u][tp]));
-        const float out = __fmul_rn(sum, sigmoid_ref(sum));
+        const float x = xin_s[t][c];
+        float sum = __fmul_rn(cw[u][K - 1], x);
+#pragma unroll
+        for (int tp = 0; tp < K - 1; tp++) sum = __fadd_rn(sum, __fmul_rn(cw[u][tp], hist[u][tp]));
+        qkv[buf][c] = __fmul_rn(sum, sigmoid_ref(sum));
+#pragma unroll
         for (int tp = 0; tp + 1 < K - 1; tp++) hist[u][tp] = hist[u][tp + 1];
         if (K > 1) hist[u][K - 2] = x;
-        if (c < nqk) qk[c / a.dk][c % a.dk] = out;
-        else red[0][c - nqk] = out;  // v staged through red row 0
-      }
-    }
-    // beta / decay for this value head
-    if (threadIdx.x == 0) {
-      const float* ba = a.ba + (int64_t)t * a.ba_ld;
-      float b, al;
-      if (a.ba_interleaved) {
-        const int base = kh * 2 * ratio;
-        b = ba[base + rep];
-        al = ba[base + ratio + rep];
-      } else {
-        b = ba[vh];
-        al = ba[a.nv + vh];
-      }
-      bg[0] = sigmoid_ref(b);
-      bg[1] = __fmul_rn(L.ssm_a[vh], softplus_ref(__fadd_rn(al, L.dt_bias[vh])));
-    }
-    __syncthreads();
-    vcol = red[0][lane];
-    // L2 norm of q and k (x * (sum x^2 + 1e-6)^-1/2), warp 0 -> q, warp 1 -> k
-    if (warp < 2) {
-      float ss = 0.f;
-      for (int i = lane; i < a.dk; i += 32) ss = fmaf(qk[warp][i], qk[warp][i], ss);
+        if (c >= nqk || qk_writer) {
+          float* co = L.conv_state[snap] + (int64_t)chan(c) * (K - 1);
 #pragma unroll
-      for (int m = 16; m >= 1; m >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, m));
-      const float scale = __fdiv_rn(1.f, sqrtf(__fadd_rn(ss, 1e-6f)));
-      __syncwarp();
-      for (int i = lane; i < a.dk; i += 32) qk[warp][i] = __fmul_rn(qk[warp][i], scale);
+          for (int tp = 0; tp < K - 1; tp++) co[tp] = hist[u][tp];
+        }
+      }
+    }
+    if (threadIdx.x == 0) {
+      bg[buf][0] = sigmoid_ref(ba_s[t][0]);
+      bg[buf][1] = __fmul_rn(ssm_a, softplus_ref(__fadd_rn(ba_s[t][1], dt_bias)));
     }
     __syncthreads();
-    const float beta = bg[0], decay = expf(bg[1]);
-    // recurrence
-    float pred = 0.f;
+    // L2 norms of q and k (x * (sum x^2 + 1e-6)^-1/2), every warp for itself
+    const float* q = qkv[buf];
+    const float* kk = qkv[buf] + a.dk;
+    float sq = 0.f, sk = 0.f;
+    for (int i = lane; i < a.dk; i += 32) {
+      sq = fmaf(q[i], q[i], sq);
+      sk = fmaf(kk[i], kk[i], sk);
+    }
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+      sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, m));
+      sk = __fadd_rn(sk, __shfl_xor_sync(0xffffffffu, sk, m));
+    }
+    const float nq = __fdiv_rn(1.f, sqrtf(__fadd_rn(sq, 1e-6f)));
+    const float nk = __fdiv_rn(1.f, sqrtf(__fadd_rn(sk, 1e-6f)));
+    const float beta = bg[buf][0], decay = expf(bg[buf][1]);
+    const float vcol = qkv[buf][nqk + 4 * warp + c4];
+    // recurrence over this lane's key rows, reduced across the 8 row groups
+    float kv[16], pred = 0.f;
 #pragma unroll
     for (int r = 0; r < 16; r++) {
       if (r < rows_i) {
+        kv[r] = __fmul_rn(kk[kr0 + r], nk);
         S[r] = __fmul_rn(S[r], decay);
-        pred = fmaf(S[r], qk[1][warp * rows_i + r], pred);
+        pred = fmaf(S[r], kv[r], pred);
       }
     }
-    pred = warp8_col_sum(pred, red, warp, lane);
+#pragma unroll
+    for (int m = 4; m <= 16; m <<= 1) pred = __fadd_rn(pred, __shfl_xor_sync(0xffffffffu, pred, m));
     const float delta = __fmul_rn(__fsub_rn(vcol, pred), beta);
     float o = 0.f;
+    float* sout = L.rec_state[snap] + (int64_t)vh * a.dk * a.dv;
 #pragma unroll
     for (int r = 0; r < 16; r++) {
       if (r < rows_i) {
-        S[r] = fmaf(qk[1][warp * rows_i + r], delta, S[r]);
-        o = fmaf(S[r], qk[0][warp * rows_i + r], o);
+        S[r] = fmaf(kv[r], delta, S[r]);
+        o = fmaf(S[r], __fmul_rn(q[kr0 + r], nq), o);
+        sout[(int64_t)(kr0 + r) * a.dv + j] = S[r];
       }
     }
-    o = warp8_col_sum(o, red, warp, lane);
-    if (!a.replay && warp == 0) a.out[(int64_t)t * a.out_ld + vh * a.dv + j] = __fmul_rn(o, qscale);
-  }
-  // write back the state after `rows` rows
-  float* sout = L.rec_state[1 - sel] + (int64_t)vh * a.dk * a.dv;
 #pragma unroll
-  for (int r = 0; r < 16; r++)
-    if (r < rows_i) sout[(int64_t)(warp * rows_i + r) * a.dv + j] = S[r];
-  float* cout_ = L.conv_state[1 - sel];
-  const bool qk_writer = rep == 0 && slice == 0;
-#pragma unroll
-  for (int u = 0; u < 2; u++) {
-    const int c = threadIdx.x + 256 * u;
-    if (c < nch && (c >= nqk || qk_writer))
-      for (int tp = 0; tp < K - 1; tp++) cout_[(int64_t)chan(c) * (K - 1) + tp] = hist[u][tp];
+    for (int m = 4; m <= 16; m <<= 1) o = __fadd_rn(o, __shfl_xor_sync(0xffffffffu, o, m));
+    if (rg == 0) a.out[(int64_t)t * a.out_ld + vh * a.dv + j] = __fmul_rn(o, qscale);
   }
 }
 
@@ -233,6 +238,9 @@ __global__ void __launch_bounds__(256) gated_norm_kernel(GatedNormArgs a) {
 }  // namespace
 
 cudaError_t deltanet_launch(const DeltaNetArgs& a, int nlayers, cudaStream_t st, bool pdl) {
+  if (a.rows < 1 || a.rows > kMaxRowsDn || a.rows >= kStateRing || a.dk > 128 || a.dk % 32 || a.dv % 32 ||
+      a.conv_k > 4 || a.conv_k < 1)
+    return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.nv * (a.dv / 32), nlayers);
   cfg.blockDim = dim3(256);
@@ -242,7 +250,12 @@ cudaError_t deltanet_launch(const DeltaNetArgs& a, int nlayers, cudaStream_t st,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, deltanet_kernel, a);
+  switch (a.conv_k) {
+    case 1: return cudaLaunchKernelEx(&cfg, deltanet_kernel<1>, a);
+    case 2: return cudaLaunchKernelEx(&cfg, deltanet_kernel<2>, a);
+    case 3: return cudaLaunchKernelEx(&cfg, deltanet_kernel<3>, a);
+    default: return cudaLaunchKernelEx(&cfg, deltanet_kernel<4>, a);
+  }
 }
 
 cudaError_t gated_norm_launch(const GatedNormArgs& a, int rows, cudaStream_t st, bool pdl) {

@@ -11,25 +11,36 @@ __global__ void __launch_bounds__(256) f32_matvec_kernel(const float* __restrict
                                                          const float* __restrict__ x, int ldx, int k,
                                                          float* __restrict__ y, int ldy, const float* norm_w,
                                                          float eps, float inv_cols) {
+  // the weight rows do not depend on the previous kernel: request them first
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + warp;
+  const int c4 = cols / 4;
+  constexpr int kMaxPer = 32;  // float4 per lane: cols <= 4096
+  float4 wv[kMaxPer];
+  if (r < rows) {
+    const float4* wr = reinterpret_cast<const float4*>(w + (int64_t)r * cols);
+#pragma unroll
+    for (int j = 0; j < kMaxPer; j++)
+      if (lane + 32 * j < c4) wv[j] = __ldg(wr + lane + 32 * j);
+  }
   pdl_wait();
   pdl_trigger();
   extern __shared__ float4 xs4[];  // [k][cols/4]
-  const int c4 = cols / 4;
+#pragma unroll 4
   for (int i = threadIdx.x; i < k * c4; i += 256) {
-    const int r = i / c4, c = i % c4;
-    xs4[i] = *reinterpret_cast<const float4*>(x + (int64_t)r * ldx + 4 * c);
+    const int rr = i / c4, c = i % c4;
+    xs4[i] = *reinterpret_cast<const float4*>(x + (int64_t)rr * ldx + 4 * c);
   }
   __syncthreads();
   if (norm_w) {  // GGUF RMSNorm of the staged rows (same order as the GEMV prologue)
     __shared__ float den[8];
     const float* xs = reinterpret_cast<const float*>(xs4);
-    const int wp = threadIdx.x >> 5, ln = threadIdx.x & 31;
-    if (wp < k) {
+    if (warp < k) {
       float ss = 0.f;
-      for (int i = ln; i < cols; i += 32) ss = fmaf(xs[wp * cols + i], xs[wp * cols + i], ss);
+      for (int i = lane; i < cols; i += 32) ss = fmaf(xs[warp * cols + i], xs[warp * cols + i], ss);
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-      if (ln == 0) den[wp] = sqrtf(__fadd_rn(__fmul_rn(ss, inv_cols), eps));
+      if (lane == 0) den[warp] = sqrtf(__fadd_rn(__fmul_rn(ss, inv_cols), eps));
     }
     __syncthreads();
     float* xw = reinterpret_cast<float*>(xs4);
@@ -37,15 +48,7 @@ __global__ void __launch_bounds__(256) f32_matvec_kernel(const float* __restrict
       xw[i] = __fmul_rn(__fdiv_rn(xw[i], den[i / cols]), norm_w[i % cols]);
     __syncthreads();
   }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = blockIdx.x * 8 + warp;
   if (r >= rows) return;
-  const float4* wr = reinterpret_cast<const float4*>(w + (int64_t)r * cols);
-  constexpr int kMaxPer = 32;  // float4 per lane: cols <= 4096
-  float4 wv[kMaxPer];
-#pragma unroll
-  for (int j = 0; j < kMaxPer; j++)
-    if (lane + 32 * j < c4) wv[j] = __ldg(wr + lane + 32 * j);
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; i++) acc[i] = 0.f;

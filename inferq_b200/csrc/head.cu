@@ -138,10 +138,12 @@ __global__ void __launch_bounds__(256) accept_kernel(HeadArgs a) {
   }
 }
 
-__global__ void commit_kernel(int* sel, int* pos, const int* result) {
+// Keep the first result[2] rows of the pass: advance the DeltaNet state ring
+// to the state after that row and the KV position past it.
+__global__ void commit_kernel(int* cur, int* pos, const int* result) {
   pdl_wait();
   pdl_trigger();
-  *sel ^= 1;
+  *cur = (*cur + result[2]) % kStateRing;
   *pos += result[2];
 }
 
@@ -161,8 +163,8 @@ cudaError_t accept_launch(const HeadArgs& a, cudaStream_t st, bool pdl) {
   return launch_pdl(accept_kernel, dim3(1), dim3(256), 0, st, pdl, a);
 }
 
-cudaError_t commit_launch(int* sel, int* pos, const int* result, cudaStream_t st, bool pdl) {
-  return launch_pdl(commit_kernel, dim3(1), dim3(1), 0, st, pdl, sel, pos, result);
+cudaError_t commit_launch(int* cur, int* pos, const int* result, cudaStream_t st, bool pdl) {
+  return launch_pdl(commit_kernel, dim3(1), dim3(1), 0, st, pdl, cur, pos, result);
 }
 
 }  // namespace iq

@@ -5,9 +5,13 @@
 namespace iq {
 
 // ----------------------------------------------------------------- DeltaNet
+// DeltaNet state buffers per layer: a ring holding the state before a pass
+// and after each of its rows (so it must exceed the rows of a pass).
+constexpr int kStateRing = 9;
+
 struct DeltaNetLayer {
-  float* conv_state[2];   // [conv_dim][K-1], double-buffered by `sel`
-  float* rec_state[2];    // [nv][dk][dv]
+  float* conv_state[kStateRing];  // [conv_dim][K-1]
+  float* rec_state[kStateRing];   // [nv][dk][dv]
   const float* conv_w;    // [conv_dim][K]
   const float* ssm_a;     // [nv]  (already -exp(A_log))
   const float* dt_bias;   // [nv]
@@ -25,9 +29,7 @@ struct DeltaNetArgs {
   int nk, nv, dk, dv, conv_k;
   int tiled_heads;              // value head layout: 1 TiledByRepeat, 0 GroupedByKeyHead
   int ba_interleaved;           // 1: ssm_ba per key head, 0: beta rows then alpha rows
-  const int* sel;               // device: which state buffer is current
-  const int* committed;         // device: rows to replay (replay mode)
-  int replay;
+  const int* cur;               // device: ring index of the current state
 };
 cudaError_t deltanet_launch(const DeltaNetArgs& a, int nlayers, cudaStream_t st, bool pdl);
 
@@ -149,8 +151,8 @@ struct HeadArgs {
 cudaError_t argmax_launch(const HeadArgs& a, cudaStream_t st, bool pdl);
 cudaError_t accept_launch(const HeadArgs& a, cudaStream_t st, bool pdl);
 
-// sel ^= 1; pos += committed  (after any replay)
-cudaError_t commit_launch(int* sel, int* pos, const int* result, cudaStream_t st, bool pdl);
+// cur = (cur + committed) mod kStateRing; pos += committed
+cudaError_t commit_launch(int* cur, int* pos, const int* result, cudaStream_t st, bool pdl);
 
 template <class K, class... Args>
 inline cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,

@@ -3,7 +3,7 @@
 // One pass (QuantizedModel::forward_inner, src/qwen/quantized_model.rs:654-752):
 //   embed -> per layer { RMSNorm -> DeltaNet | gated attention -> residual
 //                        -> RMSNorm -> MoE -> residual }
-//   -> final RMSNorm -> LM head -> argmax -> accept -> replay/commit
+//   -> final RMSNorm -> LM head -> argmax -> accept -> commit
 // Every launch is enqueued on the state's stream with programmatic dependent
 // launch, and the whole pass is captured once per row count into a CUDA graph.
 #include <algorithm>
@@ -161,7 +161,7 @@ struct Ctx {
     s->marks.emplace_back(name, e);
   }
   int* pos() const { return s->ctrl.as<int>(); }
-  int* sel() const { return s->ctrl.as<int>() + 1; }
+  int* cur() const { return s->ctrl.as<int>() + 1; }  // DeltaNet state ring index
   int* result() const { return s->ctrl.as<int>() + 2; }
   const uint8_t* act(int dt) const { return dt == Q8_0 ? s->act80.as<uint8_t>() : s->act8k.as<uint8_t>(); }
   int64_t arb(int dt) const { return dt == Q8_0 ? s->act80_bytes : s->act8k_bytes; }
@@ -466,9 +466,7 @@ int run_delta(Ctx& x, const Layer& L, const LayerRec& R, int k, int li) {
   a.conv_k = c.linear_conv_kernel_dim;
   a.tiled_heads = c.value_heads_tiled;
   a.ba_interleaved = D.ba_fused;
-  a.sel = x.sel();
-  a.committed = x.result() + 2;
-  a.replay = 0;
+  a.cur = x.cur();
   ++x.s->launch_count;
   IQ_CUDA(deltanet_launch(a, 1, x.st, x.pdl));
   x.mark("dn.recurrence");
@@ -559,48 +557,11 @@ int run_attention(Ctx& x, const Layer& L, const LayerRec& R, int k, int fi) {
   return IQ_OK;
 }
 
-__global__ void rollback_prep_kernel(int* ctrl, int rows, int committed) {
-  ctrl[1] ^= 1;                   // the pass input becomes current again
-  ctrl[0] -= rows - committed;    // truncate the KV positions
-  ctrl[4] = committed;            // rows the replay keeps
-}
-__global__ void flip_kernel(int* ctrl) { ctrl[1] ^= 1; }
-
-int replay_all(Ctx& x, int k) {
-  iq_state* s = x.s;
-  const iq_config& c = x.c;
-  if (x.m->n_linear == 0) return IQ_OK;
-  const int vdim = c.linear_num_value_heads * c.linear_value_head_dim;
-  const int conv_dim = 2 * c.linear_num_key_heads * c.linear_key_head_dim + vdim;
-  // one launch per layer keeps each layer's projection pointers simple
-  for (int li = 0; li < x.m->n_linear; li++) {
-    DeltaNetArgs a = {};
-    a.layers = s->dn_layers.as<DeltaNetLayer>() + li;
-    a.qkv = s->dn_qkv[li].as<float>();
-    a.qkv_ld = conv_dim;
-    a.ba = s->dn_ba[li].as<float>();
-    a.ba_ld = 2 * c.linear_num_value_heads;
-    a.out = nullptr;
-    a.rows = k;
-    a.nk = c.linear_num_key_heads;
-    a.nv = c.linear_num_value_heads;
-    a.dk = c.linear_key_head_dim;
-    a.dv = c.linear_value_head_dim;
-    a.conv_k = c.linear_conv_kernel_dim;
-    a.tiled_heads = c.value_heads_tiled;
-    const Layer* L = nullptr;
-    int seen = 0;
-    for (const Layer& ly : x.m->layers)
-      if (ly.type == kLinear && seen++ == li) { L = &ly; break; }
-    a.ba_interleaved = L->dn.ba_fused;
-    a.sel = x.sel();
-    a.committed = x.result() + 2;
-    a.replay = 1;
-    ++x.s->launch_count;
-    IQ_CUDA(deltanet_launch(a, 1, x.st, x.pdl));
-  x.mark("dn.recurrence");
-  }
-  return IQ_OK;
+// Undo the last pass down to `committed` of its `rows` rows: the DeltaNet
+// state after that row is already in the ring, the KV cache is truncated.
+__global__ void rollback_kernel(int* ctrl, int rows, int committed) {
+  ctrl[1] = (ctrl[1] - rows + committed + 2 * kStateRing) % kStateRing;
+  ctrl[0] -= rows - committed;
 }
 
 // The pass body shared by forward and verify.
@@ -645,10 +606,8 @@ int run_pass(iq_state* s, int k, bool verify) {
   ++x.s->launch_count;
   IQ_CUDA(accept_launch(h, x.st, x.pdl));
   x.mark("head.accept");
-  if (verify) TRY(replay_all(x, k));
-  x.mark("head.replay");
   ++x.s->launch_count;
-  IQ_CUDA(commit_launch(x.sel(), x.pos(), x.result(), x.st, x.pdl));
+  IQ_CUDA(commit_launch(x.cur(), x.pos(), x.result(), x.st, x.pdl));
   x.mark("head.commit");
   IQ_CUDA(cudaMemcpyAsync(s->h_result, x.result(), 4 * sizeof(int), cudaMemcpyDeviceToHost, x.st));
   return IQ_OK;
@@ -721,20 +680,22 @@ int alloc_state(iq_state* s) {
   IQ_CUDA(s->tokens.reserve(kMaxK * sizeof(int32_t)));
   const int64_t K_conv = c.linear_conv_kernel_dim - 1;
   std::vector<DeltaNetLayer> dl;
-  s->conv.resize(2 * m->n_linear);
-  s->rec.resize(2 * m->n_linear);
+  static_assert(kStateRing > kMaxK, "the state ring holds a pass's rows plus the state before it");
+  s->conv.resize(kStateRing * m->n_linear);
+  s->rec.resize(kStateRing * m->n_linear);
   s->dn_qkv.resize(m->n_linear);
   s->dn_ba.resize(m->n_linear);
   int li = 0;
   for (const Layer& L : m->layers) {
     if (L.type != kLinear) continue;
     DeltaNetLayer d = {};
-    for (int b = 0; b < 2; b++) {
-      IQ_CUDA(s->conv[2 * li + b].reserve(std::max<int64_t>(1, conv_dim * K_conv) * 4));
-      IQ_CUDA(s->rec[2 * li + b].reserve((size_t)c.linear_num_value_heads * c.linear_key_head_dim *
-                                         c.linear_value_head_dim * 4));
-      d.conv_state[b] = s->conv[2 * li + b].as<float>();
-      d.rec_state[b] = s->rec[2 * li + b].as<float>();
+    for (int b = 0; b < kStateRing; b++) {
+      DevBuf& cb = s->conv[kStateRing * li + b];
+      DevBuf& rb = s->rec[kStateRing * li + b];
+      IQ_CUDA(cb.reserve(std::max<int64_t>(1, conv_dim * K_conv) * 4));
+      IQ_CUDA(rb.reserve((size_t)c.linear_num_value_heads * c.linear_key_head_dim * c.linear_value_head_dim * 4));
+      d.conv_state[b] = cb.as<float>();
+      d.rec_state[b] = rb.as<float>();
     }
     d.conv_w = L.dn.conv_w.p();
     d.ssm_a = L.dn.ssm_a.p();
@@ -918,12 +879,7 @@ int iq_rollback(iq_state* s, int committed_rows) {
   IQ_CHECK(s->can_rollback, IQ_ESTATE, "no forward pass to roll back");
   IQ_CHECK(committed_rows >= 0 && committed_rows < s->last_rows, IQ_EINVAL,
            "cannot roll back to %d of %d committed rows", committed_rows, s->last_rows);
-  Ctx x(s);
-  rollback_prep_kernel<<<1, 1, 0, s->st>>>(s->ctrl.as<int>(), s->last_rows, committed_rows);
-  IQ_CUDA(cudaGetLastError());
-  int rc = replay_all(x, s->last_rows);
-  if (rc) return rc;
-  flip_kernel<<<1, 1, 0, s->st>>>(s->ctrl.as<int>());
+  rollback_kernel<<<1, 1, 0, s->st>>>(s->ctrl.as<int>(), s->last_rows, committed_rows);
   IQ_CUDA(cudaGetLastError());
   IQ_CUDA(cudaStreamSynchronize(s->st));
   s->position -= s->last_rows - committed_rows;

@@ -54,10 +54,10 @@ __device__ __forceinline__ void pack_out(uint64_t& lo, uint64_t& hi, int n, int 
 // probabilities ranking the lower expert first.  Then thread e owns experts
 // [e*per, e*per+per), finds their rank in the ascending union with warp
 // ballots, and writes the gate, up and down jobs of its resident ones.
+template <int kPerLane>  // experts per lane: ceil(E / 32) rounded up to 8, 16 or 32
 __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRouteStatic s) {
   pdl_wait();
   pdl_trigger();
-  constexpr int kPerLane = kMaxExperts / 32;
   __shared__ int sel_e[kMaxRows][16];
   __shared__ float sel_w[kMaxRows][16];
   __shared__ unsigned used[kMaxExperts / 32];
@@ -281,7 +281,9 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoeCombineArgs a) {
 
 cudaError_t moe_route_launch(const MoeRouteArgs& a, const MoeRouteStatic& s, cudaStream_t st, bool pdl) {
   if (a.rows > kMaxRows || a.experts > kMaxExperts || a.topk > 16) return cudaErrorInvalidValue;
-  return launch_pdl(moe_route_kernel, dim3(1), dim3(256), 0, st, pdl, a, s);
+  if (a.experts <= 256) return launch_pdl(moe_route_kernel<8>, dim3(1), dim3(256), 0, st, pdl, a, s);
+  if (a.experts <= 512) return launch_pdl(moe_route_kernel<16>, dim3(1), dim3(256), 0, st, pdl, a, s);
+  return launch_pdl(moe_route_kernel<32>, dim3(1), dim3(256), 0, st, pdl, a, s);
 }
 
 cudaError_t moe_act_launch(const MoeActArgs& a, cudaStream_t st, bool pdl) {

@@ -486,6 +486,7 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* __res
     if (pro.mode == kProNone && (jb.act != staged_act || jb.act_nrows != staged_rows || used != staged_stride)) {
       __syncthreads();  // no warp still reads the previous staging
       const int words = used / 16;
+#pragma unroll 4
       for (int i = threadIdx.x; i < jb.act_nrows * words; i += kQmvThreads) {
         const int r = i / words, w = i % words;
         reinterpret_cast<uint4*>(act_smem)[i] =
