@@ -93,6 +93,8 @@ int matrix_forward_dev(const iq_matrix* m, const float* x, int k, float* y, cuda
   QmvJob j;
   memset(&j, 0, sizeof j);
   j.w = m->base;
+  j.tmap = m->tmap();
+  j.tmap_tail = m->tmap_tail();
   j.act = g_scratch.act.as<uint8_t>();
   j.out = y;
   j.w_row_bytes = m->row_bytes;
@@ -135,6 +137,10 @@ int iq_matrix_create(int dtype, const void* data, int64_t rows, int64_t cols, in
   auto buf = std::make_shared<DevBuf>();
   rc = upload_rows(dtype, data, rows, cols, location, *buf, nullptr);
   if (rc) return rc;
+  auto maps = std::make_shared<DevBuf>();
+  if (dtype != F32 && dtype != F16)
+    IQ_CHECK(qmv_tensor_maps(dtype, buf->as<uint8_t>(), rows, cols, *maps) == cudaSuccess, IQ_ECUDA,
+             "cannot describe the matrix for the TMA unit");
   auto* m = new iq_matrix;
   m->dtype = dtype;
   m->rows = rows;
@@ -142,6 +148,7 @@ int iq_matrix_create(int dtype, const void* data, int64_t rows, int64_t cols, in
   m->row_bytes = dev_row_bytes(dtype, cols);
   m->storage = buf;
   m->base = buf->as<uint8_t>();
+  m->maps = maps;
   *out = m;
   return IQ_OK;
 }

@@ -108,7 +108,7 @@ __device__ __forceinline__ void quant_q8k_block_warp_v(const float (&v)[8], uint
              ((uint32_t)(uint8_t)q[3] << 24);
   packed.y = (uint32_t)(uint8_t)q[4] | ((uint32_t)(uint8_t)q[5] << 8) | ((uint32_t)(uint8_t)q[6] << 16) |
              ((uint32_t)(uint8_t)q[7] << 24);
-  *reinterpret_cast<uint2*>(act_row + (int64_t)b * 256 + tig * 64 + s * 8) = packed;
+  *reinterpret_cast<uint2*>(act_row + (int64_t)b * 256 + q8k_act_perm(32 * s + tig * 4)) = packed;
   int16_t* bs = reinterpret_cast<int16_t*>(act_row + q8k_bs_offset(nb) + b * 16);
   if (tig == 0) bs[s] = (int16_t)(sum[0] + sum[1]);
   if (lane == 0) reinterpret_cast<float*>(act_row + (int64_t)nb * 256)[b] = d;

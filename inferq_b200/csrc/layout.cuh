@@ -25,7 +25,9 @@
 //
 // Quantized activations (one row per input row):
 //   Q8_K: [nb x 256 B qs'][nb x f32 d, padded to 16 B][nb x 8 i16 sums of 32 elements]
-//        qs'[b*256 + tig*64 + s*8 + h*4 + e] = q[b*256 + 32s + 16h + tig*4 + e]
+//        qs'[b*256 + tig*64 + (((s>>1) ^ tig) & 3)*16 + (s&1)*8 + h*4 + e]
+//            = q[b*256 + 32s + 16h + tig*4 + e]
+//        (the XOR spreads the four lanes of a row group over distinct banks)
 //   Q8_0: [nb/4 x 128 B qs' (as the weights)][nb x f32 d (the f16-rounded d)]
 #pragma once
 #include "iq_common.cuh"
@@ -66,7 +68,7 @@ __host__ __device__ inline int q80_perm(int bb, int i) {
 // element i (0..255) of a Q8_K activation block
 __host__ __device__ inline int q8k_act_perm(int i) {
   int s = i / 32, ii = i % 32, h = ii / 16, tig = (ii % 16) / 4, e = ii % 4;
-  return tig * 64 + s * 8 + h * 4 + e;
+  return tig * 64 + (((s >> 1) ^ tig) & 3) * 16 + (s & 1) * 8 + h * 4 + e;
 }
 
 }  // namespace iq

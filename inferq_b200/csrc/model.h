@@ -17,7 +17,10 @@ struct Weight {
   int dt = -1;
   int64_t rows = 0, cols = 0, row_bytes = 0;
   DevBuf buf;
+  DevBuf maps;  // TMA tensor maps over buf (quantized weights): unit box, tail box
   uint8_t* p() const { return buf.as<uint8_t>(); }
+  const void* tmap() const { return maps.p; }
+  const void* tmap_tail() const { return maps.p ? static_cast<const uint8_t*>(maps.p) + 128 : nullptr; }
   bool present() const { return dt >= 0; }
 };
 

@@ -85,6 +85,10 @@ struct MoeRouteStatic {
   int ks_sh_gate, ks_sh_down, tiles_sh_gate;
   int with_shared;
   int expert_lo, expert_hi;  // experts resident on this rank: [lo, hi)
+  // TMA tensor maps (device) over the stacked tensors; expert e's rows start
+  // at row (e - expert_lo) * rows_per_expert of its map
+  const void *gate_tm, *up_tm, *down_tm, *gate_tm_tail, *up_tm_tail, *down_tm_tail;
+  const void *sh_gate_tm, *sh_up_tm, *sh_down_tm, *sh_gate_tm_tail, *sh_up_tm_tail, *sh_down_tm_tail;
 };
 
 struct MoeRouteArgs {

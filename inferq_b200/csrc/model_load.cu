@@ -29,6 +29,14 @@ struct Loader {
     return e;
   }
 
+  // The TMA tensor maps the GEMV streams a quantized weight through.
+  static int maps_for(const std::string& n, Weight& w) {
+    if (w.dt != Q4_K && w.dt != Q5_K && w.dt != Q6_K && w.dt != Q8_0) return IQ_OK;
+    IQ_CHECK(qmv_tensor_maps(w.dt, w.p(), w.rows, w.cols, w.maps) == cudaSuccess, IQ_ECUDA,
+             "cannot describe tensor \"%s\" for the TMA unit", n.c_str());
+    return IQ_OK;
+  }
+
   // A 2-D matrix [rows, cols] (a 3-D [a, b, cols] counts as a*b rows).
   int matrix(const std::string& n, int64_t rows, int64_t cols, Weight& w) const {
     const iq_tensor_view* v = find(n);
@@ -46,7 +54,7 @@ struct Loader {
     w.rows = rows;
     w.cols = cols;
     w.row_bytes = dev_row_bytes(v->dtype, cols);
-    return IQ_OK;
+    return maps_for(n, w);
   }
 
   // Rows [r0, r1) of a stacked-expert tensor [E, rows_per, cols].
@@ -66,7 +74,7 @@ struct Loader {
     w.rows = (e1 - e0) * rows_per;
     w.cols = cols;
     w.row_bytes = dev_row_bytes(v->dtype, cols);
-    return IQ_OK;
+    return maps_for(n, w);
   }
 
   // An F32 (or F16) tensor of n elements as f32 on the device.

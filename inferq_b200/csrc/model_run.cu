@@ -99,6 +99,8 @@ QmvJob make_job(const Weight& w, const uint8_t* act, int64_t arb, float* out, in
   QmvJob j;
   memset(&j, 0, sizeof j);
   j.w = w.p();
+  j.tmap = w.tmap();
+  j.tmap_tail = w.tmap_tail();
   j.act = act;
   j.out = out;
   j.resid = resid;
@@ -144,14 +146,7 @@ struct Ctx {
   bool pdl;
   // IQ_NO_PDL=1 turns programmatic dependent launch off (kernel timing,
   // debugging); results are identical either way.
-  // IQ_FUSE=1 computes the norm / quantization that precedes a projection
-  // inside every CTA of the GEMV (a prologue) instead of as its own kernel.
-  // Results are identical; the separate kernel is faster on B200 (each CTA
-  // of the fused form waits on a chain of L2 round trips before streaming).
-  bool fuse;
-  Ctx(iq_state* s_)
-      : s(s_), m(s_->m), c(s_->m->cfg), st(s_->st), pdl(!s_->profiling && !getenv("IQ_NO_PDL")),
-        fuse(getenv("IQ_FUSE") != nullptr) {}
+  Ctx(iq_state* s_) : s(s_), m(s_->m), c(s_->m->cfg), st(s_->st), pdl(!s_->profiling && !getenv("IQ_NO_PDL")) {}
   // Stage timer: under profiling every stage is bracketed by CUDA events.
   void mark(const char* name) {
     if (!s->profiling) return;
@@ -188,8 +183,7 @@ int prep(Ctx& x, const float* in, int ld, int cols, const float* norm, int k, bo
   return IQ_OK;
 }
 
-// The activation rows a prologue describes, produced by a separate kernel
-// (unfused mode; the GEMV then stages them from global memory).
+// The activation rows a projection needs (row prep or gated norm kernel).
 int pre(Ctx& x, const QmvPrologue& p) {
   if (p.mode == kProGated) {
     GatedNormArgs g = {};
@@ -214,12 +208,9 @@ int pre(Ctx& x, const QmvPrologue& p) {
 }
 
 int qmv(Ctx& x, const QmvRec& r, const QmvPrologue* pro = nullptr) {
-  if (pro && !x.fuse) {
-    TRY(pre(x, *pro));
-    pro = nullptr;
-  }
+  if (pro) TRY(pre(x, *pro));
   ++x.s->launch_count;
-  IQ_CUDA(qmv_launch(x.s->jobs.as<QmvJob>() + r.job, r.njobs, nullptr, r.ntiles, r.smem, x.st, x.pdl, pro));
+  IQ_CUDA(qmv_launch(x.s->jobs.as<QmvJob>() + r.job, r.njobs, nullptr, r.ntiles, r.smem, x.st, x.pdl));
   return IQ_OK;
 }
 
@@ -306,18 +297,14 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   const int H = c.hidden_size, E = c.num_experts;
   const bool q8k = needs(W.gate.dt, false) || needs(W.sh_gate.dt, false) || needs(W.router.dt, false);
   const bool q80 = needs(W.gate.dt, true) || needs(W.sh_gate.dt, true) || needs(W.router.dt, true);
-  const QmvPrologue in_pro =
-      row_pro(x, s->hidden.as<float>(), H, H, L.post_norm.p(), k, q8k, q80, x.fuse ? nullptr : s->xn.as<float>());
-  if (!x.fuse) TRY(pre(x, in_pro));
-  const QmvPrologue* gp = x.fuse ? &in_pro : nullptr;
-  // the f32 router normalizes the hidden rows itself when fused
-  const float* rin = x.fuse ? s->hidden.as<float>() : s->xn.as<float>();
-  const float* rnorm = x.fuse ? L.post_norm.p() : nullptr;
+  TRY(pre(x, row_pro(x, s->hidden.as<float>(), H, H, L.post_norm.p(), k, q8k, q80, s->xn.as<float>())));
+  const float* rin = s->xn.as<float>();
+  const float* rnorm = nullptr;
   float* lg = s->logits_moe.as<float>();
   if (W.router.present()) {
     ++x.s->launch_count;
     IQ_CUDA(qmv_launch(x.s->jobs.as<QmvJob>() + R.router.job, R.router.njobs, nullptr, R.router.ntiles, R.router.smem,
-                       x.st, x.pdl, gp));
+                       x.st, x.pdl));
     x.mark("moe.router");
     ++x.s->launch_count;
     IQ_CUDA(f32_matvec(W.selector.p(), 1, H, rin, H, k, lg + E, E + 1, x.st, x.pdl, rnorm, c.rms_norm_eps));
@@ -361,6 +348,18 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   t.gate = W.gate.p();
   t.up = W.up.p();
   t.down = W.down.p();
+  t.gate_tm = W.gate.tmap();
+  t.up_tm = W.up.tmap();
+  t.down_tm = W.down.tmap();
+  t.down_tm_tail = W.down.tmap_tail();
+  t.gate_tm_tail = W.gate.tmap_tail();
+  t.up_tm_tail = W.up.tmap_tail();
+  t.sh_gate_tm = W.sh_gate.tmap();
+  t.sh_up_tm = W.sh_up.tmap();
+  t.sh_down_tm = W.sh_down.tmap();
+  t.sh_gate_tm_tail = W.sh_gate.tmap_tail();
+  t.sh_up_tm_tail = W.sh_up.tmap_tail();
+  t.sh_down_tm_tail = W.sh_down.tmap_tail();
   t.gate_stride = (int64_t)F * W.gate.row_bytes;
   t.up_stride = (int64_t)F * W.up.row_bytes;
   t.down_stride = (int64_t)H * W.down.row_bytes;
@@ -395,7 +394,7 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   const int down_tiles = max_union * t.tiles_down + tiles_sh_down;
   const int gu_smem = k * (int)std::max(s->act8k_bytes, s->act80_bytes);
   ++x.s->launch_count;
-  IQ_CUDA(qmv_launch(a.gu_jobs, 0, a.gu_count, gu_tiles, gu_smem, x.st, x.pdl, gp));
+  IQ_CUDA(qmv_launch(a.gu_jobs, 0, a.gu_count, gu_tiles, gu_smem, x.st, x.pdl));
   x.mark("moe.gate_up");
   MoeActArgs b = {};
   b.gu = a.gu_out;

@@ -87,6 +87,8 @@ extern "C" int iq_matrix_forward_device_noalloc(const iq_matrix* m, const float*
   QmvJob j;
   memset(&j, 0, sizeof j);  // every byte of the job record is rewritten each call
   j.w = m->base;
+  j.tmap = m->tmap();
+  j.tmap_tail = m->tmap_tail();
   j.act = scratch;
   j.out = y;
   j.w_row_bytes = m->row_bytes;

@@ -1,15 +1,22 @@
 // qmv.cu -- skinny quantized GEMV kernels (see qmv.cuh).
 //
 // Persistent CTAs walk the launch's tiles (tile = blockIdx.x + i*gridDim.x).
-// Inside a tile, warp w owns 16 weight rows and one chunk of their blocks;
-// its blocks form one stream across tiles, and the next block of that stream
-// (possibly the first block of the next tile, possibly of another job) is
-// always loaded while the current one is computed.  Activations are staged
-// into shared memory once per change of input rows, not once per tile.
+// Inside a tile, warp w owns 16 weight rows and one chunk of their blocks
+// (units); its units form one stream across tiles and jobs.  Each warp keeps
+// the next `depth` units of its stream in flight in a ring of shared-memory
+// slots: one 2-D TMA load (tensor map over the weight tensor, box = one unit
+// x 16 rows) per unit, completing on the slot's mbarrier.  The warp waits for
+// a slot, copies the unit's fragments to registers, refills the slot with the
+// unit `depth` ahead and computes.  Activations are staged into shared memory
+// once per change of input rows, not once per tile.
 #include <algorithm>
+#include <climits>
+#include <cstring>
+#include <cudaTypedefs.h>
 #include "qmv.cuh"
 #include "layout.cuh"
 #include "devfns.cuh"
+#include "api_util.h"
 
 
 namespace iq {
@@ -37,28 +44,40 @@ struct WRegs {
 __device__ __forceinline__ void load_b_words(uint4 (&bw)[4], const uint8_t* bact, int b, int tig) {
   if (bact) {
 #pragma unroll
-    for (int i = 0; i < 4; i++) bw[i] = *reinterpret_cast<const uint4*>(bact + (int64_t)b * 256 + tig * 64 + i * 16);
+    for (int i = 0; i < 4; i++)
+      bw[i] = *reinterpret_cast<const uint4*>(bact + (int64_t)b * 256 + tig * 64 + ((i ^ tig) & 3) * 16);
   } else {
 #pragma unroll
     for (int i = 0; i < 4; i++) bw[i] = make_uint4(0, 0, 0, 0);
   }
 }
 
-// ------------------------------------------------------------------ loads
-__device__ __forceinline__ void load_block(int dt, const uint8_t* wa, const uint8_t* wb, int nb, int b, int tig,
-                                           WRegs& r) {
+// ------------------------------------------------------------------ slots
+// A slot holds one unit of a warp's 16 rows as the TMA box lands: row r's
+// unit bytes at r * unit_bytes, then (Q6_K / Q8_0) the 16-byte piece of each
+// row's f16 scale tail that covers the unit, at 16 * unit_bytes + 16 r.
+constexpr int kSlotBytes = 16 * 208 + 16 * 16;
+static_assert(kSlotBytes % 128 == 0, "TMA destinations stay 128-byte aligned");
+
+__device__ __forceinline__ int unit_bytes(int dt) {
+  return dt == Q4_K ? 144 : dt == Q5_K ? 176 : dt == Q6_K ? 208 : 128;
+}
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// The words of unit b for rows (gid, gid+8) from a filled slot.
+__device__ __forceinline__ void load_slot(int dt, const uint8_t* slot, int b, int gid, int tig, WRegs& r) {
   switch (dt) {
     case Q4_K:
     case Q5_K: {
       const int BB = dt == Q4_K ? 144 : 176, QS = dt == Q4_K ? 16 : 48;
-      const uint8_t* ba = wa + (int64_t)b * BB;
-      const uint8_t* bb = wb + (int64_t)b * BB;
-      r.r[0] = ld_stream(ba);
-      r.r[1] = ld_stream(bb);
-      r.r[2] = ld_stream(ba + QS + tig * 32);
-      r.r[3] = ld_stream(ba + QS + tig * 32 + 16);
-      r.r[4] = ld_stream(bb + QS + tig * 32);
-      r.r[5] = ld_stream(bb + QS + tig * 32 + 16);
+      const uint8_t* ba = slot + gid * BB;
+      const uint8_t* bb = slot + (gid + 8) * BB;
+      r.r[0] = lds128(ba);
+      r.r[1] = lds128(bb);
+      r.r[2] = lds128(ba + QS + tig * 32);
+      r.r[3] = lds128(ba + QS + tig * 32 + 16);
+      r.r[4] = lds128(bb + QS + tig * 32);
+      r.r[5] = lds128(bb + QS + tig * 32 + 16);
       if (dt == Q5_K) {
         const uint2 x = *reinterpret_cast<const uint2*>(ba + 16 + tig * 8);
         const uint2 y = *reinterpret_cast<const uint2*>(bb + 16 + tig * 8);
@@ -66,30 +85,67 @@ __device__ __forceinline__ void load_block(int dt, const uint8_t* wa, const uint
       }
     } break;
     case Q6_K: {
-      const uint8_t* ba = wa + (int64_t)b * 208;
-      const uint8_t* bb = wb + (int64_t)b * 208;
-      r.r[0] = ld_stream(ba + tig * 48);
-      r.r[1] = ld_stream(ba + tig * 48 + 16);
-      r.r[2] = ld_stream(ba + tig * 48 + 32);
-      r.r[3] = ld_stream(bb + tig * 48);
-      r.r[4] = ld_stream(bb + tig * 48 + 16);
-      r.r[5] = ld_stream(bb + tig * 48 + 32);
-      r.r[6] = ld_stream(ba + 192);
-      r.r[7] = ld_stream(bb + 192);
-      const uint32_t da = *reinterpret_cast<const uint16_t*>(wa + (int64_t)nb * 208 + 2 * b);
-      const uint32_t db = *reinterpret_cast<const uint16_t*>(wb + (int64_t)nb * 208 + 2 * b);
+      const uint8_t* ba = slot + gid * 208;
+      const uint8_t* bb = slot + (gid + 8) * 208;
+      r.r[0] = lds128(ba + tig * 48);
+      r.r[1] = lds128(ba + tig * 48 + 16);
+      r.r[2] = lds128(ba + tig * 48 + 32);
+      r.r[3] = lds128(bb + tig * 48);
+      r.r[4] = lds128(bb + tig * 48 + 16);
+      r.r[5] = lds128(bb + tig * 48 + 32);
+      r.r[6] = lds128(ba + 192);
+      r.r[7] = lds128(bb + 192);
+      const uint8_t* tail = slot + 16 * 208 + 2 * (b & 7);
+      const uint32_t da = *reinterpret_cast<const uint16_t*>(tail + gid * 16);
+      const uint32_t db = *reinterpret_cast<const uint16_t*>(tail + (gid + 8) * 16);
       r.e = da | (db << 16);
     } break;
     default: {  // Q8_0: b indexes groups of four blocks
-      r.r[0] = ld_stream(wa + (int64_t)b * 128 + tig * 32);
-      r.r[1] = ld_stream(wa + (int64_t)b * 128 + tig * 32 + 16);
-      r.r[2] = ld_stream(wb + (int64_t)b * 128 + tig * 32);
-      r.r[3] = ld_stream(wb + (int64_t)b * 128 + tig * 32 + 16);
-      const uint2 x = *reinterpret_cast<const uint2*>(wa + (int64_t)nb * 32 + 8 * b);
-      const uint2 y = *reinterpret_cast<const uint2*>(wb + (int64_t)nb * 32 + 8 * b);
+      const uint8_t* ba = slot + gid * 128;
+      const uint8_t* bb = slot + (gid + 8) * 128;
+      r.r[0] = lds128(ba + tig * 32);
+      r.r[1] = lds128(ba + tig * 32 + 16);
+      r.r[2] = lds128(bb + tig * 32);
+      r.r[3] = lds128(bb + tig * 32 + 16);
+      const uint8_t* tail = slot + 16 * 128 + 8 * (b & 1);
+      const uint2 x = *reinterpret_cast<const uint2*>(tail + gid * 16);
+      const uint2 y = *reinterpret_cast<const uint2*>(tail + (gid + 8) * 16);
       r.r[4] = make_uint4(x.x, x.y, y.x, y.y);
     } break;
   }
+}
+
+// -------------------------------------------------------------- mbarriers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+// Bounded wait for the phase of the given parity; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  for (int i = 0; i < (1 << 20); i++) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+// 2-D TMA tile load (this GPU's memory, no multicast) into this CTA's shared
+// memory, completing on `bar`; weights are read once per pass (evict-first).
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
 }
 
 // ---------------------------------------------------------------- compute
@@ -269,8 +325,9 @@ struct WarpTile {
   int job;                 // job index (-1: no tile)
   int row0;                // first weight row of this warp's 16
   int u0, u1;              // block (unit) range of this warp's chunk
-  const uint8_t *wa, *wb;  // the rows (gid, gid+8), clamped
   int dt, nb, ks, chunk;
+  int y0;                  // tensor-map row of row0
+  const void *tm, *tmt;    // the job's tensor maps
   __device__ bool live() const { return job >= 0 && u0 < u1; }
 };
 
@@ -289,7 +346,7 @@ __device__ __forceinline__ int find_job(const QmvJob* jobs, const int* t0, int n
 }
 
 __device__ __forceinline__ WarpTile warp_tile(const QmvJob* jobs, const int* t0, int njobs, int total, int tile,
-                                              int warp, int gid) {
+                                              int warp) {
   WarpTile w;
   w.job = -1;
   w.u0 = w.u1 = 0;
@@ -297,155 +354,80 @@ __device__ __forceinline__ WarpTile warp_tile(const QmvJob* jobs, const int* t0,
   const int j = find_job(jobs, t0, njobs, tile);
   const QmvJob& jb = jobs[j];
   w.job = j;
+  w.tm = jb.tmap;
+  w.tmt = jb.tmap_tail;
   w.ks = jb.ksplit;
   w.dt = jb.dtype;
   w.nb = jb.cols / gguf_block_elems(w.dt);
   const int rt = warp / w.ks;
   w.chunk = warp % w.ks;
   w.row0 = (tile - jb.tile0) * qmv_rows_per_cta(w.ks) + rt * 16;
+  w.y0 = jb.row_base + w.row0;
   if (w.row0 < jb.rows) {
     const int units = qmv_units(w.dt, jb.cols);
     w.u0 = w.chunk * units / w.ks;
     w.u1 = (w.chunk + 1) * units / w.ks;
   }
-  const int ra = min(w.row0 + gid, jb.rows - 1), rb = min(w.row0 + gid + 8, jb.rows - 1);
-  w.wa = jb.w + (int64_t)ra * jb.w_row_bytes;
-  w.wb = jb.w + (int64_t)rb * jb.w_row_bytes;
   return w;
-}
-
-// Build the launch's activation rows in shared memory from f32 inputs
-// (every CTA does it; the inputs are a few KB per row and L2-resident).
-__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
-
-// Four transformed inputs starting at element i (a multiple of 4) of row r.
-__device__ __forceinline__ void pro_values(const QmvPrologue& p, const float* den, int r, int i, float* v) {
-  const float4 xv = ld4(p.x + (int64_t)r * p.ldx + i);
-  const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
-  if (p.mode == kProRmsNorm) {
-    const float4 wv = ld4(p.w + i);
-    const float ws[4] = {wv.x, wv.y, wv.z, wv.w};
-    const float d = den[r];
-#pragma unroll
-    for (int e = 0; e < 4; e++) v[e] = __fmul_rn(__fdiv_rn(xs[e], d), ws[e]);
-  } else if (p.mode == kProGated) {
-    const int h = i / p.dv;
-    const float4 wv = ld4(p.w + (i - h * p.dv));
-    const float4 zv = ld4(p.z + (int64_t)r * p.ldz + i);
-    const float ws[4] = {wv.x, wv.y, wv.z, wv.w}, zs[4] = {zv.x, zv.y, zv.z, zv.w};
-    const float d = den[r * p.heads + h];
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-      const float silu = __fdiv_rn(zs[e], __fadd_rn(1.f, expf(-zs[e])));
-      v[e] = __fmul_rn(__fmul_rn(__fdiv_rn(xs[e], d), ws[e]), silu);
-    }
-  } else {
-#pragma unroll
-    for (int e = 0; e < 4; e++) v[e] = xs[e];
-  }
-}
-
-// Every CTA builds the launch's activation rows in shared memory from the f32
-// inputs: the norm statistics first (one warp per row, or eight lanes per
-// head), then one warp per Q8_K block / group of four Q8_0 blocks, two items
-// in flight per warp.  All loads are 16-byte vectors; the inputs were written
-// by the previous kernel and are read from L2.
-__device__ __noinline__ void run_prologue(const QmvPrologue& p, uint8_t* smem) {
-  __shared__ float den[kProMaxDen];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* r8k = smem;
-  uint8_t* r80 = smem + (p.want8k ? p.rows * p.stride8k : 0);
-  if (p.mode == kProRmsNorm) {
-    for (int r = warp; r < p.rows; r += kQmvWarps) {
-      const float* x = p.x + (int64_t)r * p.ldx;
-      float ss = 0.f;
-#pragma unroll 4
-      for (int i = 4 * lane; i < p.cols; i += 128) {
-        const float4 v = ld4(x + i);
-        ss = fmaf(v.x, v.x, ss);
-        ss = fmaf(v.y, v.y, ss);
-        ss = fmaf(v.z, v.z, ss);
-        ss = fmaf(v.w, v.w, ss);
-      }
-#pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-      if (lane == 0) den[r] = sqrtf(__fadd_rn(__fmul_rn(ss, p.inv_n), p.eps));
-    }
-  } else if (p.mode == kProGated) {
-    const int sub = lane & 7;
-    for (int q0 = warp * 4; q0 < p.rows * p.heads; q0 += 4 * kQmvWarps) {
-      const int q = q0 + (lane >> 3);
-      float ss = 0.f;
-      if (q < p.rows * p.heads) {
-        const int r = q / p.heads, h = q % p.heads;
-        const float* o = p.x + (int64_t)r * p.ldx + h * p.dv;
-#pragma unroll 4
-        for (int i = 4 * sub; i < p.dv; i += 32) {
-          const float4 v = ld4(o + i);
-          ss = fmaf(v.x, v.x, ss);
-          ss = fmaf(v.y, v.y, ss);
-          ss = fmaf(v.z, v.z, ss);
-          ss = fmaf(v.w, v.w, ss);
-        }
-      }
-#pragma unroll
-      for (int m = 4; m >= 1; m >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, m));
-      if (sub == 0 && q < p.rows * p.heads) den[q] = sqrtf(__fadd_rn(__fmul_rn(ss, p.inv_n), p.eps));
-    }
-  }
-  __syncthreads();
-  if (p.want8k) {
-    const int nb = p.cols / 256, n = p.rows * nb;
-    const int s = lane & 7, tig = lane >> 3;
-    for (int it = warp; it < n; it += 2 * kQmvWarps) {
-      const int it2 = it + kQmvWarps;
-      const bool two = it2 < n;
-      float va[8], vb[8];
-      {
-        const int r = it / nb, b = it % nb;
-        pro_values(p, den, r, b * 256 + 32 * s + tig * 4, va);
-        pro_values(p, den, r, b * 256 + 32 * s + 16 + tig * 4, va + 4);
-      }
-      if (two) {
-        const int r = it2 / nb, b = it2 % nb;
-        pro_values(p, den, r, b * 256 + 32 * s + tig * 4, vb);
-        pro_values(p, den, r, b * 256 + 32 * s + 16 + tig * 4, vb + 4);
-      }
-      quant_q8k_block_warp_v(va, r8k + (it / nb) * p.stride8k, nb, it % nb, lane);
-      if (two) quant_q8k_block_warp_v(vb, r8k + (it2 / nb) * p.stride8k, nb, it2 % nb, lane);
-    }
-  }
-  if (p.want80) {
-    const int nb = p.cols / 32, ng = nb / 4, n = p.rows * ng;
-    for (int it = warp; it < n; it += 2 * kQmvWarps) {
-      const int it2 = it + kQmvWarps;
-      const bool two = it2 < n;
-      float va[4], vb[4];
-      pro_values(p, den, it / ng, q80_lane_base(it % ng, lane), va);
-      if (two) pro_values(p, den, it2 / ng, q80_lane_base(it2 % ng, lane), vb);
-      quant_q80_group_warp_v(va, r80 + (it / ng) * p.stride80, nb, it % ng, lane);
-      if (two) quant_q80_group_warp_v(vb, r80 + (it2 / ng) * p.stride80, nb, it2 % ng, lane);
-    }
-  }
-  if (p.xn_out && blockIdx.x == 0)
-    for (int it = 4 * threadIdx.x; it < p.rows * p.cols; it += 4 * kQmvThreads) {
-      const int r = it / p.cols, i = it % p.cols;
-      float v[4];
-      pro_values(p, den, r, i, v);
-      *reinterpret_cast<float4*>(p.xn_out + (int64_t)r * p.ldxn + i) = make_float4(v[0], v[1], v[2], v[3]);
-    }
-  __syncthreads();
 }
 
 __device__ __forceinline__ int act_used_bytes(int dt, int cols) {
   return (int)(dt == Q8_0 ? act_row_bytes_q80(cols) : act_row_bytes_q8k(cols));
 }
 
+__device__ int g_qmv_timeout;  // set when a slot wait gave up (not expected to happen)
+
+// A warp's position in its stream of units.
+struct StreamPos {
+  int tile, b;
+  WarpTile t;
+};
+
+__device__ __forceinline__ void stream_settle(const QmvJob* jobs, const int* t0, int njobs, int total, int warp,
+                                              StreamPos& p) {
+  while (p.tile < total && p.b >= p.t.u1) {
+    p.tile += gridDim.x;
+    if (p.tile >= total) break;
+    p.t = warp_tile(jobs, t0, njobs, total, p.tile, warp);
+    p.b = p.t.u0;
+  }
+}
+
+// Lane 0: start the TMA load of unit p.b of the warp's 16 rows into `slot`.
+__device__ __forceinline__ void issue_unit(const StreamPos& p, uint8_t* slot, uint64_t* bar, uint64_t pol) {
+  const int dt = p.t.dt, ub = unit_bytes(dt);
+  const bool tail = dt == Q6_K || dt == Q8_0;
+  mbar_expect_tx(bar, 16 * ub + (tail ? 256 : 0));
+  tma_load_2d(slot, p.t.tm, p.b * ub, p.t.y0, bar, pol);
+  if (tail) {
+    const int x = dt == Q6_K ? p.t.nb * 208 + 16 * (p.b >> 3) : p.t.nb * 32 + 16 * (p.b >> 1);
+    tma_load_2d(slot + 16 * ub, p.t.tmt, x, p.t.y0, bar, pol);
+  }
+}
+
+// Dynamic shared memory: [activation rows (act_bytes, rounded up to 128)]
+// [kQmvWarps x depth slots of kSlotBytes].
 __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* __restrict__ jobs, int njobs,
-                                                             const int* __restrict__ dyn_count, QmvPrologue pro) {
-  __shared__ float part[2][kQmvWarps][32][4];
+                                                             const int* __restrict__ dyn_count, int act_bytes,
+                                                             int depth) {
+  __shared__ float part[kQmvWarps][32][4];
   __shared__ int tile0s[kSmemJobs];
-  extern __shared__ __align__(16) uint8_t act_smem[];
+  __shared__ __align__(8) uint64_t bars[kQmvWarps][kQmvMaxDepth];
+  extern __shared__ __align__(128) uint8_t act_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  // TMA destinations: 128-byte aligned (the launch adds 128 bytes of slack)
+  const uint32_t ring0 = (smem_u32(act_smem) + (uint32_t)act_bytes + 127u) & ~127u;
+  uint8_t* ring = act_smem + (ring0 - smem_u32(act_smem)) + warp * depth * kSlotBytes;
+  uint64_t* wbars = bars[warp];
+  if (lane == 0) {
+    for (int i = 0; i < depth; i++) mbar_init(&wbars[i], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+
   if (dyn_count) {
     pdl_wait();
     njobs = *dyn_count;
@@ -456,34 +438,38 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* __res
   }
   const QmvJob& last = jobs[njobs - 1];
   const int total = last.tile0 + (int)ceil_div(last.rows, qmv_rows_per_cta(last.ksplit));
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int gid = lane >> 2, tig = lane & 3;
-
   const int* t0 = nullptr;
   if (njobs <= kSmemJobs) {
     for (int i = threadIdx.x; i < njobs; i += kQmvThreads) tile0s[i] = jobs[i].tile0;
     __syncthreads();
     t0 = tile0s;
   }
-  // the first block of this warp's stream, requested before the wait
-  WarpTile cur_t = warp_tile(jobs, t0, njobs, total, blockIdx.x, warp, gid);
-  WRegs cur;
-  if (cur_t.live()) load_block(cur_t.dt, cur_t.wa, cur_t.wb, cur_t.nb, cur_t.u0, tig, cur);
+
+  // fill the ring before waiting on the previous kernel: weights do not depend on it
+  StreamPos pp;
+  pp.tile = blockIdx.x;
+  pp.t = warp_tile(jobs, t0, njobs, total, pp.tile, warp);
+  pp.b = pp.t.u0;
+  stream_settle(jobs, t0, njobs, total, warp, pp);
+  for (int i = 0; i < depth && pp.tile < total; i++) {
+    if (lane == 0) issue_unit(pp, ring + i * kSlotBytes, &wbars[i], pol);
+    pp.b++;
+    stream_settle(jobs, t0, njobs, total, warp, pp);
+  }
   pdl_wait();
   pdl_trigger();
-  if (pro.mode != kProNone) run_prologue(pro, act_smem);
-  uint8_t* pro8k = act_smem;
-  uint8_t* pro80 = act_smem + (pro.want8k ? pro.rows * pro.stride8k : 0);
 
   // staged activation key: every row of one activation buffer
   const uint8_t* staged_act = nullptr;
   int staged_rows = -1, staged_stride = 0;
-  int it = 0;
-  for (int tile = blockIdx.x; tile < total; tile += gridDim.x, it++) {
-    const QmvJob& jb = jobs[cur_t.job >= 0 ? cur_t.job : find_job(jobs, t0, njobs, tile)];
-    const int n = jb.n;
+  uint32_t n = 0;  // units consumed by this warp
+  bool ok = true;
+  for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+    const WarpTile ct = warp_tile(jobs, t0, njobs, total, tile, warp);
+    const QmvJob& jb = jobs[ct.job];
+    const int nin = jb.n;
     const int used = act_used_bytes(jb.dtype, jb.cols);
-    if (pro.mode == kProNone && (jb.act != staged_act || jb.act_nrows != staged_rows || used != staged_stride)) {
+    if (jb.act != staged_act || jb.act_nrows != staged_rows || used != staged_stride) {
       __syncthreads();  // no warp still reads the previous staging
       const int words = used / 16;
 #pragma unroll 4
@@ -497,33 +483,35 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* __res
       staged_rows = jb.act_nrows;
       staged_stride = used;
     }
-    const uint8_t* base = act_smem;
-    int stride = used;
-    if (pro.mode != kProNone) {
-      base = jb.dtype == Q8_0 ? pro80 : pro8k;
-      stride = jb.dtype == Q8_0 ? pro.stride80 : pro.stride8k;
-    }
-    const uint8_t* bact = gid < n ? base + jb.rowmap[gid] * stride : nullptr;
+    const uint8_t* bact = gid < nin ? act_smem + jb.rowmap[gid] * used : nullptr;
     ActCols ac;
-    ac.c[0] = 2 * tig < n ? base + jb.rowmap[2 * tig] * stride : nullptr;
-    ac.c[1] = 2 * tig + 1 < n ? base + jb.rowmap[2 * tig + 1] * stride : nullptr;
+    ac.c[0] = 2 * tig < nin ? act_smem + jb.rowmap[2 * tig] * used : nullptr;
+    ac.c[1] = 2 * tig + 1 < nin ? act_smem + jb.rowmap[2 * tig + 1] * used : nullptr;
 
-    // this tile's blocks, with the next block of the stream always in flight
-    const WarpTile nxt_t = warp_tile(jobs, t0, njobs, total, tile + gridDim.x, warp, gid);
     Frag f;
 #pragma unroll
     for (int i = 0; i < 4; i++) { f.acc[i] = 0.f; f.accm[i] = 0.f; }
-    if (cur_t.live()) {
-      for (int b = cur_t.u0; b < cur_t.u1; b++) {
-        WRegs nx;
-        const bool more = b + 1 < cur_t.u1;
-        if (more) load_block(cur_t.dt, cur_t.wa, cur_t.wb, cur_t.nb, b + 1, tig, nx);
-        else if (nxt_t.live()) load_block(nxt_t.dt, nxt_t.wa, nxt_t.wb, nxt_t.nb, nxt_t.u0, tig, nx);
-        compute_block(cur_t.dt, cur, bact, ac, cur_t.nb, b, tig, f);
-        if (more || nxt_t.live()) cur = nx;
+    if (ct.live() && ok) {
+      for (int b = ct.u0; b < ct.u1; b++, n++) {
+        const uint32_t si = n % depth;
+        uint8_t* slot = ring + si * kSlotBytes;
+        if (!mbar_wait(&wbars[si], (n / depth) & 1)) {
+          if (lane == 0) atomicExch(&g_qmv_timeout, 1);
+          ok = false;
+          break;
+        }
+        WRegs cur;
+        load_slot(ct.dt, slot, b, gid, tig, cur);
+        // every lane's generic reads of the slot precede the async refill
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (pp.tile < total) {
+          if (lane == 0) issue_unit(pp, slot, &wbars[si], pol);
+          pp.b++;
+          stream_settle(jobs, t0, njobs, total, warp, pp);
+        }
+        compute_block(ct.dt, cur, bact, ac, ct.nb, b, tig, f);
       }
-    } else if (nxt_t.live()) {
-      load_block(nxt_t.dt, nxt_t.wa, nxt_t.wb, nxt_t.nb, nxt_t.u0, tig, cur);
     }
 
     const bool has_min = jb.dtype == Q4_K || jb.dtype == Q5_K;
@@ -531,13 +519,13 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* __res
 #pragma unroll
     for (int i = 0; i < 4; i++) y[i] = has_min ? __fsub_rn(f.acc[i], f.accm[i]) : f.acc[i];
     const int ks = jb.ksplit;
-    bool store = cur_t.job >= 0 && cur_t.row0 < jb.rows;
+    bool store = ok && ct.row0 < jb.rows;
     if (ks > 1) {
-      float(*pb)[32][4] = part[it & 1];
+      float(*pb)[32][4] = part;
 #pragma unroll
       for (int i = 0; i < 4; i++) pb[warp][lane][i] = y[i];
       __syncthreads();
-      store = store && cur_t.chunk == 0;
+      store = store && ct.chunk == 0;
       if (store) {
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -551,16 +539,15 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* __res
     if (store) {
 #pragma unroll
       for (int i = 0; i < 4; i++) {
-        const int row = cur_t.row0 + gid + (i >= 2 ? 8 : 0);
+        const int row = ct.row0 + gid + (i >= 2 ? 8 : 0);
         const int col = 2 * tig + (i & 1);
-        if (row >= jb.rows || col >= n) continue;
+        if (row >= jb.rows || col >= nin) continue;
         const int64_t o = (int64_t)jb.outrow[col] * jb.out_ld + row;
         float v = y[i];
         if (jb.epi == kEpiResidual) v = __fadd_rn(jb.resid[o], v);
         jb.out[o] = v;
       }
     }
-    cur_t = nxt_t;
   }
 }
 
@@ -577,37 +564,92 @@ int qmv_persistent_ctas() {
   return n;
 }
 
+namespace {
+// Dynamic shared memory per CTA: with two CTAs resident on an SM ([0]) and
+// with one ([1]).
+struct SmemLimits {
+  int two = 0, one = 0;
+};
+const SmemLimits& qmv_dyn_smem_limits() {
+  static SmemLimits lim;
+  if (!lim.one) {
+    int dev = 0, per_sm = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa = {};
+    cudaFuncGetAttributes(&fa, qmv_kernel);
+    // each resident block also reserves 1 KB of shared memory for the system
+    lim.two = std::min(optin, per_sm / 2 - 1024) - (int)fa.sharedSizeBytes;
+    lim.one = optin - (int)fa.sharedSizeBytes;
+    cudaFuncSetAttribute(qmv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lim.one);
+  }
+  return lim;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+bool encode_rows(CUtensorMap* m, const uint8_t* base, int64_t rows, int64_t row_bytes, uint32_t box_bytes) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {box_bytes, 16};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+
+cudaError_t qmv_tensor_maps(int dt, const uint8_t* base, int64_t rows, int64_t cols, DevBuf& maps) {
+  if (dt != Q4_K && dt != Q5_K && dt != Q6_K && dt != Q8_0) return cudaErrorInvalidValue;
+  const int64_t rb = dev_row_bytes(dt, (int)cols);
+  const uint32_t ub = dt == Q4_K ? 144 : dt == Q5_K ? 176 : dt == Q6_K ? 208 : 128;
+  if (((uintptr_t)base & 15) || rb % 16 || rows > INT32_MAX || rb > INT32_MAX) return cudaErrorInvalidValue;
+  alignas(64) CUtensorMap h[2];
+  memset(h, 0, sizeof h);
+  if (!encode_rows(&h[0], base, rows, rb, ub)) return cudaErrorInvalidValue;
+  if ((dt == Q6_K || dt == Q8_0) && !encode_rows(&h[1], base, rows, rb, 16)) return cudaErrorInvalidValue;
+  cudaError_t e = maps.reserve(sizeof h);
+  if (e != cudaSuccess) return e;
+  return cudaMemcpy(maps.p, h, sizeof h, cudaMemcpyHostToDevice);
+}
+
 cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int ntiles, int smem_bytes,
-                       cudaStream_t stream, bool pdl, const QmvPrologue* pro) {
-  QmvPrologue p = {};
-  if (pro) {
-    p = *pro;
-    auto a16 = [](const void* q) { return ((uintptr_t)q & 15) == 0; };
-    const bool gated = p.mode == kProGated;
-    if (p.rows < 1 || p.rows > 8 || p.cols % 256 || p.ldx % 4 || !a16(p.x) ||
-        (p.mode == kProRmsNorm && !a16(p.w)) || (p.xn_out && (p.ldxn % 4 || !a16(p.xn_out))) ||
-        (gated && (p.dv % 32 || p.ldz % 4 || !a16(p.z) || !a16(p.w) || p.rows * p.heads > kProMaxDen)))
-      return cudaErrorInvalidValue;
-    smem_bytes = std::max(smem_bytes, qmv_prologue_smem(p));
-  }
-  if (smem_bytes > kQmvMaxActSmem) return cudaErrorInvalidValue;
+                       cudaStream_t stream, bool pdl) {
   if (ntiles <= 0) return cudaSuccess;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(qmv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kQmvMaxActSmem);
-    configured = true;
+  const SmemLimits& lim = qmv_dyn_smem_limits();
+  const int act = ((smem_bytes + 127) & ~127) + 128;  // + alignment slack of the ring
+  const int ring_unit = kQmvWarps * kSlotBytes;
+  int depth = std::min(kQmvMaxDepth, (lim.two - act) / ring_unit);
+  int ctas = qmv_persistent_ctas();
+  if (depth < 2) {  // many activation rows: one CTA per SM
+    depth = std::min(kQmvMaxDepth, (lim.one - act) / ring_unit);
+    ctas /= 2;
   }
+  if (depth < 2) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(std::min(ntiles, qmv_persistent_ctas()));
+  cfg.gridDim = dim3(std::min(ntiles, ctas));
   cfg.blockDim = dim3(kQmvThreads);
-  cfg.dynamicSmemBytes = smem_bytes;
+  cfg.dynamicSmemBytes = act + depth * ring_unit;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, qmv_kernel, jobs, njobs, dyn_count, p);
+  return cudaLaunchKernelEx(&cfg, qmv_kernel, jobs, njobs, dyn_count, smem_bytes, depth);
 }
 
 }  // namespace iq

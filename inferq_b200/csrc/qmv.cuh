@@ -26,6 +26,8 @@ struct QmvJob {
   const uint8_t* act;    // quantized activation rows (Q8_K or Q8_0 layout)
   float* out;
   const float* resid;
+  const void* tmap;      // device CUtensorMap over the weight tensor: box = one unit x 16 rows
+  const void* tmap_tail; // Q6_K / Q8_0: box = 16 bytes x 16 rows over the scale tails
   int64_t w_row_bytes;
   int act_row_bytes;
   int out_ld;
@@ -34,6 +36,8 @@ struct QmvJob {
   int act_nrows;         // rows of `act` staged into shared memory (> every rowmap entry)
   int tile0;             // first global tile of this job
   int epi;
+  int row_base;          // row of the tensor map where this job's row 0 lies
+  int pad_;
   uint8_t rowmap[8];     // activation row of input column i
   int16_t outrow[8];     // output row (of out) of input column i
 };
@@ -41,6 +45,7 @@ struct QmvJob {
 // Two persistent CTAs per SM; each of their warps streams 16 weight rows.
 constexpr int kQmvWarps = 8;
 constexpr int kQmvThreads = 32 * kQmvWarps;
+constexpr int kQmvMaxDepth = 4;  // weight units in flight per warp (at most)
 // Rows one CTA covers for a job.
 __host__ __device__ inline int qmv_rows_per_cta(int ksplit) { return 16 * (kQmvWarps / ksplit); }
 __host__ __device__ inline int qmv_units(int dt, int cols) {
@@ -62,10 +67,8 @@ inline int qmv_tiles(const QmvJob& j) {
   return (int)ceil_div(j.rows, qmv_rows_per_cta(j.ksplit));
 }
 
-// How the activation rows of a launch are produced in shared memory.
-// kProNone stages job.act from global memory; the other modes compute the
-// rows in every CTA from f32 inputs and quantize them straight into shared
-// memory, fusing the norm / gate that precedes the projection.
+// The activation rows a projection needs, as produced by the row-prep or
+// gated-norm kernel that precedes it (host-side description).
 enum QmvProMode : int {
   kProNone = 0,
   kProRmsNorm = 1,  // x / sqrt(mean(x^2) + eps) * w         (GGUF RMSNorm)
@@ -85,8 +88,8 @@ struct QmvPrologue {
   int heads, dv;     // Gated
   float eps, inv_n;  // inv_n = 1/cols (RmsNorm) or 1/dv (Gated)
   int want8k, want80;  // layouts to produce
-  int stride8k, stride80;  // shared-memory row strides of the two layouts
-  float* xn_out;     // RmsNorm: CTA 0 also writes the normalized rows here (or null)
+  int stride8k, stride80;  // row strides of the two layouts (bytes)
+  float* xn_out;     // RmsNorm: the normalized f32 rows are also written here (or null)
   int ldxn;
 };
 
@@ -94,15 +97,15 @@ struct QmvPrologue {
 // When `dyn_count` is non-null the job count is read on the device after the
 // programmatic-dependency wait (jobs written by the previous kernel), and
 // CTAs past the last job's tiles exit.
-// `smem_bytes` must cover n * act_row_bytes of every job in the table.
-constexpr int kQmvMaxActSmem = 64 * 1024;
+// `smem_bytes` must cover n * act_row_bytes of every job in the table; the
+// rest of the CTA's shared memory holds the weight ring (2..4 units per warp).
 cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int ntiles, int smem_bytes,
-                       cudaStream_t stream, bool pdl, const QmvPrologue* pro = nullptr);
-// Norm statistics a prologue keeps (rows, or rows x heads for Gated).
-constexpr int kProMaxDen = 512;
-// Shared memory a prologue launch needs.
-inline int qmv_prologue_smem(const QmvPrologue& p) {
-  return p.rows * (p.want8k ? p.stride8k : 0) + p.rows * (p.want80 ? p.stride80 : 0);
-}
+                       cudaStream_t stream, bool pdl);
+
+// Encode the tensor maps the kernel loads a weight tensor through (device
+// layout, `rows` x `cols`) into `maps`: [0] the unit box, [1] the tail box
+// (Q6_K / Q8_0).  Jobs point at them (tmap = maps, tmap_tail = maps + 128 B).
+struct DevBuf;
+cudaError_t qmv_tensor_maps(int dt, const uint8_t* base, int64_t rows, int64_t cols, DevBuf& maps);
 
 }  // namespace iq
