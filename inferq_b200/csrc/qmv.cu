@@ -331,7 +331,8 @@ struct WarpTile {
   __device__ bool live() const { return job >= 0 && u0 < u1; }
 };
 
-constexpr int kSmemJobs = 1152;  // job tile offsets kept in shared memory
+constexpr int kSmemJobTable = 64;  // whole job records kept in shared memory
+constexpr int kSmemJobs = kSmemJobTable * (int)(sizeof(QmvJob) / sizeof(int));  // tile offsets only
 
 // The last job with tile0 <= tile.  `t0` is the shared-memory copy of the
 // jobs' tile0 when the table fits, else null (read from global memory).
@@ -407,11 +408,16 @@ __device__ __forceinline__ void issue_unit(const StreamPos& p, uint8_t* slot, ui
 
 // Dynamic shared memory: [activation rows (act_bytes, rounded up to 128)]
 // [kQmvWarps x depth slots of kSlotBytes].
-__global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* __restrict__ jobs, int njobs,
-                                                             const int* __restrict__ dyn_count, int act_bytes,
-                                                             int depth) {
+__global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs, int njobs,
+                                                             const int* __restrict__ dyn_count, int total_hint,
+                                                             int act_bytes, int depth) {
   __shared__ float part[kQmvWarps][32][4];
-  __shared__ int tile0s[kSmemJobs];
+  // the job table in shared memory when it is small (one parallel copy, no
+  // dependent global reads later); otherwise just the jobs' tile offsets
+  __shared__ union {
+    QmvJob jobs[kSmemJobTable];
+    int tile0[kSmemJobs];
+  } tab;
   __shared__ __align__(8) uint64_t bars[kQmvWarps][kQmvMaxDepth];
   extern __shared__ __align__(128) uint8_t act_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -436,13 +442,23 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* __res
     pdl_wait();
     return;
   }
-  const QmvJob& last = jobs[njobs - 1];
-  const int total = last.tile0 + (int)ceil_div(last.rows, qmv_rows_per_cta(last.ksplit));
   const int* t0 = nullptr;
-  if (njobs <= kSmemJobs) {
-    for (int i = threadIdx.x; i < njobs; i += kQmvThreads) tile0s[i] = jobs[i].tile0;
+  if (njobs <= kSmemJobTable) {
+    constexpr int kWords = sizeof(QmvJob) / 16;
+#pragma unroll 2
+    for (int i = threadIdx.x; i < njobs * kWords; i += kQmvThreads)
+      reinterpret_cast<uint4*>(tab.jobs)[i] = reinterpret_cast<const uint4*>(jobs)[i];
     __syncthreads();
-    t0 = tile0s;
+    jobs = tab.jobs;
+  } else if (njobs <= kSmemJobs) {
+    for (int i = threadIdx.x; i < njobs; i += kQmvThreads) tab.tile0[i] = jobs[i].tile0;
+    __syncthreads();
+    t0 = tab.tile0;
+  }
+  int total = total_hint;
+  if (total <= 0) {
+    const QmvJob& last = jobs[njobs - 1];
+    total = last.tile0 + (int)ceil_div(last.rows, qmv_rows_per_cta(last.ksplit));
   }
 
   // fill the ring before waiting on the previous kernel: weights do not depend on it
@@ -649,7 +665,7 @@ cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, qmv_kernel, jobs, njobs, dyn_count, smem_bytes, depth);
+  return cudaLaunchKernelEx(&cfg, qmv_kernel, jobs, njobs, dyn_count, dyn_count ? 0 : ntiles, smem_bytes, depth);
 }
 
 }  // namespace iq
