@@ -208,7 +208,10 @@ int pre(Ctx& x, const QmvPrologue& p) {
 }
 
 int qmv(Ctx& x, const QmvRec& r, const QmvPrologue* pro = nullptr) {
-  if (pro) TRY(pre(x, *pro));
+  if (pro) {
+    TRY(pre(x, *pro));
+    x.mark("act.prep");
+  }
   ++x.s->launch_count;
   IQ_CUDA(qmv_launch(x.s->jobs.as<QmvJob>() + r.job, r.njobs, nullptr, r.ntiles, r.smem, x.st, x.pdl));
   return IQ_OK;
@@ -298,6 +301,7 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   const bool q8k = needs(W.gate.dt, false) || needs(W.sh_gate.dt, false) || needs(W.router.dt, false);
   const bool q80 = needs(W.gate.dt, true) || needs(W.sh_gate.dt, true) || needs(W.router.dt, true);
   TRY(pre(x, row_pro(x, s->hidden.as<float>(), H, H, L.post_norm.p(), k, q8k, q80, s->xn.as<float>())));
+  x.mark("act.prep");
   const float* rin = s->xn.as<float>();
   const float* rnorm = nullptr;
   float* lg = s->logits_moe.as<float>();
