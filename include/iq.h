@@ -199,6 +199,37 @@ int iq_verify(iq_state* s, const uint32_t* tokens, int rows, iq_verify_result* o
  * (QuantizedModelState::rollback).  committed_rows < rows of that pass. */
 int iq_rollback(iq_state* s, int committed_rows);
 
+/* ---------------------------------------------------------------- MTP draft
+ * The MTP predictor block (blk.N.nextn.* plus block N's attention and MoE)
+ * keeps its own KV cache inside the state; `iq_mtp_position` reports it.
+ *
+ * Catch-up (replaces synchronize_mtp + shifted_hidden_inputs,
+ * src/runtime.rs:2058-2088, :2184-2223): truncate the MTP cache to
+ * `position` (<= its current position) and run the block over `rows`
+ * committed tokens, token i paired with the target's normalized hidden row
+ * of the position before it: `prev_hidden` (H floats) for the first, NULL
+ * only at position 0 (zeros), then rows 0..rows-2 of `target_hidden`
+ * ([rows][H], host).  No logits.
+ */
+int iq_mtp_sync(iq_state* s, int64_t position, const float* prev_hidden, const uint32_t* tokens, int rows,
+                const float* target_hidden);
+
+/* Drafting (replaces draft_mtp, src/runtime.rs:1995-2056, with
+ * top1_with_scores :2245-2265 and QuantizedMtpHead::forward_with_head,
+ * src/qwen/quantized_mtp.rs:175-227): from `seed` and the target's
+ * normalized hidden row (H floats), run `depth` (1..16) MTP steps, each
+ * followed by the first `draft_vocab` rows of the LM head (the vocabulary
+ * prefix head, leading_rows); step i+1 takes step i's top-1 token and
+ * normalized hidden row.  tokens/probs/margins receive all `depth` steps
+ * (probs, margins may be NULL); *n is the number of leading drafts whose
+ * top-1 probability is >= min_conf (draft_mtp stops before the first that is
+ * not).  Stop tokens are the caller's, as in the reference.  The MTP cache
+ * advances by `depth`; the next iq_mtp_sync truncates it. */
+int iq_mtp_draft(iq_state* s, uint32_t seed, const float* hidden, int depth, int draft_vocab, float min_conf,
+                 uint32_t* tokens, float* probs, float* margins, int* n);
+
+int iq_mtp_position(const iq_state* s, int64_t* position);
+
 /* Distinct experts each MoE layer ran in the last pass (one int per layer);
  * the measured expert union that sets the pass's algorithmic bytes. */
 int iq_state_union_sizes(const iq_state* s, int32_t* per_layer);

@@ -147,7 +147,38 @@ __global__ void commit_kernel(int* cur, int* pos, const int* result) {
   *pos += result[2];
 }
 
+// One MTP draft step's bookkeeping: the drafted token (row 0's argmax)
+// becomes the next step's input token, its scores and token are recorded at
+// slot `i`, and the normalized hidden row becomes the next step's hidden
+// input (the block itself already advanced the MTP KV position).
+__global__ void __launch_bounds__(256) mtp_step_kernel(MtpStepArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    const int tok = a.result[1];
+    a.tokens[0] = tok;
+    a.out_tok[a.i] = tok;
+    a.out_margin[a.i] = a.scores[0];
+    a.out_prob[a.i] = a.scores[1];
+  }
+  for (int j = threadIdx.x; j < a.hidden; j += 256) a.hin[j] = a.xn[j];
+}
+
+__global__ void set_int_kernel(int* p, int v, int add) {
+  pdl_wait();
+  pdl_trigger();
+  *p = add ? *p + v : v;
+}
+
 }  // namespace
+
+cudaError_t mtp_step_launch(const MtpStepArgs& a, cudaStream_t st, bool pdl) {
+  return launch_pdl(mtp_step_kernel, dim3(1), dim3(256), 0, st, pdl, a);
+}
+
+cudaError_t set_int_launch(int* p, int v, bool add, cudaStream_t st, bool pdl) {
+  return launch_pdl(set_int_kernel, dim3(1), dim3(1), 0, st, pdl, p, v, add ? 1 : 0);
+}
 
 cudaError_t embed_launch(int dt, const uint8_t* w, int64_t row_bytes, int cols, const int32_t* tokens, int rows,
                          float* out, int out_ld, cudaStream_t st, bool pdl) {

@@ -153,6 +153,20 @@ struct HeadArgs {
   float* scores;                        // [2] or null
 };
 cudaError_t argmax_launch(const HeadArgs& a, cudaStream_t st, bool pdl);
+
+struct MtpStepArgs {
+  int32_t* tokens;        // [0] <- drafted token (next step's input)
+  const int* result;      // accept result of the draft row: [1] = argmax
+  const float* scores;    // [0] margin, [1] top-1 probability
+  int* out_tok; float* out_prob; float* out_margin;  // [depth]
+  int i;                  // this step's slot
+  const float* xn;        // normalized hidden row of the step
+  float* hin;             // next step's hidden input
+  int hidden;
+};
+cudaError_t mtp_step_launch(const MtpStepArgs& a, cudaStream_t st, bool pdl);
+// *p = v (add = false) or *p += v, in stream order
+cudaError_t set_int_launch(int* p, int v, bool add, cudaStream_t st, bool pdl);
 cudaError_t accept_launch(const HeadArgs& a, cudaStream_t st, bool pdl);
 
 // cur = (cur + committed) mod kStateRing; pos += committed

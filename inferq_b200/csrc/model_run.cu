@@ -31,7 +31,11 @@ struct LayerRec {
 struct KPlan {
   std::vector<LayerRec> layers;
   QmvRec lm_head;
+  LayerRec mtp;    // the MTP block (a full-attention layer + MoE)
+  QmvRec mtp_eh;   // eh_proj: [enorm(embed) | hnorm(hidden)] -> hidden
 };
+
+constexpr int kMaxDraft = 16;  // MTP draft steps per call
 
 }  // namespace iq
 
@@ -42,7 +46,7 @@ struct iq_state {
   int last_rows = 0;     // rows of the last iq_forward pass (rollback bound)
   bool can_rollback = false;
   cudaStream_t st = nullptr;
-  // control words: [0]=pos [1]=sel [2..5]=result
+  // control words: [0]=pos [1]=DeltaNet ring index [2..4]=result [5]=MTP pos
   iq::DevBuf ctrl;
   int* h_result = nullptr;   // pinned [4]
   int32_t* h_tokens = nullptr;  // pinned [8]
@@ -57,6 +61,12 @@ struct iq_state {
   iq::DevBuf hidden, xn, act8k, act80, z, dn_out, qg, kp, vp, qbuf, part, attn_out;
   iq::DevBuf logits_moe, route_e, route_w, gu_jobs, down_jobs, counts, union_list, gu_out, act_mid, y;
   iq::DevBuf logits, pval, pidx, argmax, scores;
+  // MTP predictor: position of its KV cache (host mirror of ctrl[5]), inputs,
+  // per-step outputs and the cached vocabulary-prefix head job
+  int64_t mtp_position = 0;
+  iq::DevBuf mtp_xcat, mtp_hin, mtp_res, mtp_out, mtp_head_job;
+  int mtp_head_vocab = 0;
+  float* h_mtp = nullptr;  // pinned: staging of hidden rows and outputs
   int64_t act8k_bytes = 0, act80_bytes = 0, act_mid_bytes = 0;
   int gu_ld = 0;
   int max_chunks = 0;
@@ -79,6 +89,7 @@ struct iq_state {
         if (g) cudaGraphExecDestroy(g);
     if (h_result) cudaFreeHost(h_result);
     if (h_tokens) cudaFreeHost(h_tokens);
+    if (h_mtp) cudaFreeHost(h_mtp);
     if (st) cudaStreamDestroy(st);
   }
 };
@@ -156,6 +167,7 @@ struct Ctx {
     s->marks.emplace_back(name, e);
   }
   int* pos() const { return s->ctrl.as<int>(); }
+  int* attn_pos = nullptr;  // KV position the attention layers use (default pos())
   int* cur() const { return s->ctrl.as<int>() + 1; }  // DeltaNet state ring index
   int* result() const { return s->ctrl.as<int>() + 2; }
   const uint8_t* act(int dt) const { return dt == Q8_0 ? s->act80.as<uint8_t>() : s->act8k.as<uint8_t>(); }
@@ -164,7 +176,8 @@ struct Ctx {
 
 bool needs(int dt, bool q80) { return dt >= 0 && (q80 ? dt == Q8_0 : dt != Q8_0 && dt != F32); }
 
-int prep(Ctx& x, const float* in, int ld, int cols, const float* norm, int k, bool q8k, bool q80, float* xn) {
+int prep(Ctx& x, const float* in, int ld, int cols, const float* norm, int k, bool q8k, bool q80, float* xn,
+         int ldxn = 0) {
   PrepArgs a = {};
   a.x = in;
   a.ldx = ld;
@@ -173,7 +186,7 @@ int prep(Ctx& x, const float* in, int ld, int cols, const float* norm, int k, bo
   a.eps = x.c.rms_norm_eps;
   a.inv_cols = (float)(1.0 / (double)cols);
   a.xn_out = xn;
-  a.ldxn = cols;
+  a.ldxn = ldxn ? ldxn : cols;
   a.q8k = q8k ? x.s->act8k.as<uint8_t>() : nullptr;
   a.q80 = q80 ? x.s->act80.as<uint8_t>() : nullptr;
   a.q8k_stride = (int)x.s->act8k_bytes;
@@ -204,7 +217,8 @@ int pre(Ctx& x, const QmvPrologue& p) {
     IQ_CUDA(gated_norm_launch(g, p.rows, x.st, x.pdl));
     return IQ_OK;
   }
-  return prep(x, p.x, p.ldx, p.cols, p.mode == kProRmsNorm ? p.w : nullptr, p.rows, p.want8k, p.want80, p.xn_out);
+  return prep(x, p.x, p.ldx, p.cols, p.mode == kProRmsNorm ? p.w : nullptr, p.rows, p.want8k, p.want80, p.xn_out,
+              p.ldxn);
 }
 
 int qmv(Ctx& x, const QmvRec& r, const QmvPrologue* pro = nullptr) {
@@ -282,6 +296,20 @@ int build_plans(iq_state* s) {
       }
       if (L.moe.router.present())
         R.router = add_launch(table, {J(L.moe.router, s->logits_moe.as<float>(), c.num_experts + 1)});
+    }
+    if (m->has_mtp) {
+      auto J = [&](const Weight& w, float* out, int ld, int epi = kEpiStore) {
+        return make_job(w, w.dt == Q8_0 ? s->act80.as<uint8_t>() : s->act8k.as<uint8_t>(),
+                        w.dt == Q8_0 ? s->act80_bytes : s->act8k_bytes, out, ld, k, epi, out);
+      };
+      const Layer& L = m->mtp_layer;
+      P.mtp_eh = add_launch(table, {J(m->mtp_eh_proj, hidden, H)});
+      P.mtp.proj = add_launch(table, {J(L.at.q, s->qg.as<float>(), 2 * nhd),
+                                      J(L.at.k, s->kp.as<float>(), c.num_key_value_heads * c.head_dim),
+                                      J(L.at.v, s->vp.as<float>(), c.num_key_value_heads * c.head_dim)});
+      P.mtp.out = add_launch(table, {J(L.at.o, hidden, H, kEpiResidual)});
+      if (L.moe.router.present())
+        P.mtp.router = add_launch(table, {J(L.moe.router, s->logits_moe.as<float>(), c.num_experts + 1)});
     }
     P.lm_head = add_launch(table, {make_job(m->lm_head, m->lm_head.dt == Q8_0 ? s->act80.as<uint8_t>() : s->act8k.as<uint8_t>(),
                                             m->lm_head.dt == Q8_0 ? s->act80_bytes : s->act8k_bytes,
@@ -542,7 +570,7 @@ int run_attention(Ctx& x, const Layer& L, const LayerRec& R, int k, int fi) {
   a.rotary_dim = c.rotary_dim;
   a.theta = c.rope_theta;
   a.eps = c.rms_norm_eps;
-  a.pos = x.pos();
+  a.pos = x.attn_pos ? x.attn_pos : x.pos();
   a.chunk_ctas = s->max_chunks;
   ++x.s->launch_count;
   IQ_CUDA(attn_prep_launch(a, x.st, x.pdl));
@@ -613,6 +641,107 @@ int run_pass(iq_state* s, int k, bool verify) {
   IQ_CUDA(commit_launch(x.cur(), x.pos(), x.result(), x.st, x.pdl));
   x.mark("head.commit");
   IQ_CUDA(cudaMemcpyAsync(s->h_result, x.result(), 4 * sizeof(int), cudaMemcpyDeviceToHost, x.st));
+  return IQ_OK;
+}
+
+// ---------------------------------------------------------------- MTP
+// The MTP predictor block over k rows (quantized_mtp.rs:175-227): tokens in
+// s->tokens, hidden inputs in s->mtp_hin.  x = eh_proj(enorm(embed(token)) |
+// hnorm(hidden)); the block's attention (its own KV cache, position ctrl[5])
+// and MoE; then shared_head_norm -> s->xn, quantized for the LM head.  The
+// KV position advances by k.
+int run_mtp_block(iq_state* s, int k) {
+  Ctx x(s);
+  x.attn_pos = s->ctrl.as<int>() + 5;
+  iq_model* m = s->m;
+  const iq_config& c = m->cfg;
+  const KPlan& P = s->plans[k - 1];
+  const int H = c.hidden_size;
+  float* xcat = s->mtp_xcat.as<float>();
+  ++s->launch_count;
+  IQ_CUDA(embed_launch(m->embed.dt, m->embed.p(), m->embed.row_bytes, H, s->tokens.as<int32_t>(), k,
+                       s->hidden.as<float>(), H, x.st, x.pdl));
+  QmvPrologue e = row_pro(x, s->hidden.as<float>(), H, H, m->mtp_enorm.p(), k, false, false, xcat);
+  e.ldxn = 2 * H;
+  TRY(pre(x, e));
+  QmvPrologue hh = row_pro(x, s->mtp_hin.as<float>(), H, H, m->mtp_hnorm.p(), k, false, false, xcat + H);
+  hh.ldxn = 2 * H;
+  TRY(pre(x, hh));
+  const int edt = m->mtp_eh_proj.dt;
+  QmvPrologue q = row_pro(x, xcat, 2 * H, 2 * H, nullptr, k, needs(edt, false), needs(edt, true));
+  TRY(qmv(x, P.mtp_eh, &q));
+  x.mark("mtp.eh_proj");
+  TRY(run_attention(x, m->mtp_layer, P.mtp, k, m->n_full));
+  TRY(run_moe(x, m->mtp_layer, P.mtp, k, c.num_hidden_layers));
+  TRY(pre(x, row_pro(x, s->hidden.as<float>(), H, H, m->mtp_head_norm.p(), k, needs(m->lm_head.dt, false),
+                     needs(m->lm_head.dt, true), s->xn.as<float>())));
+  ++s->launch_count;
+  IQ_CUDA(set_int_launch(x.attn_pos, k, true, x.st, x.pdl));
+  x.mark("mtp.block");
+  return IQ_OK;
+}
+
+// The vocabulary-prefix LM head job (first `vocab` rows, leading_rows).
+int mtp_head_job(iq_state* s, int vocab) {
+  if (s->mtp_head_vocab == vocab) return IQ_OK;
+  iq_model* m = s->m;
+  QmvJob j = make_job(m->lm_head, m->lm_head.dt == Q8_0 ? s->act80.as<uint8_t>() : s->act8k.as<uint8_t>(),
+                      m->lm_head.dt == Q8_0 ? s->act80_bytes : s->act8k_bytes, s->logits.as<float>(), vocab, 1,
+                      kEpiStore, nullptr);
+  j.rows = vocab;
+  j.ksplit = qmv_ksplit(m->lm_head.dt, vocab, m->lm_head.cols);
+  IQ_CUDA(s->mtp_head_job.reserve(sizeof j));
+  IQ_CUDA(cudaMemcpy(s->mtp_head_job.p, &j, sizeof j, cudaMemcpyHostToDevice));
+  s->mtp_head_vocab = vocab;
+  return IQ_OK;
+}
+
+// `depth` draft steps from s->tokens[0] / s->mtp_hin[0]; step i's token,
+// probability and margin land in s->mtp_out.
+int run_mtp_draft(iq_state* s, int depth, int vocab) {
+  iq_model* m = s->m;
+  const int H = m->cfg.hidden_size;
+  int* out = s->mtp_out.as<int>();
+  for (int i = 0; i < depth; i++) {
+    TRY(run_mtp_block(s, 1));
+    Ctx x(s);
+    ++s->launch_count;
+    IQ_CUDA(qmv_launch(s->mtp_head_job.as<QmvJob>(), 1, nullptr,
+                       (int)ceil_div(vocab, qmv_rows_per_cta(qmv_ksplit(m->lm_head.dt, vocab, m->lm_head.cols))),
+                       (int)(m->lm_head.dt == Q8_0 ? s->act80_bytes : s->act8k_bytes), x.st, x.pdl));
+    x.mark("mtp.head");
+    HeadArgs h = {};
+    h.logits = s->logits.as<float>();
+    h.logits_ld = vocab;
+    h.rows = 1;
+    h.vocab = vocab;
+    h.part_val = s->pval.as<float>();
+    h.part_idx = s->pidx.as<int>();
+    h.nparts = kArgmaxParts;
+    h.argmax = s->argmax.as<int>();
+    h.tokens = s->tokens.as<int32_t>();
+    h.verify = 0;
+    h.result = s->mtp_res.as<int>();
+    h.scores = s->scores.as<float>();
+    ++s->launch_count;
+    IQ_CUDA(argmax_launch(h, x.st, x.pdl));
+    ++s->launch_count;
+    IQ_CUDA(accept_launch(h, x.st, x.pdl));
+    MtpStepArgs a = {};
+    a.tokens = s->tokens.as<int32_t>();
+    a.result = s->mtp_res.as<int>();
+    a.scores = s->scores.as<float>();
+    a.out_tok = out;
+    a.out_prob = reinterpret_cast<float*>(out + kMaxDraft);
+    a.out_margin = reinterpret_cast<float*>(out + 2 * kMaxDraft);
+    a.i = i;
+    a.xn = s->xn.as<float>();
+    a.hin = s->mtp_hin.as<float>();
+    a.hidden = H;
+    ++s->launch_count;
+    IQ_CUDA(mtp_step_launch(a, x.st, x.pdl));
+    x.mark("mtp.pick");
+  }
   return IQ_OK;
 }
 
@@ -753,6 +882,13 @@ int alloc_state(iq_state* s) {
   IQ_CUDA(s->pidx.reserve(K * kArgmaxParts * 4));
   IQ_CUDA(s->argmax.reserve(K * 4));
   IQ_CUDA(s->scores.reserve(4 * 4));
+  if (m->has_mtp) {
+    IQ_CUDA(s->mtp_xcat.reserve(K * 2 * H * 4));
+    IQ_CUDA(s->mtp_hin.reserve(K * H * 4));
+    IQ_CUDA(s->mtp_res.reserve(4 * 4));
+    IQ_CUDA(s->mtp_out.reserve(3 * kMaxDraft * 4));
+    IQ_CUDA(cudaMallocHost(&s->h_mtp, (size_t)(K * H + 3 * kMaxDraft) * 4));
+  }
   return build_plans(s);
 }
 
@@ -762,6 +898,7 @@ int reset_state(iq_state* s) {
   IQ_CUDA(cudaMemsetAsync(s->ctrl.p, 0, 8 * sizeof(int), s->st));
   IQ_CUDA(cudaStreamSynchronize(s->st));
   s->position = 0;
+  s->mtp_position = 0;
   s->can_rollback = false;
   return IQ_OK;
 }
@@ -873,6 +1010,100 @@ int iq_verify(iq_state* s, const uint32_t* tokens, int rows, iq_verify_result* o
   out->committed = s->h_result[2];
   s->position += out->committed;
   s->can_rollback = false;
+  return IQ_OK;
+}
+
+int iq_mtp_sync(iq_state* s, int64_t position, const float* prev_hidden, const uint32_t* tokens, int rows,
+                const float* target_hidden) {
+  clear_error();
+  IQ_CHECK(s && tokens && target_hidden, IQ_EINVAL, "iq_mtp_sync: null argument");
+  IQ_CHECK(s->m->has_mtp, IQ_EUNSUPPORTED, "the model has no MTP block");
+  IQ_CHECK(rows >= 1, IQ_EINVAL, "MTP catch-up needs at least one row");
+  IQ_CHECK(position >= 0 && position <= s->mtp_position, IQ_EINVAL,
+           "MTP state at position %lld is behind target position %lld", (long long)s->mtp_position,
+           (long long)position);
+  IQ_CHECK(prev_hidden || position == 0, IQ_EINVAL, "previous target hidden row is required after position zero");
+  IQ_CHECK(position + rows <= s->max_pos, IQ_EINVAL, "MTP catch-up exceeds the state's %lld positions",
+           (long long)s->max_pos);
+  const iq_config& c = s->m->cfg;
+  const int H = c.hidden_size;
+  for (int i = 0; i < rows; i++)
+    IQ_CHECK(tokens[i] < (uint32_t)c.vocab_size, IQ_EINVAL, "token %u outside the vocabulary of %d", tokens[i],
+             c.vocab_size);
+  IQ_CUDA(cudaStreamSynchronize(s->st));
+  IQ_CUDA(set_int_launch(s->ctrl.as<int>() + 5, (int)position, false, s->st, false));
+  s->mtp_position = position;
+  for (int r0 = 0; r0 < rows; r0 += kMaxK) {
+    const int k = std::min(kMaxK, rows - r0);
+    IQ_CUDA(cudaStreamSynchronize(s->st));  // pinned staging is reused
+    for (int i = 0; i < k; i++) {
+      s->h_tokens[i] = (int32_t)tokens[r0 + i];
+      // row r takes the target hidden row of position r-1 (shifted_hidden_inputs)
+      const int r = r0 + i;
+      float* dst = s->h_mtp + (int64_t)i * H;
+      if (r > 0) memcpy(dst, target_hidden + (int64_t)(r - 1) * H, (size_t)H * 4);
+      else if (prev_hidden) memcpy(dst, prev_hidden, (size_t)H * 4);
+      else memset(dst, 0, (size_t)H * 4);
+    }
+    IQ_CUDA(cudaMemcpyAsync(s->tokens.p, s->h_tokens, k * 4, cudaMemcpyHostToDevice, s->st));
+    IQ_CUDA(cudaMemcpyAsync(s->mtp_hin.p, s->h_mtp, (size_t)k * H * 4, cudaMemcpyHostToDevice, s->st));
+    int rc = run_mtp_block(s, k);
+    if (rc) return rc;
+  }
+  IQ_CUDA(cudaStreamSynchronize(s->st));
+  if (s->profiling) collect_marks(s);
+  s->mtp_position = position + rows;
+  return IQ_OK;
+}
+
+int iq_mtp_draft(iq_state* s, uint32_t seed, const float* hidden, int depth, int draft_vocab, float min_conf,
+                 uint32_t* tokens, float* probs, float* margins, int* n) {
+  clear_error();
+  IQ_CHECK(s && hidden && tokens && n, IQ_EINVAL, "iq_mtp_draft: null argument");
+  IQ_CHECK(s->m->has_mtp, IQ_EUNSUPPORTED, "the model has no MTP block");
+  const iq_config& c = s->m->cfg;
+  const int H = c.hidden_size;
+  IQ_CHECK(depth >= 1 && depth <= kMaxDraft, IQ_EINVAL, "MTP drafts 1..%d tokens per call, got %d", kMaxDraft,
+           depth);
+  IQ_CHECK(draft_vocab >= 1 && draft_vocab <= c.vocab_size, IQ_EINVAL,
+           "draft vocabulary %d outside 1..%d", draft_vocab, c.vocab_size);
+  IQ_CHECK(seed < (uint32_t)c.vocab_size, IQ_EINVAL, "token %u outside the vocabulary of %d", seed, c.vocab_size);
+  IQ_CHECK(s->mtp_position + depth <= s->max_pos, IQ_EINVAL, "MTP drafting exceeds the state's %lld positions",
+           (long long)s->max_pos);
+  IQ_CUDA(cudaStreamSynchronize(s->st));
+  s->h_tokens[0] = (int32_t)seed;
+  memcpy(s->h_mtp, hidden, (size_t)H * 4);
+  IQ_CUDA(cudaMemcpyAsync(s->tokens.p, s->h_tokens, 4, cudaMemcpyHostToDevice, s->st));
+  IQ_CUDA(cudaMemcpyAsync(s->mtp_hin.p, s->h_mtp, (size_t)H * 4, cudaMemcpyHostToDevice, s->st));
+  int rc = mtp_head_job(s, draft_vocab);
+  if (rc) return rc;
+  if (s->profiling) {
+    Ctx x(s);
+    x.mark("start");
+  }
+  rc = run_mtp_draft(s, depth, draft_vocab);
+  if (rc) return rc;
+  float* ho = s->h_mtp + (int64_t)kMaxK * H;
+  IQ_CUDA(cudaMemcpyAsync(ho, s->mtp_out.p, 3 * kMaxDraft * 4, cudaMemcpyDeviceToHost, s->st));
+  IQ_CUDA(cudaStreamSynchronize(s->st));
+  if (s->profiling) collect_marks(s);
+  s->mtp_position += depth;
+  const int* ot = reinterpret_cast<const int*>(ho);
+  int m = 0;
+  // draft_mtp stops before a token whose top-1 probability is below min_conf
+  while (m < depth && ho[kMaxDraft + m] >= min_conf) m++;
+  for (int i = 0; i < depth; i++) {
+    tokens[i] = (uint32_t)ot[i];
+    if (probs) probs[i] = ho[kMaxDraft + i];
+    if (margins) margins[i] = ho[2 * kMaxDraft + i];
+  }
+  *n = m;
+  return IQ_OK;
+}
+
+int iq_mtp_position(const iq_state* s, int64_t* position) {
+  IQ_CHECK(s && position, IQ_EINVAL, "iq_mtp_position: null argument");
+  *position = s->mtp_position;
   return IQ_OK;
 }
 

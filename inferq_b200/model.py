@@ -55,6 +55,10 @@ def _declare(L):
         "iq_state_routes": (ctypes.c_int, [P, ctypes.c_int, P]),
         "iq_state_set_profiling": (ctypes.c_int, [P, ctypes.c_int]),
         "iq_state_profile": (ctypes.c_int, [P, ctypes.c_char_p, ctypes.c_int]),
+        "iq_mtp_sync": (ctypes.c_int, [P, ctypes.c_int64, P, P, ctypes.c_int, P]),
+        "iq_mtp_draft": (ctypes.c_int, [P, ctypes.c_uint32, P, ctypes.c_int, ctypes.c_int, ctypes.c_float, P, P, P,
+                                        ctypes.POINTER(ctypes.c_int)]),
+        "iq_mtp_position": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_int64)]),
     }
     for n, (r, a) in sig.items():
         f = getattr(L, n)
@@ -160,6 +164,31 @@ class State:
 
     def rollback(self, committed_rows: int):
         _lib.check(lib().iq_rollback(self._h, committed_rows))
+
+    # ------------------------------------------------------------ MTP
+    @property
+    def mtp_position(self) -> int:
+        v = ctypes.c_int64()
+        _lib.check(lib().iq_mtp_position(self._h, ctypes.byref(v)))
+        return v.value
+
+    def mtp_sync(self, position: int, prev_hidden, tokens, target_hidden):
+        """Catch the MTP cache up over committed `tokens` (synchronize_mtp)."""
+        tok = np.ascontiguousarray(tokens, dtype=np.uint32)
+        th = np.ascontiguousarray(target_hidden, dtype=np.float32)
+        ph = None if prev_hidden is None else np.ascontiguousarray(prev_hidden, dtype=np.float32)
+        _lib.check(lib().iq_mtp_sync(self._h, position, _lib.ptr(ph), tok.ctypes.data, len(tok), th.ctypes.data))
+
+    def mtp_draft(self, seed: int, hidden, depth: int, draft_vocab: int, min_conf: float = 0.0):
+        """`depth` MTP draft steps; returns (tokens, probs, margins, n_confident)."""
+        h = np.ascontiguousarray(hidden, dtype=np.float32)
+        tok = np.empty(depth, np.uint32)
+        pr = np.empty(depth, np.float32)
+        mg = np.empty(depth, np.float32)
+        n = ctypes.c_int()
+        _lib.check(lib().iq_mtp_draft(self._h, seed, h.ctypes.data, depth, draft_vocab, min_conf, tok.ctypes.data,
+                                      pr.ctypes.data, mg.ctypes.data, ctypes.byref(n)))
+        return tok, pr, mg, n.value
 
     def union_sizes(self) -> np.ndarray:
         out = np.zeros(self.model.cfg.num_hidden_layers, np.int32)
