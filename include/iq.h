@@ -154,12 +154,19 @@ typedef struct iq_state iq_state;
  * names and shape checks follow the reference's loaders; a missing or
  * misshapen tensor fails with its name in iq_last_error(). */
 int iq_model_create(const iq_tensor_view* tensors, int n, const iq_config* cfg, iq_model** out);
-/* Expert-parallel variant: this rank keeps experts
- * [rank*E/world, (rank+1)*E/world); dense, DeltaNet and attention weights
- * are replicated.  `nccl_comm` is an ncclComm_t of `world` ranks (one per
- * GPU) used to all-gather expert outputs after every MoE layer. */
+/* Expert-parallel variant (no reference counterpart: the reference runs on
+ * one CPU): this rank keeps experts [rank*E/world, (rank+1)*E/world) on the
+ * current device; dense, DeltaNet, attention, LM head and MTP weights are
+ * replicated.  All `world` ranks (one process per GPU) call it together
+ * with the same 128-byte NCCL unique id (from iq_nccl_unique_id on one rank,
+ * shared by the host); the library creates and owns the communicator.
+ * After every MoE layer the routed expert outputs are summed over the ranks
+ * (each slot is nonzero on its owner only), so every rank's results are
+ * bitwise those of a single GPU. */
 int iq_model_create_ep(const iq_tensor_view* tensors, int n, const iq_config* cfg, int rank, int world,
-                       void* nccl_comm, iq_model** out);
+                       const void* nccl_unique_id, iq_model** out);
+/* 128 bytes: an NCCL unique id for iq_model_create_ep. */
+int iq_nccl_unique_id(void* out);
 void iq_model_destroy(iq_model* m);
 int iq_model_weight_bytes(const iq_model* m, int64_t* bytes);
 

@@ -62,7 +62,7 @@ def build(verbose: bool = False, extra: list[str] | None = None) -> Path:
             if verbose and log.strip():
                 print(f"[{s.name}]\n{log}", file=sys.stderr)
     if todo or not LIB.exists():
-        cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcudart", "-lcuda"]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcudart", "-lcuda", "-lnccl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

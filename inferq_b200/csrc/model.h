@@ -75,5 +75,5 @@ struct iq_model {
   iq::Weight mtp_eh_proj;
   iq::Layer mtp_layer;
   int n_linear = 0, n_full = 0;
-  void* nccl_comm = nullptr;  // expert-parallel all-gather (ncclComm_t), or null
+  void* nccl_comm = nullptr;  // expert-parallel exchange (ncclComm_t, owned), or null
 };

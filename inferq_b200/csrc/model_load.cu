@@ -6,6 +6,7 @@
 // quantized_mtp.rs:104-120, quantized_model.rs:512-539.
 #include <cstring>
 #include <unordered_map>
+#include <nccl.h>
 #include "model.h"
 
 namespace iq {
@@ -195,7 +196,7 @@ int validate_config(const iq_config& c) {
   return IQ_OK;
 }
 
-int create(const iq_tensor_view* tensors, int n, const iq_config* cfg, int rank, int world, void* comm,
+int create(const iq_tensor_view* tensors, int n, const iq_config* cfg, int rank, int world, const void* nccl_id,
            iq_model** out) {
   clear_error();
   IQ_CHECK(tensors && cfg && out && n > 0, IQ_EINVAL, "iq_model_create: null argument");
@@ -210,8 +211,17 @@ int create(const iq_tensor_view* tensors, int n, const iq_config* cfg, int rank,
   m->cfg = *cfg;
   m->ep_rank = rank;
   m->ep_world = world;
-  m->nccl_comm = comm;
   IQ_CUDA(cudaGetDevice(&m->device));
+  if (world > 1) {
+    IQ_CHECK(nccl_id, IQ_EINVAL, "expert parallelism over %d ranks needs an NCCL unique id", world);
+    ncclUniqueId id;
+    memcpy(&id, nccl_id, sizeof id);
+    ncclComm_t comm = nullptr;
+    const ncclResult_t r = ncclCommInitRank(&comm, world, id, rank);
+    IQ_CHECK(r == ncclSuccess, IQ_ECUDA, "ncclCommInitRank (rank %d of %d): %s", rank, world,
+             ncclGetErrorString(r));
+    m->nccl_comm = comm;
+  }
   const iq_config& c = *cfg;
   const int64_t H = c.hidden_size;
   TRY(L.matrix("token_embd.weight", c.vocab_size, H, m->embed));
@@ -277,11 +287,24 @@ int iq_model_create(const iq_tensor_view* tensors, int n, const iq_config* cfg, 
 }
 
 int iq_model_create_ep(const iq_tensor_view* tensors, int n, const iq_config* cfg, int rank, int world,
-                       void* nccl_comm, iq_model** out) {
-  return create(tensors, n, cfg, rank, world, nccl_comm, out);
+                       const void* nccl_unique_id, iq_model** out) {
+  return create(tensors, n, cfg, rank, world, nccl_unique_id, out);
 }
 
-void iq_model_destroy(iq_model* m) { delete m; }
+int iq_nccl_unique_id(void* out) {
+  clear_error();
+  IQ_CHECK(out, IQ_EINVAL, "iq_nccl_unique_id: null argument");
+  ncclUniqueId id;
+  const ncclResult_t r = ncclGetUniqueId(&id);
+  IQ_CHECK(r == ncclSuccess, IQ_ECUDA, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+  memcpy(out, &id, sizeof id);
+  return IQ_OK;
+}
+
+void iq_model_destroy(iq_model* m) {
+  if (m && m->nccl_comm) ncclCommDestroy(static_cast<ncclComm_t>(m->nccl_comm));
+  delete m;
+}
 
 int iq_model_weight_bytes(const iq_model* m, int64_t* bytes) {
   IQ_CHECK(m && bytes, IQ_EINVAL, "iq_model_weight_bytes: null argument");

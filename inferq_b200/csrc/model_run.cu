@@ -10,6 +10,7 @@
 #include <cstring>
 #include <cstdlib>
 #include <string>
+#include <nccl.h>
 #include "model.h"
 
 namespace iq {
@@ -445,11 +446,24 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   ++x.s->launch_count;
   IQ_CUDA(moe_act_launch(b, x.st, x.pdl));
   x.mark("moe.act");
+  // Expert parallelism: this rank computes only the routed slots of its own
+  // experts; the others stay exactly zero, and one sum over the ranks then
+  // leaves every slot with the value its owner computed (x + 0 = x), so the
+  // ordered combine below is bitwise the single-GPU one.  The shared expert
+  // is replicated and stays local.
+  const bool ep = x.m->ep_world > 1;
+  const size_t routed = (size_t)k * c.num_experts_per_tok * H;
+  if (ep) IQ_CUDA(cudaMemsetAsync(a.y, 0, routed * sizeof(float), x.st));
   ++x.s->launch_count;
   IQ_CUDA(qmv_launch(a.down_jobs, 0, a.down_count, down_tiles, (k * c.num_experts_per_tok + k) * (int)s->act_mid_bytes,
                      x.st, x.pdl));
   x.mark("moe.down");
-  // expert parallelism: the all-gather of y happens here (model_ep.cu)
+  if (ep) {
+    const ncclResult_t r =
+        ncclAllReduce(a.y, a.y, routed, ncclFloat, ncclSum, static_cast<ncclComm_t>(x.m->nccl_comm), x.st);
+    IQ_CHECK(r == ncclSuccess, IQ_ECUDA, "expert exchange (ncclAllReduce): %s", ncclGetErrorString(r));
+    x.mark("moe.exchange");
+  }
   MoeCombineArgs cb = {};
   cb.y = a.y;
   cb.y_ld = H;

@@ -82,7 +82,9 @@ class Model:
     """A checkpoint resident on the current CUDA device."""
 
     def __init__(self, cfg: Config, tensors: Iterable[Tensor], *, ep_rank: int = 0, ep_world: int = 1,
-                 nccl_comm: int | None = None):
+                 nccl_id: bytes | None = None):
+        """`ep_world` > 1: expert-parallel rank `ep_rank`; every rank passes the
+        same 128-byte `nccl_id` (inferq_b200.ep.shared_unique_id)."""
         self.cfg = cfg
         keep, views = [], []
         names = []
@@ -107,8 +109,11 @@ class Model:
         if ep_world == 1:
             _lib.check(L.iq_model_create(arr, len(views), ctypes.byref(c), ctypes.byref(h)))
         else:
-            _lib.check(L.iq_model_create_ep(arr, len(views), ctypes.byref(c), ep_rank, ep_world,
-                                            nccl_comm, ctypes.byref(h)))
+            if nccl_id is None or len(nccl_id) != 128:
+                raise ValueError("expert parallelism needs the ranks' shared 128-byte NCCL unique id")
+            idbuf = ctypes.create_string_buffer(nccl_id, 128)
+            _lib.check(L.iq_model_create_ep(arr, len(views), ctypes.byref(c), ep_rank, ep_world, idbuf,
+                                            ctypes.byref(h)))
         self._h = h
         del keep, arr
 
