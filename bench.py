@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep", action="store_true",
+                    help="with N > 1: one sequence, experts split over the ranks (expert parallelism) "
+                         "instead of N independent replicas")
     return ap.parse_args()
 
 
@@ -153,10 +156,34 @@ def gemv_bytes(cfg, union, k: int) -> float:
 GEMV_STAGES = ("dn.proj", "dn.out", "attn.proj", "attn.out", "moe.gate_up", "moe.down", "head.lm_head")
 
 
-def build_model(cfg, device):
+def build_model(cfg, device, ep_rank=0, ep_world=1):
     from inferq_b200 import synth
     from inferq_b200.model import Model
+    if ep_world > 1:
+        from inferq_b200 import ep
+        return Model(cfg, synth.generate(cfg, seed=0, device=device), ep_rank=ep_rank, ep_world=ep_world,
+                     nccl_id=ep.shared_unique_id())
     return Model(cfg, synth.generate(cfg, seed=0, device=device))
+
+
+def mtp_timing(state, cfg, hidden_row, seed_token, draft_vocab=32768, depth=3, reps=10):
+    """Device time of an MTP draft call (depth steps, vocabulary-prefix head)
+    and of the catch-up of one committed row; untimed by the main line."""
+    import torch
+    t = []
+    for i in range(reps + 2):
+        pos = state.mtp_position
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        state.mtp_draft(seed_token, hidden_row, depth, min(draft_vocab, cfg.vocab_size))
+        t1 = time.perf_counter()
+        state.mtp_sync(pos, hidden_row, [seed_token], hidden_row[None])
+        t2 = time.perf_counter()
+        if i >= 2:
+            t.append((t1 - t0, t2 - t1))
+    d = np.median(np.array(t), axis=0)
+    return {"draft_us_per_call": d[0] * 1e6, "depth": depth, "draft_vocab": min(draft_vocab, cfg.vocab_size),
+            "sync_us_one_row": d[1] * 1e6, "timing": "host clock around the C-ABI call (synchronizing)"}
 
 
 def greedy_continuation(model, prompt, n):
@@ -244,13 +271,15 @@ def main():
     from inferq_b200 import synth
     from inferq_b200.model import State
     cfg = synth.qwen36_35b()
-    model = build_model(cfg, "cuda")
+    ep_mode = args.ep and world > 1
+    model = build_model(cfg, "cuda", rank if ep_mode else 0, world if ep_mode else 1)
     rng = np.random.default_rng(1234)
     prompt = rng.integers(0, cfg.vocab_size, CTX)
     n_tokens = (args.warmup + args.steps) * K_ROWS + 8
     greedy = greedy_continuation(model, prompt, n_tokens)
     state = State(model, CTX + n_tokens + 16)
-    state.forward(prompt)
+    _, _, prompt_hidden = state.forward(prompt, hidden=True)
+    state.mtp_sync(0, None, prompt, prompt_hidden)
     corrupt = np.random.default_rng(7)
     out = [greedy[0]]
 
@@ -292,7 +321,8 @@ def main():
         mx = t.clone()
         torch.distributed.all_reduce(mx[:2], op=torch.distributed.ReduceOp.MAX)
         torch.distributed.all_reduce(t[2:], op=torch.distributed.ReduceOp.SUM)
-        dev_s, wall, committed_all = float(mx[0]), float(mx[1]), float(t[2])
+        # replicas: every rank commits its own sequence; EP: all ranks commit the same one
+        dev_s, wall, committed_all = float(mx[0]), float(mx[1]), float(t[2]) / (world if ep_mode else 1)
     else:
         committed_all = committed
     # per-stage profile (separate, untimed) for the roofline of the GEMVs
@@ -301,8 +331,13 @@ def main():
         step()
     prof = state.profile()
     state.set_profiling(False)
+    mtp = None
+    if not ep_mode:  # MTP drafting cost at this context (one GPU), after everything timed
+        _, _, hrow = state.forward([out[-1]], hidden=True)
+        mtp = mtp_timing(state, cfg, hrow[0], int(out[-1]))
     if rank != 0:
         return
+    per_seq = 1 if ep_mode else world  # sequences the job ran
     union = np.mean(np.stack(unions), axis=0)
     pos = CTX + len(out)
     alg_bytes = pass_bytes(cfg, union, pos, K_ROWS)
@@ -324,7 +359,7 @@ def main():
     if not args.no_cpu_baseline:
         try:
             cb = cpu_baseline_sample(cfg)
-            cpu = {"value": (committed_all / args.steps / world) / cb["pass_s"], "unit": "tok/s",
+            cpu = {"value": (committed_all / args.steps / per_seq) / cb["pass_s"], "unit": "tok/s",
                    "cores": cb["cores"], "kind": "port", "sample": cb["sample"]}
         except Exception as e:  # the baseline is reported, never required
             cpu = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
@@ -332,13 +367,15 @@ def main():
     line = {
         "metric": METRIC, "value": committed_all / dev_s, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4/q6 dot, f32 accumulate",
+        "scaling": "strong" if ep_mode else "weak", "vs_baseline": None, "dtype": "int8xq4/q6 dot, f32 accumulate",
         "data": "synthetic (seeded random-init Q4_K_M weights, Zipf router bias)",
         "config": {"workload": "qwen3.6-35b-a3b q4_k_m verify k=4 ctx=1024, 30% corrupted greedy drafts",
-                   "verify_us_k4": ms_step * 1e3, "committed_per_step": committed_all / args.steps / world,
+                   "verify_us_k4": ms_step * 1e3, "committed_per_step": committed_all / args.steps / per_seq,
                    "expert_union_mean": float(union.mean()), "pass_bytes": alg_bytes,
                    "l2": "weights (23.6 GB) exceed L2; no flush needed",
-                   "parallelism": f"replicas x{world}", "mtp_drafting": "not yet on device",
+                   "parallelism": f"ep{world} (experts split, NCCL sum of routed outputs per MoE layer)"
+                   if ep_mode else f"replicas x{world}",
+                   "mtp": mtp,
                    "pass_roofline": {"achieved_gbs": pass_gbs, "frac": pass_gbs / peak,
                                      "scope": "whole verify pass: algorithmic bytes / device-timed pass"}},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
