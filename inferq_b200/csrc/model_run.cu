@@ -7,6 +7,7 @@
 // Every launch is enqueued on the state's stream with programmatic dependent
 // launch, and the whole pass is captured once per row count into a CUDA graph.
 #include <algorithm>
+#include <map>
 #include <cstring>
 #include <cstdlib>
 #include <string>
@@ -67,6 +68,12 @@ struct iq_state {
   int64_t mtp_position = 0;
   iq::DevBuf mtp_xcat, mtp_hin, mtp_res, mtp_out, mtp_head_job;
   int mtp_head_vocab = 0;
+  // captured MTP launch sequences: draft per (depth, vocabulary), catch-up per rows
+  std::map<std::pair<int, int>, cudaGraphExec_t> mtp_draft_graphs;
+  std::map<std::pair<int, int>, int> mtp_draft_eager;
+  cudaGraphExec_t mtp_sync_graphs[8] = {};
+  int mtp_sync_eager[8] = {};
+  std::map<cudaGraphExec_t*, int64_t> mtp_graph_launches;
   float* h_mtp = nullptr;  // pinned: staging of hidden rows and outputs
   int64_t act8k_bytes = 0, act80_bytes = 0, act_mid_bytes = 0;
   int gu_ld = 0;
@@ -88,6 +95,10 @@ struct iq_state {
     for (auto& row : graphs)
       for (auto& g : row)
         if (g) cudaGraphExecDestroy(g);
+    for (auto& g : mtp_draft_graphs)
+      if (g.second) cudaGraphExecDestroy(g.second);
+    for (auto& g : mtp_sync_graphs)
+      if (g) cudaGraphExecDestroy(g);
     if (h_result) cudaFreeHost(h_result);
     if (h_tokens) cudaFreeHost(h_tokens);
     if (h_mtp) cudaFreeHost(h_mtp);
@@ -759,6 +770,36 @@ int run_mtp_draft(iq_state* s, int depth, int vocab) {
   return IQ_OK;
 }
 
+// Replay `ge` if it exists; otherwise run `body` eagerly once (so lazily set
+// kernel attributes are configured outside any capture) and capture it into
+// `ge` on the next call.  Under profiling the body always runs eagerly.
+template <class F>
+int run_captured(iq_state* s, cudaGraphExec_t& ge, int& eager, F body) {
+  if (s->profiling) return body();
+  if (!ge) {
+    if (eager++ == 0) return body();
+    cudaGraph_t g = nullptr;
+    IQ_CUDA(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+    const int64_t before = s->launch_count;
+    int rc = body();
+    const int64_t n = s->launch_count - before;
+    s->launch_count = before;
+    cudaError_t e = cudaStreamEndCapture(s->st, &g);
+    if (rc) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    IQ_CUDA(e);
+    e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    IQ_CUDA(e);
+    s->mtp_graph_launches[&ge] = n;
+  }
+  IQ_CUDA(cudaGraphLaunch(ge, s->st));
+  s->launch_count += s->mtp_graph_launches[&ge];
+  return IQ_OK;
+}
+
 // Run a pass through its CUDA graph: the first call of each (mode, rows)
 // runs eagerly (so lazily configured kernel attributes are set outside any
 // capture), the second captures the launch sequence, later calls replay it.
@@ -1061,7 +1102,7 @@ int iq_mtp_sync(iq_state* s, int64_t position, const float* prev_hidden, const u
     }
     IQ_CUDA(cudaMemcpyAsync(s->tokens.p, s->h_tokens, k * 4, cudaMemcpyHostToDevice, s->st));
     IQ_CUDA(cudaMemcpyAsync(s->mtp_hin.p, s->h_mtp, (size_t)k * H * 4, cudaMemcpyHostToDevice, s->st));
-    int rc = run_mtp_block(s, k);
+    int rc = run_captured(s, s->mtp_sync_graphs[k - 1], s->mtp_sync_eager[k - 1], [&] { return run_mtp_block(s, k); });
     if (rc) return rc;
   }
   IQ_CUDA(cudaStreamSynchronize(s->st));
@@ -1095,7 +1136,9 @@ int iq_mtp_draft(iq_state* s, uint32_t seed, const float* hidden, int depth, int
     Ctx x(s);
     x.mark("start");
   }
-  rc = run_mtp_draft(s, depth, draft_vocab);
+  const auto key = std::make_pair(depth, draft_vocab);
+  rc = run_captured(s, s->mtp_draft_graphs[key], s->mtp_draft_eager[key],
+                    [&] { return run_mtp_draft(s, depth, draft_vocab); });
   if (rc) return rc;
   float* ho = s->h_mtp + (int64_t)kMaxK * H;
   IQ_CUDA(cudaMemcpyAsync(ho, s->mtp_out.p, 3 * kMaxDraft * 4, cudaMemcpyDeviceToHost, s->st));
