@@ -237,6 +237,21 @@ int iq_mtp_draft(iq_state* s, uint32_t seed, const float* hidden, int depth, int
 
 int iq_mtp_position(const iq_state* s, int64_t* position);
 
+/* ---------------------------------------------------------------- images
+ * A self-contained host copy of a sequence's state, the device form of
+ * SessionImage / QuantizedStateImage (src/runtime.rs:566-592,
+ * src/qwen/quantized_model.rs:59-100, restore_image :225-252): a 56-byte
+ * header (magic "IQSTATE1", version, layer count, position, MTP position,
+ * shapes), then per decoder layer in order the KV rows [pos][kv_head][head_dim]
+ * (keys, then values) of a full-attention layer or the conv [channel][K-1]
+ * and recurrent [head][key][value] state of a DeltaNet layer, then the MTP
+ * block's KV rows; all f32.  Import checks the header against the loaded
+ * model and the exact byte count, and replaces the state (rollback of the
+ * last pass is no longer available). */
+int iq_state_image_size(const iq_state* s, int64_t* bytes);
+int iq_state_export(iq_state* s, void* out, int64_t bytes);
+int iq_state_import(iq_state* s, const void* in, int64_t bytes);
+
 /* Distinct experts each MoE layer ran in the last pass (one int per layer);
  * the measured expert union that sets the pass's algorithmic bytes. */
 int iq_state_union_sizes(const iq_state* s, int32_t* per_layer);

@@ -1005,6 +1005,142 @@ int iq_state_reset(iq_state* s) {
   return reset_state(s);
 }
 
+// ------------------------------------------------------------ state image
+// A self-contained copy of a sequence's state (SessionImage / QuantizedStateImage,
+// src/runtime.rs:566-592, src/qwen/quantized_model.rs:59-100): a header, then
+// per decoder layer in order either the KV rows [pos][kv_head][head_dim]
+// (keys, then values) or the DeltaNet conv state [channel][K-1] and recurrent
+// state [head][key][value], then the MTP block's KV rows.  All f32.
+struct StateImageHeader {
+  char magic[8];
+  int32_t version, layers;
+  int64_t position, mtp_position;
+  int32_t has_mtp, kv_dim, conv_dim, conv_taps, rec_size, pad;
+};
+static_assert(sizeof(StateImageHeader) == 56, "image header layout");
+
+namespace {
+const char kImageMagic[8] = {'I', 'Q', 'S', 'T', 'A', 'T', 'E', '1'};
+
+StateImageHeader image_header(const iq_state* s) {
+  const iq_config& c = s->m->cfg;
+  StateImageHeader h = {};
+  memcpy(h.magic, kImageMagic, 8);
+  h.version = 1;
+  h.layers = c.num_hidden_layers;
+  h.position = s->position;
+  h.mtp_position = s->m->has_mtp ? s->mtp_position : 0;
+  h.has_mtp = s->m->has_mtp ? 1 : 0;
+  h.kv_dim = c.num_key_value_heads * c.head_dim;
+  const int vdim = c.linear_num_value_heads * c.linear_value_head_dim;
+  h.conv_dim = 2 * c.linear_num_key_heads * c.linear_key_head_dim + vdim;
+  h.conv_taps = c.linear_conv_kernel_dim - 1;
+  h.rec_size = c.linear_num_value_heads * c.linear_key_head_dim * c.linear_value_head_dim;
+  return h;
+}
+
+int64_t image_bytes(const iq_state* s, const StateImageHeader& h) {
+  int64_t b = sizeof(StateImageHeader);
+  for (const Layer& L : s->m->layers)
+    b += L.type == kFull ? 2 * h.position * h.kv_dim * 4 : ((int64_t)h.conv_dim * h.conv_taps + h.rec_size) * 4;
+  if (h.has_mtp) b += 2 * h.mtp_position * h.kv_dim * 4;
+  return b;
+}
+}  // namespace
+
+int iq_state_image_size(const iq_state* s, int64_t* bytes) {
+  IQ_CHECK(s && bytes, IQ_EINVAL, "iq_state_image_size: null argument");
+  *bytes = image_bytes(s, image_header(s));
+  return IQ_OK;
+}
+
+int iq_state_export(iq_state* s, void* out, int64_t bytes) {
+  clear_error();
+  IQ_CHECK(s && out, IQ_EINVAL, "iq_state_export: null argument");
+  const StateImageHeader h = image_header(s);
+  const int64_t need = image_bytes(s, h);
+  IQ_CHECK(bytes >= need, IQ_EINVAL, "state image needs %lld bytes, buffer holds %lld", (long long)need,
+           (long long)bytes);
+  IQ_CUDA(cudaStreamSynchronize(s->st));
+  int cur = 0;
+  IQ_CUDA(cudaMemcpy(&cur, s->ctrl.as<int>() + 1, 4, cudaMemcpyDeviceToHost));
+  uint8_t* p = static_cast<uint8_t*>(out);
+  memcpy(p, &h, sizeof h);
+  p += sizeof h;
+  int li = 0, fi = 0;
+  for (const Layer& L : s->m->layers) {
+    if (L.type == kFull) {
+      const size_t n = (size_t)h.position * h.kv_dim * 4;
+      IQ_CUDA(cudaMemcpy(p, s->kc[fi].p, n, cudaMemcpyDeviceToHost));
+      IQ_CUDA(cudaMemcpy(p + n, s->vc[fi].p, n, cudaMemcpyDeviceToHost));
+      p += 2 * n;
+      fi++;
+    } else {
+      const size_t nc = (size_t)h.conv_dim * h.conv_taps * 4, nr = (size_t)h.rec_size * 4;
+      if (nc) IQ_CUDA(cudaMemcpy(p, s->conv[kStateRing * li + cur].p, nc, cudaMemcpyDeviceToHost));
+      IQ_CUDA(cudaMemcpy(p + nc, s->rec[kStateRing * li + cur].p, nr, cudaMemcpyDeviceToHost));
+      p += nc + nr;
+      li++;
+    }
+  }
+  if (h.has_mtp) {
+    const size_t n = (size_t)h.mtp_position * h.kv_dim * 4;
+    IQ_CUDA(cudaMemcpy(p, s->kc[s->m->n_full].p, n, cudaMemcpyDeviceToHost));
+    IQ_CUDA(cudaMemcpy(p + n, s->vc[s->m->n_full].p, n, cudaMemcpyDeviceToHost));
+  }
+  return IQ_OK;
+}
+
+int iq_state_import(iq_state* s, const void* in, int64_t bytes) {
+  clear_error();
+  IQ_CHECK(s && in, IQ_EINVAL, "iq_state_import: null argument");
+  IQ_CHECK(bytes >= (int64_t)sizeof(StateImageHeader), IQ_EINVAL, "state image of %lld bytes has no header",
+           (long long)bytes);
+  StateImageHeader h;
+  memcpy(&h, in, sizeof h);
+  const StateImageHeader mine = image_header(s);
+  IQ_CHECK(memcmp(h.magic, kImageMagic, 8) == 0 && h.version == 1, IQ_EINVAL, "not a version-1 state image");
+  IQ_CHECK(h.layers == mine.layers && h.kv_dim == mine.kv_dim && h.conv_dim == mine.conv_dim &&
+               h.conv_taps == mine.conv_taps && h.rec_size == mine.rec_size && h.has_mtp == mine.has_mtp,
+           IQ_EINVAL, "state image shapes do not match the loaded model");
+  IQ_CHECK(h.position >= 0 && h.position <= s->max_pos && h.mtp_position >= 0 && h.mtp_position <= s->max_pos,
+           IQ_EINVAL, "state image at position %lld exceeds the state's %lld positions", (long long)h.position,
+           (long long)s->max_pos);
+  const int64_t need = image_bytes(s, h);
+  IQ_CHECK(bytes == need, IQ_EINVAL, "state image holds %lld bytes, its header describes %lld", (long long)bytes,
+           (long long)need);
+  IQ_CUDA(cudaStreamSynchronize(s->st));
+  const uint8_t* p = static_cast<const uint8_t*>(in) + sizeof h;
+  int li = 0, fi = 0;
+  for (const Layer& L : s->m->layers) {
+    if (L.type == kFull) {
+      const size_t n = (size_t)h.position * h.kv_dim * 4;
+      IQ_CUDA(cudaMemcpy(s->kc[fi].p, p, n, cudaMemcpyHostToDevice));
+      IQ_CUDA(cudaMemcpy(s->vc[fi].p, p + n, n, cudaMemcpyHostToDevice));
+      p += 2 * n;
+      fi++;
+    } else {
+      const size_t nc = (size_t)h.conv_dim * h.conv_taps * 4, nr = (size_t)h.rec_size * 4;
+      if (nc) IQ_CUDA(cudaMemcpy(s->conv[kStateRing * li].p, p, nc, cudaMemcpyHostToDevice));
+      IQ_CUDA(cudaMemcpy(s->rec[kStateRing * li].p, p + nc, nr, cudaMemcpyHostToDevice));
+      p += nc + nr;
+      li++;
+    }
+  }
+  if (h.has_mtp) {
+    const size_t n = (size_t)h.mtp_position * h.kv_dim * 4;
+    IQ_CUDA(cudaMemcpy(s->kc[s->m->n_full].p, p, n, cudaMemcpyHostToDevice));
+    IQ_CUDA(cudaMemcpy(s->vc[s->m->n_full].p, p + n, n, cudaMemcpyHostToDevice));
+  }
+  // the imported DeltaNet state is ring slot 0; positions from the header
+  int ctrl[8] = {(int)h.position, 0, 0, 0, 0, (int)h.mtp_position, 0, 0};
+  IQ_CUDA(cudaMemcpy(s->ctrl.p, ctrl, sizeof ctrl, cudaMemcpyHostToDevice));
+  s->position = h.position;
+  s->mtp_position = h.mtp_position;
+  s->can_rollback = false;
+  return IQ_OK;
+}
+
 int iq_state_position(const iq_state* s, int64_t* position) {
   IQ_CHECK(s && position, IQ_EINVAL, "iq_state_position: null argument");
   *position = s->position;

@@ -1,0 +1,69 @@
+"""Layout of the state image exported by iq_state_export (see include/iq.h):
+a 56-byte header, then per decoder layer the KV rows (full attention) or the
+DeltaNet conv + recurrent state, then the MTP block's KV rows; all f32."""
+from __future__ import annotations
+
+import numpy as np
+
+from .synth import Config
+
+HEADER = np.dtype([("magic", "S8"), ("version", "<i4"), ("layers", "<i4"), ("position", "<i8"),
+                   ("mtp_position", "<i8"), ("has_mtp", "<i4"), ("kv_dim", "<i4"), ("conv_dim", "<i4"),
+                   ("conv_taps", "<i4"), ("rec_size", "<i4"), ("pad", "<i4")])
+assert HEADER.itemsize == 56
+MAGIC = b"IQSTATE1"
+
+
+def shapes(cfg: Config) -> dict:
+    vdim = cfg.linear_num_value_heads * cfg.linear_value_head_dim
+    return {"kv_dim": cfg.num_key_value_heads * cfg.head_dim,
+            "conv_dim": 2 * cfg.linear_num_key_heads * cfg.linear_key_head_dim + vdim,
+            "conv_taps": cfg.linear_conv_kernel_dim - 1,
+            "rec_size": cfg.linear_num_value_heads * cfg.linear_key_head_dim * cfg.linear_value_head_dim}
+
+
+def image_bytes(cfg: Config, position: int, mtp_position: int = 0) -> int:
+    sh = shapes(cfg)
+    b = HEADER.itemsize
+    for l in range(cfg.num_hidden_layers):
+        if cfg.layer_is_full(l):
+            b += 2 * position * sh["kv_dim"] * 4
+        else:
+            b += (sh["conv_dim"] * sh["conv_taps"] + sh["rec_size"]) * 4
+    if cfg.mtp_num_hidden_layers:
+        b += 2 * mtp_position * sh["kv_dim"] * 4
+    return b
+
+
+def parse(buf: bytes | np.ndarray, cfg: Config) -> dict:
+    """Split an image into its header and per-layer f32 arrays (validating)."""
+    raw = np.frombuffer(bytes(buf), np.uint8)
+    h = raw[:HEADER.itemsize].view(HEADER)[0]
+    if h["magic"] != MAGIC or h["version"] != 1:
+        raise ValueError("not a version-1 state image")
+    sh = shapes(cfg)
+    for k, v in sh.items():
+        if int(h[k]) != v:
+            raise ValueError(f"image {k} {int(h[k])} does not match the model's {v}")
+    pos, mpos = int(h["position"]), int(h["mtp_position"])
+    if len(raw) != image_bytes(cfg, pos, mpos):
+        raise ValueError("image length does not match its header")
+    f = raw[HEADER.itemsize:].view(np.float32)
+    out, o = {"position": pos, "mtp_position": mpos, "layers": []}, 0
+    for l in range(cfg.num_hidden_layers):
+        if cfg.layer_is_full(l):
+            n = pos * sh["kv_dim"]
+            out["layers"].append({"keys": f[o:o + n].reshape(pos, cfg.num_key_value_heads, cfg.head_dim),
+                                  "values": f[o + n:o + 2 * n].reshape(pos, cfg.num_key_value_heads, cfg.head_dim)})
+            o += 2 * n
+        else:
+            nc = sh["conv_dim"] * sh["conv_taps"]
+            out["layers"].append({"conv": f[o:o + nc].reshape(sh["conv_dim"], sh["conv_taps"]),
+                                  "recurrent": f[o + nc:o + nc + sh["rec_size"]].reshape(
+                                      cfg.linear_num_value_heads, cfg.linear_key_head_dim,
+                                      cfg.linear_value_head_dim)})
+            o += nc + sh["rec_size"]
+    if cfg.mtp_num_hidden_layers:
+        n = mpos * sh["kv_dim"]
+        out["mtp"] = {"keys": f[o:o + n], "values": f[o + n:o + 2 * n]}
+    return out

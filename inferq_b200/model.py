@@ -59,6 +59,9 @@ def _declare(L):
         "iq_mtp_draft": (ctypes.c_int, [P, ctypes.c_uint32, P, ctypes.c_int, ctypes.c_int, ctypes.c_float, P, P, P,
                                         ctypes.POINTER(ctypes.c_int)]),
         "iq_mtp_position": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_int64)]),
+        "iq_state_image_size": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_int64)]),
+        "iq_state_export": (ctypes.c_int, [P, P, ctypes.c_int64]),
+        "iq_state_import": (ctypes.c_int, [P, P, ctypes.c_int64]),
     }
     for n, (r, a) in sig.items():
         f = getattr(L, n)
@@ -169,6 +172,20 @@ class State:
 
     def rollback(self, committed_rows: int):
         _lib.check(lib().iq_rollback(self._h, committed_rows))
+
+    # ---------------------------------------------------------- images
+    def export_image(self) -> np.ndarray:
+        """The state as a host image (iq_state_export); see inferq_b200.image."""
+        n = ctypes.c_int64()
+        _lib.check(lib().iq_state_image_size(self._h, ctypes.byref(n)))
+        buf = np.empty(n.value, np.uint8)
+        _lib.check(lib().iq_state_export(self._h, buf.ctypes.data, n.value))
+        return buf
+
+    def import_image(self, buf) -> None:
+        b = np.ascontiguousarray(np.frombuffer(bytes(buf), np.uint8) if not isinstance(buf, np.ndarray) else buf,
+                                 dtype=np.uint8)
+        _lib.check(lib().iq_state_import(self._h, b.ctypes.data, b.size))
 
     # ------------------------------------------------------------ MTP
     @property

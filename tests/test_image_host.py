@@ -1,0 +1,44 @@
+"""State-image layout on CPU: header, size formula and parsing of a
+hand-built image for the tiny and the 35B-shaped configs."""
+import numpy as np
+import pytest
+
+from inferq_b200 import image, synth
+
+
+def _build(cfg, pos, mpos, rng):
+    sh = image.shapes(cfg)
+    h = np.zeros(1, image.HEADER)
+    h["magic"], h["version"], h["layers"] = image.MAGIC, 1, cfg.num_hidden_layers
+    h["position"], h["mtp_position"], h["has_mtp"] = pos, mpos, int(cfg.mtp_num_hidden_layers > 0)
+    for k, v in sh.items():
+        h[k] = v
+    n = (image.image_bytes(cfg, pos, mpos) - image.HEADER.itemsize) // 4
+    body = rng.standard_normal(n).astype(np.float32)
+    return h.tobytes() + body.tobytes(), body
+
+
+@pytest.mark.parametrize("make", [synth.tiny, synth.mini_35b, synth.qwen36_35b])
+def test_image_round_trips_through_the_parser(make):
+    cfg = make()
+    rng = np.random.default_rng(0)
+    buf, body = _build(cfg, 7, 5 if cfg.mtp_num_hidden_layers else 0, rng)
+    out = image.parse(buf, cfg)
+    assert out["position"] == 7
+    flat = []
+    for lay in out["layers"]:
+        flat += [v.ravel() for v in lay.values()]
+    if "mtp" in out:
+        flat += [out["mtp"]["keys"], out["mtp"]["values"]]
+    assert np.array_equal(np.concatenate(flat), body)
+
+
+def test_image_rejects_truncation_and_foreign_shapes():
+    cfg = synth.mini_35b()
+    buf, _ = _build(cfg, 3, 2, np.random.default_rng(1))
+    with pytest.raises(ValueError):
+        image.parse(buf[:-4], cfg)
+    with pytest.raises(ValueError):
+        image.parse(b"NOTANIMG" + buf[8:], cfg)
+    with pytest.raises(ValueError):
+        image.parse(buf, synth.tiny())
