@@ -353,8 +353,9 @@ def main():
     prof_total = sum(v[1] for v in prof.values()) / 3
     traffic = None
     tpath = ROOT / "profiles" / "traffic.json"
-    if tpath.exists():
-        traffic = json.loads(tpath.read_text()).get("qmv_lm_head_bytes_per_launch")
+    if tpath.exists():  # ncu DRAM bytes / algorithmic bytes of the GEMV launches, times this pass's bytes
+        ratio = json.loads(tpath.read_text()).get("qmv_traffic_over_algorithmic")
+        traffic = ratio * gemv_bytes(cfg, union, K_ROWS) if ratio else None
     cpu = None
     if not args.no_cpu_baseline:
         try:
@@ -380,6 +381,7 @@ def main():
                                      "scope": "whole verify pass: algorithmic bytes / device-timed pass"}},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak if achieved else None, "traffic": traffic, "peak_kind": peak_kind,
+                     "traffic_scope": "DRAM bytes of the pass's GEMV launches (ncu ratio x weight bytes)",
                      "kernel": "qmv_kernel", "scope": "weight bytes of the pass's GEMV launches / their "
                      "event-timed durations (per-stage run, PDL off)",
                      "gemv_bytes_per_pass": g_bytes, "gemv_us_per_pass": qmv_us,
