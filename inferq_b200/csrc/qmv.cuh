@@ -58,7 +58,7 @@ __host__ __device__ inline int qmv_units(int dt, int cols) {
 // split less, so each warp streams several blocks.
 inline int qmv_ksplit(int dt, int64_t rows, int64_t cols, bool expert = false) {
   int units = qmv_units(dt, (int)cols);
-  const int64_t target = expert ? 64 : 148 * 32;
+  const int64_t target = expert ? 32 : 148 * 32;
   int ks = 1;
   while (ks < 8 && units % (ks * 2) == 0 && (rows / 16) * ks < target) ks *= 2;
   return ks;

@@ -119,7 +119,7 @@ void or_set_gemv_order(int order) { g_order = order; }
 static int device_ksplit(int dt, int64_t rows, int64_t cols, int expert) {
     if (dt == OR_F32) return 1;
     int units = (int)(dt == OR_Q8_0 ? cols / 128 : cols / 256);
-    int64_t target = expert ? 64 : 148 * 32;
+    int64_t target = expert ? 32 : 148 * 32;
     int ks = 1;
     while (ks < 8 && units % (ks * 2) == 0 && (rows / 16) * ks < target) ks *= 2;
     return ks;
