@@ -91,6 +91,8 @@ __global__ void __launch_bounds__(256) attn_scan_kernel(AttnArgs a) {
   float* Qs = Vs + 32 * HD;             // [rows * G][HD]: this KV head's query rows
   const int kvh = blockIdx.x, c = blockIdx.y;
   const int G = a.nh / a.nkv;
+  // blockIdx.z picks this CTA's share of the KV head's query heads
+  const int gpc = G / gridDim.z, g0 = blockIdx.z * gpc;
   const int pos0 = *a.pos;
   const int last = pos0 + a.rows - 1;   // last position any row attends to
   const int p0 = c * kAttnChunk;
@@ -106,11 +108,11 @@ __global__ void __launch_bounds__(256) attn_scan_kernel(AttnArgs a) {
     kr[0] = kv.x; kr[1] = kv.y; kr[2] = kv.z; kr[3] = kv.w;
     *reinterpret_cast<float4*>(Vs + p * HD + 4 * d4) = vv;
   }
-  const int nq = a.rows * G;
+  const int nq = a.rows * gpc;  // (row, query head) items of this CTA
 #pragma unroll 4
   for (int i = threadIdx.x; i < nq * HD / 4; i += 256) {
     const int q = i / (HD / 4), d4 = i % (HD / 4);
-    const int t = q / G, h = kvh * G + q % G;
+    const int t = q / gpc, h = kvh * G + g0 + q % gpc;
     *reinterpret_cast<float4*>(Qs + q * HD + 4 * d4) =
         *reinterpret_cast<const float4*>(a.qbuf + ((int64_t)t * a.nh + h) * HD + 4 * d4);
   }
@@ -118,7 +120,7 @@ __global__ void __launch_bounds__(256) attn_scan_kernel(AttnArgs a) {
   const float scale = __fdiv_rn(1.f, sqrtf((float)HD));
   const int nchunks_total = (last + kAttnChunk) / kAttnChunk;
   for (int q = warp; q < nq; q += 8) {
-    const int t = q / G, g = q % G, h = kvh * G + g;
+    const int t = q / gpc, h = kvh * G + g0 + q % gpc;
     const int attend_last = pos0 + t;
     if (p0 > attend_last) continue;  // this chunk is entirely in row t's future
     const float* qs = Qs + q * HD;
@@ -200,8 +202,11 @@ cudaError_t attn_prep_launch(const AttnArgs& a, cudaStream_t st, bool pdl) {
 }
 
 cudaError_t attn_scan_launch(const AttnArgs& a, cudaStream_t st, bool pdl) {
-  dim3 grid(a.nkv, a.chunk_ctas);
-  const size_t smem = (size_t)(32 * (a.hd + 1) + 32 * a.hd + a.rows * (a.nh / a.nkv) * a.hd) * sizeof(float);
+  const int G = a.nh / a.nkv;
+  int split = 1;  // query-head groups per KV head: at least ~2 CTAs per SM's worth of work
+  while (split * 2 <= G && G % (split * 2) == 0 && a.nkv * a.chunk_ctas * split < 2 * 148) split *= 2;
+  dim3 grid(a.nkv, a.chunk_ctas, split);
+  const size_t smem = (size_t)(32 * (a.hd + 1) + 32 * a.hd + a.rows * (G / split) * a.hd) * sizeof(float);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   switch (a.hd / 32) {
     case 2: return launch_scan<2>(grid, smem, st, pdl, a);
