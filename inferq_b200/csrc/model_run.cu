@@ -666,6 +666,8 @@ int run_pass(iq_state* s, int k, bool verify) {
   IQ_CUDA(commit_launch(x.cur(), x.pos(), x.result(), x.st, x.pdl));
   x.mark("head.commit");
   IQ_CUDA(cudaMemcpyAsync(s->h_result, x.result(), 4 * sizeof(int), cudaMemcpyDeviceToHost, x.st));
+  // the GEMVs' bounded-wait status travels back with the result
+  if (int* f = qmv_timeout_flag()) IQ_CUDA(cudaMemcpyAsync(s->h_result + 4, f, sizeof(int), cudaMemcpyDeviceToHost, x.st));
   return IQ_OK;
 }
 
@@ -860,7 +862,8 @@ int alloc_state(iq_state* s) {
   const int64_t E = c.num_experts, topk = c.num_experts_per_tok;
   const int64_t F = c.moe_intermediate_size, Fs = c.shared_expert_intermediate_size;
   IQ_CUDA(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
-  IQ_CUDA(cudaMallocHost(&s->h_result, 4 * sizeof(int)));
+  IQ_CUDA(cudaMallocHost(&s->h_result, 8 * sizeof(int)));
+  memset(s->h_result, 0, 8 * sizeof(int));
   IQ_CUDA(cudaMallocHost(&s->h_tokens, kMaxK * sizeof(int32_t)));
   IQ_CUDA(s->ctrl.reserve(8 * sizeof(int)));
   IQ_CUDA(cudaMemset(s->ctrl.p, 0, 8 * sizeof(int)));
@@ -945,6 +948,16 @@ int alloc_state(iq_state* s) {
     IQ_CUDA(cudaMallocHost(&s->h_mtp, (size_t)(K * H + 3 * kMaxDraft) * 4));
   }
   return build_plans(s);
+}
+
+// After a synchronized pass: a GEMV that gave up waiting for its weights
+// (bounded wait) fails the call with IQ_ETIMEDOUT; the flag is cleared.
+int check_device_waits(iq_state* s) {
+  if (!s->h_result[4]) return IQ_OK;
+  s->h_result[4] = 0;
+  if (int* f = qmv_timeout_flag()) IQ_CUDA(cudaMemset(f, 0, sizeof(int)));
+  set_error("a GEMV gave up waiting for its weight tiles (bounded device wait); results of this pass are invalid");
+  return IQ_ETIMEDOUT;
 }
 
 int reset_state(iq_state* s) {
@@ -1175,6 +1188,7 @@ int iq_forward(iq_state* s, const uint32_t* tokens, int rows, float* logits, flo
   }
   IQ_CUDA(cudaStreamSynchronize(s->st));
   if (s->profiling) collect_marks(s);
+  TRY(check_device_waits(s));
   s->can_rollback = true;
   return IQ_OK;
 }
@@ -1196,6 +1210,7 @@ int iq_verify(iq_state* s, const uint32_t* tokens, int rows, iq_verify_result* o
   if (rc) return rc;
   IQ_CUDA(cudaStreamSynchronize(s->st));
   if (s->profiling) collect_marks(s);
+  TRY(check_device_waits(s));
   out->accepted = s->h_result[0];
   out->authoritative = s->h_result[1];
   out->committed = s->h_result[2];

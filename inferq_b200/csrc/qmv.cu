@@ -10,6 +10,7 @@
 // unit `depth` ahead and computes.  Activations are staged into shared memory
 // once per change of input rows, not once per tile.
 #include <algorithm>
+#include <cstdlib>
 #include <climits>
 #include <cstring>
 #include <cudaTypedefs.h>
@@ -125,9 +126,9 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 // Bounded wait for the phase of the given parity; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int limit = 1 << 20) {
   const uint32_t a = smem_u32(bar);
-  for (int i = 0; i < (1 << 20); i++) {
+  for (int i = 0; i < limit; i++) {
     uint32_t ok;
     asm volatile(
         "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
@@ -410,7 +411,7 @@ __device__ __forceinline__ void issue_unit(const StreamPos& p, uint8_t* slot, ui
 // [kQmvWarps x depth slots of kSlotBytes].
 __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs, int njobs,
                                                              const int* __restrict__ dyn_count, int total_hint,
-                                                             int act_bytes, int depth) {
+                                                             int act_bytes, int depth, int test_skip) {
   __shared__ float part[kQmvWarps][32][4];
   // the job table in shared memory when it is small (one parallel copy, no
   // dependent global reads later); otherwise just the jobs' tile offsets
@@ -467,8 +468,14 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
   pp.t = warp_tile(jobs, t0, njobs, total, pp.tile, warp);
   pp.b = pp.t.u0;
   stream_settle(jobs, t0, njobs, total, warp, pp);
+  // test_skip (tests only): CTA 0's warp 0 never requests its first unit, so
+  // its first slot wait must run out and take the timeout path below
+  const bool skip_first = test_skip && blockIdx.x == 0 && warp == 0;
+  const int wait_limit = test_skip ? 256 : 1 << 20;
+  uint32_t issued = 0;
   for (int i = 0; i < depth && pp.tile < total; i++) {
-    if (lane == 0) issue_unit(pp, ring + i * kSlotBytes, &wbars[i], pol);
+    if (lane == 0 && !(skip_first && i == 0)) issue_unit(pp, ring + i * kSlotBytes, &wbars[i], pol);
+    issued++;
     pp.b++;
     stream_settle(jobs, t0, njobs, total, warp, pp);
   }
@@ -511,9 +518,11 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
       for (int b = ct.u0; b < ct.u1; b++, n++) {
         const uint32_t si = n % depth;
         uint8_t* slot = ring + si * kSlotBytes;
-        if (!mbar_wait(&wbars[si], (n / depth) & 1)) {
+        if (!mbar_wait(&wbars[si], (n / depth) & 1, wait_limit)) {
           if (lane == 0) atomicExch(&g_qmv_timeout, 1);
           ok = false;
+          // let this warp's other copies land (bounded) before it stops using the ring
+          for (uint32_t j = n + 1; j < issued; j++) mbar_wait(&wbars[j % depth], (j / depth) & 1);
           break;
         }
         WRegs cur;
@@ -523,6 +532,7 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
         __syncwarp();
         if (pp.tile < total) {
           if (lane == 0) issue_unit(pp, slot, &wbars[si], pol);
+          issued++;
           pp.b++;
           stream_settle(jobs, t0, njobs, total, warp, pp);
         }
@@ -568,6 +578,18 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
 }
 
 }  // namespace
+
+int* qmv_timeout_flag() {
+  static int* ptr[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_qmv_timeout) == cudaSuccess) ptr[dev] = static_cast<int*>(p);
+  }
+  return ptr[dev];
+}
 
 int qmv_persistent_ctas() {
   static int n = 0;
@@ -665,7 +687,9 @@ cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, qmv_kernel, jobs, njobs, dyn_count, dyn_count ? 0 : ntiles, smem_bytes, depth);
+  static const int test_skip = getenv("IQ_QMV_TEST_TIMEOUT") ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, qmv_kernel, jobs, njobs, dyn_count, dyn_count ? 0 : ntiles, smem_bytes, depth,
+                            test_skip);
 }
 
 }  // namespace iq

@@ -105,6 +105,10 @@ cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int 
 // Encode the tensor maps the kernel loads a weight tensor through (device
 // layout, `rows` x `cols`) into `maps`: [0] the unit box, [1] the tail box
 // (Q6_K / Q8_0).  Jobs point at them (tmap = maps, tmap_tail = maps + 128 B).
+// Device address of the flag a GEMV sets when a bounded wait for its weight
+// slots gave up (0 = never); the caller clears it.
+int* qmv_timeout_flag();
+
 struct DevBuf;
 cudaError_t qmv_tensor_maps(int dt, const uint8_t* base, int64_t rows, int64_t cols, DevBuf& maps);
 
