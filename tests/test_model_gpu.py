@@ -180,3 +180,51 @@ def test_35b_widths_match_the_oracle(cuda):
     # last-bit differences; the oracle's two orders bound that noise.
     noise = np.abs(ref - dev).max()
     assert np.abs(lg - ref).max() <= max(TOL, 2 * noise), (np.abs(lg - ref).max(), noise)
+
+
+def _80b(layers, interval=None):
+    cfg = synth.coder_next_80b()
+    cfg.name = f"coder-next-80b-widths-{layers}-layers"
+    cfg.num_hidden_layers = layers
+    if interval:
+        cfg.full_attention_interval = interval
+    return cfg
+
+
+def test_80b_widths_match_the_oracle(cuda):
+    """Coder-Next-80B shapes (512 experts, top-10,
+    qwen3_next layouts).  Attention + MoE layers hold every row to the
+    device-order oracle and the reference order.  A DeltaNet layer holds the
+    rows after the first sharply; on row 0 the recurrent output of this seed
+    is near zero (fresh state) and the gated RMSNorm amplifies the
+    recurrence's summation order (the device sums key rows per lane then
+    across lanes, the reference sequentially), measured 0.035 on the logits,
+    so row 0 is held to 0.05 against the reference order."""
+    prompt = [11, 4097, 42]
+    for cfg, first in ((_80b(2, interval=1), 0), (_80b(1), 1)):
+        tensors = list(synth.generate(cfg, seed=3, device="cuda"))
+        model = Model(cfg, tensors)
+        om = oracle.OracleModel(cfg, tensors)
+        _, lg, hd = State(model, 64).forward(prompt, logits=True, hidden=True)
+        dev, dev_h = _oracle_logits(om, prompt, 1)
+        ref, _ = _oracle_logits(om, prompt, 0)
+        assert np.abs(hd[first:] - dev_h[first:]).max() <= 1e-4, cfg.name
+        assert np.abs(lg[first:] - dev[first:]).max() <= 1e-3, cfg.name
+        assert np.abs(lg[first:] - ref[first:]).max() <= TOL, cfg.name
+        assert np.abs(lg[:first] - ref[:first]).max() <= 0.05 if first else True, cfg.name
+        del model, om
+
+
+def test_80b_widths_verify_equals_sequential(cuda):
+    cfg = _80b(4)
+    model = Model(cfg, list(synth.generate(cfg, seed=3, device="cuda")))
+    prompt = [11, 4097, 42]
+    toks = [int(t) for t in np.random.default_rng(8).integers(0, cfg.vocab_size, 8)]
+    seq = State(model, 64)
+    seq.forward(prompt)
+    rows = [seq.forward([t], logits=True)[1][0] for t in toks]
+    vs = State(model, 64)
+    vs.forward(prompt)
+    _, vl, _ = vs.verify(toks, logits=True)
+    for i in range(8):
+        assert np.array_equal(_bits(vl[i]), _bits(rows[i])), i
