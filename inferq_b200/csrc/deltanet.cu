@@ -6,10 +6,10 @@
 // src/qwen/deltanet.rs:122-217 (S *= exp(g); pred = S^T k;
 // delta = (v - pred) * beta; S += k delta^T; o = S^T q / sqrt(dk)).
 //
-// Grid: one CTA per (value head, 32-column slice of the value dimension).
-// The delta rule is separable over value columns, so a slice's dk x 32 state
-// block lives in registers for the whole pass: warp w owns columns 4w..4w+3,
-// lane = (column, group of dk/8 key rows), and the sums over key rows are
+// Grid: one CTA per (value head, 16-column slice of the value dimension).
+// The delta rule is separable over value columns, so a slice's dk x 16 state
+// block lives in registers for the whole pass: warp w owns columns 2w, 2w+1,
+// lane = (column, group of dk/16 key rows), and the sums over key rows are
 // shuffles inside the warp.  The conv outputs of a row are shared through a
 // double-buffered shared row, so a row costs one CTA barrier.  Rows are
 // processed serially inside the CTA, so a row's result never depends on how
@@ -35,13 +35,15 @@ __device__ __forceinline__ float softplus_ref(float v) {
 
 constexpr int kMaxRowsDn = 8;
 
-template <int K>  // conv kernel width
+template <int K, int COLS>  // conv kernel width; value columns per CTA (32 or 16)
 __global__ void __launch_bounds__(256) deltanet_kernel(DeltaNetArgs a) {
   pdl_wait();
   pdl_trigger();
   const int layer = blockIdx.y;
   const DeltaNetLayer& L = a.layers[layer];
-  const int slices = a.dv / 32;
+  constexpr int CPW = COLS / 8;        // columns per warp
+  constexpr int GROUPS = 32 / CPW;     // key-row groups per column (lanes)
+  const int slices = a.dv / COLS;
   const int vh = blockIdx.x / slices;
   const int slice = blockIdx.x % slices;
   const int ratio = a.nv / a.nk;
@@ -49,9 +51,9 @@ __global__ void __launch_bounds__(256) deltanet_kernel(DeltaNetArgs a) {
   const int rep = a.tiled_heads ? vh / a.nk : vh % ratio;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int key_dim = a.nk * a.dk;
-  const int rows_i = a.dk / 8;   // key rows per lane
-  const int c4 = lane & 3, rg = lane >> 2;
-  const int j = slice * 32 + 4 * warp + c4;  // value column of this lane
+  const int rows_i = a.dk / GROUPS;  // key rows per lane
+  const int c4 = lane % CPW, rg = lane / CPW;
+  const int j = slice * COLS + CPW * warp + c4;  // value column of this lane
   const int kr0 = rg * rows_i;               // first key row of this lane
   const int cur = *a.cur;
   const int rows = a.rows;
@@ -60,11 +62,11 @@ __global__ void __launch_bounds__(256) deltanet_kernel(DeltaNetArgs a) {
   __shared__ float qkv[2][2 * 128 + 32];
   __shared__ float bg[2][2];
   const int nqk = 2 * a.dk;
-  const int nch = nqk + 32;
+  const int nch = nqk + COLS;
   auto chan = [&](int c) {
     if (c < a.dk) return kh * a.dk + c;
     if (c < nqk) return key_dim + kh * a.dk + (c - a.dk);
-    return 2 * key_dim + vh * a.dv + slice * 32 + (c - nqk);
+    return 2 * key_dim + vh * a.dv + slice * COLS + (c - nqk);
   };
   // every input of the pass, requested before any arithmetic and parked in
   // shared memory: thread t owns conv channels t and t+256; thread 0 also
@@ -154,7 +156,7 @@ __global__ void __launch_bounds__(256) deltanet_kernel(DeltaNetArgs a) {
     const float nq = __fdiv_rn(1.f, sqrtf(__fadd_rn(sq, 1e-6f)));
     const float nk = __fdiv_rn(1.f, sqrtf(__fadd_rn(sk, 1e-6f)));
     const float beta = bg[buf][0], decay = expf(bg[buf][1]);
-    const float vcol = qkv[buf][nqk + 4 * warp + c4];
+    const float vcol = qkv[buf][nqk + CPW * warp + c4];
     // recurrence over this lane's key rows, reduced across the 8 row groups
     float kv[16], pred = 0.f;
 #pragma unroll
@@ -166,7 +168,7 @@ __global__ void __launch_bounds__(256) deltanet_kernel(DeltaNetArgs a) {
       }
     }
 #pragma unroll
-    for (int m = 4; m <= 16; m <<= 1) pred = __fadd_rn(pred, __shfl_xor_sync(0xffffffffu, pred, m));
+    for (int m = CPW; m <= 16; m <<= 1) pred = __fadd_rn(pred, __shfl_xor_sync(0xffffffffu, pred, m));
     const float delta = __fmul_rn(__fsub_rn(vcol, pred), beta);
     float o = 0.f;
     float* sout = L.rec_state[snap] + (int64_t)vh * a.dk * a.dv;
@@ -179,7 +181,7 @@ __global__ void __launch_bounds__(256) deltanet_kernel(DeltaNetArgs a) {
       }
     }
 #pragma unroll
-    for (int m = 4; m <= 16; m <<= 1) o = __fadd_rn(o, __shfl_xor_sync(0xffffffffu, o, m));
+    for (int m = CPW; m <= 16; m <<= 1) o = __fadd_rn(o, __shfl_xor_sync(0xffffffffu, o, m));
     if (rg == 0) a.out[(int64_t)t * a.out_ld + vh * a.dv + j] = __fmul_rn(o, qscale);
   }
 }
@@ -242,7 +244,9 @@ cudaError_t deltanet_launch(const DeltaNetArgs& a, int nlayers, cudaStream_t st,
       a.conv_k > 4 || a.conv_k < 1)
     return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.nv * (a.dv / 32), nlayers);
+  // 16 value columns per CTA: 2 CTAs per SM at 35B shapes, 8 key rows a lane
+  const int cols = 16;
+  cfg.gridDim = dim3(a.nv * (a.dv / cols), nlayers);
   cfg.blockDim = dim3(256);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -250,11 +254,17 @@ cudaError_t deltanet_launch(const DeltaNetArgs& a, int nlayers, cudaStream_t st,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
+  if (cols == 16) switch (a.conv_k) {
+      case 1: return cudaLaunchKernelEx(&cfg, deltanet_kernel<1, 16>, a);
+      case 2: return cudaLaunchKernelEx(&cfg, deltanet_kernel<2, 16>, a);
+      case 3: return cudaLaunchKernelEx(&cfg, deltanet_kernel<3, 16>, a);
+      default: return cudaLaunchKernelEx(&cfg, deltanet_kernel<4, 16>, a);
+    }
   switch (a.conv_k) {
-    case 1: return cudaLaunchKernelEx(&cfg, deltanet_kernel<1>, a);
-    case 2: return cudaLaunchKernelEx(&cfg, deltanet_kernel<2>, a);
-    case 3: return cudaLaunchKernelEx(&cfg, deltanet_kernel<3>, a);
-    default: return cudaLaunchKernelEx(&cfg, deltanet_kernel<4>, a);
+    case 1: return cudaLaunchKernelEx(&cfg, deltanet_kernel<1, 32>, a);
+    case 2: return cudaLaunchKernelEx(&cfg, deltanet_kernel<2, 32>, a);
+    case 3: return cudaLaunchKernelEx(&cfg, deltanet_kernel<3, 32>, a);
+    default: return cudaLaunchKernelEx(&cfg, deltanet_kernel<4, 32>, a);
   }
 }
 
