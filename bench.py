@@ -186,6 +186,36 @@ def mtp_timing(state, cfg, hidden_row, seed_token, draft_vocab=32768, depth=3, r
             "sync_us_one_row": d[1] * 1e6, "timing": "host clock around the C-ABI call (synchronizing)"}
 
 
+def wide_timing(rows=8192, cols=2048, n=512, reps=10):
+    """The tensor-core wide product (prefill-shaped: n input rows through one
+    Q8_0 projection of the 35B width) timed with CUDA events: quantize +
+    product per call, and its rate against the measured dense bf16 peak."""
+    import torch
+
+    from inferq_b200 import _lib
+    from inferq_b200 import quants as Q
+    g = torch.Generator(device="cuda").manual_seed(5)
+    w = Q.encode(torch.randn(rows, cols, device="cuda", generator=g) * 0.02, Q.Q8_0)
+    m = _lib.Matrix(Q.Q8_0, w, rows, cols)
+    del w
+    x = torch.randn(n, cols, device="cuda", generator=g)
+    for _ in range(3):
+        m.forward_wide(x)
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        m.forward_wide(x)
+    e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / reps * 1e3
+    tops = 2.0 * rows * cols * n / us / 1e6
+    peaks = ROOT / "MEASURED_PEAKS.json"
+    bf16 = json.loads(peaks.read_text()).get("bf16_tflops") if peaks.exists() else 1590.0
+    return {"shape": f"Q8_0 {rows}x{cols}, {n} input rows", "us": us, "int_tops": tops,
+            "frac_of_bf16_peak": tops / bf16, "kernel": "wide_q80_kernel (tcgen05, exact block dots)"}
+
+
 def greedy_continuation(model, prompt, n):
     from inferq_b200.model import State
     s = State(model, CTX + n + 16)
@@ -335,6 +365,12 @@ def main():
     if not ep_mode:  # MTP drafting cost at this context (one GPU), after everything timed
         _, _, hrow = state.forward([out[-1]], hidden=True)
         mtp = mtp_timing(state, cfg, hrow[0], int(out[-1]))
+    wide = None
+    if rank == 0 and not ep_mode:
+        try:
+            wide = wide_timing()
+        except Exception as e:  # reported, never required
+            wide = {"failed": str(e)}
     if rank != 0:
         return
     per_seq = 1 if ep_mode else world  # sequences the job ran
@@ -377,6 +413,7 @@ def main():
                    "parallelism": f"ep{world} (experts split, NCCL sum of routed outputs per MoE layer)"
                    if ep_mode else f"replicas x{world}",
                    "mtp": mtp,
+                   "wide": wide,
                    "pass_roofline": {"achieved_gbs": pass_gbs, "frac": pass_gbs / peak,
                                      "scope": "whole verify pass: algorithmic bytes / device-timed pass"}},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

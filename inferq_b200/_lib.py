@@ -58,6 +58,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "iq_matrix_forward_rows": (I32, [P, P, I64, P]),
         "iq_matrix_forward_device": (I32, [P, P, I32, P, P]),
         "iq_matrix_forward_device_noalloc": (I32, [P, P, I32, P, P]),
+        "iq_matrix_forward_wide": (I32, [P, P, I32, P, P]),
         "iq_qgemv": (I32, [I32, P, I64, I64, P, I32, P, P]),
         "iq_qgemv_ksplit": (I32, [I32, I64, I64]),
         "iq_matrix_dequantize": (I32, [P, P, I64, P]),
@@ -116,6 +117,17 @@ class Matrix:
         x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, self.cols)
         y = np.empty((x.shape[0], self.rows), np.float32)
         check(lib().iq_matrix_forward_rows(self._h, ptr(x), x.shape[0], ptr(y)))
+        return y
+
+    def forward_wide(self, x, stream=None):
+        """Many input rows on the tensor cores (Q8_0): ``x`` a CUDA f32 tensor
+        [n, cols]; returns a CUDA f32 tensor [n, rows] (enqueued on the
+        current stream unless ``stream`` is given)."""
+        import torch
+        x = x.float().contiguous().view(-1, self.cols)
+        y = torch.empty(x.shape[0], self.rows, device=x.device, dtype=torch.float32)
+        st = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+        check(lib().iq_matrix_forward_wide(self._h, ptr(x), x.shape[0], ptr(y), st))
         return y
 
     def dequantize(self, ids=None) -> np.ndarray:

@@ -184,6 +184,20 @@ int iq_matrix_forward_device(const iq_matrix* m, const float* x, int input_rows,
   return matrix_forward_dev(m, x, input_rows, y, static_cast<cudaStream_t>(stream));
 }
 
+int iq_matrix_forward_wide(const iq_matrix* m, const float* x, int input_rows, float* y, void* stream) {
+  clear_error();
+  IQ_CHECK(m && x && y, IQ_EINVAL, "iq_matrix_forward_wide: null argument");
+  IQ_CHECK(m->dtype == Q8_0, IQ_EUNSUPPORTED, "the wide product takes Q8_0 matrices, got dtype %d", m->dtype);
+  IQ_CHECK(m->cols % 128 == 0, IQ_EINVAL, "the wide product needs cols %% 128 == 0, got %lld", (long long)m->cols);
+  IQ_CHECK(input_rows >= 1, IQ_EINVAL, "expected at least one input row, got %d", input_rows);
+  const int64_t nb = m->cols / 32;
+  IQ_CUDA(g_scratch.x.reserve((size_t)(input_rows * m->cols * 2)));
+  IQ_CUDA(g_scratch.act.reserve((size_t)(nb * wide_ldd(input_rows) * 4)));
+  IQ_CUDA(wide_q80_forward(m->base, m->rows, m->cols, m->row_bytes, x, (int)m->cols, input_rows, y, (int)m->rows,
+                           g_scratch.x.as<__half>(), g_scratch.act.as<float>(), static_cast<cudaStream_t>(stream)));
+  return IQ_OK;
+}
+
 int iq_matrix_forward_rows(const iq_matrix* m, const float* x, int64_t input_rows, float* y) {
   clear_error();
   IQ_CHECK(m && x && y, IQ_EINVAL, "iq_matrix_forward_rows: null argument");

@@ -1,0 +1,97 @@
+"""The wide Q8_0 product on the tensor cores (iq_matrix_forward_wide) against
+the CPU oracle.
+
+The reference computes prefill through the same QuantizedMatrix::forward as
+decode (src/runtime.rs:748-771, src/gguf.rs:406-456), so the wide product has
+to give the integer block dots of src/qgemm.rs:369-397 (Q8_0 x Q8_0).  Its f32
+order is one FMA per block in ascending block order: bitwise the oracle's
+device order with one K chunk (oracle/iq_oracle_dot.c dev_block_chunks).
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from inferq_b200 import _lib
+from inferq_b200 import quants as Q
+
+pytestmark = pytest.mark.gpu
+
+
+def _weights(rows, cols, seed):
+    g = torch.Generator().manual_seed(seed)
+    return Q.encode(torch.randn(rows, cols, generator=g) * 0.02, Q.Q8_0).numpy()
+
+
+def _inputs(n, cols, seed):
+    x = np.random.default_rng(seed).standard_normal((n, cols)).astype(np.float32)
+    x[0] *= 30.0
+    if n > 2:
+        x[2] = 0.0          # an all-zero row (block scale 0)
+        x[1, :64] = 1e-30   # tiny blocks
+    return x
+
+
+@pytest.mark.parametrize("rows,cols,n", [
+    (128, 128, 1), (200, 1024, 37), (128, 512, 128), (300, 256, 129), (1000, 2048, 300),
+])
+def test_wide_matches_the_oracle_bitwise(cuda, rows, cols, n):
+    w = _weights(rows, cols, rows + n)
+    x = _inputs(n, cols, n)
+    m = _lib.Matrix(Q.Q8_0, w, rows, cols)
+    got = m.forward_wide(torch.from_numpy(x).cuda()).cpu().numpy()
+    ref = oracle.qmatvec(Q.Q8_0, w, rows, cols, x, order=1, ksplit=1)
+    bad = np.argwhere(got.view(np.uint32) != ref.view(np.uint32))
+    assert len(bad) == 0, (len(bad), bad[:5], np.abs(got - ref).max())
+
+
+def test_wide_equals_the_narrow_path_where_it_runs_unsplit(cuda):
+    rows, cols = 16384, 128
+    assert _lib.ksplit(Q.Q8_0, rows, cols) == 1
+    w = _weights(rows, cols, 7)
+    x = _inputs(24, cols, 3)
+    m = _lib.Matrix(Q.Q8_0, w, rows, cols)
+    wide = m.forward_wide(torch.from_numpy(x).cuda()).cpu().numpy()
+    narrow = m.forward_rows(x)
+    assert np.array_equal(wide.view(np.uint32), narrow.view(np.uint32))
+    # and at a split shape, equal to the oracle's one-chunk order instead
+    rows, cols = 512, 2048
+    assert _lib.ksplit(Q.Q8_0, rows, cols) > 1
+    w = _weights(rows, cols, 8)
+    m = _lib.Matrix(Q.Q8_0, w, rows, cols)
+    wide = m.forward_wide(torch.from_numpy(x[:5]).cuda().repeat(1, 16)).cpu().numpy()
+    ref = oracle.qmatvec(Q.Q8_0, w, rows, cols, np.tile(x[:5], (1, 16)), order=1, ksplit=1)
+    assert np.array_equal(wide.view(np.uint32), ref.view(np.uint32))
+
+
+def test_wide_rows_do_not_depend_on_their_neighbours_at_full_width(cuda):
+    """512 input rows at a 35B projection shape: each output row equals the
+    same input row run alone (size-independent property), and the result is
+    within f32 rounding of a float64 product of the decoded operands."""
+    rows, cols, n = 8192, 2048, 512
+    g = torch.Generator(device="cuda").manual_seed(11)
+    w = Q.encode(torch.randn(rows, cols, device="cuda", generator=g) * 0.02, Q.Q8_0)
+    m = _lib.Matrix(Q.Q8_0, w, rows, cols)
+    x = torch.randn(n, cols, device="cuda", generator=g)
+    y = m.forward_wide(x)
+    for i in (0, 1, 127, 128, 300, 511):
+        yi = m.forward_wide(x[i:i + 1])
+        assert torch.equal(yi[0].view(torch.int32), y[i].view(torch.int32)), i
+    # float64 reference over the quantized operands, sampled rows
+    ids = torch.tensor([0, 1, 2, 4095, 8191])
+    wd = torch.from_numpy(m.dequantize(ids.numpy().astype(np.int32))).double()
+    xq = torch.from_numpy(oracle.dequant(Q.Q8_0, oracle.quant_q80(x.cpu().numpy()), n, cols)).double()
+    ref = xq @ wd.T
+    err = (y[:, ids].cpu().double() - ref).abs().max().item()
+    assert err <= 1e-4 * ref.abs().max().item(), err
+
+
+def test_wide_rejects_what_it_does_not_support(cuda):
+    w = Q.encode(torch.randn(64, 256) * 0.02, Q.Q4_K).numpy()
+    m = _lib.Matrix(Q.Q4_K, w, 64, 256)
+    with pytest.raises(_lib.IqError):
+        m.forward_wide(torch.zeros(4, 256, device="cuda"))
+    w8 = _weights(64, 128, 1)
+    m8 = _lib.Matrix(Q.Q8_0, w8, 64, 128)
+    with pytest.raises(_lib.IqError):  # no input rows
+        m8.forward_wide(torch.zeros(0, 128, device="cuda"))
