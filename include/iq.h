@@ -99,6 +99,14 @@ int iq_matrix_forward_device_noalloc(const iq_matrix* m, const float* x, int inp
  * Scratch (2 B per input element) is held per thread between calls. */
 int iq_matrix_forward_wide(const iq_matrix* m, const float* x, int input_rows, float* y, void* stream);
 
+/* Synchronize `stream` and report whether any matrix product on this
+ * device gave up a bounded device wait since the last check (IQ_ETIMEDOUT;
+ * the results of that call are invalid), clearing the record.  The record
+ * is per device and shared with the model passes' GEMVs, which report their
+ * own timeouts from iq_forward / iq_verify.  No counterpart in the
+ * reference (its CPU kernels have no device waits). */
+int iq_matrix_status(void* stream);
+
 /* One-shot form over GGUF bytes in host memory (uploads, multiplies,
  * frees): int iq_qgemv of the boundary table, mirroring forward_rows. */
 int iq_qgemv(int dtype, const void* w, int64_t rows, int64_t cols, const float* x, int k, float* y,

@@ -59,6 +59,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "iq_matrix_forward_device": (I32, [P, P, I32, P, P]),
         "iq_matrix_forward_device_noalloc": (I32, [P, P, I32, P, P]),
         "iq_matrix_forward_wide": (I32, [P, P, I32, P, P]),
+        "iq_matrix_status": (I32, [P]),
         "iq_qgemv": (I32, [I32, P, I64, I64, P, I32, P, P]),
         "iq_qgemv_ksplit": (I32, [I32, I64, I64]),
         "iq_matrix_dequantize": (I32, [P, P, I64, P]),
@@ -145,6 +146,12 @@ class Matrix:
         if h is not None and _lib is not None:
             _lib.iq_matrix_destroy(h)
             self._h = None
+
+
+def status(stream=None) -> None:
+    """Synchronize ``stream`` and raise IqError(IQ_ETIMEDOUT) if a matrix
+    product on this device gave up a bounded wait since the last check."""
+    check(lib().iq_matrix_status(stream))
 
 
 def ksplit(dtype: int, rows: int, cols: int) -> int:

@@ -198,6 +198,24 @@ int iq_matrix_forward_wide(const iq_matrix* m, const float* x, int input_rows, f
   return IQ_OK;
 }
 
+int iq_matrix_status(void* stream) {
+  clear_error();
+  IQ_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  bool hit = false;
+  for (int* f : {qmv_timeout_flag(), wide_timeout_flag()}) {
+    if (!f) continue;
+    int v = 0;
+    IQ_CUDA(cudaMemcpy(&v, f, sizeof v, cudaMemcpyDeviceToHost));
+    if (v) {
+      hit = true;
+      IQ_CUDA(cudaMemset(f, 0, sizeof v));
+    }
+  }
+  IQ_CHECK(!hit, IQ_ETIMEDOUT,
+           "a matrix product gave up a bounded device wait since the last check; its results are invalid");
+  return IQ_OK;
+}
+
 int iq_matrix_forward_rows(const iq_matrix* m, const float* x, int64_t input_rows, float* y) {
   clear_error();
   IQ_CHECK(m && x && y, IQ_EINVAL, "iq_matrix_forward_rows: null argument");

@@ -33,10 +33,12 @@
 // (one lane).  The two issuers sit in different warps: a lane suspended in
 // an mbarrier wait holds its whole warp, so issuers that wait on each
 // other's progress must not share one.  Every wait is bounded; a wait that
-// runs out sets the shared timeout flag and the CTA winds down (copies and
-// MMAs drained, TMEM freed) without storing.
+// runs out sets the wide product's timeout flag (reported by
+// iq_matrix_status) and the CTA winds down (copies and MMAs drained, TMEM
+// freed) without storing.
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
+#include <cstdlib>
 #include <cstring>
 #include "iq_common.cuh"
 #include "kernels.cuh"
@@ -64,6 +66,8 @@ static_assert(kStageBytes % 1024 == 0, "swizzled atoms stay 1024-byte aligned");
 // f32 D, f16 A and B, both K-major, N = 128, M = 128.
 constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kToks >> 3) << 17) | ((uint32_t)(kRows >> 4) << 24);
 
+__device__ int g_wide_timeout;  // set when a bounded wait gave up
+
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void bar_init(uint64_t* b, uint32_t n) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n) : "memory");
@@ -74,9 +78,9 @@ __device__ __forceinline__ void bar_arrive(uint64_t* b) {
 __device__ __forceinline__ void bar_expect(uint64_t* b, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity) {
+__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, int limit = kWaitLimit) {
   const uint32_t a = su32(b);
-  for (int i = 0; i < kWaitLimit; i++) {
+  for (int i = 0; i < limit; i++) {
     uint32_t ok;
     asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
                  : "=r"(ok)
@@ -156,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     wide_q80_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                     const __grid_constant__ CUtensorMap tm_d, const __grid_constant__ CUtensorMap tm_s,
                     int scale_x0, int rows, int nb, int ntok, float* __restrict__ y, int out_ld,
-                    int* timeout_flag) {
+                    int* timeout_flag, int test_skip) {
   __shared__ __align__(8) uint64_t full_op[kStages], full_cvt[kStages], empty_op[kStages];
   __shared__ __align__(8) uint64_t full_side[kSide], empty_side[kSide];
   __shared__ __align__(8) uint64_t tfull[4], tempty[4], drained;
@@ -199,6 +203,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_after();
   const uint32_t tmem = tmem_base_s;
   volatile int* abort_v = &abort_s;
+  // test_skip (tests only): the MMA thread skips the first stage, so the
+  // epilogue's first TMEM wait runs out and the CTA takes the wind-down path
+  const int lim = test_skip ? 256 : kWaitLimit;
   auto give_up = [&]() {
     atomicExch(timeout_flag, 1);
     *abort_v = 1;
@@ -211,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int s = it % kStages;
       uint8_t* st = smem + s * kStageBytes;
       // the four converter warps decide together (they share a named barrier)
-      const uint32_t bad = (*abort_v || !bar_wait(&full_op[s], (it / kStages) & 1)) ? 1u : 0u;
+      const uint32_t bad = (*abort_v || !bar_wait(&full_op[s], (it / kStages) & 1, lim)) ? 1u : 0u;
       uint32_t any_bad;
       asm volatile(
           "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.or.pred q, 1, %2, p; selp.u32 %0, 1, 0, q; }"
@@ -252,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int e = it % kSide;
       const uint8_t* sd = side + e * kSideBytes;
       // warp-uniform outcomes: the TMEM loads below are warp-collective
-      if (!__all_sync(0xffffffffu, bar_wait(&full_side[e], (it / kSide) & 1))) {
+      if (!__all_sync(0xffffffffu, bar_wait(&full_side[e], (it / kSide) & 1, lim))) {
         give_up();
         ok = false;
         break;
@@ -261,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const __half* ws = reinterpret_cast<const __half*>(sd + kOffS + r * 16 + 8 * (it & 1));
 #pragma unroll 1
       for (int j = 0; j < 4; j++) {
-        if (!__all_sync(0xffffffffu, bar_wait(&tfull[j], it & 1))) { give_up(); ok = false; break; }
+        if (!__all_sync(0xffffffffu, bar_wait(&tfull[j], it & 1, lim))) { give_up(); ok = false; break; }
         tc_after();
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(j * 128 + cb), v);
@@ -295,13 +302,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     int issued = 0;
     for (int it = 0; it < nst && !*abort_v; it++) {
       const int s = it % kStages, e = it % kSide;
-      if (it >= kStages && !bar_wait(&empty_op[s], ((it / kStages) + 1) & 1)) { give_up(); break; }
+      if (it >= kStages && !bar_wait(&empty_op[s], ((it / kStages) + 1) & 1, lim)) { give_up(); break; }
       uint8_t* st = smem + s * kStageBytes;
       bar_expect(&full_op[s], kOpTmaBytes);
       tma2d(st + kOffRaw, &tm_w, it * 128, row0, &full_op[s]);
       tma2d(st + kOffB, &tm_x, it * kStageK, tok0, &full_op[s]);
       tma2d(st + kOffB + kAtom, &tm_x, it * kStageK + 64, tok0, &full_op[s]);
-      if (it >= kSide && !bar_wait(&empty_side[e], ((it / kSide) + 1) & 1)) {
+      if (it >= kSide && !bar_wait(&empty_side[e], ((it / kSide) + 1) & 1, lim)) {
         issued = it + 1;
         give_up();
         break;
@@ -314,23 +321,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (*abort_v) {  // let the copies in flight land before the CTA exits
       for (int it = issued > kStages ? issued - kStages : 0; it < issued; it++)
-        bar_wait(&full_op[it % kStages], (it / kStages) & 1);
+        bar_wait(&full_op[it % kStages], (it / kStages) & 1, lim);
       for (int it = issued > kSide ? issued - kSide : 0; it < issued; it++)
-        bar_wait(&full_side[it % kSide], (it / kSide) & 1);
+        bar_wait(&full_side[it % kSide], (it / kSide) & 1, lim);
     }
   } else if (warp == kMmaWarp && lane == 0) {
     // ------------------------------------------------------- MMA issuer
     for (int it = 0; it < nst && !*abort_v; it++) {
       const int s = it % kStages;
-      if (!bar_wait(&full_op[s], (it / kStages) & 1) || !bar_wait(&full_cvt[s], (it / kStages) & 1)) {
+      if (!bar_wait(&full_op[s], (it / kStages) & 1, lim) || !bar_wait(&full_cvt[s], (it / kStages) & 1, lim)) {
         give_up();
         break;
       }
+      if (test_skip && it == 0) continue;
       tc_after();
       const uint32_t a0 = su32(smem + s * kStageBytes + kOffA), b0 = su32(smem + s * kStageBytes + kOffB);
       bool ok = true;
       for (int j = 0; j < 4; j++) {
-        if (it > 0 && !bar_wait(&tempty[j], (it - 1) & 1)) { give_up(); ok = false; break; }
+        if (it > 0 && !bar_wait(&tempty[j], (it - 1) & 1, lim)) { give_up(); ok = false; break; }
         tc_after();
         const uint32_t off = (uint32_t)((j >> 1) * kAtom + (j & 1) * 64);
 #pragma unroll
@@ -343,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(&empty_op[s]);
     }
     mma_commit(&drained);  // every MMA issued above has completed when this fires
-    bar_wait(&drained, 0);
+    bar_wait(&drained, 0, lim);
   }
   __syncwarp();
   tc_before();
@@ -401,6 +409,18 @@ bool encode2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t
 
 int wide_ldd(int ntok) { return (ntok + 3) & ~3; }
 
+int* wide_timeout_flag() {
+  static int* ptr[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_wide_timeout) == cudaSuccess) ptr[dev] = static_cast<int*>(p);
+  }
+  return ptr[dev];
+}
+
 cudaError_t wide_q80_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
                              int ldx, int ntok, float* y, int out_ld, __half* qx, float* dT, cudaStream_t st) {
   if (cols % kStageK || ntok < 1 || ntok > 65535 || rows < 1 || rows > INT32_MAX || ((uintptr_t)w & 15) || ((uintptr_t)qx & 15) ||
@@ -427,8 +447,11 @@ cudaError_t wide_q80_forward(const uint8_t* w, int64_t rows, int64_t cols, int64
     attr = true;
   }
   const dim3 grid((unsigned)((ntok + kToks - 1) / kToks), (unsigned)((rows + kRows - 1) / kRows));
-  wide_q80_kernel<<<grid, kThreads, kSmemBytes, st>>>(mw, mx, md, ms, nb * 32, (int)rows, nb, ntok, y, out_ld,
-                                                      qmv_timeout_flag());
+  int* flag = wide_timeout_flag();
+  if (!flag) return cudaErrorInvalidDevice;
+  static const int test_skip = getenv("IQ_WIDE_TEST_TIMEOUT") ? 1 : 0;
+  wide_q80_kernel<<<grid, kThreads, kSmemBytes, st>>>(mw, mx, md, ms, nb * 32, (int)rows, nb, ntok, y, out_ld, flag,
+                                                      test_skip);
   return cudaGetLastError();
 }
 

@@ -37,3 +37,35 @@ def test_gemv_wait_timeout_reaches_the_host(cuda):
     line = [l for l in r.stdout.splitlines() if l.startswith(("ERROR", "NO-ERROR"))][-1]
     assert line.startswith("ERROR -6"), line
     assert "gave up" in line
+
+
+WIDE_CHILD = r"""
+import numpy as np
+import torch
+from inferq_b200 import _lib
+from inferq_b200 import quants as Q
+w = Q.encode(torch.randn(256, 512) * 0.02, Q.Q8_0).numpy()
+m = _lib.Matrix(Q.Q8_0, w, 256, 512)
+m.forward_wide(torch.randn(64, 512, device="cuda"))
+try:
+    _lib.status()
+    print("NO-ERROR")
+except _lib.IqError as e:
+    print("ERROR", e.code, e)
+_lib.status()  # the record was cleared by the first check
+print("CLEARED")
+"""
+
+
+def test_wide_product_wait_timeout_reaches_the_host(cuda):
+    """IQ_WIDE_TEST_TIMEOUT: the MMA thread skips the first stage, the
+    epilogue's first TMEM-buffer wait runs out, every role winds down (TMA
+    copies and MMAs drained, TMEM freed) and iq_matrix_status reports
+    IQ_ETIMEDOUT; the context stays usable."""
+    env = dict(os.environ, IQ_WIDE_TEST_TIMEOUT="1")
+    r = subprocess.run([sys.executable, "-c", WIDE_CHILD], env=env, capture_output=True, text=True, timeout=300,
+                       cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [l for l in r.stdout.splitlines() if l.startswith(("ERROR", "NO-ERROR", "CLEARED"))]
+    assert lines[0].startswith("ERROR -6") and "gave up" in lines[0], lines
+    assert lines[-1] == "CLEARED"
