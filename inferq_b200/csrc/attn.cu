@@ -187,11 +187,9 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a) {
 
 template <int D>
 cudaError_t launch_scan(dim3 grid, size_t smem, cudaStream_t st, bool pdl, const AttnArgs& a) {
-  static bool configured = false;
-  if (!configured) {
+  static bool configured[64] = {};
+  if (first_on_device(configured))
     cudaFuncSetAttribute(attn_scan_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    configured = true;
-  }
   return launch_pdl(attn_scan_kernel<D>, grid, dim3(256), smem, st, pdl, a);
 }
 

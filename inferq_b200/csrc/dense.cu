@@ -83,11 +83,9 @@ __global__ void __launch_bounds__(256) f32_matvec_kernel(const float* __restrict
 cudaError_t f32_matvec(const float* w, int rows, int cols, const float* x, int ldx, int k, float* y, int ldy,
                        cudaStream_t st, bool pdl, const float* norm_w, float eps) {
   if (cols % 4 || cols > 4096 || k < 1 || k > 8) return cudaErrorInvalidValue;
-  static bool configured = false;
-  if (!configured) {
+  static bool configured[64] = {};
+  if (first_on_device(configured))
     cudaFuncSetAttribute(f32_matvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 4096 * 4);
-    configured = true;
-  }
   cudaLaunchConfig_t cfg = {};
   cfg.dynamicSmemBytes = (size_t)k * cols * sizeof(float);
   cfg.gridDim = dim3((unsigned)ceil_div(rows, 8));

@@ -63,6 +63,17 @@ __device__ __forceinline__ uint4 ld_stream(const void* p) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
   return v;
 }
+// True the first time it is called for the current device with this flag
+// set (one flag per device): for per-device one-time setup such as a
+// kernel's shared-memory opt-in attribute.
+inline bool first_on_device(bool (&done)[64]) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  if (done[dev]) return false;
+  done[dev] = true;
+  return true;
+}
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 

@@ -592,27 +592,33 @@ int* qmv_timeout_flag() {
 }
 
 int qmv_persistent_ctas() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
+  static int n[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!n[dev]) {
+    int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    n = sms * 2;
+    n[dev] = sms * 2;
   }
-  return n;
+  return n[dev];
 }
 
 namespace {
 // Dynamic shared memory per CTA: with two CTAs resident on an SM ([0]) and
-// with one ([1]).
+// with one ([1]).  Per device: the opt-in attribute is set on each device
+// the first time a GEMV launches there.
 struct SmemLimits {
   int two = 0, one = 0;
 };
 const SmemLimits& qmv_dyn_smem_limits() {
-  static SmemLimits lim;
+  static SmemLimits lims[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  SmemLimits& lim = lims[dev];
   if (!lim.one) {
-    int dev = 0, per_sm = 0, optin = 0;
-    cudaGetDevice(&dev);
+    int per_sm = 0, optin = 0;
     cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaFuncAttributes fa = {};

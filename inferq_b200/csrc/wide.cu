@@ -440,11 +440,10 @@ cudaError_t wide_q80_forward(const uint8_t* w, int64_t rows, int64_t cols, int64
       !encode2d(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dT, (uint64_t)ntok, (uint64_t)nb, (uint64_t)ldd * 4, kToks, 4,
                 CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
-  static bool attr = false;
-  if (!attr) {
+  static bool attr[64] = {};  // the shared-memory opt-in is per device
+  if (first_on_device(attr)) {
     e = cudaFuncSetAttribute(wide_q80_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
-    attr = true;
   }
   const dim3 grid((unsigned)((ntok + kToks - 1) / kToks), (unsigned)((rows + kRows - 1) / kRows));
   int* flag = wide_timeout_flag();
