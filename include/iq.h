@@ -96,7 +96,8 @@ int iq_matrix_forward_device_noalloc(const iq_matrix* m, const float* x, int inp
  * quantized to Q8_0 as in iq_matrix_forward_device, exact integer block
  * dots, one f32 FMA per block in ascending block order -- bitwise the
  * narrow path's result whenever iq_qgemv_ksplit() is 1 for the shape.
- * Scratch (2 B per input element) is held per thread between calls. */
+ * Scratch (2 B per input element and per matrix element) is held per
+ * thread between calls. */
 int iq_matrix_forward_wide(const iq_matrix* m, const float* x, int input_rows, float* y, void* stream);
 
 /* Synchronize `stream` and report whether any matrix product on this

@@ -63,7 +63,7 @@ int upload_rows(int dtype, const void* data, int64_t rows, int64_t cols, int loc
 }
 
 struct Scratch {
-  DevBuf x, y, act, jobs;
+  DevBuf x, y, act, jobs, wide_w;
 };
 static thread_local Scratch g_scratch;
 
@@ -193,8 +193,10 @@ int iq_matrix_forward_wide(const iq_matrix* m, const float* x, int input_rows, f
   const int64_t nb = m->cols / 32;
   IQ_CUDA(g_scratch.x.reserve((size_t)(input_rows * m->cols * 2)));
   IQ_CUDA(g_scratch.act.reserve((size_t)(nb * wide_ldd(input_rows) * 4)));
+  IQ_CUDA(g_scratch.wide_w.reserve((size_t)(m->rows * m->cols * 2)));
   IQ_CUDA(wide_q80_forward(m->base, m->rows, m->cols, m->row_bytes, x, (int)m->cols, input_rows, y, (int)m->rows,
-                           g_scratch.x.as<__half>(), g_scratch.act.as<float>(), static_cast<cudaStream_t>(stream)));
+                           g_scratch.x.as<__half>(), g_scratch.act.as<float>(), g_scratch.wide_w.as<__half>(),
+                           static_cast<cudaStream_t>(stream)));
   return IQ_OK;
 }
 

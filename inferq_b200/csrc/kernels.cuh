@@ -33,11 +33,12 @@ cudaError_t f32_matvec(const float* w, int rows, int cols, const float* x, int l
                        int ldy, cudaStream_t st, bool pdl, const float* norm_w = nullptr, float eps = 0.f);
 
 // Wide Q8_0 product on the tensor cores (wide.cu): y[t*out_ld + r] for
-// ntok input rows x[t*ldx ..]; qx (ntok x cols f16) and dT (cols/32 x
-// wide_ldd(ntok) f32) are scratch.  cols % 128 == 0.
+// ntok input rows x[t*ldx ..]; qx (ntok x cols f16), dT (cols/32 x
+// wide_ldd(ntok) f32) and wx (rows x cols f16) are scratch.  cols % 128 == 0.
 int wide_ldd(int ntok);
 int* wide_timeout_flag();  // device flag: a wide-product wait gave up
 cudaError_t wide_q80_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
-                             int ldx, int ntok, float* y, int out_ld, __half* qx, float* dT, cudaStream_t st);
+                             int ldx, int ntok, float* y, int out_ld, __half* qx, float* dT, __half* wx,
+                             cudaStream_t st);
 
 }  // namespace iq

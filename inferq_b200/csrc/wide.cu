@@ -14,28 +14,33 @@
 // The epilogue then applies the scale product and the FMA in block order,
 // so outputs are bitwise those of the per-block device order.
 //
+// Two kernels per call besides the input quantizer: wide_expand_q80_kernel
+// writes the weights once as f16 integers (row-major, a bandwidth-bound
+// pass), and wide_q80_kernel multiplies.  Expanding inside the product
+// kernel was measured slower: its converter warps took issue slots and
+// shared-memory bandwidth from the epilogue, which paces the kernel.
+//
 // Tiles.  One CTA computes 128 weight rows x 128 input rows.  An operand
 // stage covers one group of four Q8_0 blocks (128 K elements):
-//   A  32 KB  weights as f16, K-major, 128-byte swizzle (two 64-element
-//             atoms); the raw 16 KB group lands (TMA) in its upper half and
-//             the converter warps expand it in place
-//   B  32 KB  input rows as f16 integers (TMA, 128-byte swizzle)
-// and is released as soon as the MMAs that read it complete.  The scales
-// the epilogue needs go to a deeper side ring that the epilogue releases:
-//   D   2 KB  input-row block scales [4 blocks][128 rows] f32 (TMA)
-//   S   2 KB  the weight rows' f16 scale tail, 16 B per row (TMA; the
-//             group's four scales are one half of it)
+//   A  32 KB  weights, f16, K-major, 128-byte swizzle (two 64-element atoms)
+//   B  32 KB  input rows, f16 integers, same layout
+// both by TMA, released as soon as the MMAs that read the stage complete.
+// The scales the epilogue needs go to a deeper side ring that the epilogue
+// releases:
+//   D   2 KB  input-row block scales [4 blocks][128 rows] f32
+//   S   2 KB  the weight rows' f16 scale tail, 16 B per row (the group's
+//             four scales are one half of it)
 // Three operand stages (192 KB) and six side entries (24 KB).  TMEM holds
 // four 128-column f32 buffers, one per block of a stage.
 //
-// Warp roles: 0-3 converters, 4-19 epilogue (warp w reads TMEM lanes
-// 32*(w%4).. and 32 of the 128 columns), 20 TMA loads (one lane), 21 MMAs
-// (one lane).  The two issuers sit in different warps: a lane suspended in
-// an mbarrier wait holds its whole warp, so issuers that wait on each
-// other's progress must not share one.  Every wait is bounded; a wait that
-// runs out sets the wide product's timeout flag (reported by
-// iq_matrix_status) and the CTA winds down (copies and MMAs drained, TMEM
-// freed) without storing.
+// Warp roles: 0-15 epilogue (warp w reads TMEM lanes 32*(w%4).. and 32 of the
+// 128 columns, in two 16-column halves with one load in flight while the
+// previous half is scaled), 16 TMA loads (one lane), 17 MMAs (one lane).
+// The two issuers sit in different warps: a lane suspended in an mbarrier
+// wait holds its whole warp, so issuers that wait on each other's progress
+// must not share one.  Every wait is bounded; a wait that runs out sets the
+// wide product's timeout flag (reported by iq_matrix_status) and the CTA
+// winds down (copies and MMAs drained, TMEM freed) without storing.
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 #include <cstdlib>
@@ -49,15 +54,16 @@ namespace {
 
 constexpr int kRows = 128, kToks = 128, kStageK = 128;
 constexpr int kStages = 3;
-constexpr int kConvWarps = 4, kEpiWarps = 16;
-constexpr int kCtlWarp = kConvWarps + kEpiWarps;
-constexpr int kMmaWarp = kCtlWarp + 1;
+constexpr int kEpiWarps = 16;
+constexpr int kTmaWarp = kEpiWarps, kMmaWarp = kEpiWarps + 1;
 constexpr int kThreads = (kMmaWarp + 1) * 32;
+// registers per thread: 18 warps spread 5/5/4/4 over the SM's four register
+// files of 16384, so at most 16384 / (5 * 32) -> 96
+constexpr int kBoundThreads = 640;
 constexpr int kAtom = 128 * 128;  // one 64-element f16 atom of 128 rows
-constexpr int kOffA = 0, kOffRaw = kAtom, kOffB = 2 * kAtom;
+constexpr int kOffA = 0, kOffB = 2 * kAtom;
 constexpr int kStageBytes = 4 * kAtom;
 constexpr int kSide = 6, kSideBytes = 4096, kOffS = 2048;  // D at 0, S at 2048
-constexpr int kOpTmaBytes = 3 * kAtom;                     // raw group + two B atoms
 constexpr int kSmemBytes = kStages * kStageBytes + kSide * kSideBytes + 1024;
 constexpr int kTmemCols = 512;
 constexpr int kWaitLimit = 1 << 20;
@@ -78,7 +84,7 @@ __device__ __forceinline__ void bar_arrive(uint64_t* b) {
 __device__ __forceinline__ void bar_expect(uint64_t* b, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, int limit = kWaitLimit) {
+__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, int limit) {
   const uint32_t a = su32(b);
   for (int i = 0; i < limit; i++) {
     uint32_t ok;
@@ -118,16 +124,25 @@ __device__ __forceinline__ void mma_commit(uint64_t* b) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(b))
                : "memory");
 }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+// Start a 16-column TMEM load (lanes of this warp's quarter); the registers
+// are valid only after tmem_wait16 on the same array.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+// Wait for this thread's TMEM loads; the array is an in/out operand so no
+// use of it can be scheduled before the wait.
+__device__ __forceinline__ void tmem_wait16(uint32_t (&v)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]),
+                 "+r"(v[15])
+               :
+               : "memory");
 }
 
 // (a0, a1) = fma(dw * d0, v0, a0), fma(dw * d1, v1, a1), each lane rounded
@@ -145,6 +160,16 @@ __device__ __forceinline__ void scale_fma2(float& a0, float& a1, float dw, float
       : "+f"(a0), "+f"(a1)
       : "f"(d0), "f"(d1), "f"(dw), "r"(v0), "r"(v1));
 }
+// acc[0..15] += the 16 scaled block dots v of columns d[0..15].
+__device__ __forceinline__ void scale_half(float* acc, float dw, const float* d, const uint32_t (&v)[16]) {
+  const float4* d4 = reinterpret_cast<const float4*>(d);
+#pragma unroll
+  for (int i4 = 0; i4 < 4; i4++) {
+    const float4 x = d4[i4];
+    scale_fma2(acc[4 * i4], acc[4 * i4 + 1], dw, x.x, x.y, v[4 * i4], v[4 * i4 + 1]);
+    scale_fma2(acc[4 * i4 + 2], acc[4 * i4 + 3], dw, x.z, x.w, v[4 * i4 + 2], v[4 * i4 + 3]);
+  }
+}
 
 // Four signed bytes -> four f16 (exact): 0x6400 | (q ^ 0x80) is 1024 + q + 128.
 __device__ __forceinline__ uint2 s8x4_to_f16x4(uint32_t w) {
@@ -156,12 +181,12 @@ __device__ __forceinline__ uint2 s8x4_to_f16x4(uint32_t w) {
   return make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBoundThreads, 1)
     wide_q80_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                     const __grid_constant__ CUtensorMap tm_d, const __grid_constant__ CUtensorMap tm_s,
                     int scale_x0, int rows, int nb, int ntok, float* __restrict__ y, int out_ld,
                     int* timeout_flag, int test_skip) {
-  __shared__ __align__(8) uint64_t full_op[kStages], full_cvt[kStages], empty_op[kStages];
+  __shared__ __align__(8) uint64_t full_op[kStages], empty_op[kStages];
   __shared__ __align__(8) uint64_t full_side[kSide], empty_side[kSide];
   __shared__ __align__(8) uint64_t tfull[4], tempty[4], drained;
   __shared__ uint32_t tmem_base_s;
@@ -177,7 +202,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; s++) {
       bar_init(&full_op[s], 1);
-      bar_init(&full_cvt[s], kConvWarps);
       bar_init(&empty_op[s], 1);
     }
     for (int e = 0; e < kSide; e++) {
@@ -211,82 +235,55 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_v = 1;
   };
 
-  if (warp < kConvWarps) {
-    // ------------------------------------------------------- converters
-    const int c = threadIdx.x;  // 0..127
-    for (int it = 0; it < nst; it++) {
-      const int s = it % kStages;
-      uint8_t* st = smem + s * kStageBytes;
-      // the four converter warps decide together (they share a named barrier)
-      const uint32_t bad = (*abort_v || !bar_wait(&full_op[s], (it / kStages) & 1, lim)) ? 1u : 0u;
-      uint32_t any_bad;
-      asm volatile(
-          "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.or.pred q, 1, %2, p; selp.u32 %0, 1, 0, q; }"
-          : "=r"(any_bad)
-          : "r"(bad), "n"(kConvWarps * 32)
-          : "memory");
-      if (any_bad) { give_up(); break; }
-      uint4 raw[8];
-#pragma unroll
-      for (int i = 0; i < 8; i++) raw[i] = *reinterpret_cast<const uint4*>(st + kOffRaw + (c + 128 * i) * 16);
-      asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");  // raw fully read
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const int id = c + 128 * i, r = id >> 3, cc = id & 7, tig = cc >> 1;
-        const uint32_t wd[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-          // device layout byte tig*32 + bb*8 + h*4 + e = block bb element 16h + 4tig + e
-          const int bb = 2 * (cc & 1) + (q >> 1), h = q & 1;
-          const int kin = (bb & 1) * 32 + 16 * h + 4 * tig;
-          const int chunk = kin >> 3;
-          uint8_t* dst = st + kOffA + (bb >> 1) * kAtom + r * 128 + ((chunk ^ (r & 7)) << 4) + (tig & 1) * 8;
-          *reinterpret_cast<uint2*>(dst) = s8x4_to_f16x4(wd[q]);
-        }
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) bar_arrive(&full_cvt[s]);
-    }
-  } else if (warp < kCtlWarp) {
+  if (warp < kEpiWarps) {
     // --------------------------------------------------------- epilogue
-    const int q = warp & 3, cb = 32 * ((warp - kConvWarps) >> 2), r = 32 * q + lane;
+    const int q = warp & 3, cb = 32 * (warp >> 2), r = 32 * q + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)cb;
     float acc[32];
 #pragma unroll
     for (int i = 0; i < 32; i++) acc[i] = 0.f;
+    uint32_t va[16], vb[16];
     bool ok = true;
     for (int it = 0; it < nst && ok; it++) {
       const int e = it % kSide;
       const uint8_t* sd = side + e * kSideBytes;
       // warp-uniform outcomes: the TMEM loads below are warp-collective
-      if (!__all_sync(0xffffffffu, bar_wait(&full_side[e], (it / kSide) & 1, lim))) {
+      if (!__all_sync(0xffffffffu, bar_wait(&full_side[e], (it / kSide) & 1, lim)) ||
+          !__all_sync(0xffffffffu, bar_wait(&tfull[0], it & 1, lim))) {
         give_up();
         ok = false;
         break;
       }
+      tc_after();
+      tmem_ld16(lane_base, va);
+      tmem_wait16(va);
       const float* ds = reinterpret_cast<const float*>(sd);
       const __half* ws = reinterpret_cast<const __half*>(sd + kOffS + r * 16 + 8 * (it & 1));
-#pragma unroll 1
+#pragma unroll
       for (int j = 0; j < 4; j++) {
-        if (!__all_sync(0xffffffffu, bar_wait(&tfull[j], it & 1, lim))) { give_up(); ok = false; break; }
-        tc_after();
-        uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(j * 128 + cb), v);
+        const float dw = __half2float(ws[j]);
+        tmem_ld16(lane_base + (uint32_t)(j * 128 + 16), vb);  // second half, in flight
+        scale_half(acc, dw, ds + j * 128 + cb, va);
+        tmem_wait16(vb);
         tc_before();
         __syncwarp();
         if (lane == 0) bar_arrive(&tempty[j]);
-        const float dw = __half2float(ws[j]);
-        const float4* dx = reinterpret_cast<const float4*>(ds + j * 128 + cb);
-#pragma unroll
-        for (int i4 = 0; i4 < 8; i4++) {
-          const float4 d4 = dx[i4];
-          scale_fma2(acc[4 * i4], acc[4 * i4 + 1], dw, d4.x, d4.y, v[4 * i4], v[4 * i4 + 1]);
-          scale_fma2(acc[4 * i4 + 2], acc[4 * i4 + 3], dw, d4.z, d4.w, v[4 * i4 + 2], v[4 * i4 + 3]);
+        if (j < 3) {
+          if (!__all_sync(0xffffffffu, bar_wait(&tfull[j + 1], it & 1, lim))) {
+            give_up();
+            ok = false;
+            break;
+          }
+          tc_after();
+          tmem_ld16(lane_base + (uint32_t)((j + 1) * 128), va);  // next block's first half, in flight
         }
+        scale_half(acc + 16, dw, ds + j * 128 + cb + 16, vb);
+        if (j < 3) tmem_wait16(va);
       }
       __syncwarp();
       if (lane == 0) bar_arrive(&empty_side[e]);
     }
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");  // nothing in flight past this point
     if (ok && !*abort_v) {
       const int row = row0 + r;
       if (row < rows) {
@@ -297,15 +294,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == kCtlWarp && lane == 0) {
+  } else if (warp == kTmaWarp && lane == 0) {
     // ------------------------------------------------------ TMA producer
     int issued = 0;
     for (int it = 0; it < nst && !*abort_v; it++) {
       const int s = it % kStages, e = it % kSide;
       if (it >= kStages && !bar_wait(&empty_op[s], ((it / kStages) + 1) & 1, lim)) { give_up(); break; }
       uint8_t* st = smem + s * kStageBytes;
-      bar_expect(&full_op[s], kOpTmaBytes);
-      tma2d(st + kOffRaw, &tm_w, it * 128, row0, &full_op[s]);
+      bar_expect(&full_op[s], kStageBytes);
+      tma2d(st + kOffA, &tm_w, it * kStageK, row0, &full_op[s]);
+      tma2d(st + kOffA + kAtom, &tm_w, it * kStageK + 64, row0, &full_op[s]);
       tma2d(st + kOffB, &tm_x, it * kStageK, tok0, &full_op[s]);
       tma2d(st + kOffB + kAtom, &tm_x, it * kStageK + 64, tok0, &full_op[s]);
       if (it >= kSide && !bar_wait(&empty_side[e], ((it / kSide) + 1) & 1, lim)) {
@@ -329,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------- MMA issuer
     for (int it = 0; it < nst && !*abort_v; it++) {
       const int s = it % kStages;
-      if (!bar_wait(&full_op[s], (it / kStages) & 1, lim) || !bar_wait(&full_cvt[s], (it / kStages) & 1, lim)) {
+      if (!bar_wait(&full_op[s], (it / kStages) & 1, lim)) {
         give_up();
         break;
       }
@@ -338,7 +336,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t a0 = su32(smem + s * kStageBytes + kOffA), b0 = su32(smem + s * kStageBytes + kOffB);
       bool ok = true;
       for (int j = 0; j < 4; j++) {
-        if (it > 0 && !bar_wait(&tempty[j], (it - 1) & 1, lim)) { give_up(); ok = false; break; }
+        if (it > 0 && !bar_wait(&tempty[j], (it - 1) & 1, lim)) {
+          give_up();
+          ok = false;
+          break;
+        }
         tc_after();
         const uint32_t off = (uint32_t)((j >> 1) * kAtom + (j & 1) * 64);
 #pragma unroll
@@ -379,6 +381,26 @@ __global__ void wide_act_kernel(const float* __restrict__ x, int ldx, int cols, 
   const int qi = (int)(int8_t)roundf(__fmul_rn(v, id));
   q[(int64_t)t * cols + b * 32 + lane] = __int2half_rn(qi);
   if (lane == 0) dT[(int64_t)b * ldd + t] = __half2float(__float2half_rn(d));
+}
+
+// Device-layout Q8_0 rows -> f16 integers, row-major (the weight operand of
+// the product).  One thread per 16-byte chunk of a four-block group: byte
+// tig*32 + bb*8 + h*4 + e holds element 16h + 4tig + e of block bb.
+__global__ void wide_expand_q80_kernel(const uint8_t* __restrict__ w, int64_t w_row_bytes, int rows, int cols,
+                                       __half* __restrict__ out) {
+  const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int groups = cols / 128;
+  const int64_t r = id / (groups * 8);
+  if (r >= rows) return;
+  const int g = (int)(id / 8 % groups), cc = (int)(id & 7), tig = cc >> 1;
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(w + r * w_row_bytes + g * 128 + cc * 16));
+  const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    const int bb = 2 * (cc & 1) + (q >> 1), h = q & 1;
+    const int k = g * 128 + bb * 32 + 16 * h + 4 * tig;
+    *reinterpret_cast<uint2*>(out + r * cols + k) = s8x4_to_f16x4(wd[q]);
+  }
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
@@ -422,17 +444,20 @@ int* wide_timeout_flag() {
 }
 
 cudaError_t wide_q80_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
-                             int ldx, int ntok, float* y, int out_ld, __half* qx, float* dT, cudaStream_t st) {
-  if (cols % kStageK || ntok < 1 || ntok > 65535 || rows < 1 || rows > INT32_MAX || ((uintptr_t)w & 15) || ((uintptr_t)qx & 15) ||
-      ((uintptr_t)dT & 15) || w_row_bytes % 16)
+                             int ldx, int ntok, float* y, int out_ld, __half* qx, float* dT, __half* wx,
+                             cudaStream_t st) {
+  if (cols % kStageK || ntok < 1 || ntok > 65535 || rows < 1 || rows > INT32_MAX || ((uintptr_t)w & 15) ||
+      ((uintptr_t)qx & 15) || ((uintptr_t)dT & 15) || ((uintptr_t)wx & 15) || w_row_bytes % 16)
     return cudaErrorInvalidValue;
   const int nb = (int)(cols / 32), ldd = wide_ldd(ntok);
   wide_act_kernel<<<dim3((unsigned)((nb + 7) / 8), (unsigned)ntok), 256, 0, st>>>(x, ldx, (int)cols, qx, dT, ldd);
+  const int64_t chunks = rows * (cols / 128) * 8;
+  wide_expand_q80_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(w, w_row_bytes, (int)rows, (int)cols, wx);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   alignas(64) CUtensorMap mw, mx, md, ms;
-  if (!encode2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)w_row_bytes, (uint64_t)rows, (uint64_t)w_row_bytes,
-                128, kRows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+  if (!encode2d(&mw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, wx, (uint64_t)cols, (uint64_t)rows, (uint64_t)cols * 2, 64,
+                kRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode2d(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)w_row_bytes, (uint64_t)rows, (uint64_t)w_row_bytes,
                 16, kRows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
       !encode2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, qx, (uint64_t)cols, (uint64_t)ntok, (uint64_t)cols * 2, 64,
@@ -445,10 +470,10 @@ cudaError_t wide_q80_forward(const uint8_t* w, int64_t rows, int64_t cols, int64
     e = cudaFuncSetAttribute(wide_q80_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
   }
-  const dim3 grid((unsigned)((ntok + kToks - 1) / kToks), (unsigned)((rows + kRows - 1) / kRows));
   int* flag = wide_timeout_flag();
   if (!flag) return cudaErrorInvalidDevice;
   static const int test_skip = getenv("IQ_WIDE_TEST_TIMEOUT") ? 1 : 0;
+  const dim3 grid((unsigned)((ntok + kToks - 1) / kToks), (unsigned)((rows + kRows - 1) / kRows));
   wide_q80_kernel<<<grid, kThreads, kSmemBytes, st>>>(mw, mx, md, ms, nb * 32, (int)rows, nb, ntok, y, out_ld, flag,
                                                       test_skip);
   return cudaGetLastError();
