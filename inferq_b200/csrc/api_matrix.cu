@@ -187,16 +187,26 @@ int iq_matrix_forward_device(const iq_matrix* m, const float* x, int input_rows,
 int iq_matrix_forward_wide(const iq_matrix* m, const float* x, int input_rows, float* y, void* stream) {
   clear_error();
   IQ_CHECK(m && x && y, IQ_EINVAL, "iq_matrix_forward_wide: null argument");
-  IQ_CHECK(m->dtype == Q8_0, IQ_EUNSUPPORTED, "the wide product takes Q8_0 matrices, got dtype %d", m->dtype);
+  IQ_CHECK(m->dtype == Q8_0 || m->dtype == Q4_K, IQ_EUNSUPPORTED,
+           "the wide product takes Q8_0 or Q4_K matrices, got dtype %d", m->dtype);
+  IQ_CHECK(input_rows >= 1 && input_rows <= 65535, IQ_EINVAL, "expected 1..65535 input rows, got %d", input_rows);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (m->dtype == Q4_K) {
+    const size_t need = wide_q4k_scratch_bytes(m->rows, m->cols, input_rows, nullptr, nullptr);
+    IQ_CUDA(g_scratch.wide_w.reserve(need));
+    WideQ4kScratch sc;
+    wide_q4k_scratch_bytes(m->rows, m->cols, input_rows, &sc, g_scratch.wide_w.as<uint8_t>());
+    IQ_CUDA(wide_q4k_forward(m->base, m->rows, m->cols, m->row_bytes, x, (int)m->cols, input_rows, y, (int)m->rows,
+                             sc, st));
+    return IQ_OK;
+  }
   IQ_CHECK(m->cols % 128 == 0, IQ_EINVAL, "the wide product needs cols %% 128 == 0, got %lld", (long long)m->cols);
-  IQ_CHECK(input_rows >= 1, IQ_EINVAL, "expected at least one input row, got %d", input_rows);
   const int64_t nb = m->cols / 32;
   IQ_CUDA(g_scratch.x.reserve((size_t)(input_rows * m->cols * 2)));
   IQ_CUDA(g_scratch.act.reserve((size_t)(nb * wide_ldd(input_rows) * 4)));
   IQ_CUDA(g_scratch.wide_w.reserve((size_t)(m->rows * m->cols * 2)));
   IQ_CUDA(wide_q80_forward(m->base, m->rows, m->cols, m->row_bytes, x, (int)m->cols, input_rows, y, (int)m->rows,
-                           g_scratch.x.as<__half>(), g_scratch.act.as<float>(), g_scratch.wide_w.as<__half>(),
-                           static_cast<cudaStream_t>(stream)));
+                           g_scratch.x.as<__half>(), g_scratch.act.as<float>(), g_scratch.wide_w.as<__half>(), st));
   return IQ_OK;
 }
 

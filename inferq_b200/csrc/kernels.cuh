@@ -37,6 +37,18 @@ cudaError_t f32_matvec(const float* w, int rows, int cols, const float* x, int l
 // wide_ldd(ntok) f32) and wx (rows x cols f16) are scratch.  cols % 128 == 0.
 int wide_ldd(int ntok);
 int* wide_timeout_flag();  // device flag: a wide-product wait gave up
+// Q4_K x Q8_K wide product (wide.cu); cols % 256 == 0.  Scratch carved from
+// one buffer by wide_q4k_scratch_bytes (base NULL: size only).
+struct WideQ4kScratch {
+  __half* qx;
+  float* dT;
+  uint8_t* bm;
+  __half* wx;
+  uint8_t* am;
+};
+size_t wide_q4k_scratch_bytes(int64_t rows, int64_t cols, int ntok, WideQ4kScratch* sc, uint8_t* base);
+cudaError_t wide_q4k_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
+                             int ldx, int ntok, float* y, int out_ld, const WideQ4kScratch& sc, cudaStream_t st);
 cudaError_t wide_q80_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
                              int ldx, int ntok, float* y, int out_ld, __half* qx, float* dT, __half* wx,
                              cudaStream_t st);

@@ -403,6 +403,348 @@ __global__ void wide_expand_q80_kernel(const uint8_t* __restrict__ w, int64_t w_
   }
 }
 
+// ----------------------------------------------------------------- Q4_K
+// The same product for Q4_K weights x Q8_K input rows, bitwise the
+// per-block device order (src/qgemm.rs:153-240 forms the same integers):
+//     isum = sum_s sc[s] * sum_{e in s} q_e x_e,  msum = sum_s mn[s] * bsum_s
+//     acc  = fmaf(d_x * d_w, (float)isum, acc),  accm = fmaf(d_x * dmin, (float)msum, accm)
+//     y    = acc - accm
+// The sub-block scales are folded into the weight operand, A = sc[s] * q
+// (<= 63 * 15, exact in f16), so the tensor cores form isum directly.  A
+// whole block can reach 256 * 945 * 128 > 2^24, so each block's two halves
+// go to separate TMEM accumulators (each below 2^24, exact) and
+// (float)isum is their f32 sum (one rounding of the exact integer).  msum is
+// one more K=16 MMA per block: A_m = (mn[0..7], 64 * mn[0..7]) against
+// B_m = (bsum mod 64, bsum div 64), all exact in f16.  Tiles: 128 weight
+// rows x 64 input rows, one 256-element block per stage; TMEM holds two
+// blocks' three 64-column accumulators.
+constexpr int kQ4Toks = 64;
+constexpr int kQ4AtomA = 128 * 128, kQ4AtomB = kQ4Toks * 128;
+constexpr int kQ4OffB = 4 * kQ4AtomA, kQ4OffAm = kQ4OffB + 4 * kQ4AtomB, kQ4OffBm = kQ4OffAm + 4096;
+constexpr int kQ4StageBytes = kQ4OffBm + 2048;  // 102 KB
+constexpr int kQ4Stages = 2;
+constexpr int kQ4Side = 4, kQ4SideBytes = 2560, kQ4OffH = 256;  // input-row d (64 f32), then 16-B row headers
+constexpr int kQ4SmemBytes = kQ4Stages * kQ4StageBytes + kQ4Side * kQ4SideBytes + 1024;
+static_assert(kQ4StageBytes % 1024 == 0, "swizzled atoms stay 1024-byte aligned");
+constexpr uint32_t kQ4Idesc = (1u << 4) | ((uint32_t)(kQ4Toks >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+
+__device__ __forceinline__ void mma_f16_n64(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(kQ4Idesc), "r"(accumulate)
+      : "memory");
+}
+// K-major operand without swizzle: 8-row x 16-byte core matrices, the two
+// 16-byte K halves 128 bytes apart, 8-row groups 256 bytes apart.
+__device__ __forceinline__ uint64_t plain_desc(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(256 >> 4) << 32) |
+         ((uint64_t)1 << 46);
+}
+// 1-D bulk copy global -> shared (this GPU's memory, no multicast).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   su32(dst)),
+               "l"(src), "r"(bytes), "r"(su32(b))
+               : "memory");
+}
+// Byte offset of (row, K half) in a core-matrix tile of the min operands.
+__host__ __device__ __forceinline__ int plain_off(int row, int half) {
+  return (row >> 3) * 256 + half * 128 + (row & 7) * 16;
+}
+
+__global__ void __launch_bounds__(kBoundThreads, 1)
+    wide_q4k_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                    const __grid_constant__ CUtensorMap tm_d, const __grid_constant__ CUtensorMap tm_h,
+                    const uint8_t* __restrict__ am, const uint8_t* __restrict__ bm, int rows, int nb, int ntok,
+                    float* __restrict__ y, int out_ld, int* timeout_flag, int test_skip) {
+  __shared__ __align__(8) uint64_t full_op[kQ4Stages], empty_op[kQ4Stages];
+  __shared__ __align__(8) uint64_t full_side[kQ4Side], empty_side[kQ4Side];
+  __shared__ __align__(8) uint64_t tfull[2], tempty[2], drained;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int abort_s;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (su32(smem_raw) & 1023)) & 1023);
+  uint8_t* side = smem + kQ4Stages * kQ4StageBytes;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tok0 = blockIdx.x * kQ4Toks, row0 = blockIdx.y * 128;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kQ4Stages; s++) {
+      bar_init(&full_op[s], 1);
+      bar_init(&empty_op[s], 1);
+    }
+    for (int e = 0; e < kQ4Side; e++) {
+      bar_init(&full_side[e], 1);
+      bar_init(&empty_side[e], kEpiWarps);
+    }
+    for (int j = 0; j < 2; j++) {
+      bar_init(&tfull[j], 1);
+      bar_init(&tempty[j], kEpiWarps);
+    }
+    bar_init(&drained, 1);
+    abort_s = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base_s)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_before();
+  __syncthreads();
+  tc_after();
+  const uint32_t tmem = tmem_base_s;
+  volatile int* abort_v = &abort_s;
+  const int lim = test_skip ? 256 : kWaitLimit;
+  auto give_up = [&]() {
+    atomicExch(timeout_flag, 1);
+    *abort_v = 1;
+  };
+
+  if (warp < kEpiWarps) {
+    // --------------------------------------------------------- epilogue
+    const int q = warp & 3, cb = 16 * (warp >> 2), r = 32 * q + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)cb;
+    float acc[16], accm[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) acc[i] = accm[i] = 0.f;
+    bool ok = true;
+    for (int it = 0; it < nb && ok; it++) {
+      const int e = it % kQ4Side, buf = it & 1;
+      const uint8_t* sd = side + e * kQ4SideBytes;
+      if (!__all_sync(0xffffffffu, bar_wait(&full_side[e], (it / kQ4Side) & 1, lim)) ||
+          !__all_sync(0xffffffffu, bar_wait(&tfull[buf], (it >> 1) & 1, lim))) {
+        give_up();
+        ok = false;
+        break;
+      }
+      tc_after();
+      uint32_t va[16], vb[16], vm[16];
+      tmem_ld16(lane_base + (uint32_t)(buf * 192), va);
+      tmem_ld16(lane_base + (uint32_t)(buf * 192 + 64), vb);
+      tmem_ld16(lane_base + (uint32_t)(buf * 192 + 128), vm);
+      tmem_wait16(va);
+      tmem_wait16(vb);
+      tmem_wait16(vm);
+      tc_before();
+      __syncwarp();
+      if (lane == 0) bar_arrive(&tempty[buf]);
+      const float* dx = reinterpret_cast<const float*>(sd) + cb;
+      const __half* hd = reinterpret_cast<const __half*>(sd + kQ4OffH + r * 16);
+      const float dw = __half2float(hd[0]), dmin = __half2float(hd[1]);
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        const float isum = __fadd_rn(__uint_as_float(va[i]), __uint_as_float(vb[i]));
+        acc[i] = __fmaf_rn(__fmul_rn(dx[i], dw), isum, acc[i]);
+        accm[i] = __fmaf_rn(__fmul_rn(dx[i], dmin), __uint_as_float(vm[i]), accm[i]);
+      }
+      __syncwarp();
+      if (lane == 0) bar_arrive(&empty_side[e]);
+    }
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    if (ok && !*abort_v) {
+      const int row = row0 + r;
+      if (row < rows) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const int t = tok0 + cb + i;
+          if (t < ntok) y[(int64_t)t * out_ld + row] = __fsub_rn(acc[i], accm[i]);
+        }
+      }
+    }
+  } else if (warp == kTmaWarp && lane == 0) {
+    // ------------------------------------------------------ TMA producer
+    const uint8_t* am_tile = am + (int64_t)blockIdx.y * nb * 4096;
+    const uint8_t* bm_tile = bm + (int64_t)blockIdx.x * nb * 2048;
+    int issued = 0;
+    for (int it = 0; it < nb && !*abort_v; it++) {
+      const int s = it % kQ4Stages, e = it % kQ4Side;
+      if (it >= kQ4Stages && !bar_wait(&empty_op[s], ((it / kQ4Stages) + 1) & 1, lim)) { give_up(); break; }
+      uint8_t* st = smem + s * kQ4StageBytes;
+      bar_expect(&full_op[s], kQ4StageBytes);
+#pragma unroll
+      for (int a = 0; a < 4; a++) {
+        tma2d(st + a * kQ4AtomA, &tm_w, it * 256 + 64 * a, row0, &full_op[s]);
+        tma2d(st + kQ4OffB + a * kQ4AtomB, &tm_x, it * 256 + 64 * a, tok0, &full_op[s]);
+      }
+      bulk_load(st + kQ4OffAm, am_tile + (int64_t)it * 4096, 4096, &full_op[s]);
+      bulk_load(st + kQ4OffBm, bm_tile + (int64_t)it * 2048, 2048, &full_op[s]);
+      if (it >= kQ4Side && !bar_wait(&empty_side[e], ((it / kQ4Side) + 1) & 1, lim)) {
+        issued = it + 1;
+        give_up();
+        break;
+      }
+      uint8_t* sd = side + e * kQ4SideBytes;
+      bar_expect(&full_side[e], kQ4OffH + 2048);
+      tma2d(sd, &tm_d, tok0, it, &full_side[e]);
+      tma2d(sd + kQ4OffH, &tm_h, it * 144, row0, &full_side[e]);
+      issued = it + 1;
+    }
+    if (*abort_v) {
+      for (int it = issued > kQ4Stages ? issued - kQ4Stages : 0; it < issued; it++)
+        bar_wait(&full_op[it % kQ4Stages], (it / kQ4Stages) & 1, lim);
+      for (int it = issued > kQ4Side ? issued - kQ4Side : 0; it < issued; it++)
+        bar_wait(&full_side[it % kQ4Side], (it / kQ4Side) & 1, lim);
+    }
+  } else if (warp == kMmaWarp && lane == 0) {
+    // ------------------------------------------------------- MMA issuer
+    for (int it = 0; it < nb && !*abort_v; it++) {
+      const int s = it % kQ4Stages, buf = it & 1;
+      if (!bar_wait(&full_op[s], (it / kQ4Stages) & 1, lim)) {
+        give_up();
+        break;
+      }
+      if (test_skip && it == 0) continue;
+      if (it >= 2 && !bar_wait(&tempty[buf], ((it >> 1) + 1) & 1, lim)) {
+        give_up();
+        break;
+      }
+      tc_after();
+      const uint32_t a0 = su32(smem + s * kQ4StageBytes), b0 = a0 + kQ4OffB;
+      const uint32_t d0 = tmem + (uint32_t)(buf * 192);
+#pragma unroll
+      for (int kk = 0; kk < 16; kk++) {  // K steps of 16: halves 0..127 -> a, 128..255 -> b
+        const uint32_t off_a = (uint32_t)((kk >> 2) * kQ4AtomA + (kk & 3) * 32);
+        const uint32_t off_b = (uint32_t)((kk >> 2) * kQ4AtomB + (kk & 3) * 32);
+        mma_f16_n64(d0 + (kk < 8 ? 0u : 64u), sw128_desc(a0 + off_a), sw128_desc(b0 + off_b),
+                    (uint32_t)((kk & 7) != 0));
+      }
+      mma_f16_n64(d0 + 128u, plain_desc(a0 + kQ4OffAm), plain_desc(a0 + kQ4OffBm), 0u);
+      mma_commit(&tfull[buf]);
+      mma_commit(&empty_op[s]);
+    }
+    mma_commit(&drained);
+    bar_wait(&drained, 0, lim);
+  }
+  __syncwarp();
+  tc_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// Input rows -> Q8_K integers as f16 (row-major), the block scales d
+// transposed (dT[b * ldd + t]) and the min operand tiles: per 64 input
+// rows and block, core-matrix order, (bsum_s mod 64, bsum_s div 64) for the
+// eight 32-element sub-block sums.  The arithmetic is the narrow path's Q8_K
+// quantizer (candle BlockQ8K::from_float: the first value of largest
+// magnitude sets iscale = -128 / v, q = min(round(iscale * x), 127),
+// d = 1 / iscale).  One warp per (row, block); lane tig*8 + s holds elements
+// 32s + 16h + 4tig + e.
+__global__ void wide_act_q8k_kernel(const float* __restrict__ x, int ldx, int cols, __half* __restrict__ q,
+                                    float* __restrict__ dT, int ldd, uint8_t* __restrict__ bm) {
+  const int t = blockIdx.y, b = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int nb = cols / 256;
+  if (b >= nb) return;
+  const int s = lane & 7, tig = lane >> 3;
+  const float* xr = x + (int64_t)t * ldx + b * 256;
+  float v[8];
+#pragma unroll
+  for (int h = 0; h < 2; h++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) v[4 * h + e] = xr[32 * s + 16 * h + 4 * tig + e];
+  float amax = 0.f, vmax = 0.f;
+  int imax = 1 << 30;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const float a = fabsf(v[i]);
+    if (amax < a) { amax = a; vmax = v[i]; imax = 32 * s + 16 * (i / 4) + tig * 4 + (i % 4); }
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    const float oa = __shfl_xor_sync(0xffffffffu, amax, m);
+    const float ov = __shfl_xor_sync(0xffffffffu, vmax, m);
+    const int oi = __shfl_xor_sync(0xffffffffu, imax, m);
+    if (oa > amax || (oa == amax && oi < imax)) { amax = oa; vmax = ov; imax = oi; }
+  }
+  int qi[8];
+  float d = 0.f;
+  if (amax != 0.f) {
+    const float iscale = __fdiv_rn(-128.f, vmax);
+#pragma unroll
+    for (int i = 0; i < 8; i++) qi[i] = (int)(int8_t)fminf(roundf(__fmul_rn(iscale, v[i])), 127.f);
+    d = __fdiv_rn(1.f, iscale);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; i++) qi[i] = 0;
+  }
+  __half* qr = q + (int64_t)t * cols + b * 256;
+  int sum = 0;
+#pragma unroll
+  for (int h = 0; h < 2; h++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      qr[32 * s + 16 * h + 4 * tig + e] = __int2half_rn(qi[4 * h + e]);
+      sum += qi[4 * h + e];
+    }
+  sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 16);  // lanes s, s+8, ...: the sum of sub-block s
+  if (lane == 0) dT[(int64_t)b * ldd + t] = d;
+  if (tig == 0) {
+    const int lo = sum & 63, hi = (sum - lo) / 64;  // sum = 64 * hi + lo, 0 <= lo < 64
+    __half* tile = reinterpret_cast<__half*>(bm + ((int64_t)(t / kQ4Toks) * nb + b) * 2048);
+    const int tt = t % kQ4Toks;
+    tile[plain_off(tt, 0) / 2 + s] = __int2half_rn(lo);
+    tile[plain_off(tt, 1) / 2 + s] = __int2half_rn(hi);
+  }
+}
+
+// Device-layout Q4_K rows (16-byte header d, dmin, 12 scale bytes; then the
+// 128 quant bytes, byte tig*32 + j*8 + h*4 + e holding GGUF byte
+// 32j + 16h + 4tig + e) -> A = sc[s] * q as f16 (row-major) and the min
+// operand tiles (per 128 rows and block, core-matrix order: mn[0..7],
+// 64 * mn[0..7]).  One thread per 16-byte quant chunk.
+__global__ void wide_expand_q4k_kernel(const uint8_t* __restrict__ w, int64_t w_row_bytes, int rows, int cols,
+                                       __half* __restrict__ out, uint8_t* __restrict__ am) {
+  const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int nb = cols / 256;
+  const int64_t r = id / (nb * 8);
+  if (r >= rows) return;
+  const int b = (int)(id / 8 % nb), c = (int)(id & 7), tig = c >> 1;
+  const uint8_t* blk = w + r * w_row_bytes + (int64_t)b * 144;
+  const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(blk + 16 + c * 16));
+  // six-bit scales and mins as bytes: sc0-3, sc4-7, mn0-3, mn4-7
+  const uint32_t s_lo = hdr.y & 0x3F3F3F3Fu, m_lo = hdr.z & 0x3F3F3F3Fu;
+  const uint32_t s_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
+  const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
+  const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int qw = 0; qw < 4; qw++) {
+    const int j = 2 * (c & 1) + (qw >> 1), h = qw & 1;
+    const int slo = 2 * j, shi = 2 * j + 1;
+    const int sc_lo = (int)(((slo < 4 ? s_lo : s_hi) >> (8 * (slo & 3))) & 0xFF);
+    const int sc_hi = (int)(((shi < 4 ? s_lo : s_hi) >> (8 * (shi & 3))) & 0xFF);
+    const int k = b * 256 + 64 * j + 16 * h + 4 * tig;
+    __half2 lo[2], hi[2];
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      const int b0 = (int)((wd[qw] >> (8 * e)) & 0xFF), b1 = (int)((wd[qw] >> (8 * (e + 1))) & 0xFF);
+      lo[e / 2] = __halves2half2(__int2half_rn(sc_lo * (b0 & 15)), __int2half_rn(sc_lo * (b1 & 15)));
+      hi[e / 2] = __halves2half2(__int2half_rn(sc_hi * (b0 >> 4)), __int2half_rn(sc_hi * (b1 >> 4)));
+    }
+    *reinterpret_cast<uint2*>(out + r * cols + k) =
+        make_uint2(*reinterpret_cast<uint32_t*>(&lo[0]), *reinterpret_cast<uint32_t*>(&lo[1]));
+    *reinterpret_cast<uint2*>(out + r * cols + k + 32) =
+        make_uint2(*reinterpret_cast<uint32_t*>(&hi[0]), *reinterpret_cast<uint32_t*>(&hi[1]));
+  }
+  if (c == 0) {
+    __half* tile = reinterpret_cast<__half*>(am + ((r / 128) * nb + b) * 4096);
+    const int rr = (int)(r % 128);
+#pragma unroll
+    for (int s = 0; s < 8; s++) {
+      const int mn = (int)(((s < 4 ? m_lo : m_hi) >> (8 * (s & 3))) & 0xFF);
+      tile[plain_off(rr, 0) / 2 + s] = __int2half_rn(mn);
+      tile[plain_off(rr, 1) / 2 + s] = __int2half_rn(64 * mn);
+    }
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -477,6 +819,71 @@ cudaError_t wide_q80_forward(const uint8_t* w, int64_t rows, int64_t cols, int64
   wide_q80_kernel<<<grid, kThreads, kSmemBytes, st>>>(mw, mx, md, ms, nb * 32, (int)rows, nb, ntok, y, out_ld, flag,
                                                       test_skip);
   return cudaGetLastError();
+}
+
+cudaError_t wide_q4k_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
+                             int ldx, int ntok, float* y, int out_ld, const WideQ4kScratch& sc, cudaStream_t st) {
+  if (cols % 256 || ntok < 1 || ntok > 65535 || rows < 1 || rows > INT32_MAX || ((uintptr_t)w & 15) ||
+      w_row_bytes % 16)
+    return cudaErrorInvalidValue;
+  const int nb = (int)(cols / 256), ldd = wide_ldd(ntok);
+  const int ttiles = (ntok + kQ4Toks - 1) / kQ4Toks, rtiles = (int)((rows + 127) / 128);
+  cudaError_t e = cudaMemsetAsync(sc.bm, 0, (size_t)ttiles * nb * 2048, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(sc.am, 0, (size_t)rtiles * nb * 4096, st);
+  if (e != cudaSuccess) return e;
+  wide_act_q8k_kernel<<<dim3((unsigned)((nb + 7) / 8), (unsigned)ntok), 256, 0, st>>>(x, ldx, (int)cols, sc.qx,
+                                                                                       sc.dT, ldd, sc.bm);
+  const int64_t chunks = rows * nb * 8;
+  wide_expand_q4k_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(w, w_row_bytes, (int)rows, (int)cols,
+                                                                           sc.wx, sc.am);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  alignas(64) CUtensorMap mw, mx, md, mh;
+  if (!encode2d(&mw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc.wx, (uint64_t)cols, (uint64_t)rows, (uint64_t)cols * 2, 64,
+                128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc.qx, (uint64_t)cols, (uint64_t)ntok, (uint64_t)cols * 2, 64,
+                kQ4Toks, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode2d(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, sc.dT, (uint64_t)ntok, (uint64_t)nb, (uint64_t)ldd * 4,
+                kQ4Toks, 1, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode2d(&mh, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)w_row_bytes, (uint64_t)rows, (uint64_t)w_row_bytes,
+                16, 128, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  static bool attr[64] = {};
+  if (first_on_device(attr)) {
+    e = cudaFuncSetAttribute(wide_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kQ4SmemBytes);
+    if (e != cudaSuccess) return e;
+  }
+  int* flag = wide_timeout_flag();
+  if (!flag) return cudaErrorInvalidDevice;
+  static const int test_skip = getenv("IQ_WIDE_TEST_TIMEOUT") ? 1 : 0;
+  const dim3 grid((unsigned)ttiles, (unsigned)rtiles);
+  wide_q4k_kernel<<<grid, kThreads, kQ4SmemBytes, st>>>(mw, mx, md, mh, sc.am, sc.bm, (int)rows, nb, ntok, y, out_ld,
+                                                        flag, test_skip);
+  return cudaGetLastError();
+}
+
+size_t wide_q4k_scratch_bytes(int64_t rows, int64_t cols, int ntok, WideQ4kScratch* sc, uint8_t* base) {
+  const int nb = (int)(cols / 256);
+  const int ttiles = (ntok + kQ4Toks - 1) / kQ4Toks, rtiles = (int)((rows + 127) / 128);
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    const size_t o = off;
+    off += (n + 255) & ~(size_t)255;
+    return base ? base + o : nullptr;
+  };
+  uint8_t* qx = take((size_t)ntok * cols * 2);
+  uint8_t* dT = take((size_t)nb * wide_ldd(ntok) * 4);
+  uint8_t* bm = take((size_t)ttiles * nb * 2048);
+  uint8_t* wx = take((size_t)rows * cols * 2);
+  uint8_t* am = take((size_t)rtiles * nb * 4096);
+  if (sc) {
+    sc->qx = reinterpret_cast<__half*>(qx);
+    sc->dT = reinterpret_cast<float*>(dT);
+    sc->bm = bm;
+    sc->wx = reinterpret_cast<__half*>(wx);
+    sc->am = am;
+  }
+  return off;
 }
 
 }  // namespace iq
