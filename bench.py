@@ -188,32 +188,37 @@ def mtp_timing(state, cfg, hidden_row, seed_token, draft_vocab=32768, depth=3, r
 
 def wide_timing(rows=8192, cols=2048, n=512, reps=10):
     """The tensor-core wide product (prefill-shaped: n input rows through one
-    Q8_0 projection of the 35B width) timed with CUDA events: quantize +
-    product per call, and its rate against the measured dense bf16 peak."""
+    projection of the 35B width), Q8_0 and Q4_K, timed with CUDA events:
+    quantize + expand + product per call, and the rate against the measured
+    dense bf16 peak."""
     import torch
 
     from inferq_b200 import _lib
     from inferq_b200 import quants as Q
-    g = torch.Generator(device="cuda").manual_seed(5)
-    w = Q.encode(torch.randn(rows, cols, device="cuda", generator=g) * 0.02, Q.Q8_0)
-    m = _lib.Matrix(Q.Q8_0, w, rows, cols)
-    del w
-    x = torch.randn(n, cols, device="cuda", generator=g)
-    for _ in range(3):
-        m.forward_wide(x)
-    st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for _ in range(reps):
-        m.forward_wide(x)
-    e1.record(st)
-    torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) / reps * 1e3
-    tops = 2.0 * rows * cols * n / us / 1e6
     peaks = ROOT / "MEASURED_PEAKS.json"
     bf16 = json.loads(peaks.read_text()).get("bf16_tflops") if peaks.exists() else 1590.0
-    return {"shape": f"Q8_0 {rows}x{cols}, {n} input rows", "us": us, "int_tops": tops,
-            "frac_of_bf16_peak": tops / bf16, "kernel": "wide_q80_kernel (tcgen05, exact block dots)"}
+    out = {"shape": f"{rows}x{cols}, {n} input rows", "kernel": "wide_q80_kernel / wide_q4k_kernel "
+           "(tcgen05, exact block dots)"}
+    for name, dt in (("q8_0", Q.Q8_0), ("q4_k", Q.Q4_K)):
+        g = torch.Generator(device="cuda").manual_seed(5)
+        w = Q.encode(torch.randn(rows, cols, device="cuda", generator=g) * 0.02, dt)
+        m = _lib.Matrix(dt, w, rows, cols)
+        del w
+        x = torch.randn(n, cols, device="cuda", generator=g)
+        for _ in range(3):
+            m.forward_wide(x)
+        st = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            m.forward_wide(x)
+        e1.record(st)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / reps * 1e3
+        tops = 2.0 * rows * cols * n / us / 1e6
+        out[name] = {"us": us, "int_tops": tops, "frac_of_bf16_peak": tops / bf16}
+        del m
+    return out
 
 
 def greedy_continuation(model, prompt, n):
