@@ -188,7 +188,7 @@ def mtp_timing(state, cfg, hidden_row, seed_token, draft_vocab=32768, depth=3, r
 
 def wide_timing(rows=8192, cols=2048, n=512, reps=10):
     """The tensor-core wide product (prefill-shaped: n input rows through one
-    projection of the 35B width), Q8_0 and Q4_K, timed with CUDA events:
+    projection of the 35B width), Q8_0, Q4_K and Q6_K, timed with CUDA events:
     quantize + expand + product per call, and the rate against the measured
     dense bf16 peak."""
     import torch
@@ -197,9 +197,9 @@ def wide_timing(rows=8192, cols=2048, n=512, reps=10):
     from inferq_b200 import quants as Q
     peaks = ROOT / "MEASURED_PEAKS.json"
     bf16 = json.loads(peaks.read_text()).get("bf16_tflops") if peaks.exists() else 1590.0
-    out = {"shape": f"{rows}x{cols}, {n} input rows", "kernel": "wide_q80_kernel / wide_q4k_kernel "
+    out = {"shape": f"{rows}x{cols}, {n} input rows", "kernel": "wide_q80_kernel / wide_q4k_kernel / wide_q6k_kernel "
            "(tcgen05, exact block dots)"}
-    for name, dt in (("q8_0", Q.Q8_0), ("q4_k", Q.Q4_K)):
+    for name, dt in (("q8_0", Q.Q8_0), ("q4_k", Q.Q4_K), ("q6_k", Q.Q6_K)):
         g = torch.Generator(device="cuda").manual_seed(5)
         w = Q.encode(torch.randn(rows, cols, device="cuda", generator=g) * 0.02, dt)
         m = _lib.Matrix(dt, w, rows, cols)

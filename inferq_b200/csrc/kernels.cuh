@@ -47,6 +47,16 @@ struct WideQ4kScratch {
   uint8_t* am;
 };
 size_t wide_q4k_scratch_bytes(int64_t rows, int64_t cols, int ntok, WideQ4kScratch* sc, uint8_t* base);
+// Q6_K x Q8_K wide product; cols % 256 == 0.
+struct WideQ6kScratch {
+  __half* qx;
+  float* dT;
+  __half* lo;
+  __half* hi;
+};
+size_t wide_q6k_scratch_bytes(int64_t rows, int64_t cols, int ntok, WideQ6kScratch* sc, uint8_t* base);
+cudaError_t wide_q6k_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
+                             int ldx, int ntok, float* y, int out_ld, const WideQ6kScratch& sc, cudaStream_t st);
 cudaError_t wide_q4k_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
                              int ldx, int ntok, float* y, int out_ld, const WideQ4kScratch& sc, cudaStream_t st);
 cudaError_t wide_q80_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,

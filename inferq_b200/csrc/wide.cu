@@ -46,6 +46,7 @@
 #include <cstdlib>
 #include <cstring>
 #include "iq_common.cuh"
+#include "layout.cuh"
 #include "kernels.cuh"
 #include "qmv.cuh"
 
@@ -685,7 +686,7 @@ __global__ void wide_act_q8k_kernel(const float* __restrict__ x, int ldx, int co
   sum += __shfl_xor_sync(0xffffffffu, sum, 8);
   sum += __shfl_xor_sync(0xffffffffu, sum, 16);  // lanes s, s+8, ...: the sum of sub-block s
   if (lane == 0) dT[(int64_t)b * ldd + t] = d;
-  if (tig == 0) {
+  if (bm && tig == 0) {
     const int lo = sum & 63, hi = (sum - lo) / 64;  // sum = 64 * hi + lo, 0 <= lo < 64
     __half* tile = reinterpret_cast<__half*>(bm + ((int64_t)(t / kQ4Toks) * nb + b) * 2048);
     const int tt = t % kQ4Toks;
@@ -743,6 +744,221 @@ __global__ void wide_expand_q4k_kernel(const uint8_t* __restrict__ w, int64_t w_
       tile[plain_off(rr, 1) / 2 + s] = __int2half_rn(64 * mn);
     }
   }
+}
+
+// ----------------------------------------------------------------- Q6_K
+// Q6_K weights x Q8_K input rows, bitwise the per-block device order:
+//     isum = sum_s sc[s] * sum_{e in s} (q_e - 32) x_e   (16-element s, int8 sc)
+//     acc  = fmaf(d_x * d_w, (float)isum, acc)
+// sc * (q - 32) reaches 4096, not exact in f16, so the scale is split,
+// sc = 16 * sh + sl (sl = sc & 15, sh = sc >> 4), into two operands
+// A_lo = sl * (q - 32) (|.| <= 480) and A_hi = sh * (q - 32) (|.| <= 256),
+// each with its own TMEM accumulator over the whole block (at most
+// 256 * 480 * 128 < 2^24, exact); (float)isum = fmaf(16, hi, lo), one
+// rounding of the exact integer.  Tiles: 128 weight rows x 128 input rows,
+// a quarter block (64 K elements) per stage, two blocks in TMEM.
+constexpr int kQ6Atom = 128 * 128;
+constexpr int kQ6StageBytes = 3 * kQ6Atom;  // A_lo, A_hi, B
+constexpr int kQ6Stages = 4;
+constexpr int kQ6Side = 4, kQ6SideBytes = 2560, kQ6OffT = 512;  // input-row d (128 f32), then the d tail box
+constexpr int kQ6SmemBytes = kQ6Stages * kQ6StageBytes + kQ6Side * kQ6SideBytes + 1024;
+
+__global__ void __launch_bounds__(kBoundThreads, 1)
+    wide_q6k_kernel(const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_hi,
+                    const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_d,
+                    const __grid_constant__ CUtensorMap tm_t, int tail_x0, int rows, int nb, int ntok,
+                    float* __restrict__ y, int out_ld, int* timeout_flag, int test_skip) {
+  __shared__ __align__(8) uint64_t full_op[kQ6Stages], empty_op[kQ6Stages];
+  __shared__ __align__(8) uint64_t full_side[kQ6Side], empty_side[kQ6Side];
+  __shared__ __align__(8) uint64_t tfull[2], tempty[2], drained;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int abort_s;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (su32(smem_raw) & 1023)) & 1023);
+  uint8_t* side = smem + kQ6Stages * kQ6StageBytes;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tok0 = blockIdx.x * 128, row0 = blockIdx.y * 128;
+  const int nst = nb * 4;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kQ6Stages; s++) {
+      bar_init(&full_op[s], 1);
+      bar_init(&empty_op[s], 1);
+    }
+    for (int e = 0; e < kQ6Side; e++) {
+      bar_init(&full_side[e], 1);
+      bar_init(&empty_side[e], kEpiWarps);
+    }
+    for (int j = 0; j < 2; j++) {
+      bar_init(&tfull[j], 1);
+      bar_init(&tempty[j], kEpiWarps);
+    }
+    bar_init(&drained, 1);
+    abort_s = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base_s)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_before();
+  __syncthreads();
+  tc_after();
+  const uint32_t tmem = tmem_base_s;
+  volatile int* abort_v = &abort_s;
+  const int lim = test_skip ? 256 : kWaitLimit;
+  auto give_up = [&]() {
+    atomicExch(timeout_flag, 1);
+    *abort_v = 1;
+  };
+
+  if (warp < kEpiWarps) {
+    // --------------------------------------------------------- epilogue
+    const int q = warp & 3, cb = 32 * (warp >> 2), r = 32 * q + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)cb;
+    float acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; i++) acc[i] = 0.f;
+    bool ok = true;
+    for (int blk = 0; blk < nb && ok; blk++) {
+      const int e = blk % kQ6Side, buf = blk & 1;
+      const uint8_t* sd = side + e * kQ6SideBytes;
+      if (!__all_sync(0xffffffffu, bar_wait(&full_side[e], (blk / kQ6Side) & 1, lim)) ||
+          !__all_sync(0xffffffffu, bar_wait(&tfull[buf], (blk >> 1) & 1, lim))) {
+        give_up();
+        ok = false;
+        break;
+      }
+      tc_after();
+      const float* dx = reinterpret_cast<const float*>(sd) + cb;
+      const float dw = __half2float(*reinterpret_cast<const __half*>(sd + kQ6OffT + r * 16 + 2 * (blk & 7)));
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        uint32_t vl[16], vh[16];
+        tmem_ld16(lane_base + (uint32_t)(buf * 256 + 16 * h), vl);
+        tmem_ld16(lane_base + (uint32_t)(buf * 256 + 128 + 16 * h), vh);
+        tmem_wait16(vl);
+        tmem_wait16(vh);
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const float isum = __fmaf_rn(16.f, __uint_as_float(vh[i]), __uint_as_float(vl[i]));
+          acc[16 * h + i] = __fmaf_rn(__fmul_rn(dx[16 * h + i], dw), isum, acc[16 * h + i]);
+        }
+      }
+      tc_before();
+      __syncwarp();
+      if (lane == 0) {
+        bar_arrive(&tempty[buf]);
+        bar_arrive(&empty_side[e]);
+      }
+    }
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    if (ok && !*abort_v) {
+      const int row = row0 + r;
+      if (row < rows) {
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          const int t = tok0 + cb + i;
+          if (t < ntok) y[(int64_t)t * out_ld + row] = acc[i];
+        }
+      }
+    }
+  } else if (warp == kTmaWarp && lane == 0) {
+    // ------------------------------------------------------ TMA producer
+    int issued = 0, sides = 0;
+    for (int it = 0; it < nst && !*abort_v; it++) {
+      const int s = it % kQ6Stages, blk = it >> 2;
+      if (it >= kQ6Stages && !bar_wait(&empty_op[s], ((it / kQ6Stages) + 1) & 1, lim)) { give_up(); break; }
+      uint8_t* st = smem + s * kQ6StageBytes;
+      bar_expect(&full_op[s], kQ6StageBytes);
+      tma2d(st, &tm_lo, it * 64, row0, &full_op[s]);
+      tma2d(st + kQ6Atom, &tm_hi, it * 64, row0, &full_op[s]);
+      tma2d(st + 2 * kQ6Atom, &tm_x, it * 64, tok0, &full_op[s]);
+      issued = it + 1;
+      if ((it & 3) == 0) {
+        const int e = blk % kQ6Side;
+        if (blk >= kQ6Side && !bar_wait(&empty_side[e], ((blk / kQ6Side) + 1) & 1, lim)) { give_up(); break; }
+        uint8_t* sd = side + e * kQ6SideBytes;
+        bar_expect(&full_side[e], kQ6OffT + 2048);
+        tma2d(sd, &tm_d, tok0, blk, &full_side[e]);
+        tma2d(sd + kQ6OffT, &tm_t, tail_x0 + 16 * (blk >> 3), row0, &full_side[e]);
+        sides = blk + 1;
+      }
+    }
+    if (*abort_v) {
+      for (int it = issued > kQ6Stages ? issued - kQ6Stages : 0; it < issued; it++)
+        bar_wait(&full_op[it % kQ6Stages], (it / kQ6Stages) & 1, lim);
+      for (int b = sides > kQ6Side ? sides - kQ6Side : 0; b < sides; b++)
+        bar_wait(&full_side[b % kQ6Side], (b / kQ6Side) & 1, lim);
+    }
+  } else if (warp == kMmaWarp && lane == 0) {
+    // ------------------------------------------------------- MMA issuer
+    for (int it = 0; it < nst && !*abort_v; it++) {
+      const int s = it % kQ6Stages, blk = it >> 2, quarter = it & 3, buf = blk & 1;
+      if (!bar_wait(&full_op[s], (it / kQ6Stages) & 1, lim)) {
+        give_up();
+        break;
+      }
+      if (test_skip && blk == 0) continue;
+      if (quarter == 0 && blk >= 2 && !bar_wait(&tempty[buf], ((blk >> 1) + 1) & 1, lim)) {
+        give_up();
+        break;
+      }
+      tc_after();
+      const uint32_t a_lo = su32(smem + s * kQ6StageBytes), a_hi = a_lo + kQ6Atom, bx = a_lo + 2 * kQ6Atom;
+      const uint32_t d0 = tmem + (uint32_t)(buf * 256);
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) {
+        const uint32_t acc_in = (uint32_t)((quarter | kk) != 0);
+        mma_f16(d0, sw128_desc(a_lo + 32 * kk), sw128_desc(bx + 32 * kk), acc_in);
+        mma_f16(d0 + 128u, sw128_desc(a_hi + 32 * kk), sw128_desc(bx + 32 * kk), acc_in);
+      }
+      mma_commit(&empty_op[s]);
+      if (quarter == 3) mma_commit(&tfull[buf]);
+    }
+    mma_commit(&drained);
+    bar_wait(&drained, 0, lim);
+  }
+  __syncwarp();
+  tc_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// Device-layout Q6_K rows -> the two scale-split operands A_lo = sl * (q - 32)
+// and A_hi = sh * (q - 32) as f16 (row-major).  One thread per 16-element
+// sub-block; the 6-bit values come from the device re-pack (q6k_dev_value),
+// the int8 scales from the 16 bytes after the quants.
+__global__ void wide_expand_q6k_kernel(const uint8_t* __restrict__ w, int64_t w_row_bytes, int rows, int cols,
+                                       __half* __restrict__ lo, __half* __restrict__ hi) {
+  const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int nb = cols / 256;
+  const int64_t r = id / (nb * 16);
+  if (r >= rows) return;
+  const int b = (int)(id / 16 % nb), sb = (int)(id & 15);
+  const uint8_t* blk = w + r * w_row_bytes + (int64_t)b * 208;
+  const int sc = (int)(int8_t)blk[192 + sb];
+  const int sh = sc >> 4, sl = sc & 15;  // sc = 16 * sh + sl
+  __half vl[16], vh[16];
+#pragma unroll
+  for (int e = 0; e < 16; e++) {
+    const int v = q6k_dev_value(blk, 16 * sb + e) - 32;
+    vl[e] = __int2half_rn(sl * v);
+    vh[e] = __int2half_rn(sh * v);
+  }
+  const int64_t k = r * cols + (int64_t)b * 256 + 16 * sb;
+  uint4* dl = reinterpret_cast<uint4*>(lo + k);
+  uint4* dh = reinterpret_cast<uint4*>(hi + k);
+  dl[0] = *reinterpret_cast<const uint4*>(&vl[0]);
+  dl[1] = *reinterpret_cast<const uint4*>(&vl[8]);
+  dh[0] = *reinterpret_cast<const uint4*>(&vh[0]);
+  dh[1] = *reinterpret_cast<const uint4*>(&vh[8]);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
@@ -884,6 +1100,66 @@ size_t wide_q4k_scratch_bytes(int64_t rows, int64_t cols, int ntok, WideQ4kScrat
     sc->am = am;
   }
   return off;
+}
+
+size_t wide_q6k_scratch_bytes(int64_t rows, int64_t cols, int ntok, WideQ6kScratch* sc, uint8_t* base) {
+  const int nb = (int)(cols / 256);
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    const size_t o = off;
+    off += (n + 255) & ~(size_t)255;
+    return base ? base + o : nullptr;
+  };
+  uint8_t* qx = take((size_t)ntok * cols * 2);
+  uint8_t* dT = take((size_t)nb * wide_ldd(ntok) * 4);
+  uint8_t* lo = take((size_t)rows * cols * 2);
+  uint8_t* hi = take((size_t)rows * cols * 2);
+  if (sc) {
+    sc->qx = reinterpret_cast<__half*>(qx);
+    sc->dT = reinterpret_cast<float*>(dT);
+    sc->lo = reinterpret_cast<__half*>(lo);
+    sc->hi = reinterpret_cast<__half*>(hi);
+  }
+  return off;
+}
+
+cudaError_t wide_q6k_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
+                             int ldx, int ntok, float* y, int out_ld, const WideQ6kScratch& sc, cudaStream_t st) {
+  if (cols % 256 || ntok < 1 || ntok > 65535 || rows < 1 || rows > INT32_MAX || ((uintptr_t)w & 15) ||
+      w_row_bytes % 16)
+    return cudaErrorInvalidValue;
+  const int nb = (int)(cols / 256), ldd = wide_ldd(ntok);
+  wide_act_q8k_kernel<<<dim3((unsigned)((nb + 7) / 8), (unsigned)ntok), 256, 0, st>>>(x, ldx, (int)cols, sc.qx,
+                                                                                       sc.dT, ldd, nullptr);
+  const int64_t subs = rows * nb * 16;
+  wide_expand_q6k_kernel<<<(unsigned)((subs + 255) / 256), 256, 0, st>>>(w, w_row_bytes, (int)rows, (int)cols, sc.lo,
+                                                                         sc.hi);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  alignas(64) CUtensorMap mlo, mhi, mx, md, mt;
+  if (!encode2d(&mlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc.lo, (uint64_t)cols, (uint64_t)rows, (uint64_t)cols * 2, 64,
+                128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode2d(&mhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc.hi, (uint64_t)cols, (uint64_t)rows, (uint64_t)cols * 2, 64,
+                128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc.qx, (uint64_t)cols, (uint64_t)ntok, (uint64_t)cols * 2, 64,
+                128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode2d(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, sc.dT, (uint64_t)ntok, (uint64_t)nb, (uint64_t)ldd * 4, 128, 1,
+                CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode2d(&mt, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)w_row_bytes, (uint64_t)rows, (uint64_t)w_row_bytes,
+                16, 128, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  static bool attr[64] = {};
+  if (first_on_device(attr)) {
+    e = cudaFuncSetAttribute(wide_q6k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kQ6SmemBytes);
+    if (e != cudaSuccess) return e;
+  }
+  int* flag = wide_timeout_flag();
+  if (!flag) return cudaErrorInvalidDevice;
+  static const int test_skip = getenv("IQ_WIDE_TEST_TIMEOUT") ? 1 : 0;
+  const dim3 grid((unsigned)((ntok + 127) / 128), (unsigned)((rows + 127) / 128));
+  wide_q6k_kernel<<<grid, kThreads, kQ6SmemBytes, st>>>(mlo, mhi, mx, md, mt, nb * 208, (int)rows, nb, ntok, y,
+                                                        out_ld, flag, test_skip);
+  return cudaGetLastError();
 }
 
 }  // namespace iq

@@ -89,24 +89,28 @@ def test_wide_rows_do_not_depend_on_their_neighbours_at_full_width(cuda):
 @pytest.mark.parametrize("rows,cols,n", [
     (128, 256, 1), (200, 512, 37), (128, 1024, 64), (300, 256, 129), (1000, 2048, 300),
 ])
-def test_wide_q4k_matches_the_oracle_bitwise(cuda, rows, cols, n):
-    """Q4_K x Q8_K: scale-folded f16 operands, split half-block accumulators
-    and the min term on the tensor cores, bitwise the one-chunk order."""
+@pytest.mark.parametrize("dt", [Q.Q4_K, Q.Q6_K])
+def test_wide_kquant_matches_the_oracle_bitwise(cuda, dt, rows, cols, n):
+    """K-quants x Q8_K: scale-folded f16 operands (Q4_K: sc*q with split
+    half-block accumulators and the min term; Q6_K: the scale split into
+    16*sh + sl, two accumulators) on the tensor cores, bitwise the one-chunk
+    order."""
     g = torch.Generator().manual_seed(rows + 7 * n)
-    w = Q.encode(torch.randn(rows, cols, generator=g) * 0.02, Q.Q4_K).numpy()
+    w = Q.encode(torch.randn(rows, cols, generator=g) * 0.02, dt).numpy()
     x = _inputs(n, cols, n + 1)
-    m = _lib.Matrix(Q.Q4_K, w, rows, cols)
+    m = _lib.Matrix(dt, w, rows, cols)
     got = m.forward_wide(torch.from_numpy(x).cuda()).cpu().numpy()
-    ref = oracle.qmatvec(Q.Q4_K, w, rows, cols, x, order=1, ksplit=1)
+    ref = oracle.qmatvec(dt, w, rows, cols, x, order=1, ksplit=1)
     bad = np.argwhere(got.view(np.uint32) != ref.view(np.uint32))
     assert len(bad) == 0, (len(bad), bad[:5], np.abs(got - ref).max())
 
 
-def test_wide_q4k_at_full_width_equals_rows_run_alone(cuda):
+@pytest.mark.parametrize("dt", [Q.Q4_K, Q.Q6_K])
+def test_wide_kquant_at_full_width_equals_rows_run_alone(cuda, dt):
     rows, cols, n = 4096, 2048, 512
     g = torch.Generator(device="cuda").manual_seed(12)
-    w = Q.encode(torch.randn(rows, cols, device="cuda", generator=g) * 0.02, Q.Q4_K)
-    m = _lib.Matrix(Q.Q4_K, w, rows, cols)
+    w = Q.encode(torch.randn(rows, cols, device="cuda", generator=g) * 0.02, dt)
+    m = _lib.Matrix(dt, w, rows, cols)
     x = torch.randn(n, cols, device="cuda", generator=g)
     y = m.forward_wide(x)
     for i in (0, 63, 64, 511):
@@ -114,8 +118,8 @@ def test_wide_q4k_at_full_width_equals_rows_run_alone(cuda):
 
 
 def test_wide_rejects_what_it_does_not_support(cuda):
-    w = Q.encode(torch.randn(64, 256) * 0.02, Q.Q6_K).numpy()
-    m = _lib.Matrix(Q.Q6_K, w, 64, 256)
+    w = Q.encode(torch.randn(64, 256) * 0.02, Q.Q5_K).numpy()
+    m = _lib.Matrix(Q.Q5_K, w, 64, 256)
     with pytest.raises(_lib.IqError):
         m.forward_wide(torch.zeros(4, 256, device="cuda"))
     w8 = _weights(64, 128, 1)
