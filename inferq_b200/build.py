@@ -21,7 +21,7 @@ BUILD = PKG / "_build"
 LIB = PKG / "libiq.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
+NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-ffp-contract=off", "--expt-relaxed-constexpr",
               "-I" + str(ROOT / "include"), "-I" + str(CSRC)]
 
 

@@ -16,7 +16,7 @@
 namespace iq {
 namespace {
 
-__device__ __forceinline__ float sigmoidf_ref(float v) { return __fdiv_rn(1.f, __fadd_rn(1.f, expf(-v))); }
+__device__ __forceinline__ float sigmoidf_ref(float v) { return __fdiv_rn(1.f, __fadd_rn(1.f, exp_ref(-v))); }
 
 // converted_norm + apply_rope on one head vector held in smem `v` (hd floats).
 __device__ void norm_rope(float* v, const float* w, int hd, int rd, double theta, float eps, int position) {
@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(256) attn_scan_kernel(AttnArgs a) {
     float m = sc;
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float e = valid ? expf(sc - m) : 0.f;
+    const float e = valid ? exp_ref(sc - m) : 0.f;
     float l = e;
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a) {
 #pragma unroll 8
   for (int c = 0; c < nchunks; c++) {
     const float* pc = part + c * (a.hd + 2);
-    const float w = expf(pc[0] - M);
+    const float w = exp_ref(pc[0] - M);
     L = fmaf(pc[1], w, L);
     o = fmaf(pc[2 + i], w, o);
   }

@@ -4,20 +4,30 @@
 // conv + SiLU, per-key-head L2 norm, beta = sigmoid(b),
 // g = ssm_a * softplus(a + dt_bias)) and the recurrence of
 // src/qwen/deltanet.rs:122-217 (S *= exp(g); pred = S^T k;
-// delta = (v - pred) * beta; S += k delta^T; o = S^T q / sqrt(dk)).
+// delta = (v - pred) * beta; S += k delta^T; o = sum_i S[i,:] q[i] / sqrt(dk)).
 //
-// Grid: one CTA per (value head, 16-column slice of the value dimension).
-// The delta rule is separable over value columns, so a slice's dk x 16 state
-// block lives in registers for the whole pass: warp w owns columns 2w, 2w+1,
-// lane = (column, group of dk/16 key rows), and the sums over key rows are
-// shuffles inside the warp.  The conv outputs of a row are shared through a
-// double-buffered shared row, so a row costs one CTA barrier.  Rows are
-// processed serially inside the CTA, so a row's result never depends on how
-// many rows the pass holds.
+// Summation order is the reference's: every sum over key rows (pred, o) and
+// over a head's elements (the L2 norms) runs sequentially from element 0,
+// each product rounded before it is added (deltanet.rs:187-216,
+// quantized_deltanet.rs:724-731).  So one thread owns one value column j and
+// walks the dk key rows of S[:, j] in order, with the column in registers.
 //
-// Rollback: the state lives in a ring of kStateRing buffers.  A pass reads
-// buffer `cur` and writes the state after its row t to buffer cur+1+t, so
-// committing c rows (any c <= rows) only moves `cur` by c.
+// Grid: one CTA per value head, dv/32 warps; warp w owns columns
+// 32w .. 32w+31.  The conv, the norms and beta/g of all the pass's rows are
+// computed first by the whole CTA (they do not depend on the state); then
+// each warp runs the rows: the o-sum of row t and the pred-sum of row t+1
+// walk the key rows in the same loop (two independent chains).
+//
+// Rollback without state copies: the recurrent state is one buffer per layer
+// (the state before the last pass) plus, per row of the last pass, an update
+// record {normalized k, delta, decay} per value head.  A row's update is
+// S = (S * decay) + k delta^T (two roundings per element), so replaying the
+// first `pending` records reproduces the state after those rows bit for bit.
+// The next pass replays the committed rows of the previous one into the base
+// buffer before its own rows (ahead of the programmatic-dependency wait, so
+// it overlaps the projection GEMV).  The conv state (small) keeps a ring of
+// kStateRing buffers: a pass reads slot `cur` and writes the state after its
+// row t to slot cur+1+t, and committing c rows moves `cur` by c.
 #include "kernels.cuh"
 #include "model_kernels.cuh"
 #include "devfns.cuh"
@@ -25,165 +35,209 @@
 namespace iq {
 namespace {
 
-__device__ __forceinline__ float sigmoid_ref(float v) { return __fdiv_rn(1.f, __fadd_rn(1.f, expf(-v))); }
+__device__ __forceinline__ float sigmoid_ref(float v) { return __fdiv_rn(1.f, __fadd_rn(1.f, exp_ref(-v))); }
 
 __device__ __forceinline__ float softplus_ref(float v) {
   if (v > 20.f) return v;
-  if (v < -20.f) return expf(v);
-  return log1pf(expf(v));
+  if (v < -20.f) return exp_ref(v);
+  return log1p_ref(exp_ref(v));
 }
 
-constexpr int kMaxRowsDn = 8;
-
-template <int K, int COLS>  // conv kernel width; value columns per CTA (32 or 16)
-__global__ void __launch_bounds__(256) deltanet_kernel(DeltaNetArgs a) {
-  pdl_wait();
-  pdl_trigger();
-  const int layer = blockIdx.y;
-  const DeltaNetLayer& L = a.layers[layer];
-  constexpr int CPW = COLS / 8;        // columns per warp
-  constexpr int GROUPS = 32 / CPW;     // key-row groups per column (lanes)
-  const int slices = a.dv / COLS;
-  const int vh = blockIdx.x / slices;
-  const int slice = blockIdx.x % slices;
+// DK key rows, DV value columns per head (32 * warps), conv width K.
+template <int DK, int DV, int K>
+__global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
+  constexpr int NT = DV;               // threads
+  constexpr int NCH = 2 * DK + DV;     // conv channels of this head: q | k | v
+  constexpr int CPT = (NCH + NT - 1) / NT;
+  constexpr int QS = DK + 4;           // padded row of q/k in shared memory
+  const DeltaNetLayer& L = *a.layers;
+  const int vh = blockIdx.x;
   const int ratio = a.nv / a.nk;
   const int kh = a.tiled_heads ? vh % a.nk : vh / ratio;
   const int rep = a.tiled_heads ? vh / a.nk : vh % ratio;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int key_dim = a.nk * a.dk;
-  const int rows_i = a.dk / GROUPS;  // key rows per lane
-  const int c4 = lane % CPW, rg = lane / CPW;
-  const int j = slice * COLS + CPW * warp + c4;  // value column of this lane
-  const int kr0 = rg * rows_i;               // first key row of this lane
-  const int cur = *a.cur;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int j = tid;                   // value column of this thread
+  const int key_dim = a.nk * DK;
   const int rows = a.rows;
+  const int rec_stride = a.rec_stride;
+  float* rec_head = L.rec_log + (int64_t)vh * kMaxRowsDelta * rec_stride;  // [row][k DK | delta DV | decay]
+  float* base = L.rec_state + (int64_t)vh * DK * DV + j;
 
-  // per row t (double-buffered by t & 1): conv outputs q | k | v(32 columns)
-  __shared__ float qkv[2][2 * 128 + 32];
-  __shared__ float bg[2][2];
-  const int nqk = 2 * a.dk;
-  const int nch = nqk + COLS;
+  // ---- before the dependency wait: state column, replay of the committed
+  // rows of the previous pass, conv weights and history (none of them is
+  // written by the kernels this pass runs before this one)
+  float S[DK];
+#pragma unroll
+  for (int i = 0; i < DK; i++) S[i] = base[(int64_t)i * DV];
+  const int pend = *a.pending;
+  for (int r = 0; r < pend; r++) {
+    const float* rc = rec_head + (int64_t)r * rec_stride;
+    const float decay = rc[DK + DV], delta = rc[DK + j];
+#pragma unroll
+    for (int i = 0; i < DK; i++) S[i] = __fadd_rn(__fmul_rn(S[i], decay), __fmul_rn(rc[i], delta));
+  }
+  if (pend > 0) {
+#pragma unroll
+    for (int i = 0; i < DK; i++) base[(int64_t)i * DV] = S[i];
+  }
+  const int cur = *a.cur;
   auto chan = [&](int c) {
-    if (c < a.dk) return kh * a.dk + c;
-    if (c < nqk) return key_dim + kh * a.dk + (c - a.dk);
-    return 2 * key_dim + vh * a.dv + slice * COLS + (c - nqk);
+    if (c < DK) return kh * DK + c;
+    if (c < 2 * DK) return key_dim + kh * DK + (c - DK);
+    return 2 * key_dim + vh * DV + (c - 2 * DK);
   };
-  // every input of the pass, requested before any arithmetic and parked in
-  // shared memory: thread t owns conv channels t and t+256; thread 0 also
-  // reads beta/alpha
-  __shared__ float xin_s[kMaxRowsDn][2 * 128 + 32];
-  __shared__ float ba_s[kMaxRowsDn][2];
-  float cw[2][4], hist[2][3];
+  float cw[CPT][4], hist[CPT][3];
   const float* cin = L.conv_state[cur];
-  {
-    float xin[kMaxRowsDn][2];
 #pragma unroll
-    for (int u = 0; u < 2; u++) {
-      const int c = threadIdx.x + 256 * u;
-      const bool own = c < nch;
-      const int g = own ? chan(c) : 0;
+  for (int u = 0; u < CPT; u++) {
+    const int c = tid + NT * u;
+    const bool own = c < NCH;
+    const int g = own ? chan(c) : 0;
 #pragma unroll
-      for (int t = 0; t < kMaxRowsDn; t++) xin[t][u] = (own && t < rows) ? a.qkv[(int64_t)t * a.qkv_ld + g] : 0.f;
+    for (int tp = 0; tp < 4; tp++) cw[u][tp] = (own && tp < K) ? L.conv_w[(int64_t)g * K + tp] : 0.f;
 #pragma unroll
-      for (int tp = 0; tp < 4; tp++) cw[u][tp] = (own && tp < K) ? L.conv_w[(int64_t)g * K + tp] : 0.f;
-#pragma unroll
-      for (int tp = 0; tp < 3; tp++) hist[u][tp] = (own && tp < K - 1) ? cin[(int64_t)g * (K - 1) + tp] : 0.f;
-    }
-    if (threadIdx.x < 2 * kMaxRowsDn) {
-      const int t = threadIdx.x >> 1;
-      int idx = (threadIdx.x & 1) ? a.nv + vh : vh;
-      if (a.ba_interleaved) idx = kh * 2 * ratio + ((threadIdx.x & 1) ? ratio : 0) + rep;
-      if (t < rows) ba_s[t][threadIdx.x & 1] = a.ba[(int64_t)t * a.ba_ld + idx];
-    }
-#pragma unroll
-    for (int u = 0; u < 2; u++) {
-      const int c = threadIdx.x + 256 * u;
-      if (c < nch)
-#pragma unroll
-        for (int t = 0; t < kMaxRowsDn; t++) xin_s[t][c] = xin[t][u];
-    }
+    for (int tp = 0; tp < 3; tp++) hist[u][tp] = (own && tp < K - 1) ? cin[(int64_t)g * (K - 1) + tp] : 0.f;
   }
   const float ssm_a = L.ssm_a[vh], dt_bias = L.dt_bias[vh];
-  float S[16];
-  const float* sin_ = L.rec_state[cur] + (int64_t)vh * a.dk * a.dv;
-#pragma unroll
-  for (int r = 0; r < 16; r++) S[r] = r < rows_i ? sin_[(int64_t)(kr0 + r) * a.dv + j] : 0.f;
-  const float qscale = __fdiv_rn(1.f, sqrtf((float)a.dk));
-  const bool qk_writer = rep == 0 && slice == 0;
-  __syncthreads();  // ba_s is written by threads 0..15 and read by thread 0
+  // (the replay's reads of this head's records precede the record writes
+  // below: every thread passes the CTA barriers in between)
 
+  pdl_wait();
+  pdl_trigger();
+
+  __shared__ __align__(16) float qk[kMaxRowsDelta][2][QS];  // conv outputs, then normalized q and k
+  __shared__ float vs[kMaxRowsDelta][DV];
+  __shared__ float beta_s[kMaxRowsDelta], decay_s[kMaxRowsDelta];
+  // every input of the pass requested before any arithmetic
+  float xin[CPT][kMaxRowsDelta];
+#pragma unroll
+  for (int u = 0; u < CPT; u++) {
+    const int c = tid + NT * u;
+    const bool own = c < NCH;
+    const int g = own ? chan(c) : 0;
+#pragma unroll
+    for (int t = 0; t < kMaxRowsDelta; t++) xin[u][t] = (own && t < rows) ? a.qkv[(int64_t)t * a.qkv_ld + g] : 0.f;
+  }
+  float bin = 0.f, ain = 0.f;
+  if (tid < rows) {
+    int bi = vh, ai = a.nv + vh;
+    if (a.ba_interleaved) {
+      bi = kh * 2 * ratio + rep;
+      ai = kh * 2 * ratio + ratio + rep;
+    }
+    bin = a.ba[(int64_t)tid * a.ba_ld + bi];
+    ain = a.ba[(int64_t)tid * a.ba_ld + ai];
+  }
+  // causal depthwise conv + SiLU per channel and row (quantized_deltanet.rs:733-759)
+  const bool qk_writer = rep == 0;
+#pragma unroll
+  for (int u = 0; u < CPT; u++) {
+    const int c = tid + NT * u;
+    if (c >= NCH) continue;
+#pragma unroll
+    for (int t = 0; t < kMaxRowsDelta; t++) {
+      if (t >= rows) break;
+      const float x = xin[u][t];
+      float sum = __fmul_rn(cw[u][K - 1], x);
+#pragma unroll
+      for (int tp = 0; tp < K - 1; tp++) sum = __fadd_rn(sum, __fmul_rn(cw[u][tp], hist[u][tp]));
+      const float y = __fmul_rn(sum, sigmoid_ref(sum));
+      if (c < 2 * DK) qk[t][c / DK][c % DK] = y;
+      else vs[t][c - 2 * DK] = y;
+#pragma unroll
+      for (int tp = 0; tp + 1 < K - 1; tp++) hist[u][tp] = hist[u][tp + 1];
+      if (K > 1) hist[u][K - 2] = x;
+      if (c >= 2 * DK || qk_writer) {
+        float* co = L.conv_state[(cur + 1 + t) % kStateRing] + (int64_t)chan(c) * (K - 1);
+#pragma unroll
+        for (int tp = 0; tp < K - 1; tp++) co[tp] = hist[u][tp];
+      }
+    }
+  }
+  if (tid < rows) {
+    beta_s[tid] = sigmoid_ref(bin);
+    decay_s[tid] = exp_ref(__fmul_rn(ssm_a, softplus_ref(__fadd_rn(ain, dt_bias))));
+  }
+  __syncthreads();
+  // L2 norms: x * (sum x^2 + 1e-6)^-1/2 with the sum in element order
+  // (quantized_deltanet.rs:724-731); one thread per (row, q|k)
+  __shared__ float nscale[kMaxRowsDelta][2];
+  if (tid < 2 * rows) {
+    const float* v = qk[tid >> 1][tid & 1];
+    float ss = 0.f;
+#pragma unroll 8
+    for (int i = 0; i < DK; i++) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+    nscale[tid >> 1][tid & 1] = __fdiv_rn(1.f, sqrtf(__fadd_rn(ss, 1e-6f)));
+  }
+  __syncthreads();
+  for (int e = tid; e < rows * 2 * DK; e += NT) {
+    const int t = e / (2 * DK), w = (e / DK) & 1, i = e % DK;
+    qk[t][w][i] = __fmul_rn(qk[t][w][i], nscale[t][w]);
+  }
+  __syncthreads();
+  // update records of this pass: normalized k and decay (delta below)
+  for (int e = tid; e < rows * DK; e += NT) rec_head[(int64_t)(e / DK) * rec_stride + e % DK] = qk[e / DK][1][e % DK];
+  if (tid < rows) rec_head[(int64_t)tid * rec_stride + DK + DV] = decay_s[tid];
+
+  // ---- the recurrence, one value column per thread
+  const float qscale = __fdiv_rn(1.f, sqrtf((float)DK));
+  float pred = 0.f;
+  {
+    const float decay = decay_s[0];
+    const float4* k4 = reinterpret_cast<const float4*>(qk[0][1]);
+#pragma unroll
+    for (int i4 = 0; i4 < DK / 4; i4++) {
+      const float4 kv = k4[i4];
+      const float kk[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        S[4 * i4 + e] = __fmul_rn(S[4 * i4 + e], decay);
+        pred = __fadd_rn(pred, __fmul_rn(S[4 * i4 + e], kk[e]));
+      }
+    }
+  }
   for (int t = 0; t < rows; t++) {
-    const int buf = t & 1;
-    const int snap = (cur + 1 + t) % kStateRing;
-    // causal depthwise conv + SiLU (src/qwen/quantized_deltanet.rs:733-759)
+    const float delta = __fmul_rn(__fsub_rn(vs[t][j], pred), beta_s[t]);
+    rec_head[(int64_t)t * rec_stride + DK + j] = delta;
+    const float4* k4 = reinterpret_cast<const float4*>(qk[t][1]);
+    const float4* q4 = reinterpret_cast<const float4*>(qk[t][0]);
+    float o = 0.f;
+    if (t + 1 < rows) {
+      // S += k delta^T and o-sum of row t; decay and pred-sum of row t+1
+      const float4* n4 = reinterpret_cast<const float4*>(qk[t + 1][1]);
+      const float decay = decay_s[t + 1];
+      float pn = 0.f;
 #pragma unroll
-    for (int u = 0; u < 2; u++) {
-      const int c = threadIdx.x + 256 * u;
-      if (c < nch) {
-        const float x = xin_s[t][c];
-        float sum = __fmul_rn(cw[u][K - 1], x);
+      for (int i4 = 0; i4 < DK / 4; i4++) {
+        const float4 kv = k4[i4], qv = q4[i4], nv = n4[i4];
+        const float kk[4] = {kv.x, kv.y, kv.z, kv.w}, qq[4] = {qv.x, qv.y, qv.z, qv.w};
+        const float nn[4] = {nv.x, nv.y, nv.z, nv.w};
 #pragma unroll
-        for (int tp = 0; tp < K - 1; tp++) sum = __fadd_rn(sum, __fmul_rn(cw[u][tp], hist[u][tp]));
-        qkv[buf][c] = __fmul_rn(sum, sigmoid_ref(sum));
+        for (int e = 0; e < 4; e++) {
+          float s = __fadd_rn(S[4 * i4 + e], __fmul_rn(kk[e], delta));
+          o = __fadd_rn(o, __fmul_rn(__fmul_rn(s, qq[e]), qscale));
+          s = __fmul_rn(s, decay);
+          pn = __fadd_rn(pn, __fmul_rn(s, nn[e]));
+          S[4 * i4 + e] = s;
+        }
+      }
+      pred = pn;
+    } else {
 #pragma unroll
-        for (int tp = 0; tp + 1 < K - 1; tp++) hist[u][tp] = hist[u][tp + 1];
-        if (K > 1) hist[u][K - 2] = x;
-        if (c >= nqk || qk_writer) {
-          float* co = L.conv_state[snap] + (int64_t)chan(c) * (K - 1);
+      for (int i4 = 0; i4 < DK / 4; i4++) {
+        const float4 kv = k4[i4], qv = q4[i4];
+        const float kk[4] = {kv.x, kv.y, kv.z, kv.w}, qq[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
-          for (int tp = 0; tp < K - 1; tp++) co[tp] = hist[u][tp];
+        for (int e = 0; e < 4; e++) {
+          const float s = __fadd_rn(S[4 * i4 + e], __fmul_rn(kk[e], delta));
+          o = __fadd_rn(o, __fmul_rn(__fmul_rn(s, qq[e]), qscale));
+          S[4 * i4 + e] = s;
         }
       }
     }
-    if (threadIdx.x == 0) {
-      bg[buf][0] = sigmoid_ref(ba_s[t][0]);
-      bg[buf][1] = __fmul_rn(ssm_a, softplus_ref(__fadd_rn(ba_s[t][1], dt_bias)));
-    }
-    __syncthreads();
-    // L2 norms of q and k (x * (sum x^2 + 1e-6)^-1/2), every warp for itself
-    const float* q = qkv[buf];
-    const float* kk = qkv[buf] + a.dk;
-    float sq = 0.f, sk = 0.f;
-    for (int i = lane; i < a.dk; i += 32) {
-      sq = fmaf(q[i], q[i], sq);
-      sk = fmaf(kk[i], kk[i], sk);
-    }
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) {
-      sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, m));
-      sk = __fadd_rn(sk, __shfl_xor_sync(0xffffffffu, sk, m));
-    }
-    const float nq = __fdiv_rn(1.f, sqrtf(__fadd_rn(sq, 1e-6f)));
-    const float nk = __fdiv_rn(1.f, sqrtf(__fadd_rn(sk, 1e-6f)));
-    const float beta = bg[buf][0], decay = expf(bg[buf][1]);
-    const float vcol = qkv[buf][nqk + CPW * warp + c4];
-    // recurrence over this lane's key rows, reduced across the 8 row groups
-    float kv[16], pred = 0.f;
-#pragma unroll
-    for (int r = 0; r < 16; r++) {
-      if (r < rows_i) {
-        kv[r] = __fmul_rn(kk[kr0 + r], nk);
-        S[r] = __fmul_rn(S[r], decay);
-        pred = fmaf(S[r], kv[r], pred);
-      }
-    }
-#pragma unroll
-    for (int m = CPW; m <= 16; m <<= 1) pred = __fadd_rn(pred, __shfl_xor_sync(0xffffffffu, pred, m));
-    const float delta = __fmul_rn(__fsub_rn(vcol, pred), beta);
-    float o = 0.f;
-    float* sout = L.rec_state[snap] + (int64_t)vh * a.dk * a.dv;
-#pragma unroll
-    for (int r = 0; r < 16; r++) {
-      if (r < rows_i) {
-        S[r] = fmaf(kv[r], delta, S[r]);
-        o = fmaf(S[r], __fmul_rn(q[kr0 + r], nq), o);
-        sout[(int64_t)(kr0 + r) * a.dv + j] = S[r];
-      }
-    }
-#pragma unroll
-    for (int m = CPW; m <= 16; m <<= 1) o = __fadd_rn(o, __shfl_xor_sync(0xffffffffu, o, m));
-    if (rg == 0) a.out[(int64_t)t * a.out_ld + vh * a.dv + j] = __fmul_rn(o, qscale);
+    a.out[(int64_t)t * a.out_ld + vh * DV + j] = o;
   }
+  (void)lane;
 }
 
 // Gated RMSNorm of every value head (src/qwen/norm.rs:16-25:
@@ -229,7 +283,7 @@ __global__ void __launch_bounds__(256) gated_norm_kernel(GatedNormArgs a) {
     const float den = sqrtf(__fadd_rn(__fmul_rn(ss, a.inv_dv), a.eps));
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-      const float silu = __fdiv_rn(zv[j][i], __fadd_rn(1.f, expf(-zv[j][i])));
+      const float silu = __fdiv_rn(zv[j][i], __fadd_rn(1.f, exp_ref(-zv[j][i])));
       v[j][i] = __fmul_rn(__fmul_rn(__fdiv_rn(v[j][i], den), wv[j][i]), silu);
     }
   }
@@ -237,35 +291,45 @@ __global__ void __launch_bounds__(256) gated_norm_kernel(GatedNormArgs a) {
                    a.q80 ? a.q80 + (int64_t)row * a.q80_stride : nullptr, nullptr, xs);
 }
 
+template <int DK, int DV>
+cudaError_t deltanet_launch_k(const DeltaNetArgs& a, cudaLaunchConfig_t& cfg) {
+  switch (a.conv_k) {
+    case 1: return cudaLaunchKernelEx(&cfg, deltanet_kernel<DK, DV, 1>, a);
+    case 2: return cudaLaunchKernelEx(&cfg, deltanet_kernel<DK, DV, 2>, a);
+    case 3: return cudaLaunchKernelEx(&cfg, deltanet_kernel<DK, DV, 3>, a);
+    default: return cudaLaunchKernelEx(&cfg, deltanet_kernel<DK, DV, 4>, a);
+  }
+}
+
 }  // namespace
 
-cudaError_t deltanet_launch(const DeltaNetArgs& a, int nlayers, cudaStream_t st, bool pdl) {
-  if (a.rows < 1 || a.rows > kMaxRowsDn || a.rows >= kStateRing || a.dk > 128 || a.dk % 32 || a.dv % 32 ||
-      a.conv_k > 4 || a.conv_k < 1)
+int deltanet_rec_stride(int dk, int dv) { return (int)align_up(dk + dv + 1, 4); }
+
+bool deltanet_supported(int dk, int dv) {
+  // (dk 128 with dv 32 would hold too many conv inputs per thread)
+  return (dk == 32 || dk == 64 || dk == 128) && (dv == 32 || dv == 64 || dv == 128) && !(dk == 128 && dv == 32);
+}
+
+cudaError_t deltanet_launch(const DeltaNetArgs& a, cudaStream_t st, bool pdl) {
+  if (a.rows < 1 || a.rows > kMaxRowsDelta || a.rows >= kStateRing || !deltanet_supported(a.dk, a.dv) ||
+      a.conv_k > 4 || a.conv_k < 1 || a.rec_stride != deltanet_rec_stride(a.dk, a.dv))
     return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  // 16 value columns per CTA: 2 CTAs per SM at 35B shapes, 8 key rows a lane
-  const int cols = 16;
-  cfg.gridDim = dim3(a.nv * (a.dv / cols), nlayers);
-  cfg.blockDim = dim3(256);
+  cfg.gridDim = dim3(a.nv);
+  cfg.blockDim = dim3(a.dv);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (cols == 16) switch (a.conv_k) {
-      case 1: return cudaLaunchKernelEx(&cfg, deltanet_kernel<1, 16>, a);
-      case 2: return cudaLaunchKernelEx(&cfg, deltanet_kernel<2, 16>, a);
-      case 3: return cudaLaunchKernelEx(&cfg, deltanet_kernel<3, 16>, a);
-      default: return cudaLaunchKernelEx(&cfg, deltanet_kernel<4, 16>, a);
-    }
-  switch (a.conv_k) {
-    case 1: return cudaLaunchKernelEx(&cfg, deltanet_kernel<1, 32>, a);
-    case 2: return cudaLaunchKernelEx(&cfg, deltanet_kernel<2, 32>, a);
-    case 3: return cudaLaunchKernelEx(&cfg, deltanet_kernel<3, 32>, a);
-    default: return cudaLaunchKernelEx(&cfg, deltanet_kernel<4, 32>, a);
-  }
+#define IQ_DN_CASE(dk_, dv_) \
+  if (a.dk == dk_ && a.dv == dv_) return deltanet_launch_k<dk_, dv_>(a, cfg);
+  IQ_DN_CASE(128, 128) IQ_DN_CASE(128, 64)
+  IQ_DN_CASE(64, 128) IQ_DN_CASE(64, 64) IQ_DN_CASE(64, 32)
+  IQ_DN_CASE(32, 128) IQ_DN_CASE(32, 64) IQ_DN_CASE(32, 32)
+#undef IQ_DN_CASE
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t gated_norm_launch(const GatedNormArgs& a, int rows, cudaStream_t st, bool pdl) {

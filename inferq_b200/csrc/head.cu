@@ -46,8 +46,8 @@ __device__ __forceinline__ Best merge(Best a, Best b, bool scores) {
     r.v2 = fmaxf(a.v2, b.i >= 0 ? b.v : -INFINITY);
   }
   if (scores) {
-    const float ea = a.i >= 0 ? __fmul_rn(a.se, expf(a.v - r.v)) : 0.f;
-    const float eb = b.i >= 0 ? __fmul_rn(b.se, expf(b.v - r.v)) : 0.f;
+    const float ea = a.i >= 0 ? __fmul_rn(a.se, exp_ref(a.v - r.v)) : 0.f;
+    const float eb = b.i >= 0 ? __fmul_rn(b.se, exp_ref(b.v - r.v)) : 0.f;
     r.se = __fadd_rn(ea, eb);
   } else {
     r.se = 0.f;
@@ -140,11 +140,12 @@ __global__ void __launch_bounds__(256) accept_kernel(HeadArgs a) {
 
 // Keep the first result[2] rows of the pass: advance the DeltaNet state ring
 // to the state after that row and the KV position past it.
-__global__ void commit_kernel(int* cur, int* pos, const int* result) {
+__global__ void commit_kernel(int* cur, int* pos, int* pending, const int* result) {
   pdl_wait();
   pdl_trigger();
   *cur = (*cur + result[2]) % kStateRing;
   *pos += result[2];
+  *pending = result[2];
 }
 
 // One MTP draft step's bookkeeping: the drafted token (row 0's argmax)
@@ -194,8 +195,8 @@ cudaError_t accept_launch(const HeadArgs& a, cudaStream_t st, bool pdl) {
   return launch_pdl(accept_kernel, dim3(1), dim3(256), 0, st, pdl, a);
 }
 
-cudaError_t commit_launch(int* cur, int* pos, const int* result, cudaStream_t st, bool pdl) {
-  return launch_pdl(commit_kernel, dim3(1), dim3(1), 0, st, pdl, cur, pos, result);
+cudaError_t commit_launch(int* cur, int* pos, int* pending, const int* result, cudaStream_t st, bool pdl) {
+  return launch_pdl(commit_kernel, dim3(1), dim3(1), 0, st, pdl, cur, pos, pending, result);
 }
 
 }  // namespace iq

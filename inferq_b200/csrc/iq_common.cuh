@@ -74,6 +74,16 @@ inline bool first_on_device(bool (&done)[64]) {
   return true;
 }
 
+// exp and log1p of an f32 argument evaluated in double precision and rounded
+// once to f32.  That is the correctly rounded f32 result except in
+// vanishingly rare near-halfway cases, which is what the reference's libm
+// expf / log1pf return in practice (within about half an ulp), so the model
+// kernels and the reference agree on these to the bit.  (CUDA's single-
+// precision expf may differ from it by an ulp or two, and a last-bit
+// difference can flip a later activation rounding.)
+__device__ __forceinline__ float exp_ref(float x) { return (float)exp((double)x); }
+__device__ __forceinline__ float log1p_ref(float x) { return (float)log1p((double)x); }
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 

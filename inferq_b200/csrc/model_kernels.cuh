@@ -5,20 +5,24 @@
 namespace iq {
 
 // ----------------------------------------------------------------- DeltaNet
-// DeltaNet state buffers per layer: a ring holding the state before a pass
-// and after each of its rows (so it must exceed the rows of a pass).
+// DeltaNet state per layer: the conv state in a ring holding the state
+// before a pass and after each of its rows (so it must exceed the rows of a
+// pass); the recurrent state as one base buffer plus the update records of
+// the last pass's rows (see deltanet.cu).
 constexpr int kStateRing = 9;
+constexpr int kMaxRowsDelta = 8;
 
 struct DeltaNetLayer {
   float* conv_state[kStateRing];  // [conv_dim][K-1]
-  float* rec_state[kStateRing];   // [nv][dk][dv]
+  float* rec_state;       // [nv][dk][dv]: the state before the `pending` records
+  float* rec_log;         // [nv][kMaxRowsDelta][rec_stride]: k[dk] | delta[dv] | decay per row
   const float* conv_w;    // [conv_dim][K]
   const float* ssm_a;     // [nv]  (already -exp(A_log))
   const float* dt_bias;   // [nv]
 };
 
 struct DeltaNetArgs {
-  const DeltaNetLayer* layers;  // device array, gridDim.y entries
+  const DeltaNetLayer* layers;  // device pointer to this layer's entry
   const float* qkv;             // projections [rows][qkv_ld] (first conv_dim cols)
   int qkv_ld;
   const float* ba;              // beta/alpha projections [rows][ba_ld]
@@ -29,9 +33,13 @@ struct DeltaNetArgs {
   int nk, nv, dk, dv, conv_k;
   int tiled_heads;              // value head layout: 1 TiledByRepeat, 0 GroupedByKeyHead
   int ba_interleaved;           // 1: ssm_ba per key head, 0: beta rows then alpha rows
-  const int* cur;               // device: ring index of the current state
+  int rec_stride;               // deltanet_rec_stride(dk, dv)
+  const int* cur;               // device: conv ring index of the current state
+  const int* pending;           // device: records of the last pass still to replay
 };
-cudaError_t deltanet_launch(const DeltaNetArgs& a, int nlayers, cudaStream_t st, bool pdl);
+int deltanet_rec_stride(int dk, int dv);
+bool deltanet_supported(int dk, int dv);
+cudaError_t deltanet_launch(const DeltaNetArgs& a, cudaStream_t st, bool pdl);
 
 struct GatedNormArgs {
   const float* o;  int o_ld;
@@ -169,8 +177,9 @@ cudaError_t mtp_step_launch(const MtpStepArgs& a, cudaStream_t st, bool pdl);
 cudaError_t set_int_launch(int* p, int v, bool add, cudaStream_t st, bool pdl);
 cudaError_t accept_launch(const HeadArgs& a, cudaStream_t st, bool pdl);
 
-// cur = (cur + committed) mod kStateRing; pos += committed
-cudaError_t commit_launch(int* cur, int* pos, const int* result, cudaStream_t st, bool pdl);
+// cur = (cur + committed) mod kStateRing; pos += committed;
+// pending = committed (the DeltaNet records the next pass replays)
+cudaError_t commit_launch(int* cur, int* pos, int* pending, const int* result, cudaStream_t st, bool pdl);
 
 template <class K, class... Args>
 inline cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,

@@ -48,13 +48,15 @@ struct iq_state {
   int last_rows = 0;     // rows of the last iq_forward pass (rollback bound)
   bool can_rollback = false;
   cudaStream_t st = nullptr;
-  // control words: [0]=pos [1]=DeltaNet ring index [2..4]=result [5]=MTP pos
+  // control words: [0]=pos [1]=DeltaNet conv ring index [2..4]=result
+  // [5]=MTP pos [6]=DeltaNet update records still to replay (pending)
   iq::DevBuf ctrl;
   int* h_result = nullptr;   // pinned [4]
   int32_t* h_tokens = nullptr;  // pinned [8]
   iq::DevBuf tokens;
   // DeltaNet
-  std::vector<iq::DevBuf> conv, rec;  // 2 per linear layer
+  std::vector<iq::DevBuf> conv;       // kStateRing per linear layer
+  std::vector<iq::DevBuf> rec, rec_log;  // per linear layer: base state, update records
   std::vector<iq::DevBuf> dn_qkv, dn_ba;  // per linear layer pass projections
   iq::DevBuf dn_layers;  // DeltaNetLayer[n_linear]
   // attention
@@ -180,7 +182,8 @@ struct Ctx {
   }
   int* pos() const { return s->ctrl.as<int>(); }
   int* attn_pos = nullptr;  // KV position the attention layers use (default pos())
-  int* cur() const { return s->ctrl.as<int>() + 1; }  // DeltaNet state ring index
+  int* cur() const { return s->ctrl.as<int>() + 1; }  // DeltaNet conv ring index
+  int* pending() const { return s->ctrl.as<int>() + 6; }  // DeltaNet records to replay
   int* result() const { return s->ctrl.as<int>() + 2; }
   const uint8_t* act(int dt) const { return dt == Q8_0 ? s->act80.as<uint8_t>() : s->act8k.as<uint8_t>(); }
   int64_t arb(int dt) const { return dt == Q8_0 ? s->act80_bytes : s->act8k_bytes; }
@@ -522,9 +525,11 @@ int run_delta(Ctx& x, const Layer& L, const LayerRec& R, int k, int li) {
   a.conv_k = c.linear_conv_kernel_dim;
   a.tiled_heads = c.value_heads_tiled;
   a.ba_interleaved = D.ba_fused;
+  a.rec_stride = deltanet_rec_stride(a.dk, a.dv);
   a.cur = x.cur();
+  a.pending = x.pending();
   ++x.s->launch_count;
-  IQ_CUDA(deltanet_launch(a, 1, x.st, x.pdl));
+  IQ_CUDA(deltanet_launch(a, x.st, x.pdl));
   x.mark("dn.recurrence");
   GatedNormArgs g = {};
   g.o = s->dn_out.as<float>();
@@ -614,10 +619,12 @@ int run_attention(Ctx& x, const Layer& L, const LayerRec& R, int k, int fi) {
 }
 
 // Undo the last pass down to `committed` of its `rows` rows: the DeltaNet
-// state after that row is already in the ring, the KV cache is truncated.
+// conv state after that row is already in the ring, the recurrent state is
+// the base plus that many update records, the KV cache is truncated.
 __global__ void rollback_kernel(int* ctrl, int rows, int committed) {
   ctrl[1] = (ctrl[1] - rows + committed + 2 * kStateRing) % kStateRing;
   ctrl[0] -= rows - committed;
+  ctrl[6] = committed;
 }
 
 // The pass body shared by forward and verify.
@@ -663,7 +670,7 @@ int run_pass(iq_state* s, int k, bool verify) {
   IQ_CUDA(accept_launch(h, x.st, x.pdl));
   x.mark("head.accept");
   ++x.s->launch_count;
-  IQ_CUDA(commit_launch(x.cur(), x.pos(), x.result(), x.st, x.pdl));
+  IQ_CUDA(commit_launch(x.cur(), x.pos(), x.pending(), x.result(), x.st, x.pdl));
   x.mark("head.commit");
   IQ_CUDA(cudaMemcpyAsync(s->h_result, x.result(), 4 * sizeof(int), cudaMemcpyDeviceToHost, x.st));
   // the GEMVs' bounded-wait status travels back with the result
@@ -870,9 +877,15 @@ int alloc_state(iq_state* s) {
   IQ_CUDA(s->tokens.reserve(kMaxK * sizeof(int32_t)));
   const int64_t K_conv = c.linear_conv_kernel_dim - 1;
   std::vector<DeltaNetLayer> dl;
-  static_assert(kStateRing > kMaxK, "the state ring holds a pass's rows plus the state before it");
+  static_assert(kStateRing > kMaxK, "the conv ring holds a pass's rows plus the state before it");
+  static_assert(kMaxRowsDelta >= kMaxK, "update records cover every row of a pass");
+  IQ_CHECK(m->n_linear == 0 || deltanet_supported(c.linear_key_head_dim, c.linear_value_head_dim), IQ_EUNSUPPORTED,
+           "DeltaNet head dims %d x %d (supported: 32, 64, 128 each)", c.linear_key_head_dim,
+           c.linear_value_head_dim);
+  const int rec_stride = deltanet_rec_stride(c.linear_key_head_dim, c.linear_value_head_dim);
   s->conv.resize(kStateRing * m->n_linear);
-  s->rec.resize(kStateRing * m->n_linear);
+  s->rec.resize(m->n_linear);
+  s->rec_log.resize(m->n_linear);
   s->dn_qkv.resize(m->n_linear);
   s->dn_ba.resize(m->n_linear);
   int li = 0;
@@ -881,12 +894,13 @@ int alloc_state(iq_state* s) {
     DeltaNetLayer d = {};
     for (int b = 0; b < kStateRing; b++) {
       DevBuf& cb = s->conv[kStateRing * li + b];
-      DevBuf& rb = s->rec[kStateRing * li + b];
       IQ_CUDA(cb.reserve(std::max<int64_t>(1, conv_dim * K_conv) * 4));
-      IQ_CUDA(rb.reserve((size_t)c.linear_num_value_heads * c.linear_key_head_dim * c.linear_value_head_dim * 4));
       d.conv_state[b] = cb.as<float>();
-      d.rec_state[b] = rb.as<float>();
     }
+    IQ_CUDA(s->rec[li].reserve((size_t)c.linear_num_value_heads * c.linear_key_head_dim * c.linear_value_head_dim * 4));
+    IQ_CUDA(s->rec_log[li].reserve((size_t)c.linear_num_value_heads * kMaxRowsDelta * rec_stride * 4));
+    d.rec_state = s->rec[li].as<float>();
+    d.rec_log = s->rec_log[li].as<float>();
     d.conv_w = L.dn.conv_w.p();
     d.ssm_a = L.dn.ssm_a.p();
     d.dt_bias = L.dn.dt_bias.p();
@@ -963,6 +977,7 @@ int check_device_waits(iq_state* s) {
 int reset_state(iq_state* s) {
   for (auto& b : s->conv) IQ_CUDA(cudaMemsetAsync(b.p, 0, b.bytes, s->st));
   for (auto& b : s->rec) IQ_CUDA(cudaMemsetAsync(b.p, 0, b.bytes, s->st));
+  for (auto& b : s->rec_log) IQ_CUDA(cudaMemsetAsync(b.p, 0, b.bytes, s->st));
   IQ_CUDA(cudaMemsetAsync(s->ctrl.p, 0, 8 * sizeof(int), s->st));
   IQ_CUDA(cudaStreamSynchronize(s->st));
   s->position = 0;
@@ -1075,8 +1090,13 @@ int iq_state_export(iq_state* s, void* out, int64_t bytes) {
   IQ_CHECK(bytes >= need, IQ_EINVAL, "state image needs %lld bytes, buffer holds %lld", (long long)need,
            (long long)bytes);
   IQ_CUDA(cudaStreamSynchronize(s->st));
-  int cur = 0;
-  IQ_CUDA(cudaMemcpy(&cur, s->ctrl.as<int>() + 1, 4, cudaMemcpyDeviceToHost));
+  int ctrl[8];
+  IQ_CUDA(cudaMemcpy(ctrl, s->ctrl.p, sizeof ctrl, cudaMemcpyDeviceToHost));
+  const int cur = ctrl[1], pending = ctrl[6];
+  const iq_config& c = s->m->cfg;
+  const int dk = c.linear_key_head_dim, dv = c.linear_value_head_dim, nv = c.linear_num_value_heads;
+  const int rec_stride = deltanet_rec_stride(dk, dv);
+  std::vector<float> log;
   uint8_t* p = static_cast<uint8_t*>(out);
   memcpy(p, &h, sizeof h);
   p += sizeof h;
@@ -1091,7 +1111,28 @@ int iq_state_export(iq_state* s, void* out, int64_t bytes) {
     } else {
       const size_t nc = (size_t)h.conv_dim * h.conv_taps * 4, nr = (size_t)h.rec_size * 4;
       if (nc) IQ_CUDA(cudaMemcpy(p, s->conv[kStateRing * li + cur].p, nc, cudaMemcpyDeviceToHost));
-      IQ_CUDA(cudaMemcpy(p + nc, s->rec[kStateRing * li + cur].p, nr, cudaMemcpyDeviceToHost));
+      IQ_CUDA(cudaMemcpy(p + nc, s->rec[li].p, nr, cudaMemcpyDeviceToHost));
+      if (pending > 0) {
+        // the committed rows of the last pass: replay their update records
+        // (S = S * decay + k delta, each product rounded; the host build
+        // does not contract these into fused multiply-adds), as the next
+        // pass would on the device
+        log.resize((size_t)nv * kMaxRowsDelta * rec_stride);
+        IQ_CUDA(cudaMemcpy(log.data(), s->rec_log[li].p, log.size() * 4, cudaMemcpyDeviceToHost));
+        float* S = reinterpret_cast<float*>(p + nc);
+        for (int h = 0; h < nv; h++)
+          for (int r = 0; r < pending; r++) {
+            const float* rc = log.data() + ((size_t)h * kMaxRowsDelta + r) * rec_stride;
+            const float decay = rc[dk + dv];
+            float* Sh = S + (size_t)h * dk * dv;
+            for (int i = 0; i < dk; i++)
+              for (int j = 0; j < dv; j++) {
+                const float a = Sh[(size_t)i * dv + j] * decay;
+                const float b = rc[i] * rc[dk + j];
+                Sh[(size_t)i * dv + j] = a + b;
+              }
+          }
+      }
       p += nc + nr;
       li++;
     }
@@ -1135,7 +1176,7 @@ int iq_state_import(iq_state* s, const void* in, int64_t bytes) {
     } else {
       const size_t nc = (size_t)h.conv_dim * h.conv_taps * 4, nr = (size_t)h.rec_size * 4;
       if (nc) IQ_CUDA(cudaMemcpy(s->conv[kStateRing * li].p, p, nc, cudaMemcpyHostToDevice));
-      IQ_CUDA(cudaMemcpy(s->rec[kStateRing * li].p, p + nc, nr, cudaMemcpyHostToDevice));
+      IQ_CUDA(cudaMemcpy(s->rec[li].p, p + nc, nr, cudaMemcpyHostToDevice));
       p += nc + nr;
       li++;
     }
@@ -1145,7 +1186,8 @@ int iq_state_import(iq_state* s, const void* in, int64_t bytes) {
     IQ_CUDA(cudaMemcpy(s->kc[s->m->n_full].p, p, n, cudaMemcpyHostToDevice));
     IQ_CUDA(cudaMemcpy(s->vc[s->m->n_full].p, p + n, n, cudaMemcpyHostToDevice));
   }
-  // the imported DeltaNet state is ring slot 0; positions from the header
+  // the imported DeltaNet state is conv ring slot 0 and the recurrent base
+  // with no records pending; positions from the header
   int ctrl[8] = {(int)h.position, 0, 0, 0, 0, (int)h.mtp_position, 0, 0};
   IQ_CUDA(cudaMemcpy(s->ctrl.p, ctrl, sizeof ctrl, cudaMemcpyHostToDevice));
   s->position = h.position;

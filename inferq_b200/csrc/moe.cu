@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRoute
     float den = 0.f;
 #pragma unroll
     for (int i = 0; i < kPerLane; i++) {
-      p[i] = lane + 32 * i < E ? expf(p[i] - mx) : 0.f;
+      p[i] = lane + 32 * i < E ? exp_ref(p[i] - mx) : 0.f;
       den = __fadd_rn(den, p[i]);
     }
 #pragma unroll
@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(256) moe_act_kernel(MoeActArgs a) {
 #pragma unroll
   for (int j = 0; j < MAXB; j++)
 #pragma unroll
-    for (int i = 0; i < 8; i++) v[j][i] = __fmul_rn(__fdiv_rn(v[j][i], __fadd_rn(1.f, expf(-v[j][i]))), u[j][i]);
+    for (int i = 0; i < 8; i++) v[j][i] = __fmul_rn(__fdiv_rn(v[j][i], __fadd_rn(1.f, exp_ref(-v[j][i]))), u[j][i]);
   uint8_t* ar = a.act + (int64_t)slot * a.act_bytes;
   finish_row<MAXB>(v, nb, ffn, q80 ? nullptr : ar, q80 ? ar : nullptr, nullptr, xs);
 }
@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoeCombineArgs a) {
   const float4 ysh = *reinterpret_cast<const float4*>(a.y + (int64_t)(a.rows * a.topk + t) * a.y_ld + i);
   float4* hp = reinterpret_cast<float4*>(a.hidden + (int64_t)t * a.hidden_ld + i);
   const float4 h = *hp;
-  const float selector = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-sl)));
+  const float selector = __fdiv_rn(1.f, __fadd_rn(1.f, exp_ref(-sl)));
   float r[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int q = 0; q < kMaxTopk; q++)

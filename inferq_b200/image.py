@@ -67,3 +67,36 @@ def parse(buf: bytes | np.ndarray, cfg: Config) -> dict:
         n = mpos * sh["kv_dim"]
         out["mtp"] = {"keys": f[o:o + n], "values": f[o + n:o + 2 * n]}
     return out
+
+
+def build(cfg: Config, parts: dict) -> np.ndarray:
+    """The inverse of ``parse``: an image from a dict of the same form
+    (``position``, ``mtp_position``, ``layers`` and, with an MTP block, ``mtp``)."""
+    sh = shapes(cfg)
+    pos, mpos = int(parts["position"]), int(parts.get("mtp_position", 0))
+    h = np.zeros(1, HEADER)
+    h["magic"], h["version"], h["layers"] = MAGIC, 1, cfg.num_hidden_layers
+    h["position"], h["mtp_position"] = pos, mpos
+    h["has_mtp"] = 1 if cfg.mtp_num_hidden_layers else 0
+    for k, v in sh.items():
+        h[k] = v
+    chunks = [h.view(np.uint8)]
+    for l, layer in enumerate(parts["layers"]):
+        if cfg.layer_is_full(l):
+            for k in ("keys", "values"):
+                a = np.ascontiguousarray(layer[k], np.float32).reshape(-1)
+                assert a.size == pos * sh["kv_dim"], (l, k)
+                chunks.append(a.view(np.uint8))
+        else:
+            c = np.ascontiguousarray(layer["conv"], np.float32).reshape(-1)
+            r = np.ascontiguousarray(layer["recurrent"], np.float32).reshape(-1)
+            assert c.size == sh["conv_dim"] * sh["conv_taps"] and r.size == sh["rec_size"], l
+            chunks += [c.view(np.uint8), r.view(np.uint8)]
+    if cfg.mtp_num_hidden_layers:
+        for k in ("keys", "values"):
+            a = np.ascontiguousarray(parts["mtp"][k], np.float32).reshape(-1)
+            assert a.size == mpos * sh["kv_dim"], k
+            chunks.append(a.view(np.uint8))
+    out = np.concatenate(chunks)
+    assert out.size == image_bytes(cfg, pos, mpos)
+    return out

@@ -140,6 +140,13 @@ static void matvec_rows(const mat_t* m, int64_t r0, int64_t n, const float* x, f
 static float sigmoid_ref(float v) { return 1.f / (1.f + expf(-v)); }
 static float softplus_ref(float v) { return v > 20.f ? v : v < -20.f ? expf(v) : log1pf(expf(v)); }
 
+/* Rounding-level perturbation (a diagnostic of the reference arithmetic's
+ * own conditioning, off by default): mode 1 moves every RMSNorm output
+ * element by one ulp (odd elements up, even ones down), mode 2 the other
+ * way, as a different but equally valid summation order would move them. */
+static int g_perturb = 0;
+void or_set_perturb(int on) { g_perturb = on; }
+
 /* gguf_rms_norm (quantized_layer.rs:230-236): x / sqrt(mean(x^2) + eps) * w */
 static void rms_norm(const float* x, const float* w, int n, float eps, float* out) {
     float ss = 0.f;
@@ -147,6 +154,9 @@ static void rms_norm(const float* x, const float* w, int n, float eps, float* ou
     float var = ss * (float)(1.0 / (double)n);
     float den = sqrtf(var + eps);
     for (int i = 0; i < n; i++) out[i] = (x[i] / den) * w[i];
+    if (g_perturb)
+        for (int i = 0; i < n; i++)
+            out[i] = nextafterf(out[i], ((i & 1) ^ (g_perturb == 2)) ? INFINITY : -INFINITY);
 }
 
 /* ------------------------------------------------------------- creation */
@@ -564,3 +574,108 @@ int or_mtp_forward(const or_model* m, or_state* s, uint32_t token, const float* 
 }
 
 void or_state_set_mtp_position(or_state* s, int64_t p) { s->mtp_position = p; }
+
+/* ------------------------------------------------------------ state images
+ * The library's state-image layout (iq.h, iq_state_export), restated so a
+ * test can start the oracle from exactly the state the device holds
+ * (teacher forcing) and compare the states after a step: a 56-byte header
+ * {magic "IQSTATE1", i32 version, i32 layers, i64 position, i64 mtp_position,
+ * i32 has_mtp, kv_dim, conv_dim, conv_taps, rec_size, pad}, then per decoder
+ * layer the KV rows (keys then values, [pos][kv_dim]) of an attention layer
+ * or the conv [conv_dim][taps] and recurrent [nv][dk][dv] state of a
+ * DeltaNet layer, then the MTP block's KV rows; all f32.  The reference's
+ * own image (QuantizedStateImage, src/qwen/quantized_model.rs:59-100) holds
+ * the same per-layer tensors. */
+typedef struct {
+    char magic[8];
+    int32_t version, layers;
+    int64_t position, mtp_position;
+    int32_t has_mtp, kv_dim, conv_dim, conv_taps, rec_size, pad;
+} img_header_t;
+
+static void img_dims(const or_model* m, int64_t* kv_dim, int64_t* conv_n, int64_t* rec_n) {
+    const or_config* c = &m->c;
+    *kv_dim = (int64_t)c->num_key_value_heads * c->head_dim;
+    int64_t conv_dim = 2 * (int64_t)c->linear_num_key_heads * c->linear_key_head_dim +
+                       (int64_t)c->linear_num_value_heads * c->linear_value_head_dim;
+    *conv_n = conv_dim * (c->linear_conv_kernel_dim - 1);
+    *rec_n = (int64_t)c->linear_num_value_heads * c->linear_key_head_dim * c->linear_value_head_dim;
+}
+
+static int64_t img_bytes(const or_model* m, int64_t pos, int64_t mtp_pos) {
+    int64_t kv, cn, rn;
+    img_dims(m, &kv, &cn, &rn);
+    int64_t b = (int64_t)sizeof(img_header_t);
+    for (int l = 0; l < m->c.num_hidden_layers; l++) b += m->layers[l].full ? 2 * pos * kv * 4 : (cn + rn) * 4;
+    if (m->has_mtp) b += 2 * mtp_pos * kv * 4;
+    return b;
+}
+
+int64_t or_state_image_size(const or_model* m, const or_state* s) {
+    return img_bytes(m, s->position, m->has_mtp ? s->mtp_position : 0);
+}
+
+int or_state_export(const or_model* m, const or_state* s, uint8_t* out, int64_t bytes) {
+    int64_t kv, cn, rn;
+    img_dims(m, &kv, &cn, &rn);
+    const int64_t mtp_pos = m->has_mtp ? s->mtp_position : 0;
+    if (bytes < img_bytes(m, s->position, mtp_pos)) return -1;
+    img_header_t h;
+    memset(&h, 0, sizeof h);
+    memcpy(h.magic, "IQSTATE1", 8);
+    h.version = 1;
+    h.layers = m->c.num_hidden_layers;
+    h.position = s->position;
+    h.mtp_position = mtp_pos;
+    h.has_mtp = m->has_mtp;
+    h.kv_dim = (int32_t)kv;
+    h.conv_dim = (int32_t)(2 * (int64_t)m->c.linear_num_key_heads * m->c.linear_key_head_dim +
+                           (int64_t)m->c.linear_num_value_heads * m->c.linear_value_head_dim);
+    h.conv_taps = m->c.linear_conv_kernel_dim - 1;
+    h.rec_size = (int32_t)rn;
+    memcpy(out, &h, sizeof h);
+    uint8_t* p = out + sizeof h;
+    for (int l = 0; l < m->c.num_hidden_layers; l++) {
+        const lstate_t* st = &s->l[l];
+        if (m->layers[l].full) {
+            size_t n = (size_t)(s->position * kv * 4);
+            memcpy(p, st->keys, n); memcpy(p + n, st->values, n); p += 2 * n;
+        } else {
+            memcpy(p, st->conv, (size_t)cn * 4); memcpy(p + cn * 4, st->rec, (size_t)rn * 4); p += (cn + rn) * 4;
+        }
+    }
+    if (m->has_mtp) {
+        size_t n = (size_t)(mtp_pos * kv * 4);
+        memcpy(p, s->mtp.keys, n); memcpy(p + n, s->mtp.values, n);
+    }
+    return 0;
+}
+
+int or_state_import(const or_model* m, or_state* s, const uint8_t* in, int64_t bytes) {
+    img_header_t h;
+    int64_t kv, cn, rn;
+    img_dims(m, &kv, &cn, &rn);
+    if (bytes < (int64_t)sizeof h) return -1;
+    memcpy(&h, in, sizeof h);
+    if (memcmp(h.magic, "IQSTATE1", 8) || h.version != 1 || h.layers != m->c.num_hidden_layers) return -2;
+    if (h.kv_dim != kv || h.rec_size != rn || h.has_mtp != m->has_mtp) return -3;
+    if (h.position > s->max_pos || h.mtp_position > s->max_pos) return -4;
+    if (bytes != img_bytes(m, h.position, h.mtp_position)) return -5;
+    const uint8_t* p = in + sizeof h;
+    for (int l = 0; l < m->c.num_hidden_layers; l++) {
+        lstate_t* st = &s->l[l];
+        if (m->layers[l].full) {
+            size_t n = (size_t)(h.position * kv * 4);
+            memcpy(st->keys, p, n); memcpy(st->values, p + n, n); p += 2 * n;
+        } else {
+            memcpy(st->conv, p, (size_t)cn * 4); memcpy(st->rec, p + cn * 4, (size_t)rn * 4); p += (cn + rn) * 4;
+        }
+    }
+    if (m->has_mtp) {
+        size_t n = (size_t)(h.mtp_position * kv * 4);
+        memcpy(s->mtp.keys, p, n); memcpy(s->mtp.values, p + n, n);
+    }
+    s->position = h.position;
+    s->mtp_position = h.mtp_position;
+    return 0;
+}

@@ -81,6 +81,13 @@ def set_gemv_order(order: int) -> None:
     lib().or_set_gemv_order(order)
 
 
+def set_perturb(mode: int) -> None:
+    """Diagnostic: 1 or 2 moves every RMSNorm output by one ulp (two
+    opposite patterns), 0 turns it off: the conditioning of the reference
+    arithmetic itself under rounding-level changes."""
+    lib().or_set_perturb(int(mode))
+
+
 def argmax(v: np.ndarray) -> int:
     v = np.ascontiguousarray(v, np.float32)
     return int(lib().or_argmax(_p(v), len(v)))
@@ -109,6 +116,10 @@ class OracleModel:
         L.or_forward.argtypes = [P, P, P, ctypes.c_int, P, P, P]
         L.or_mtp_forward.argtypes = [P, P, ctypes.c_uint32, P, ctypes.c_int64, P, P]
         L.or_state_set_mtp_position.argtypes = [P, ctypes.c_int64]
+        L.or_state_image_size.restype = ctypes.c_int64
+        L.or_state_image_size.argtypes = [P, P]
+        L.or_state_export.argtypes = [P, P, P, ctypes.c_int64]
+        L.or_state_import.argtypes = [P, P, P, ctypes.c_int64]
         self.cfg = cfg
         self._keep = []
         views = []
@@ -167,6 +178,25 @@ class OracleState:
                                   None if lg is None else _p(lg), _p(out))
         assert rc == 0, rc
         return lg, out
+
+    @property
+    def position(self) -> int:
+        L = lib()
+        L.or_state_position.restype = ctypes.c_int64
+        L.or_state_position.argtypes = [ctypes.c_void_p]
+        return int(L.or_state_position(self._h))
+
+    def export_image(self) -> np.ndarray:
+        """The state in the library's image layout (inferq_b200.image)."""
+        n = lib().or_state_image_size(self.model._h, self._h)
+        buf = np.empty(n, np.uint8)
+        assert lib().or_state_export(self.model._h, self._h, _p(buf), n) == 0
+        return buf
+
+    def import_image(self, buf) -> None:
+        b = np.ascontiguousarray(buf, np.uint8)
+        rc = lib().or_state_import(self.model._h, self._h, _p(b), b.size)
+        assert rc == 0, rc
 
     def copy_from(self, other: "OracleState"):
         lib().or_state_copy(self.model._h, self._h, other._h)

@@ -42,3 +42,33 @@ def test_image_rejects_truncation_and_foreign_shapes():
         image.parse(b"NOTANIMG" + buf[8:], cfg)
     with pytest.raises(ValueError):
         image.parse(buf, synth.tiny())
+
+
+@pytest.mark.parametrize("make", [synth.tiny, synth.mini_35b])
+def test_build_is_the_inverse_of_parse(make):
+    cfg = make()
+    buf, _ = _build(cfg, 9, 4 if cfg.mtp_num_hidden_layers else 0, np.random.default_rng(2))
+    again = image.build(cfg, image.parse(buf, cfg))
+    assert again.tobytes() == buf
+
+
+def test_oracle_state_image_round_trip():
+    """The oracle's import/export of the library's image layout: an oracle
+    state exported and imported into a fresh state continues identically."""
+    import oracle
+    cfg = synth.tiny()
+    tensors = list(synth.generate(cfg, seed=4))
+    om = oracle.OracleModel(cfg, tensors)
+    a = om.state(64)
+    a.forward([5, 9, 400])
+    img = a.export_image()
+    parsed = image.parse(img, cfg)
+    assert parsed["position"] == 3
+    assert np.any(parsed["layers"][0]["recurrent"] != 0) and np.any(parsed["layers"][3]["keys"] != 0)
+    b = om.state(64)
+    b.forward([1])
+    b.import_image(img)
+    assert b.position == 3
+    la, _, _ = a.forward([77, 78])
+    lb, _, _ = b.forward([77, 78])
+    assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
