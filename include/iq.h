@@ -242,6 +242,11 @@ int iq_rollback(iq_state* s, int committed_rows);
 int iq_mtp_sync(iq_state* s, int64_t position, const float* prev_hidden, const uint32_t* tokens, int rows,
                 const float* target_hidden);
 
+/* The MTP input rows iq_mtp_sync builds, on the host only (no device work):
+ * out[r] = target_hidden[r-1] for r >= 1, out[0] = prev_hidden (zeros when
+ * NULL).  Replaces shifted_hidden_inputs (src/runtime.rs:2184-2223). */
+int iq_mtp_shifted_inputs(const float* prev_hidden, const float* target_hidden, int rows, int hidden, float* out);
+
 /* Drafting (replaces draft_mtp, src/runtime.rs:1995-2056, with
  * top1_with_scores :2245-2265 and QuantizedMtpHead::forward_with_head,
  * src/qwen/quantized_mtp.rs:175-227): from `seed` and the target's

@@ -1261,6 +1261,22 @@ int iq_verify(iq_state* s, const uint32_t* tokens, int rows, iq_verify_result* o
   return IQ_OK;
 }
 
+// Row r of the MTP inputs takes the target's hidden row of the position
+// before it: prev_hidden (or zeros at position 0) for the first, then rows
+// 0..rows-2 of target_hidden (shifted_hidden_inputs, src/runtime.rs:2184-2223).
+static void shifted_row(const float* prev_hidden, const float* target_hidden, int r, int H, float* dst) {
+  if (r > 0) memcpy(dst, target_hidden + (int64_t)(r - 1) * H, (size_t)H * 4);
+  else if (prev_hidden) memcpy(dst, prev_hidden, (size_t)H * 4);
+  else memset(dst, 0, (size_t)H * 4);
+}
+
+int iq_mtp_shifted_inputs(const float* prev_hidden, const float* target_hidden, int rows, int hidden, float* out) {
+  clear_error();
+  IQ_CHECK(target_hidden && out && rows >= 0 && hidden > 0, IQ_EINVAL, "iq_mtp_shifted_inputs: bad argument");
+  for (int r = 0; r < rows; r++) shifted_row(prev_hidden, target_hidden, r, hidden, out + (int64_t)r * hidden);
+  return IQ_OK;
+}
+
 int iq_mtp_sync(iq_state* s, int64_t position, const float* prev_hidden, const uint32_t* tokens, int rows,
                 const float* target_hidden) {
   clear_error();
@@ -1286,12 +1302,7 @@ int iq_mtp_sync(iq_state* s, int64_t position, const float* prev_hidden, const u
     IQ_CUDA(cudaStreamSynchronize(s->st));  // pinned staging is reused
     for (int i = 0; i < k; i++) {
       s->h_tokens[i] = (int32_t)tokens[r0 + i];
-      // row r takes the target hidden row of position r-1 (shifted_hidden_inputs)
-      const int r = r0 + i;
-      float* dst = s->h_mtp + (int64_t)i * H;
-      if (r > 0) memcpy(dst, target_hidden + (int64_t)(r - 1) * H, (size_t)H * 4);
-      else if (prev_hidden) memcpy(dst, prev_hidden, (size_t)H * 4);
-      else memset(dst, 0, (size_t)H * 4);
+      shifted_row(prev_hidden, target_hidden, r0 + i, H, s->h_mtp + (int64_t)i * H);
     }
     IQ_CUDA(cudaMemcpyAsync(s->tokens.p, s->h_tokens, k * 4, cudaMemcpyHostToDevice, s->st));
     IQ_CUDA(cudaMemcpyAsync(s->mtp_hin.p, s->h_mtp, (size_t)k * H * 4, cudaMemcpyHostToDevice, s->st));

@@ -159,6 +159,17 @@ static void rms_norm(const float* x, const float* w, int n, float eps, float* ou
             out[i] = nextafterf(out[i], ((i & 1) ^ (g_perturb == 2)) ? INFINITY : -INFINITY);
 }
 
+void or_rms_norm(const float* x, const float* w, int n, float eps, float* out) { rms_norm(x, w, n, eps, out); }
+
+/* accepted_draft_prefix (runtime.rs:2225-2236): the number of leading
+ * drafts equal to the greedy argmax of the row before them; logits holds
+ * ndrafts+1 rows of `vocab`. */
+int or_accepted_prefix(const uint32_t* drafts, int ndrafts, const float* logits, int64_t vocab) {
+    int a = 0;
+    while (a < ndrafts && or_argmax(logits + (int64_t)a * vocab, vocab) == (int64_t)drafts[a]) a++;
+    return a;
+}
+
 /* ------------------------------------------------------------- creation */
 #define REQ(x) do { if (!(x)) { free(m->layers); free(m); return NULL; } } while (0)
 
@@ -303,6 +314,66 @@ void or_state_copy(const or_model* m, or_state* dst, const or_state* src) {
 int64_t or_state_position(const or_state* s) { return s->position; }
 
 /* ------------------------------------------------------------ DeltaNet */
+/* causal_depthwise_conv_step + SiLU (quantized_deltanet.rs:733-759): per
+ * channel, sum = w[K-1]*x + sum_tap w[tap]*history[tap] (each product
+ * rounded, added in tap order), output silu(sum), history shifted left and
+ * the input appended.  state is [channels][K-1]. */
+void or_conv_step(const float* input, const float* weights, int channels, int kernel, float* state, float* output) {
+    for (int ch = 0; ch < channels; ch++) {
+        const float* w = weights + (int64_t)ch * kernel;
+        float* hist = state + (int64_t)ch * (kernel - 1);
+        float sum = w[kernel - 1] * input[ch];
+        for (int tap = 0; tap < kernel - 1; tap++) sum += w[tap] * hist[tap];
+        output[ch] = sum * sigmoid_ref(sum);
+        for (int tap = 0; tap + 1 < kernel - 1; tap++) hist[tap] = hist[tap + 1];
+        if (kernel > 1) hist[kernel - 2] = input[ch];
+    }
+}
+
+/* normalize (quantized_deltanet.rs:724-731): x * (sum x^2 + 1e-6)^-1/2, the
+ * sum in element order. */
+void or_l2_normalize(float* a, int n) {
+    float ss = 0.f;
+    for (int i = 0; i < n; i++) ss += a[i] * a[i];
+    float scale = 1.f / sqrtf(ss + 1e-6f);
+    for (int i = 0; i < n; i++) a[i] *= scale;
+}
+
+float or_softplus(float v) { return softplus_ref(v); }
+
+/* ValueHeadLayout::index (quantized_deltanet.rs:358-376): the value head of
+ * (key head, repeat): GroupedByKeyHead key*ratio + repeat (Qwen3-Next),
+ * TiledByRepeat repeat*key_heads + key (Qwen3.6). */
+int or_value_head(int key, int repeat, int key_heads, int ratio, int tiled) {
+    return tiled ? repeat * key_heads + key : key * ratio + repeat;
+}
+
+/* delta_head_step (deltanet.rs:170-217) on one head's [dk][dv] state:
+ * S *= exp(g); pred_j = sum_i S[i][j] k[i]; delta_j = (v_j - pred_j) beta;
+ * S[i][j] += k[i] delta_j; out_j = sum_i S[i][j] q[i] q_scale, every sum in
+ * key-row order and every product rounded. */
+static void delta_head_step(const float* qq, const float* kk, const float* vv, float g, float beta, int dk, int dv,
+                            float q_scale, float* S, float* out_h) {
+    float decay = expf(g);
+    for (int i = 0; i < dk * dv; i++) S[i] *= decay;
+    for (int j = 0; j < dv; j++) out_h[j] = 0.f;
+    for (int i = 0; i < dk; i++) for (int j = 0; j < dv; j++) out_h[j] += S[i * dv + j] * kk[i];
+    for (int j = 0; j < dv; j++) out_h[j] = (vv[j] - out_h[j]) * beta;
+    for (int i = 0; i < dk; i++) for (int j = 0; j < dv; j++) S[i * dv + j] += kk[i] * out_h[j];
+    for (int j = 0; j < dv; j++) out_h[j] = 0.f;
+    for (int i = 0; i < dk; i++) for (int j = 0; j < dv; j++) out_h[j] += S[i * dv + j] * qq[i] * q_scale;
+}
+
+/* recurrent_delta_step (deltanet.rs:122-166): every head on its own state
+ * block [heads][dk][dv]; q_scale = 1/sqrt(dk). */
+void or_delta_step(const float* q, const float* k, const float* v, const float* g, const float* beta, int heads,
+                   int dk, int dv, float* state, float* out) {
+    float q_scale = 1.f / sqrtf((float)dk);
+    for (int h = 0; h < heads; h++)
+        delta_head_step(q + h * dk, k + h * dk, v + h * dv, g[h], beta[h], dk, dv, q_scale,
+                        state + (int64_t)h * dk * dv, out + h * dv);
+}
+
 static void delta_row(const or_model* m, const layer_t* L, lstate_t* st, const float* x, float* out) {
     const or_config* c = &m->c;
     const int nk = c->linear_num_key_heads, nv = c->linear_num_value_heads;
@@ -320,30 +391,16 @@ static void delta_row(const or_model* m, const layer_t* L, lstate_t* st, const f
     matvec(&L->z, x, z);
     if (L->ba_fused) matvec(&L->ba, x, ba);
     else { matvec(&L->beta, x, ba); matvec(&L->alpha, x, ba + nv); }
-    /* causal depthwise conv step + SiLU (quantized_deltanet.rs:733-759) */
-    for (int ch = 0; ch < conv_dim; ch++) {
-        const float* w = L->conv_w + (int64_t)ch * K;
-        float* hist = st->conv + (int64_t)ch * (K - 1);
-        float sum = w[K - 1] * proj[ch];
-        for (int tap = 0; tap < K - 1; tap++) sum += w[tap] * hist[tap];
-        cv[ch] = sum * sigmoid_ref(sum);
-        for (int tap = 0; tap + 1 < K - 1; tap++) hist[tap] = hist[tap + 1];
-        if (K > 1) hist[K - 2] = proj[ch];
-    }
+    or_conv_step(proj, L->conv_w, conv_dim, K, st->conv, cv);
     float* q = cv; float* k = cv + kd; const float* v = cv + 2 * kd;
     for (int kh = 0; kh < nk; kh++) {
-        for (int which = 0; which < 2; which++) {  /* normalize (:724-731) */
-            float* a = (which ? k : q) + kh * dk;
-            float ss = 0.f;
-            for (int i = 0; i < dk; i++) ss += a[i] * a[i];
-            float scale = 1.f / sqrtf(ss + 1e-6f);
-            for (int i = 0; i < dk; i++) a[i] *= scale;
-        }
+        or_l2_normalize(q + kh * dk, dk);
+        or_l2_normalize(k + kh * dk, dk);
     }
     float q_scale = 1.f / sqrtf((float)dk);
     for (int kh = 0; kh < nk; kh++)
         for (int rep = 0; rep < ratio; rep++) {
-            int vh = c->value_heads_tiled ? rep * nk + kh : kh * ratio + rep;
+            int vh = or_value_head(kh, rep, nk, ratio, c->value_heads_tiled);
             memcpy(qr + vh * dk, q + kh * dk, (size_t)dk * 4);
             memcpy(kr + vh * dk, k + kh * dk, (size_t)dk * 4);
             float b, al;
@@ -351,18 +408,8 @@ static void delta_row(const or_model* m, const layer_t* L, lstate_t* st, const f
             else { b = ba[vh]; al = ba[nv + vh]; }
             float beta = sigmoid_ref(b);
             float gdec = L->ssm_a[vh] * softplus_ref(al + L->dt_bias[vh]);
-            /* delta_head_step (deltanet.rs:170-217) */
-            float* S = st->rec + (int64_t)vh * dk * dv;
-            const float* kk = kr + vh * dk; const float* qq = qr + vh * dk; const float* vv = v + vh * dv;
-            float decay = expf(gdec);
-            for (int i = 0; i < dk * dv; i++) S[i] *= decay;
-            float* out_h = o + vh * dv;
-            for (int j = 0; j < dv; j++) out_h[j] = 0.f;
-            for (int i = 0; i < dk; i++) for (int j = 0; j < dv; j++) out_h[j] += S[i * dv + j] * kk[i];
-            for (int j = 0; j < dv; j++) out_h[j] = (vv[j] - out_h[j]) * beta;
-            for (int i = 0; i < dk; i++) for (int j = 0; j < dv; j++) S[i * dv + j] += kk[i] * out_h[j];
-            for (int j = 0; j < dv; j++) out_h[j] = 0.f;
-            for (int i = 0; i < dk; i++) for (int j = 0; j < dv; j++) out_h[j] += S[i * dv + j] * qq[i] * q_scale;
+            delta_head_step(qr + vh * dk, kr + vh * dk, v + vh * dv, gdec, beta, dk, dv, q_scale,
+                            st->rec + (int64_t)vh * dk * dv, o + vh * dv);
         }
     /* rms_norm_gated (norm.rs:16-25) per value head */
     for (int vh = 0; vh < nv; vh++) {
@@ -411,6 +458,54 @@ static void apply_rope(float* v, int64_t pos, int rd, double theta) {  /* :841-8
     }
 }
 
+/* The per-head scan of one query row (quantized_attention.rs:409-589):
+ * scores dot8(q, key) * (1/sqrt(hd)) over `positions` cached rows, softmax
+ * (max, exp, sum in position order, divide), probability-weighted value sum
+ * in position order, output times sigmoid(gate).  Query head h reads KV head
+ * h / (nh / nkv).  q and gate of head h at qg + h*q_ld and + gate_off;
+ * keys/values [positions][nkv][hd]; res [nh][hd]. */
+static void attend_row(const float* qg, int q_ld, int gate_off, const float* keys, const float* values, int nh, int nkv,
+                       int hd, int64_t positions, float* scores, float* res) {
+    const int G = nh / nkv;
+    float scale = 1.f / sqrtf((float)hd);
+    for (int h = 0; h < nh; h++) {
+        const float* q = qg + (int64_t)h * q_ld;
+        const float* gate = q + gate_off;
+        int kvh = h / G;
+        float mx = -INFINITY;
+        for (int64_t p = 0; p < positions; p++) {
+            scores[p] = dot8(q, keys + (p * nkv + kvh) * hd, hd) * scale;
+            if (scores[p] > mx) mx = scores[p];
+        }
+        float den = 0.f;
+        for (int64_t p = 0; p < positions; p++) { scores[p] = expf(scores[p] - mx); den += scores[p]; }
+        float* o = res + (int64_t)h * hd;
+        for (int d = 0; d < hd; d++) o[d] = 0.f;
+        for (int64_t p = 0; p < positions; p++) {
+            float prob = scores[p] / den;
+            const float* vr = values + (p * nkv + kvh) * hd;
+            for (int d = 0; d < hd; d++) o[d] += prob * vr[d];
+        }
+        for (int d = 0; d < hd; d++) o[d] *= sigmoid_ref(gate[d]);
+    }
+}
+
+/* Exported forms of the attention pieces for known-answer tests. */
+float or_dot8(const float* a, const float* b, int n) { return dot8(a, b, n); }
+void or_converted_norm(float* v, const float* w, int n, float eps) { converted_norm(v, w, n, eps); }
+void or_attend(const float* q, const float* gate, const float* keys, const float* values, int nh, int nkv, int hd,
+               int64_t positions, float* out) {
+    /* q and gate as [nh][hd] each: interleave into the layer's [q | gate] rows */
+    float* qg = (float*)malloc((size_t)nh * 2 * hd * 4);
+    float* scores = (float*)malloc((size_t)(positions > 0 ? positions : 1) * 4);
+    for (int h = 0; h < nh; h++) {
+        memcpy(qg + (int64_t)h * 2 * hd, q + (int64_t)h * hd, (size_t)hd * 4);
+        memcpy(qg + (int64_t)h * 2 * hd + hd, gate + (int64_t)h * hd, (size_t)hd * 4);
+    }
+    attend_row(qg, 2 * hd, hd, keys, values, nh, nkv, hd, positions, scores, out);
+    free(qg); free(scores);
+}
+
 static void attn_row(const or_model* m, const layer_t* L, lstate_t* st, int64_t pos, const float* x, float* out) {
     const or_config* c = &m->c;
     const int nh = c->num_attention_heads, nkv = c->num_key_value_heads, hd = c->head_dim;
@@ -429,34 +524,42 @@ static void attn_row(const or_model* m, const layer_t* L, lstate_t* st, int64_t 
     }
     memcpy(st->keys + pos * nkv * hd, kv, (size_t)nkv * hd * 4);
     memcpy(st->values + pos * nkv * hd, vv, (size_t)nkv * hd * 4);
-    float scale = 1.f / sqrtf((float)hd);
     for (int h = 0; h < nh; h++) {
         float* q = qg + h * 2 * hd;
-        const float* gate = q + hd;
         converted_norm(q, L->q_norm, hd, c->rms_norm_eps);
         apply_rope(q, pos, c->rotary_dim, c->rope_theta);
-        int kvh = h / G;
-        float mx = -INFINITY;
-        for (int64_t p = 0; p <= pos; p++) {
-            scores[p] = dot8(q, st->keys + (p * nkv + kvh) * hd, hd) * scale;
-            if (scores[p] > mx) mx = scores[p];
-        }
-        float den = 0.f;
-        for (int64_t p = 0; p <= pos; p++) { scores[p] = expf(scores[p] - mx); den += scores[p]; }
-        float* o = res + h * hd;
-        for (int d = 0; d < hd; d++) o[d] = 0.f;
-        for (int64_t p = 0; p <= pos; p++) {
-            float prob = scores[p] / den;
-            const float* vr = st->values + (p * nkv + kvh) * hd;
-            for (int d = 0; d < hd; d++) o[d] += prob * vr[d];
-        }
-        for (int d = 0; d < hd; d++) o[d] *= sigmoid_ref(gate[d]);
     }
+    attend_row(qg, 2 * hd, hd, st->keys, st->values, nh, nkv, hd, pos + 1, scores, res);
+    (void)G;
     matvec(&L->o, res, out);
     free(qg); free(kv); free(vv); free(res); free(scores);
 }
 
 /* ----------------------------------------------------------------- MoE */
+/* top_k_routes (moe.rs:21-54): softmax over the router logits (max, exp,
+ * sum in expert order, divide), the top_k experts by probability (equal
+ * probabilities rank the lower expert first; the reference's unstable sort
+ * leaves that order unspecified), weights renormalized to sum to one when
+ * norm_topk.  experts/weights receive topk entries; rank needs E ints. */
+void or_route(const float* lg, int E, int topk, int norm_topk, int* rank, float* w) {
+    float* pr = (float*)malloc((size_t)E * 4);
+    float mx = -INFINITY;
+    for (int e = 0; e < E; e++) mx = fmaxf(mx, lg[e]);
+    float den = 0.f;
+    for (int e = 0; e < E; e++) den += expf(lg[e] - mx);
+    for (int e = 0; e < E; e++) pr[e] = expf(lg[e] - mx) / den;
+    for (int e = 0; e < E; e++) rank[e] = e;
+    for (int r = 0; r < topk; r++) {
+        int best = r;
+        for (int i = r + 1; i < E; i++)
+            if (pr[rank[i]] > pr[rank[best]] || (pr[rank[i]] == pr[rank[best]] && rank[i] < rank[best])) best = i;
+        int t = rank[r]; rank[r] = rank[best]; rank[best] = t;
+    }
+    float sum = 0.f;
+    for (int r = 0; r < topk; r++) { w[r] = pr[rank[r]]; sum += w[r]; }
+    if (norm_topk) for (int r = 0; r < topk; r++) w[r] /= sum;
+    free(pr);
+}
 static void moe_row(const or_model* m, const layer_t* L, const float* x, float* out, int* experts_out) {
     const or_config* c = &m->c;
     const int E = c->num_experts, H = c->hidden_size, F = c->moe_intermediate_size;
@@ -468,22 +571,9 @@ static void moe_row(const or_model* m, const layer_t* L, const float* x, float* 
     float* u = (float*)malloc((size_t)(F > Fs ? F : Fs) * 4);
     float* y = (float*)malloc((size_t)H * 4);
     matvec(&L->router, x, lg);
-    float mx = -INFINITY;
-    for (int e = 0; e < E; e++) mx = fmaxf(mx, lg[e]);
-    float den = 0.f;
-    for (int e = 0; e < E; e++) den += expf(lg[e] - mx);
-    for (int e = 0; e < E; e++) pr[e] = expf(lg[e] - mx) / den;
-    /* top-k by probability; equal probabilities rank the lower expert first */
-    for (int e = 0; e < E; e++) rank[e] = e;
-    for (int r = 0; r < topk; r++) {
-        int best = r;
-        for (int i = r + 1; i < E; i++)
-            if (pr[rank[i]] > pr[rank[best]] || (pr[rank[i]] == pr[rank[best]] && rank[i] < rank[best])) best = i;
-        int t = rank[r]; rank[r] = rank[best]; rank[best] = t;
-    }
-    float w[16], sum = 0.f;
-    for (int r = 0; r < topk; r++) { w[r] = pr[rank[r]]; sum += w[r]; }
-    if (c->norm_topk_prob) for (int r = 0; r < topk; r++) w[r] /= sum;
+    float w[16];
+    or_route(lg, E, topk, c->norm_topk_prob, rank, w);
+    (void)pr;
     for (int i = 0; i < H; i++) out[i] = 0.f;
     for (int r = 0; r < topk; r++) {
         int e = rank[r];

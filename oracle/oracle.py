@@ -93,6 +93,104 @@ def argmax(v: np.ndarray) -> int:
     return int(lib().or_argmax(_p(v), len(v)))
 
 
+# ------------------------------------------------------- layer primitives
+def _f32(a):
+    return np.ascontiguousarray(a, np.float32)
+
+
+def conv_step(inp, weights, kernel: int, state):
+    """causal_depthwise_conv_step + SiLU; returns (output, new state)."""
+    inp, w, st = _f32(inp), _f32(weights), _f32(state).copy()
+    out = np.empty_like(inp)
+    lib().or_conv_step.argtypes = [P, P, I32, I32, P, P]
+    lib().or_conv_step(_p(inp), _p(w), len(inp), kernel, _p(st), _p(out))
+    return out, st
+
+
+def l2_normalize(a):
+    a = _f32(a).copy()
+    lib().or_l2_normalize.argtypes = [P, I32]
+    lib().or_l2_normalize(_p(a), len(a))
+    return a
+
+
+def softplus(v: float) -> float:
+    L = lib()
+    L.or_softplus.restype = ctypes.c_float
+    L.or_softplus.argtypes = [ctypes.c_float]
+    return float(L.or_softplus(v))
+
+
+def delta_step(q, k, v, g, beta, heads: int, key_dim: int, value_dim: int, state):
+    """recurrent_delta_step; returns (out, new state)."""
+    q, k, v, g, beta = map(_f32, (q, k, v, g, beta))
+    st = _f32(state).copy()
+    out = np.empty(heads * value_dim, np.float32)
+    lib().or_delta_step.argtypes = [P, P, P, P, P, I32, I32, I32, P, P]
+    lib().or_delta_step(_p(q), _p(k), _p(v), _p(g), _p(beta), heads, key_dim, value_dim, _p(st), _p(out))
+    return out, st
+
+
+def route(logits, topk: int, norm_topk: bool = True):
+    """top_k_routes for one row: (experts, weights)."""
+    lg = _f32(logits)
+    rank = np.empty(len(lg), np.int32)
+    w = np.empty(topk, np.float32)
+    lib().or_route.argtypes = [P, I32, I32, I32, P, P]
+    lib().or_route(_p(lg), len(lg), topk, int(norm_topk), _p(rank), _p(w))
+    return rank[:topk].copy(), w
+
+
+def rms_norm(x, w, eps: float):
+    """gguf_rms_norm of one row (w already 1 + gamma)."""
+    L = lib()
+    L.or_rms_norm.argtypes = [P, P, I32, ctypes.c_float, P]
+    x, w = _f32(x), _f32(w)
+    out = np.empty_like(x)
+    L.or_rms_norm(_p(x), _p(w), len(x), eps, _p(out))
+    return out
+
+
+def converted_norm(v, w, eps: float):
+    L = lib()
+    L.or_converted_norm.argtypes = [P, P, I32, ctypes.c_float]
+    v, w = _f32(v).copy(), _f32(w)
+    L.or_converted_norm(_p(v), _p(w), len(v), eps)
+    return v
+
+
+def dot8(a, b) -> float:
+    L = lib()
+    L.or_dot8.restype = ctypes.c_float
+    L.or_dot8.argtypes = [P, P, I32]
+    a, b = _f32(a), _f32(b)
+    return float(L.or_dot8(_p(a) if a.size else None, _p(b) if b.size else None, len(a)))
+
+
+def attend(q, gate, keys, values, nh: int, nkv: int, hd: int):
+    """The per-head scan of one query row over keys/values [positions][nkv][hd]."""
+    L = lib()
+    L.or_attend.argtypes = [P, P, P, P, I32, I32, I32, I64, P]
+    q, gate, keys, values = map(_f32, (q, gate, keys, values))
+    out = np.empty(nh * hd, np.float32)
+    L.or_attend(_p(q), _p(gate), _p(keys), _p(values), nh, nkv, hd, keys.size // (nkv * hd), _p(out))
+    return out
+
+
+def value_head(key: int, repeat: int, key_heads: int, ratio: int, tiled: bool) -> int:
+    L = lib()
+    L.or_value_head.argtypes = [I32, I32, I32, I32, I32]
+    return int(L.or_value_head(key, repeat, key_heads, ratio, int(tiled)))
+
+
+def accepted_prefix(drafts, logits) -> int:
+    L = lib()
+    L.or_accepted_prefix.argtypes = [P, I32, P, I64]
+    d = np.ascontiguousarray(drafts, np.uint32)
+    lg = _f32(logits)
+    return int(L.or_accepted_prefix(_p(d) if d.size else None, len(d), _p(lg), lg.shape[-1]))
+
+
 # ------------------------------------------------------------------ model
 class OracleModel:
     """The CPU restatement of the reference model over host tensors.
