@@ -171,18 +171,43 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a) {
 #pragma unroll 8
   for (int c = 0; c < nchunks; c++) M = fmaxf(M, part[c * (a.hd + 2)]);
   const int i = threadIdx.x;
-  if (i >= a.hd) return;
-  float L = 0.f, o = 0.f;
+  __shared__ float ys[256];
+  if (i < a.hd) {
+    float L = 0.f, o = 0.f;
 #pragma unroll 8
-  for (int c = 0; c < nchunks; c++) {
-    const float* pc = part + c * (a.hd + 2);
-    const float w = exp_ref(pc[0] - M);
-    L = fmaf(pc[1], w, L);
-    o = fmaf(pc[2 + i], w, o);
+    for (int c = 0; c < nchunks; c++) {
+      const float* pc = part + c * (a.hd + 2);
+      const float w = exp_ref(pc[0] - M);
+      L = fmaf(pc[1], w, L);
+      o = fmaf(pc[2 + i], w, o);
+    }
+    o = __fdiv_rn(o, L);
+    const float gate = a.qg[(int64_t)t * a.qg_ld + (int64_t)h * 2 * a.hd + a.hd + i];
+    const float y = __fmul_rn(o, sigmoidf_ref(gate));
+    if (a.q8k_out || a.q80_out) ys[i] = y;
+    else a.out[(int64_t)t * a.out_ld + (int64_t)h * a.hd + i] = y;
   }
-  o = __fdiv_rn(o, L);
-  const float gate = a.qg[(int64_t)t * a.qg_ld + (int64_t)h * 2 * a.hd + a.hd + i];
-  a.out[(int64_t)t * a.out_ld + (int64_t)h * a.hd + i] = __fmul_rn(o, sigmoidf_ref(gate));
+  if (!a.q8k_out && !a.q80_out) return;
+  // the output projection's activation row, quantized here: a head of 256 is
+  // one Q8_K block (block h of the row), a head of 128k is k Q8_0 groups
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cols = a.nh * a.hd;
+  if (a.q8k_out) {
+    if (warp == 0) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) v[e] = ys[q8k_lane_pos(lane, e)];
+      quant_q8k_block_warp_v(v, a.q8k_out + (int64_t)t * a.q8k_stride, cols / 256, h, lane);
+    }
+  } else if (warp < a.hd / 128) {
+    const int g = h * (a.hd / 128) + warp;
+    const int base = q80_lane_base(g, lane) - h * a.hd;
+    float v[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) v[e] = ys[base + e];
+    quant_q80_group_warp_v(v, a.q80_out + (int64_t)t * a.q80_stride, cols / 32, g, lane);
+  }
 }
 
 template <int D>
@@ -215,6 +240,7 @@ cudaError_t attn_scan_launch(const AttnArgs& a, cudaStream_t st, bool pdl) {
 }
 
 cudaError_t attn_combine_launch(const AttnArgs& a, cudaStream_t st, bool pdl) {
+  if (a.hd > 256 || (a.q8k_out && a.hd != 256) || (a.q80_out && a.hd % 128)) return cudaErrorInvalidValue;
   return launch_pdl(attn_combine_kernel, dim3(a.rows * a.nh), dim3(256), 0, st, pdl, a);
 }
 

@@ -13,7 +13,9 @@
 // walks the dk key rows of S[:, j] in order, with the column in registers.
 //
 // Grid: one CTA per value head, dv/32 warps; warp w owns columns
-// 32w .. 32w+31.  The conv, the norms and beta/g of all the pass's rows are
+// 32w .. 32w+31, and the head's dk x dv state sits in shared memory (column j
+// is thread j's; rolled loops keep the code small enough for the
+// instruction cache).  The conv, the norms and beta/g of all the pass's rows are
 // computed first by the whole CTA (they do not depend on the state); then
 // each warp runs the rows: the o-sum of row t and the pred-sum of row t+1
 // walk the key rows in the same loop (two independent chains).
@@ -28,6 +30,7 @@
 // it overlaps the projection GEMV).  The conv state (small) keeps a ring of
 // kStateRing buffers: a pass reads slot `cur` and writes the state after its
 // row t to slot cur+1+t, and committing c rows moves `cur` by c.
+#include <mutex>
 #include "kernels.cuh"
 #include "model_kernels.cuh"
 #include "devfns.cuh"
@@ -44,6 +47,36 @@ __device__ __forceinline__ float softplus_ref(float v) {
 }
 
 // DK key rows, DV value columns per head (32 * warps), conv width K.
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void bar_init(uint64_t* b) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(b)) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void bar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(b)), "r"(bytes) : "memory");
+}
+// Bulk copy of `bytes` (a multiple of 16, 16-byte aligned ends) from this
+// GPU's global memory into this CTA's shared memory, completing on `b`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, int bytes, uint64_t* b) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(b))
+               : "memory");
+}
+// Bounded wait for phase `parity` of `b`; false if it did not complete.
+__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, int limit = 1 << 20) {
+  for (int i = 0; i < limit; i++) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_addr(b)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
 template <int DK, int DV, int K>
 __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
   constexpr int NT = DV;               // threads
@@ -66,19 +99,36 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
   // ---- before the dependency wait: state column, replay of the committed
   // rows of the previous pass, conv weights and history (none of them is
   // written by the kernels this pass runs before this one)
-  float S[DK];
-#pragma unroll
-  for (int i = 0; i < DK; i++) S[i] = base[(int64_t)i * DV];
+  // the head's state, one column per thread, in shared memory (rolled loops
+  // keep the kernel's code small; the column accesses are conflict-free),
+  // brought in with the update records to replay by one bulk copy each
+  extern __shared__ __align__(128) float Ssm[];  // [DK][DV], then [kMaxRowsDelta][rec_stride]
+  float* rec_s = Ssm + DK * DV;
+  float* Sc = Ssm + j;
+  __shared__ __align__(8) uint64_t bar;
   const int pend = *a.pending;
+  if (tid == 0) {
+    bar_init(&bar);
+    bar_expect_tx(&bar, (uint32_t)(DK * DV * 4 + pend * rec_stride * 4));
+    bulk_load(Ssm, L.rec_state + (int64_t)vh * DK * DV, DK * DV * 4, &bar);
+    if (pend > 0) bulk_load(rec_s, rec_head, pend * rec_stride * 4, &bar);
+  }
+  __syncthreads();  // the barrier is initialized before anyone waits on it
+  if (!bar_wait(&bar, 0)) {
+    // (not expected) the copies did not land: report, let them finish, stop
+    if (tid == 0) atomicExch(a.timeout_flag, 1);
+    bar_wait(&bar, 0, 1 << 22);
+    return;
+  }
   for (int r = 0; r < pend; r++) {
-    const float* rc = rec_head + (int64_t)r * rec_stride;
+    const float* rc = rec_s + r * rec_stride;
     const float decay = rc[DK + DV], delta = rc[DK + j];
-#pragma unroll
-    for (int i = 0; i < DK; i++) S[i] = __fadd_rn(__fmul_rn(S[i], decay), __fmul_rn(rc[i], delta));
+#pragma unroll 4
+    for (int i = 0; i < DK; i++) Sc[i * DV] = __fadd_rn(__fmul_rn(Sc[i * DV], decay), __fmul_rn(rc[i], delta));
   }
   if (pend > 0) {
-#pragma unroll
-    for (int i = 0; i < DK; i++) base[(int64_t)i * DV] = S[i];
+#pragma unroll 8
+    for (int i = 0; i < DK; i++) base[(int64_t)i * DV] = Sc[i * DV];
   }
   const int cur = *a.cur;
   auto chan = [&](int c) {
@@ -108,6 +158,11 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
   __shared__ __align__(16) float qk[kMaxRowsDelta][2][QS];  // conv outputs, then normalized q and k
   __shared__ float vs[kMaxRowsDelta][DV];
   __shared__ float beta_s[kMaxRowsDelta], decay_s[kMaxRowsDelta];
+  __shared__ float os[kMaxRowsDelta][DV];  // recurrent outputs (fused gated norm)
+  float zin[kMaxRowsDelta];                // gate projections of this column (fused gated norm)
+#pragma unroll
+  for (int t = 0; t < kMaxRowsDelta; t++)
+    zin[t] = (a.q80 && t < rows) ? a.z[(int64_t)t * a.z_ld + vh * DV + j] : 0.f;
   // every input of the pass requested before any arithmetic
   float xin[CPT][kMaxRowsDelta];
 #pragma unroll
@@ -185,14 +240,15 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
   {
     const float decay = decay_s[0];
     const float4* k4 = reinterpret_cast<const float4*>(qk[0][1]);
-#pragma unroll
+#pragma unroll 2
     for (int i4 = 0; i4 < DK / 4; i4++) {
       const float4 kv = k4[i4];
       const float kk[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
       for (int e = 0; e < 4; e++) {
-        S[4 * i4 + e] = __fmul_rn(S[4 * i4 + e], decay);
-        pred = __fadd_rn(pred, __fmul_rn(S[4 * i4 + e], kk[e]));
+        const float sv = __fmul_rn(Sc[(4 * i4 + e) * DV], decay);
+        Sc[(4 * i4 + e) * DV] = sv;
+        pred = __fadd_rn(pred, __fmul_rn(sv, kk[e]));
       }
     }
   }
@@ -207,37 +263,70 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
       const float4* n4 = reinterpret_cast<const float4*>(qk[t + 1][1]);
       const float decay = decay_s[t + 1];
       float pn = 0.f;
-#pragma unroll
+#pragma unroll 2
       for (int i4 = 0; i4 < DK / 4; i4++) {
         const float4 kv = k4[i4], qv = q4[i4], nv = n4[i4];
         const float kk[4] = {kv.x, kv.y, kv.z, kv.w}, qq[4] = {qv.x, qv.y, qv.z, qv.w};
         const float nn[4] = {nv.x, nv.y, nv.z, nv.w};
 #pragma unroll
         for (int e = 0; e < 4; e++) {
-          float s = __fadd_rn(S[4 * i4 + e], __fmul_rn(kk[e], delta));
-          o = __fadd_rn(o, __fmul_rn(__fmul_rn(s, qq[e]), qscale));
-          s = __fmul_rn(s, decay);
-          pn = __fadd_rn(pn, __fmul_rn(s, nn[e]));
-          S[4 * i4 + e] = s;
+          float sv = __fadd_rn(Sc[(4 * i4 + e) * DV], __fmul_rn(kk[e], delta));
+          o = __fadd_rn(o, __fmul_rn(__fmul_rn(sv, qq[e]), qscale));
+          sv = __fmul_rn(sv, decay);
+          pn = __fadd_rn(pn, __fmul_rn(sv, nn[e]));
+          Sc[(4 * i4 + e) * DV] = sv;
         }
       }
       pred = pn;
     } else {
-#pragma unroll
+#pragma unroll 2
       for (int i4 = 0; i4 < DK / 4; i4++) {
         const float4 kv = k4[i4], qv = q4[i4];
         const float kk[4] = {kv.x, kv.y, kv.z, kv.w}, qq[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
         for (int e = 0; e < 4; e++) {
-          const float s = __fadd_rn(S[4 * i4 + e], __fmul_rn(kk[e], delta));
-          o = __fadd_rn(o, __fmul_rn(__fmul_rn(s, qq[e]), qscale));
-          S[4 * i4 + e] = s;
+          const float sv = __fadd_rn(Sc[(4 * i4 + e) * DV], __fmul_rn(kk[e], delta));
+          o = __fadd_rn(o, __fmul_rn(__fmul_rn(sv, qq[e]), qscale));
         }
       }
     }
-    a.out[(int64_t)t * a.out_ld + vh * DV + j] = o;
+    if (a.q80) os[t][j] = o;
+    else a.out[(int64_t)t * a.out_ld + vh * DV + j] = o;
   }
-  (void)lane;
+  if (!a.q80) return;
+  // gated RMSNorm of this value head (src/qwen/norm.rs:16-25): the sum of
+  // squares in element order, then norm(o) * w * silu(z), z = g / (1 + e^-g);
+  // then Q8_0 quantization of each 32-column block (one warp), as
+  // BlockQ8_0::from_float: d = amax / 127 (kept as f16), q = round(x / d).
+  __syncthreads();
+  __shared__ float den_s[kMaxRowsDelta];
+  if (tid < rows) {
+    float ss = 0.f;
+    for (int i = 0; i < DV; i++) ss = __fadd_rn(ss, __fmul_rn(os[tid][i], os[tid][i]));
+    den_s[tid] = sqrtf(__fadd_rn(__fmul_rn(ss, a.inv_dv), a.eps));
+  }
+  __syncthreads();
+  const int col = vh * DV + j;                // column of the row
+  const int grp = col >> 7, ig = col & 127;   // 128-element group, index inside it
+  const int bb = ig >> 5, tq = ig & 31;
+  const int qlane = ((tq & 15) >> 2) * 8 + bb * 2 + (tq >> 4);
+  const int nbq = a.nv * DV / 32;
+  const float wj = a.norm_w[j];
+#pragma unroll
+  for (int t = 0; t < kMaxRowsDelta; t++) {
+    if (t >= rows) break;
+    const float zz = zin[t];
+    const float silu = __fdiv_rn(zz, __fadd_rn(1.f, exp_ref(-zz)));
+    const float g = __fmul_rn(__fmul_rn(__fdiv_rn(os[t][j], den_s[t]), wj), silu);
+    float amax = fabsf(g);
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+    const float d = __fdiv_rn(amax, 127.f);
+    const float id = d != 0.f ? __fdiv_rn(1.f, d) : 0.f;
+    uint8_t* row = a.q80 + (int64_t)t * a.q80_stride;
+    row[grp * 128 + qlane * 4 + (tq & 3)] = (uint8_t)(int8_t)roundf(__fmul_rn(g, id));
+    if (lane == 0) reinterpret_cast<float*>(row + (int64_t)nbq * 32)[col >> 5] = __half2float(__float2half_rn(d));
+  }
 }
 
 // Gated RMSNorm of every value head (src/qwen/norm.rs:16-25:
@@ -291,13 +380,40 @@ __global__ void __launch_bounds__(256) gated_norm_kernel(GatedNormArgs a) {
                    a.q80 ? a.q80 + (int64_t)row * a.q80_stride : nullptr, nullptr, xs);
 }
 
+int deltanet_smem_bytes(int dk, int dv) {
+  return (dk * dv + kMaxRowsDelta * ((dk + dv + 1 + 3) / 4 * 4)) * (int)sizeof(float);
+}
+
+template <int DK, int DV, int K>
+cudaError_t deltanet_launch_one(const DeltaNetArgs& a, cudaLaunchConfig_t& cfg) {
+  // the state's shared memory exceeds the default 48 KB at 128 x 128: opt in
+  // once per device (kept only once the attribute call succeeded)
+  static std::mutex mu;
+  static bool done[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!done[dev]) {
+      e = cudaFuncSetAttribute(deltanet_kernel<DK, DV, K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               deltanet_smem_bytes(DK, DV));
+      if (e != cudaSuccess) return e;
+      done[dev] = true;
+    }
+  }
+  cfg.dynamicSmemBytes = deltanet_smem_bytes(DK, DV);
+  return cudaLaunchKernelEx(&cfg, deltanet_kernel<DK, DV, K>, a);
+}
+
 template <int DK, int DV>
 cudaError_t deltanet_launch_k(const DeltaNetArgs& a, cudaLaunchConfig_t& cfg) {
   switch (a.conv_k) {
-    case 1: return cudaLaunchKernelEx(&cfg, deltanet_kernel<DK, DV, 1>, a);
-    case 2: return cudaLaunchKernelEx(&cfg, deltanet_kernel<DK, DV, 2>, a);
-    case 3: return cudaLaunchKernelEx(&cfg, deltanet_kernel<DK, DV, 3>, a);
-    default: return cudaLaunchKernelEx(&cfg, deltanet_kernel<DK, DV, 4>, a);
+    case 1: return deltanet_launch_one<DK, DV, 1>(a, cfg);
+    case 2: return deltanet_launch_one<DK, DV, 2>(a, cfg);
+    case 3: return deltanet_launch_one<DK, DV, 3>(a, cfg);
+    default: return deltanet_launch_one<DK, DV, 4>(a, cfg);
   }
 }
 
@@ -312,7 +428,9 @@ bool deltanet_supported(int dk, int dv) {
 
 cudaError_t deltanet_launch(const DeltaNetArgs& a, cudaStream_t st, bool pdl) {
   if (a.rows < 1 || a.rows > kMaxRowsDelta || a.rows >= kStateRing || !deltanet_supported(a.dk, a.dv) ||
-      a.conv_k > 4 || a.conv_k < 1 || a.rec_stride != deltanet_rec_stride(a.dk, a.dv))
+      a.conv_k > 4 || a.conv_k < 1 || a.rec_stride != deltanet_rec_stride(a.dk, a.dv) ||
+      (a.q80 && (!a.z || !a.norm_w || (a.nv * a.dv) % 128)) || !a.timeout_flag ||
+      ((uintptr_t)a.layers & 7))
     return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.nv);

@@ -3,6 +3,7 @@
 // src/qwen/quantized_moe.rs:253).  One warp per weight row; lane l sums the
 // float4 at columns 4l + 128t in order of t, then a butterfly over lanes.
 #include "kernels.cuh"
+#include "devfns.cuh"
 
 namespace iq {
 namespace {
@@ -10,7 +11,8 @@ namespace {
 __global__ void __launch_bounds__(256) f32_matvec_kernel(const float* __restrict__ w, int rows, int cols,
                                                          const float* __restrict__ x, int ldx, int k,
                                                          float* __restrict__ y, int ldy, const float* norm_w,
-                                                         float eps, float inv_cols) {
+                                                         float eps, float inv_cols, uint8_t* q8k_out,
+                                                         int q8k_stride) {
   // the weight rows do not depend on the previous kernel: request them first
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * 8 + warp;
@@ -47,6 +49,18 @@ __global__ void __launch_bounds__(256) f32_matvec_kernel(const float* __restrict
     for (int i = threadIdx.x; i < k * cols; i += 256)
       xw[i] = __fmul_rn(__fdiv_rn(xw[i], den[i / cols]), norm_w[i % cols]);
     __syncthreads();
+    if (q8k_out) {
+      // the normalized rows quantized to Q8_K for the matrices that follow
+      // (the (row, block) pairs shared out over every warp of the grid)
+      const int nb = cols / 256;
+      for (int p = blockIdx.x * 8 + warp; p < k * nb; p += gridDim.x * 8) {
+        const int row = p / nb, b = p % nb;
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = xw[row * cols + b * 256 + q8k_lane_pos(lane, i)];
+        quant_q8k_block_warp_v(v, q8k_out + (int64_t)row * q8k_stride, nb, b, lane);
+      }
+    }
   }
   if (r >= rows) return;
   float acc[8];
@@ -81,8 +95,8 @@ __global__ void __launch_bounds__(256) f32_matvec_kernel(const float* __restrict
 }  // namespace
 
 cudaError_t f32_matvec(const float* w, int rows, int cols, const float* x, int ldx, int k, float* y, int ldy,
-                       cudaStream_t st, bool pdl, const float* norm_w, float eps) {
-  if (cols % 4 || cols > 4096 || k < 1 || k > 8) return cudaErrorInvalidValue;
+                       cudaStream_t st, bool pdl, const float* norm_w, float eps, uint8_t* q8k_out, int q8k_stride) {
+  if (cols % 4 || cols > 4096 || k < 1 || k > 8 || (q8k_out && (!norm_w || cols % 256))) return cudaErrorInvalidValue;
   static bool configured[64] = {};
   if (first_on_device(configured))
     cudaFuncSetAttribute(f32_matvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 4096 * 4);
@@ -97,7 +111,7 @@ cudaError_t f32_matvec(const float* w, int rows, int cols, const float* x, int l
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, f32_matvec_kernel, w, rows, cols, x, ldx, k, y, ldy, norm_w, eps,
-                            (float)(1.0 / (double)cols));
+                            (float)(1.0 / (double)cols), q8k_out, q8k_stride);
 }
 
 }  // namespace iq

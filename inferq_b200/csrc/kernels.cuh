@@ -19,6 +19,14 @@ struct PrepArgs {
   uint8_t* q80;          // optional Q8_0 activation rows
   int q8k_stride;        // row strides in bytes (0: packed for `cols`)
   int q80_stride;
+  // Optional MoE combine applied to x first, written back to x (the hidden
+  // rows): x += sum_route y[row*topk + q] * w[row*topk + q] + y_shared[row] *
+  // sigmoid(selector logit), in route order (src/qwen/quantized_moe.rs:384-400).
+  const float* comb_y;   // [slot][comb_y_ld]: routed slots row*topk+q, shared slot rows*topk+row
+  int comb_y_ld;
+  const float* comb_w;   // [rows][topk] route weights
+  const float* comb_logits;  // selector logit at [row * comb_logits_ld + comb_experts]
+  int comb_logits_ld, comb_experts, comb_topk, comb_rows;
 };
 
 
@@ -28,9 +36,12 @@ cudaError_t dequant_rows(int dt, const uint8_t* w, int64_t row_bytes, int cols, 
 cudaError_t prep_rows(const PrepArgs& a, int rows, cudaStream_t st, bool pdl);
 
 // f32 matrix rows (router): y[i*ld + r] = dot(w[r], x[i]); fixed lane order.
-// With norm_w set, the input rows are first RMS-normalized (GGUF RMSNorm).
+// With norm_w set, the input rows are first RMS-normalized (GGUF RMSNorm),
+// and with q8k_out also written as Q8_K activation rows (row stride
+// q8k_stride bytes) for the quantized matrices that take the same input.
 cudaError_t f32_matvec(const float* w, int rows, int cols, const float* x, int ldx, int k, float* y,
-                       int ldy, cudaStream_t st, bool pdl, const float* norm_w = nullptr, float eps = 0.f);
+                       int ldy, cudaStream_t st, bool pdl, const float* norm_w = nullptr, float eps = 0.f,
+                       uint8_t* q8k_out = nullptr, int q8k_stride = 0);
 
 // Wide Q8_0 product on the tensor cores (wide.cu): y[t*out_ld + r] for
 // ntok input rows x[t*ldx ..]; qx (ntok x cols f16), dT (cols/32 x

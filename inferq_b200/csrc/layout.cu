@@ -98,6 +98,40 @@ __global__ void __launch_bounds__(256) prep_rows_kernel(PrepArgs a) {
       ld_q8k_lane(x, warp + 8 * j, lane, v[j], a.cols);
       if (a.norm_w) ld_q8k_lane(a.norm_w, warp + 8 * j, lane, w[j], a.cols);
     }
+  if (a.comb_y) {
+    // the MoE combine of this row, element by element as moe_combine does:
+    // r = sum_q y_q * w_q (route order), h += r + y_shared * sigmoid(sel)
+    const float sl = a.comb_logits[(int64_t)row * a.comb_logits_ld + a.comb_experts];
+    const float selector = __fdiv_rn(1.f, __fadd_rn(1.f, exp_ref(-sl)));
+    const float* ysh = a.comb_y + (int64_t)(a.comb_rows * a.comb_topk + row) * a.comb_y_ld;
+#pragma unroll
+    for (int j = 0; j < MAXB; j++) {
+      const int b = warp + 8 * j;
+      if (b >= nb) continue;
+      // every route's values requested before the ordered sum
+      constexpr int kMaxTopk = 16;
+      float r[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, ys[8], yq[kMaxTopk][8], wq[kMaxTopk];
+#pragma unroll
+      for (int q = 0; q < kMaxTopk; q++)
+        if (q < a.comb_topk) {
+          wq[q] = a.comb_w[row * a.comb_topk + q];
+          ld_q8k_lane(a.comb_y + (int64_t)(row * a.comb_topk + q) * a.comb_y_ld, b, lane, yq[q], a.cols);
+        }
+      ld_q8k_lane(ysh, b, lane, ys, a.cols);
+#pragma unroll
+      for (int q = 0; q < kMaxTopk; q++)
+        if (q < a.comb_topk)
+#pragma unroll
+          for (int i = 0; i < 8; i++) r[i] = __fadd_rn(r[i], __fmul_rn(yq[q][i], wq[q]));
+#pragma unroll
+      for (int i = 0; i < 8; i++) v[j][i] = __fadd_rn(v[j][i], __fadd_rn(r[i], __fmul_rn(ys[i], selector)));
+      if (b * 256 + 32 * (lane & 7) < a.cols) {
+        float* p = const_cast<float*>(x) + b * 256 + 32 * (lane & 7) + 4 * (lane >> 3);
+        *reinterpret_cast<float4*>(p) = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+        *reinterpret_cast<float4*>(p + 16) = make_float4(v[j][4], v[j][5], v[j][6], v[j][7]);
+      }
+    }
+  }
   if (a.norm_w) {
     float ss = 0.f;
 #pragma unroll
@@ -150,7 +184,8 @@ cudaError_t prep_rows(const PrepArgs& a, int rows, cudaStream_t st, bool pdl) {
   const int nb = (a.cols + 255) / 256;
   auto a16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
   if (a.cols % (a.q8k ? 256 : 128) || a.ldx % 4 || !a16(a.x) || (a.norm_w && !a16(a.norm_w)) ||
-      (a.xn_out && (a.ldxn % 4 || !a16(a.xn_out))))
+      (a.xn_out && (a.ldxn % 4 || !a16(a.xn_out))) ||
+      (a.comb_y && (a.comb_y_ld % 4 || !a16(a.comb_y) || a.comb_topk > 16 || a.cols % 256)))
     return cudaErrorInvalidValue;
   if (nb <= 8) return cudaLaunchKernelEx(&cfg, prep_rows_kernel<1>, a);
   if (nb <= 16) return cudaLaunchKernelEx(&cfg, prep_rows_kernel<2>, a);

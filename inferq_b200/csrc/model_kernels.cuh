@@ -36,6 +36,15 @@ struct DeltaNetArgs {
   int rec_stride;               // deltanet_rec_stride(dk, dv)
   const int* cur;               // device: conv ring index of the current state
   const int* pending;           // device: records of the last pass still to replay
+  // Optional fused gated RMSNorm + Q8_0 quantization of the output rows (for
+  // a Q8_0 output projection): q80 = quant(norm(o) * w * silu(z)); `out` is
+  // then not written.
+  uint8_t* q80;                 // [rows][q80_stride] Q8_0 activation rows, or null
+  int q80_stride;
+  const float* z;  int z_ld;    // gate projections [rows][z_ld]
+  const float* norm_w;          // [dv]
+  float eps, inv_dv;
+  int* timeout_flag;            // device flag set when a bounded wait gave up
 };
 int deltanet_rec_stride(int dk, int dv);
 bool deltanet_supported(int dk, int dv);
@@ -70,6 +79,10 @@ struct AttnArgs {
   float eps;
   const int* pos;                // device: position of row 0
   int chunk_ctas;                // chunks the grid covers: ceil(max positions / kAttnChunk)
+  // Optional: the combine writes the output projection's quantized input
+  // rows (Q8_K when hd == 256, Q8_0 when hd % 128 == 0) instead of `out`.
+  uint8_t* q8k_out; int q8k_stride;
+  uint8_t* q80_out; int q80_stride;
 };
 // Positions per split of the scan.  Chunk c always covers absolute positions
 // [c*kAttnChunk, (c+1)*kAttnChunk), and a row combines its chunks in order, so
@@ -119,6 +132,7 @@ struct MoeRouteArgs {
   int gu_ld;
   const uint8_t* act_mid; int act_mid_bytes;   // silu(g)*u rows per slot, in the down matrix's layout
   float* y;  int y_ld;                         // [slot][hidden]
+  int swiglu_down;  // 1: down jobs stage silu(g)*u from gu_out themselves (kActSwiGLU)
 };
 cudaError_t moe_route_launch(const MoeRouteArgs& a, const MoeRouteStatic& s, cudaStream_t st, bool pdl);
 

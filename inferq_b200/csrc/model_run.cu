@@ -171,7 +171,17 @@ struct Ctx {
   bool pdl;
   // IQ_NO_PDL=1 turns programmatic dependent launch off (kernel timing,
   // debugging); results are identical either way.
-  Ctx(iq_state* s_) : s(s_), m(s_->m), c(s_->m->cfg), st(s_->st), pdl(!s_->profiling && !getenv("IQ_NO_PDL")) {}
+  // Kernel fusions (IQ_FUSE=<bitmask>; results are bitwise the same either
+  // way).  Default 1|2|4|16, measured faster at k = 1, 4 and 8 (35B shapes);
+  // 8 puts redundant normalization on every router CTA and measured slower:
+  // 1 MoE combine into the next RMSNorm, 2 gated norm + Q8_0 into the
+  // DeltaNet kernel, 4 SwiGLU into the down GEMV, 8 RMSNorm + Q8_K into the
+  // f32 router, 16 output-projection quantization into the attention combine.
+  int fuse;
+  Ctx(iq_state* s_) : s(s_), m(s_->m), c(s_->m->cfg), st(s_->st), pdl(!s_->profiling && !getenv("IQ_NO_PDL")) {
+    const char* f = getenv("IQ_FUSE");
+    fuse = f ? atoi(f) : 23;
+  }
   // Stage timer: under profiling every stage is bracketed by CUDA events.
   void mark(const char* name) {
     if (!s->profiling) return;
@@ -182,6 +192,10 @@ struct Ctx {
   }
   int* pos() const { return s->ctrl.as<int>(); }
   int* attn_pos = nullptr;  // KV position the attention layers use (default pos())
+  // The MoE combine of the last MoE block, applied by the next kernel that
+  // normalizes the hidden rows (one launch fewer per layer).
+  bool comb_pending = false;
+  MoeCombineArgs comb = {};
   int* cur() const { return s->ctrl.as<int>() + 1; }  // DeltaNet conv ring index
   int* pending() const { return s->ctrl.as<int>() + 6; }  // DeltaNet records to replay
   int* result() const { return s->ctrl.as<int>() + 2; }
@@ -191,8 +205,11 @@ struct Ctx {
 
 bool needs(int dt, bool q80) { return dt >= 0 && (q80 ? dt == Q8_0 : dt != Q8_0 && dt != F32); }
 
+int flush_combine(Ctx& x);
+
 int prep(Ctx& x, const float* in, int ld, int cols, const float* norm, int k, bool q8k, bool q80, float* xn,
          int ldxn = 0) {
+  if (x.comb_pending && in != x.s->hidden.as<float>()) TRY(flush_combine(x));
   PrepArgs a = {};
   a.x = in;
   a.ldx = ld;
@@ -206,8 +223,28 @@ int prep(Ctx& x, const float* in, int ld, int cols, const float* norm, int k, bo
   a.q80 = q80 ? x.s->act80.as<uint8_t>() : nullptr;
   a.q8k_stride = (int)x.s->act8k_bytes;
   a.q80_stride = (int)x.s->act80_bytes;
+  if (x.comb_pending && in == x.s->hidden.as<float>()) {
+    a.comb_y = x.comb.y;
+    a.comb_y_ld = x.comb.y_ld;
+    a.comb_w = x.comb.route_weight;
+    a.comb_logits = x.comb.logits;
+    a.comb_logits_ld = x.comb.logits_ld;
+    a.comb_experts = x.comb.experts;
+    a.comb_topk = x.comb.topk;
+    a.comb_rows = x.comb.rows;
+    x.comb_pending = false;
+  }
   ++x.s->launch_count;
   IQ_CUDA(prep_rows(a, k, x.st, x.pdl));
+  return IQ_OK;
+}
+
+// Launch a pending MoE combine on its own (when no normalizing kernel follows).
+int flush_combine(Ctx& x) {
+  if (!x.comb_pending) return IQ_OK;
+  x.comb_pending = false;
+  ++x.s->launch_count;
+  IQ_CUDA(moe_combine_launch(x.comb, x.st, x.pdl));
   return IQ_OK;
 }
 
@@ -343,11 +380,19 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   const int H = c.hidden_size, E = c.num_experts;
   const bool q8k = needs(W.gate.dt, false) || needs(W.sh_gate.dt, false) || needs(W.router.dt, false);
   const bool q80 = needs(W.gate.dt, true) || needs(W.sh_gate.dt, true) || needs(W.router.dt, true);
+  float* lg = s->logits_moe.as<float>();
+  if ((x.fuse & 8) && !W.router.present() && !q80 && !x.comb_pending && H % 256 == 0) {
+    // f32 router: it normalizes the rows itself and writes their Q8_K form
+    // for the expert matrices (one launch for norm, quantization and router)
+    ++x.s->launch_count;
+    IQ_CUDA(f32_matvec(W.router_sel.p(), E + 1, H, s->hidden.as<float>(), H, k, lg, E + 1, x.st, x.pdl,
+                       L.post_norm.p(), c.rms_norm_eps, s->act8k.as<uint8_t>(), (int)s->act8k_bytes));
+    x.mark("moe.router");
+  } else {
   TRY(pre(x, row_pro(x, s->hidden.as<float>(), H, H, L.post_norm.p(), k, q8k, q80, s->xn.as<float>())));
   x.mark("act.prep");
   const float* rin = s->xn.as<float>();
   const float* rnorm = nullptr;
-  float* lg = s->logits_moe.as<float>();
   if (W.router.present()) {
     ++x.s->launch_count;
     IQ_CUDA(qmv_launch(x.s->jobs.as<QmvJob>() + R.router.job, R.router.njobs, nullptr, R.router.ntiles, R.router.smem,
@@ -360,6 +405,7 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
     ++x.s->launch_count;
     IQ_CUDA(f32_matvec(W.router_sel.p(), E + 1, H, rin, H, k, lg, E + 1, x.st, x.pdl, rnorm, c.rms_norm_eps));
     x.mark("moe.router");
+  }
   }
   MoeRouteArgs a = {};
   a.logits = lg;
@@ -390,6 +436,7 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   a.act_mid_bytes = (int)s->act_mid_bytes;
   a.y = s->y.as<float>();
   a.y_ld = H;
+  a.swiglu_down = (x.fuse & 4) ? 1 : 0;
   MoeRouteStatic t = {};
   const int F = c.moe_intermediate_size, Fs = c.shared_expert_intermediate_size;
   t.gate = W.gate.p();
@@ -457,9 +504,11 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   b.act_bytes = (int)s->act_mid_bytes;
   b.down_q80 = W.down.dt == Q8_0;
   b.sh_down_q80 = W.sh_down.dt == Q8_0;
-  ++x.s->launch_count;
-  IQ_CUDA(moe_act_launch(b, x.st, x.pdl));
-  x.mark("moe.act");
+  if (!(x.fuse & 4)) {  // else SwiGLU and its quantization run inside the down GEMV (kActSwiGLU jobs)
+    ++x.s->launch_count;
+    IQ_CUDA(moe_act_launch(b, x.st, x.pdl));
+    x.mark("moe.act");
+  }
   // Expert parallelism: this rank computes only the routed slots of its own
   // experts; the others stay exactly zero, and one sum over the ranks then
   // leaves every slot with the value its owner computed (x + 0 = x), so the
@@ -469,8 +518,8 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   const size_t routed = (size_t)k * c.num_experts_per_tok * H;
   if (ep) IQ_CUDA(cudaMemsetAsync(a.y, 0, routed * sizeof(float), x.st));
   ++x.s->launch_count;
-  IQ_CUDA(qmv_launch(a.down_jobs, 0, a.down_count, down_tiles, (k * c.num_experts_per_tok + k) * (int)s->act_mid_bytes,
-                     x.st, x.pdl));
+  IQ_CUDA(qmv_launch(a.down_jobs, 0, a.down_count, down_tiles,
+                     ((x.fuse & 4) ? k : k * c.num_experts_per_tok + k) * (int)s->act_mid_bytes, x.st, x.pdl));
   x.mark("moe.down");
   if (ep) {
     const ncclResult_t r =
@@ -490,9 +539,9 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   cb.rows = k;
   cb.topk = c.num_experts_per_tok;
   cb.dim = H;
-  ++x.s->launch_count;
-  IQ_CUDA(moe_combine_launch(cb, x.st, x.pdl));
-  x.mark("moe.combine");
+  x.comb = cb;
+  x.comb_pending = true;  // applied by the next normalization of the hidden rows
+  if (!(x.fuse & 1)) TRY(flush_combine(x));
   return IQ_OK;
 }
 
@@ -526,11 +575,29 @@ int run_delta(Ctx& x, const Layer& L, const LayerRec& R, int k, int li) {
   a.tiled_heads = c.value_heads_tiled;
   a.ba_interleaved = D.ba_fused;
   a.rec_stride = deltanet_rec_stride(a.dk, a.dv);
+  a.timeout_flag = qmv_timeout_flag();
   a.cur = x.cur();
   a.pending = x.pending();
+  // a Q8_0 output projection takes its activations straight from the
+  // recurrence kernel (gated norm and quantization fused)
+  const bool fuse = (x.fuse & 2) && D.out.dt == Q8_0 && vdim % 128 == 0;
+  if (fuse) {
+    a.q80 = s->act80.as<uint8_t>();
+    a.q80_stride = (int)s->act80_bytes;
+    a.z = s->z.as<float>();
+    a.z_ld = vdim;
+    a.norm_w = D.norm.p();
+    a.eps = c.rms_norm_eps;
+    a.inv_dv = (float)(1.0 / c.linear_value_head_dim);
+  }
   ++x.s->launch_count;
   IQ_CUDA(deltanet_launch(a, x.st, x.pdl));
   x.mark("dn.recurrence");
+  if (fuse) {
+    TRY(qmv(x, R.out));
+    x.mark("dn.out");
+    return IQ_OK;
+  }
   GatedNormArgs g = {};
   g.o = s->dn_out.as<float>();
   g.o_ld = vdim;
@@ -602,6 +669,17 @@ int run_attention(Ctx& x, const Layer& L, const LayerRec& R, int k, int fi) {
   a.eps = c.rms_norm_eps;
   a.pos = x.attn_pos ? x.attn_pos : x.pos();
   a.chunk_ctas = s->max_chunks;
+  // the combine quantizes the output projection's input itself when a head
+  // is whole blocks of that projection's activation format
+  const bool o8k = needs(A.o.dt, false), o80 = needs(A.o.dt, true);
+  const bool fuse_out = (x.fuse & 16) && ((o8k && c.head_dim == 256) || (o80 && c.head_dim % 128 == 0));
+  if (fuse_out && o8k) {
+    a.q8k_out = s->act8k.as<uint8_t>();
+    a.q8k_stride = (int)s->act8k_bytes;
+  } else if (fuse_out) {
+    a.q80_out = s->act80.as<uint8_t>();
+    a.q80_stride = (int)s->act80_bytes;
+  }
   ++x.s->launch_count;
   IQ_CUDA(attn_prep_launch(a, x.st, x.pdl));
   x.mark("attn.prep");
@@ -613,7 +691,7 @@ int run_attention(Ctx& x, const Layer& L, const LayerRec& R, int k, int fi) {
   x.mark("attn.combine");
   const QmvPrologue out_pro = row_pro(x, s->attn_out.as<float>(), nhd, nhd, nullptr, k, needs(A.o.dt, false),
                                      needs(A.o.dt, true));
-  TRY(qmv(x, R.out, &out_pro));
+  TRY(qmv(x, R.out, fuse_out ? nullptr : &out_pro));
   x.mark("attn.out");
   return IQ_OK;
 }
@@ -663,6 +741,7 @@ int run_pass(iq_state* s, int k, bool verify) {
   h.verify = verify ? 1 : 0;
   h.result = x.result();
   h.scores = nullptr;
+  TRY(flush_combine(x));
   ++x.s->launch_count;
   IQ_CUDA(argmax_launch(h, x.st, x.pdl));
   x.mark("head.argmax");
@@ -709,6 +788,7 @@ int run_mtp_block(iq_state* s, int k) {
   TRY(run_moe(x, m->mtp_layer, P.mtp, k, c.num_hidden_layers));
   TRY(pre(x, row_pro(x, s->hidden.as<float>(), H, H, m->mtp_head_norm.p(), k, needs(m->lm_head.dt, false),
                      needs(m->lm_head.dt, true), s->xn.as<float>())));
+  TRY(flush_combine(x));
   ++s->launch_count;
   IQ_CUDA(set_int_launch(x.attn_pos, k, true, x.st, x.pdl));
   x.mark("mtp.block");

@@ -24,12 +24,13 @@ static_assert(offsetof(QmvJob, rowmap) % 8 == 0 && offsetof(QmvJob, outrow) % 8 
 __device__ __forceinline__ void put_job(QmvJob* j, const uint8_t* w, const void* tm, const void* tm_tail,
                                         int row_base, int64_t w_row_bytes, int dt, int rows, int cols, int ks,
                                         const uint8_t* act, int act_bytes, float* out, int out_ld, int n, int tile0,
-                                        int act_nrows, uint64_t rowmap, uint64_t out_lo, uint64_t out_hi) {
+                                        int act_nrows, uint64_t rowmap, uint64_t out_lo, uint64_t out_hi,
+                                        int act_mode = kActQuantized) {
   j->w = w;
   j->tmap = tm;
   j->tmap_tail = tm_tail;
   j->row_base = row_base;
-  j->pad_ = 0;
+  j->act_mode = act_mode;
   j->act = act;
   j->out = out;
   j->resid = nullptr;
@@ -180,9 +181,15 @@ __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRoute
     put_job(&a.gu_jobs[2 * ri + 1], s.up + le * s.up_stride, s.up_tm, s.up_tm_tail, le * a.ffn, s.gate_row_bytes,
             s.gate_dt, a.ffn, a.hidden, s.ks_gate, ain, ab, a.gu_out + a.ffn, a.gu_ld, n,
             (2 * ri + 1) * s.tiles_gate, a.rows, gmap, olo, ohi);
-    put_job(&a.down_jobs[ri], s.down + le * s.down_stride, s.down_tm, s.down_tm_tail, le * a.hidden,
-            s.down_row_bytes, s.down_dt, a.hidden, a.ffn, s.ks_down, a.act_mid, a.act_mid_bytes, a.y, a.y_ld, n,
-            ri * s.tiles_down, slots_routed + a.rows, dmap, olo, ohi);
+    // down: staged from this expert's gate|up rows as quant(silu(g) * u)
+    if (a.swiglu_down)
+      put_job(&a.down_jobs[ri], s.down + le * s.down_stride, s.down_tm, s.down_tm_tail, le * a.hidden,
+              s.down_row_bytes, s.down_dt, a.hidden, a.ffn, s.ks_down, reinterpret_cast<const uint8_t*>(a.gu_out),
+              a.gu_ld * 4, a.y, a.y_ld, n, ri * s.tiles_down, slots_routed + a.rows, dmap, olo, ohi, kActSwiGLU);
+    else
+      put_job(&a.down_jobs[ri], s.down + le * s.down_stride, s.down_tm, s.down_tm_tail, le * a.hidden,
+              s.down_row_bytes, s.down_dt, a.hidden, a.ffn, s.ks_down, a.act_mid, a.act_mid_bytes, a.y, a.y_ld, n,
+              ri * s.tiles_down, slots_routed + a.rows, dmap, olo, ohi);
   }
   if (threadIdx.x == 0) {
     // shared expert: every row, slots rows*topk + t
@@ -201,9 +208,15 @@ __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRoute
     put_job(&a.gu_jobs[2 * n_res + 1], s.sh_up, s.sh_up_tm, s.sh_up_tm_tail, 0, s.sh_gate_row_bytes, s.sh_gate_dt,
             a.sh_ffn, a.hidden, s.ks_sh_gate, ain, ab, a.gu_out + a.sh_ffn, a.gu_ld, a.rows,
             2 * n_res * s.tiles_gate + s.tiles_sh_gate, a.rows, gmap, olo, ohi);
-    put_job(&a.down_jobs[n_res], s.sh_down, s.sh_down_tm, s.sh_down_tm_tail, 0, s.sh_down_row_bytes, s.sh_down_dt,
-            a.hidden, a.sh_ffn, s.ks_sh_down, a.act_mid, a.act_mid_bytes, a.y, a.y_ld, a.rows, n_res * s.tiles_down,
-            slots_routed + a.rows, dmap, olo, ohi);
+    if (a.swiglu_down)
+      put_job(&a.down_jobs[n_res], s.sh_down, s.sh_down_tm, s.sh_down_tm_tail, 0, s.sh_down_row_bytes,
+              s.sh_down_dt, a.hidden, a.sh_ffn, s.ks_sh_down, reinterpret_cast<const uint8_t*>(a.gu_out),
+              a.gu_ld * 4, a.y, a.y_ld, a.rows, n_res * s.tiles_down, slots_routed + a.rows, dmap, olo, ohi,
+              kActSwiGLU);
+    else
+      put_job(&a.down_jobs[n_res], s.sh_down, s.sh_down_tm, s.sh_down_tm_tail, 0, s.sh_down_row_bytes,
+              s.sh_down_dt, a.hidden, a.sh_ffn, s.ks_sh_down, a.act_mid, a.act_mid_bytes, a.y, a.y_ld, a.rows,
+              n_res * s.tiles_down, slots_routed + a.rows, dmap, olo, ohi);
     *a.gu_count = s.with_shared ? 2 * n_res + 2 : 2 * n_res;
     *a.down_count = s.with_shared ? n_res + 1 : n_res;
     *a.union_size = total_union;

@@ -482,9 +482,10 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
   pdl_wait();
   pdl_trigger();
 
-  // staged activation key: every row of one activation buffer
+  // staged activation key: every row of one activation buffer (or, for a
+  // SwiGLU job, the job itself)
   const uint8_t* staged_act = nullptr;
-  int staged_rows = -1, staged_stride = 0;
+  int staged_rows = -1, staged_stride = 0, staged_job = -1;
   uint32_t n = 0;  // units consumed by this warp
   bool ok = true;
   for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
@@ -492,7 +493,46 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
     const QmvJob& jb = jobs[ct.job];
     const int nin = jb.n;
     const int used = act_used_bytes(jb.dtype, jb.cols);
-    if (jb.act != staged_act || jb.act_nrows != staged_rows || used != staged_stride) {
+    const bool swiglu = jb.act_mode == kActSwiGLU;
+    if (swiglu && ct.job != staged_job) {
+      // silu(g) * u of the job's input rows (g / (1 + exp(-g)), times u;
+      // src/qwen/quantized_moe.rs:446), quantized as the activation row of the
+      // job's matrix (Q8_K blocks of 256 or Q8_0 groups of 128 per warp);
+      // staged as rows 0..n-1
+      __syncthreads();  // no warp still reads the previous staging
+      const float* gu = reinterpret_cast<const float*>(jb.act);
+      const int gl = jb.act_row_bytes / 4, F = jb.cols;
+      if (jb.dtype == Q8_0) {
+        const int ng = F / 128;
+        for (int i = warp; i < nin * ng; i += kQmvWarps) {
+          const int c = i / ng, g = i % ng;
+          const float* gr = gu + (int64_t)jb.rowmap[c] * gl;
+          const int e0 = q80_lane_base(g, lane);
+          float v[4];
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const float x = gr[e0 + e];
+            v[e] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.f, exp_ref(-x))), gr[F + e0 + e]);
+          }
+          quant_q80_group_warp_v(v, act_smem + c * used, F / 32, g, lane);
+        }
+      } else {
+        const int nbk = F / 256;
+        for (int i = warp; i < nin * nbk; i += kQmvWarps) {
+          const int c = i / nbk, b = i % nbk;
+          const float* gr = gu + (int64_t)jb.rowmap[c] * gl;
+          float g8[8], u8[8];
+          ld_q8k_lane(gr, b, lane, g8);
+          ld_q8k_lane(gr + F, b, lane, u8);
+#pragma unroll
+          for (int e = 0; e < 8; e++) g8[e] = __fmul_rn(__fdiv_rn(g8[e], __fadd_rn(1.f, exp_ref(-g8[e]))), u8[e]);
+          quant_q8k_block_warp_v(g8, act_smem + c * used, nbk, b, lane);
+        }
+      }
+      __syncthreads();
+      staged_job = ct.job;
+      staged_act = nullptr;
+    } else if (!swiglu && (jb.act != staged_act || jb.act_nrows != staged_rows || used != staged_stride)) {
       __syncthreads();  // no warp still reads the previous staging
       const int words = used / 16;
 #pragma unroll 4
@@ -505,11 +545,14 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
       staged_act = jb.act;
       staged_rows = jb.act_nrows;
       staged_stride = used;
+      staged_job = -1;
     }
-    const uint8_t* bact = gid < nin ? act_smem + jb.rowmap[gid] * used : nullptr;
+    // staged row of input column i: rowmap[i], or i for a SwiGLU job
+    auto srow = [&](int i) { return swiglu ? i : (int)jb.rowmap[i]; };
+    const uint8_t* bact = gid < nin ? act_smem + srow(gid) * used : nullptr;
     ActCols ac;
-    ac.c[0] = 2 * tig < nin ? act_smem + jb.rowmap[2 * tig] * used : nullptr;
-    ac.c[1] = 2 * tig + 1 < nin ? act_smem + jb.rowmap[2 * tig + 1] * used : nullptr;
+    ac.c[0] = 2 * tig < nin ? act_smem + srow(2 * tig) * used : nullptr;
+    ac.c[1] = 2 * tig + 1 < nin ? act_smem + srow(2 * tig + 1) * used : nullptr;
 
     Frag f;
 #pragma unroll

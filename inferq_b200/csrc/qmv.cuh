@@ -16,6 +16,11 @@
 
 namespace iq {
 
+enum QmvActMode : int {
+  kActQuantized = 0,  // act rows are quantized activation rows (Q8_K / Q8_0 layout)
+  kActSwiGLU = 1,     // act rows are f32 gate|up projections: stage quant(silu(g) * u)
+};
+
 enum QmvEpilogue : int {
   kEpiStore = 0,     // out = y
   kEpiResidual = 1,  // out = resid + y   (resid may alias out)
@@ -37,7 +42,9 @@ struct QmvJob {
   int tile0;             // first global tile of this job
   int epi;
   int row_base;          // row of the tensor map where this job's row 0 lies
-  int pad_;
+  int act_mode;          // kActQuantized, or kActSwiGLU: `act` holds f32 rows
+                         // [gate cols | up cols] (act_row_bytes apart, selected by
+                         // rowmap) staged as the quantized silu(gate) * up
   uint8_t rowmap[8];     // activation row of input column i
   int16_t outrow[8];     // output row (of out) of input column i
 };
