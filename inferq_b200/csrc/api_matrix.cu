@@ -65,7 +65,14 @@ int upload_rows(int dtype, const void* data, int64_t rows, int64_t cols, int loc
 struct Scratch {
   DevBuf x, y, act, jobs, wide_w;
 };
-static thread_local Scratch g_scratch;
+// Operator scratch: one set per thread and per device, so a thread that calls
+// on several GPUs never hands one GPU's buffer to another's kernel.
+Scratch& scratch() {
+  static thread_local Scratch per_device[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  return per_device[dev];
+}
 
 // y[i*rows + r] for i < k <= 8; x, y device pointers.
 int matrix_forward_dev(const iq_matrix* m, const float* x, int k, float* y, cudaStream_t st) {
@@ -76,26 +83,26 @@ int matrix_forward_dev(const iq_matrix* m, const float* x, int k, float* y, cuda
   }
   const bool kq = m->dtype != Q8_0;
   const int64_t arb = kq ? act_row_bytes_q8k(m->cols) : act_row_bytes_q80(m->cols);
-  IQ_CUDA(g_scratch.act.reserve((size_t)(arb * 8)));
+  IQ_CUDA(scratch().act.reserve((size_t)(arb * 8)));
   if ((uintptr_t)x & 15) {  // the quantizer reads 16-byte vectors
-    IQ_CUDA(g_scratch.x.reserve((size_t)(m->cols * k * sizeof(float))));
-    IQ_CUDA(cudaMemcpyAsync(g_scratch.x.p, x, (size_t)(m->cols * k * sizeof(float)), cudaMemcpyDeviceToDevice, st));
-    x = g_scratch.x.as<float>();
+    IQ_CUDA(scratch().x.reserve((size_t)(m->cols * k * sizeof(float))));
+    IQ_CUDA(cudaMemcpyAsync(scratch().x.p, x, (size_t)(m->cols * k * sizeof(float)), cudaMemcpyDeviceToDevice, st));
+    x = scratch().x.as<float>();
   }
   PrepArgs pa = {};
   pa.x = x;
   pa.ldx = (int)m->cols;
   pa.cols = (int)m->cols;
   pa.inv_cols = 1.f / (float)m->cols;
-  if (kq) pa.q8k = g_scratch.act.as<uint8_t>();
-  else pa.q80 = g_scratch.act.as<uint8_t>();
+  if (kq) pa.q8k = scratch().act.as<uint8_t>();
+  else pa.q80 = scratch().act.as<uint8_t>();
   IQ_CUDA(prep_rows(pa, k, st, false));
   QmvJob j;
   memset(&j, 0, sizeof j);
   j.w = m->base;
   j.tmap = m->tmap();
   j.tmap_tail = m->tmap_tail();
-  j.act = g_scratch.act.as<uint8_t>();
+  j.act = scratch().act.as<uint8_t>();
   j.out = y;
   j.w_row_bytes = m->row_bytes;
   j.act_row_bytes = (int)arb;
@@ -193,29 +200,29 @@ int iq_matrix_forward_wide(const iq_matrix* m, const float* x, int input_rows, f
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (m->dtype == Q6_K) {
     const size_t need = wide_q6k_scratch_bytes(m->rows, m->cols, input_rows, nullptr, nullptr);
-    IQ_CUDA(g_scratch.wide_w.reserve(need));
+    IQ_CUDA(scratch().wide_w.reserve(need));
     WideQ6kScratch sc;
-    wide_q6k_scratch_bytes(m->rows, m->cols, input_rows, &sc, g_scratch.wide_w.as<uint8_t>());
+    wide_q6k_scratch_bytes(m->rows, m->cols, input_rows, &sc, scratch().wide_w.as<uint8_t>());
     IQ_CUDA(wide_q6k_forward(m->base, m->rows, m->cols, m->row_bytes, x, (int)m->cols, input_rows, y, (int)m->rows,
                              sc, st));
     return IQ_OK;
   }
   if (m->dtype == Q4_K) {
     const size_t need = wide_q4k_scratch_bytes(m->rows, m->cols, input_rows, nullptr, nullptr);
-    IQ_CUDA(g_scratch.wide_w.reserve(need));
+    IQ_CUDA(scratch().wide_w.reserve(need));
     WideQ4kScratch sc;
-    wide_q4k_scratch_bytes(m->rows, m->cols, input_rows, &sc, g_scratch.wide_w.as<uint8_t>());
+    wide_q4k_scratch_bytes(m->rows, m->cols, input_rows, &sc, scratch().wide_w.as<uint8_t>());
     IQ_CUDA(wide_q4k_forward(m->base, m->rows, m->cols, m->row_bytes, x, (int)m->cols, input_rows, y, (int)m->rows,
                              sc, st));
     return IQ_OK;
   }
   IQ_CHECK(m->cols % 128 == 0, IQ_EINVAL, "the wide product needs cols %% 128 == 0, got %lld", (long long)m->cols);
   const int64_t nb = m->cols / 32;
-  IQ_CUDA(g_scratch.x.reserve((size_t)(input_rows * m->cols * 2)));
-  IQ_CUDA(g_scratch.act.reserve((size_t)(nb * wide_ldd(input_rows) * 4)));
-  IQ_CUDA(g_scratch.wide_w.reserve((size_t)(m->rows * m->cols * 2)));
+  IQ_CUDA(scratch().x.reserve((size_t)(input_rows * m->cols * 2)));
+  IQ_CUDA(scratch().act.reserve((size_t)(nb * wide_ldd(input_rows) * 4)));
+  IQ_CUDA(scratch().wide_w.reserve((size_t)(m->rows * m->cols * 2)));
   IQ_CUDA(wide_q80_forward(m->base, m->rows, m->cols, m->row_bytes, x, (int)m->cols, input_rows, y, (int)m->rows,
-                           g_scratch.x.as<__half>(), g_scratch.act.as<float>(), g_scratch.wide_w.as<__half>(), st));
+                           scratch().x.as<__half>(), scratch().act.as<float>(), scratch().wide_w.as<__half>(), st));
   return IQ_OK;
 }
 
@@ -242,14 +249,14 @@ int iq_matrix_forward_rows(const iq_matrix* m, const float* x, int64_t input_row
   IQ_CHECK(m && x && y, IQ_EINVAL, "iq_matrix_forward_rows: null argument");
   IQ_CHECK(input_rows >= 1, IQ_EINVAL, "expected at least one input row, got %lld", (long long)input_rows);
   cudaStream_t st = nullptr;
-  IQ_CUDA(g_scratch.x.reserve((size_t)(8 * m->cols * 4)));
-  IQ_CUDA(g_scratch.y.reserve((size_t)(8 * m->rows * 4)));
+  IQ_CUDA(scratch().x.reserve((size_t)(8 * m->cols * 4)));
+  IQ_CUDA(scratch().y.reserve((size_t)(8 * m->rows * 4)));
   for (int64_t r0 = 0; r0 < input_rows; r0 += 8) {
     const int k = (int)std::min<int64_t>(8, input_rows - r0);
-    IQ_CUDA(cudaMemcpyAsync(g_scratch.x.p, x + r0 * m->cols, (size_t)(k * m->cols * 4), cudaMemcpyHostToDevice, st));
-    int rc = matrix_forward_dev(m, g_scratch.x.as<float>(), k, g_scratch.y.as<float>(), st);
+    IQ_CUDA(cudaMemcpyAsync(scratch().x.p, x + r0 * m->cols, (size_t)(k * m->cols * 4), cudaMemcpyHostToDevice, st));
+    int rc = matrix_forward_dev(m, scratch().x.as<float>(), k, scratch().y.as<float>(), st);
     if (rc) return rc;
-    IQ_CUDA(cudaMemcpyAsync(y + r0 * m->rows, g_scratch.y.p, (size_t)(k * m->rows * 4), cudaMemcpyDeviceToHost, st));
+    IQ_CUDA(cudaMemcpyAsync(y + r0 * m->rows, scratch().y.p, (size_t)(k * m->rows * 4), cudaMemcpyDeviceToHost, st));
   }
   IQ_CUDA(cudaStreamSynchronize(st));
   return IQ_OK;

@@ -213,8 +213,11 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a) {
 template <int D>
 cudaError_t launch_scan(dim3 grid, size_t smem, cudaStream_t st, bool pdl, const AttnArgs& a) {
   static bool configured[64] = {};
-  if (first_on_device(configured))
-    cudaFuncSetAttribute(attn_scan_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  static std::mutex mu;
+  const cudaError_t e = once_per_device(configured, mu, [] {
+    return cudaFuncSetAttribute(attn_scan_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  });
+  if (e != cudaSuccess) return e;
   return launch_pdl(attn_scan_kernel<D>, grid, dim3(256), smem, st, pdl, a);
 }
 

@@ -387,22 +387,14 @@ int deltanet_smem_bytes(int dk, int dv) {
 template <int DK, int DV, int K>
 cudaError_t deltanet_launch_one(const DeltaNetArgs& a, cudaLaunchConfig_t& cfg) {
   // the state's shared memory exceeds the default 48 KB at 128 x 128: opt in
-  // once per device (kept only once the attribute call succeeded)
+  // once per device
   static std::mutex mu;
   static bool done[64] = {};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  const cudaError_t e = once_per_device(done, mu, [] {
+    return cudaFuncSetAttribute(deltanet_kernel<DK, DV, K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                deltanet_smem_bytes(DK, DV));
+  });
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (!done[dev]) {
-      e = cudaFuncSetAttribute(deltanet_kernel<DK, DV, K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               deltanet_smem_bytes(DK, DV));
-      if (e != cudaSuccess) return e;
-      done[dev] = true;
-    }
-  }
   cfg.dynamicSmemBytes = deltanet_smem_bytes(DK, DV);
   return cudaLaunchKernelEx(&cfg, deltanet_kernel<DK, DV, K>, a);
 }

@@ -98,8 +98,11 @@ cudaError_t f32_matvec(const float* w, int rows, int cols, const float* x, int l
                        cudaStream_t st, bool pdl, const float* norm_w, float eps, uint8_t* q8k_out, int q8k_stride) {
   if (cols % 4 || cols > 4096 || k < 1 || k > 8 || (q8k_out && (!norm_w || cols % 256))) return cudaErrorInvalidValue;
   static bool configured[64] = {};
-  if (first_on_device(configured))
-    cudaFuncSetAttribute(f32_matvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 4096 * 4);
+  static std::mutex mu;
+  const cudaError_t e = once_per_device(configured, mu, [] {
+    return cudaFuncSetAttribute(f32_matvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 4096 * 4);
+  });
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.dynamicSmemBytes = (size_t)k * cols * sizeof(float);
   cfg.gridDim = dim3((unsigned)ceil_div(rows, 8));

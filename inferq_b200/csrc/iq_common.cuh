@@ -5,6 +5,7 @@
 // __fadd_rn so the compiler cannot contract it into an FMA.
 #pragma once
 #include <cstdint>
+#include <mutex>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 
@@ -15,8 +16,8 @@ enum Dtype : int { F32 = 0, F16 = 1, Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14, 
 
 constexpr int kWarp = 32;
 
-__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
-__host__ __device__ inline int64_t align_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
+__host__ __device__ constexpr inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+__host__ __device__ constexpr inline int64_t align_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
 
 // ------------------------------------------------------------ layouts
 // GGUF block sizes (bytes per block, weights per block).
@@ -46,12 +47,12 @@ __host__ __device__ inline int64_t dev_row_bytes(int dt, int64_t cols) {
 // as three planes; Q8_0 {qs[32] permuted, f32 d} as two planes.
 // Q8_K activation row: nb x 256 quants, nb f32 d (padded to 16 B), then
 // nb x 16 B of eight i16 sums of 32 quants.
-__host__ __device__ inline int64_t q8k_bs_offset(int64_t nb) { return nb * 256 + align_up(nb * 4, 16); }
-__host__ __device__ inline int64_t act_row_bytes_q8k(int64_t cols) {
+__host__ __device__ constexpr inline int64_t q8k_bs_offset(int64_t nb) { return nb * 256 + align_up(nb * 4, 16); }
+__host__ __device__ constexpr inline int64_t act_row_bytes_q8k(int64_t cols) {
   int64_t nb = cols / 256;
   return q8k_bs_offset(nb) + nb * 16;
 }
-__host__ __device__ inline int64_t act_row_bytes_q80(int64_t cols) {
+__host__ __device__ constexpr inline int64_t act_row_bytes_q80(int64_t cols) {
   int64_t nb = cols / 32;
   return align_up(nb * 32 + nb * 4, 16);
 }
@@ -63,15 +64,21 @@ __device__ __forceinline__ uint4 ld_stream(const void* p) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
   return v;
 }
-// True the first time it is called for the current device with this flag
-// set (one flag per device): for per-device one-time setup such as a
-// kernel's shared-memory opt-in attribute.
-inline bool first_on_device(bool (&done)[64]) {
+// Per-device one-time setup (a kernel's shared-memory opt-in attribute and
+// the like): runs `setup()` on the current device until it first succeeds
+// (one flag per device, guarded by one lock per flag set), and returns its
+// result, or cudaSuccess once it has succeeded.
+template <class F>
+inline cudaError_t once_per_device(bool (&done)[64], std::mutex& mu, F setup) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
-  if (done[dev]) return false;
-  done[dev] = true;
-  return true;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(mu);
+  if (done[dev]) return cudaSuccess;
+  e = setup();
+  if (e == cudaSuccess) done[dev] = true;
+  return e;
 }
 
 // exp and log1p of an f32 argument evaluated in double precision and rounded

@@ -14,10 +14,16 @@ namespace iq {
 namespace {
 
 // Largest problem the fixed scratch holds: 8 input rows of up to 4096
-// columns (Q8_K rows are 4672 bytes at 4096 columns, Q8_0 rows 4608).
+// columns (a quantized activation row is 4416 bytes in the Q8_K layout and
+// 4608 bytes in the Q8_0 layout at 4096 columns; the checks below tie the
+// size to the layout functions).
 constexpr int kNoAllocMaxRows = 8;
 constexpr int kNoAllocMaxCols = 4096;
 constexpr int kNoAllocActBytes = 8 * 4672;
+static_assert(kNoAllocMaxRows * act_row_bytes_q8k(kNoAllocMaxCols) <= kNoAllocActBytes,
+              "the scratch holds the largest Q8_K activation rows");
+static_assert(kNoAllocMaxRows * act_row_bytes_q80(kNoAllocMaxCols) <= kNoAllocActBytes,
+              "the scratch holds the largest Q8_0 activation rows");
 constexpr int kNoAllocJobOffset = kNoAllocActBytes;            // 256-aligned
 constexpr int kNoAllocBytes = kNoAllocJobOffset + 256;
 

@@ -10,6 +10,7 @@
 // unit `depth` ahead and computes.  Activations are staged into shared memory
 // once per change of input rows, not once per tile.
 #include <algorithm>
+#include <mutex>
 #include <cstdlib>
 #include <climits>
 #include <cstring>
@@ -624,9 +625,10 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
 
 int* qmv_timeout_flag() {
   static int* ptr[64] = {};
+  static std::mutex mu;
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
   if (!ptr[dev]) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_qmv_timeout) == cudaSuccess) ptr[dev] = static_cast<int*>(p);
@@ -636,9 +638,10 @@ int* qmv_timeout_flag() {
 
 int qmv_persistent_ctas() {
   static int n[64] = {};
+  static std::mutex mu;
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  std::lock_guard<std::mutex> lk(mu);
   if (!n[dev]) {
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -654,22 +657,29 @@ namespace {
 struct SmemLimits {
   int two = 0, one = 0;
 };
-const SmemLimits& qmv_dyn_smem_limits() {
+// Limits of the current device, set up (with the opt-in attribute) the first
+// time they are asked for there; zeros while the setup fails.
+SmemLimits qmv_dyn_smem_limits() {
   static SmemLimits lims[64];
+  static std::mutex mu;
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SmemLimits();
+  std::lock_guard<std::mutex> lk(mu);
   SmemLimits& lim = lims[dev];
   if (!lim.one) {
     int per_sm = 0, optin = 0;
-    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaFuncAttributes fa = {};
-    cudaFuncGetAttributes(&fa, qmv_kernel);
+    if (cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        cudaFuncGetAttributes(&fa, qmv_kernel) != cudaSuccess)
+      return SmemLimits();
     // each resident block also reserves 1 KB of shared memory for the system
-    lim.two = std::min(optin, per_sm / 2 - 1024) - (int)fa.sharedSizeBytes;
-    lim.one = optin - (int)fa.sharedSizeBytes;
-    cudaFuncSetAttribute(qmv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lim.one);
+    SmemLimits l;
+    l.two = std::min(optin, per_sm / 2 - 1024) - (int)fa.sharedSizeBytes;
+    l.one = optin - (int)fa.sharedSizeBytes;
+    if (cudaFuncSetAttribute(qmv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, l.one) != cudaSuccess)
+      return SmemLimits();
+    lim = l;
   }
   return lim;
 }
@@ -716,7 +726,8 @@ cudaError_t qmv_tensor_maps(int dt, const uint8_t* base, int64_t rows, int64_t c
 cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int ntiles, int smem_bytes,
                        cudaStream_t stream, bool pdl) {
   if (ntiles <= 0) return cudaSuccess;
-  const SmemLimits& lim = qmv_dyn_smem_limits();
+  const SmemLimits lim = qmv_dyn_smem_limits();
+  if (!lim.one) return cudaErrorInvalidValue;
   const int act = ((smem_bytes + 127) & ~127) + 128;  // + alignment slack of the ring
   const int ring_unit = kQmvWarps * kSlotBytes;
   int depth = std::min(kQmvMaxDepth, (lim.two - act) / ring_unit);

@@ -68,6 +68,11 @@ constexpr int kSide = 6, kSideBytes = 4096, kOffS = 2048;  // D at 0, S at 2048
 constexpr int kSmemBytes = kStages * kStageBytes + kSide * kSideBytes + 1024;
 constexpr int kTmemCols = 512;
 constexpr int kWaitLimit = 1 << 20;
+// Waits that only let work already in flight finish before the CTA winds
+// down (copies landing, MMAs completing) always use this longer bound, also
+// when a test shortens the other waits: no async operation may outlive the
+// CTA's shared memory or TMEM.
+constexpr int kDrainLimit = 1 << 24;
 static_assert(kStageBytes % 1024 == 0, "swizzled atoms stay 1024-byte aligned");
 
 // f32 D, f16 A and B, both K-major, N = 128, M = 128.
@@ -320,9 +325,9 @@ __global__ void __launch_bounds__(kBoundThreads, 1)
     }
     if (*abort_v) {  // let the copies in flight land before the CTA exits
       for (int it = issued > kStages ? issued - kStages : 0; it < issued; it++)
-        bar_wait(&full_op[it % kStages], (it / kStages) & 1, lim);
+        bar_wait(&full_op[it % kStages], (it / kStages) & 1, kDrainLimit);
       for (int it = issued > kSide ? issued - kSide : 0; it < issued; it++)
-        bar_wait(&full_side[it % kSide], (it / kSide) & 1, lim);
+        bar_wait(&full_side[it % kSide], (it / kSide) & 1, kDrainLimit);
     }
   } else if (warp == kMmaWarp && lane == 0) {
     // ------------------------------------------------------- MMA issuer
@@ -354,7 +359,7 @@ __global__ void __launch_bounds__(kBoundThreads, 1)
       mma_commit(&empty_op[s]);
     }
     mma_commit(&drained);  // every MMA issued above has completed when this fires
-    bar_wait(&drained, 0, lim);
+    bar_wait(&drained, 0, kDrainLimit);
   }
   __syncwarp();
   tc_before();
@@ -586,9 +591,9 @@ __global__ void __launch_bounds__(kBoundThreads, 1)
     }
     if (*abort_v) {
       for (int it = issued > kQ4Stages ? issued - kQ4Stages : 0; it < issued; it++)
-        bar_wait(&full_op[it % kQ4Stages], (it / kQ4Stages) & 1, lim);
+        bar_wait(&full_op[it % kQ4Stages], (it / kQ4Stages) & 1, kDrainLimit);
       for (int it = issued > kQ4Side ? issued - kQ4Side : 0; it < issued; it++)
-        bar_wait(&full_side[it % kQ4Side], (it / kQ4Side) & 1, lim);
+        bar_wait(&full_side[it % kQ4Side], (it / kQ4Side) & 1, kDrainLimit);
     }
   } else if (warp == kMmaWarp && lane == 0) {
     // ------------------------------------------------------- MMA issuer
@@ -618,7 +623,7 @@ __global__ void __launch_bounds__(kBoundThreads, 1)
       mma_commit(&empty_op[s]);
     }
     mma_commit(&drained);
-    bar_wait(&drained, 0, lim);
+    bar_wait(&drained, 0, kDrainLimit);
   }
   __syncwarp();
   tc_before();
@@ -890,9 +895,9 @@ __global__ void __launch_bounds__(kBoundThreads, 1)
     }
     if (*abort_v) {
       for (int it = issued > kQ6Stages ? issued - kQ6Stages : 0; it < issued; it++)
-        bar_wait(&full_op[it % kQ6Stages], (it / kQ6Stages) & 1, lim);
+        bar_wait(&full_op[it % kQ6Stages], (it / kQ6Stages) & 1, kDrainLimit);
       for (int b = sides > kQ6Side ? sides - kQ6Side : 0; b < sides; b++)
-        bar_wait(&full_side[b % kQ6Side], (b / kQ6Side) & 1, lim);
+        bar_wait(&full_side[b % kQ6Side], (b / kQ6Side) & 1, kDrainLimit);
     }
   } else if (warp == kMmaWarp && lane == 0) {
     // ------------------------------------------------------- MMA issuer
@@ -920,7 +925,7 @@ __global__ void __launch_bounds__(kBoundThreads, 1)
       if (quarter == 3) mma_commit(&tfull[buf]);
     }
     mma_commit(&drained);
-    bar_wait(&drained, 0, lim);
+    bar_wait(&drained, 0, kDrainLimit);
   }
   __syncwarp();
   tc_before();
@@ -1024,10 +1029,11 @@ cudaError_t wide_q80_forward(const uint8_t* w, int64_t rows, int64_t cols, int64
                 CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
   static bool attr[64] = {};  // the shared-memory opt-in is per device
-  if (first_on_device(attr)) {
-    e = cudaFuncSetAttribute(wide_q80_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-  }
+  static std::mutex mu;
+  e = once_per_device(attr, mu, [] {
+    return cudaFuncSetAttribute(wide_q80_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  });
+  if (e != cudaSuccess) return e;
   int* flag = wide_timeout_flag();
   if (!flag) return cudaErrorInvalidDevice;
   static const int test_skip = getenv("IQ_WIDE_TEST_TIMEOUT") ? 1 : 0;
@@ -1064,11 +1070,12 @@ cudaError_t wide_q4k_forward(const uint8_t* w, int64_t rows, int64_t cols, int64
       !encode2d(&mh, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)w_row_bytes, (uint64_t)rows, (uint64_t)w_row_bytes,
                 16, 128, CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
-  static bool attr[64] = {};
-  if (first_on_device(attr)) {
-    e = cudaFuncSetAttribute(wide_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kQ4SmemBytes);
-    if (e != cudaSuccess) return e;
-  }
+  static bool attr[64] = {};  // the shared-memory opt-in is per device
+  static std::mutex mu;
+  e = once_per_device(attr, mu, [] {
+    return cudaFuncSetAttribute(wide_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kQ4SmemBytes);
+  });
+  if (e != cudaSuccess) return e;
   int* flag = wide_timeout_flag();
   if (!flag) return cudaErrorInvalidDevice;
   static const int test_skip = getenv("IQ_WIDE_TEST_TIMEOUT") ? 1 : 0;
@@ -1148,11 +1155,12 @@ cudaError_t wide_q6k_forward(const uint8_t* w, int64_t rows, int64_t cols, int64
       !encode2d(&mt, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)w_row_bytes, (uint64_t)rows, (uint64_t)w_row_bytes,
                 16, 128, CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
-  static bool attr[64] = {};
-  if (first_on_device(attr)) {
-    e = cudaFuncSetAttribute(wide_q6k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kQ6SmemBytes);
-    if (e != cudaSuccess) return e;
-  }
+  static bool attr[64] = {};  // the shared-memory opt-in is per device
+  static std::mutex mu;
+  e = once_per_device(attr, mu, [] {
+    return cudaFuncSetAttribute(wide_q6k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kQ6SmemBytes);
+  });
+  if (e != cudaSuccess) return e;
   int* flag = wide_timeout_flag();
   if (!flag) return cudaErrorInvalidDevice;
   static const int test_skip = getenv("IQ_WIDE_TEST_TIMEOUT") ? 1 : 0;
