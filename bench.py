@@ -22,9 +22,10 @@ config     verify_us: one verification pass at k = 1, 2, 4, 8 (context 1024,
            tensor-core product at a 35B projection shape
 roofline   the quantized GEMV (the dominant kernel): its weight bytes over its
            event-timed launches, against the measured HBM copy bandwidth
-cpu_baseline  the CPU restatement of the reference (oracle/; the Rust
-           reference cannot be built here) on the host cores, on a bounded
-           sample of the same step
+cpu_baseline  the same MTP rounds through the CPU restatement of the
+           reference (oracle/; the Rust reference cannot be built here) on
+           the host cores: full model, reference-order AVX2 dots, snapshots
+           and rollback, from a seeded state at context 3072
 
 Run: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 Under torchrun the N ranks run one sequence with the experts split over them
@@ -322,59 +323,73 @@ def ngram_tiny(steps, warmup):
             "us_per_step": dev / steps * 1e6}
 
 
-def cpu_baseline_sample(cfg_full, budget_s: float = 20.0):
-    """Time the oracle on a bounded sample: one row through 4 of the 40
-    layers (3 DeltaNet + 1 attention, full widths) and the full LM head,
-    scaled to a k=4 verify pass of the 40-layer model."""
+def cpu_mtp_rounds(cfg, steps: int, warmup: int):
+    """The same MTP round on the host cores through the CPU restatement of
+    the reference (oracle/: the reference-order quantized dots with AVX2 and
+    multi-row weight reuse, OpenMP over weight rows; verification snapshots
+    and rollback as QuantizedStateSnapshots), full 40-layer model, from a
+    seeded state image at context 3072.  Returns per-round times."""
     import torch
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle
-    from inferq_b200 import synth
-    c = synth.qwen36_35b()
-    c.num_hidden_layers = 4
-    c.mtp_num_hidden_layers = 0
-    tensors = [synth.Tensor(t.name, t.dtype, t.shape, t.data.cpu()) for t in
-               synth.generate(c, seed=0, device="cuda" if torch.cuda.is_available() else "cpu")]
-    om = oracle.OracleModel(c, tensors)
-    st = om.state(64)
-    st.forward([1])  # warm-up (first touches of the weights)
-    t0 = time.time()
-    rows = 0
-    while True:
-        st.forward([2 + rows], logits=True)
-        rows += 1
-        if time.time() - t0 > budget_s / 4 or rows >= 4:
-            break
-    per_row_4l = (time.time() - t0) / rows
-    t1 = time.time()
-    h = np.random.default_rng(0).standard_normal(c.hidden_size).astype(np.float32)
-    lm = [t for t in tensors if t.name == "output.weight"][0]
-    oracle.qmatvec(lm.dtype, lm.data.numpy(), c.vocab_size, c.hidden_size, h)
-    t_head = time.time() - t1
-    t_layers4 = max(per_row_4l - t_head, 0.0)
-    per_row_full = t_head + t_layers4 * (cfg_full.num_hidden_layers / 4)
-    return {"per_row_s": per_row_full, "pass_s": per_row_full * K_ROWS, "cores": os.cpu_count(),
-            "sample": f"{rows} row(s) through 4 of 40 layers (full widths) + full LM head, "
-                      f"scaled x10 per layer and x{K_ROWS} rows to one k={K_ROWS} pass"}
+    from inferq_b200 import image, synth
+    dev = "cuda" if torch.cuda.is_available() else "cpu"  # device only generates the seeded weights
+    tensors = [synth.Tensor(t.name, t.dtype, t.shape, t.data.cpu()) for t in synth.generate(cfg, seed=0, device=dev)]
+    om = oracle.OracleModel(cfg, tensors)
+    n = (steps + warmup) * K_ROWS + 16
+    st = om.state(CTX_MTP + n)
+    st.enable_snapshots(K_ROWS)
+    st.import_image(image.synthetic(cfg, CTX_MTP, seed=5))
+    rng = np.random.default_rng(6)
+    seed = int(rng.integers(cfg.vocab_size))
+    hidden = rng.standard_normal(cfg.hidden_size).astype(np.float32)
+    pos = CTX_MTP
+    vocab = min(DRAFT_VOCAB, cfg.vocab_size)
+    times, committed = [], []
+    for i in range(steps + warmup):
+        t0 = time.perf_counter()
+        st.set_mtp_position(pos)
+        drafts, h, tok = [], hidden, seed
+        for _ in range(MTP_DEPTH):  # draft_mtp against the vocabulary-prefix head
+            lg, h = st.mtp(tok, h, vocab)
+            tok = oracle.argmax(lg)
+            drafts.append(tok)
+        lg, hd, _ = st.forward([seed] + drafts, hidden=True)
+        acc = oracle.accepted_prefix(drafts, lg)
+        auth = oracle.argmax(lg[acc])
+        st.rollback(acc + 1)
+        st.set_mtp_position(pos)  # catch-up over the committed rows
+        st.mtp(seed, hidden, 0)
+        for j in range(acc):
+            st.mtp(drafts[j], hd[j], 0)
+        pos += acc + 1
+        seed, hidden = auth, np.ascontiguousarray(hd[acc])
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+            committed.append(acc + 1)
+    return {"round_s": times, "committed": committed, "cores": os.cpu_count(),
+            "sample": f"{len(times)} full MTP rounds (draft {MTP_DEPTH} on the {vocab}-row prefix head, k={K_ROWS} "
+                      f"verify of all {cfg.num_hidden_layers} layers, rollback, catch-up) from a seeded state at "
+                      f"context {CTX_MTP}, OpenMP on {os.cpu_count()} cores"}
 
 
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
+    os.environ["OMP_NUM_THREADS"] = str(os.cpu_count())  # before the oracle's OpenMP runtime starts
     from inferq_b200 import synth
     cfg = synth.qwen36_35b()
-    results = [cpu_baseline_sample(cfg, budget_s=10.0) for _ in range(max(1, min(args.steps, 3)))]
-    pass_s = float(np.median([r["pass_s"] for r in results]))
-    committed_per_step = 1.0
-    v = committed_per_step / pass_s
+    r = cpu_mtp_rounds(cfg, args.steps, args.warmup)
+    total = float(sum(r["round_s"]))
+    v = sum(r["committed"]) / total
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world,
-            "steps": len(results), "warmup": 1, "ms_per_step": pass_s * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8xq4/q6 dot, f32 accumulate",
-            "data": "synthetic (seeded random-init weights)",
-            "config": {"workload": WORKLOAD, "verify_us_k4": pass_s * 1e6},
-            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": results[0]["cores"], "kind": "port",
-                             "sample": results[0]["sample"]},
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8xq4/q6 dot, f32 accumulate", "data": "synthetic (seeded random-init Q4_K_M weights)",
+            "config": {"workload": WORKLOAD, "context": CTX_MTP,
+                       "committed_per_step": sum(r["committed"]) / args.steps},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": r["cores"], "kind": "port", "sample": r["sample"]},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -475,10 +490,9 @@ def main():
     cpu = None
     if not args.no_cpu_baseline and world == 1:
         try:
-            cb = cpu_baseline_sample(cfg)
-            cpu = {"value": 1.0 / cb["pass_s"], "unit": "tok/s", "cores": cb["cores"], "kind": "port",
-                   "sample": cb["sample"] + "; one committed token per step (the CPU arm's MTP acceptance "
-                   "is not modelled)"}
+            cb = cpu_mtp_rounds(cfg, 3, 1)
+            cpu = {"value": sum(cb["committed"]) / sum(cb["round_s"]), "unit": "tok/s", "cores": cb["cores"],
+                   "kind": "port", "sample": cb["sample"]}
         except Exception as e:  # the baseline is reported, never required
             cpu = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
                    "sample": f"failed: {e}"}

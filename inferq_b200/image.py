@@ -100,3 +100,28 @@ def build(cfg: Config, parts: dict) -> np.ndarray:
     out = np.concatenate(chunks)
     assert out.size == image_bytes(cfg, pos, mpos)
     return out
+
+
+def synthetic(cfg: Config, position: int, seed: int = 0) -> np.ndarray:
+    """A seeded state image at `position` (KV rows and conv history N(0, 1),
+    recurrent state N(0, 0.05^2); all zeros at position 0, the true fresh
+    state): a long-context starting point that costs no prefill."""
+    rng = np.random.default_rng(seed)
+    sh = shapes(cfg)
+    layers = []
+    for l in range(cfg.num_hidden_layers):
+        if cfg.layer_is_full(l):
+            layers.append({"keys": rng.standard_normal((position, sh["kv_dim"]), np.float32),
+                           "values": rng.standard_normal((position, sh["kv_dim"]), np.float32)})
+        else:
+            conv = np.zeros((sh["conv_dim"], sh["conv_taps"]), np.float32)
+            rec = np.zeros(sh["rec_size"], np.float32)
+            if position:
+                conv = rng.standard_normal(conv.shape, np.float32)
+                rec = (0.05 * rng.standard_normal(rec.shape)).astype(np.float32)
+            layers.append({"conv": conv, "recurrent": rec})
+    parts = {"position": position, "mtp_position": position if cfg.mtp_num_hidden_layers else 0, "layers": layers}
+    if cfg.mtp_num_hidden_layers:
+        parts["mtp"] = {"keys": rng.standard_normal((position, sh["kv_dim"]), np.float32),
+                        "values": rng.standard_normal((position, sh["kv_dim"]), np.float32)}
+    return build(cfg, parts)

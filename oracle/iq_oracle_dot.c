@@ -189,6 +189,14 @@ static void block_terms(int dtype, const uint8_t* blk, const uint8_t* xq, int b,
     }
 }
 
+/* The AVX2 forms (iq_oracle_avx2.c) and a switch to the scalar ones. */
+int or_have_avx2(void);
+void or_q4k_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, int T, float* out);
+void or_q6k_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, int T, float* out);
+void or_q80_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, int T, float* out);
+static int g_force_scalar = 0;
+void or_force_scalar(int on) { g_force_scalar = on; }
+
 static int block_bytes(int dtype) {
     return dtype == OR_Q4_K ? 144 : dtype == OR_Q5_K ? 176 : dtype == OR_Q6_K ? 210 : 34;
 }
@@ -218,8 +226,9 @@ int or_qmatvec(int dtype, const void* wv, int64_t rows, int64_t cols,
     const uint8_t* w = (const uint8_t*)wv;
     if (dtype == OR_F32) { /* plain serial f32 dot (candle's f32 matmul order is unpinned) */
         const float* wf = (const float*)wv;
-        for (int i = 0; i < k; i++)
-            for (int64_t r = 0; r < rows; r++) {
+        #pragma omp parallel for schedule(static)
+        for (int64_t r = 0; r < rows; r++)
+            for (int i = 0; i < k; i++) {
                 float s = 0.f;
                 for (int64_t c = 0; c < cols; c++) s += wf[r * cols + c] * x[i * cols + c];
                 y[i * rows + r] = s;
@@ -239,6 +248,28 @@ int or_qmatvec(int dtype, const void* wv, int64_t rows, int64_t cols,
     }
     int64_t rb = or_row_bytes(dtype, cols);
     if (ksplit < 1) ksplit = 1;
+    /* the AVX2 forms of the reference order: a weight row decoded once for
+     * up to eight input rows (bitwise the scalar forms below) */
+    static int avx2 = -1;
+    if (avx2 < 0) avx2 = or_have_avx2();
+    if (order == 0 && avx2 && !g_force_scalar && (dtype == OR_Q4_K || dtype == OR_Q6_K || dtype == OR_Q8_0)) {
+        #pragma omp parallel for schedule(static)
+        for (int64_t r = 0; r < rows; r++) {
+            const uint8_t* wr = w + r * rb;
+            for (int i0 = 0; i0 < k; i0 += 8) {
+                const uint8_t* xs[8];
+                float o[8];
+                int T = k - i0 < 8 ? k - i0 : 8;
+                for (int t = 0; t < T; t++) xs[t] = xq + (i0 + t) * xbytes;
+                if (dtype == OR_Q4_K) or_q4k_rows_avx2(wr, nb, xs, T, o);
+                else if (dtype == OR_Q6_K) or_q6k_rows_avx2(wr, nb, xs, T, o);
+                else or_q80_rows_avx2(wr, nb, xs, T, o);
+                for (int t = 0; t < T; t++) y[(i0 + t) * rows + r] = o[t];
+            }
+        }
+        free(xq);
+        return 0;
+    }
     #pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < rows; r++) {
         const uint8_t* wr = w + r * rb;

@@ -78,6 +78,8 @@ typedef struct {
     float* rec;   /* [nv][dk][dv] */
     float* keys;  /* [max_pos][nkv][hd] */
     float* values;
+    float** snap_conv;  /* snapshots after each row of a pass (or NULL) */
+    float** snap_rec;
 } lstate_t;
 
 typedef struct or_state {
@@ -86,6 +88,12 @@ typedef struct or_state {
     lstate_t* l;
     lstate_t mtp;
     int64_t mtp_position;
+    /* verification snapshots (QuantizedStateSnapshots, quantized_model.rs:99-204):
+     * with snap_rows > 0, a pass stores each DeltaNet layer's conv and
+     * recurrent state after its rows 0..snap_rows-2, so a rollback is a copy */
+    int snap_rows;
+    int64_t snap_pos0;  /* position of the last pass's row 0 */
+    int snap_taken;     /* rows of the last pass */
 } or_state;
 
 /* --------------------------------------------------------------- helpers */
@@ -130,6 +138,13 @@ static void matvec_n(const mat_t* m, const uint8_t* p, int64_t n, const float* x
     or_qmatvec(m->dt, p, n, m->cols, x, 1, y, g_order, g_order ? device_ksplit(m->dt, n, m->cols, expert) : 1);
 }
 static void matvec(const mat_t* m, const float* x, float* y) { matvec_n(m, m->p, m->rows, x, y, 0); }
+/* R input rows x [R][cols] -> y [R][n] (each weight row read once for all R,
+ * the reference's multi-row pass; every output is computed exactly as for a
+ * single row) */
+static void matvec_nk(const mat_t* m, const uint8_t* p, int64_t n, const float* x, int R, float* y, int expert) {
+    or_qmatvec(m->dt, p, n, m->cols, x, R, y, g_order, g_order ? device_ksplit(m->dt, n, m->cols, expert) : 1);
+}
+static void matvec_k(const mat_t* m, const float* x, int R, float* y) { matvec_nk(m, m->p, m->rows, x, R, y, 0); }
 /* an expert-class matrix (routed or shared expert) */
 static void matvec_e(const mat_t* m, const float* x, float* y) { matvec_n(m, m->p, m->rows, x, y, 1); }
 /* rows [r0, r0+n) of a stacked expert matrix */
@@ -279,8 +294,58 @@ or_state* or_state_create(const or_model* m, int64_t max_pos) {
     return s;
 }
 
+/* Keep snapshots for passes of up to `rows` rows (0 turns them off). */
+int or_state_enable_snapshots(const or_model* m, or_state* s, int rows) {
+    const or_config* c = &m->c;
+    int64_t conv_n = (2 * (int64_t)c->linear_num_key_heads * c->linear_key_head_dim +
+                      (int64_t)c->linear_num_value_heads * c->linear_value_head_dim) * (c->linear_conv_kernel_dim - 1);
+    int64_t rec_n = (int64_t)c->linear_num_value_heads * c->linear_key_head_dim * c->linear_value_head_dim;
+    if (rows > 8 || rows < 0 || s->snap_rows) return -1;
+    s->snap_rows = rows;
+    for (int i = 0; i < s->nlayers; i++) {
+        if (m->layers[i].full || rows < 2) continue;
+        lstate_t* L = &s->l[i];
+        L->snap_conv = (float**)calloc((size_t)rows, sizeof(float*));
+        L->snap_rec = (float**)calloc((size_t)rows, sizeof(float*));
+        for (int r = 0; r + 1 < rows; r++) {
+            L->snap_conv[r] = (float*)malloc((size_t)(conv_n + 1) * 4);
+            L->snap_rec[r] = (float*)malloc((size_t)rec_n * 4);
+        }
+    }
+    return 0;
+}
+
+/* Keep the first `committed` rows of the last pass (rollback,
+ * quantized_model.rs:177-204): DeltaNet state from the snapshot after row
+ * committed-1, KV cache truncated by the position. */
+int or_state_rollback(const or_model* m, or_state* s, int committed) {
+    const or_config* c = &m->c;
+    if (committed < 1 || committed > s->snap_taken) return -1;
+    if (committed == s->snap_taken) return 0;
+    if (!s->snap_rows) return -2;
+    int64_t conv_n = (2 * (int64_t)c->linear_num_key_heads * c->linear_key_head_dim +
+                      (int64_t)c->linear_num_value_heads * c->linear_value_head_dim) * (c->linear_conv_kernel_dim - 1);
+    int64_t rec_n = (int64_t)c->linear_num_value_heads * c->linear_key_head_dim * c->linear_value_head_dim;
+    for (int i = 0; i < s->nlayers; i++) {
+        if (m->layers[i].full) continue;
+        lstate_t* L = &s->l[i];
+        memcpy(L->conv, L->snap_conv[committed - 1], (size_t)conv_n * 4);
+        memcpy(L->rec, L->snap_rec[committed - 1], (size_t)rec_n * 4);
+    }
+    s->position = s->snap_pos0 + committed;
+    s->snap_taken = committed;
+    return 0;
+}
+
 void or_state_destroy(or_state* s) {
     if (!s) return;
+    for (int i = 0; i < s->nlayers; i++) {
+        lstate_t* L = &s->l[i];
+        if (L->snap_conv) {
+            for (int r = 0; r + 1 < s->snap_rows; r++) { free(L->snap_conv[r]); free(L->snap_rec[r]); }
+            free(L->snap_conv); free(L->snap_rec);
+        }
+    }
     for (int i = 0; i < s->nlayers; i++) lstate_free(&s->l[i]);
     lstate_free(&s->mtp);
     free(s->l);
@@ -374,57 +439,74 @@ void or_delta_step(const float* q, const float* k, const float* v, const float* 
                         state + (int64_t)h * dk * dv, out + h * dv);
 }
 
-static void delta_row(const or_model* m, const layer_t* L, lstate_t* st, const float* x, float* out) {
+/* The DeltaNet mixer over R rows x [R][H] -> out [R][H]
+ * (quantized_deltanet.rs:517-703): projections of all rows, then per row in
+ * order the conv step, L2 norms, beta/decay and the delta rule, then the
+ * gated norm and the output projection of all rows. */
+static void delta_rows(const or_model* m, const layer_t* L, lstate_t* st, const float* x, int R, float* out) {
     const or_config* c = &m->c;
     const int nk = c->linear_num_key_heads, nv = c->linear_num_value_heads;
     const int dk = c->linear_key_head_dim, dv = c->linear_value_head_dim, K = c->linear_conv_kernel_dim;
     const int kd = nk * dk, vd = nv * dv, conv_dim = 2 * kd + vd, ratio = nv / nk;
-    float* proj = (float*)malloc((size_t)conv_dim * 4);
-    float* z = (float*)malloc((size_t)vd * 4);
-    float* ba = (float*)malloc((size_t)2 * nv * 4);
+    float* proj = (float*)malloc((size_t)R * conv_dim * 4);
+    float* z = (float*)malloc((size_t)R * vd * 4);
+    float* ba = (float*)malloc((size_t)R * 2 * nv * 4);
+    float* tmp = (float*)malloc((size_t)R * nv * 4);
     float* cv = (float*)malloc((size_t)conv_dim * 4);
     float* qr = (float*)malloc((size_t)nv * dk * 4);
     float* kr = (float*)malloc((size_t)nv * dk * 4);
     float* o = (float*)malloc((size_t)vd * 4);
-    float* g = (float*)malloc((size_t)vd * 4);
-    matvec(&L->qkv, x, proj);
-    matvec(&L->z, x, z);
-    if (L->ba_fused) matvec(&L->ba, x, ba);
-    else { matvec(&L->beta, x, ba); matvec(&L->alpha, x, ba + nv); }
-    or_conv_step(proj, L->conv_w, conv_dim, K, st->conv, cv);
-    float* q = cv; float* k = cv + kd; const float* v = cv + 2 * kd;
-    for (int kh = 0; kh < nk; kh++) {
-        or_l2_normalize(q + kh * dk, dk);
-        or_l2_normalize(k + kh * dk, dk);
+    float* g = (float*)malloc((size_t)R * vd * 4);
+    matvec_k(&L->qkv, x, R, proj);
+    matvec_k(&L->z, x, R, z);
+    if (L->ba_fused) matvec_k(&L->ba, x, R, ba);
+    else {
+        matvec_k(&L->beta, x, R, tmp);
+        for (int r = 0; r < R; r++) memcpy(ba + (int64_t)r * 2 * nv, tmp + (int64_t)r * nv, (size_t)nv * 4);
+        matvec_k(&L->alpha, x, R, tmp);
+        for (int r = 0; r < R; r++) memcpy(ba + (int64_t)r * 2 * nv + nv, tmp + (int64_t)r * nv, (size_t)nv * 4);
     }
-    float q_scale = 1.f / sqrtf((float)dk);
-    for (int kh = 0; kh < nk; kh++)
-        for (int rep = 0; rep < ratio; rep++) {
-            int vh = or_value_head(kh, rep, nk, ratio, c->value_heads_tiled);
-            memcpy(qr + vh * dk, q + kh * dk, (size_t)dk * 4);
-            memcpy(kr + vh * dk, k + kh * dk, (size_t)dk * 4);
-            float b, al;
-            if (L->ba_fused) { int base = kh * 2 * ratio; b = ba[base + rep]; al = ba[base + ratio + rep]; }
-            else { b = ba[vh]; al = ba[nv + vh]; }
-            float beta = sigmoid_ref(b);
-            float gdec = L->ssm_a[vh] * softplus_ref(al + L->dt_bias[vh]);
-            delta_head_step(qr + vh * dk, kr + vh * dk, v + vh * dv, gdec, beta, dk, dv, q_scale,
-                            st->rec + (int64_t)vh * dk * dv, o + vh * dv);
+    for (int r = 0; r < R; r++) {
+        const float* bar = ba + (int64_t)r * 2 * nv;
+        or_conv_step(proj + (int64_t)r * conv_dim, L->conv_w, conv_dim, K, st->conv, cv);
+        float* q = cv; float* k = cv + kd; const float* v = cv + 2 * kd;
+        for (int kh = 0; kh < nk; kh++) {
+            or_l2_normalize(q + kh * dk, dk);
+            or_l2_normalize(k + kh * dk, dk);
         }
-    /* rms_norm_gated (norm.rs:16-25) per value head */
-    for (int vh = 0; vh < nv; vh++) {
-        const float* oh = o + vh * dv;
-        float ss = 0.f;
-        for (int j = 0; j < dv; j++) ss += oh[j] * oh[j];
-        float den = sqrtf(ss * (float)(1.0 / dv) + c->rms_norm_eps);
-        for (int j = 0; j < dv; j++) {
-            float zz = z[vh * dv + j];
-            float silu = zz / (1.f + expf(-zz));
-            g[vh * dv + j] = ((oh[j] / den) * L->ssm_norm[j]) * silu;
+        float q_scale = 1.f / sqrtf((float)dk);
+        for (int kh = 0; kh < nk; kh++)
+            for (int rep = 0; rep < ratio; rep++) {
+                int vh = or_value_head(kh, rep, nk, ratio, c->value_heads_tiled);
+                memcpy(qr + vh * dk, q + kh * dk, (size_t)dk * 4);
+                memcpy(kr + vh * dk, k + kh * dk, (size_t)dk * 4);
+                float b, al;
+                if (L->ba_fused) { int base = kh * 2 * ratio; b = bar[base + rep]; al = bar[base + ratio + rep]; }
+                else { b = bar[vh]; al = bar[nv + vh]; }
+                float beta = sigmoid_ref(b);
+                float gdec = L->ssm_a[vh] * softplus_ref(al + L->dt_bias[vh]);
+                delta_head_step(qr + vh * dk, kr + vh * dk, v + vh * dv, gdec, beta, dk, dv, q_scale,
+                                st->rec + (int64_t)vh * dk * dv, o + vh * dv);
+            }
+        if (st->snap_conv && r + 1 < R) {  /* entry state of the next row */
+            memcpy(st->snap_conv[r], st->conv, (size_t)conv_dim * (K - 1) * 4);
+            memcpy(st->snap_rec[r], st->rec, (size_t)nv * dk * dv * 4);
+        }
+        /* rms_norm_gated (norm.rs:16-25) per value head */
+        for (int vh = 0; vh < nv; vh++) {
+            const float* oh = o + vh * dv;
+            float ss = 0.f;
+            for (int j = 0; j < dv; j++) ss += oh[j] * oh[j];
+            float den = sqrtf(ss * (float)(1.0 / dv) + c->rms_norm_eps);
+            for (int j = 0; j < dv; j++) {
+                float zz = z[(int64_t)r * vd + vh * dv + j];
+                float silu = zz / (1.f + expf(-zz));
+                g[(int64_t)r * vd + vh * dv + j] = ((oh[j] / den) * L->ssm_norm[j]) * silu;
+            }
         }
     }
-    matvec(&L->out, g, out);
-    free(proj); free(z); free(ba); free(cv); free(qr); free(kr); free(o); free(g);
+    matvec_k(&L->out, g, R, out);
+    free(proj); free(z); free(ba); free(tmp); free(cv); free(qr); free(kr); free(o); free(g);
 }
 
 /* ----------------------------------------------------------- attention */
@@ -506,32 +588,39 @@ void or_attend(const float* q, const float* gate, const float* keys, const float
     free(qg); free(scores);
 }
 
-static void attn_row(const or_model* m, const layer_t* L, lstate_t* st, int64_t pos, const float* x, float* out) {
+/* Gated attention over R rows at positions pos .. pos+R-1
+ * (quantized_attention.rs:409-507): projections of all rows, then per row in
+ * order its K/V appended and its causal scan, then the output projection. */
+static void attn_rows(const or_model* m, const layer_t* L, lstate_t* st, int64_t pos, const float* x, int R,
+                      float* out) {
     const or_config* c = &m->c;
     const int nh = c->num_attention_heads, nkv = c->num_key_value_heads, hd = c->head_dim;
-    const int G = nh / nkv;
-    float* qg = (float*)malloc((size_t)nh * 2 * hd * 4);
-    float* kv = (float*)malloc((size_t)nkv * hd * 4);
-    float* vv = (float*)malloc((size_t)nkv * hd * 4);
-    float* res = (float*)malloc((size_t)nh * hd * 4);
-    float* scores = (float*)malloc((size_t)(pos + 1) * 4);
-    matvec(&L->q, x, qg);
-    matvec(&L->k, x, kv);
-    matvec(&L->v, x, vv);
-    for (int h = 0; h < nkv; h++) {
-        converted_norm(kv + h * hd, L->k_norm, hd, c->rms_norm_eps);
-        apply_rope(kv + h * hd, pos, c->rotary_dim, c->rope_theta);
+    float* qg = (float*)malloc((size_t)R * nh * 2 * hd * 4);
+    float* kv = (float*)malloc((size_t)R * nkv * hd * 4);
+    float* vv = (float*)malloc((size_t)R * nkv * hd * 4);
+    float* res = (float*)malloc((size_t)R * nh * hd * 4);
+    float* scores = (float*)malloc((size_t)(pos + R) * 4);
+    matvec_k(&L->q, x, R, qg);
+    matvec_k(&L->k, x, R, kv);
+    matvec_k(&L->v, x, R, vv);
+    for (int r = 0; r < R; r++) {
+        const int64_t p = pos + r;
+        float* kr = kv + (int64_t)r * nkv * hd;
+        for (int h = 0; h < nkv; h++) {
+            converted_norm(kr + h * hd, L->k_norm, hd, c->rms_norm_eps);
+            apply_rope(kr + h * hd, p, c->rotary_dim, c->rope_theta);
+        }
+        memcpy(st->keys + p * nkv * hd, kr, (size_t)nkv * hd * 4);
+        memcpy(st->values + p * nkv * hd, vv + (int64_t)r * nkv * hd, (size_t)nkv * hd * 4);
+        float* qr = qg + (int64_t)r * nh * 2 * hd;
+        for (int h = 0; h < nh; h++) {
+            float* q = qr + h * 2 * hd;
+            converted_norm(q, L->q_norm, hd, c->rms_norm_eps);
+            apply_rope(q, p, c->rotary_dim, c->rope_theta);
+        }
+        attend_row(qr, 2 * hd, hd, st->keys, st->values, nh, nkv, hd, p + 1, scores, res + (int64_t)r * nh * hd);
     }
-    memcpy(st->keys + pos * nkv * hd, kv, (size_t)nkv * hd * 4);
-    memcpy(st->values + pos * nkv * hd, vv, (size_t)nkv * hd * 4);
-    for (int h = 0; h < nh; h++) {
-        float* q = qg + h * 2 * hd;
-        converted_norm(q, L->q_norm, hd, c->rms_norm_eps);
-        apply_rope(q, pos, c->rotary_dim, c->rope_theta);
-    }
-    attend_row(qg, 2 * hd, hd, st->keys, st->values, nh, nkv, hd, pos + 1, scores, res);
-    (void)G;
-    matvec(&L->o, res, out);
+    matvec_k(&L->o, res, R, out);
     free(qg); free(kv); free(vv); free(res); free(scores);
 }
 
@@ -560,54 +649,92 @@ void or_route(const float* lg, int E, int topk, int norm_topk, int* rank, float*
     if (norm_topk) for (int r = 0; r < topk; r++) w[r] /= sum;
     free(pr);
 }
-static void moe_row(const or_model* m, const layer_t* L, const float* x, float* out, int* experts_out) {
+/* The sparse MoE block over R rows (quantized_moe.rs:237-460): router of
+ * all rows, routes per row, then each distinct expert in ascending order
+ * over the rows routed to it (routed_grouped_by_expert), the shared expert
+ * over all rows; per row out = sum over its routes in route order of y * w,
+ * then + shared * sigmoid(x . selector).  experts_out [R][topk] or NULL. */
+static void moe_rows(const or_model* m, const layer_t* L, const float* x, int R, float* out, int* experts_out) {
     const or_config* c = &m->c;
     const int E = c->num_experts, H = c->hidden_size, F = c->moe_intermediate_size;
     const int Fs = c->shared_expert_intermediate_size, topk = c->num_experts_per_tok;
-    float* lg = (float*)malloc((size_t)E * 4);
-    float* pr = (float*)malloc((size_t)E * 4);
+    const int FF = F > Fs ? F : Fs;
+    float* lg = (float*)malloc((size_t)R * E * 4);
     int* rank = (int*)malloc((size_t)E * sizeof(int));
-    float* g = (float*)malloc((size_t)(F > Fs ? F : Fs) * 4);
-    float* u = (float*)malloc((size_t)(F > Fs ? F : Fs) * 4);
-    float* y = (float*)malloc((size_t)H * 4);
-    matvec(&L->router, x, lg);
-    float w[16];
-    or_route(lg, E, topk, c->norm_topk_prob, rank, w);
-    (void)pr;
-    for (int i = 0; i < H; i++) out[i] = 0.f;
-    for (int r = 0; r < topk; r++) {
-        int e = rank[r];
-        if (experts_out) experts_out[r] = e;
-        matvec_rows(&L->gate, (int64_t)e * F, F, x, g);
-        matvec_rows(&L->up, (int64_t)e * F, F, x, u);
-        for (int i = 0; i < F; i++) g[i] = (g[i] / (1.f + expf(-g[i]))) * u[i];
-        matvec_rows(&L->down, (int64_t)e * H, H, g, y);
-        for (int i = 0; i < H; i++) out[i] += y[i] * w[r];
+    int* route_e = (int*)malloc((size_t)R * topk * sizeof(int));
+    float* route_w = (float*)malloc((size_t)R * topk * 4);
+    float* yslot = (float*)malloc((size_t)R * topk * H * 4);
+    float* xs = (float*)malloc((size_t)R * H * 4);
+    float* g = (float*)malloc((size_t)R * FF * 4);
+    float* u = (float*)malloc((size_t)R * FF * 4);
+    float* y = (float*)malloc((size_t)R * H * 4);
+    int* slot_of = (int*)malloc((size_t)R * topk * sizeof(int));
+    matvec_k(&L->router, x, R, lg);
+    for (int r = 0; r < R; r++) {
+        or_route(lg + (int64_t)r * E, E, topk, c->norm_topk_prob, rank, route_w + r * topk);
+        for (int q = 0; q < topk; q++) {
+            route_e[r * topk + q] = rank[q];
+            if (experts_out) experts_out[r * topk + q] = rank[q];
+        }
     }
-    matvec_e(&L->sh_gate, x, g);
-    matvec_e(&L->sh_up, x, u);
-    for (int i = 0; i < Fs; i++) g[i] = (g[i] / (1.f + expf(-g[i]))) * u[i];
-    matvec_e(&L->sh_down, g, y);
-    float sel = 0.f;
-    for (int i = 0; i < H; i++) sel += x[i] * L->selector[i];
-    sel = 1.f / (1.f + expf(-sel));
-    for (int i = 0; i < H; i++) out[i] = out[i] + y[i] * sel;
-    free(lg); free(pr); free(rank); free(g); free(u); free(y);
+    for (int e = 0; e < E; e++) {
+        int n = 0;
+        for (int r = 0; r < R; r++)
+            for (int q = 0; q < topk; q++)
+                if (route_e[r * topk + q] == e) {
+                    memcpy(xs + (int64_t)n * H, x + (int64_t)r * H, (size_t)H * 4);
+                    slot_of[n++] = r * topk + q;
+                }
+        if (!n) continue;
+        matvec_nk(&L->gate, L->gate.p + (int64_t)e * F * or_row_bytes(L->gate.dt, L->gate.cols), F, xs, n, g, 1);
+        matvec_nk(&L->up, L->up.p + (int64_t)e * F * or_row_bytes(L->up.dt, L->up.cols), F, xs, n, u, 1);
+        for (int i = 0; i < n * F; i++) g[i] = (g[i] / (1.f + expf(-g[i]))) * u[i];
+        matvec_nk(&L->down, L->down.p + (int64_t)e * H * or_row_bytes(L->down.dt, L->down.cols), H, g, n, y, 1);
+        for (int i = 0; i < n; i++) memcpy(yslot + (int64_t)slot_of[i] * H, y + (int64_t)i * H, (size_t)H * 4);
+    }
+    for (int r = 0; r < R; r++) {
+        float* o = out + (int64_t)r * H;
+        for (int i = 0; i < H; i++) o[i] = 0.f;
+        for (int q = 0; q < topk; q++) {
+            const float* ys = yslot + (int64_t)(r * topk + q) * H;
+            const float w = route_w[r * topk + q];
+            for (int i = 0; i < H; i++) o[i] += ys[i] * w;
+        }
+    }
+    matvec_nk(&L->sh_gate, L->sh_gate.p, Fs, x, R, g, 1);
+    matvec_nk(&L->sh_up, L->sh_up.p, Fs, x, R, u, 1);
+    for (int i = 0; i < R * Fs; i++) g[i] = (g[i] / (1.f + expf(-g[i]))) * u[i];
+    matvec_nk(&L->sh_down, L->sh_down.p, H, g, R, y, 1);
+    for (int r = 0; r < R; r++) {
+        const float* xr = x + (int64_t)r * H;
+        float sel = 0.f;
+        for (int i = 0; i < H; i++) sel += xr[i] * L->selector[i];
+        sel = 1.f / (1.f + expf(-sel));
+        float* o = out + (int64_t)r * H;
+        const float* ys = y + (int64_t)r * H;
+        for (int i = 0; i < H; i++) o[i] = o[i] + ys[i] * sel;
+    }
+    free(lg); free(rank); free(route_e); free(route_w); free(yslot); free(xs); free(g); free(u); free(y); free(slot_of);
 }
 
-/* One decoder layer on one row, in place (quantized_layer.rs:101-225). */
-static void layer_row(const or_model* m, const layer_t* L, lstate_t* st, int64_t pos, float* h, int* experts) {
+/* One decoder layer on R rows at positions pos.., in place
+ * (quantized_layer.rs:101-225). */
+static void layer_rows(const or_model* m, const layer_t* L, lstate_t* st, int64_t pos, float* h, int R,
+                       int* experts) {
     const int H = m->c.hidden_size;
-    float* xn = (float*)malloc((size_t)H * 4);
-    float* mix = (float*)malloc((size_t)H * 4);
-    rms_norm(h, L->attn_norm, H, m->c.rms_norm_eps, xn);
-    if (L->full) attn_row(m, L, st, pos, xn, mix);
-    else delta_row(m, L, st, xn, mix);
-    for (int i = 0; i < H; i++) h[i] = h[i] + mix[i];
-    rms_norm(h, L->post_norm, H, m->c.rms_norm_eps, xn);
-    moe_row(m, L, xn, mix, experts);
-    for (int i = 0; i < H; i++) h[i] = h[i] + mix[i];
+    float* xn = (float*)malloc((size_t)R * H * 4);
+    float* mix = (float*)malloc((size_t)R * H * 4);
+    for (int r = 0; r < R; r++) rms_norm(h + (int64_t)r * H, L->attn_norm, H, m->c.rms_norm_eps, xn + (int64_t)r * H);
+    if (L->full) attn_rows(m, L, st, pos, xn, R, mix);
+    else delta_rows(m, L, st, xn, R, mix);
+    for (int i = 0; i < R * H; i++) h[i] = h[i] + mix[i];
+    for (int r = 0; r < R; r++) rms_norm(h + (int64_t)r * H, L->post_norm, H, m->c.rms_norm_eps, xn + (int64_t)r * H);
+    moe_rows(m, L, xn, R, mix, experts);
+    for (int i = 0; i < R * H; i++) h[i] = h[i] + mix[i];
     free(xn); free(mix);
+}
+static void layer_row(const or_model* m, const layer_t* L, lstate_t* st, int64_t pos, float* h, int* experts) {
+    layer_rows(m, L, st, pos, h, 1, experts);
 }
 
 /* Evaluate `rows` tokens (QuantizedModel::forward_detailed).  logits
@@ -616,26 +743,36 @@ static void layer_row(const or_model* m, const layer_t* L, lstate_t* st, int64_t
 int or_forward(const or_model* m, or_state* s, const uint32_t* tokens, int rows, float* logits, float* hidden,
                int32_t* experts) {
     const or_config* c = &m->c;
-    const int H = c->hidden_size;
+    const int H = c->hidden_size, topk = c->num_experts_per_tok;
     if (s->position + rows > s->max_pos) return -1;
-    float* h = (float*)malloc((size_t)H * 4);
-    float* hn = (float*)malloc((size_t)H * 4);
-    for (int r = 0; r < rows; r++) {
-        if (tokens[r] >= (uint32_t)c->vocab_size) { free(h); free(hn); return -2; }
-        or_dequant_rows(m->embed.dt, m->embed.p + (int64_t)tokens[r] * or_row_bytes(m->embed.dt, H), 1, H, h);
+    for (int r = 0; r < rows; r++)
+        if (tokens[r] >= (uint32_t)c->vocab_size) return -2;
+    /* passes of up to 8 rows through every layer (the reference's verify
+     * width; a row's arithmetic does not depend on the pass it runs in) */
+    if (s->snap_rows > 0 && rows > s->snap_rows) return -3;
+    s->snap_pos0 = s->position;
+    s->snap_taken = rows;
+    for (int r0 = 0; r0 < rows; r0 += 8) {
+        const int R = rows - r0 < 8 ? rows - r0 : 8;
+        float* h = (float*)malloc((size_t)R * H * 4);
+        float* hn = (float*)malloc((size_t)R * H * 4);
+        int* ex = (int*)malloc((size_t)R * topk * sizeof(int));
+        for (int r = 0; r < R; r++)
+            or_dequant_rows(m->embed.dt, m->embed.p + (int64_t)tokens[r0 + r] * or_row_bytes(m->embed.dt, H), 1, H,
+                            h + (int64_t)r * H);
         for (int l = 0; l < c->num_hidden_layers; l++) {
-            int ex[16];
-            layer_row(m, &m->layers[l], &s->l[l], s->position, h, ex);
+            layer_rows(m, &m->layers[l], &s->l[l], s->position, h, R, ex);
             if (experts)
-                for (int i = 0; i < c->num_experts_per_tok; i++)
-                    experts[((int64_t)r * c->num_hidden_layers + l) * c->num_experts_per_tok + i] = ex[i];
+                for (int r = 0; r < R; r++)
+                    for (int i = 0; i < topk; i++)
+                        experts[((int64_t)(r0 + r) * c->num_hidden_layers + l) * topk + i] = ex[r * topk + i];
         }
-        rms_norm(h, m->out_norm, H, c->rms_norm_eps, hn);
-        if (hidden) memcpy(hidden + (int64_t)r * H, hn, (size_t)H * 4);
-        if (logits) matvec(&m->lm_head, hn, logits + (int64_t)r * c->vocab_size);
-        s->position++;
+        for (int r = 0; r < R; r++) rms_norm(h + (int64_t)r * H, m->out_norm, H, c->rms_norm_eps, hn + (int64_t)r * H);
+        if (hidden) memcpy(hidden + (int64_t)r0 * H, hn, (size_t)R * H * 4);
+        if (logits) matvec_k(&m->lm_head, hn, R, logits + (int64_t)r0 * c->vocab_size);
+        s->position += R;
+        free(h); free(hn); free(ex);
     }
-    free(h); free(hn);
     return 0;
 }
 

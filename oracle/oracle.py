@@ -81,6 +81,16 @@ def set_gemv_order(order: int) -> None:
     lib().or_set_gemv_order(order)
 
 
+def force_scalar(on: bool) -> None:
+    """Use the scalar restatement of the reference order even where the
+    AVX2 form (bitwise the same) is available."""
+    lib().or_force_scalar(int(on))
+
+
+def have_avx2() -> bool:
+    return bool(lib().or_have_avx2())
+
+
 def set_perturb(mode: int) -> None:
     """Diagnostic: 1 or 2 moves every RMSNorm output by one ulp (two
     opposite patterns), 0 turns it off: the conditioning of the reference
@@ -295,6 +305,22 @@ class OracleState:
         b = np.ascontiguousarray(buf, np.uint8)
         rc = lib().or_state_import(self.model._h, self._h, _p(b), b.size)
         assert rc == 0, rc
+
+    def enable_snapshots(self, rows: int) -> None:
+        """Keep the DeltaNet state after each row of a pass of up to `rows`
+        rows, so rollback() is a copy (QuantizedStateSnapshots)."""
+        L = lib()
+        L.or_state_enable_snapshots.argtypes = [P, P, I32]
+        assert L.or_state_enable_snapshots(self.model._h, self._h, rows) == 0
+
+    def rollback(self, committed: int) -> None:
+        """Keep the first `committed` rows of the last pass."""
+        L = lib()
+        L.or_state_rollback.argtypes = [P, P, I32]
+        assert L.or_state_rollback(self.model._h, self._h, committed) == 0
+
+    def set_mtp_position(self, position: int) -> None:
+        lib().or_state_set_mtp_position(self._h, position)
 
     def copy_from(self, other: "OracleState"):
         lib().or_state_copy(self.model._h, self._h, other._h)

@@ -72,3 +72,23 @@ def test_oracle_state_image_round_trip():
     la, _, _ = a.forward([77, 78])
     lb, _, _ = b.forward([77, 78])
     assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+
+
+def test_oracle_rollback_restores_the_committed_rows():
+    """The oracle's verification snapshots: a 4-row pass rolled back to 2
+    rows continues exactly like a 2-row pass (DeltaNet state from the
+    snapshot, KV truncated by the position)."""
+    import oracle
+    cfg = synth.tiny()
+    om = oracle.OracleModel(cfg, list(synth.generate(cfg, seed=6)))
+    a, b = om.state(64), om.state(64)
+    a.enable_snapshots(4)
+    for st in (a, b):
+        st.forward([3, 4, 5])
+    a.forward([7, 8, 9, 10])
+    a.rollback(2)
+    b.forward([7, 8])
+    assert a.position == b.position == 5
+    la, _, _ = a.forward([11])
+    lb, _, _ = b.forward([11])
+    assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))

@@ -66,3 +66,25 @@ def test_argmax_takes_the_last_max_and_skips_non_finite():
     assert oracle.argmax(np.array([1, 3, 3, 2], np.float32)) == 2
     assert oracle.argmax(np.array([np.nan, 1, np.inf, -np.inf], np.float32)) == 1
     assert oracle.argmax(np.array([np.nan], np.float32)) == -1
+
+
+@pytest.mark.parametrize("dtype", [12, 14, 8])
+def test_avx2_reference_order_equals_the_scalar_restatement(dtype):
+    """The oracle's AVX2 reference-order kernels (the CPU baseline's fast
+    path) are bitwise its scalar restatement of src/qgemm.rs, for 1..11
+    input rows (several 8-row tiles)."""
+    import torch
+    from inferq_b200 import quants as Q
+    if not oracle.have_avx2():
+        pytest.skip("no AVX2 on this CPU")
+    rows, cols = 37, 1024
+    w = Q.encode(torch.randn(rows, cols, generator=torch.Generator().manual_seed(dtype)) * 0.02, dtype).numpy()
+    for k in (1, 4, 8, 11):
+        x = np.random.default_rng(k).standard_normal((k, cols)).astype(np.float32)
+        fast = oracle.qmatvec(dtype, w, rows, cols, x)
+        oracle.force_scalar(True)
+        try:
+            slow = oracle.qmatvec(dtype, w, rows, cols, x)
+        finally:
+            oracle.force_scalar(False)
+        assert np.array_equal(fast.view(np.uint32), slow.view(np.uint32)), k
