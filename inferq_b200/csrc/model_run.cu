@@ -24,6 +24,7 @@ struct QmvRec {
   int njobs = 0;
   int ntiles = 0;
   int smem = 0;
+  int slot = 0;   // ring slot bytes: the largest unit of the launch's dtypes
 };
 
 struct LayerRec {
@@ -156,6 +157,7 @@ QmvRec add_launch(std::vector<QmvJob>& table, std::vector<QmvJob> jobs) {
     j.tile0 = tiles;
     tiles += qmv_tiles(j);
     smem = std::max(smem, j.n * j.act_row_bytes);
+    r.slot = std::max(r.slot, qmv_slot_bytes(j.dtype));
     table.push_back(j);
   }
   r.ntiles = tiles;
@@ -173,7 +175,9 @@ struct Ctx {
   // debugging); results are identical either way.
   // Kernel fusions (IQ_FUSE=<bitmask>; results are bitwise the same either
   // way).  Default 1|2|4|16, measured faster at k = 1, 4 and 8 (35B shapes);
-  // 8 puts redundant normalization on every router CTA and measured slower:
+  // 8 puts redundant normalization on every router CTA and measured slower;
+  // 32 (not a fusion, off by default: measured 1% slower at k = 4) sizes
+  // GEMV ring slots per launch:
   // 1 MoE combine into the next RMSNorm, 2 gated norm + Q8_0 into the
   // DeltaNet kernel, 4 SwiGLU into the down GEMV, 8 RMSNorm + Q8_K into the
   // f32 router, 16 output-projection quantization into the attention combine.
@@ -182,6 +186,8 @@ struct Ctx {
     const char* f = getenv("IQ_FUSE");
     fuse = f ? atoi(f) : 23;
   }
+  // ring slots sized for the launch's dtypes (fuse bit 32), else the largest
+  int slot(int bytes) const { return (fuse & 32) ? bytes : 0; }
   // Stage timer: under profiling every stage is bracketed by CUDA events.
   void mark(const char* name) {
     if (!s->profiling) return;
@@ -279,7 +285,7 @@ int qmv(Ctx& x, const QmvRec& r, const QmvPrologue* pro = nullptr) {
     x.mark("act.prep");
   }
   ++x.s->launch_count;
-  IQ_CUDA(qmv_launch(x.s->jobs.as<QmvJob>() + r.job, r.njobs, nullptr, r.ntiles, r.smem, x.st, x.pdl));
+  IQ_CUDA(qmv_launch(x.s->jobs.as<QmvJob>() + r.job, r.njobs, nullptr, r.ntiles, r.smem, x.st, x.pdl, x.slot(r.slot)));
   return IQ_OK;
 }
 
@@ -396,7 +402,7 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   if (W.router.present()) {
     ++x.s->launch_count;
     IQ_CUDA(qmv_launch(x.s->jobs.as<QmvJob>() + R.router.job, R.router.njobs, nullptr, R.router.ntiles, R.router.smem,
-                       x.st, x.pdl));
+                       x.st, x.pdl, x.slot(R.router.slot)));
     x.mark("moe.router");
     ++x.s->launch_count;
     IQ_CUDA(f32_matvec(W.selector.p(), 1, H, rin, H, k, lg + E, E + 1, x.st, x.pdl, rnorm, c.rms_norm_eps));
@@ -488,7 +494,8 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   const int down_tiles = max_union * t.tiles_down + tiles_sh_down;
   const int gu_smem = k * (int)std::max(s->act8k_bytes, s->act80_bytes);
   ++x.s->launch_count;
-  IQ_CUDA(qmv_launch(a.gu_jobs, 0, a.gu_count, gu_tiles, gu_smem, x.st, x.pdl));
+  IQ_CUDA(qmv_launch(a.gu_jobs, 0, a.gu_count, gu_tiles, gu_smem, x.st, x.pdl,
+                     x.slot(std::max(qmv_slot_bytes(W.gate.dt), qmv_slot_bytes(W.sh_gate.dt)))));
   x.mark("moe.gate_up");
   MoeActArgs b = {};
   b.gu = a.gu_out;
@@ -519,7 +526,8 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   if (ep) IQ_CUDA(cudaMemsetAsync(a.y, 0, routed * sizeof(float), x.st));
   ++x.s->launch_count;
   IQ_CUDA(qmv_launch(a.down_jobs, 0, a.down_count, down_tiles,
-                     ((x.fuse & 4) ? k : k * c.num_experts_per_tok + k) * (int)s->act_mid_bytes, x.st, x.pdl));
+                     ((x.fuse & 4) ? k : k * c.num_experts_per_tok + k) * (int)s->act_mid_bytes, x.st, x.pdl,
+                     x.slot(std::max(qmv_slot_bytes(W.down.dt), qmv_slot_bytes(W.sh_down.dt)))));
   x.mark("moe.down");
   if (ep) {
     const ncclResult_t r =
@@ -822,7 +830,8 @@ int run_mtp_draft(iq_state* s, int depth, int vocab) {
     ++s->launch_count;
     IQ_CUDA(qmv_launch(s->mtp_head_job.as<QmvJob>(), 1, nullptr,
                        (int)ceil_div(vocab, qmv_rows_per_cta(qmv_ksplit(m->lm_head.dt, vocab, m->lm_head.cols))),
-                       (int)(m->lm_head.dt == Q8_0 ? s->act80_bytes : s->act8k_bytes), x.st, x.pdl));
+                       (int)(m->lm_head.dt == Q8_0 ? s->act80_bytes : s->act8k_bytes), x.st, x.pdl,
+                       x.slot(qmv_slot_bytes(m->lm_head.dt))));
     x.mark("mtp.head");
     HeadArgs h = {};
     h.logits = s->logits.as<float>();

@@ -409,10 +409,12 @@ __device__ __forceinline__ void issue_unit(const StreamPos& p, uint8_t* slot, ui
 }
 
 // Dynamic shared memory: [activation rows (act_bytes, rounded up to 128)]
-// [kQmvWarps x depth slots of kSlotBytes].
+// [kQmvWarps x depth slots of slot_bytes] (slot_bytes: the largest unit of the
+// launch's dtypes, a multiple of 128 up to kSlotBytes).
 __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs, int njobs,
                                                              const int* __restrict__ dyn_count, int total_hint,
-                                                             int act_bytes, int depth, int test_skip) {
+                                                             int act_bytes, int depth, int slot_bytes,
+                                                             int test_skip) {
   __shared__ float part[kQmvWarps][32][4];
   // the job table in shared memory when it is small (one parallel copy, no
   // dependent global reads later); otherwise just the jobs' tile offsets
@@ -426,7 +428,7 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
   const int gid = lane >> 2, tig = lane & 3;
   // TMA destinations: 128-byte aligned (the launch adds 128 bytes of slack)
   const uint32_t ring0 = (smem_u32(act_smem) + (uint32_t)act_bytes + 127u) & ~127u;
-  uint8_t* ring = act_smem + (ring0 - smem_u32(act_smem)) + warp * depth * kSlotBytes;
+  uint8_t* ring = act_smem + (ring0 - smem_u32(act_smem)) + warp * depth * slot_bytes;
   uint64_t* wbars = bars[warp];
   if (lane == 0) {
     for (int i = 0; i < depth; i++) mbar_init(&wbars[i], 1);
@@ -475,7 +477,7 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
   const int wait_limit = test_skip ? 256 : 1 << 20;
   uint32_t issued = 0;
   for (int i = 0; i < depth && pp.tile < total; i++) {
-    if (lane == 0 && !(skip_first && i == 0)) issue_unit(pp, ring + i * kSlotBytes, &wbars[i], pol);
+    if (lane == 0 && !(skip_first && i == 0)) issue_unit(pp, ring + i * slot_bytes, &wbars[i], pol);
     issued++;
     pp.b++;
     stream_settle(jobs, t0, njobs, total, warp, pp);
@@ -561,7 +563,7 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
     if (ct.live() && ok) {
       for (int b = ct.u0; b < ct.u1; b++, n++) {
         const uint32_t si = n % depth;
-        uint8_t* slot = ring + si * kSlotBytes;
+        uint8_t* slot = ring + si * slot_bytes;
         if (!mbar_wait(&wbars[si], (n / depth) & 1, wait_limit)) {
           if (lane == 0) atomicExch(&g_qmv_timeout, 1);
           ok = false;
@@ -724,12 +726,14 @@ cudaError_t qmv_tensor_maps(int dt, const uint8_t* base, int64_t rows, int64_t c
 }
 
 cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int ntiles, int smem_bytes,
-                       cudaStream_t stream, bool pdl) {
+                       cudaStream_t stream, bool pdl, int slot_bytes) {
   if (ntiles <= 0) return cudaSuccess;
   const SmemLimits lim = qmv_dyn_smem_limits();
   if (!lim.one) return cudaErrorInvalidValue;
+  if (slot_bytes <= 0) slot_bytes = kSlotBytes;
+  if (slot_bytes % 128 || slot_bytes > kSlotBytes) return cudaErrorInvalidValue;
   const int act = ((smem_bytes + 127) & ~127) + 128;  // + alignment slack of the ring
-  const int ring_unit = kQmvWarps * kSlotBytes;
+  const int ring_unit = kQmvWarps * slot_bytes;
   int depth = std::min(kQmvMaxDepth, (lim.two - act) / ring_unit);
   int ctas = qmv_persistent_ctas();
   if (depth < 2) {  // many activation rows: one CTA per SM
@@ -749,7 +753,7 @@ cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int 
   cfg.numAttrs = pdl ? 1 : 0;
   static const int test_skip = getenv("IQ_QMV_TEST_TIMEOUT") ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, qmv_kernel, jobs, njobs, dyn_count, dyn_count ? 0 : ntiles, smem_bytes, depth,
-                            test_skip);
+                            slot_bytes, test_skip);
 }
 
 }  // namespace iq

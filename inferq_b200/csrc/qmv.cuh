@@ -52,7 +52,7 @@ struct QmvJob {
 // Two persistent CTAs per SM; each of their warps streams 16 weight rows.
 constexpr int kQmvWarps = 8;
 constexpr int kQmvThreads = 32 * kQmvWarps;
-constexpr int kQmvMaxDepth = 4;  // weight units in flight per warp (at most)
+constexpr int kQmvMaxDepth = 8;  // weight units in flight per warp (at most)
 // Rows one CTA covers for a job.
 __host__ __device__ inline int qmv_rows_per_cta(int ksplit) { return 16 * (kQmvWarps / ksplit); }
 __host__ __device__ inline int qmv_units(int dt, int cols) {
@@ -106,8 +106,16 @@ struct QmvPrologue {
 // CTAs past the last job's tiles exit.
 // `smem_bytes` must cover n * act_row_bytes of every job in the table; the
 // rest of the CTA's shared memory holds the weight ring (2..4 units per warp).
+// `slot_bytes` (0: the largest of any dtype) sizes each ring slot for the
+// largest unit the launch streams (qmv_slot_bytes of its dtypes), so launches
+// of smaller units keep more of them in flight.
 cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int ntiles, int smem_bytes,
-                       cudaStream_t stream, bool pdl);
+                       cudaStream_t stream, bool pdl, int slot_bytes = 0);
+// Ring slot bytes of one unit of dtype `dt` (16 rows, plus the scale-tail
+// piece of Q6_K / Q8_0), a multiple of 128.
+inline int qmv_slot_bytes(int dt) {
+  return dt == Q4_K ? 16 * 144 : dt == Q5_K ? 16 * 176 : dt == Q6_K ? 16 * 208 + 256 : 16 * 128 + 256;
+}
 
 // Encode the tensor maps the kernel loads a weight tensor through (device
 // layout, `rows` x `cols`) into `maps`: [0] the unit box, [1] the tail box
