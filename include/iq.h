@@ -33,6 +33,7 @@ extern "C" {
 #define IQ_Q4_K 12
 #define IQ_Q5_K 13
 #define IQ_Q6_K 14
+#define IQ_BF16 30
 
 /* Where a caller-supplied buffer lives. */
 #define IQ_HOST 0
@@ -53,7 +54,11 @@ typedef struct iq_matrix iq_matrix;
 /* Upload `rows` GGUF rows of `cols` weights (bytes at `data`, in host or
  * device memory per `location`) to the current device in the device layout.
  * Replaces GgufCheckpoint::load_matrix -> QuantizedMatrix::new
- * (src/gguf.rs:1234-1253, :305-330): same dtype set minus BF16. */
+ * (src/gguf.rs:1234-1253, :305-330): the same dtype set, Q4_K, Q5_K, Q6_K,
+ * Q8_0, F32 and BF16 (cols a multiple of 8).  A BF16 matrix multiplies its
+ * input rows rounded to bf16 (candle's BF16 vec-dot input type) with exact
+ * products summed in f32; the model loader takes BF16 only for 1-D
+ * tensors, and the wide form takes quantized matrices only. */
 int iq_matrix_create(int dtype, const void* data, int64_t rows, int64_t cols, int location,
                      iq_matrix** out);
 /* A matrix of the first `rows` rows sharing storage with `m`

@@ -21,7 +21,7 @@ void set_error(const char* fmt, ...) {
 void clear_error() { g_error.clear(); }
 
 static bool supported_dtype(int dt) {
-  return dt == F32 || dt == Q8_0 || dt == Q4_K || dt == Q5_K || dt == Q6_K;
+  return dt == F32 || dt == BF16 || dt == Q8_0 || dt == Q4_K || dt == Q5_K || dt == Q6_K;
 }
 
 // Checks shared by every upload: the reference accepts Q4_K, Q5_K, Q6_K, Q8_0,
@@ -29,10 +29,10 @@ static bool supported_dtype(int dt) {
 // whole blocks, and for Q8_0 whole groups of four blocks.
 int validate_matrix_shape(int dtype, int64_t rows, int64_t cols) {
   IQ_CHECK(supported_dtype(dtype), IQ_EUNSUPPORTED,
-           "unsupported executable GGUF matrix dtype %d; expected Q4_K, Q5_K, Q6_K, Q8_0, or F32", dtype);
+           "unsupported executable GGUF matrix dtype %d; expected Q4_K, Q5_K, Q6_K, Q8_0, F32, or BF16", dtype);
   IQ_CHECK(rows > 0 && cols > 0, IQ_EINVAL, "matrix shape [%lld, %lld] is empty", (long long)rows,
            (long long)cols);
-  const int64_t unit = dtype == Q8_0 ? 128 : dtype == F32 ? 4 : 256;
+  const int64_t unit = dtype == Q8_0 ? 128 : dtype == F32 ? 4 : dtype == BF16 ? 8 : 256;
   IQ_CHECK(cols % unit == 0, IQ_EINVAL, "matrix with %lld columns is not a multiple of %lld for dtype %d",
            (long long)cols, (long long)unit, dtype);
   IQ_CHECK(rows < (1ll << 31), IQ_EINVAL, "matrix has too many rows (%lld)", (long long)rows);
@@ -45,7 +45,7 @@ int upload_rows(int dtype, const void* data, int64_t rows, int64_t cols, int loc
   const int64_t src_bytes = gguf_row_bytes(dtype, cols) * rows;
   const int64_t dst_bytes = dev_row_bytes(dtype, cols) * rows;
   IQ_CUDA(out.reserve((size_t)dst_bytes));
-  if (dtype == F32) {
+  if (dtype == F32 || dtype == BF16) {  // used as stored
     IQ_CUDA(cudaMemcpyAsync(out.p, data, (size_t)src_bytes,
                             location == IQ_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, st));
     return IQ_OK;
@@ -79,6 +79,11 @@ int matrix_forward_dev(const iq_matrix* m, const float* x, int k, float* y, cuda
   if (m->dtype == F32) {
     IQ_CUDA(f32_matvec(reinterpret_cast<const float*>(m->base), (int)m->rows, (int)m->cols, x, (int)m->cols, k, y,
                        (int)m->rows, st, false));
+    return IQ_OK;
+  }
+  if (m->dtype == BF16) {
+    IQ_CUDA(bf16_matvec(reinterpret_cast<const uint16_t*>(m->base), (int)m->rows, (int)m->cols, x, (int)m->cols, k,
+                        y, (int)m->rows, st));
     return IQ_OK;
   }
   const bool kq = m->dtype != Q8_0;
@@ -145,7 +150,7 @@ int iq_matrix_create(int dtype, const void* data, int64_t rows, int64_t cols, in
   rc = upload_rows(dtype, data, rows, cols, location, *buf, nullptr);
   if (rc) return rc;
   auto maps = std::make_shared<DevBuf>();
-  if (dtype != F32 && dtype != F16)
+  if (dtype != F32 && dtype != F16 && dtype != BF16)
     IQ_CHECK(qmv_tensor_maps(dtype, buf->as<uint8_t>(), rows, cols, *maps) == cudaSuccess, IQ_ECUDA,
              "cannot describe the matrix for the TMA unit");
   auto* m = new iq_matrix;
@@ -274,7 +279,7 @@ int iq_qgemv(int dtype, const void* w, int64_t rows, int64_t cols, const float* 
 
 int iq_qgemv_ksplit(int dtype, int64_t rows, int64_t cols) {
   if (validate_matrix_shape(dtype, rows, cols)) return IQ_EINVAL;
-  return dtype == F32 ? 1 : qmv_ksplit(dtype, rows, cols);
+  return dtype == F32 || dtype == BF16 ? 1 : qmv_ksplit(dtype, rows, cols);
 }
 
 int iq_matrix_dequantize(const iq_matrix* m, const int32_t* ids, int64_t n, float* out) {

@@ -2,6 +2,7 @@
 // whose GGUF tensor is F32 and which the reference multiplies in f32,
 // src/qwen/quantized_moe.rs:253).  One warp per weight row; lane l sums the
 // float4 at columns 4l + 128t in order of t, then a butterfly over lanes.
+#include <cuda_bf16.h>
 #include "kernels.cuh"
 #include "devfns.cuh"
 
@@ -92,7 +93,60 @@ __global__ void __launch_bounds__(256) f32_matvec_kernel(const float* __restrict
   }
 }
 
+// One warp per weight row; the k input rows are staged rounded to bf16 (as
+// f32); each lane sums its columns' exact products in column order, then the
+// lanes combine in a fixed tree.
+__global__ void __launch_bounds__(256) bf16_matvec_kernel(const uint16_t* __restrict__ w, int rows, int cols,
+                                                         const float* __restrict__ x, int ldx, int k,
+                                                         float* __restrict__ y, int ldy) {
+  extern __shared__ float xb[];  // [k][cols]
+  for (int i = threadIdx.x; i < k * cols; i += 256) {
+    const int rr = i / cols, c = i % cols;
+    xb[i] = __bfloat162float(__float2bfloat16_rn(x[(int64_t)rr * ldx + c]));
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + warp;
+  if (r >= rows) return;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  const uint16_t* wr = w + (int64_t)r * cols;
+  for (int c = 8 * lane; c < cols; c += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(wr + c);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const float wf = __uint_as_float(e & 1 ? (u[e / 2] & 0xffff0000u) : (u[e / 2] << 16));
+#pragma unroll
+      for (int i = 0; i < 8; i++)
+        if (i < k) acc[i] = fmaf(wf, xb[i * cols + c + e], acc[i]);  // the product is exact
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    if (i >= k) break;
+    float v = acc[i];
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+    if (lane == 0) y[(int64_t)i * ldy + r] = v;
+  }
+}
+
 }  // namespace
+
+cudaError_t bf16_matvec(const uint16_t* w, int rows, int cols, const float* x, int ldx, int k, float* y, int ldy,
+                        cudaStream_t st) {
+  if (cols % 8 || k < 1 || k > 8 || (size_t)k * cols * sizeof(float) > 200 * 1024 || ((uintptr_t)w & 15))
+    return cudaErrorInvalidValue;
+  static bool configured[64] = {};
+  static std::mutex mu;
+  const cudaError_t e = once_per_device(configured, mu, [] {
+    return cudaFuncSetAttribute(bf16_matvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  });
+  if (e != cudaSuccess) return e;
+  bf16_matvec_kernel<<<(unsigned)ceil_div(rows, 8), 256, (size_t)k * cols * sizeof(float), st>>>(w, rows, cols, x,
+                                                                                                ldx, k, y, ldy);
+  return cudaGetLastError();
+}
 
 cudaError_t f32_matvec(const float* w, int rows, int cols, const float* x, int ldx, int k, float* y, int ldy,
                        cudaStream_t st, bool pdl, const float* norm_w, float eps, uint8_t* q8k_out, int q8k_stride) {

@@ -56,6 +56,7 @@ __device__ __forceinline__ float dev_weight(int dt, const uint8_t* row, int nb, 
       return __fmul_rn((float)q, d);
     }
     case F32: return reinterpret_cast<const float*>(row)[e];
+    case BF16: return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(row)[e] << 16);
     default: return __half2float(reinterpret_cast<const __half*>(row)[e]);
   }
 }

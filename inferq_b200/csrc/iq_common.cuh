@@ -12,7 +12,7 @@
 namespace iq {
 
 // GGML dtype ids.
-enum Dtype : int { F32 = 0, F16 = 1, Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14, Q8_K = 15 };
+enum Dtype : int { F32 = 0, F16 = 1, Q8_0 = 8, Q4_K = 12, Q5_K = 13, Q6_K = 14, Q8_K = 15, BF16 = 30 };
 
 constexpr int kWarp = 32;
 

@@ -43,6 +43,11 @@ cudaError_t f32_matvec(const float* w, int rows, int cols, const float* x, int l
                        int ldy, cudaStream_t st, bool pdl, const float* norm_w = nullptr, float eps = 0.f,
                        uint8_t* q8k_out = nullptr, int q8k_stride = 0);
 
+// BF16 matrix rows (row-major bf16 bits): y[i*ldy + r] = sum_c w[r][c] *
+// bf16(x[i][c]) with exact products summed in f32; k <= 8, cols % 8 == 0.
+cudaError_t bf16_matvec(const uint16_t* w, int rows, int cols, const float* x, int ldx, int k, float* y, int ldy,
+                        cudaStream_t st);
+
 // Wide Q8_0 product on the tensor cores (wide.cu): y[t*out_ld + r] for
 // ntok input rows x[t*ldx ..]; qx (ntok x cols f16), dT (cols/32 x
 // wide_ldd(ntok) f32) and wx (rows x cols f16) are scratch.  cols % 128 == 0.

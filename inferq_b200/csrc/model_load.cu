@@ -44,6 +44,9 @@ struct Loader {
     if (!v) return missing(n);
     IQ_CHECK(v->ndim >= 2 && v->shape[v->ndim - 1] == cols && elems(v) == rows * cols, IQ_EINVAL,
              "invalid GGUF shape for \"%s\": expected [%lld, %lld]", n.c_str(), (long long)rows, (long long)cols);
+    IQ_CHECK(v->dtype != BF16, IQ_EUNSUPPORTED,
+             "tensor \"%s\" is BF16: the model pass takes quantized or F32 matrices (BF16 matrices run through "
+             "the operator entry points)", n.c_str());
     int rc = validate_matrix_shape(v->dtype, rows, cols);
     if (rc) {
       set_error("tensor \"%s\": %s", n.c_str(), iq_last_error());
@@ -66,6 +69,8 @@ struct Loader {
     IQ_CHECK(v->ndim == 3 && v->shape[0] == E && v->shape[1] == rows_per && v->shape[2] == cols, IQ_EINVAL,
              "invalid expert shape for \"%s\": expected [%lld, %lld, %lld]", n.c_str(), (long long)E,
              (long long)rows_per, (long long)cols);
+    IQ_CHECK(v->dtype != BF16, IQ_EUNSUPPORTED, "expert tensor \"%s\" is BF16 (quantized experts only)",
+             n.c_str());
     int rc = validate_matrix_shape(v->dtype, rows_per, cols);
     if (rc) return rc;
     const uint8_t* base = static_cast<const uint8_t*>(v->data) + e0 * rows_per * gguf_row_bytes(v->dtype, cols);
@@ -84,7 +89,8 @@ struct Loader {
     if (!v) return missing(name);
     IQ_CHECK(elems(v) == n, IQ_EINVAL, "invalid length for \"%s\": %lld elements, expected %lld", name.c_str(),
              (long long)elems(v), (long long)n);
-    IQ_CHECK(v->dtype == F32 || v->dtype == F16, IQ_EUNSUPPORTED, "tensor \"%s\" must be F32 or F16", name.c_str());
+    IQ_CHECK(v->dtype == F32 || v->dtype == F16 || v->dtype == BF16, IQ_EUNSUPPORTED,
+             "tensor \"%s\" must be F32, F16 or BF16", name.c_str());
     IQ_CUDA(out.buf.reserve((size_t)n * 4));
     out.n = n;
     if (v->dtype == F32) {
@@ -92,10 +98,19 @@ struct Loader {
                          v->location == IQ_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice));
       return IQ_OK;
     }
-    IQ_CHECK(v->location == IQ_HOST, IQ_EUNSUPPORTED, "F16 vector \"%s\" must be in host memory", name.c_str());
+    IQ_CHECK(v->location == IQ_HOST, IQ_EUNSUPPORTED, "F16 / BF16 vector \"%s\" must be in host memory",
+             name.c_str());
     std::vector<float> tmp(n);
-    const __half* h = static_cast<const __half*>(v->data);
-    for (int64_t i = 0; i < n; i++) tmp[i] = __half2float(h[i]);
+    if (v->dtype == BF16) {  // exact widening (src/gguf.rs:1487-1495 loads BF16 vectors as f32)
+      const uint16_t* h = static_cast<const uint16_t*>(v->data);
+      for (int64_t i = 0; i < n; i++) {
+        const uint32_t u = (uint32_t)h[i] << 16;
+        memcpy(&tmp[i], &u, 4);
+      }
+    } else {
+      const __half* h = static_cast<const __half*>(v->data);
+      for (int64_t i = 0; i < n; i++) tmp[i] = __half2float(h[i]);
+    }
     IQ_CUDA(cudaMemcpy(out.buf.p, tmp.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
     return IQ_OK;
   }

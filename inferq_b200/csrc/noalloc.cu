@@ -71,6 +71,7 @@ extern "C" int iq_matrix_forward_device_noalloc(const iq_matrix* m, const float*
            (long long)m->cols);
   IQ_CHECK(((uintptr_t)x & 15) == 0, IQ_EINVAL,
            "the no-allocation forward needs 16-byte aligned input rows (it cannot stage a copy)");
+  IQ_CHECK(m->dtype != BF16, IQ_EUNSUPPORTED, "the no-allocation forward takes quantized or F32 matrices");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (m->dtype == F32) {
     IQ_CUDA(f32_matvec(reinterpret_cast<const float*>(m->base), (int)m->rows, (int)m->cols, x, (int)m->cols,

@@ -13,10 +13,10 @@ from __future__ import annotations
 
 import torch
 
-F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K = 0, 1, 8, 12, 13, 14, 15
-BLOCK = {Q8_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256, F32: 1, F16: 1}
-BLOCK_BYTES = {Q8_0: 34, Q4_K: 144, Q5_K: 176, Q6_K: 210, F32: 4, F16: 2}
-NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
+F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K, BF16 = 0, 1, 8, 12, 13, 14, 15, 30
+BLOCK = {Q8_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256, F32: 1, F16: 1, BF16: 1}
+BLOCK_BYTES = {Q8_0: 34, Q4_K: 144, Q5_K: 176, Q6_K: 210, F32: 4, F16: 2, BF16: 2}
+NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K", BF16: "BF16"}
 
 
 def row_bytes(dtype: int, cols: int) -> int:
@@ -122,5 +122,7 @@ def encode(x: torch.Tensor, dtype: int) -> torch.Tensor:
         return x.contiguous().view(torch.uint8).reshape(rows, rb)
     if dtype == F16:
         return x.to(torch.float16).contiguous().view(torch.uint8).reshape(rows, rb)
+    if dtype == BF16:
+        return x.to(torch.bfloat16).contiguous().view(torch.uint8).reshape(rows, rb)
     out = _ENCODERS[dtype](x.reshape(-1, BLOCK[dtype]).contiguous())
     return out.reshape(rows, rb).contiguous()

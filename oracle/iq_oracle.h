@@ -24,7 +24,7 @@ extern "C" {
 #endif
 
 enum { OR_F32 = 0, OR_F16 = 1, OR_Q8_0 = 8, OR_Q4_K = 12, OR_Q5_K = 13,
-       OR_Q6_K = 14, OR_Q8_K = 15 };
+       OR_Q6_K = 14, OR_Q8_K = 15, OR_BF16 = 30 };
 
 /* Bytes of one GGUF row of `cols` weights (cols a multiple of the block). */
 int64_t or_row_bytes(int dtype, int64_t cols);

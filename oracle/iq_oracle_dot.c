@@ -235,6 +235,34 @@ int or_qmatvec(int dtype, const void* wv, int64_t rows, int64_t cols,
             }
         return 0;
     }
+    if (dtype == OR_BF16) {
+        /* QuantizedMatrix of BF16 (src/gguf.rs:305-316) runs candle's matmul
+         * with bf16 as the vec-dot type: input rows rounded to bf16 (round to
+         * nearest even), exact products summed in f32 (candle-core 0.11.0,
+         * unvendored; its summation order is unpinned: serial here) */
+        const uint16_t* wb = (const uint16_t*)wv;
+        float* xb = (float*)malloc((size_t)(k * cols) * 4);
+        for (int64_t i = 0; i < k * cols; i++) {
+            uint32_t u;
+            memcpy(&u, x + i, 4);
+            u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;  /* RNE to bf16 (finite inputs) */
+            memcpy(xb + i, &u, 4);
+        }
+        #pragma omp parallel for schedule(static)
+        for (int64_t r = 0; r < rows; r++)
+            for (int i = 0; i < k; i++) {
+                float s = 0.f;
+                for (int64_t c = 0; c < cols; c++) {
+                    uint32_t u = (uint32_t)wb[r * cols + c] << 16;
+                    float w;
+                    memcpy(&w, &u, 4);
+                    s += w * xb[i * cols + c];
+                }
+                y[i * rows + r] = s;
+            }
+        free(xb);
+        return 0;
+    }
     int is_k = dtype == OR_Q4_K || dtype == OR_Q5_K || dtype == OR_Q6_K;
     if (!is_k && dtype != OR_Q8_0) return -1;
     int blk = is_k ? 256 : 32;

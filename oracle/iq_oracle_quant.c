@@ -133,6 +133,9 @@ int or_dequant_rows(int dtype, const void* w, int64_t rows, int64_t cols, float*
     switch (dtype) {
     case OR_F32: memcpy(out, w, (size_t)n * 4); return 0;
     case OR_F16: for (int64_t i = 0; i < n; i++) out[i] = or_f16_to_f32(rd16(p + 2 * i)); return 0;
+    case OR_BF16:  /* exact widening: the bf16 bits are the top half of the f32 */
+        for (int64_t i = 0; i < n; i++) { uint32_t u = (uint32_t)rd16(p + 2 * i) << 16; memcpy(out + i, &u, 4); }
+        return 0;
     case OR_Q4_K: for (int64_t i = 0; i < n / 256; i++) deq_q4k(p + 144 * i, out + 256 * i); return 0;
     case OR_Q5_K: for (int64_t i = 0; i < n / 256; i++) deq_q5k(p + 176 * i, out + 256 * i); return 0;
     case OR_Q6_K: for (int64_t i = 0; i < n / 256; i++) deq_q6k(p + 210 * i, out + 256 * i); return 0;
