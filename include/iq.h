@@ -206,8 +206,14 @@ int iq_state_position(const iq_state* s, int64_t* position);
 int iq_state_stream(const iq_state* s, void** stream);
 
 /* Evaluate `rows` tokens at the state's position and commit all of them
- * (QuantizedModel::forward_detailed, quantized_model.rs:599-621; prefill
- * splits into passes of at most 8 rows).  Outputs are host buffers or NULL:
+ * (QuantizedModel::forward_detailed, quantized_model.rs:599-621).  Up to 63
+ * rows run as passes of at most 8 rows, bitwise the verify path.  From 64
+ * rows, when every dense matrix is Q8_0, Q4_K or Q6_K and the experts sit on
+ * one GPU, the call takes the wide prefill pass instead (the reference's
+ * prefill_in_passes, src/runtime.rs:748-771: 512-row chunks; projections on
+ * the tensor cores, experts grouped by expert, the recurrence and attention
+ * in their sequential kernels): the reference's arithmetic up to f32
+ * summation order, not bitwise the 8-row passes.  Outputs are host buffers or NULL:
  * logits [rows][vocab], normalized hidden [rows][hidden], argmax [rows]
  * (ties to the last index, sampling.rs:104-112).  The pre-pass state of the
  * last pass is kept, so iq_rollback may follow. */

@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
   float zin[kMaxRowsDelta];                // gate projections of this column (fused gated norm)
 #pragma unroll
   for (int t = 0; t < kMaxRowsDelta; t++)
-    zin[t] = (a.q80 && t < rows) ? a.z[(int64_t)t * a.z_ld + vh * DV + j] : 0.f;
+    zin[t] = ((a.q80 || a.g_out) && t < rows) ? a.z[(int64_t)t * a.z_ld + vh * DV + j] : 0.f;
   // every input of the pass requested before any arithmetic
   float xin[CPT][kMaxRowsDelta];
 #pragma unroll
@@ -290,10 +290,10 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
         }
       }
     }
-    if (a.q80) os[t][j] = o;
+    if (a.q80 || a.g_out) os[t][j] = o;
     else a.out[(int64_t)t * a.out_ld + vh * DV + j] = o;
   }
-  if (!a.q80) return;
+  if (!a.q80 && !a.g_out) return;
   // gated RMSNorm of this value head (src/qwen/norm.rs:16-25): the sum of
   // squares in element order, then norm(o) * w * silu(z), z = g / (1 + e^-g);
   // then Q8_0 quantization of each 32-column block (one warp), as
@@ -318,6 +318,10 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
     const float zz = zin[t];
     const float silu = __fdiv_rn(zz, __fadd_rn(1.f, exp_ref(-zz)));
     const float g = __fmul_rn(__fmul_rn(__fdiv_rn(os[t][j], den_s[t]), wj), silu);
+    if (a.g_out) {
+      a.g_out[(int64_t)t * a.g_ld + col] = g;
+      continue;
+    }
     float amax = fabsf(g);
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
@@ -421,7 +425,8 @@ bool deltanet_supported(int dk, int dv) {
 cudaError_t deltanet_launch(const DeltaNetArgs& a, cudaStream_t st, bool pdl) {
   if (a.rows < 1 || a.rows > kMaxRowsDelta || a.rows >= kStateRing || !deltanet_supported(a.dk, a.dv) ||
       a.conv_k > 4 || a.conv_k < 1 || a.rec_stride != deltanet_rec_stride(a.dk, a.dv) ||
-      (a.q80 && (!a.z || !a.norm_w || (a.nv * a.dv) % 128)) || !a.timeout_flag ||
+      (a.q80 && (!a.z || !a.norm_w || (a.nv * a.dv) % 128)) || (a.g_out && (a.q80 || !a.z || !a.norm_w)) ||
+      !a.timeout_flag ||
       ((uintptr_t)a.layers & 7))
     return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};

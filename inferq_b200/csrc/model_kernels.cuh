@@ -45,6 +45,9 @@ struct DeltaNetArgs {
   const float* norm_w;          // [dv]
   float eps, inv_dv;
   int* timeout_flag;            // device flag set when a bounded wait gave up
+  // Or: the gated norm's f32 rows (not quantized) [rows][g_ld]; needs z,
+  // norm_w, eps, inv_dv as above.
+  float* g_out;  int g_ld;
 };
 int deltanet_rec_stride(int dk, int dv);
 bool deltanet_supported(int dk, int dv);
@@ -135,6 +138,10 @@ struct MoeRouteArgs {
   int swiglu_down;  // 1: down jobs stage silu(g)*u from gu_out themselves (kActSwiGLU)
 };
 cudaError_t moe_route_launch(const MoeRouteArgs& a, const MoeRouteStatic& s, cudaStream_t st, bool pdl);
+// Routes only (any number of rows): route_e / route_w [row][topk], the same
+// arithmetic as moe_route's per-row routing.
+cudaError_t moe_route_rows_launch(const float* logits, int ld, int rows, int E, int topk, int norm_topk,
+                                  int* route_e, float* route_w, cudaStream_t st);
 
 struct MoeActArgs {
   const float* gu; int gu_ld;  // [slot][gate ffn | up ffn]

@@ -55,25 +55,14 @@ __device__ __forceinline__ void pack_out(uint64_t& lo, uint64_t& hi, int n, int 
   else hi |= x << (16 * (n - 4));
 }
 
-// One CTA.  Warp t < rows routes row t with its probabilities in registers
-// (lane l holds experts l, l+32, ...): top-k by repeated warp arg-max, equal
-// probabilities ranking the lower expert first.  Then thread e owns experts
-// [e*per, e*per+per), finds their rank in the ascending union with warp
-// ballots, and writes the gate, up and down jobs of its resident ones.
-template <int kPerLane>  // experts per lane: ceil(E / 32) rounded up to 8, 16 or 32
-__global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRouteStatic s) {
-  pdl_wait();
-  pdl_trigger();
-  __shared__ int sel_e[kMaxRows][16];
-  __shared__ float sel_w[kMaxRows][16];
-  __shared__ unsigned used[kMaxExperts / 32];
-  __shared__ int wcount[2][8];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int E = a.experts;
-  for (int i = threadIdx.x; i < kMaxExperts / 32; i += 256) used[i] = 0;
-  __syncthreads();
-  if (warp < a.rows) {
-    const float* lg = a.logits + (int64_t)warp * a.logits_ld;
+// Top-k routing of one row by one warp (moe.rs:21-54): softmax over the E
+// logits (lane l holds experts l, l+32, ...), then top-k by repeated warp
+// arg-max with equal probabilities ranking the lower expert first; lane 0
+// leaves the experts in sel_e and their weights in sel_w (renormalized to sum
+// to one when norm_topk).
+template <int kPerLane>
+__device__ __forceinline__ void route_row_warp(const float* lg, int E, int topk, int norm_topk, int lane, int* sel_e,
+                                               float* sel_w) {
     float p[kPerLane];
     float mx = -INFINITY;
 #pragma unroll
@@ -94,7 +83,7 @@ __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRoute
     for (int o = 16; o >= 1; o >>= 1) den = __fadd_rn(den, __shfl_xor_sync(0xffffffffu, den, o));
 #pragma unroll
     for (int i = 0; i < kPerLane; i++) p[i] = lane + 32 * i < E ? __fdiv_rn(p[i], den) : -1.f;
-    for (int r = 0; r < a.topk; r++) {
+    for (int r = 0; r < topk; r++) {
       float best = -1.f;
       int bi = 0x7fffffff;
 #pragma unroll
@@ -111,17 +100,57 @@ __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRoute
 #pragma unroll
       for (int i = 0; i < kPerLane; i++)
         if (lane + 32 * i == bi) p[i] = -1.f;
-      if (lane == 0) { sel_e[warp][r] = bi; sel_w[warp][r] = best; }
+      if (lane == 0) { sel_e[r] = bi; sel_w[r] = best; }
     }
     __syncwarp();
     if (lane == 0) {
       float sum = 0.f;
-      for (int r = 0; r < a.topk; r++) sum = __fadd_rn(sum, sel_w[warp][r]);
+      for (int r = 0; r < topk; r++) sum = __fadd_rn(sum, sel_w[r]);
+      for (int r = 0; r < topk; r++) sel_w[r] = norm_topk ? __fdiv_rn(sel_w[r], sum) : sel_w[r];
+    }
+    __syncwarp();
+}
+
+// Routes of `rows` rows (warp per row): route_e / route_w [row][topk].
+template <int kPerLane>
+__global__ void __launch_bounds__(256) route_rows_kernel(const float* logits, int ld, int rows, int E, int topk,
+                                                         int norm_topk, int* route_e, float* route_w) {
+  __shared__ int se[8][16];
+  __shared__ float sw[8][16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= rows) return;
+  route_row_warp<kPerLane>(logits + (int64_t)row * ld, E, topk, norm_topk, lane, se[warp], sw[warp]);
+  if (lane < topk) {
+    route_e[row * topk + lane] = se[warp][lane];
+    route_w[row * topk + lane] = sw[warp][lane];
+  }
+}
+
+// One CTA.  Warp t < rows routes row t with its probabilities in registers
+// (lane l holds experts l, l+32, ...): top-k by repeated warp arg-max, equal
+// probabilities ranking the lower expert first.  Then thread e owns experts
+// [e*per, e*per+per), finds their rank in the ascending union with warp
+// ballots, and writes the gate, up and down jobs of its resident ones.
+template <int kPerLane>  // experts per lane: ceil(E / 32) rounded up to 8, 16 or 32
+__global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRouteStatic s) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int sel_e[kMaxRows][16];
+  __shared__ float sel_w[kMaxRows][16];
+  __shared__ unsigned used[kMaxExperts / 32];
+  __shared__ int wcount[2][8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = a.experts;
+  for (int i = threadIdx.x; i < kMaxExperts / 32; i += 256) used[i] = 0;
+  __syncthreads();
+  if (warp < a.rows) {
+    route_row_warp<kPerLane>(a.logits + (int64_t)warp * a.logits_ld, E, a.topk, a.norm_topk, lane, sel_e[warp],
+                             sel_w[warp]);
+    if (lane == 0) {
       for (int r = 0; r < a.topk; r++) {
-        const float w = a.norm_topk ? __fdiv_rn(sel_w[warp][r], sum) : sel_w[warp][r];
-        sel_w[warp][r] = w;
         a.route_expert[warp * a.topk + r] = sel_e[warp][r];
-        a.route_weight[warp * a.topk + r] = w;
+        a.route_weight[warp * a.topk + r] = sel_w[warp][r];
         atomicOr(&used[sel_e[warp][r] / 32], 1u << (sel_e[warp][r] % 32));
       }
     }
@@ -305,6 +334,16 @@ cudaError_t moe_route_launch(const MoeRouteArgs& a, const MoeRouteStatic& s, cud
   if (a.experts <= 256) return launch_pdl(moe_route_kernel<8>, dim3(1), dim3(256), 0, st, pdl, a, s);
   if (a.experts <= 512) return launch_pdl(moe_route_kernel<16>, dim3(1), dim3(256), 0, st, pdl, a, s);
   return launch_pdl(moe_route_kernel<32>, dim3(1), dim3(256), 0, st, pdl, a, s);
+}
+
+cudaError_t moe_route_rows_launch(const float* logits, int ld, int rows, int E, int topk, int norm_topk,
+                                  int* route_e, float* route_w, cudaStream_t st) {
+  if (E > kMaxExperts || topk > 16 || rows < 1) return cudaErrorInvalidValue;
+  const dim3 grid((unsigned)ceil_div(rows, 8));
+  if (E <= 256) route_rows_kernel<8><<<grid, 256, 0, st>>>(logits, ld, rows, E, topk, norm_topk, route_e, route_w);
+  else if (E <= 512) route_rows_kernel<16><<<grid, 256, 0, st>>>(logits, ld, rows, E, topk, norm_topk, route_e, route_w);
+  else route_rows_kernel<32><<<grid, 256, 0, st>>>(logits, ld, rows, E, topk, norm_topk, route_e, route_w);
+  return cudaGetLastError();
 }
 
 cudaError_t moe_act_launch(const MoeActArgs& a, cudaStream_t st, bool pdl) {

@@ -1,0 +1,528 @@
+// wide_pass.cu -- the wide prefill pass: many tokens through every layer at
+// once, the form of the reference's prefill in 512-row passes
+// (prefill_in_passes, src/runtime.rs:748-771; QuantizedModel::forward over a
+// pass's rows, src/qwen/quantized_model.rs:654-752).
+//
+// Per chunk of up to kWideRows rows and per layer:
+//   * the dense projections (DeltaNet qkv / gate / beta / alpha / out,
+//     attention q / k / v / o, the shared expert, the quantized router and the
+//     LM head) run on the tcgen05 wide products, each weight read once for
+//     the whole chunk;
+//   * the DeltaNet recurrence and the causal attention scan run in their
+//     exact sequential kernels over 8-row slices of the chunk (the state
+//     advances slice by slice, exactly as consecutive 8-row passes would);
+//   * the routed experts run as one grouped GEMV launch: after the routes
+//     are read back, every (expert, up to 8 of its rows) group becomes one
+//     job, so an expert's weights are read once per 8 of its rows; the down
+//     projection stages silu(g) * u itself; the ordered combine adds each
+//     row's routes in route order.
+// Rows therefore compute the reference's arithmetic up to f32 summation
+// order (the wide products sum a row's blocks in one chunk), not bitwise the
+// 8-row decode path; the state they leave behind is used by later passes as
+// any other.  Supported when every dense matrix has a wide product (Q8_0,
+// Q4_K, Q6_K) and the experts are resident on one GPU (wide_capable).
+#include <algorithm>
+#include <cstring>
+#include "state.h"
+
+namespace iq {
+namespace {
+
+#define TRY_IQ(x)           \
+  do {                      \
+    int _rc = (x);          \
+    if (_rc) return _rc;    \
+  } while (0)
+
+// ----------------------------------------------------------- small kernels
+__global__ void add_rows_kernel(float* __restrict__ h, const float* __restrict__ y, int64_t n4) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 a = reinterpret_cast<float4*>(h)[i];
+    const float4 b = reinterpret_cast<const float4*>(y)[i];
+    a.x = __fadd_rn(a.x, b.x);
+    a.y = __fadd_rn(a.y, b.y);
+    a.z = __fadd_rn(a.z, b.z);
+    a.w = __fadd_rn(a.w, b.w);
+    reinterpret_cast<float4*>(h)[i] = a;
+  }
+}
+
+// out[r][i] = silu(g) * u with g = in[r][i], u = in[r][F + i] (candle's
+// elementwise silu, g / (1 + exp(-g)))
+__global__ void swiglu_rows_kernel(const float* __restrict__ in, int ld, int F, int rows, float* __restrict__ out,
+                                   int out_ld) {
+  const int64_t n = (int64_t)rows * F;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = e / F, i = e % F;
+    const float g = in[r * ld + i], u = in[r * ld + F + i];
+    out[r * out_ld + i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, exp_ref(-g))), u);
+  }
+}
+
+// dst[j] = src[idx[j]] (rows of `cols` floats); idx < 0 leaves a zero row
+__global__ void gather_rows_kernel(const float* __restrict__ src, const int* __restrict__ idx, int n, int cols,
+                                   float* __restrict__ dst) {
+  const int j = blockIdx.x;
+  if (j >= n) return;
+  const int r = idx[j];
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) dst[(int64_t)j * cols + c] = r >= 0 ? src[(int64_t)r * cols + c] : 0.f;
+}
+
+// hidden[r] += (sum_q y[map[r][q]] * w[r][q], in route order) + ysh[r] *
+// sigmoid(selector logit), element by element as moe_combine does
+__global__ void wide_combine_kernel(float* __restrict__ hidden, int H, int topk, const int* __restrict__ map,
+                                    const float* __restrict__ yg, const float* __restrict__ rw,
+                                    const float* __restrict__ ysh, const float* __restrict__ lg, int lg_ld,
+                                    int experts) {
+  const int r = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= H) return;
+  const float sl = lg[(int64_t)r * lg_ld + experts];
+  const float selector = __fdiv_rn(1.f, __fadd_rn(1.f, exp_ref(-sl)));
+  float acc = 0.f;
+  for (int q = 0; q < topk; q++)
+    acc = __fadd_rn(acc, __fmul_rn(yg[(int64_t)map[r * topk + q] * H + i], rw[r * topk + q]));
+  float* h = hidden + (int64_t)r * H + i;
+  *h = __fadd_rn(*h, __fadd_rn(acc, __fmul_rn(ysh[(int64_t)r * H + i], selector)));
+}
+
+// per 8-row slice j: [3j] conv ring index, [3j+1] records pending, [3j+2] position
+__global__ void wide_ctrl_kernel(const int* __restrict__ ctrl, int* __restrict__ wc, int slices) {
+  const int j = threadIdx.x;
+  if (j >= slices) return;
+  wc[3 * j] = (ctrl[1] + 8 * j) % kStateRing;
+  wc[3 * j + 1] = j == 0 ? ctrl[6] : 8;
+  wc[3 * j + 2] = ctrl[0] + 8 * j;
+}
+
+__global__ void wide_commit_kernel(int* ctrl, int rows, int last) {
+  ctrl[0] += rows;
+  ctrl[1] = (ctrl[1] + rows) % kStateRing;
+  ctrl[6] = last;
+}
+
+constexpr int kMaxKPass = 8;
+
+bool wide_dtype(int dt) { return dt == Q8_0 || dt == Q4_K || dt == Q6_K; }
+
+// y[t*ldy + r] = row r of w (rows [0, w.rows)) . x[t*ldx ..] for n input rows
+int wide_project(iq_state* s, const Weight& w, const float* x, int ldx, int n, float* y, int ldy) {
+  cudaStream_t st = s->st;
+  DevBuf& sc = s->wide.scratch;
+  if (w.dt == Q8_0) {
+    const size_t qx = align_up((int64_t)n * w.cols * 2, 256);
+    const size_t dT = align_up((int64_t)(w.cols / 32) * wide_ldd(n) * 4, 256);
+    const size_t wx = (size_t)w.rows * w.cols * 2;
+    IQ_CUDA(sc.reserve(qx + dT + wx));
+    uint8_t* b = sc.as<uint8_t>();
+    IQ_CUDA(wide_q80_forward(w.p(), w.rows, w.cols, w.row_bytes, x, ldx, n, y, ldy, reinterpret_cast<__half*>(b),
+                             reinterpret_cast<float*>(b + qx), reinterpret_cast<__half*>(b + qx + dT), st));
+  } else if (w.dt == Q4_K) {
+    IQ_CUDA(sc.reserve(wide_q4k_scratch_bytes(w.rows, w.cols, n, nullptr, nullptr)));
+    WideQ4kScratch k;
+    wide_q4k_scratch_bytes(w.rows, w.cols, n, &k, sc.as<uint8_t>());
+    IQ_CUDA(wide_q4k_forward(w.p(), w.rows, w.cols, w.row_bytes, x, ldx, n, y, ldy, k, st));
+  } else if (w.dt == Q6_K) {
+    IQ_CUDA(sc.reserve(wide_q6k_scratch_bytes(w.rows, w.cols, n, nullptr, nullptr)));
+    WideQ6kScratch k;
+    wide_q6k_scratch_bytes(w.rows, w.cols, n, &k, sc.as<uint8_t>());
+    IQ_CUDA(wide_q6k_forward(w.p(), w.rows, w.cols, w.row_bytes, x, ldx, n, y, ldy, k, st));
+  } else {
+    set_error("wide pass: matrix dtype %d has no wide product", w.dt);
+    return IQ_EUNSUPPORTED;
+  }
+  return IQ_OK;
+}
+
+int add_rows(iq_state* s, float* h, const float* y, int64_t n) {
+  const int64_t n4 = n / 4;
+  add_rows_kernel<<<(unsigned)std::min<int64_t>(ceil_div(n4, 256), 148 * 8), 256, 0, s->st>>>(h, y, n4);
+  IQ_CUDA(cudaGetLastError());
+  return IQ_OK;
+}
+
+// RMSNorm of n rows (f32 out, no quantization), the row-prep kernel
+int norm_rows(iq_state* s, const float* x, const float* w, int n, int H, float* out, uint8_t* q8k = nullptr,
+              int q8k_stride = 0, uint8_t* q80 = nullptr, int q80_stride = 0) {
+  const iq_config& c = s->m->cfg;
+  PrepArgs a = {};
+  a.x = x;
+  a.ldx = H;
+  a.cols = H;
+  a.norm_w = w;
+  a.eps = c.rms_norm_eps;
+  a.inv_cols = (float)(1.0 / (double)H);
+  a.xn_out = out;
+  a.ldxn = H;
+  a.q8k = q8k;
+  a.q8k_stride = q8k_stride;
+  a.q80 = q80;
+  a.q80_stride = q80_stride;
+  IQ_CUDA(prep_rows(a, n, s->st, false));
+  return IQ_OK;
+}
+
+int wide_delta(iq_state* s, const Layer& L, int li, int n, int slices) {
+  const iq_config& c = s->m->cfg;
+  auto& W = s->wide;
+  const DeltaWeights& D = L.dn;
+  const int nv = c.linear_num_value_heads, vdim = nv * c.linear_value_head_dim;
+  const int conv_dim = 2 * c.linear_num_key_heads * c.linear_key_head_dim + vdim;
+  float* qkv = W.big.as<float>();
+  TRY_IQ(wide_project(s, D.qkv, W.xn.as<float>(), c.hidden_size, n, qkv, conv_dim));
+  TRY_IQ(wide_project(s, D.z, W.xn.as<float>(), c.hidden_size, n, W.z.as<float>(), vdim));
+  if (D.ba_fused) {
+    TRY_IQ(wide_project(s, D.ba, W.xn.as<float>(), c.hidden_size, n, W.ba.as<float>(), 2 * nv));
+  } else {
+    TRY_IQ(wide_project(s, D.beta, W.xn.as<float>(), c.hidden_size, n, W.ba.as<float>(), 2 * nv));
+    TRY_IQ(wide_project(s, D.alpha, W.xn.as<float>(), c.hidden_size, n, W.ba.as<float>() + nv, 2 * nv));
+  }
+  for (int j = 0; j < slices; j++) {
+    const int r0 = 8 * j, k = std::min(8, n - r0);
+    DeltaNetArgs a = {};
+    a.layers = s->dn_layers.as<DeltaNetLayer>() + li;
+    a.qkv = qkv + (int64_t)r0 * conv_dim;
+    a.qkv_ld = conv_dim;
+    a.ba = W.ba.as<float>() + (int64_t)r0 * 2 * nv;
+    a.ba_ld = 2 * nv;
+    a.out = nullptr;
+    a.out_ld = vdim;
+    a.rows = k;
+    a.nk = c.linear_num_key_heads;
+    a.nv = nv;
+    a.dk = c.linear_key_head_dim;
+    a.dv = c.linear_value_head_dim;
+    a.conv_k = c.linear_conv_kernel_dim;
+    a.tiled_heads = c.value_heads_tiled;
+    a.ba_interleaved = D.ba_fused;
+    a.rec_stride = deltanet_rec_stride(a.dk, a.dv);
+    a.timeout_flag = qmv_timeout_flag();
+    a.cur = W.ctrl.as<int>() + 3 * j;
+    a.pending = W.ctrl.as<int>() + 3 * j + 1;
+    a.z = W.z.as<float>() + (int64_t)r0 * vdim;
+    a.z_ld = vdim;
+    a.norm_w = D.norm.p();
+    a.eps = c.rms_norm_eps;
+    a.inv_dv = (float)(1.0 / c.linear_value_head_dim);
+    a.g_out = W.o.as<float>() + (int64_t)r0 * vdim;
+    a.g_ld = vdim;
+    IQ_CUDA(deltanet_launch(a, s->st, false));
+  }
+  TRY_IQ(wide_project(s, D.out, W.o.as<float>(), vdim, n, W.y.as<float>(), c.hidden_size));
+  return add_rows(s, W.hidden.as<float>(), W.y.as<float>(), (int64_t)n * c.hidden_size);
+}
+
+int wide_attention(iq_state* s, const Layer& L, int fi, int n, int slices) {
+  const iq_config& c = s->m->cfg;
+  auto& W = s->wide;
+  const AttnWeights& A = L.at;
+  const int nhd = c.num_attention_heads * c.head_dim, kvd = c.num_key_value_heads * c.head_dim;
+  TRY_IQ(wide_project(s, A.q, W.xn.as<float>(), c.hidden_size, n, W.big.as<float>(), 2 * nhd));
+  TRY_IQ(wide_project(s, A.k, W.xn.as<float>(), c.hidden_size, n, W.kp.as<float>(), kvd));
+  TRY_IQ(wide_project(s, A.v, W.xn.as<float>(), c.hidden_size, n, W.vp.as<float>(), kvd));
+  for (int j = 0; j < slices; j++) {
+    const int r0 = 8 * j, k = std::min(8, n - r0);
+    AttnArgs a = {};
+    a.qg = W.big.as<float>() + (int64_t)r0 * 2 * nhd;
+    a.qg_ld = 2 * nhd;
+    a.kp = W.kp.as<float>() + (int64_t)r0 * kvd;
+    a.kp_ld = kvd;
+    a.vp = W.vp.as<float>() + (int64_t)r0 * kvd;
+    a.vp_ld = kvd;
+    a.q_norm = A.q_norm.p();
+    a.k_norm = A.k_norm.p();
+    a.kcache = s->kc[fi].as<float>();
+    a.vcache = s->vc[fi].as<float>();
+    a.qbuf = s->qbuf.as<float>();
+    a.part = s->part.as<float>();
+    a.out = W.o.as<float>() + (int64_t)r0 * nhd;
+    a.out_ld = nhd;
+    a.rows = k;
+    a.nh = c.num_attention_heads;
+    a.nkv = c.num_key_value_heads;
+    a.hd = c.head_dim;
+    a.rotary_dim = c.rotary_dim;
+    a.theta = c.rope_theta;
+    a.eps = c.rms_norm_eps;
+    a.pos = W.ctrl.as<int>() + 3 * j + 2;
+    a.chunk_ctas = s->max_chunks;
+    IQ_CUDA(attn_prep_launch(a, s->st, false));
+    IQ_CUDA(attn_scan_launch(a, s->st, false));
+    IQ_CUDA(attn_combine_launch(a, s->st, false));
+  }
+  TRY_IQ(wide_project(s, A.o, W.o.as<float>(), nhd, n, W.y.as<float>(), c.hidden_size));
+  return add_rows(s, W.hidden.as<float>(), W.y.as<float>(), (int64_t)n * c.hidden_size);
+}
+
+int wide_moe(iq_state* s, const Layer& L, int n) {
+  const iq_config& c = s->m->cfg;
+  auto& W = s->wide;
+  const MoeWeights& M = L.moe;
+  const int H = c.hidden_size, E = c.num_experts, topk = c.num_experts_per_tok;
+  const int F = c.moe_intermediate_size, Fs = c.shared_expert_intermediate_size;
+  cudaStream_t st = s->st;
+  TRY_IQ(norm_rows(s, W.hidden.as<float>(), L.post_norm.p(), n, H, W.xn.as<float>()));
+  // router logits [n][E + 1]: column E is the shared expert's selector
+  float* lg = W.lg.as<float>();
+  if (M.router.present()) {
+    TRY_IQ(wide_project(s, M.router, W.xn.as<float>(), H, n, lg, E + 1));
+    for (int r0 = 0; r0 < n; r0 += kMaxKPass)
+      IQ_CUDA(f32_matvec(M.selector.p(), 1, H, W.xn.as<float>() + (int64_t)r0 * H, H, std::min(kMaxKPass, n - r0),
+                         lg + (int64_t)r0 * (E + 1) + E, E + 1, st, false));
+  } else {
+    for (int r0 = 0; r0 < n; r0 += kMaxKPass)
+      IQ_CUDA(f32_matvec(M.router_sel.p(), E + 1, H, W.xn.as<float>() + (int64_t)r0 * H, H,
+                         std::min(kMaxKPass, n - r0), lg + (int64_t)r0 * (E + 1), E + 1, st, false));
+  }
+  IQ_CUDA(moe_route_rows_launch(lg, E + 1, n, E, topk, c.norm_topk_prob, W.re.as<int>(), W.rw.as<float>(), st));
+  IQ_CUDA(cudaMemcpyAsync(W.h_routes, W.re.p, (size_t)n * topk * 4, cudaMemcpyDeviceToHost, st));
+  // the shared expert over every row meanwhile
+  TRY_IQ(wide_project(s, M.sh_gate, W.xn.as<float>(), H, n, W.gush.as<float>(), 2 * Fs));
+  TRY_IQ(wide_project(s, M.sh_up, W.xn.as<float>(), H, n, W.gush.as<float>() + Fs, 2 * Fs));
+  swiglu_rows_kernel<<<(unsigned)std::min<int64_t>(ceil_div((int64_t)n * Fs, 256), 148 * 8), 256, 0, st>>>(
+      W.gush.as<float>(), 2 * Fs, Fs, n, W.o.as<float>(), Fs);
+  IQ_CUDA(cudaGetLastError());
+  TRY_IQ(wide_project(s, M.sh_down, W.o.as<float>(), Fs, n, W.ysh.as<float>(), H));
+  IQ_CUDA(cudaStreamSynchronize(st));
+  // groups of at most 8 rows per expert, experts ascending, rows in order;
+  // gathered row g*8+i is member i of group g
+  std::vector<std::vector<int>> by_e(E);
+  for (int r = 0; r < n; r++)
+    for (int q = 0; q < topk; q++) by_e[W.h_routes[r * topk + q]].push_back(r * topk + q);
+  int groups = 0;
+  for (int e = 0; e < E; e++) groups += (int)ceil_div((int64_t)by_e[e].size(), 8);
+  const int ng_rows = 8 * groups;
+  IQ_CHECK(ng_rows < 32768, IQ_EUNSUPPORTED, "wide pass: %d expert slots exceed the GEMV's row index", ng_rows);
+  const bool q80 = M.gate.dt == Q8_0;
+  const int arb = (int)(q80 ? act_row_bytes_q80(H) : act_row_bytes_q8k(H));
+  const int gu_ld = 2 * F;
+  IQ_CUDA(W.xg.reserve((size_t)ng_rows * H * 4));
+  IQ_CUDA(W.actg.reserve((size_t)ng_rows * arb));
+  IQ_CUDA(W.gu.reserve((size_t)ng_rows * gu_ld * 4));
+  IQ_CUDA(W.yg.reserve((size_t)ng_rows * H * 4));
+  IQ_CUDA(W.jobs.reserve((size_t)3 * groups * sizeof(QmvJob)));
+  IQ_CUDA(W.map.reserve(((size_t)n * topk + ng_rows) * 4));
+  std::vector<int> gather((size_t)ng_rows, -1);  // source row per gathered slot (-1 padding)
+  W.map_host.assign((size_t)n * topk, 0);
+  const int ks_gate = qmv_ksplit(M.gate.dt, F, H, true), ks_down = qmv_ksplit(M.down.dt, H, F, true);
+  const int tg = (int)ceil_div(F, qmv_rows_per_cta(ks_gate)), td = (int)ceil_div(H, qmv_rows_per_cta(ks_down));
+  std::vector<QmvJob>& jt = W.job_table;
+  jt.clear();
+  std::vector<QmvJob> down;
+  int gt = 0, dtiles = 0, g = 0;
+  for (int e = 0; e < E; e++) {
+    const std::vector<int>& sl = by_e[e];
+    for (size_t g0 = 0; g0 < sl.size(); g0 += 8, g++) {
+      const int ng = (int)std::min<size_t>(8, sl.size() - g0);
+      const int base = 8 * g;
+      for (int i = 0; i < ng; i++) {
+        gather[base + i] = sl[g0 + i] / topk;
+        W.map_host[sl[g0 + i]] = base + i;
+      }
+      QmvJob j;
+      memset(&j, 0, sizeof j);
+      j.dtype = M.gate.dt;
+      j.rows = F;
+      j.cols = H;
+      j.ksplit = ks_gate;
+      j.n = ng;
+      j.act_nrows = ng;
+      j.epi = kEpiStore;
+      j.w_row_bytes = M.gate.row_bytes;
+      j.act = W.actg.as<uint8_t>() + (int64_t)base * arb;
+      j.act_row_bytes = arb;
+      j.out_ld = gu_ld;
+      for (int i = 0; i < 8; i++) {
+        j.rowmap[i] = (uint8_t)(i < ng ? i : 0);
+        j.outrow[i] = (int16_t)(base + i);
+      }
+      j.row_base = e * F;
+      j.w = M.gate.p() + (int64_t)e * F * M.gate.row_bytes;
+      j.tmap = M.gate.tmap();
+      j.tmap_tail = M.gate.tmap_tail();
+      j.out = W.gu.as<float>();
+      j.tile0 = gt;
+      jt.push_back(j);
+      gt += tg;
+      j.w = M.up.p() + (int64_t)e * F * M.up.row_bytes;
+      j.tmap = M.up.tmap();
+      j.tmap_tail = M.up.tmap_tail();
+      j.out = W.gu.as<float>() + F;
+      j.tile0 = gt;
+      jt.push_back(j);
+      gt += tg;
+      QmvJob d;
+      memset(&d, 0, sizeof d);
+      d.dtype = M.down.dt;
+      d.rows = H;
+      d.cols = F;
+      d.ksplit = ks_down;
+      d.n = ng;
+      d.act_nrows = ng;
+      d.epi = kEpiStore;
+      d.w_row_bytes = M.down.row_bytes;
+      d.act = reinterpret_cast<const uint8_t*>(W.gu.as<float>() + (int64_t)base * gu_ld);
+      d.act_row_bytes = gu_ld * 4;
+      d.act_mode = kActSwiGLU;
+      d.out = W.yg.as<float>();
+      d.out_ld = H;
+      for (int i = 0; i < 8; i++) {
+        d.rowmap[i] = (uint8_t)(i < ng ? i : 0);
+        d.outrow[i] = (int16_t)(base + i);
+      }
+      d.row_base = e * H;
+      d.w = M.down.p() + (int64_t)e * H * M.down.row_bytes;
+      d.tmap = M.down.tmap();
+      d.tmap_tail = M.down.tmap_tail();
+      d.tile0 = dtiles;
+      down.push_back(d);
+      dtiles += td;
+    }
+  }
+  const int njobs = (int)jt.size();
+  for (auto& d : down) jt.push_back(d);
+  int* d_map = W.map.as<int>();
+  int* d_gather = d_map + (size_t)n * topk;
+  IQ_CUDA(cudaMemcpyAsync(W.jobs.p, jt.data(), jt.size() * sizeof(QmvJob), cudaMemcpyHostToDevice, st));
+  IQ_CUDA(cudaMemcpyAsync(d_map, W.map_host.data(), (size_t)n * topk * 4, cudaMemcpyHostToDevice, st));
+  IQ_CUDA(cudaMemcpyAsync(d_gather, gather.data(), gather.size() * 4, cudaMemcpyHostToDevice, st));
+  // (host vectors stay alive until the stream synchronizes at the end of the chunk)
+  gather_rows_kernel<<<ng_rows, 256, 0, st>>>(W.xn.as<float>(), d_gather, ng_rows, H, W.xg.as<float>());
+  IQ_CUDA(cudaGetLastError());
+  PrepArgs pa = {};
+  pa.x = W.xg.as<float>();
+  pa.ldx = H;
+  pa.cols = H;
+  pa.inv_cols = (float)(1.0 / (double)H);
+  if (q80) { pa.q80 = W.actg.as<uint8_t>(); pa.q80_stride = arb; }
+  else { pa.q8k = W.actg.as<uint8_t>(); pa.q8k_stride = arb; }
+  IQ_CUDA(prep_rows(pa, ng_rows, st, false));
+  IQ_CUDA(qmv_launch(W.jobs.as<QmvJob>(), njobs, nullptr, gt, 8 * arb, st, false));
+  const int mid = (int)std::max(act_row_bytes_q8k(F), act_row_bytes_q80(F));
+  IQ_CUDA(qmv_launch(W.jobs.as<QmvJob>() + njobs, (int)down.size(), nullptr, dtiles, 8 * mid, st, false));
+  const dim3 grid((unsigned)ceil_div(H, 256), (unsigned)n);
+  wide_combine_kernel<<<grid, 256, 0, st>>>(W.hidden.as<float>(), H, topk, d_map, W.yg.as<float>(), W.rw.as<float>(),
+                                            W.ysh.as<float>(), lg, E + 1, E);
+  IQ_CUDA(cudaGetLastError());
+  return IQ_OK;
+}
+
+int alloc_wide(iq_state* s, int n) {
+  const iq_config& c = s->m->cfg;
+  auto& W = s->wide;
+  const int64_t H = c.hidden_size, vdim = (int64_t)c.linear_num_value_heads * c.linear_value_head_dim;
+  const int64_t conv_dim = 2 * (int64_t)c.linear_num_key_heads * c.linear_key_head_dim + vdim;
+  const int64_t nhd = (int64_t)c.num_attention_heads * c.head_dim, kvd = (int64_t)c.num_key_value_heads * c.head_dim;
+  const int64_t E = c.num_experts, topk = c.num_experts_per_tok, Fs = c.shared_expert_intermediate_size;
+  IQ_CUDA(W.hidden.reserve(n * H * 4));
+  IQ_CUDA(W.xn.reserve(n * H * 4));
+  IQ_CUDA(W.big.reserve(n * std::max(conv_dim, 2 * nhd) * 4));
+  IQ_CUDA(W.z.reserve(n * std::max<int64_t>(vdim, 1) * 4));
+  IQ_CUDA(W.ba.reserve(n * 2 * std::max(c.linear_num_value_heads, 1) * 4));
+  IQ_CUDA(W.o.reserve(n * std::max({vdim, nhd, Fs}) * 4));
+  IQ_CUDA(W.y.reserve(n * H * 4));
+  IQ_CUDA(W.kp.reserve(n * kvd * 4));
+  IQ_CUDA(W.vp.reserve(n * kvd * 4));
+  IQ_CUDA(W.tokens.reserve(n * 4));
+  IQ_CUDA(W.ctrl.reserve(3 * ceil_div(n, 8) * 4));
+  IQ_CUDA(W.lg.reserve(n * (E + 1) * 4));
+  IQ_CUDA(W.re.reserve(n * topk * 4));
+  IQ_CUDA(W.rw.reserve(n * topk * 4));
+  IQ_CUDA(W.ysh.reserve(n * H * 4));
+  IQ_CUDA(W.gush.reserve(n * 2 * Fs * 4));
+  IQ_CUDA(W.argres.reserve(8 * 4));
+  if (!W.h_routes) IQ_CUDA(cudaMallocHost(&W.h_routes, (size_t)kWideRows * topk * 4));
+  return IQ_OK;
+}
+
+// One chunk of n <= kWideRows rows.
+int wide_chunk(iq_state* s, const uint32_t* tokens, int n, float* logits, float* hidden, int32_t* argmax, int row0) {
+  iq_model* m = s->m;
+  const iq_config& c = m->cfg;
+  auto& W = s->wide;
+  cudaStream_t st = s->st;
+  const int H = c.hidden_size, V = c.vocab_size;
+  const int slices = (int)ceil_div(n, 8);
+  std::vector<int32_t> tk(tokens, tokens + n);
+  IQ_CUDA(cudaMemcpyAsync(W.tokens.p, tk.data(), (size_t)n * 4, cudaMemcpyHostToDevice, st));
+  wide_ctrl_kernel<<<1, 256, 0, st>>>(s->ctrl.as<int>(), W.ctrl.as<int>(), slices);
+  IQ_CUDA(cudaGetLastError());
+  IQ_CUDA(embed_launch(m->embed.dt, m->embed.p(), m->embed.row_bytes, H, W.tokens.as<int32_t>(), n,
+                       W.hidden.as<float>(), H, st, false));
+  int li = 0, fi = 0;
+  for (int l = 0; l < c.num_hidden_layers; l++) {
+    const Layer& L = m->layers[l];
+    TRY_IQ(norm_rows(s, W.hidden.as<float>(), L.attn_norm.p(), n, H, W.xn.as<float>()));
+    if (L.type == kLinear) TRY_IQ(wide_delta(s, L, li++, n, slices));
+    else TRY_IQ(wide_attention(s, L, fi++, n, slices));
+    TRY_IQ(wide_moe(s, L, n));
+  }
+  TRY_IQ(norm_rows(s, W.hidden.as<float>(), m->out_norm.p(), n, H, W.xn.as<float>()));
+  if (hidden)
+    IQ_CUDA(cudaMemcpyAsync(hidden + (int64_t)row0 * H, W.xn.p, (size_t)n * H * 4, cudaMemcpyDeviceToHost, st));
+  if (logits || argmax) {
+    IQ_CUDA(W.logits.reserve((size_t)n * V * 4));
+    TRY_IQ(wide_project(s, m->lm_head, W.xn.as<float>(), H, n, W.logits.as<float>(), V));
+    if (logits)
+      IQ_CUDA(cudaMemcpyAsync(logits + (int64_t)row0 * V, W.logits.p, (size_t)n * V * 4, cudaMemcpyDeviceToHost, st));
+    if (argmax) {
+      for (int r0 = 0; r0 < n; r0 += 8) {
+        HeadArgs h = {};
+        h.logits = W.logits.as<float>() + (int64_t)r0 * V;
+        h.logits_ld = V;
+        h.rows = std::min(8, n - r0);
+        h.vocab = V;
+        h.part_val = s->pval.as<float>();
+        h.part_idx = s->pidx.as<int>();
+        h.nparts = 128;
+        h.argmax = s->argmax.as<int>();
+        h.tokens = s->tokens.as<int32_t>();
+        h.verify = 0;
+        h.result = W.argres.as<int>();
+        IQ_CUDA(argmax_launch(h, st, false));
+        IQ_CUDA(accept_launch(h, st, false));
+        IQ_CUDA(cudaMemcpyAsync(argmax + row0 + r0, s->argmax.p, (size_t)h.rows * 4, cudaMemcpyDeviceToHost, st));
+      }
+    }
+  }
+  const int last = n - 8 * (slices - 1);
+  wide_commit_kernel<<<1, 1, 0, st>>>(s->ctrl.as<int>(), n, last);
+  IQ_CUDA(cudaGetLastError());
+  IQ_CUDA(cudaStreamSynchronize(st));
+  s->position += n;
+  s->last_rows = last;
+  return IQ_OK;
+}
+
+}  // namespace
+
+bool wide_capable(const iq_model* m) {
+  if (m->ep_world > 1) return false;
+  const iq_config& c = m->cfg;
+  if (c.num_hidden_layers < 1 || c.num_experts_per_tok > 16 || c.hidden_size % 256) return false;
+  auto ok = [](const Weight& w) { return wide_dtype(w.dt); };
+  if (!ok(m->lm_head)) return false;
+  for (const Layer& L : m->layers) {
+    if (L.type == kLinear) {
+      const DeltaWeights& D = L.dn;
+      if (!ok(D.qkv) || !ok(D.z) || !ok(D.out) || (D.ba_fused ? !ok(D.ba) : (!ok(D.beta) || !ok(D.alpha)))) return false;
+    } else {
+      const AttnWeights& A = L.at;
+      if (!ok(A.q) || !ok(A.k) || !ok(A.v) || !ok(A.o)) return false;
+    }
+    const MoeWeights& M = L.moe;
+    if (!ok(M.sh_gate) || !ok(M.sh_up) || !ok(M.sh_down)) return false;
+    if (M.router.present() && !ok(M.router)) return false;
+    if (M.gate.dt == F32 || M.down.dt == F32) return false;
+  }
+  return true;
+}
+
+int wide_forward(iq_state* s, const uint32_t* tokens, int rows, float* logits, float* hidden, int32_t* argmax) {
+  TRY_IQ(alloc_wide(s, std::min(rows, kWideRows)));
+  for (int r0 = 0; r0 < rows; r0 += kWideRows)
+    TRY_IQ(wide_chunk(s, tokens + r0, std::min(kWideRows, rows - r0), logits, hidden, argmax, r0));
+  return IQ_OK;
+}
+
+}  // namespace iq

@@ -118,8 +118,9 @@ static const float* getvec(const or_tensor* t, int n, const char* name) {
 }
 
 /* Accumulation order of every projection: 0 = the reference's AVX2 lane
- * order (default), 1 = the device's block-chunk order (a diagnostic that
- * isolates f32-order effects from everything else). */
+ * order (default), 1 = the device's block-chunk order of the 8-row passes,
+ * 2 = the device order of the wide prefill pass (diagnostics that isolate
+ * f32-order effects from everything else). */
 static int g_order = 0;
 void or_set_gemv_order(int order) { g_order = order; }
 
@@ -134,15 +135,23 @@ static int device_ksplit(int dt, int64_t rows, int64_t cols, int expert) {
 }
 
 /* y[rows] = W x  (one input row) */
+/* The chunk count of the device order for a matrix: `expert` 0 dense, 1 a
+ * routed expert, 2 the shared expert.  Order 2 is the wide prefill pass's:
+ * dense and shared matrices in one chunk (the tensor-core products), routed
+ * experts as the GEMV splits them. */
+static int order_ksplit(int dt, int64_t n, int64_t cols, int expert) {
+    if (g_order == 2) return expert == 1 ? device_ksplit(dt, n, cols, 1) : 1;
+    return g_order ? device_ksplit(dt, n, cols, expert != 0) : 1;
+}
 static void matvec_n(const mat_t* m, const uint8_t* p, int64_t n, const float* x, float* y, int expert) {
-    or_qmatvec(m->dt, p, n, m->cols, x, 1, y, g_order, g_order ? device_ksplit(m->dt, n, m->cols, expert) : 1);
+    or_qmatvec(m->dt, p, n, m->cols, x, 1, y, g_order ? 1 : 0, order_ksplit(m->dt, n, m->cols, expert));
 }
 static void matvec(const mat_t* m, const float* x, float* y) { matvec_n(m, m->p, m->rows, x, y, 0); }
 /* R input rows x [R][cols] -> y [R][n] (each weight row read once for all R,
  * the reference's multi-row pass; every output is computed exactly as for a
  * single row) */
 static void matvec_nk(const mat_t* m, const uint8_t* p, int64_t n, const float* x, int R, float* y, int expert) {
-    or_qmatvec(m->dt, p, n, m->cols, x, R, y, g_order, g_order ? device_ksplit(m->dt, n, m->cols, expert) : 1);
+    or_qmatvec(m->dt, p, n, m->cols, x, R, y, g_order ? 1 : 0, order_ksplit(m->dt, n, m->cols, expert));
 }
 static void matvec_k(const mat_t* m, const float* x, int R, float* y) { matvec_nk(m, m->p, m->rows, x, R, y, 0); }
 /* an expert-class matrix (routed or shared expert) */
@@ -701,10 +710,10 @@ static void moe_rows(const or_model* m, const layer_t* L, const float* x, int R,
             for (int i = 0; i < H; i++) o[i] += ys[i] * w;
         }
     }
-    matvec_nk(&L->sh_gate, L->sh_gate.p, Fs, x, R, g, 1);
-    matvec_nk(&L->sh_up, L->sh_up.p, Fs, x, R, u, 1);
+    matvec_nk(&L->sh_gate, L->sh_gate.p, Fs, x, R, g, 2);
+    matvec_nk(&L->sh_up, L->sh_up.p, Fs, x, R, u, 2);
     for (int i = 0; i < R * Fs; i++) g[i] = (g[i] / (1.f + expf(-g[i]))) * u[i];
-    matvec_nk(&L->sh_down, L->sh_down.p, H, g, R, y, 1);
+    matvec_nk(&L->sh_down, L->sh_down.p, H, g, R, y, 2);
     for (int r = 0; r < R; r++) {
         const float* xr = x + (int64_t)r * H;
         float sel = 0.f;
