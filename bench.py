@@ -217,6 +217,85 @@ def wide_timing(rows=8192, cols=2048, n=512, reps=10):
     return out
 
 
+WIDE_WIDTHS = (64, 256, 512)
+WIDE_CTX = 2048
+
+
+def wide_flops_per_row(cfg) -> tuple[float, float]:
+    """Multiply-add FLOPs per row of one pass: (the dense projections, shared
+    experts and LM head, which the wide pass runs on the tensor cores; the
+    routed experts' top-k SwiGLU FFNs, which it runs as grouped GEMVs)."""
+    H = cfg.hidden_size
+    nk, nv, dk, dv = (cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_key_head_dim,
+                      cfg.linear_value_head_dim)
+    conv_dim, vdim = 2 * nk * dk + nv * dv, nv * dv
+    nh, nkv, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+    dn = (conv_dim + vdim + 2 * nv) * H + H * vdim
+    att = (2 * nh * hd + 2 * nkv * hd) * H + H * nh * hd
+    shared = 3 * cfg.shared_expert_intermediate_size * H
+    dense = sum(att if cfg.layer_is_full(l) else dn for l in range(cfg.num_hidden_layers))
+    dense += cfg.num_hidden_layers * shared + cfg.vocab_size * H
+    routed = cfg.num_hidden_layers * cfg.num_experts_per_tok * 3 * cfg.moe_intermediate_size * H
+    return 2.0 * dense, 2.0 * routed
+
+
+def wide_prefill(steps, warmup, widths=WIDE_WIDTHS, ctx=WIDE_CTX):
+    """The wide verify/prefill pass on the 35B shapes with Q8_0 weights (full
+    40 layers): one step = one iq_forward of `width` seeded uniform-random
+    token ids at position 2048 (the state image of a 2048-token prefill is
+    restored before every step, outside the timed region), timed with CUDA
+    events on the state's stream, and on the host clock through the C ABI
+    (token ids in, per-row argmax out)."""
+    import torch
+    from inferq_b200 import quants as Q
+    from inferq_b200 import synth
+    from inferq_b200.model import Model, State
+    cfg = synth.qwen36_35b()
+    cfg.name = "qwen3.6-35b-a3b-shapes-q8_0"
+    cfg.dtypes = {"default": Q.Q8_0, "router": Q.F32}
+    t0 = time.perf_counter()
+    model = Model(cfg, synth.generate(cfg, seed=0, device="cuda"))
+    build_s = time.perf_counter() - t0
+    rng = np.random.default_rng(2048)
+    st = State(model, ctx + max(widths) + 16)
+    t0 = time.perf_counter()
+    st.forward(rng.integers(0, cfg.vocab_size, ctx))
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    img = st.export_image()
+    stream = torch.cuda.ExternalStream(st.stream())
+    dense, routed = wide_flops_per_row(cfg)
+    peaks = ROOT / "MEASURED_PEAKS.json"
+    bf16 = json.loads(peaks.read_text()).get("bf16_tflops") if peaks.exists() else 1590.0
+    out = {"workload": f"{cfg.name}, full {cfg.num_hidden_layers} layers, rows of seeded uniform-random token ids "
+                       f"at context {ctx} (state image restored before each step)",
+           "weights_gb": model.weight_bytes() / 1e9, "model_build_s": build_s,
+           "prefill_2048_tok_s": ctx / prefill_s, "dense_flops_per_row": dense, "routed_flops_per_row": routed}
+    for w in widths:
+        toks = rng.integers(0, cfg.vocab_size, w)
+        dev, host = [], []
+        for i in range(warmup + steps):
+            st.import_image(img)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
+            e0.record(stream)
+            st.forward(toks)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            if i >= warmup:
+                host.append(time.perf_counter() - t0)
+                dev.append(e0.elapsed_time(e1) / 1e3)
+        d, h = float(np.mean(dev)), float(np.mean(host))
+        assert st.position == ctx + w
+        out[str(w)] = {"tok_s": w / d, "e2e_tok_s": w / h, "pass_us": d * 1e6,
+                       "dense_tflops": dense * w / d / 1e12, "dense_frac_of_bf16_peak": dense * w / d / 1e12 / bf16,
+                       "all_tflops": (dense + routed) * w / d / 1e12}
+    del st, model
+    torch.cuda.empty_cache()
+    return out
+
+
 def greedy_continuation(model, prompt, n, margins=False):
     """Plain greedy decoding of n tokens after the prompt (one row per pass);
     with margins, also each emitted position's top-2 logit margin."""
@@ -459,7 +538,7 @@ def main():
         committed_all = committed
     # ---- verify sweep (context 1024) and the GEMV stage profile at k=4
     sweep, union, prof, pos = verify_sweep(model, cfg, args.sweep_steps, max(2, args.warmup), barrier)
-    ngram = wide = None
+    ngram = wide = prefill = None
     if not ep_mode or world == 1:
         if rank == 0:
             try:
@@ -470,6 +549,10 @@ def main():
                 wide = wide_timing()
             except Exception as e:
                 wide = {"failed": str(e)}
+            try:
+                prefill = wide_prefill(max(3, args.steps // 4), 3)
+            except Exception as e:
+                prefill = {"failed": str(e)}
     if rank != 0:
         return
     per_seq = 1 if ep_mode else world
@@ -518,7 +601,7 @@ def main():
                    "l2": "weights (23.6 GB) exceed L2; no flush needed",
                    "parallelism": f"ep{world} (experts split, NCCL sum of routed outputs per MoE layer)"
                    if ep_mode else f"replicas x{world}",
-                   "ngram": ngram, "wide": wide},
+                   "ngram": ngram, "wide": wide, "wide_prefill": prefill},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak if achieved else None, "traffic": traffic, "peak_kind": peak_kind,
                      "traffic_scope": "DRAM bytes of the pass's GEMV launches: the ncu ratio of a 4-layer capture "

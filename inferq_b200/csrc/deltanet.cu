@@ -13,12 +13,14 @@
 // walks the dk key rows of S[:, j] in order, with the column in registers.
 //
 // Grid: one CTA per value head, dv/32 warps; warp w owns columns
-// 32w .. 32w+31, and the head's dk x dv state sits in shared memory (column j
-// is thread j's; rolled loops keep the code small enough for the
-// instruction cache).  The conv, the norms and beta/g of all the pass's rows are
-// computed first by the whole CTA (they do not depend on the state); then
-// each warp runs the rows: the o-sum of row t and the pred-sum of row t+1
-// walk the key rows in the same loop (two independent chains).
+// 32w .. 32w+31, and column j of the head's dk x dv state lives in thread j's
+// registers (the key-row walks are fully unrolled).  Rows run in blocks of
+// up to 8: the conv, the norms and beta/g of a block's rows are computed
+// first by the whole CTA (they do not depend on the state); then each thread
+// runs the block's rows: the o-sum of row t and the decay and pred-sum of
+// row t+1 walk the key rows in the same loop (two independent chains).  A
+// pass may hold any number of rows (the wide prefill hands a whole chunk to
+// one launch); only its final block is kept for rollback.
 //
 // Rollback without state copies: the recurrent state is one buffer per layer
 // (the state before the last pass) plus, per row of the last pass, an update
@@ -47,42 +49,13 @@ __device__ __forceinline__ float softplus_ref(float v) {
 }
 
 // DK key rows, DV value columns per head (32 * warps), conv width K.
-__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ void bar_init(uint64_t* b) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(b)) : "memory");
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ void bar_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(b)), "r"(bytes) : "memory");
-}
-// Bulk copy of `bytes` (a multiple of 16, 16-byte aligned ends) from this
-// GPU's global memory into this CTA's shared memory, completing on `b`.
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, int bytes, uint64_t* b) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_addr(dst)),
-               "l"(src), "r"(bytes), "r"(smem_addr(b))
-               : "memory");
-}
-// Bounded wait for phase `parity` of `b`; false if it did not complete.
-__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, int limit = 1 << 20) {
-  for (int i = 0; i < limit; i++) {
-    uint32_t ok;
-    asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-        : "=r"(ok)
-        : "r"(smem_addr(b)), "r"(parity)
-        : "memory");
-    if (ok) return true;
-  }
-  return false;
-}
-
 template <int DK, int DV, int K>
 __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
   constexpr int NT = DV;               // threads
   constexpr int NCH = 2 * DK + DV;     // conv channels of this head: q | k | v
   constexpr int CPT = (NCH + NT - 1) / NT;
   constexpr int QS = DK + 4;           // padded row of q/k in shared memory
+  constexpr int B = kMaxRowsDelta;     // rows per block
   const DeltaNetLayer& L = *a.layers;
   const int vh = blockIdx.x;
   const int ratio = a.nv / a.nk;
@@ -93,42 +66,30 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
   const int key_dim = a.nk * DK;
   const int rows = a.rows;
   const int rec_stride = a.rec_stride;
-  float* rec_head = L.rec_log + (int64_t)vh * kMaxRowsDelta * rec_stride;  // [row][k DK | delta DV | decay]
+  float* rec_head = L.rec_log + (int64_t)vh * B * rec_stride;  // [row][k DK | delta DV | decay]
   float* base = L.rec_state + (int64_t)vh * DK * DV + j;
 
   // ---- before the dependency wait: state column, replay of the committed
   // rows of the previous pass, conv weights and history (none of them is
   // written by the kernels this pass runs before this one)
-  // the head's state, one column per thread, in shared memory (rolled loops
-  // keep the kernel's code small; the column accesses are conflict-free),
-  // brought in with the update records to replay by one bulk copy each
-  extern __shared__ __align__(128) float Ssm[];  // [DK][DV], then [kMaxRowsDelta][rec_stride]
-  float* rec_s = Ssm + DK * DV;
-  float* Sc = Ssm + j;
-  __shared__ __align__(8) uint64_t bar;
+  extern __shared__ __align__(16) float rec_s[];  // [B][rec_stride]
   const int pend = *a.pending;
-  if (tid == 0) {
-    bar_init(&bar);
-    bar_expect_tx(&bar, (uint32_t)(DK * DV * 4 + pend * rec_stride * 4));
-    bulk_load(Ssm, L.rec_state + (int64_t)vh * DK * DV, DK * DV * 4, &bar);
-    if (pend > 0) bulk_load(rec_s, rec_head, pend * rec_stride * 4, &bar);
-  }
-  __syncthreads();  // the barrier is initialized before anyone waits on it
-  if (!bar_wait(&bar, 0)) {
-    // (not expected) the copies did not land: report, let them finish, stop
-    if (tid == 0) atomicExch(a.timeout_flag, 1);
-    bar_wait(&bar, 0, 1 << 22);
-    return;
-  }
+  float S[DK];  // column j of the head's state, key rows in order
+#pragma unroll
+  for (int i = 0; i < DK; i++) S[i] = base[(int64_t)i * DV];
+  for (int e = tid; e < pend * rec_stride; e += NT) rec_s[e] = rec_head[e];
+  __syncthreads();
   for (int r = 0; r < pend; r++) {
     const float* rc = rec_s + r * rec_stride;
     const float decay = rc[DK + DV], delta = rc[DK + j];
-#pragma unroll 4
-    for (int i = 0; i < DK; i++) Sc[i * DV] = __fadd_rn(__fmul_rn(Sc[i * DV], decay), __fmul_rn(rc[i], delta));
-  }
-  if (pend > 0) {
-#pragma unroll 8
-    for (int i = 0; i < DK; i++) base[(int64_t)i * DV] = Sc[i * DV];
+    const float4* k4 = reinterpret_cast<const float4*>(rc);
+#pragma unroll
+    for (int i4 = 0; i4 < DK / 4; i4++) {
+      const float4 kv = k4[i4];
+      const float kk[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int e = 0; e < 4; e++) S[4 * i4 + e] = __fadd_rn(__fmul_rn(S[4 * i4 + e], decay), __fmul_rn(kk[e], delta));
+    }
   }
   const int cur = *a.cur;
   auto chan = [&](int c) {
@@ -155,181 +116,218 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
   pdl_wait();
   pdl_trigger();
 
-  __shared__ __align__(16) float qk[kMaxRowsDelta][2][QS];  // conv outputs, then normalized q and k
-  __shared__ float vs[kMaxRowsDelta][DV];
-  __shared__ float beta_s[kMaxRowsDelta], decay_s[kMaxRowsDelta];
-  __shared__ float os[kMaxRowsDelta][DV];  // recurrent outputs (fused gated norm)
-  float zin[kMaxRowsDelta];                // gate projections of this column (fused gated norm)
-#pragma unroll
-  for (int t = 0; t < kMaxRowsDelta; t++)
-    zin[t] = ((a.q80 || a.g_out) && t < rows) ? a.z[(int64_t)t * a.z_ld + vh * DV + j] : 0.f;
-  // every input of the pass requested before any arithmetic
-  float xin[CPT][kMaxRowsDelta];
-#pragma unroll
-  for (int u = 0; u < CPT; u++) {
-    const int c = tid + NT * u;
-    const bool own = c < NCH;
-    const int g = own ? chan(c) : 0;
-#pragma unroll
-    for (int t = 0; t < kMaxRowsDelta; t++) xin[u][t] = (own && t < rows) ? a.qkv[(int64_t)t * a.qkv_ld + g] : 0.f;
-  }
-  float bin = 0.f, ain = 0.f;
-  if (tid < rows) {
-    int bi = vh, ai = a.nv + vh;
-    if (a.ba_interleaved) {
-      bi = kh * 2 * ratio + rep;
-      ai = kh * 2 * ratio + ratio + rep;
-    }
-    bin = a.ba[(int64_t)tid * a.ba_ld + bi];
-    ain = a.ba[(int64_t)tid * a.ba_ld + ai];
-  }
-  // causal depthwise conv + SiLU per channel and row (quantized_deltanet.rs:733-759)
+  __shared__ __align__(16) float qk[B][2][QS];  // conv outputs, then normalized q and k
+  __shared__ float vs[B][DV];
+  __shared__ float beta_s[B], decay_s[B];
+  __shared__ __align__(16) float os[B][DV];  // recurrent outputs (fused gated norm)
+  __shared__ float nscale[B][2];
+  __shared__ float den_s[B];
   const bool qk_writer = rep == 0;
-#pragma unroll
-  for (int u = 0; u < CPT; u++) {
-    const int c = tid + NT * u;
-    if (c >= NCH) continue;
-#pragma unroll
-    for (int t = 0; t < kMaxRowsDelta; t++) {
-      if (t >= rows) break;
-      const float x = xin[u][t];
-      float sum = __fmul_rn(cw[u][K - 1], x);
-#pragma unroll
-      for (int tp = 0; tp < K - 1; tp++) sum = __fadd_rn(sum, __fmul_rn(cw[u][tp], hist[u][tp]));
-      const float y = __fmul_rn(sum, sigmoid_ref(sum));
-      if (c < 2 * DK) qk[t][c / DK][c % DK] = y;
-      else vs[t][c - 2 * DK] = y;
-#pragma unroll
-      for (int tp = 0; tp + 1 < K - 1; tp++) hist[u][tp] = hist[u][tp + 1];
-      if (K > 1) hist[u][K - 2] = x;
-      if (c >= 2 * DK || qk_writer) {
-        float* co = L.conv_state[(cur + 1 + t) % kStateRing] + (int64_t)chan(c) * (K - 1);
-#pragma unroll
-        for (int tp = 0; tp < K - 1; tp++) co[tp] = hist[u][tp];
-      }
-    }
-  }
-  if (tid < rows) {
-    beta_s[tid] = sigmoid_ref(bin);
-    decay_s[tid] = exp_ref(__fmul_rn(ssm_a, softplus_ref(__fadd_rn(ain, dt_bias))));
-  }
-  __syncthreads();
-  // L2 norms: x * (sum x^2 + 1e-6)^-1/2 with the sum in element order
-  // (quantized_deltanet.rs:724-731); one thread per (row, q|k)
-  __shared__ float nscale[kMaxRowsDelta][2];
-  if (tid < 2 * rows) {
-    const float* v = qk[tid >> 1][tid & 1];
-    float ss = 0.f;
-#pragma unroll 8
-    for (int i = 0; i < DK; i++) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
-    nscale[tid >> 1][tid & 1] = __fdiv_rn(1.f, sqrtf(__fadd_rn(ss, 1e-6f)));
-  }
-  __syncthreads();
-  for (int e = tid; e < rows * 2 * DK; e += NT) {
-    const int t = e / (2 * DK), w = (e / DK) & 1, i = e % DK;
-    qk[t][w][i] = __fmul_rn(qk[t][w][i], nscale[t][w]);
-  }
-  __syncthreads();
-  // update records of this pass: normalized k and decay (delta below)
-  for (int e = tid; e < rows * DK; e += NT) rec_head[(int64_t)(e / DK) * rec_stride + e % DK] = qk[e / DK][1][e % DK];
-  if (tid < rows) rec_head[(int64_t)tid * rec_stride + DK + DV] = decay_s[tid];
-
-  // ---- the recurrence, one value column per thread
+  const bool gated = a.q80 || a.g_out;
   const float qscale = __fdiv_rn(1.f, sqrtf((float)DK));
-  float pred = 0.f;
-  {
-    const float decay = decay_s[0];
-    const float4* k4 = reinterpret_cast<const float4*>(qk[0][1]);
-#pragma unroll 2
-    for (int i4 = 0; i4 < DK / 4; i4++) {
-      const float4 kv = k4[i4];
-      const float kk[4] = {kv.x, kv.y, kv.z, kv.w};
+  // The final block of up to B rows keeps update records and conv slots so
+  // that the pass can be rolled back inside it; the rows before it (a wide
+  // pass's prefix) advance the state directly.  Conv slots: the history
+  // after the prefix in slot0, after final row t in slot0 + 1 + t; slot0 is
+  // cur + 1 when there is a prefix (never cur itself, which other heads may
+  // still be reading: the ring holds cur, slot0 and B rows).
+  const int last = rows > 0 ? (rows - 1) % B + 1 : 0;
+  const int pre = rows - last;
+  const int slot0 = pre > 0 ? (cur + 1) % kStateRing : cur;
+  const int col = vh * DV + j;  // column of the gated output row
+
+  for (int b0 = 0; b0 < rows; b0 += B) {
+    const int nb = min(B, rows - b0);
+    const bool fin = b0 == pre;
+    if (fin && (pre > 0 || pend > 0)) {
+      // the state before the final block becomes the base the records apply to
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const float sv = __fmul_rn(Sc[(4 * i4 + e) * DV], decay);
-        Sc[(4 * i4 + e) * DV] = sv;
-        pred = __fadd_rn(pred, __fmul_rn(sv, kk[e]));
+      for (int i = 0; i < DK; i++) base[(int64_t)i * DV] = S[i];
+    }
+    if (fin && pre > 0) {
+#pragma unroll
+      for (int u = 0; u < CPT; u++) {
+        const int c = tid + NT * u;
+        if (c < NCH && (c >= 2 * DK || qk_writer)) {
+          float* co = L.conv_state[slot0] + (int64_t)chan(c) * (K - 1);
+#pragma unroll
+          for (int tp = 0; tp < K - 1; tp++) co[tp] = hist[u][tp];
+        }
       }
     }
-  }
-  for (int t = 0; t < rows; t++) {
-    const float delta = __fmul_rn(__fsub_rn(vs[t][j], pred), beta_s[t]);
-    rec_head[(int64_t)t * rec_stride + DK + j] = delta;
-    const float4* k4 = reinterpret_cast<const float4*>(qk[t][1]);
-    const float4* q4 = reinterpret_cast<const float4*>(qk[t][0]);
-    float o = 0.f;
-    if (t + 1 < rows) {
-      // S += k delta^T and o-sum of row t; decay and pred-sum of row t+1
-      const float4* n4 = reinterpret_cast<const float4*>(qk[t + 1][1]);
-      const float decay = decay_s[t + 1];
-      float pn = 0.f;
-#pragma unroll 2
+    float zin[B];  // gate projections of this column (fused gated norm)
+#pragma unroll
+    for (int t = 0; t < B; t++) zin[t] = (gated && t < nb) ? a.z[(int64_t)(b0 + t) * a.z_ld + col] : 0.f;
+    // every input of the block requested before any arithmetic
+    float xin[CPT][B];
+#pragma unroll
+    for (int u = 0; u < CPT; u++) {
+      const int c = tid + NT * u;
+      const bool own = c < NCH;
+      const int g = own ? chan(c) : 0;
+#pragma unroll
+      for (int t = 0; t < B; t++) xin[u][t] = (own && t < nb) ? a.qkv[(int64_t)(b0 + t) * a.qkv_ld + g] : 0.f;
+    }
+    float bin = 0.f, ain = 0.f;
+    if (tid < nb) {
+      int bi = vh, ai = a.nv + vh;
+      if (a.ba_interleaved) {
+        bi = kh * 2 * ratio + rep;
+        ai = kh * 2 * ratio + ratio + rep;
+      }
+      bin = a.ba[(int64_t)(b0 + tid) * a.ba_ld + bi];
+      ain = a.ba[(int64_t)(b0 + tid) * a.ba_ld + ai];
+    }
+    // causal depthwise conv + SiLU per channel and row (quantized_deltanet.rs:733-759)
+#pragma unroll
+    for (int u = 0; u < CPT; u++) {
+      const int c = tid + NT * u;
+      if (c >= NCH) continue;
+#pragma unroll
+      for (int t = 0; t < B; t++) {
+        if (t >= nb) break;
+        const float x = xin[u][t];
+        float sum = __fmul_rn(cw[u][K - 1], x);
+#pragma unroll
+        for (int tp = 0; tp < K - 1; tp++) sum = __fadd_rn(sum, __fmul_rn(cw[u][tp], hist[u][tp]));
+        const float y = __fmul_rn(sum, sigmoid_ref(sum));
+        if (c < 2 * DK) qk[t][c / DK][c % DK] = y;
+        else vs[t][c - 2 * DK] = y;
+#pragma unroll
+        for (int tp = 0; tp + 1 < K - 1; tp++) hist[u][tp] = hist[u][tp + 1];
+        if (K > 1) hist[u][K - 2] = x;
+        if (fin && (c >= 2 * DK || qk_writer)) {
+          float* co = L.conv_state[(slot0 + 1 + t) % kStateRing] + (int64_t)chan(c) * (K - 1);
+#pragma unroll
+          for (int tp = 0; tp < K - 1; tp++) co[tp] = hist[u][tp];
+        }
+      }
+    }
+    if (tid < nb) {
+      beta_s[tid] = sigmoid_ref(bin);
+      decay_s[tid] = exp_ref(__fmul_rn(ssm_a, softplus_ref(__fadd_rn(ain, dt_bias))));
+    }
+    __syncthreads();
+    // L2 norms: x * (sum x^2 + 1e-6)^-1/2 with the sum in element order
+    // (quantized_deltanet.rs:724-731); one thread per (row, q|k)
+    if (tid < 2 * nb) {
+      const float4* v4 = reinterpret_cast<const float4*>(qk[tid >> 1][tid & 1]);
+      float ss = 0.f;
+#pragma unroll 8
+      for (int i4 = 0; i4 < DK / 4; i4++) {
+        const float4 v = v4[i4];
+        ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
+        ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
+        ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
+        ss = __fadd_rn(ss, __fmul_rn(v.w, v.w));
+      }
+      nscale[tid >> 1][tid & 1] = __fdiv_rn(1.f, sqrtf(__fadd_rn(ss, 1e-6f)));
+    }
+    __syncthreads();
+    for (int e = tid; e < nb * 2 * DK; e += NT) {
+      const int t = e / (2 * DK), w = (e / DK) & 1, i = e % DK;
+      qk[t][w][i] = __fmul_rn(qk[t][w][i], nscale[t][w]);
+    }
+    __syncthreads();
+    if (fin) {
+      // update records of the final block: normalized k and decay (delta below)
+      for (int e = tid; e < nb * DK; e += NT) rec_head[(int64_t)(e / DK) * rec_stride + e % DK] = qk[e / DK][1][e % DK];
+      if (tid < nb) rec_head[(int64_t)tid * rec_stride + DK + DV] = decay_s[tid];
+    }
+
+    // ---- the recurrence, one value column per thread, state in registers
+    float pred = 0.f;
+    {
+      const float decay = decay_s[0];
+      const float4* k4 = reinterpret_cast<const float4*>(qk[0][1]);
+#pragma unroll
+      for (int i4 = 0; i4 < DK / 4; i4++) {
+        const float4 kv = k4[i4];
+        const float kk[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          S[4 * i4 + e] = __fmul_rn(S[4 * i4 + e], decay);
+          pred = __fadd_rn(pred, __fmul_rn(S[4 * i4 + e], kk[e]));
+        }
+      }
+    }
+    for (int t = 0; t < nb; t++) {
+      const float delta = __fmul_rn(__fsub_rn(vs[t][j], pred), beta_s[t]);
+      if (fin) rec_head[(int64_t)t * rec_stride + DK + j] = delta;
+      // S += k delta^T and the o-sum of row t; the decay and pred-sum of row
+      // t+1 in the same walk (the block's last row: decay 1, an exact
+      // multiply, and a pred-sum that is not used)
+      const bool more = t + 1 < nb;
+      const float4* k4 = reinterpret_cast<const float4*>(qk[t][1]);
+      const float4* q4 = reinterpret_cast<const float4*>(qk[t][0]);
+      const float4* n4 = reinterpret_cast<const float4*>(qk[more ? t + 1 : t][1]);
+      const float decay = more ? decay_s[t + 1] : 1.f;
+      float o = 0.f, pn = 0.f;
+#pragma unroll
       for (int i4 = 0; i4 < DK / 4; i4++) {
         const float4 kv = k4[i4], qv = q4[i4], nv = n4[i4];
         const float kk[4] = {kv.x, kv.y, kv.z, kv.w}, qq[4] = {qv.x, qv.y, qv.z, qv.w};
         const float nn[4] = {nv.x, nv.y, nv.z, nv.w};
 #pragma unroll
         for (int e = 0; e < 4; e++) {
-          float sv = __fadd_rn(Sc[(4 * i4 + e) * DV], __fmul_rn(kk[e], delta));
+          float sv = __fadd_rn(S[4 * i4 + e], __fmul_rn(kk[e], delta));
           o = __fadd_rn(o, __fmul_rn(__fmul_rn(sv, qq[e]), qscale));
           sv = __fmul_rn(sv, decay);
           pn = __fadd_rn(pn, __fmul_rn(sv, nn[e]));
-          Sc[(4 * i4 + e) * DV] = sv;
+          S[4 * i4 + e] = sv;
         }
       }
       pred = pn;
-    } else {
-#pragma unroll 2
-      for (int i4 = 0; i4 < DK / 4; i4++) {
-        const float4 kv = k4[i4], qv = q4[i4];
-        const float kk[4] = {kv.x, kv.y, kv.z, kv.w}, qq[4] = {qv.x, qv.y, qv.z, qv.w};
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const float sv = __fadd_rn(Sc[(4 * i4 + e) * DV], __fmul_rn(kk[e], delta));
-          o = __fadd_rn(o, __fmul_rn(__fmul_rn(sv, qq[e]), qscale));
+      if (gated) os[t][j] = o;
+      else a.out[(int64_t)(b0 + t) * a.out_ld + col] = o;
+    }
+    if (gated) {
+      // gated RMSNorm of this value head (src/qwen/norm.rs:16-25): the sum
+      // of squares in element order, then norm(o) * w * silu(z),
+      // z = g / (1 + e^-g); then Q8_0 quantization of each 32-column block
+      // (one warp), as BlockQ8_0::from_float: d = amax / 127 (kept as f16),
+      // q = round(x / d).
+      __syncthreads();
+      if (tid < nb) {
+        const float4* o4 = reinterpret_cast<const float4*>(os[tid]);
+        float ss = 0.f;
+#pragma unroll 8
+        for (int i4 = 0; i4 < DV / 4; i4++) {
+          const float4 v = o4[i4];
+          ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
+          ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
+          ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
+          ss = __fadd_rn(ss, __fmul_rn(v.w, v.w));
         }
+        den_s[tid] = sqrtf(__fadd_rn(__fmul_rn(ss, a.inv_dv), a.eps));
+      }
+      __syncthreads();
+      const int grp = col >> 7, ig = col & 127;   // 128-element group, index inside it
+      const int bb = ig >> 5, tq = ig & 31;
+      const int qlane = ((tq & 15) >> 2) * 8 + bb * 2 + (tq >> 4);
+      const int nbq = a.nv * DV / 32;
+      const float wj = a.norm_w[j];
+#pragma unroll
+      for (int t = 0; t < B; t++) {
+        if (t >= nb) break;
+        const float zz = zin[t];
+        const float silu = __fdiv_rn(zz, __fadd_rn(1.f, exp_ref(-zz)));
+        const float g = __fmul_rn(__fmul_rn(__fdiv_rn(os[t][j], den_s[t]), wj), silu);
+        if (a.g_out) {
+          a.g_out[(int64_t)(b0 + t) * a.g_ld + col] = g;
+          continue;
+        }
+        float amax = fabsf(g);
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+        const float d = __fdiv_rn(amax, 127.f);
+        const float id = d != 0.f ? __fdiv_rn(1.f, d) : 0.f;
+        uint8_t* row = a.q80 + (int64_t)(b0 + t) * a.q80_stride;
+        row[grp * 128 + qlane * 4 + (tq & 3)] = (uint8_t)(int8_t)roundf(__fmul_rn(g, id));
+        if (lane == 0) reinterpret_cast<float*>(row + (int64_t)nbq * 32)[col >> 5] = __half2float(__float2half_rn(d));
       }
     }
-    if (a.q80 || a.g_out) os[t][j] = o;
-    else a.out[(int64_t)t * a.out_ld + vh * DV + j] = o;
-  }
-  if (!a.q80 && !a.g_out) return;
-  // gated RMSNorm of this value head (src/qwen/norm.rs:16-25): the sum of
-  // squares in element order, then norm(o) * w * silu(z), z = g / (1 + e^-g);
-  // then Q8_0 quantization of each 32-column block (one warp), as
-  // BlockQ8_0::from_float: d = amax / 127 (kept as f16), q = round(x / d).
-  __syncthreads();
-  __shared__ float den_s[kMaxRowsDelta];
-  if (tid < rows) {
-    float ss = 0.f;
-    for (int i = 0; i < DV; i++) ss = __fadd_rn(ss, __fmul_rn(os[tid][i], os[tid][i]));
-    den_s[tid] = sqrtf(__fadd_rn(__fmul_rn(ss, a.inv_dv), a.eps));
-  }
-  __syncthreads();
-  const int col = vh * DV + j;                // column of the row
-  const int grp = col >> 7, ig = col & 127;   // 128-element group, index inside it
-  const int bb = ig >> 5, tq = ig & 31;
-  const int qlane = ((tq & 15) >> 2) * 8 + bb * 2 + (tq >> 4);
-  const int nbq = a.nv * DV / 32;
-  const float wj = a.norm_w[j];
-#pragma unroll
-  for (int t = 0; t < kMaxRowsDelta; t++) {
-    if (t >= rows) break;
-    const float zz = zin[t];
-    const float silu = __fdiv_rn(zz, __fadd_rn(1.f, exp_ref(-zz)));
-    const float g = __fmul_rn(__fmul_rn(__fdiv_rn(os[t][j], den_s[t]), wj), silu);
-    if (a.g_out) {
-      a.g_out[(int64_t)t * a.g_ld + col] = g;
-      continue;
-    }
-    float amax = fabsf(g);
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
-    const float d = __fdiv_rn(amax, 127.f);
-    const float id = d != 0.f ? __fdiv_rn(1.f, d) : 0.f;
-    uint8_t* row = a.q80 + (int64_t)t * a.q80_stride;
-    row[grp * 128 + qlane * 4 + (tq & 3)] = (uint8_t)(int8_t)roundf(__fmul_rn(g, id));
-    if (lane == 0) reinterpret_cast<float*>(row + (int64_t)nbq * 32)[col >> 5] = __half2float(__float2half_rn(d));
+    __syncthreads();  // the block's shared rows are read before the next block writes them
   }
 }
 
@@ -385,13 +383,13 @@ __global__ void __launch_bounds__(256) gated_norm_kernel(GatedNormArgs a) {
 }
 
 int deltanet_smem_bytes(int dk, int dv) {
-  return (dk * dv + kMaxRowsDelta * ((dk + dv + 1 + 3) / 4 * 4)) * (int)sizeof(float);
+  return kMaxRowsDelta * ((dk + dv + 1 + 3) / 4 * 4) * (int)sizeof(float);
 }
 
 template <int DK, int DV, int K>
 cudaError_t deltanet_launch_one(const DeltaNetArgs& a, cudaLaunchConfig_t& cfg) {
-  // the state's shared memory exceeds the default 48 KB at 128 x 128: opt in
-  // once per device
+  // the update records and the static rows exceed the default 48 KB at
+  // 128 x 128: opt in once per device
   static std::mutex mu;
   static bool done[64] = {};
   const cudaError_t e = once_per_device(done, mu, [] {
@@ -423,7 +421,10 @@ bool deltanet_supported(int dk, int dv) {
 }
 
 cudaError_t deltanet_launch(const DeltaNetArgs& a, cudaStream_t st, bool pdl) {
-  if (a.rows < 1 || a.rows > kMaxRowsDelta || a.rows >= kStateRing || !deltanet_supported(a.dk, a.dv) ||
+  // any number of rows: the final block of up to kMaxRowsDelta keeps its
+  // conv slots after cur and the slot of the prefix
+  static_assert(kStateRing >= kMaxRowsDelta + 2, "the conv ring holds cur, the prefix slot and a final block");
+  if (a.rows < 1 || !deltanet_supported(a.dk, a.dv) ||
       a.conv_k > 4 || a.conv_k < 1 || a.rec_stride != deltanet_rec_stride(a.dk, a.dv) ||
       (a.q80 && (!a.z || !a.norm_w || (a.nv * a.dv) % 128)) || (a.g_out && (a.q80 || !a.z || !a.norm_w)) ||
       !a.timeout_flag ||

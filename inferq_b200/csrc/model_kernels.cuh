@@ -9,7 +9,7 @@ namespace iq {
 // before a pass and after each of its rows (so it must exceed the rows of a
 // pass); the recurrent state as one base buffer plus the update records of
 // the last pass's rows (see deltanet.cu).
-constexpr int kStateRing = 9;
+constexpr int kStateRing = 10;  // cur, the state after a prefix, 8 rows
 constexpr int kMaxRowsDelta = 8;
 
 struct DeltaNetLayer {

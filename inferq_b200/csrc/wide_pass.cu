@@ -8,9 +8,10 @@
 //     attention q / k / v / o, the shared expert, the quantized router and the
 //     LM head) run on the tcgen05 wide products, each weight read once for
 //     the whole chunk;
-//   * the DeltaNet recurrence and the causal attention scan run in their
-//     exact sequential kernels over 8-row slices of the chunk (the state
-//     advances slice by slice, exactly as consecutive 8-row passes would);
+//   * the DeltaNet recurrence runs in its exact sequential kernel over all
+//     the chunk's rows in one launch (rows in order, the final block of up
+//     to 8 kept for rollback); the causal attention scan runs over 8-row
+//     slices of the chunk (as consecutive 8-row passes would);
 //   * the routed experts run as one grouped GEMV launch: after the routes
 //     are read back, every (expert, up to 8 of its rows) group becomes one
 //     job, so an expert's weights are read once per 8 of its rows; the down
@@ -86,18 +87,20 @@ __global__ void wide_combine_kernel(float* __restrict__ hidden, int H, int topk,
   *h = __fadd_rn(*h, __fadd_rn(acc, __fmul_rn(ysh[(int64_t)r * H + i], selector)));
 }
 
-// per 8-row slice j: [3j] conv ring index, [3j+1] records pending, [3j+2] position
+// per 8-row slice j of the attention scan: [3j + 2] the slice's first position
 __global__ void wide_ctrl_kernel(const int* __restrict__ ctrl, int* __restrict__ wc, int slices) {
   const int j = threadIdx.x;
   if (j >= slices) return;
-  wc[3 * j] = (ctrl[1] + 8 * j) % kStateRing;
-  wc[3 * j + 1] = j == 0 ? ctrl[6] : 8;
   wc[3 * j + 2] = ctrl[0] + 8 * j;
 }
 
+// The chunk's rows before its final block are committed for good: the conv
+// history after them sits in slot cur + 1 (deltanet_kernel), the final
+// block's rows after it, so the ring index moves by one for the prefix plus
+// the final rows, and rollback_kernel can step back inside the final block.
 __global__ void wide_commit_kernel(int* ctrl, int rows, int last) {
   ctrl[0] += rows;
-  ctrl[1] = (ctrl[1] + rows) % kStateRing;
+  ctrl[1] = (ctrl[1] + (rows > last ? 1 : 0) + last) % kStateRing;
   ctrl[6] = last;
 }
 
@@ -162,7 +165,7 @@ int norm_rows(iq_state* s, const float* x, const float* w, int n, int H, float* 
   return IQ_OK;
 }
 
-int wide_delta(iq_state* s, const Layer& L, int li, int n, int slices) {
+int wide_delta(iq_state* s, const Layer& L, int li, int n) {
   const iq_config& c = s->m->cfg;
   auto& W = s->wide;
   const DeltaWeights& D = L.dn;
@@ -177,37 +180,36 @@ int wide_delta(iq_state* s, const Layer& L, int li, int n, int slices) {
     TRY_IQ(wide_project(s, D.beta, W.xn.as<float>(), c.hidden_size, n, W.ba.as<float>(), 2 * nv));
     TRY_IQ(wide_project(s, D.alpha, W.xn.as<float>(), c.hidden_size, n, W.ba.as<float>() + nv, 2 * nv));
   }
-  for (int j = 0; j < slices; j++) {
-    const int r0 = 8 * j, k = std::min(8, n - r0);
-    DeltaNetArgs a = {};
-    a.layers = s->dn_layers.as<DeltaNetLayer>() + li;
-    a.qkv = qkv + (int64_t)r0 * conv_dim;
-    a.qkv_ld = conv_dim;
-    a.ba = W.ba.as<float>() + (int64_t)r0 * 2 * nv;
-    a.ba_ld = 2 * nv;
-    a.out = nullptr;
-    a.out_ld = vdim;
-    a.rows = k;
-    a.nk = c.linear_num_key_heads;
-    a.nv = nv;
-    a.dk = c.linear_key_head_dim;
-    a.dv = c.linear_value_head_dim;
-    a.conv_k = c.linear_conv_kernel_dim;
-    a.tiled_heads = c.value_heads_tiled;
-    a.ba_interleaved = D.ba_fused;
-    a.rec_stride = deltanet_rec_stride(a.dk, a.dv);
-    a.timeout_flag = qmv_timeout_flag();
-    a.cur = W.ctrl.as<int>() + 3 * j;
-    a.pending = W.ctrl.as<int>() + 3 * j + 1;
-    a.z = W.z.as<float>() + (int64_t)r0 * vdim;
-    a.z_ld = vdim;
-    a.norm_w = D.norm.p();
-    a.eps = c.rms_norm_eps;
-    a.inv_dv = (float)(1.0 / c.linear_value_head_dim);
-    a.g_out = W.o.as<float>() + (int64_t)r0 * vdim;
-    a.g_ld = vdim;
-    IQ_CUDA(deltanet_launch(a, s->st, false));
-  }
+  // one launch over every row of the chunk: the recurrence walks them in
+  // order and keeps only the final block for rollback
+  DeltaNetArgs a = {};
+  a.layers = s->dn_layers.as<DeltaNetLayer>() + li;
+  a.qkv = qkv;
+  a.qkv_ld = conv_dim;
+  a.ba = W.ba.as<float>();
+  a.ba_ld = 2 * nv;
+  a.out = nullptr;
+  a.out_ld = vdim;
+  a.rows = n;
+  a.nk = c.linear_num_key_heads;
+  a.nv = nv;
+  a.dk = c.linear_key_head_dim;
+  a.dv = c.linear_value_head_dim;
+  a.conv_k = c.linear_conv_kernel_dim;
+  a.tiled_heads = c.value_heads_tiled;
+  a.ba_interleaved = D.ba_fused;
+  a.rec_stride = deltanet_rec_stride(a.dk, a.dv);
+  a.timeout_flag = qmv_timeout_flag();
+  a.cur = s->ctrl.as<int>() + 1;
+  a.pending = s->ctrl.as<int>() + 6;
+  a.z = W.z.as<float>();
+  a.z_ld = vdim;
+  a.norm_w = D.norm.p();
+  a.eps = c.rms_norm_eps;
+  a.inv_dv = (float)(1.0 / c.linear_value_head_dim);
+  a.g_out = W.o.as<float>();
+  a.g_ld = vdim;
+  IQ_CUDA(deltanet_launch(a, s->st, false));
   TRY_IQ(wide_project(s, D.out, W.o.as<float>(), vdim, n, W.y.as<float>(), c.hidden_size));
   return add_rows(s, W.hidden.as<float>(), W.y.as<float>(), (int64_t)n * c.hidden_size);
 }
@@ -453,7 +455,7 @@ int wide_chunk(iq_state* s, const uint32_t* tokens, int n, float* logits, float*
   for (int l = 0; l < c.num_hidden_layers; l++) {
     const Layer& L = m->layers[l];
     TRY_IQ(norm_rows(s, W.hidden.as<float>(), L.attn_norm.p(), n, H, W.xn.as<float>()));
-    if (L.type == kLinear) TRY_IQ(wide_delta(s, L, li++, n, slices));
+    if (L.type == kLinear) TRY_IQ(wide_delta(s, L, li++, n));
     else TRY_IQ(wide_attention(s, L, fi++, n, slices));
     TRY_IQ(wide_moe(s, L, n));
   }
