@@ -227,12 +227,29 @@ cudaError_t attn_prep_launch(const AttnArgs& a, cudaStream_t st, bool pdl) {
   return launch_pdl(attn_prep_kernel, dim3(a.rows, a.nh + a.nkv), dim3(256), 0, st, pdl, a);
 }
 
-cudaError_t attn_scan_launch(const AttnArgs& a, cudaStream_t st, bool pdl) {
+namespace {
+int scan_split(const AttnArgs& a) {
   const int G = a.nh / a.nkv;
   int split = 1;  // query-head groups per KV head: at least ~2 CTAs per SM's worth of work
   while (split * 2 <= G && G % (split * 2) == 0 && a.nkv * a.chunk_ctas * split < 2 * 148) split *= 2;
+  return split;
+}
+size_t scan_smem(const AttnArgs& a, int rows) {
+  const int gpc = a.nh / a.nkv / scan_split(a);
+  return (size_t)(32 * (a.hd + 1) + 32 * a.hd + rows * gpc * a.hd) * sizeof(float);
+}
+}  // namespace
+
+int attn_scan_max_rows(const AttnArgs& a, int want) {
+  int rows = want;
+  while (rows > 1 && scan_smem(a, rows) > 200 * 1024) rows /= 2;
+  return rows;
+}
+
+cudaError_t attn_scan_launch(const AttnArgs& a, cudaStream_t st, bool pdl) {
+  const int split = scan_split(a);
   dim3 grid(a.nkv, a.chunk_ctas, split);
-  const size_t smem = (size_t)(32 * (a.hd + 1) + 32 * a.hd + a.rows * (G / split) * a.hd) * sizeof(float);
+  const size_t smem = scan_smem(a, a.rows);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   switch (a.hd / 32) {
     case 2: return launch_scan<2>(grid, smem, st, pdl, a);

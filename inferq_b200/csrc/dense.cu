@@ -93,6 +93,64 @@ __global__ void __launch_bounds__(256) f32_matvec_kernel(const float* __restrict
   }
 }
 
+// Many input rows (the wide pass): the same per-row arithmetic as
+// f32_matvec_kernel (lane l sums the float4 at columns 4l + 128t in order of
+// t with fused multiply-adds, then the butterfly), with a CTA's 8 weight rows
+// held in registers while its 64 input rows pass through shared memory in
+// groups of 8.  Grid: (weight rows / 8, input rows / 64).
+__global__ void __launch_bounds__(256) f32_rows_kernel(const float* __restrict__ w, int rows, int cols,
+                                                      const float* __restrict__ x, int ldx, int n,
+                                                      float* __restrict__ y, int ldy) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + warp;
+  const int c4 = cols / 4;
+  constexpr int kMaxPer = 32;  // float4 per lane: cols <= 4096
+  float4 wv[kMaxPer];
+  if (r < rows) {
+    const float4* wr = reinterpret_cast<const float4*>(w + (int64_t)r * cols);
+#pragma unroll
+    for (int j = 0; j < kMaxPer; j++)
+      if (lane + 32 * j < c4) wv[j] = __ldg(wr + lane + 32 * j);
+  }
+  extern __shared__ float4 xs4[];  // [8][cols/4]
+  const int g1 = min(n, (int)(blockIdx.y + 1) * 64);
+  for (int g = blockIdx.y * 64; g < g1; g += 8) {
+    const int k = min(8, g1 - g);
+    __syncthreads();
+    for (int i = threadIdx.x; i < k * c4; i += 256)
+      xs4[i] = *reinterpret_cast<const float4*>(x + (int64_t)(g + i / c4) * ldx + 4 * (i % c4));
+    __syncthreads();
+    if (r >= rows) continue;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxPer; j++) {
+      if (lane + 32 * j >= c4) break;
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        if (i < k) {
+          const float4 xv = xs4[i * c4 + lane + 32 * j];
+          float t = acc[i];
+          t = fmaf(wv[j].x, xv.x, t);
+          t = fmaf(wv[j].y, xv.y, t);
+          t = fmaf(wv[j].z, xv.z, t);
+          t = fmaf(wv[j].w, xv.w, t);
+          acc[i] = t;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      if (i >= k) break;
+      float v = acc[i];
+#pragma unroll
+      for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+      if (lane == 0) y[(int64_t)(g + i) * ldy + r] = v;
+    }
+  }
+}
+
 // One warp per weight row; the k input rows are staged rounded to bf16 (as
 // f32); each lane sums its columns' exact products in column order, then the
 // lanes combine in a fixed tree.
@@ -169,6 +227,20 @@ cudaError_t f32_matvec(const float* w, int rows, int cols, const float* x, int l
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, f32_matvec_kernel, w, rows, cols, x, ldx, k, y, ldy, norm_w, eps,
                             (float)(1.0 / (double)cols), q8k_out, q8k_stride);
+}
+
+cudaError_t f32_rows(const float* w, int rows, int cols, const float* x, int ldx, int n, float* y, int ldy,
+                     cudaStream_t st) {
+  if (cols % 4 || cols > 4096 || n < 1 || rows < 1 || ((uintptr_t)x & 15) || ldx % 4) return cudaErrorInvalidValue;
+  static bool configured[64] = {};
+  static std::mutex mu;
+  const cudaError_t e = once_per_device(configured, mu, [] {
+    return cudaFuncSetAttribute(f32_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 4096 * 4);
+  });
+  if (e != cudaSuccess) return e;
+  f32_rows_kernel<<<dim3((unsigned)ceil_div(rows, 8), (unsigned)ceil_div(n, 64)), 256, (size_t)8 * cols * 4, st>>>(
+      w, rows, cols, x, ldx, n, y, ldy);
+  return cudaGetLastError();
 }
 
 }  // namespace iq

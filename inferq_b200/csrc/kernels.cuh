@@ -39,6 +39,10 @@ cudaError_t prep_rows(const PrepArgs& a, int rows, cudaStream_t st, bool pdl);
 // With norm_w set, the input rows are first RMS-normalized (GGUF RMSNorm),
 // and with q8k_out also written as Q8_K activation rows (row stride
 // q8k_stride bytes) for the quantized matrices that take the same input.
+// y[t*ldy + r] = w row r . x row t for n input rows (any n), the f32_matvec
+// arithmetic per row (the wide pass's router)
+cudaError_t f32_rows(const float* w, int rows, int cols, const float* x, int ldx, int n, float* y, int ldy,
+                     cudaStream_t st);
 cudaError_t f32_matvec(const float* w, int rows, int cols, const float* x, int ldx, int k, float* y,
                        int ldy, cudaStream_t st, bool pdl, const float* norm_w = nullptr, float eps = 0.f,
                        uint8_t* q8k_out = nullptr, int q8k_stride = 0);

@@ -93,6 +93,9 @@ struct AttnArgs {
 constexpr int kAttnChunk = 32;
 cudaError_t attn_prep_launch(const AttnArgs& a, cudaStream_t st, bool pdl);
 cudaError_t attn_scan_launch(const AttnArgs& a, cudaStream_t st, bool pdl);
+// The most rows (a power-of-two fraction of `want`) one scan launch holds
+// with this geometry (the query rows share the CTA's shared memory).
+int attn_scan_max_rows(const AttnArgs& a, int want);
 cudaError_t attn_combine_launch(const AttnArgs& a, cudaStream_t st, bool pdl);
 
 // ---------------------------------------------------------------------- MoE

@@ -87,11 +87,11 @@ __global__ void wide_combine_kernel(float* __restrict__ hidden, int H, int topk,
   *h = __fadd_rn(*h, __fadd_rn(acc, __fmul_rn(ysh[(int64_t)r * H + i], selector)));
 }
 
-// per 8-row slice j of the attention scan: [3j + 2] the slice's first position
-__global__ void wide_ctrl_kernel(const int* __restrict__ ctrl, int* __restrict__ wc, int slices) {
+// per attention slice j of `rows` rows: [j] the slice's first position
+__global__ void wide_ctrl_kernel(const int* __restrict__ ctrl, int* __restrict__ wc, int slices, int rows) {
   const int j = threadIdx.x;
   if (j >= slices) return;
-  wc[3 * j + 2] = ctrl[0] + 8 * j;
+  wc[j] = ctrl[0] + rows * j;
 }
 
 // The chunk's rows before its final block are committed for good: the conv
@@ -104,7 +104,6 @@ __global__ void wide_commit_kernel(int* ctrl, int rows, int last) {
   ctrl[6] = last;
 }
 
-constexpr int kMaxKPass = 8;
 
 bool wide_dtype(int dt) { return dt == Q8_0 || dt == Q4_K || dt == Q6_K; }
 
@@ -214,7 +213,7 @@ int wide_delta(iq_state* s, const Layer& L, int li, int n) {
   return add_rows(s, W.hidden.as<float>(), W.y.as<float>(), (int64_t)n * c.hidden_size);
 }
 
-int wide_attention(iq_state* s, const Layer& L, int fi, int n, int slices) {
+int wide_attention(iq_state* s, const Layer& L, int fi, int n) {
   const iq_config& c = s->m->cfg;
   auto& W = s->wide;
   const AttnWeights& A = L.at;
@@ -222,8 +221,11 @@ int wide_attention(iq_state* s, const Layer& L, int fi, int n, int slices) {
   TRY_IQ(wide_project(s, A.q, W.xn.as<float>(), c.hidden_size, n, W.big.as<float>(), 2 * nhd));
   TRY_IQ(wide_project(s, A.k, W.xn.as<float>(), c.hidden_size, n, W.kp.as<float>(), kvd));
   TRY_IQ(wide_project(s, A.v, W.xn.as<float>(), c.hidden_size, n, W.vp.as<float>(), kvd));
-  for (int j = 0; j < slices; j++) {
-    const int r0 = 8 * j, k = std::min(8, n - r0);
+  // slices of W.attn_rows rows: every row's arithmetic is its own (fixed
+  // 32-position chunks merged in order), so the slice size changes no result
+  const int R = W.attn_rows;
+  for (int j = 0, r0 = 0; r0 < n; j++, r0 += R) {
+    const int k = std::min(R, n - r0);
     AttnArgs a = {};
     a.qg = W.big.as<float>() + (int64_t)r0 * 2 * nhd;
     a.qg_ld = 2 * nhd;
@@ -235,8 +237,8 @@ int wide_attention(iq_state* s, const Layer& L, int fi, int n, int slices) {
     a.k_norm = A.k_norm.p();
     a.kcache = s->kc[fi].as<float>();
     a.vcache = s->vc[fi].as<float>();
-    a.qbuf = s->qbuf.as<float>();
-    a.part = s->part.as<float>();
+    a.qbuf = W.qbuf.as<float>();
+    a.part = W.part.as<float>();
     a.out = W.o.as<float>() + (int64_t)r0 * nhd;
     a.out_ld = nhd;
     a.rows = k;
@@ -246,7 +248,7 @@ int wide_attention(iq_state* s, const Layer& L, int fi, int n, int slices) {
     a.rotary_dim = c.rotary_dim;
     a.theta = c.rope_theta;
     a.eps = c.rms_norm_eps;
-    a.pos = W.ctrl.as<int>() + 3 * j + 2;
+    a.pos = W.ctrl.as<int>() + j;
     a.chunk_ctas = s->max_chunks;
     IQ_CUDA(attn_prep_launch(a, s->st, false));
     IQ_CUDA(attn_scan_launch(a, s->st, false));
@@ -268,13 +270,9 @@ int wide_moe(iq_state* s, const Layer& L, int n) {
   float* lg = W.lg.as<float>();
   if (M.router.present()) {
     TRY_IQ(wide_project(s, M.router, W.xn.as<float>(), H, n, lg, E + 1));
-    for (int r0 = 0; r0 < n; r0 += kMaxKPass)
-      IQ_CUDA(f32_matvec(M.selector.p(), 1, H, W.xn.as<float>() + (int64_t)r0 * H, H, std::min(kMaxKPass, n - r0),
-                         lg + (int64_t)r0 * (E + 1) + E, E + 1, st, false));
+    IQ_CUDA(f32_rows(M.selector.p(), 1, H, W.xn.as<float>(), H, n, lg + E, E + 1, st));
   } else {
-    for (int r0 = 0; r0 < n; r0 += kMaxKPass)
-      IQ_CUDA(f32_matvec(M.router_sel.p(), E + 1, H, W.xn.as<float>() + (int64_t)r0 * H, H,
-                         std::min(kMaxKPass, n - r0), lg + (int64_t)r0 * (E + 1), E + 1, st, false));
+    IQ_CUDA(f32_rows(M.router_sel.p(), E + 1, H, W.xn.as<float>(), H, n, lg, E + 1, st));
   }
   IQ_CUDA(moe_route_rows_launch(lg, E + 1, n, E, topk, c.norm_topk_prob, W.re.as<int>(), W.rw.as<float>(), st));
   IQ_CUDA(cudaMemcpyAsync(W.h_routes, W.re.p, (size_t)n * topk * 4, cudaMemcpyDeviceToHost, st));
@@ -426,7 +424,21 @@ int alloc_wide(iq_state* s, int n) {
   IQ_CUDA(W.kp.reserve(n * kvd * 4));
   IQ_CUDA(W.vp.reserve(n * kvd * 4));
   IQ_CUDA(W.tokens.reserve(n * 4));
-  IQ_CUDA(W.ctrl.reserve(3 * ceil_div(n, 8) * 4));
+  IQ_CUDA(W.ctrl.reserve(ceil_div(n, 8) * 4));
+  if (c.num_attention_heads > 0 && s->m->n_linear < c.num_hidden_layers) {
+    // attention slices: as many rows as the scan's shared memory and a
+    // partials buffer of at most 512 MB hold
+    AttnArgs g = {};
+    g.nh = c.num_attention_heads;
+    g.nkv = c.num_key_value_heads;
+    g.hd = c.head_dim;
+    g.chunk_ctas = s->max_chunks;
+    int R = attn_scan_max_rows(g, 32);
+    while (R > 8 && (int64_t)R * nhd * s->max_chunks * 4 > (int64_t)512 << 20) R /= 2;
+    W.attn_rows = R;
+    IQ_CUDA(W.qbuf.reserve(R * nhd * 4));
+    IQ_CUDA(W.part.reserve((size_t)R * c.num_attention_heads * s->max_chunks * (c.head_dim + 2) * 4));
+  }
   IQ_CUDA(W.lg.reserve(n * (E + 1) * 4));
   IQ_CUDA(W.re.reserve(n * topk * 4));
   IQ_CUDA(W.rw.reserve(n * topk * 4));
@@ -444,10 +456,10 @@ int wide_chunk(iq_state* s, const uint32_t* tokens, int n, float* logits, float*
   auto& W = s->wide;
   cudaStream_t st = s->st;
   const int H = c.hidden_size, V = c.vocab_size;
-  const int slices = (int)ceil_div(n, 8);
   std::vector<int32_t> tk(tokens, tokens + n);
   IQ_CUDA(cudaMemcpyAsync(W.tokens.p, tk.data(), (size_t)n * 4, cudaMemcpyHostToDevice, st));
-  wide_ctrl_kernel<<<1, 256, 0, st>>>(s->ctrl.as<int>(), W.ctrl.as<int>(), slices);
+  wide_ctrl_kernel<<<1, 256, 0, st>>>(s->ctrl.as<int>(), W.ctrl.as<int>(), (int)ceil_div(n, W.attn_rows),
+                                      W.attn_rows);
   IQ_CUDA(cudaGetLastError());
   IQ_CUDA(embed_launch(m->embed.dt, m->embed.p(), m->embed.row_bytes, H, W.tokens.as<int32_t>(), n,
                        W.hidden.as<float>(), H, st, false));
@@ -456,7 +468,7 @@ int wide_chunk(iq_state* s, const uint32_t* tokens, int n, float* logits, float*
     const Layer& L = m->layers[l];
     TRY_IQ(norm_rows(s, W.hidden.as<float>(), L.attn_norm.p(), n, H, W.xn.as<float>()));
     if (L.type == kLinear) TRY_IQ(wide_delta(s, L, li++, n));
-    else TRY_IQ(wide_attention(s, L, fi++, n, slices));
+    else TRY_IQ(wide_attention(s, L, fi++, n));
     TRY_IQ(wide_moe(s, L, n));
   }
   TRY_IQ(norm_rows(s, W.hidden.as<float>(), m->out_norm.p(), n, H, W.xn.as<float>()));
@@ -487,7 +499,7 @@ int wide_chunk(iq_state* s, const uint32_t* tokens, int n, float* logits, float*
       }
     }
   }
-  const int last = n - 8 * (slices - 1);
+  const int last = (n - 1) % kMaxRowsDelta + 1;  // the final block the DeltaNet kernels keep
   wide_commit_kernel<<<1, 1, 0, st>>>(s->ctrl.as<int>(), n, last);
   IQ_CUDA(cudaGetLastError());
   IQ_CUDA(cudaStreamSynchronize(st));
