@@ -109,7 +109,7 @@ Q4_K_M = {
 
 
 def tiny() -> Config:
-    """the tiny Qwen3-Next-style model, every matrix Q8_0."""
+    """The tiny Qwen3-Next-style model (hidden 512, 4 layers), every matrix Q8_0."""
     return Config(
         name="tiny-qwen3next-q8_0", hidden_size=512, num_hidden_layers=4, vocab_size=8192,
         num_attention_heads=8, num_key_value_heads=2, head_dim=64, rotary_dim=16,
@@ -121,7 +121,7 @@ def tiny() -> Config:
 
 
 def qwen36_35b() -> Config:
-    """BASELINE configs 2/3: Qwen3.6-35B-A3B shapes, Q4_K_M mix, one MTP layer."""
+    """Qwen3.6-35B-A3B shapes (40 layers, 256 experts), Q4_K_M mix, one MTP layer."""
     return Config(
         name="qwen3.6-35b-a3b-q4_k_m", hidden_size=2048, num_hidden_layers=40, vocab_size=248320,
         num_attention_heads=16, num_key_value_heads=2, head_dim=256, rotary_dim=64,
@@ -133,7 +133,7 @@ def qwen36_35b() -> Config:
 
 
 def coder_next_80b() -> Config:
-    """Qwen3-Next-80B / Coder-Next shapes, Q4_K_M mix."""
+    """Qwen3-Next-80B / Coder-Next shapes (48 layers, 512 experts), Q4_K_M mix."""
     c = qwen36_35b()
     c.name = "qwen3-coder-next-80b-q4_k_m"
     c.num_hidden_layers = 48
