@@ -6,8 +6,8 @@
 // the next `depth` units of its stream in flight in a ring of shared-memory
 // slots: one 2-D TMA load (tensor map over the weight tensor, box = one unit
 // x 16 rows) per unit, completing on the slot's mbarrier.  The warp waits for
-// a slot, copies the unit's fragments to registers, refills the slot with the
-// unit `depth` ahead and computes.  Activations are staged into shared memory
+// a slot, copies the unit's fragments to registers, computes, then refills
+// the slot with the unit `depth` ahead.  Activations are staged into shared memory
 // once per change of input rows, not once per tile.
 #include <algorithm>
 #include <mutex>
@@ -414,7 +414,8 @@ __device__ __forceinline__ void issue_unit(const StreamPos& p, uint8_t* slot, ui
 __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs, int njobs,
                                                              const int* __restrict__ dyn_count, int total_hint,
                                                              int act_bytes, int depth, int slot_bytes,
-                                                             int test_skip) {
+                                                             int flags) {
+  const bool test_skip = flags & 1;
   __shared__ float part[kQmvWarps][32][4];
   // the job table in shared memory when it is small (one parallel copy, no
   // dependent global reads later); otherwise just the jobs' tile offsets
@@ -490,6 +491,7 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
   const uint8_t* staged_act = nullptr;
   int staged_rows = -1, staged_stride = 0, staged_job = -1;
   uint32_t n = 0;  // units consumed by this warp
+  uint32_t si = 0, phase = 0;  // its ring slot (n mod depth) and that slot's parity (n / depth mod 2)
   bool ok = true;
   for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
     const WarpTile ct = warp_tile(jobs, t0, njobs, total, tile, warp);
@@ -562,9 +564,8 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
     for (int i = 0; i < 4; i++) { f.acc[i] = 0.f; f.accm[i] = 0.f; }
     if (ct.live() && ok) {
       for (int b = ct.u0; b < ct.u1; b++, n++) {
-        const uint32_t si = n % depth;
         uint8_t* slot = ring + si * slot_bytes;
-        if (!mbar_wait(&wbars[si], (n / depth) & 1, wait_limit)) {
+        if (!mbar_wait(&wbars[si], phase, wait_limit)) {
           if (lane == 0) atomicExch(&g_qmv_timeout, 1);
           ok = false;
           // let this warp's other copies land (bounded) before it stops using the ring
@@ -573,8 +574,9 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
         }
         WRegs cur;
         load_slot(ct.dt, slot, b, gid, tig, cur);
-        // every lane's generic reads of the slot precede the async refill
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        compute_block(ct.dt, cur, bact, ac, ct.nb, b, tig, f);
+        // refill the slot once the unit's words have been used: every lane's
+        // reads of it have completed before lane 0 hands it to the copy engine
         __syncwarp();
         if (pp.tile < total) {
           if (lane == 0) issue_unit(pp, slot, &wbars[si], pol);
@@ -582,7 +584,10 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
           pp.b++;
           stream_settle(jobs, t0, njobs, total, warp, pp);
         }
-        compute_block(ct.dt, cur, bact, ac, ct.nb, b, tig, f);
+        if (++si == (uint32_t)depth) {
+          si = 0;
+          phase ^= 1u;
+        }
       }
     }
 
@@ -751,9 +756,10 @@ cudaError_t qmv_launch(const QmvJob* jobs, int njobs, const int* dyn_count, int 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  static const int test_skip = getenv("IQ_QMV_TEST_TIMEOUT") ? 1 : 0;
+  // bit 0 (tests only): one first slot is never requested
+  static const int flags = getenv("IQ_QMV_TEST_TIMEOUT") ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, qmv_kernel, jobs, njobs, dyn_count, dyn_count ? 0 : ntiles, smem_bytes, depth,
-                            slot_bytes, test_skip);
+                            slot_bytes, flags);
 }
 
 }  // namespace iq

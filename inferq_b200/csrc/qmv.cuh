@@ -12,6 +12,7 @@
 // partials are added left to right.  ksplit depends only on the matrix
 // shape, so an output row never depends on how many input rows ran with it.
 #pragma once
+#include <cstdlib>
 #include "iq_common.cuh"
 
 namespace iq {
