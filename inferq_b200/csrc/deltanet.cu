@@ -12,15 +12,16 @@
 // quantized_deltanet.rs:724-731).  So one thread owns one value column j and
 // walks the dk key rows of S[:, j] in order, with the column in registers.
 //
-// Grid: one CTA per value head, dv/32 warps; warp w owns columns
-// 32w .. 32w+31, and column j of the head's dk x dv state lives in thread j's
-// registers (the key-row walks are fully unrolled).  Rows run in blocks of
-// up to 8: the conv, the norms and beta/g of a block's rows are computed
-// first by the whole CTA (they do not depend on the state); then each thread
-// runs the block's rows: the o-sum of row t and the decay and pred-sum of
-// row t+1 walk the key rows in the same loop (two independent chains).  A
-// pass may hold any number of rows (the wide prefill hands a whole chunk to
-// one launch); only its final block is kept for rollback.
+// Grid: one CTA per value head, 2 * dv threads: two walkers per value column
+// j, each holding column j of the head's dk x dv state in registers (the
+// key-row walks are fully unrolled) and applying the same updates.  Rows run
+// in blocks of up to 8: the conv, the norms and beta/g of a block's rows are
+// computed first by the whole CTA (they do not depend on the state); then,
+// per row t, the output walker sums o(t) while the prediction walker sums
+// pred(t+1) and hands delta(t+1) to its partner through shared memory (one
+// CTA barrier per row).  Each scheduler thus holds two independent chains.
+// A pass may hold any number of rows (the wide prefill hands a whole chunk
+// to one launch); only its final block is kept for rollback.
 //
 // Rollback without state copies: the recurrent state is one buffer per layer
 // (the state before the last pass) plus, per row of the last pass, an update
@@ -50,8 +51,8 @@ __device__ __forceinline__ float softplus_ref(float v) {
 
 // DK key rows, DV value columns per head (32 * warps), conv width K.
 template <int DK, int DV, int K>
-__global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
-  constexpr int NT = DV;               // threads
+__global__ void __launch_bounds__(2 * DV) deltanet_kernel(DeltaNetArgs a) {
+  constexpr int NT = 2 * DV;           // threads: the output and the prediction walker of each column
   constexpr int NCH = 2 * DK + DV;     // conv channels of this head: q | k | v
   constexpr int CPT = (NCH + NT - 1) / NT;
   constexpr int QS = DK + 4;           // padded row of q/k in shared memory
@@ -62,7 +63,8 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
   const int kh = a.tiled_heads ? vh % a.nk : vh / ratio;
   const int rep = a.tiled_heads ? vh / a.nk : vh % ratio;
   const int tid = threadIdx.x, lane = tid & 31;
-  const int j = tid;                   // value column of this thread
+  const int j = tid % DV;              // value column of this thread
+  const bool walker_o = tid < DV;      // the output walker (else the prediction walker)
   const int key_dim = a.nk * DK;
   const int rows = a.rows;
   const int rec_stride = a.rec_stride;
@@ -122,6 +124,7 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
   __shared__ __align__(16) float os[B][DV];  // recurrent outputs (fused gated norm)
   __shared__ float nscale[B][2];
   __shared__ float den_s[B];
+  __shared__ float dsm[B][DV];  // delta of each row, from the prediction walker
   const bool qk_writer = rep == 0;
   const bool gated = a.q80 || a.g_out;
   const float qscale = __fdiv_rn(1.f, sqrtf((float)DK));
@@ -139,7 +142,7 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
   for (int b0 = 0; b0 < rows; b0 += B) {
     const int nb = min(B, rows - b0);
     const bool fin = b0 == pre;
-    if (fin && (pre > 0 || pend > 0)) {
+    if (fin && (pre > 0 || pend > 0) && walker_o) {
       // the state before the final block becomes the base the records apply to
 #pragma unroll
       for (int i = 0; i < DK; i++) base[(int64_t)i * DV] = S[i];
@@ -157,7 +160,7 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
     }
     float zin[B];  // gate projections of this column (fused gated norm)
 #pragma unroll
-    for (int t = 0; t < B; t++) zin[t] = (gated && t < nb) ? a.z[(int64_t)(b0 + t) * a.z_ld + col] : 0.f;
+    for (int t = 0; t < B; t++) zin[t] = (gated && walker_o && t < nb) ? a.z[(int64_t)(b0 + t) * a.z_ld + col] : 0.f;
     // every input of the block requested before any arithmetic
     float xin[CPT][B];
 #pragma unroll
@@ -235,11 +238,15 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
       if (tid < nb) rec_head[(int64_t)tid * rec_stride + DK + DV] = decay_s[tid];
     }
 
-    // ---- the recurrence, one value column per thread, state in registers
-    float pred = 0.f;
+    // ---- the recurrence, state in registers.  Both walkers of column j hold
+    // the column and apply the same updates (bitwise the same state); the
+    // output walker sums row t's output, the prediction walker row t+1's
+    // pred and hands delta(t+1) over through shared memory, one CTA barrier
+    // per row.
     {
       const float decay = decay_s[0];
       const float4* k4 = reinterpret_cast<const float4*>(qk[0][1]);
+      float pred = 0.f;
 #pragma unroll
       for (int i4 = 0; i4 < DK / 4; i4++) {
         const float4 kv = k4[i4];
@@ -247,39 +254,60 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
 #pragma unroll
         for (int e = 0; e < 4; e++) {
           S[4 * i4 + e] = __fmul_rn(S[4 * i4 + e], decay);
-          pred = __fadd_rn(pred, __fmul_rn(S[4 * i4 + e], kk[e]));
+          if (!walker_o) pred = __fadd_rn(pred, __fmul_rn(S[4 * i4 + e], kk[e]));
         }
+      }
+      if (!walker_o) {
+        const float delta = __fmul_rn(__fsub_rn(vs[0][j], pred), beta_s[0]);
+        dsm[0][j] = delta;
+        if (fin) rec_head[DK + j] = delta;
       }
     }
+    __syncthreads();
     for (int t = 0; t < nb; t++) {
-      const float delta = __fmul_rn(__fsub_rn(vs[t][j], pred), beta_s[t]);
-      if (fin) rec_head[(int64_t)t * rec_stride + DK + j] = delta;
-      // S += k delta^T and the o-sum of row t; the decay and pred-sum of row
-      // t+1 in the same walk (the block's last row: decay 1, an exact
-      // multiply, and a pred-sum that is not used)
+      const float delta = dsm[t][j];
+      // S += k delta^T, then the decay of row t+1 (the block's last row:
+      // decay 1, an exact multiply)
       const bool more = t + 1 < nb;
       const float4* k4 = reinterpret_cast<const float4*>(qk[t][1]);
-      const float4* q4 = reinterpret_cast<const float4*>(qk[t][0]);
-      const float4* n4 = reinterpret_cast<const float4*>(qk[more ? t + 1 : t][1]);
       const float decay = more ? decay_s[t + 1] : 1.f;
-      float o = 0.f, pn = 0.f;
+      if (walker_o) {
+        const float4* q4 = reinterpret_cast<const float4*>(qk[t][0]);
+        float o = 0.f;
 #pragma unroll
-      for (int i4 = 0; i4 < DK / 4; i4++) {
-        const float4 kv = k4[i4], qv = q4[i4], nv = n4[i4];
-        const float kk[4] = {kv.x, kv.y, kv.z, kv.w}, qq[4] = {qv.x, qv.y, qv.z, qv.w};
-        const float nn[4] = {nv.x, nv.y, nv.z, nv.w};
+        for (int i4 = 0; i4 < DK / 4; i4++) {
+          const float4 kv = k4[i4], qv = q4[i4];
+          const float kk[4] = {kv.x, kv.y, kv.z, kv.w}, qq[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-          float sv = __fadd_rn(S[4 * i4 + e], __fmul_rn(kk[e], delta));
-          o = __fadd_rn(o, __fmul_rn(__fmul_rn(sv, qq[e]), qscale));
-          sv = __fmul_rn(sv, decay);
-          pn = __fadd_rn(pn, __fmul_rn(sv, nn[e]));
-          S[4 * i4 + e] = sv;
+          for (int e = 0; e < 4; e++) {
+            const float sv = __fadd_rn(S[4 * i4 + e], __fmul_rn(kk[e], delta));
+            o = __fadd_rn(o, __fmul_rn(__fmul_rn(sv, qq[e]), qscale));
+            S[4 * i4 + e] = __fmul_rn(sv, decay);
+          }
+        }
+        if (gated) os[t][j] = o;
+        else a.out[(int64_t)(b0 + t) * a.out_ld + col] = o;
+      } else {
+        const float4* n4 = reinterpret_cast<const float4*>(qk[more ? t + 1 : t][1]);
+        float pn = 0.f;
+#pragma unroll
+        for (int i4 = 0; i4 < DK / 4; i4++) {
+          const float4 kv = k4[i4], nv = n4[i4];
+          const float kk[4] = {kv.x, kv.y, kv.z, kv.w}, nn[4] = {nv.x, nv.y, nv.z, nv.w};
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const float sv = __fmul_rn(__fadd_rn(S[4 * i4 + e], __fmul_rn(kk[e], delta)), decay);
+            pn = __fadd_rn(pn, __fmul_rn(sv, nn[e]));
+            S[4 * i4 + e] = sv;
+          }
+        }
+        if (more) {
+          const float dn = __fmul_rn(__fsub_rn(vs[t + 1][j], pn), beta_s[t + 1]);
+          dsm[t + 1][j] = dn;
+          if (fin) rec_head[(int64_t)(t + 1) * rec_stride + DK + j] = dn;
         }
       }
-      pred = pn;
-      if (gated) os[t][j] = o;
-      else a.out[(int64_t)(b0 + t) * a.out_ld + col] = o;
+      __syncthreads();
     }
     if (gated) {
       // gated RMSNorm of this value head (src/qwen/norm.rs:16-25): the sum
@@ -302,6 +330,7 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
         den_s[tid] = sqrtf(__fadd_rn(__fmul_rn(ss, a.inv_dv), a.eps));
       }
       __syncthreads();
+      if (walker_o) {
       const int grp = col >> 7, ig = col & 127;   // 128-element group, index inside it
       const int bb = ig >> 5, tq = ig & 31;
       const int qlane = ((tq & 15) >> 2) * 8 + bb * 2 + (tq >> 4);
@@ -325,6 +354,7 @@ __global__ void __launch_bounds__(DV) deltanet_kernel(DeltaNetArgs a) {
         uint8_t* row = a.q80 + (int64_t)(b0 + t) * a.q80_stride;
         row[grp * 128 + qlane * 4 + (tq & 3)] = (uint8_t)(int8_t)roundf(__fmul_rn(g, id));
         if (lane == 0) reinterpret_cast<float*>(row + (int64_t)nbq * 32)[col >> 5] = __half2float(__float2half_rn(d));
+      }
       }
     }
     __syncthreads();  // the block's shared rows are read before the next block writes them
@@ -432,7 +462,7 @@ cudaError_t deltanet_launch(const DeltaNetArgs& a, cudaStream_t st, bool pdl) {
     return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.nv);
-  cfg.blockDim = dim3(a.dv);
+  cfg.blockDim = dim3(2 * a.dv);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
