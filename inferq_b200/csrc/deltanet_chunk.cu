@@ -1,0 +1,354 @@
+// deltanet_chunk.cu -- the chunked Gated DeltaNet recurrence for the rows of
+// a wide pass that precede its final block.
+//
+// The sequential rule (src/qwen/deltanet.rs:122-217, per value head, state
+// S [dk][dv]): S *= g_t; pred = S^T k_t; delta_t = beta_t (v_t - pred);
+// S += k_t delta_t^T; o_t = S^T q_t / sqrt(dk).  Over a chunk of C rows
+// starting from S0, with L_t = sum_{s<=t} log g_s and r(t,s) = exp(L_t - L_s):
+//
+//   delta_t = beta_t (v_t - e^{L_t} S0^T k_t) - sum_{s<t} beta_t r(t,s) (k_t.k_s) delta_s
+//   o_t     = (e^{L_t} S0^T q_t + sum_{s<=t} r(t,s) (q_t.k_s) delta_s) / sqrt(dk)
+//   S_C     = e^{L_{C-1}} S0 + sum_s r(C-1,s) k_s delta_s^T
+//
+// (the WY / UT form: the lower-triangular solve for delta runs as forward
+// substitution).  This is the same arithmetic up to f32 rounding order, so
+// the wide pass uses it where the reference's own prefill is not bitwise
+// its split passes either (src/runtime.rs:740-747); decays enter only as
+// exp of differences of the cumulative log-decay, never as a product that
+// could underflow.  Every sum below has a fixed order, restated by the CPU
+// oracle's wide order:
+//   * dots over the key dimension (k_t.k_s, q_t.k_s): sequential in i;
+//   * S0^T k_t and S0^T q_t per column: eight parts of dk/8 consecutive key
+//     rows, each sequential, combined as ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7));
+//   * the sums over s: part p takes s = p (mod 8) in ascending order, the
+//     parts combined by the same tree;
+//   * the state update: e^{L_{C-1}} S0, then + (r k_s[i]) delta_s in s order.
+//
+// Three launches: per-row conv + SiLU, L2 norms, beta and log-decay (the
+// sequential kernel's formulas, so these values are bitwise its own); the
+// chunk kernel, CTA (value head, 32 columns), 256 threads = 32 columns x 8
+// parts, 64-row chunks in order; the gated RMSNorm of the rows.
+#include <mutex>
+#include "model_kernels.cuh"
+#include "devfns.cuh"
+
+namespace iq {
+namespace {
+
+constexpr int kChunk = 64;
+
+__device__ __forceinline__ float sigmoid_c(float v) { return __fdiv_rn(1.f, __fadd_rn(1.f, exp_ref(-v))); }
+__device__ __forceinline__ float softplus_c(float v) {
+  if (v > 20.f) return v;
+  if (v < -20.f) return exp_ref(v);
+  return log1p_ref(exp_ref(v));
+}
+
+// grid (rows): conv + SiLU of every channel of row t (quantized_deltanet.rs:
+// 733-759), L2 norms of its q and k heads (:724-731), beta = sigmoid(b) and
+// log g = ssm_a * softplus(a + dt_bias) per value head.  The CTA of the last
+// row also stores the conv history after the rows in conv slot cur + 1.
+template <int K>
+__global__ void __launch_bounds__(256) dn_prep_kernel(DeltaChunkArgs a) {
+  extern __shared__ float y[];  // [conv_dim]
+  __shared__ float nscale[64];
+  const DeltaNetLayer& L = *a.layers;
+  const int t = blockIdx.x;
+  const int key_dim = a.nk * a.dk, conv_dim = 2 * key_dim + a.nv * a.dv;
+  const int cur = *a.cur;
+  const float* cin = L.conv_state[cur];
+  for (int g = threadIdx.x; g < conv_dim; g += 256) {
+    float w[4], h[3];
+#pragma unroll
+    for (int tp = 0; tp < K; tp++) w[tp] = L.conv_w[(int64_t)g * K + tp];
+#pragma unroll
+    for (int tp = 0; tp < K - 1; tp++) {
+      const int r = t - (K - 1) + tp;  // the input row this history tap holds
+      h[tp] = r >= 0 ? a.qkv[(int64_t)r * a.qkv_ld + g] : cin[(int64_t)g * (K - 1) + t + tp];
+    }
+    const float x = a.qkv[(int64_t)t * a.qkv_ld + g];
+    float sum = __fmul_rn(w[K - 1], x);
+#pragma unroll
+    for (int tp = 0; tp < K - 1; tp++) sum = __fadd_rn(sum, __fmul_rn(w[tp], h[tp]));
+    y[g] = __fmul_rn(sum, sigmoid_c(sum));
+    if (t == a.rows - 1) {
+      // the history after the last row: inputs t-K+2 .. t
+      float* co = L.conv_state[(cur + 1) % kStateRing] + (int64_t)g * (K - 1);
+#pragma unroll
+      for (int tp = 0; tp < K - 1; tp++) {
+        const int r = t - (K - 2) + tp;
+        co[tp] = r >= 0 ? a.qkv[(int64_t)r * a.qkv_ld + g] : cin[(int64_t)g * (K - 1) + t + 1 + tp];
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 2 * a.nk) {  // q heads, then k heads
+    const float* v = y + (threadIdx.x < a.nk ? threadIdx.x * a.dk : key_dim + (threadIdx.x - a.nk) * a.dk);
+    float ss = 0.f;
+    for (int i = 0; i < a.dk; i++) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+    nscale[threadIdx.x] = __fdiv_rn(1.f, sqrtf(__fadd_rn(ss, 1e-6f)));
+  }
+  __syncthreads();
+  float* out = a.cv + (int64_t)t * conv_dim;
+  for (int g = threadIdx.x; g < conv_dim; g += 256)
+    out[g] = g < 2 * key_dim ? __fmul_rn(y[g], nscale[g / a.dk]) : y[g];
+  const int ratio = a.nv / a.nk;
+  for (int vh = threadIdx.x; vh < a.nv; vh += 256) {
+    const int kh = a.tiled_heads ? vh % a.nk : vh / ratio;
+    const int rep = a.tiled_heads ? vh / a.nk : vh % ratio;
+    int bi = vh, ai = a.nv + vh;
+    if (a.ba_interleaved) {
+      bi = kh * 2 * ratio + rep;
+      ai = kh * 2 * ratio + ratio + rep;
+    }
+    const float b = a.ba[(int64_t)t * a.ba_ld + bi], al = a.ba[(int64_t)t * a.ba_ld + ai];
+    a.bl[(int64_t)t * 2 * a.nv + vh] = sigmoid_c(b);
+    a.bl[(int64_t)t * 2 * a.nv + a.nv + vh] = __fmul_rn(L.ssm_a[vh], softplus_c(__fadd_rn(al, L.dt_bias[vh])));
+  }
+}
+
+// Sum of the eight parts of a column (lanes 8c .. 8c+7):
+// ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)); every lane of the group gets it.
+__device__ __forceinline__ float parts_sum(float v) {
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+  v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+  return v;
+}
+
+// grid (nv, dv / 32), 256 threads: warp w owns columns 4w .. 4w+3 of the
+// CTA's 32; lane = 8 * column + part.  Part p holds key rows
+// [p*DK/8, (p+1)*DK/8) of its column of the state in registers.
+template <int DK>
+__global__ void __launch_bounds__(256, 1) dn_chunk_kernel(DeltaChunkArgs a) {
+  constexpr int KP = DK / 8;
+  constexpr int KS = DK + 1;  // padded rows of k and q in shared memory
+  extern __shared__ float sm[];
+  float* Ks = sm;                       // [kChunk][KS]
+  float* Qs = Ks + kChunk * KS;         // [kChunk][KS]
+  float* A = Qs + kChunk * KS;          // [kChunk][kChunk] beta_t r(t,s) k_t.k_s (s < t)
+  float* M = A + kChunk * kChunk;       // [kChunk][kChunk] r(t,s) q_t.k_s (s <= t)
+  float* D = M + kChunk * kChunk;       // [kChunk][32] delta
+  float* Vs = D + kChunk * 32;          // [kChunk][32]
+  float* Ls = Vs + kChunk * 32;         // [kChunk] cumulative log-decay
+  float* Es = Ls + kChunk;              // [kChunk] e^{L_t}
+  float* Bs = Es + kChunk;              // [kChunk] beta
+  float* Ws = Bs + kChunk;              // [kChunk] r(C-1, s)
+  // then [kChunk][32] S0^T k_t and [kChunk][32] S0^T q_t (Ps, Rs below)
+  const DeltaNetLayer& L = *a.layers;
+  const int vh = blockIdx.x, DV = a.dv;
+  const int ratio = a.nv / a.nk;
+  const int kh = a.tiled_heads ? vh % a.nk : vh / ratio;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int p = lane & 7, cl = 4 * warp + (lane >> 3);  // part, column within the CTA's 32
+  const int col = blockIdx.y * 32 + cl;                  // column of the head
+  const int i0 = p * KP;
+  const int key_dim = a.nk * DK, conv_dim = 2 * key_dim + a.nv * DV;
+  float* base = L.rec_state + (int64_t)vh * DK * DV + col;
+  float S[KP];
+#pragma unroll
+  for (int ii = 0; ii < KP; ii++) S[ii] = base[(int64_t)(i0 + ii) * DV];
+  // replay the committed rows of the previous pass (S = S g + k delta)
+  const int pend = *a.pending;
+  const float* rec_head = L.rec_log + (int64_t)vh * kMaxRowsDelta * a.rec_stride;
+  for (int r = 0; r < pend; r++) {
+    const float* rc = rec_head + (int64_t)r * a.rec_stride;
+    const float decay = rc[DK + DV], delta = rc[DK + col];
+#pragma unroll
+    for (int ii = 0; ii < KP; ii++) S[ii] = __fadd_rn(__fmul_rn(S[ii], decay), __fmul_rn(rc[i0 + ii], delta));
+  }
+  const float qscale = __fdiv_rn(1.f, sqrtf((float)DK));
+  for (int c0 = 0; c0 < a.rows; c0 += kChunk) {
+    const int C = min(kChunk, a.rows - c0);
+    __syncthreads();  // the previous chunk's shared rows are no longer read
+    for (int e = threadIdx.x; e < C * DK; e += 256) {
+      const int t = e / DK, i = e % DK;
+      const float* row = a.cv + (int64_t)(c0 + t) * conv_dim;
+      Qs[t * KS + i] = row[kh * DK + i];
+      Ks[t * KS + i] = row[key_dim + kh * DK + i];
+    }
+    for (int e = threadIdx.x; e < C * 32; e += 256) {
+      const int t = e / 32, c = e % 32;
+      Vs[e] = a.cv[(int64_t)(c0 + t) * conv_dim + 2 * key_dim + vh * DV + blockIdx.y * 32 + c];
+    }
+    if (threadIdx.x == 0) {
+      float l = 0.f;
+      for (int t = 0; t < C; t++) {
+        l = __fadd_rn(l, a.bl[(int64_t)(c0 + t) * 2 * a.nv + a.nv + vh]);
+        Ls[t] = l;
+        Es[t] = exp_ref(l);
+        Bs[t] = a.bl[(int64_t)(c0 + t) * 2 * a.nv + vh];
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x < C) Ws[threadIdx.x] = exp_ref(__fsub_rn(Ls[C - 1], Ls[threadIdx.x]));
+    {
+      // q_t.k_s and k_t.k_s for a 4 x 4 tile of (t, s) per thread: 32
+      // independent sums, each over i in order
+      const int tt = (threadIdx.x >> 4) * 4, ss = (threadIdx.x & 15) * 4;
+      float qk[4][4], kk[4][4];
+#pragma unroll
+      for (int x = 0; x < 4; x++)
+#pragma unroll
+        for (int y = 0; y < 4; y++) qk[x][y] = kk[x][y] = 0.f;
+      if (tt < C && ss <= tt + 3 && ss < C) {
+#pragma unroll 4
+        for (int i = 0; i < DK; i++) {
+          float qv[4], kv[4], sv[4];
+#pragma unroll
+          for (int x = 0; x < 4; x++) {
+            qv[x] = Qs[(tt + x) * KS + i];
+            kv[x] = Ks[(tt + x) * KS + i];
+            sv[x] = Ks[(ss + x) * KS + i];
+          }
+#pragma unroll
+          for (int x = 0; x < 4; x++)
+#pragma unroll
+            for (int y = 0; y < 4; y++) {
+              qk[x][y] = __fadd_rn(qk[x][y], __fmul_rn(qv[x], sv[y]));
+              kk[x][y] = __fadd_rn(kk[x][y], __fmul_rn(kv[x], sv[y]));
+            }
+        }
+      }
+#pragma unroll
+      for (int x = 0; x < 4; x++)
+#pragma unroll
+        for (int y = 0; y < 4; y++) {
+          const int t = tt + x, s2 = ss + y;
+          float m = 0.f, aa = 0.f;
+          if (t < C && s2 <= t) {
+            const float r = exp_ref(__fsub_rn(Ls[t], Ls[s2]));
+            m = __fmul_rn(r, qk[x][y]);
+            if (s2 < t) aa = __fmul_rn(__fmul_rn(Bs[t], r), kk[x][y]);
+          }
+          M[t * kChunk + s2] = m;
+          A[t * kChunk + s2] = aa;
+        }
+    }
+    // S0^T k_t and S0^T q_t of every row (independent of delta): eight parts
+    float* Ps = Ws + kChunk;
+    float* Rs = Ps + kChunk * 32;
+    for (int t = 0; t < C; t++) {
+      const float* kt = Ks + t * KS + i0;
+      const float* qt = Qs + t * KS + i0;
+      float pk = 0.f, pq = 0.f;
+#pragma unroll
+      for (int ii = 0; ii < KP; ii++) {
+        pk = __fadd_rn(pk, __fmul_rn(S[ii], kt[ii]));
+        pq = __fadd_rn(pq, __fmul_rn(S[ii], qt[ii]));
+      }
+      pk = parts_sum(pk);
+      pq = parts_sum(pq);
+      if (p == 0) {
+        Ps[t * 32 + cl] = pk;
+        Rs[t * 32 + cl] = pq;
+      }
+    }
+    __syncthreads();
+    // forward substitution, rows in order (a column's eight lanes sit in one warp)
+    for (int t = 0; t < C; t++) {
+      const float Bv = __fmul_rn(Bs[t], __fsub_rn(Vs[t * 32 + cl], __fmul_rn(Es[t], Ps[t * 32 + cl])));
+      float sub = 0.f;
+      for (int s2 = p; s2 < t; s2 += 8) sub = __fadd_rn(sub, __fmul_rn(A[t * kChunk + s2], D[s2 * 32 + cl]));
+      const float delta = __fsub_rn(Bv, parts_sum(sub));
+      if (p == 0) D[t * 32 + cl] = delta;
+      __syncwarp();
+    }
+    // outputs of every row
+    for (int t = 0; t < C; t++) {
+      float os = 0.f;
+      for (int s2 = p; s2 <= t; s2 += 8) os = __fadd_rn(os, __fmul_rn(M[t * kChunk + s2], D[s2 * 32 + cl]));
+      const float o = __fmul_rn(qscale, __fadd_rn(__fmul_rn(Es[t], Rs[t * 32 + cl]), parts_sum(os)));
+      if (p == 0) a.o[(int64_t)(c0 + t) * a.o_ld + vh * DV + col] = o;
+    }
+    __syncwarp();
+    // S = e^{L_{C-1}} S + sum_s (r(C-1,s) k_s[i]) delta_s
+    const float eC = Es[C - 1];
+#pragma unroll
+    for (int ii = 0; ii < KP; ii++) S[ii] = __fmul_rn(eC, S[ii]);
+    for (int s = 0; s < C; s++) {
+      const float ws = Ws[s], ds = D[s * 32 + cl];
+      const float* ks = Ks + s * KS + i0;
+#pragma unroll
+      for (int ii = 0; ii < KP; ii++) S[ii] = __fadd_rn(S[ii], __fmul_rn(__fmul_rn(ws, ks[ii]), ds));
+    }
+  }
+#pragma unroll
+  for (int ii = 0; ii < KP; ii++) base[(int64_t)(i0 + ii) * DV] = S[ii];
+}
+
+// grid (rows): the gated RMSNorm of every value head of row t
+// (src/qwen/norm.rs:16-25), the sequential kernel's formula.
+__global__ void __launch_bounds__(256) dn_gated_kernel(DeltaChunkArgs a) {
+  __shared__ float den[128];
+  const int t = blockIdx.x;
+  const float* o = a.o + (int64_t)t * a.o_ld;
+  for (int vh = threadIdx.x; vh < a.nv; vh += 256) {
+    float ss = 0.f;
+    for (int i = 0; i < a.dv; i++) ss = __fadd_rn(ss, __fmul_rn(o[vh * a.dv + i], o[vh * a.dv + i]));
+    den[vh] = sqrtf(__fadd_rn(__fmul_rn(ss, a.inv_dv), a.eps));
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < a.nv * a.dv; e += 256) {
+    const float zz = a.z[(int64_t)t * a.z_ld + e];
+    const float silu = __fdiv_rn(zz, __fadd_rn(1.f, exp_ref(-zz)));
+    a.g_out[(int64_t)t * a.g_ld + e] =
+        __fmul_rn(__fmul_rn(__fdiv_rn(o[e], den[e / a.dv]), a.norm_w[e % a.dv]), silu);
+  }
+}
+
+size_t chunk_smem(int dk) {
+  return (size_t)(2 * kChunk * (dk + 1) + 2 * kChunk * kChunk + 4 * kChunk * 32 + 4 * kChunk) * sizeof(float);
+}
+
+template <int DK>
+cudaError_t launch_chunk(const DeltaChunkArgs& a, cudaStream_t st) {
+  static std::mutex mu;
+  static bool done[64] = {};
+  const cudaError_t e = once_per_device(done, mu, [] {
+    return cudaFuncSetAttribute(dn_chunk_kernel<DK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)chunk_smem(DK));
+  });
+  if (e != cudaSuccess) return e;
+  dn_chunk_kernel<DK><<<dim3(a.nv, a.dv / 32), 256, chunk_smem(DK), st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int K>
+cudaError_t launch_prep(const DeltaChunkArgs& a, size_t smem, cudaStream_t st) {
+  static std::mutex mu;
+  static bool done[64] = {};
+  const cudaError_t e = once_per_device(done, mu, [] {
+    return cudaFuncSetAttribute(dn_prep_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  });
+  if (e != cudaSuccess) return e;
+  dn_prep_kernel<K><<<a.rows, 256, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool deltanet_chunk_supported(int nk, int nv, int dk, int dv, int conv_k) {
+  return (dk == 64 || dk == 128) && dv % 32 == 0 && dv >= 32 && dv <= 128 && nv <= 128 && 2 * nk <= 64 && conv_k >= 2 &&
+         conv_k <= 4 && (size_t)(2 * nk * dk + nv * dv) * 4 <= 200 * 1024;
+}
+
+cudaError_t deltanet_chunk_launch(const DeltaChunkArgs& a, cudaStream_t st) {
+  if (a.rows < 1 || !deltanet_chunk_supported(a.nk, a.nv, a.dk, a.dv, a.conv_k) ||
+      a.rec_stride != deltanet_rec_stride(a.dk, a.dv) || !a.cv || !a.bl || !a.o || !a.g_out || !a.z || !a.norm_w)
+    return cudaErrorInvalidValue;
+  const size_t smem = (size_t)(2 * a.nk * a.dk + a.nv * a.dv) * sizeof(float);
+  cudaError_t e;
+  switch (a.conv_k) {
+    case 2: e = launch_prep<2>(a, smem, st); break;
+    case 3: e = launch_prep<3>(a, smem, st); break;
+    default: e = launch_prep<4>(a, smem, st); break;
+  }
+  if (e != cudaSuccess) return e;
+  e = a.dk == 128 ? launch_chunk<128>(a, st) : launch_chunk<64>(a, st);
+  if (e != cudaSuccess) return e;
+  dn_gated_kernel<<<a.rows, 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace iq

@@ -117,8 +117,18 @@ __global__ void __launch_bounds__(256) f32_rows_kernel(const float* __restrict__
   for (int g = blockIdx.y * 64; g < g1; g += 8) {
     const int k = min(8, g1 - g);
     __syncthreads();
-    for (int i = threadIdx.x; i < k * c4; i += 256)
-      xs4[i] = *reinterpret_cast<const float4*>(x + (int64_t)(g + i / c4) * ldx + 4 * (i % c4));
+    // eight loads in flight per thread before their stores
+    for (int i0 = threadIdx.x; i0 < k * c4; i0 += 256 * 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int i = i0 + 256 * u;
+        if (i < k * c4) v[u] = *reinterpret_cast<const float4*>(x + (int64_t)(g + i / c4) * ldx + 4 * (i % c4));
+      }
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+        if (i0 + 256 * u < k * c4) xs4[i0 + 256 * u] = v[u];
+    }
     __syncthreads();
     if (r >= rows) continue;
     float acc[8];

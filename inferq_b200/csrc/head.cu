@@ -100,6 +100,42 @@ __global__ void __launch_bounds__(256) argmax_part_kernel(HeadArgs a) {
   }
 }
 
+// grid (rows): the argmax of each of many rows (the wide pass), one CTA per
+// row with the same comparison (better(): the tie rule) as the split form.
+__global__ void __launch_bounds__(256) rows_argmax_kernel(const float* __restrict__ logits, int64_t ld, int vocab,
+                                                          int* __restrict__ out) {
+  const int t = blockIdx.x;
+  const float* l = logits + (int64_t)t * ld;
+  Best b = {-INFINITY, -1, -INFINITY, 0.f};
+  const bool vec = ((ld | vocab) & 3) == 0 && (((uintptr_t)logits & 15) == 0);
+  const int n4 = vec ? vocab / 4 : 0;
+  for (int i0 = threadIdx.x; i0 < n4; i0 += 256 * 4) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+      if (i0 + 256 * u < n4) v[u] = reinterpret_cast<const float4*>(l)[i0 + 256 * u];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      if (i0 + 256 * u >= n4) break;
+      const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        if (!isfinite(e[q])) continue;
+        Best x = {e[q], 4 * (i0 + 256 * u) + q, -INFINITY, 1.f};
+        b = merge(b, x, false);
+      }
+    }
+  }
+  for (int i = 4 * n4 + threadIdx.x; i < vocab; i += 256) {
+    const float v = l[i];
+    if (!isfinite(v)) continue;
+    Best x = {v, i, -INFINITY, 1.f};
+    b = merge(b, x, false);
+  }
+  b = block_best(b, false);
+  if (threadIdx.x == 0) out[t] = b.i;
+}
+
 // One CTA: final argmax per row, then accept and the authoritative token.
 __global__ void __launch_bounds__(256) accept_kernel(HeadArgs a) {
   pdl_wait();
@@ -188,6 +224,12 @@ cudaError_t embed_launch(int dt, const uint8_t* w, int64_t row_bytes, int cols, 
 
 cudaError_t argmax_launch(const HeadArgs& a, cudaStream_t st, bool pdl) {
   return launch_pdl(argmax_part_kernel, dim3(a.rows, a.nparts), dim3(256), 0, st, pdl, a);
+}
+
+cudaError_t rows_argmax_launch(const float* logits, int64_t ld, int rows, int vocab, int* out, cudaStream_t st) {
+  if (rows < 1 || vocab < 1) return cudaErrorInvalidValue;
+  rows_argmax_kernel<<<rows, 256, 0, st>>>(logits, ld, vocab, out);
+  return cudaGetLastError();
 }
 
 cudaError_t accept_launch(const HeadArgs& a, cudaStream_t st, bool pdl) {

@@ -53,6 +53,30 @@ int deltanet_rec_stride(int dk, int dv);
 bool deltanet_supported(int dk, int dv);
 cudaError_t deltanet_launch(const DeltaNetArgs& a, cudaStream_t st, bool pdl);
 
+// The chunked recurrence over the rows of a wide pass before its final block
+// (deltanet_chunk.cu): advances the layer's base state over `rows` rows
+// (after replaying `pending` records), writes the conv history after them to
+// conv slot cur + 1, and the gated-norm output rows to g_out.
+struct DeltaChunkArgs {
+  const DeltaNetLayer* layers;
+  const float* qkv;  int qkv_ld;
+  const float* ba;   int ba_ld;
+  int rows;
+  int nk, nv, dk, dv, conv_k;
+  int tiled_heads, ba_interleaved, rec_stride;
+  const int* cur;
+  const int* pending;
+  float* cv;                    // scratch [rows][conv_dim]: normalized q, k, then v
+  float* bl;                    // scratch [rows][2 nv]: beta, then log-decay
+  float* o;  int o_ld;          // scratch: recurrent outputs [rows][o_ld]
+  const float* z;  int z_ld;
+  const float* norm_w;
+  float eps, inv_dv;
+  float* g_out;  int g_ld;
+};
+bool deltanet_chunk_supported(int nk, int nv, int dk, int dv, int conv_k);
+cudaError_t deltanet_chunk_launch(const DeltaChunkArgs& a, cudaStream_t st);
+
 struct GatedNormArgs {
   const float* o;  int o_ld;
   const float* z;  int z_ld;
@@ -200,6 +224,9 @@ cudaError_t mtp_step_launch(const MtpStepArgs& a, cudaStream_t st, bool pdl);
 // *p = v (add = false) or *p += v, in stream order
 cudaError_t set_int_launch(int* p, int v, bool add, cudaStream_t st, bool pdl);
 cudaError_t accept_launch(const HeadArgs& a, cudaStream_t st, bool pdl);
+// out[t] = argmax of logits row t (ld apart) for `rows` rows, the accept
+// kernel's tie rule; one CTA per row.
+cudaError_t rows_argmax_launch(const float* logits, int64_t ld, int rows, int vocab, int* out, cudaStream_t st);
 
 // cur = (cur + committed) mod kStateRing; pos += committed;
 // pending = committed (the DeltaNet records the next pass replays)

@@ -87,11 +87,18 @@ __global__ void wide_combine_kernel(float* __restrict__ hidden, int H, int topk,
   *h = __fadd_rn(*h, __fadd_rn(acc, __fmul_rn(ysh[(int64_t)r * H + i], selector)));
 }
 
-// per attention slice j of `rows` rows: [j] the slice's first position
+// [0] the conv ring index and [1] the pending records (none) of the
+// sequential DeltaNet launch over a chunk's final block (the chunked launch
+// before it leaves the history after the prefix in slot cur + 1); [2 + j]
+// the first position of attention slice j of `rows` rows
 __global__ void wide_ctrl_kernel(const int* __restrict__ ctrl, int* __restrict__ wc, int slices, int rows) {
   const int j = threadIdx.x;
+  if (j == 0) {
+    wc[0] = (ctrl[1] + 1) % kStateRing;
+    wc[1] = 0;
+  }
   if (j >= slices) return;
-  wc[j] = ctrl[0] + rows * j;
+  wc[2 + j] = ctrl[0] + rows * j;
 }
 
 // The chunk's rows before its final block are committed for good: the conv
@@ -179,34 +186,76 @@ int wide_delta(iq_state* s, const Layer& L, int li, int n) {
     TRY_IQ(wide_project(s, D.beta, W.xn.as<float>(), c.hidden_size, n, W.ba.as<float>(), 2 * nv));
     TRY_IQ(wide_project(s, D.alpha, W.xn.as<float>(), c.hidden_size, n, W.ba.as<float>() + nv, 2 * nv));
   }
-  // one launch over every row of the chunk: the recurrence walks them in
-  // order and keeps only the final block for rollback
+  // The rows before the final block of up to 8 run in the chunked form; the
+  // final block runs in the sequential kernel, which keeps its update
+  // records for rollback (when the chunked form does not fit the head
+  // shapes, the sequential kernel takes every row).
+  const int dk = c.linear_key_head_dim, dv = c.linear_value_head_dim;
+  const int last = (n - 1) % kMaxRowsDelta + 1, pre = n - last;
+  const bool chunked = pre > 0 && deltanet_chunk_supported(c.linear_num_key_heads, nv, dk, dv,
+                                                           c.linear_conv_kernel_dim);
+  const int r0 = chunked ? pre : 0;
+  if (chunked) {
+    DeltaChunkArgs h = {};
+    h.layers = s->dn_layers.as<DeltaNetLayer>() + li;
+    h.qkv = qkv;
+    h.qkv_ld = conv_dim;
+    h.ba = W.ba.as<float>();
+    h.ba_ld = 2 * nv;
+    h.rows = pre;
+    h.nk = c.linear_num_key_heads;
+    h.nv = nv;
+    h.dk = dk;
+    h.dv = dv;
+    h.conv_k = c.linear_conv_kernel_dim;
+    h.tiled_heads = c.value_heads_tiled;
+    h.ba_interleaved = D.ba_fused;
+    h.rec_stride = deltanet_rec_stride(dk, dv);
+    h.cur = s->ctrl.as<int>() + 1;
+    h.pending = s->ctrl.as<int>() + 6;
+    IQ_CUDA(W.cv.reserve((size_t)n * conv_dim * 4));
+    IQ_CUDA(W.bl.reserve((size_t)n * 2 * nv * 4));
+    IQ_CUDA(W.dno.reserve((size_t)n * vdim * 4));
+    h.cv = W.cv.as<float>();
+    h.bl = W.bl.as<float>();
+    h.o = W.dno.as<float>();
+    h.o_ld = vdim;
+    h.z = W.z.as<float>();
+    h.z_ld = vdim;
+    h.norm_w = D.norm.p();
+    h.eps = c.rms_norm_eps;
+    h.inv_dv = (float)(1.0 / dv);
+    h.g_out = W.o.as<float>();
+    h.g_ld = vdim;
+    IQ_CUDA(deltanet_chunk_launch(h, s->st));
+  }
   DeltaNetArgs a = {};
   a.layers = s->dn_layers.as<DeltaNetLayer>() + li;
-  a.qkv = qkv;
+  a.qkv = qkv + (int64_t)r0 * conv_dim;
   a.qkv_ld = conv_dim;
-  a.ba = W.ba.as<float>();
+  a.ba = W.ba.as<float>() + (int64_t)r0 * 2 * nv;
   a.ba_ld = 2 * nv;
   a.out = nullptr;
   a.out_ld = vdim;
-  a.rows = n;
+  a.rows = n - r0;
   a.nk = c.linear_num_key_heads;
   a.nv = nv;
-  a.dk = c.linear_key_head_dim;
-  a.dv = c.linear_value_head_dim;
+  a.dk = dk;
+  a.dv = dv;
   a.conv_k = c.linear_conv_kernel_dim;
   a.tiled_heads = c.value_heads_tiled;
   a.ba_interleaved = D.ba_fused;
   a.rec_stride = deltanet_rec_stride(a.dk, a.dv);
   a.timeout_flag = qmv_timeout_flag();
-  a.cur = s->ctrl.as<int>() + 1;
-  a.pending = s->ctrl.as<int>() + 6;
-  a.z = W.z.as<float>();
+  // after the chunked prefix: the history in slot cur + 1, nothing to replay
+  a.cur = chunked ? W.ctrl.as<int>() : s->ctrl.as<int>() + 1;
+  a.pending = chunked ? W.ctrl.as<int>() + 1 : s->ctrl.as<int>() + 6;
+  a.z = W.z.as<float>() + (int64_t)r0 * vdim;
   a.z_ld = vdim;
   a.norm_w = D.norm.p();
   a.eps = c.rms_norm_eps;
   a.inv_dv = (float)(1.0 / c.linear_value_head_dim);
-  a.g_out = W.o.as<float>();
+  a.g_out = W.o.as<float>() + (int64_t)r0 * vdim;
   a.g_ld = vdim;
   IQ_CUDA(deltanet_launch(a, s->st, false));
   TRY_IQ(wide_project(s, D.out, W.o.as<float>(), vdim, n, W.y.as<float>(), c.hidden_size));
@@ -248,7 +297,7 @@ int wide_attention(iq_state* s, const Layer& L, int fi, int n) {
     a.rotary_dim = c.rotary_dim;
     a.theta = c.rope_theta;
     a.eps = c.rms_norm_eps;
-    a.pos = W.ctrl.as<int>() + j;
+    a.pos = W.ctrl.as<int>() + 2 + j;
     a.chunk_ctas = s->max_chunks;
     IQ_CUDA(attn_prep_launch(a, s->st, false));
     IQ_CUDA(attn_scan_launch(a, s->st, false));
@@ -424,7 +473,7 @@ int alloc_wide(iq_state* s, int n) {
   IQ_CUDA(W.kp.reserve(n * kvd * 4));
   IQ_CUDA(W.vp.reserve(n * kvd * 4));
   IQ_CUDA(W.tokens.reserve(n * 4));
-  IQ_CUDA(W.ctrl.reserve(ceil_div(n, 8) * 4));
+  IQ_CUDA(W.ctrl.reserve((2 + ceil_div(n, 8)) * 4));
   if (c.num_attention_heads > 0 && s->m->n_linear < c.num_hidden_layers) {
     // attention slices: as many rows as the scan's shared memory and a
     // partials buffer of at most 512 MB hold
@@ -444,7 +493,7 @@ int alloc_wide(iq_state* s, int n) {
   IQ_CUDA(W.rw.reserve(n * topk * 4));
   IQ_CUDA(W.ysh.reserve(n * H * 4));
   IQ_CUDA(W.gush.reserve(n * 2 * Fs * 4));
-  IQ_CUDA(W.argres.reserve(8 * 4));
+  IQ_CUDA(W.argres.reserve(n * 4));
   if (!W.h_routes) IQ_CUDA(cudaMallocHost(&W.h_routes, (size_t)kWideRows * topk * 4));
   return IQ_OK;
 }
@@ -480,23 +529,8 @@ int wide_chunk(iq_state* s, const uint32_t* tokens, int n, float* logits, float*
     if (logits)
       IQ_CUDA(cudaMemcpyAsync(logits + (int64_t)row0 * V, W.logits.p, (size_t)n * V * 4, cudaMemcpyDeviceToHost, st));
     if (argmax) {
-      for (int r0 = 0; r0 < n; r0 += 8) {
-        HeadArgs h = {};
-        h.logits = W.logits.as<float>() + (int64_t)r0 * V;
-        h.logits_ld = V;
-        h.rows = std::min(8, n - r0);
-        h.vocab = V;
-        h.part_val = s->pval.as<float>();
-        h.part_idx = s->pidx.as<int>();
-        h.nparts = 128;
-        h.argmax = s->argmax.as<int>();
-        h.tokens = s->tokens.as<int32_t>();
-        h.verify = 0;
-        h.result = W.argres.as<int>();
-        IQ_CUDA(argmax_launch(h, st, false));
-        IQ_CUDA(accept_launch(h, st, false));
-        IQ_CUDA(cudaMemcpyAsync(argmax + row0 + r0, s->argmax.p, (size_t)h.rows * 4, cudaMemcpyDeviceToHost, st));
-      }
+      IQ_CUDA(rows_argmax_launch(W.logits.as<float>(), V, n, V, W.argres.as<int>(), st));
+      IQ_CUDA(cudaMemcpyAsync(argmax + row0, W.argres.p, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
     }
   }
   const int last = (n - 1) % kMaxRowsDelta + 1;  // the final block the DeltaNet kernels keep

@@ -172,9 +172,43 @@ static int g_perturb = 0;
 void or_set_perturb(int on) { g_perturb = on; }
 
 /* gguf_rms_norm (quantized_layer.rs:230-236): x / sqrt(mean(x^2) + eps) * w */
+/* The device row-prep kernel's sum of squares (inferq_b200/csrc/layout.cu
+ * prep_rows_kernel), used by the device orders: thread (warp w, lane l) of
+ * 256 takes the 256-element blocks b = w + 8j and in each the elements
+ * 32 (l & 7) + 16 (i / 4) + 4 (l >> 3) + (i % 4), i = 0..7, as fused
+ * multiply-adds; each warp's lanes combine by the xor butterfly 16, 8, 4, 2,
+ * 1; the eight warp sums are added in warp order. */
+static float dev_sum_squares(const float* x, int n) {
+    const int nb = (n + 255) / 256;
+    float red[8];
+    for (int wp = 0; wp < 8; wp++) {
+        float lanes[32], nx[32];
+        for (int l = 0; l < 32; l++) {
+            float acc = 0.f;
+            for (int b = wp; b < nb; b += 8)
+                for (int i = 0; i < 8; i++) {
+                    int idx = b * 256 + 32 * (l & 7) + 16 * (i / 4) + 4 * (l >> 3) + (i % 4);
+                    float v = idx < n ? x[idx] : 0.f;
+                    acc = fmaf(v, v, acc);
+                }
+            lanes[l] = acc;
+        }
+        for (int m = 16; m >= 1; m >>= 1) {
+            for (int l = 0; l < 32; l++) nx[l] = lanes[l] + lanes[l ^ m];
+            memcpy(lanes, nx, sizeof lanes);
+        }
+        red[wp] = lanes[0];
+    }
+    float t = red[0];
+    for (int i = 1; i < 8; i++) t = t + red[i];
+    return t;
+}
+
 static void rms_norm(const float* x, const float* w, int n, float eps, float* out) {
     float ss = 0.f;
-    for (int i = 0; i < n; i++) ss += x[i] * x[i];
+    if (g_order) ss = dev_sum_squares(x, n);
+    else
+        for (int i = 0; i < n; i++) ss += x[i] * x[i];
     float var = ss * (float)(1.0 / (double)n);
     float den = sqrtf(var + eps);
     for (int i = 0; i < n; i++) out[i] = (x[i] / den) * w[i];
@@ -448,6 +482,87 @@ void or_delta_step(const float* q, const float* k, const float* v, const float* 
                         state + (int64_t)h * dk * dv, out + h * dv);
 }
 
+/* ------------------------------------------------ chunked recurrence */
+/* The device's chunked form of the recurrence for the rows of a wide pass
+ * before its final block (order 2; inferq_b200/csrc/deltanet_chunk.cu
+ * states the algebra).  Same arithmetic as delta_head_step up to f32
+ * rounding order; this restates the device's order exactly: key-dimension
+ * dots sequential, S0^T k / S0^T q in eight parts of dk/8 rows combined as
+ * ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)), sums over s split s = p (mod 8) and
+ * combined the same way, decays as exp of cumulative log-decay differences. */
+static float expd(float x) { return (float)exp((double)x); }
+static float tree8(const float* p) {
+    return ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
+}
+#define CHUNK 64
+/* One value head over C rows: q/k [C][ld_qk], v [C][ld_v], beta/lg [C];
+ * S [dk][dv] advanced in place; o [C][ld_o] raw outputs. */
+static void delta_chunk(const float* q, const float* k, int ld_qk, const float* v, int ld_v, const float* beta,
+                        const float* lg, int C, int dk, int dv, float* S, float* o, int ld_o) {
+    static float A[CHUNK][CHUNK], M[CHUNK][CHUNK], D[CHUNK][128], Lc[CHUNK], E[CHUNK], W[CHUNK];
+    const int kp = dk / 8;
+    const float qscale = 1.f / sqrtf((float)dk);
+    float l = 0.f;
+    for (int t = 0; t < C; t++) { l = l + lg[t]; Lc[t] = l; E[t] = expd(l); }
+    for (int s = 0; s < C; s++) W[s] = expd(Lc[C - 1] - Lc[s]);
+    for (int t = 0; t < C; t++)
+        for (int s = 0; s < C; s++) {
+            float m = 0.f, aa = 0.f;
+            if (s <= t) {
+                float r = expd(Lc[t] - Lc[s]);
+                float qk = 0.f;
+                for (int i = 0; i < dk; i++) qk = qk + q[t * ld_qk + i] * k[s * ld_qk + i];
+                m = r * qk;
+                if (s < t) {
+                    float kk = 0.f;
+                    for (int i = 0; i < dk; i++) kk = kk + k[t * ld_qk + i] * k[s * ld_qk + i];
+                    aa = (beta[t] * r) * kk;
+                }
+            }
+            M[t][s] = m;
+            A[t][s] = aa;
+        }
+    for (int j = 0; j < dv; j++) {
+        for (int t = 0; t < C; t++) {
+            float pk[8], pq[8], ps[8], po[8];
+            for (int p = 0; p < 8; p++) {
+                float a1 = 0.f, a2 = 0.f;
+                for (int ii = 0; ii < kp; ii++) {
+                    int i = p * kp + ii;
+                    a1 = a1 + S[i * dv + j] * k[t * ld_qk + i];
+                    a2 = a2 + S[i * dv + j] * q[t * ld_qk + i];
+                }
+                pk[p] = a1; pq[p] = a2;
+            }
+            float P = tree8(pk), R = tree8(pq);
+            float B = beta[t] * (v[t * ld_v + j] - E[t] * P);
+            for (int p = 0; p < 8; p++) {
+                float acc = 0.f;
+                for (int s = p; s < t; s += 8) acc = acc + A[t][s] * D[s][j];
+                ps[p] = acc;
+            }
+            D[t][j] = B - tree8(ps);
+            for (int p = 0; p < 8; p++) {
+                float acc = 0.f;
+                for (int s = p; s <= t; s += 8) acc = acc + M[t][s] * D[s][j];
+                po[p] = acc;
+            }
+            o[t * ld_o + j] = qscale * (E[t] * R + tree8(po));
+        }
+        for (int i = 0; i < dk; i++) {
+            float acc = E[C - 1] * S[i * dv + j];
+            for (int s = 0; s < C; s++) acc = acc + (W[s] * k[s * ld_qk + i]) * D[s][j];
+            S[i * dv + j] = acc;
+        }
+    }
+}
+static int chunk_supported(const or_config* c) {
+    int nk = c->linear_num_key_heads, nv = c->linear_num_value_heads, dk = c->linear_key_head_dim;
+    int dv = c->linear_value_head_dim, K = c->linear_conv_kernel_dim;
+    return (dk == 64 || dk == 128) && dv % 32 == 0 && dv >= 32 && dv <= 128 && nv <= 128 && 2 * nk <= 64 &&
+           K >= 2 && K <= 4 && (2 * nk * dk + nv * dv) * 4 <= 200 * 1024;
+}
+
 /* The DeltaNet mixer over R rows x [R][H] -> out [R][H]
  * (quantized_deltanet.rs:517-703): projections of all rows, then per row in
  * order the conv step, L2 norms, beta/decay and the delta rule, then the
@@ -464,7 +579,6 @@ static void delta_rows(const or_model* m, const layer_t* L, lstate_t* st, const 
     float* cv = (float*)malloc((size_t)conv_dim * 4);
     float* qr = (float*)malloc((size_t)nv * dk * 4);
     float* kr = (float*)malloc((size_t)nv * dk * 4);
-    float* o = (float*)malloc((size_t)vd * 4);
     float* g = (float*)malloc((size_t)R * vd * 4);
     matvec_k(&L->qkv, x, R, proj);
     matvec_k(&L->z, x, R, z);
@@ -475,7 +589,31 @@ static void delta_rows(const or_model* m, const layer_t* L, lstate_t* st, const 
         matvec_k(&L->alpha, x, R, tmp);
         for (int r = 0; r < R; r++) memcpy(ba + (int64_t)r * 2 * nv + nv, tmp + (int64_t)r * nv, (size_t)nv * 4);
     }
+    /* order 2 over a wide pass: the rows before the final block of up to 8 in
+     * the chunked form (delta_chunk), the final block row by row */
+    const int pre = (g_order == 2 && R > 8 && chunk_supported(c)) ? R - ((R - 1) % 8 + 1) : 0;
+    float* oall = (float*)malloc((size_t)R * vd * 4);
+    float *cq = NULL, *ck = NULL, *cvv = NULL, *cb = NULL, *cl = NULL;
+    if (pre > 0) {
+        cq = (float*)malloc((size_t)pre * nv * dk * 4);
+        ck = (float*)malloc((size_t)pre * nv * dk * 4);
+        cvv = (float*)malloc((size_t)pre * vd * 4);
+        cb = (float*)malloc((size_t)pre * nv * 4);
+        cl = (float*)malloc((size_t)pre * nv * 4);
+    }
     for (int r = 0; r < R; r++) {
+        if (r == pre && pre > 0) {
+            for (int vh = 0; vh < nv; vh++) {
+                float bh[CHUNK], lh[CHUNK];
+                for (int c0 = 0; c0 < pre; c0 += CHUNK) {
+                    int C = pre - c0 < CHUNK ? pre - c0 : CHUNK;
+                    for (int t = 0; t < C; t++) { bh[t] = cb[(c0 + t) * nv + vh]; lh[t] = cl[(c0 + t) * nv + vh]; }
+                    delta_chunk(cq + (int64_t)c0 * nv * dk + vh * dk, ck + (int64_t)c0 * nv * dk + vh * dk, nv * dk,
+                                cvv + (int64_t)c0 * vd + vh * dv, vd, bh, lh, C, dk, dv,
+                                st->rec + (int64_t)vh * dk * dv, oall + (int64_t)c0 * vd + vh * dv, vd);
+                }
+            }
+        }
         const float* bar = ba + (int64_t)r * 2 * nv;
         or_conv_step(proj + (int64_t)r * conv_dim, L->conv_w, conv_dim, K, st->conv, cv);
         float* q = cv; float* k = cv + kd; const float* v = cv + 2 * kd;
@@ -494,16 +632,26 @@ static void delta_rows(const or_model* m, const layer_t* L, lstate_t* st, const 
                 else { b = bar[vh]; al = bar[nv + vh]; }
                 float beta = sigmoid_ref(b);
                 float gdec = L->ssm_a[vh] * softplus_ref(al + L->dt_bias[vh]);
-                delta_head_step(qr + vh * dk, kr + vh * dk, v + vh * dv, gdec, beta, dk, dv, q_scale,
-                                st->rec + (int64_t)vh * dk * dv, o + vh * dv);
+                if (r < pre) {
+                    memcpy(cq + ((int64_t)r * nv + vh) * dk, q + kh * dk, (size_t)dk * 4);
+                    memcpy(ck + ((int64_t)r * nv + vh) * dk, k + kh * dk, (size_t)dk * 4);
+                    memcpy(cvv + (int64_t)r * vd + vh * dv, v + vh * dv, (size_t)dv * 4);
+                    cb[r * nv + vh] = beta;
+                    cl[r * nv + vh] = gdec;
+                } else {
+                    delta_head_step(qr + vh * dk, kr + vh * dk, v + vh * dv, gdec, beta, dk, dv, q_scale,
+                                    st->rec + (int64_t)vh * dk * dv, oall + (int64_t)r * vd + vh * dv);
+                }
             }
         if (st->snap_conv && r + 1 < R) {  /* entry state of the next row */
             memcpy(st->snap_conv[r], st->conv, (size_t)conv_dim * (K - 1) * 4);
             memcpy(st->snap_rec[r], st->rec, (size_t)nv * dk * dv * 4);
         }
+    }
+    for (int r = 0; r < R; r++) {
         /* rms_norm_gated (norm.rs:16-25) per value head */
         for (int vh = 0; vh < nv; vh++) {
-            const float* oh = o + vh * dv;
+            const float* oh = oall + (int64_t)r * vd + vh * dv;
             float ss = 0.f;
             for (int j = 0; j < dv; j++) ss += oh[j] * oh[j];
             float den = sqrtf(ss * (float)(1.0 / dv) + c->rms_norm_eps);
@@ -514,8 +662,9 @@ static void delta_rows(const or_model* m, const layer_t* L, lstate_t* st, const 
             }
         }
     }
+    free(oall); free(cq); free(ck); free(cvv); free(cb); free(cl);
     matvec_k(&L->out, g, R, out);
-    free(proj); free(z); free(ba); free(tmp); free(cv); free(qr); free(kr); free(o); free(g);
+    free(proj); free(z); free(ba); free(tmp); free(cv); free(qr); free(kr); free(g);
 }
 
 /* ----------------------------------------------------------- attention */
@@ -761,8 +910,10 @@ int or_forward(const or_model* m, or_state* s, const uint32_t* tokens, int rows,
     if (s->snap_rows > 0 && rows > s->snap_rows) return -3;
     s->snap_pos0 = s->position;
     s->snap_taken = rows;
-    for (int r0 = 0; r0 < rows; r0 += 8) {
-        const int R = rows - r0 < 8 ? rows - r0 : 8;
+    /* order 2 restates the wide pass: from 64 rows, passes of up to 512 */
+    const int pass = (g_order == 2 && rows >= 64) ? 512 : 8;
+    for (int r0 = 0; r0 < rows; r0 += pass) {
+        const int R = rows - r0 < pass ? rows - r0 : pass;
         float* h = (float*)malloc((size_t)R * H * 4);
         float* hn = (float*)malloc((size_t)R * H * 4);
         int* ex = (int*)malloc((size_t)R * topk * sizeof(int));

@@ -1,15 +1,17 @@
 """The wide prefill pass (iq_forward from 64 rows: tensor-core projections,
-experts grouped by expert, the recurrence and attention in their sequential
-kernels) against the CPU oracle and against the 8-row passes.
+experts grouped by expert, the DeltaNet recurrence in its chunked form up to
+the final block of each 512-row chunk, attention in its sequential kernels)
+against the CPU oracle run in the same order, and against the 8-row passes.
 
-The wide pass sums each dense projection's blocks in one chunk, so it is the
-reference arithmetic up to f32 summation order, not bitwise the 8-row passes
+The wide pass sums each dense projection's blocks in one chunk and runs the
+chunked recurrence, so it is the reference arithmetic up to f32 rounding
+order, not bitwise the 8-row passes
 (the reference's own prefill is not bitwise its split passes either,
 src/runtime.rs:740-747).  Held:
 
 * one decoder layer over 200 rows against the oracle run in the wide pass's
-  accumulation order: median logit error at rounding level, rows beyond
-  2e-2 (listed) no more frequent than the oracle's own order gap makes them;
+  order: median logit error at rounding level (1e-4), rows beyond 2e-2 no
+  more frequent or larger than among the oracle's own rounding variants;
   the whole model and 600 rows across a chunk boundary held to the spread
   of the oracle's own rounding-level variants;
 * the state the wide pass leaves behind continues exactly like a state: a
@@ -77,34 +79,6 @@ def _oracle(om, prompt, order):
     return lg, hd
 
 
-@pytest.mark.parametrize("kind", ["deltanet", "attention"])
-@pytest.mark.parametrize("case", list(CASES))
-def test_wide_prefill_matches_the_oracle_per_layer(cuda, case, kind):
-    """One decoder layer + head over 200 wide rows: the typical row equals
-    the oracle in the wide pass's order to rounding, and rows beyond 2e-2
-    are no more frequent than the gap between the oracle's reference and
-    wide orders makes them (the seeded random model amplifies a single
-    flipped activation rounding; one layer keeps that from compounding)."""
-    cfg = _one_layer(CASES[case](), kind)
-    tensors = list(synth.generate(cfg, seed=31))
-    model, om = Model(cfg, tensors), oracle.OracleModel(cfg, tensors)
-    n = 200
-    prompt = np.random.default_rng(5).integers(0, cfg.vocab_size, n)
-    st = State(model, n + 16)
-    _, lg, _ = st.forward(prompt, logits=True)
-    wide, _ = _oracle(om, prompt, 2)
-    ref, _ = _oracle(om, prompt, 0)
-    e = np.abs(lg - wide).max(axis=1)
-    gap = np.abs(ref - wide).max(axis=1)
-    events = [(i, round(float(e[i]), 4), round(float(gap[i]), 4)) for i in range(n) if e[i] > TOL]
-    print(f"{cfg.name}: wide rows vs the oracle in their order: median {np.median(e):.2e}, max {e.max():.4f}; "
-          f"rows beyond {TOL} (row, error, oracle reference-vs-wide-order gap) {events}")
-    assert np.median(e) <= 1e-4
-    n_gap = int((gap > TOL).sum())
-    assert (e > TOL).sum() <= n_gap + 2 * np.sqrt(n_gap + 1) + 1
-    assert st.position == n
-
-
 VARIANTS = ((0, 0), (2, 1), (2, 2), (1, 0))  # (GEMV order, norm perturbation) besides the wide order (2, 0)
 
 
@@ -116,7 +90,7 @@ def _oracle_variant(om, prompt, order, perturb):
         oracle.set_perturb(0)
 
 
-def _check_spread(name, e, gaps):
+def _check_spread(name, e, gaps, median=None):
     """The device is one more valid order of the same arithmetic: held to
     the spread of the oracle's own variants run over the same rows (typical
     row, count of rows beyond the tolerance, largest error)."""
@@ -124,20 +98,34 @@ def _check_spread(name, e, gaps):
     n_dev, n_var = int((e > TOL).sum()), int((g > TOL).sum(axis=0).max())
     print(f"{name}: rows {len(e)}, median {np.median(e):.2e} (variants {np.median(g, axis=0).max():.2e}), "
           f"max {e.max():.4f} (variants {g.max():.4f}), rows beyond {TOL}: device {n_dev}, one variant at most {n_var}")
-    assert np.median(e) <= max(1e-4, 2 * np.median(g, axis=0).max())
+    assert np.median(e) <= (median if median is not None else max(1e-4, 2 * np.median(g, axis=0).max()))
     assert n_dev <= n_var + 2 * np.sqrt(n_var + 1)
     assert e.max() <= 2 * g.max() + TOL
 
 
-def _whole_model(cfg, model, om, n, seed):
+def _whole_model(cfg, model, om, n, seed, median=None):
     prompt = np.random.default_rng(seed).integers(0, cfg.vocab_size, n)
     st = State(model, n + 16)
     _, lg, _ = st.forward(prompt, logits=True)
     wide, _ = _oracle(om, prompt, 2)
     e = np.abs(lg - wide).max(axis=1)
     gaps = [np.abs(_oracle_variant(om, prompt, o, p) - wide).max(axis=1) for o, p in VARIANTS]
-    _check_spread(f"{cfg.name} {n} rows", e, gaps)
+    _check_spread(f"{cfg.name} {n} rows", e, gaps, median)
     assert st.position == n
+
+
+@pytest.mark.parametrize("kind", ["deltanet", "attention"])
+@pytest.mark.parametrize("case", list(CASES))
+def test_wide_prefill_matches_the_oracle_per_layer(cuda, case, kind):
+    """One decoder layer + head over 200 wide rows against the oracle in the
+    wide pass's order (the chunked recurrence included): the typical row
+    equal to rounding, and rows beyond 2e-2 no more frequent or larger than
+    among the oracle's own rounding-level variants (the seeded random model
+    amplifies a single flipped activation rounding; one layer keeps that
+    from compounding)."""
+    cfg = _one_layer(CASES[case](), kind)
+    tensors = list(synth.generate(cfg, seed=31))
+    _whole_model(cfg, Model(cfg, tensors), oracle.OracleModel(cfg, tensors), 200, 5, median=1e-4)
 
 
 def test_wide_prefill_matches_the_oracle(pair):
