@@ -18,8 +18,9 @@
 // could underflow.  Every sum below has a fixed order, restated by the CPU
 // oracle's wide order:
 //   * dots over the key dimension (k_t.k_s, q_t.k_s): sequential in i;
-//   * S0^T k_t and S0^T q_t per column: eight parts of dk/8 consecutive key
-//     rows, each sequential, combined as ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7));
+//   * S0^T k_t and S0^T q_t per column: eight parts, part p the key rows
+//     i = p (mod 8) in ascending order, combined as
+//     ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7));
 //   * the sums over s: part p takes s = p (mod 8) in ascending order, the
 //     parts combined by the same tree;
 //   * the state update: e^{L_{C-1}} S0, then + (r k_s[i]) delta_s in s order.
@@ -27,7 +28,7 @@
 // Three launches: per-row conv + SiLU, L2 norms, beta and log-decay (the
 // sequential kernel's formulas, so these values are bitwise its own); the
 // chunk kernel, CTA (value head, 32 columns), 256 threads = 32 columns x 8
-// parts, 64-row chunks in order; the gated RMSNorm of the rows.
+// parts, 32-row chunks in order; the gated RMSNorm of the rows.
 #include <mutex>
 #include "model_kernels.cuh"
 #include "devfns.cuh"
@@ -35,7 +36,7 @@
 namespace iq {
 namespace {
 
-constexpr int kChunk = 64;
+constexpr int kChunk = 32;
 
 __device__ __forceinline__ float sigmoid_c(float v) { return __fdiv_rn(1.f, __fadd_rn(1.f, exp_ref(-v))); }
 __device__ __forceinline__ float softplus_c(float v) {
@@ -117,10 +118,10 @@ __device__ __forceinline__ float parts_sum(float v) {
 }
 
 // grid (nv, dv / 32), 256 threads: warp w owns columns 4w .. 4w+3 of the
-// CTA's 32; lane = 8 * column + part.  Part p holds key rows
-// [p*DK/8, (p+1)*DK/8) of its column of the state in registers.
+// CTA's 32; lane = 8 * column + part.  Part p holds key rows i = p (mod 8)
+// of its column of the state in registers (S[ii] is row p + 8 ii).
 template <int DK>
-__global__ void __launch_bounds__(256, 1) dn_chunk_kernel(DeltaChunkArgs a) {
+__global__ void __launch_bounds__(256, 2) dn_chunk_kernel(DeltaChunkArgs a) {
   constexpr int KP = DK / 8;
   constexpr int KS = DK + 1;  // padded rows of k and q in shared memory
   extern __shared__ float sm[];
@@ -142,12 +143,11 @@ __global__ void __launch_bounds__(256, 1) dn_chunk_kernel(DeltaChunkArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int p = lane & 7, cl = 4 * warp + (lane >> 3);  // part, column within the CTA's 32
   const int col = blockIdx.y * 32 + cl;                  // column of the head
-  const int i0 = p * KP;
   const int key_dim = a.nk * DK, conv_dim = 2 * key_dim + a.nv * DV;
   float* base = L.rec_state + (int64_t)vh * DK * DV + col;
   float S[KP];
 #pragma unroll
-  for (int ii = 0; ii < KP; ii++) S[ii] = base[(int64_t)(i0 + ii) * DV];
+  for (int ii = 0; ii < KP; ii++) S[ii] = base[(int64_t)(p + 8 * ii) * DV];
   // replay the committed rows of the previous pass (S = S g + k delta)
   const int pend = *a.pending;
   const float* rec_head = L.rec_log + (int64_t)vh * kMaxRowsDelta * a.rec_stride;
@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(256, 1) dn_chunk_kernel(DeltaChunkArgs a) {
     const float* rc = rec_head + (int64_t)r * a.rec_stride;
     const float decay = rc[DK + DV], delta = rc[DK + col];
 #pragma unroll
-    for (int ii = 0; ii < KP; ii++) S[ii] = __fadd_rn(__fmul_rn(S[ii], decay), __fmul_rn(rc[i0 + ii], delta));
+    for (int ii = 0; ii < KP; ii++) S[ii] = __fadd_rn(__fmul_rn(S[ii], decay), __fmul_rn(rc[p + 8 * ii], delta));
   }
   const float qscale = __fdiv_rn(1.f, sqrtf((float)DK));
   for (int c0 = 0; c0 < a.rows; c0 += kChunk) {
@@ -183,37 +183,30 @@ __global__ void __launch_bounds__(256, 1) dn_chunk_kernel(DeltaChunkArgs a) {
     __syncthreads();
     if (threadIdx.x < C) Ws[threadIdx.x] = exp_ref(__fsub_rn(Ls[C - 1], Ls[threadIdx.x]));
     {
-      // q_t.k_s and k_t.k_s for a 4 x 4 tile of (t, s) per thread: 32
+      // q_t.k_s and k_t.k_s for a 2 x 2 tile of (t, s) per thread: eight
       // independent sums, each over i in order
-      const int tt = (threadIdx.x >> 4) * 4, ss = (threadIdx.x & 15) * 4;
-      float qk[4][4], kk[4][4];
-#pragma unroll
-      for (int x = 0; x < 4; x++)
-#pragma unroll
-        for (int y = 0; y < 4; y++) qk[x][y] = kk[x][y] = 0.f;
-      if (tt < C && ss <= tt + 3 && ss < C) {
-#pragma unroll 4
+      const int tt = (threadIdx.x >> 4) * 2, ss = (threadIdx.x & 15) * 2;
+      float qk[2][2] = {{0.f, 0.f}, {0.f, 0.f}}, kk[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+      if (tt < C && ss <= tt + 1 && ss < C) {
+#pragma unroll 8
         for (int i = 0; i < DK; i++) {
-          float qv[4], kv[4], sv[4];
-#pragma unroll
-          for (int x = 0; x < 4; x++) {
-            qv[x] = Qs[(tt + x) * KS + i];
-            kv[x] = Ks[(tt + x) * KS + i];
-            sv[x] = Ks[(ss + x) * KS + i];
-          }
-#pragma unroll
-          for (int x = 0; x < 4; x++)
-#pragma unroll
-            for (int y = 0; y < 4; y++) {
-              qk[x][y] = __fadd_rn(qk[x][y], __fmul_rn(qv[x], sv[y]));
-              kk[x][y] = __fadd_rn(kk[x][y], __fmul_rn(kv[x], sv[y]));
-            }
+          const float q0 = Qs[tt * KS + i], q1 = Qs[(tt + 1) * KS + i];
+          const float k0 = Ks[tt * KS + i], k1 = Ks[(tt + 1) * KS + i];
+          const float s0 = Ks[ss * KS + i], s1 = Ks[(ss + 1) * KS + i];
+          qk[0][0] = __fadd_rn(qk[0][0], __fmul_rn(q0, s0));
+          qk[0][1] = __fadd_rn(qk[0][1], __fmul_rn(q0, s1));
+          qk[1][0] = __fadd_rn(qk[1][0], __fmul_rn(q1, s0));
+          qk[1][1] = __fadd_rn(qk[1][1], __fmul_rn(q1, s1));
+          kk[0][0] = __fadd_rn(kk[0][0], __fmul_rn(k0, s0));
+          kk[0][1] = __fadd_rn(kk[0][1], __fmul_rn(k0, s1));
+          kk[1][0] = __fadd_rn(kk[1][0], __fmul_rn(k1, s0));
+          kk[1][1] = __fadd_rn(kk[1][1], __fmul_rn(k1, s1));
         }
       }
 #pragma unroll
-      for (int x = 0; x < 4; x++)
+      for (int x = 0; x < 2; x++)
 #pragma unroll
-        for (int y = 0; y < 4; y++) {
+        for (int y = 0; y < 2; y++) {
           const int t = tt + x, s2 = ss + y;
           float m = 0.f, aa = 0.f;
           if (t < C && s2 <= t) {
@@ -229,13 +222,13 @@ __global__ void __launch_bounds__(256, 1) dn_chunk_kernel(DeltaChunkArgs a) {
     float* Ps = Ws + kChunk;
     float* Rs = Ps + kChunk * 32;
     for (int t = 0; t < C; t++) {
-      const float* kt = Ks + t * KS + i0;
-      const float* qt = Qs + t * KS + i0;
+      const float* kt = Ks + t * KS + p;
+      const float* qt = Qs + t * KS + p;
       float pk = 0.f, pq = 0.f;
 #pragma unroll
       for (int ii = 0; ii < KP; ii++) {
-        pk = __fadd_rn(pk, __fmul_rn(S[ii], kt[ii]));
-        pq = __fadd_rn(pq, __fmul_rn(S[ii], qt[ii]));
+        pk = __fadd_rn(pk, __fmul_rn(S[ii], kt[8 * ii]));
+        pq = __fadd_rn(pq, __fmul_rn(S[ii], qt[8 * ii]));
       }
       pk = parts_sum(pk);
       pq = parts_sum(pq);
@@ -268,13 +261,13 @@ __global__ void __launch_bounds__(256, 1) dn_chunk_kernel(DeltaChunkArgs a) {
     for (int ii = 0; ii < KP; ii++) S[ii] = __fmul_rn(eC, S[ii]);
     for (int s = 0; s < C; s++) {
       const float ws = Ws[s], ds = D[s * 32 + cl];
-      const float* ks = Ks + s * KS + i0;
+      const float* ks = Ks + s * KS + p;
 #pragma unroll
-      for (int ii = 0; ii < KP; ii++) S[ii] = __fadd_rn(S[ii], __fmul_rn(__fmul_rn(ws, ks[ii]), ds));
+      for (int ii = 0; ii < KP; ii++) S[ii] = __fadd_rn(S[ii], __fmul_rn(__fmul_rn(ws, ks[8 * ii]), ds));
     }
   }
 #pragma unroll
-  for (int ii = 0; ii < KP; ii++) base[(int64_t)(i0 + ii) * DV] = S[ii];
+  for (int ii = 0; ii < KP; ii++) base[(int64_t)(p + 8 * ii) * DV] = S[ii];
 }
 
 // grid (rows): the gated RMSNorm of every value head of row t

@@ -487,14 +487,15 @@ void or_delta_step(const float* q, const float* k, const float* v, const float* 
  * before its final block (order 2; inferq_b200/csrc/deltanet_chunk.cu
  * states the algebra).  Same arithmetic as delta_head_step up to f32
  * rounding order; this restates the device's order exactly: key-dimension
- * dots sequential, S0^T k / S0^T q in eight parts of dk/8 rows combined as
+ * dots sequential, S0^T k / S0^T q in eight parts (part p: rows i = p mod 8)
+ * combined as
  * ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)), sums over s split s = p (mod 8) and
  * combined the same way, decays as exp of cumulative log-decay differences. */
 static float expd(float x) { return (float)exp((double)x); }
 static float tree8(const float* p) {
     return ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
 }
-#define CHUNK 64
+#define CHUNK 32
 /* One value head over C rows: q/k [C][ld_qk], v [C][ld_v], beta/lg [C];
  * S [dk][dv] advanced in place; o [C][ld_o] raw outputs. */
 static void delta_chunk(const float* q, const float* k, int ld_qk, const float* v, int ld_v, const float* beta,
@@ -528,7 +529,7 @@ static void delta_chunk(const float* q, const float* k, int ld_qk, const float* 
             for (int p = 0; p < 8; p++) {
                 float a1 = 0.f, a2 = 0.f;
                 for (int ii = 0; ii < kp; ii++) {
-                    int i = p * kp + ii;
+                    int i = p + 8 * ii;
                     a1 = a1 + S[i * dv + j] * k[t * ld_qk + i];
                     a2 = a2 + S[i * dv + j] * q[t * ld_qk + i];
                 }
