@@ -18,17 +18,21 @@
 // could underflow.  Every sum below has a fixed order, restated by the CPU
 // oracle's wide order:
 //   * dots over the key dimension (k_t.k_s, q_t.k_s): sequential in i;
-//   * S0^T k_t and S0^T q_t per column: eight parts, part p the key rows
+//   * U_t = beta_t v_t - sum_{s<t} A[t][s] U_s and W_t = (beta_t e_t) k_t -
+//     sum_{s<t} A[t][s] W_s (so delta = U - W S0), each sum in s order;
+//   * W_t S0 and S0^T q_t per column: eight parts, part p the key rows
 //     i = p (mod 8) in ascending order, combined as
 //     ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7));
-//   * the sums over s: part p takes s = p (mod 8) in ascending order, the
-//     parts combined by the same tree;
+//   * the output sum over s: part p takes s = p (mod 8) in ascending order,
+//     the parts combined by the same tree;
 //   * the state update: e^{L_{C-1}} S0, then + (r k_s[i]) delta_s in s order.
 //
-// Three launches: per-row conv + SiLU, L2 norms, beta and log-decay (the
-// sequential kernel's formulas, so these values are bitwise its own); the
-// chunk kernel, CTA (value head, 32 columns), 256 threads = 32 columns x 8
-// parts, 32-row chunks in order; the gated RMSNorm of the rows.
+// Four launches: per-row conv + SiLU, L2 norms, beta and log-decay (the
+// sequential kernel's formulas, so these values are bitwise its own); per
+// (head, 32-row chunk) at once, everything that does not depend on the state
+// (A, M, the decays and the substitutions for U and W); the chunks in order
+// per (head, 16 columns), only the state-dependent products; the gated
+// RMSNorm of the rows.
 #include <mutex>
 #include "model_kernels.cuh"
 #include "devfns.cuh"
@@ -117,33 +121,169 @@ __device__ __forceinline__ float parts_sum(float v) {
   return v;
 }
 
-// grid (nv, dv / 32), 256 threads: warp w owns columns 4w .. 4w+3 of the
-// CTA's 32; lane = 8 * column + part.  Part p holds key rows i = p (mod 8)
-// of its column of the state in registers (S[ii] is row p + 8 ii).
+// Per (value head, chunk), independent of the state (every chunk of every
+// head at once): the cumulative log-decay L, e_t = e^{L_t},
+// w_s = r(C-1, s), M[t][s] = r(t,s) q_t.k_s (s <= t), A[t][s] =
+// beta_t r(t,s) k_t.k_s (s < t), and the forward substitutions
+//   U_t = beta_t v_t - sum_{s<t} A[t][s] U_s      (dv columns)
+//   W_t = (beta_t e_t) k_t - sum_{s<t} A[t][s] W_s (dk columns)
+// so that the chunk's deltas are U - W S0.  grid (nv, chunks), 256 threads.
 template <int DK>
-__global__ void __launch_bounds__(256, 2) dn_chunk_kernel(DeltaChunkArgs a) {
-  constexpr int KP = DK / 8;
-  constexpr int KS = DK + 1;  // padded rows of k and q in shared memory
+__global__ void __launch_bounds__(256) dn_wy_kernel(DeltaChunkArgs a) {
+  constexpr int KS = DK + 1;
   extern __shared__ float sm[];
-  float* Ks = sm;                       // [kChunk][KS]
-  float* Qs = Ks + kChunk * KS;         // [kChunk][KS]
-  float* A = Qs + kChunk * KS;          // [kChunk][kChunk] beta_t r(t,s) k_t.k_s (s < t)
-  float* M = A + kChunk * kChunk;       // [kChunk][kChunk] r(t,s) q_t.k_s (s <= t)
-  float* D = M + kChunk * kChunk;       // [kChunk][32] delta
-  float* Vs = D + kChunk * 32;          // [kChunk][32]
-  float* Ls = Vs + kChunk * 32;         // [kChunk] cumulative log-decay
-  float* Es = Ls + kChunk;              // [kChunk] e^{L_t}
-  float* Bs = Es + kChunk;              // [kChunk] beta
-  float* Ws = Bs + kChunk;              // [kChunk] r(C-1, s)
-  // then [kChunk][32] S0^T k_t and [kChunk][32] S0^T q_t (Ps, Rs below)
+  float* Ks = sm;                   // [kChunk][KS]
+  float* Qs = Ks + kChunk * KS;     // [kChunk][KS]
+  float* A = Qs + kChunk * KS;      // [kChunk][kChunk]
+  float* Ls = A + kChunk * kChunk;  // [kChunk]
+  float* Bs = Ls + kChunk;          // [kChunk] beta
+  float* Es = Bs + kChunk;          // [kChunk]
+  const int vh = blockIdx.x, ch = blockIdx.y, DV = a.dv;
+  const int c0 = ch * kChunk, C = min(kChunk, a.rows - c0);
+  const int ratio = a.nv / a.nk;
+  const int kh = a.tiled_heads ? vh % a.nk : vh / ratio;
+  const int key_dim = a.nk * DK, conv_dim = 2 * key_dim + a.nv * DV;
+  const int64_t hc = (int64_t)vh * gridDim.y + ch;  // (head, chunk) record
+  for (int e = threadIdx.x; e < C * DK; e += 256) {
+    const int t = e / DK, i = e % DK;
+    const float* row = a.cv + (int64_t)(c0 + t) * conv_dim;
+    Qs[t * KS + i] = row[kh * DK + i];
+    Ks[t * KS + i] = row[key_dim + kh * DK + i];
+  }
+  if (threadIdx.x == 0) {
+    float l = 0.f;
+    for (int t = 0; t < C; t++) {
+      l = __fadd_rn(l, a.bl[(int64_t)(c0 + t) * 2 * a.nv + a.nv + vh]);
+      Ls[t] = l;
+      Es[t] = exp_ref(l);
+      Bs[t] = a.bl[(int64_t)(c0 + t) * 2 * a.nv + vh];
+    }
+  }
+  __syncthreads();
+  float* ew = a.wy_ew + hc * 2 * kChunk;  // [e | w]
+  if (threadIdx.x < C) {
+    ew[threadIdx.x] = Es[threadIdx.x];
+    ew[kChunk + threadIdx.x] = exp_ref(__fsub_rn(Ls[C - 1], Ls[threadIdx.x]));
+  }
+  float* Mg = a.wy_m + hc * kChunk * kChunk;
+  {
+    // q_t.k_s and k_t.k_s for a 2 x 2 tile of (t, s) per thread, each sum
+    // over i in order
+    const int tt = (threadIdx.x >> 4) * 2, ss = (threadIdx.x & 15) * 2;
+    float qk[2][2] = {{0.f, 0.f}, {0.f, 0.f}}, kk[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    if (tt < C && ss <= tt + 1 && ss < C) {
+#pragma unroll 8
+      for (int i = 0; i < DK; i++) {
+        const float q0 = Qs[tt * KS + i], q1 = Qs[(tt + 1) * KS + i];
+        const float k0 = Ks[tt * KS + i], k1 = Ks[(tt + 1) * KS + i];
+        const float s0 = Ks[ss * KS + i], s1 = Ks[(ss + 1) * KS + i];
+        qk[0][0] = __fadd_rn(qk[0][0], __fmul_rn(q0, s0));
+        qk[0][1] = __fadd_rn(qk[0][1], __fmul_rn(q0, s1));
+        qk[1][0] = __fadd_rn(qk[1][0], __fmul_rn(q1, s0));
+        qk[1][1] = __fadd_rn(qk[1][1], __fmul_rn(q1, s1));
+        kk[0][0] = __fadd_rn(kk[0][0], __fmul_rn(k0, s0));
+        kk[0][1] = __fadd_rn(kk[0][1], __fmul_rn(k0, s1));
+        kk[1][0] = __fadd_rn(kk[1][0], __fmul_rn(k1, s0));
+        kk[1][1] = __fadd_rn(kk[1][1], __fmul_rn(k1, s1));
+      }
+    }
+#pragma unroll
+    for (int x = 0; x < 2; x++)
+#pragma unroll
+      for (int y = 0; y < 2; y++) {
+        const int t = tt + x, s2 = ss + y;
+        float m = 0.f, aa = 0.f;
+        if (t < C && s2 <= t) {
+          const float r = exp_ref(__fsub_rn(Ls[t], Ls[s2]));
+          m = __fmul_rn(r, qk[x][y]);
+          if (s2 < t) aa = __fmul_rn(__fmul_rn(Bs[t], r), kk[x][y]);
+        }
+        Mg[t * kChunk + s2] = m;
+        A[t * kChunk + s2] = aa;
+      }
+  }
+  __syncthreads();
+  // forward substitution, one column per thread: U (dv) then W (dk)
+  float* Xs = Es + kChunk;  // [kChunk][dv + dk]
+  const int XW = DV + DK;
+  for (int col = threadIdx.x; col < XW; col += 256) {
+    const bool isu = col < DV;
+    for (int t = 0; t < C; t++) {
+      const float y = isu ? __fmul_rn(Bs[t], a.cv[(int64_t)(c0 + t) * conv_dim + 2 * key_dim + vh * DV + col])
+                          : __fmul_rn(__fmul_rn(Bs[t], Es[t]), Ks[t * KS + col - DV]);
+      float acc = 0.f;
+      for (int s2 = 0; s2 < t; s2++) acc = __fadd_rn(acc, __fmul_rn(A[t * kChunk + s2], Xs[s2 * XW + col]));
+      Xs[t * XW + col] = __fsub_rn(y, acc);
+    }
+  }
+  __syncthreads();
+  float* X = a.wy_x + hc * kChunk * XW;  // [t][dv | dk]
+  for (int e = threadIdx.x; e < C * XW; e += 256) X[e] = Xs[e];
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+constexpr int kSeqCols = 16;  // value columns per CTA of the in-order kernel
+// shared floats of one staged chunk: q, k, W rows, M, e | w, U columns
+__host__ __device__ constexpr int seq_buf_floats(int dk) {
+  return 3 * kChunk * (dk + 4) + kChunk * kChunk + 2 * kChunk + kChunk * kSeqCols;
+}
+
+// The chunks in order, CTA (value head, 16 columns), 128 threads: warp w owns
+// columns 4w .. 4w+3 of the CTA's 16; lane = 8 * column + part.  Part p
+// holds key rows i = p (mod 8) of its column of the state in registers
+// (S[ii] is row p + 8 ii).  Per chunk: delta_t = U_t - W_t S0 and
+// S0^T q_t (eight parts), o_t = (e_t S0^T q_t + sum_{s<=t} M[t][s] delta_s)
+// / sqrt(dk), then the state update.  A chunk's rows are staged by cp.async
+// (one buffer, so two CTAs fit per SM).
+template <int DK>
+__global__ void __launch_bounds__(128, 2) dn_seq_kernel(DeltaChunkArgs a) {
+  constexpr int KP = DK / 8;
+  constexpr int KS = DK + 4;  // 16-byte rows; the part reads (stride 8) stay conflict-free
+  constexpr int CW = kSeqCols;
+  constexpr int BUF = seq_buf_floats(DK);
+  extern __shared__ __align__(16) float sm[];
+  float* D = sm + BUF;         // [kChunk][CW] delta
+  float* Rs = D + kChunk * CW; // [kChunk][CW] S0^T q
   const DeltaNetLayer& L = *a.layers;
   const int vh = blockIdx.x, DV = a.dv;
   const int ratio = a.nv / a.nk;
   const int kh = a.tiled_heads ? vh % a.nk : vh / ratio;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int p = lane & 7, cl = 4 * warp + (lane >> 3);  // part, column within the CTA's 32
-  const int col = blockIdx.y * 32 + cl;                  // column of the head
+  const int p = lane & 7, cl = 4 * warp + (lane >> 3);
+  const int col0 = blockIdx.y * CW, col = col0 + cl;
   const int key_dim = a.nk * DK, conv_dim = 2 * key_dim + a.nv * DV;
+  const int nch = (a.rows + kChunk - 1) / kChunk;
+  const int XW = DV + DK;
+  auto stage = [&](int ch) {
+    float* b = sm;
+    float *Qs = b, *Ks = Qs + kChunk * KS, *Wr = Ks + kChunk * KS, *M = Wr + kChunk * KS;
+    float *Ew = M + kChunk * kChunk, *Us = Ew + 2 * kChunk;
+    const int c0 = ch * kChunk, C = min(kChunk, a.rows - c0);
+    const int64_t hc = (int64_t)vh * nch + ch;
+    const float* X = a.wy_x + hc * kChunk * XW;
+    for (int e = threadIdx.x; e < C * (DK / 4); e += 128) {
+      const int t = e / (DK / 4), i = 4 * (e % (DK / 4));
+      const float* row = a.cv + (int64_t)(c0 + t) * conv_dim;
+      cp_async16(Qs + t * KS + i, row + kh * DK + i);
+      cp_async16(Ks + t * KS + i, row + key_dim + kh * DK + i);
+      cp_async16(Wr + t * KS + i, X + (int64_t)t * XW + DV + i);
+    }
+    for (int e = threadIdx.x; e < kChunk * kChunk / 4; e += 128)
+      cp_async16(M + 4 * e, a.wy_m + hc * kChunk * kChunk + 4 * e);
+    if (threadIdx.x < 2 * kChunk / 4) cp_async16(Ew + 4 * threadIdx.x, a.wy_ew + hc * 2 * kChunk + 4 * threadIdx.x);
+    for (int e = threadIdx.x; e < C * (CW / 4); e += 128) {
+      const int t = e / (CW / 4), c = 4 * (e % (CW / 4));
+      cp_async16(Us + t * CW + c, X + (int64_t)t * XW + col0 + c);
+    }
+    cp_async_commit();
+  };
   float* base = L.rec_state + (int64_t)vh * DK * DV + col;
   float S[KP];
 #pragma unroll
@@ -158,113 +298,50 @@ __global__ void __launch_bounds__(256, 2) dn_chunk_kernel(DeltaChunkArgs a) {
     for (int ii = 0; ii < KP; ii++) S[ii] = __fadd_rn(__fmul_rn(S[ii], decay), __fmul_rn(rc[p + 8 * ii], delta));
   }
   const float qscale = __fdiv_rn(1.f, sqrtf((float)DK));
-  for (int c0 = 0; c0 < a.rows; c0 += kChunk) {
-    const int C = min(kChunk, a.rows - c0);
-    __syncthreads();  // the previous chunk's shared rows are no longer read
-    for (int e = threadIdx.x; e < C * DK; e += 256) {
-      const int t = e / DK, i = e % DK;
-      const float* row = a.cv + (int64_t)(c0 + t) * conv_dim;
-      Qs[t * KS + i] = row[kh * DK + i];
-      Ks[t * KS + i] = row[key_dim + kh * DK + i];
-    }
-    for (int e = threadIdx.x; e < C * 32; e += 256) {
-      const int t = e / 32, c = e % 32;
-      Vs[e] = a.cv[(int64_t)(c0 + t) * conv_dim + 2 * key_dim + vh * DV + blockIdx.y * 32 + c];
-    }
-    if (threadIdx.x == 0) {
-      float l = 0.f;
-      for (int t = 0; t < C; t++) {
-        l = __fadd_rn(l, a.bl[(int64_t)(c0 + t) * 2 * a.nv + a.nv + vh]);
-        Ls[t] = l;
-        Es[t] = exp_ref(l);
-        Bs[t] = a.bl[(int64_t)(c0 + t) * 2 * a.nv + vh];
-      }
-    }
+  for (int ch = 0; ch < nch; ch++) {
+    const int c0 = ch * kChunk, C = min(kChunk, a.rows - c0);
+    stage(ch);
+    cp_async_wait<0>();
     __syncthreads();
-    if (threadIdx.x < C) Ws[threadIdx.x] = exp_ref(__fsub_rn(Ls[C - 1], Ls[threadIdx.x]));
-    {
-      // q_t.k_s and k_t.k_s for a 2 x 2 tile of (t, s) per thread: eight
-      // independent sums, each over i in order
-      const int tt = (threadIdx.x >> 4) * 2, ss = (threadIdx.x & 15) * 2;
-      float qk[2][2] = {{0.f, 0.f}, {0.f, 0.f}}, kk[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-      if (tt < C && ss <= tt + 1 && ss < C) {
-#pragma unroll 8
-        for (int i = 0; i < DK; i++) {
-          const float q0 = Qs[tt * KS + i], q1 = Qs[(tt + 1) * KS + i];
-          const float k0 = Ks[tt * KS + i], k1 = Ks[(tt + 1) * KS + i];
-          const float s0 = Ks[ss * KS + i], s1 = Ks[(ss + 1) * KS + i];
-          qk[0][0] = __fadd_rn(qk[0][0], __fmul_rn(q0, s0));
-          qk[0][1] = __fadd_rn(qk[0][1], __fmul_rn(q0, s1));
-          qk[1][0] = __fadd_rn(qk[1][0], __fmul_rn(q1, s0));
-          qk[1][1] = __fadd_rn(qk[1][1], __fmul_rn(q1, s1));
-          kk[0][0] = __fadd_rn(kk[0][0], __fmul_rn(k0, s0));
-          kk[0][1] = __fadd_rn(kk[0][1], __fmul_rn(k0, s1));
-          kk[1][0] = __fadd_rn(kk[1][0], __fmul_rn(k1, s0));
-          kk[1][1] = __fadd_rn(kk[1][1], __fmul_rn(k1, s1));
-        }
-      }
-#pragma unroll
-      for (int x = 0; x < 2; x++)
-#pragma unroll
-        for (int y = 0; y < 2; y++) {
-          const int t = tt + x, s2 = ss + y;
-          float m = 0.f, aa = 0.f;
-          if (t < C && s2 <= t) {
-            const float r = exp_ref(__fsub_rn(Ls[t], Ls[s2]));
-            m = __fmul_rn(r, qk[x][y]);
-            if (s2 < t) aa = __fmul_rn(__fmul_rn(Bs[t], r), kk[x][y]);
-          }
-          M[t * kChunk + s2] = m;
-          A[t * kChunk + s2] = aa;
-        }
-    }
-    // S0^T k_t and S0^T q_t of every row (independent of delta): eight parts
-    float* Ps = Ws + kChunk;
-    float* Rs = Ps + kChunk * 32;
+    const float* b = sm;
+    const float *Qs = b, *Ks = Qs + kChunk * KS, *Wr = Ks + kChunk * KS, *M = Wr + kChunk * KS;
+    const float *Ew = M + kChunk * kChunk, *Us = Ew + 2 * kChunk;
+#pragma unroll 4
     for (int t = 0; t < C; t++) {
-      const float* kt = Ks + t * KS + p;
+      const float* wt = Wr + t * KS + p;
       const float* qt = Qs + t * KS + p;
-      float pk = 0.f, pq = 0.f;
+      float pw = 0.f, pq = 0.f;
 #pragma unroll
       for (int ii = 0; ii < KP; ii++) {
-        pk = __fadd_rn(pk, __fmul_rn(S[ii], kt[8 * ii]));
+        pw = __fadd_rn(pw, __fmul_rn(S[ii], wt[8 * ii]));
         pq = __fadd_rn(pq, __fmul_rn(S[ii], qt[8 * ii]));
       }
-      pk = parts_sum(pk);
+      pw = parts_sum(pw);
       pq = parts_sum(pq);
       if (p == 0) {
-        Ps[t * 32 + cl] = pk;
-        Rs[t * 32 + cl] = pq;
+        D[t * CW + cl] = __fsub_rn(Us[t * CW + cl], pw);
+        Rs[t * CW + cl] = pq;
       }
     }
-    __syncthreads();
-    // forward substitution, rows in order (a column's eight lanes sit in one warp)
-    for (int t = 0; t < C; t++) {
-      const float Bv = __fmul_rn(Bs[t], __fsub_rn(Vs[t * 32 + cl], __fmul_rn(Es[t], Ps[t * 32 + cl])));
-      float sub = 0.f;
-      for (int s2 = p; s2 < t; s2 += 8) sub = __fadd_rn(sub, __fmul_rn(A[t * kChunk + s2], D[s2 * 32 + cl]));
-      const float delta = __fsub_rn(Bv, parts_sum(sub));
-      if (p == 0) D[t * 32 + cl] = delta;
-      __syncwarp();
-    }
-    // outputs of every row
+    __syncwarp();
+#pragma unroll 4
     for (int t = 0; t < C; t++) {
       float os = 0.f;
-      for (int s2 = p; s2 <= t; s2 += 8) os = __fadd_rn(os, __fmul_rn(M[t * kChunk + s2], D[s2 * 32 + cl]));
-      const float o = __fmul_rn(qscale, __fadd_rn(__fmul_rn(Es[t], Rs[t * 32 + cl]), parts_sum(os)));
+      for (int s2 = p; s2 <= t; s2 += 8) os = __fadd_rn(os, __fmul_rn(M[t * kChunk + s2], D[s2 * CW + cl]));
+      const float o = __fmul_rn(qscale, __fadd_rn(__fmul_rn(Ew[t], Rs[t * CW + cl]), parts_sum(os)));
       if (p == 0) a.o[(int64_t)(c0 + t) * a.o_ld + vh * DV + col] = o;
     }
-    __syncwarp();
     // S = e^{L_{C-1}} S + sum_s (r(C-1,s) k_s[i]) delta_s
-    const float eC = Es[C - 1];
+    const float eC = Ew[C - 1];
 #pragma unroll
     for (int ii = 0; ii < KP; ii++) S[ii] = __fmul_rn(eC, S[ii]);
-    for (int s = 0; s < C; s++) {
-      const float ws = Ws[s], ds = D[s * 32 + cl];
-      const float* ks = Ks + s * KS + p;
+    for (int s2 = 0; s2 < C; s2++) {
+      const float ws = Ew[kChunk + s2], ds = D[s2 * CW + cl];
+      const float* ks = Ks + s2 * KS + p;
 #pragma unroll
       for (int ii = 0; ii < KP; ii++) S[ii] = __fadd_rn(S[ii], __fmul_rn(__fmul_rn(ws, ks[8 * ii]), ds));
     }
+    __syncthreads();  // the staged rows are read before the next chunk's copies land
   }
 #pragma unroll
   for (int ii = 0; ii < KP; ii++) base[(int64_t)(p + 8 * ii) * DV] = S[ii];
@@ -290,20 +367,27 @@ __global__ void __launch_bounds__(256) dn_gated_kernel(DeltaChunkArgs a) {
   }
 }
 
-size_t chunk_smem(int dk) {
-  return (size_t)(2 * kChunk * (dk + 1) + 2 * kChunk * kChunk + 4 * kChunk * 32 + 4 * kChunk) * sizeof(float);
+size_t wy_smem(int dk) {
+  return (size_t)(2 * kChunk * (dk + 1) + kChunk * kChunk + 3 * kChunk + kChunk * (128 + dk)) * sizeof(float);
 }
+size_t seq_smem(int dk) { return (size_t)(seq_buf_floats(dk) + 2 * kChunk * kSeqCols) * sizeof(float); }
 
 template <int DK>
 cudaError_t launch_chunk(const DeltaChunkArgs& a, cudaStream_t st) {
   static std::mutex mu;
   static bool done[64] = {};
   const cudaError_t e = once_per_device(done, mu, [] {
-    return cudaFuncSetAttribute(dn_chunk_kernel<DK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)chunk_smem(DK));
+    cudaError_t r = cudaFuncSetAttribute(dn_wy_kernel<DK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)wy_smem(DK));
+    if (r != cudaSuccess) return r;
+    return cudaFuncSetAttribute(dn_seq_kernel<DK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)seq_smem(DK));
   });
   if (e != cudaSuccess) return e;
-  dn_chunk_kernel<DK><<<dim3(a.nv, a.dv / 32), 256, chunk_smem(DK), st>>>(a);
+  const int nch = (a.rows + kChunk - 1) / kChunk;
+  dn_wy_kernel<DK><<<dim3(a.nv, nch), 256, wy_smem(DK), st>>>(a);
+  cudaError_t r = cudaGetLastError();
+  if (r != cudaSuccess) return r;
+  dn_seq_kernel<DK><<<dim3(a.nv, a.dv / kSeqCols), 128, seq_smem(DK), st>>>(a);
   return cudaGetLastError();
 }
 
@@ -322,13 +406,14 @@ cudaError_t launch_prep(const DeltaChunkArgs& a, size_t smem, cudaStream_t st) {
 }  // namespace
 
 bool deltanet_chunk_supported(int nk, int nv, int dk, int dv, int conv_k) {
-  return (dk == 64 || dk == 128) && dv % 32 == 0 && dv >= 32 && dv <= 128 && nv <= 128 && 2 * nk <= 64 && conv_k >= 2 &&
+  return (dk == 64 || dk == 128) && dv % 16 == 0 && dv >= 16 && dv <= 128 && nv <= 128 && 2 * nk <= 64 && conv_k >= 2 &&
          conv_k <= 4 && (size_t)(2 * nk * dk + nv * dv) * 4 <= 200 * 1024;
 }
 
 cudaError_t deltanet_chunk_launch(const DeltaChunkArgs& a, cudaStream_t st) {
   if (a.rows < 1 || !deltanet_chunk_supported(a.nk, a.nv, a.dk, a.dv, a.conv_k) ||
-      a.rec_stride != deltanet_rec_stride(a.dk, a.dv) || !a.cv || !a.bl || !a.o || !a.g_out || !a.z || !a.norm_w)
+      a.rec_stride != deltanet_rec_stride(a.dk, a.dv) || !a.cv || !a.bl || !a.o || !a.g_out || !a.z || !a.norm_w ||
+      !a.wy_x || !a.wy_m || !a.wy_ew)
     return cudaErrorInvalidValue;
   const size_t smem = (size_t)(2 * a.nk * a.dk + a.nv * a.dv) * sizeof(float);
   cudaError_t e;

@@ -69,6 +69,11 @@ struct DeltaChunkArgs {
   float* cv;                    // scratch [rows][conv_dim]: normalized q, k, then v
   float* bl;                    // scratch [rows][2 nv]: beta, then log-decay
   float* o;  int o_ld;          // scratch: recurrent outputs [rows][o_ld]
+  // scratch per (value head, 32-row chunk): wy_x [kChunk][dv + dk] (U | W),
+  // wy_m [kChunk][kChunk], wy_ew [2][kChunk] (e_t, then w_s)
+  float* wy_x;
+  float* wy_m;
+  float* wy_ew;
   const float* z;  int z_ld;
   const float* norm_w;
   float eps, inv_dv;

@@ -216,6 +216,13 @@ int wide_delta(iq_state* s, const Layer& L, int li, int n) {
     IQ_CUDA(W.cv.reserve((size_t)n * conv_dim * 4));
     IQ_CUDA(W.bl.reserve((size_t)n * 2 * nv * 4));
     IQ_CUDA(W.dno.reserve((size_t)n * vdim * 4));
+    const int64_t nch = ceil_div(pre, 32);  // the chunked kernels' 32-row chunks
+    IQ_CUDA(W.wyx.reserve((size_t)nv * nch * 32 * (dk + dv) * 4));
+    IQ_CUDA(W.wym.reserve((size_t)nv * nch * 32 * 32 * 4));
+    IQ_CUDA(W.wyew.reserve((size_t)nv * nch * 64 * 4));
+    h.wy_x = W.wyx.as<float>();
+    h.wy_m = W.wym.as<float>();
+    h.wy_ew = W.wyew.as<float>();
     h.cv = W.cv.as<float>();
     h.bl = W.bl.as<float>();
     h.o = W.dno.as<float>();

@@ -487,7 +487,8 @@ void or_delta_step(const float* q, const float* k, const float* v, const float* 
  * before its final block (order 2; inferq_b200/csrc/deltanet_chunk.cu
  * states the algebra).  Same arithmetic as delta_head_step up to f32
  * rounding order; this restates the device's order exactly: key-dimension
- * dots sequential, S0^T k / S0^T q in eight parts (part p: rows i = p mod 8)
+ * dots sequential; U and W of delta = U - W S0 by forward substitution in s
+ * order; W_t S0 and S0^T q in eight parts (part p: rows i = p mod 8)
  * combined as
  * ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)), sums over s split s = p (mod 8) and
  * combined the same way, decays as exp of cumulative log-decay differences. */
@@ -523,32 +524,44 @@ static void delta_chunk(const float* q, const float* k, int ld_qk, const float* 
             M[t][s] = m;
             A[t][s] = aa;
         }
-    for (int j = 0; j < dv; j++) {
+    /* U_t = beta_t v_t - sum_{s<t} A U_s, W_t = (beta_t e_t) k_t - sum_{s<t} A W_s */
+    static float U[CHUNK][128], Wk[CHUNK][128];
+    for (int j = 0; j < dv; j++)
         for (int t = 0; t < C; t++) {
-            float pk[8], pq[8], ps[8], po[8];
+            float acc = 0.f;
+            for (int s = 0; s < t; s++) acc = acc + A[t][s] * U[s][j];
+            U[t][j] = beta[t] * v[t * ld_v + j] - acc;
+        }
+    for (int i = 0; i < dk; i++)
+        for (int t = 0; t < C; t++) {
+            float acc = 0.f;
+            for (int s = 0; s < t; s++) acc = acc + A[t][s] * Wk[s][i];
+            Wk[t][i] = (beta[t] * E[t]) * k[t * ld_qk + i] - acc;
+        }
+    for (int j = 0; j < dv; j++) {
+        float R[CHUNK];
+        for (int t = 0; t < C; t++) {
+            float pw[8], pq[8];
             for (int p = 0; p < 8; p++) {
                 float a1 = 0.f, a2 = 0.f;
                 for (int ii = 0; ii < kp; ii++) {
                     int i = p + 8 * ii;
-                    a1 = a1 + S[i * dv + j] * k[t * ld_qk + i];
+                    a1 = a1 + S[i * dv + j] * Wk[t][i];
                     a2 = a2 + S[i * dv + j] * q[t * ld_qk + i];
                 }
-                pk[p] = a1; pq[p] = a2;
+                pw[p] = a1; pq[p] = a2;
             }
-            float P = tree8(pk), R = tree8(pq);
-            float B = beta[t] * (v[t * ld_v + j] - E[t] * P);
-            for (int p = 0; p < 8; p++) {
-                float acc = 0.f;
-                for (int s = p; s < t; s += 8) acc = acc + A[t][s] * D[s][j];
-                ps[p] = acc;
-            }
-            D[t][j] = B - tree8(ps);
+            D[t][j] = U[t][j] - tree8(pw);
+            R[t] = tree8(pq);
+        }
+        for (int t = 0; t < C; t++) {
+            float po[8];
             for (int p = 0; p < 8; p++) {
                 float acc = 0.f;
                 for (int s = p; s <= t; s += 8) acc = acc + M[t][s] * D[s][j];
                 po[p] = acc;
             }
-            o[t * ld_o + j] = qscale * (E[t] * R + tree8(po));
+            o[t * ld_o + j] = qscale * (E[t] * R[t] + tree8(po));
         }
         for (int i = 0; i < dk; i++) {
             float acc = E[C - 1] * S[i * dv + j];
@@ -560,7 +573,7 @@ static void delta_chunk(const float* q, const float* k, int ld_qk, const float* 
 static int chunk_supported(const or_config* c) {
     int nk = c->linear_num_key_heads, nv = c->linear_num_value_heads, dk = c->linear_key_head_dim;
     int dv = c->linear_value_head_dim, K = c->linear_conv_kernel_dim;
-    return (dk == 64 || dk == 128) && dv % 32 == 0 && dv >= 32 && dv <= 128 && nv <= 128 && 2 * nk <= 64 &&
+    return (dk == 64 || dk == 128) && dv % 16 == 0 && dv >= 16 && dv <= 128 && nv <= 128 && 2 * nk <= 64 &&
            K >= 2 && K <= 4 && (2 * nk * dk + nv * dv) * 4 <= 200 * 1024;
 }
 
