@@ -119,42 +119,81 @@ __global__ void __launch_bounds__(256) attn_scan_kernel(AttnArgs a) {
   __syncthreads();
   const float scale = __fdiv_rn(1.f, sqrtf((float)HD));
   const int nchunks_total = (last + kAttnChunk) / kAttnChunk;
-  for (int q = warp; q < nq; q += 8) {
-    const int t = q / gpc, h = kvh * G + g0 + q % gpc;
-    const int attend_last = pos0 + t;
-    if (p0 > attend_last) continue;  // this chunk is entirely in row t's future
-    const float* qs = Qs + q * HD;
-    const float* kr = Ks + lane * (HD + 1);
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll 8
-    for (int d = 0; d < HD; d += 4) {
-      s0 = fmaf(qs[d], kr[d], s0);
-      s1 = fmaf(qs[d + 1], kr[d + 1], s1);
-      s2 = fmaf(qs[d + 2], kr[d + 2], s2);
-      s3 = fmaf(qs[d + 3], kr[d + 3], s3);
+  // a warp takes its queries q = warp + 8 j in groups of QG: each K element
+  // a lane loads feeds QG score chains and each V element QG accumulators;
+  // every query keeps exactly its own operation order
+  constexpr int QG = 4;
+  for (int q0 = warp; q0 < nq; q0 += 8 * QG) {
+    bool live[QG];
+    int tq[QG], hq[QG];
+    bool anyl = false;
+#pragma unroll
+    for (int g = 0; g < QG; g++) {
+      const int q = q0 + 8 * g;
+      tq[g] = q / gpc;
+      hq[g] = kvh * G + g0 + q % gpc;
+      live[g] = q < nq && p0 <= pos0 + tq[g];  // else: past the queries, or the chunk is in row t's future
+      anyl |= live[g];
     }
-    const bool valid = p0 + lane <= attend_last;
-    float sc = valid ? __fmul_rn(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)), scale) : -INFINITY;
-    float m = sc;
+    if (!anyl) continue;
+    const float* kr = Ks + lane * (HD + 1);
+    float s[QG][4];
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float e = valid ? exp_ref(sc - m) : 0.f;
-    float l = e;
+    for (int g = 0; g < QG; g++) s[g][0] = s[g][1] = s[g][2] = s[g][3] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < HD; d += 4) {
+      const float k0 = kr[d], k1 = kr[d + 1], k2 = kr[d + 2], k3 = kr[d + 3];
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
-    float acc[D];
+      for (int g = 0; g < QG; g++) {
+        if (!live[g]) continue;
+        const float* qs = Qs + (q0 + 8 * g) * HD;
+        s[g][0] = fmaf(qs[d], k0, s[g][0]);
+        s[g][1] = fmaf(qs[d + 1], k1, s[g][1]);
+        s[g][2] = fmaf(qs[d + 2], k2, s[g][2]);
+        s[g][3] = fmaf(qs[d + 3], k3, s[g][3]);
+      }
+    }
+    float e[QG], m[QG], l[QG];
 #pragma unroll
-    for (int d = 0; d < D; d++) acc[d] = 0.f;
+    for (int g = 0; g < QG; g++) {
+      const bool valid = live[g] && p0 + lane <= pos0 + tq[g];
+      const float sc = valid ? __fmul_rn(__fadd_rn(__fadd_rn(s[g][0], s[g][1]), __fadd_rn(s[g][2], s[g][3])), scale)
+                             : -INFINITY;
+      float mm = sc;
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+      e[g] = valid ? exp_ref(sc - mm) : 0.f;
+      float ll = e[g];
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) ll = __fadd_rn(ll, __shfl_xor_sync(0xffffffffu, ll, o));
+      m[g] = mm;
+      l[g] = ll;
+    }
+    float acc[QG][D];
+#pragma unroll
+    for (int g = 0; g < QG; g++)
+#pragma unroll
+      for (int d = 0; d < D; d++) acc[g][d] = 0.f;
     for (int p = 0; p < 32; p++) {
-      const float ep = __shfl_sync(0xffffffffu, e, p);
+      float ep[QG];
+#pragma unroll
+      for (int g = 0; g < QG; g++) ep[g] = __shfl_sync(0xffffffffu, e[g], p);
       const float* vr = Vs + p * HD + lane;
 #pragma unroll
-      for (int d = 0; d < D; d++) acc[d] = fmaf(ep, vr[32 * d], acc[d]);
-    }
-    float* part = a.part + (((int64_t)t * a.nh + h) * nchunks_total + c) * (HD + 2);
-    if (lane == 0) { part[0] = m; part[1] = l; }
+      for (int d = 0; d < D; d++) {
+        const float v = vr[32 * d];
 #pragma unroll
-    for (int d = 0; d < D; d++) part[2 + 32 * d + lane] = acc[d];
+        for (int g = 0; g < QG; g++) acc[g][d] = fmaf(ep[g], v, acc[g][d]);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < QG; g++) {
+      if (!live[g]) continue;
+      float* part = a.part + (((int64_t)tq[g] * a.nh + hq[g]) * nchunks_total + c) * (HD + 2);
+      if (lane == 0) { part[0] = m[g]; part[1] = l[g]; }
+#pragma unroll
+      for (int d = 0; d < D; d++) part[2 + 32 * d + lane] = acc[g][d];
+    }
   }
 }
 
