@@ -211,12 +211,14 @@ int iq_state_stream(const iq_state* s, void** stream);
  * rows, when every dense matrix is Q8_0, Q4_K or Q6_K and the experts sit on
  * one GPU, the call takes the wide prefill pass instead (the reference's
  * prefill_in_passes, src/runtime.rs:748-771: 512-row chunks; projections on
- * the tensor cores, experts grouped by expert, the recurrence and attention
- * in their sequential kernels): the reference's arithmetic up to f32
- * summation order, not bitwise the 8-row passes.  Outputs are host buffers or NULL:
+ * the tensor cores, the DeltaNet recurrence in its chunked form up to each
+ * chunk's final block of up to 8 rows, attention in its sequential kernels,
+ * experts grouped by expert): the reference's arithmetic up to f32 rounding
+ * order, not bitwise the 8-row passes.  Outputs are host buffers or NULL:
  * logits [rows][vocab], normalized hidden [rows][hidden], argmax [rows]
- * (ties to the last index, sampling.rs:104-112).  The pre-pass state of the
- * last pass is kept, so iq_rollback may follow. */
+ * (ties to the last index, sampling.rs:104-112).  The state before the last
+ * pass (for the wide pass: before its final block of up to 8 rows) is kept,
+ * so iq_rollback may follow. */
 int iq_forward(iq_state* s, const uint32_t* tokens, int rows, float* logits, float* hidden, int32_t* argmax);
 
 typedef struct iq_verify_result {
@@ -235,7 +237,9 @@ typedef struct iq_verify_result {
 int iq_verify(iq_state* s, const uint32_t* tokens, int rows, iq_verify_result* out, float* logits, float* hidden);
 
 /* Roll the last iq_forward pass back to its first `committed_rows` rows
- * (QuantizedModelState::rollback).  committed_rows < rows of that pass. */
+ * (QuantizedModelState::rollback).  committed_rows < rows of that pass; after
+ * a wide pass the rows counted are those of its final block of up to 8
+ * (rows before it are committed for good). */
 int iq_rollback(iq_state* s, int committed_rows);
 
 /* ---------------------------------------------------------------- MTP draft
