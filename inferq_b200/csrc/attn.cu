@@ -206,20 +206,39 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs a) {
   const int nchunks = (pos0 + t + 1 + kAttnChunk - 1) / kAttnChunk;
   const int nchunks_total = (pos0 + a.rows - 1 + kAttnChunk) / kAttnChunk;
   const float* part = a.part + ((int64_t)t * a.nh + h) * nchunks_total * (a.hd + 2);
-  float M = -INFINITY;
-#pragma unroll 8
-  for (int c = 0; c < nchunks; c++) M = fmaxf(M, part[c * (a.hd + 2)]);
   const int i = threadIdx.x;
+  // M = the chunks' largest max (exact in any order)
+  __shared__ float red[8];
+  float mx = -INFINITY;
+  for (int c = i; c < nchunks; c += 256) mx = fmaxf(mx, part[c * (a.hd + 2)]);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((i & 31) == 0) red[i >> 5] = mx;
+  __syncthreads();
+  float M = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; w++) M = fmaxf(M, red[w]);
+  // the chunks in order, 256 at a time: their weights exp(m_c - M) once per
+  // CTA, then L = sum l_c w_c and o = sum o_c w_c as ordered chains
+  __shared__ float wc[256];
   __shared__ float ys[256];
-  if (i < a.hd) {
-    float L = 0.f, o = 0.f;
+  float L = 0.f, o = 0.f;
+  for (int c0 = 0; c0 < nchunks; c0 += 256) {
+    const int nc = min(256, nchunks - c0);
+    __syncthreads();  // the previous weights are read
+    if (i < nc) wc[i] = exp_ref(part[(c0 + i) * (a.hd + 2)] - M);
+    __syncthreads();
+    if (i < a.hd) {
 #pragma unroll 8
-    for (int c = 0; c < nchunks; c++) {
-      const float* pc = part + c * (a.hd + 2);
-      const float w = exp_ref(pc[0] - M);
-      L = fmaf(pc[1], w, L);
-      o = fmaf(pc[2 + i], w, o);
+      for (int c = 0; c < nc; c++) {
+        const float* pc = part + (c0 + c) * (a.hd + 2);
+        const float w = wc[c];
+        L = fmaf(pc[1], w, L);
+        o = fmaf(pc[2 + i], w, o);
+      }
     }
+  }
+  if (i < a.hd) {
     o = __fdiv_rn(o, L);
     const float gate = a.qg[(int64_t)t * a.qg_ld + (int64_t)h * 2 * a.hd + a.hd + i];
     const float y = __fmul_rn(o, sigmoidf_ref(gate));
