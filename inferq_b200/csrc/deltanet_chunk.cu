@@ -21,7 +21,7 @@
 //   * U_t = beta_t v_t - sum_{s<t} A[t][s] U_s and W_t = (beta_t e_t) k_t -
 //     sum_{s<t} A[t][s] W_s (so delta = U - W S0), each sum in s order;
 //   * W_t S0 and S0^T q_t per column: eight parts, part p the key rows
-//     i = p (mod 8) in ascending order, combined as
+//     [p dk/8, (p+1) dk/8) in ascending order, combined as
 //     ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7));
 //   * the output sum over s: part p takes s = p (mod 8) in ascending order,
 //     the parts combined by the same tree;
@@ -230,22 +230,27 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 constexpr int kSeqCols = 16;  // value columns per CTA of the in-order kernel
+// A staged q / k / W row, part-major: part p (key rows [p dk/8, (p+1) dk/8))
+// at p * (dk/8 + 4), so a lane reads its part as 16-byte words and the eight
+// parts of a column fall in distinct bank groups.
+__host__ __device__ constexpr int seq_row_floats(int dk) { return 8 * (dk / 8 + 4); }
 // shared floats of one staged chunk: q, k, W rows, M, e | w, U columns
 __host__ __device__ constexpr int seq_buf_floats(int dk) {
-  return 3 * kChunk * (dk + 4) + kChunk * kChunk + 2 * kChunk + kChunk * kSeqCols;
+  return 3 * kChunk * seq_row_floats(dk) + kChunk * kChunk + 2 * kChunk + kChunk * kSeqCols;
 }
 
 // The chunks in order, CTA (value head, 16 columns), 128 threads: warp w owns
 // columns 4w .. 4w+3 of the CTA's 16; lane = 8 * column + part.  Part p
-// holds key rows i = p (mod 8) of its column of the state in registers
-// (S[ii] is row p + 8 ii).  Per chunk: delta_t = U_t - W_t S0 and
+// holds key rows [p dk/8, (p+1) dk/8) of its column of the state in
+// registers (S[ii] is row p dk/8 + ii).  Per chunk: delta_t = U_t - W_t S0 and
 // S0^T q_t (eight parts), o_t = (e_t S0^T q_t + sum_{s<=t} M[t][s] delta_s)
 // / sqrt(dk), then the state update.  A chunk's rows are staged by cp.async
 // (one buffer, so two CTAs fit per SM).
 template <int DK>
 __global__ void __launch_bounds__(128, 2) dn_seq_kernel(DeltaChunkArgs a) {
   constexpr int KP = DK / 8;
-  constexpr int KS = DK + 4;  // 16-byte rows; the part reads (stride 8) stay conflict-free
+  constexpr int KS = seq_row_floats(DK);  // staged row stride
+  constexpr int PS = KP + 4;              // part stride within a row
   constexpr int CW = kSeqCols;
   constexpr int BUF = seq_buf_floats(DK);
   extern __shared__ __align__(16) float sm[];
@@ -270,10 +275,11 @@ __global__ void __launch_bounds__(128, 2) dn_seq_kernel(DeltaChunkArgs a) {
     const float* X = a.wy_x + hc * kChunk * XW;
     for (int e = threadIdx.x; e < C * (DK / 4); e += 128) {
       const int t = e / (DK / 4), i = 4 * (e % (DK / 4));
+      const int d = t * KS + (i / KP) * PS + i % KP;  // part-major position of element i
       const float* row = a.cv + (int64_t)(c0 + t) * conv_dim;
-      cp_async16(Qs + t * KS + i, row + kh * DK + i);
-      cp_async16(Ks + t * KS + i, row + key_dim + kh * DK + i);
-      cp_async16(Wr + t * KS + i, X + (int64_t)t * XW + DV + i);
+      cp_async16(Qs + d, row + kh * DK + i);
+      cp_async16(Ks + d, row + key_dim + kh * DK + i);
+      cp_async16(Wr + d, X + (int64_t)t * XW + DV + i);
     }
     for (int e = threadIdx.x; e < kChunk * kChunk / 4; e += 128)
       cp_async16(M + 4 * e, a.wy_m + hc * kChunk * kChunk + 4 * e);
@@ -287,7 +293,7 @@ __global__ void __launch_bounds__(128, 2) dn_seq_kernel(DeltaChunkArgs a) {
   float* base = L.rec_state + (int64_t)vh * DK * DV + col;
   float S[KP];
 #pragma unroll
-  for (int ii = 0; ii < KP; ii++) S[ii] = base[(int64_t)(p + 8 * ii) * DV];
+  for (int ii = 0; ii < KP; ii++) S[ii] = base[(int64_t)(p * KP + ii) * DV];
   // replay the committed rows of the previous pass (S = S g + k delta)
   const int pend = *a.pending;
   const float* rec_head = L.rec_log + (int64_t)vh * kMaxRowsDelta * a.rec_stride;
@@ -295,7 +301,7 @@ __global__ void __launch_bounds__(128, 2) dn_seq_kernel(DeltaChunkArgs a) {
     const float* rc = rec_head + (int64_t)r * a.rec_stride;
     const float decay = rc[DK + DV], delta = rc[DK + col];
 #pragma unroll
-    for (int ii = 0; ii < KP; ii++) S[ii] = __fadd_rn(__fmul_rn(S[ii], decay), __fmul_rn(rc[p + 8 * ii], delta));
+    for (int ii = 0; ii < KP; ii++) S[ii] = __fadd_rn(__fmul_rn(S[ii], decay), __fmul_rn(rc[p * KP + ii], delta));
   }
   const float qscale = __fdiv_rn(1.f, sqrtf((float)DK));
   for (int ch = 0; ch < nch; ch++) {
@@ -308,13 +314,18 @@ __global__ void __launch_bounds__(128, 2) dn_seq_kernel(DeltaChunkArgs a) {
     const float *Ew = M + kChunk * kChunk, *Us = Ew + 2 * kChunk;
 #pragma unroll 4
     for (int t = 0; t < C; t++) {
-      const float* wt = Wr + t * KS + p;
-      const float* qt = Qs + t * KS + p;
+      const float4* wt = reinterpret_cast<const float4*>(Wr + t * KS + p * PS);
+      const float4* qt = reinterpret_cast<const float4*>(Qs + t * KS + p * PS);
       float pw = 0.f, pq = 0.f;
 #pragma unroll
-      for (int ii = 0; ii < KP; ii++) {
-        pw = __fadd_rn(pw, __fmul_rn(S[ii], wt[8 * ii]));
-        pq = __fadd_rn(pq, __fmul_rn(S[ii], qt[8 * ii]));
+      for (int i4 = 0; i4 < KP / 4; i4++) {
+        const float4 w4 = wt[i4], q4 = qt[i4];
+        const float wv[4] = {w4.x, w4.y, w4.z, w4.w}, qv[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          pw = __fadd_rn(pw, __fmul_rn(S[4 * i4 + e], wv[e]));
+          pq = __fadd_rn(pq, __fmul_rn(S[4 * i4 + e], qv[e]));
+        }
       }
       pw = parts_sum(pw);
       pq = parts_sum(pq);
@@ -337,14 +348,19 @@ __global__ void __launch_bounds__(128, 2) dn_seq_kernel(DeltaChunkArgs a) {
     for (int ii = 0; ii < KP; ii++) S[ii] = __fmul_rn(eC, S[ii]);
     for (int s2 = 0; s2 < C; s2++) {
       const float ws = Ew[kChunk + s2], ds = D[s2 * CW + cl];
-      const float* ks = Ks + s2 * KS + p;
+      const float4* ks = reinterpret_cast<const float4*>(Ks + s2 * KS + p * PS);
 #pragma unroll
-      for (int ii = 0; ii < KP; ii++) S[ii] = __fadd_rn(S[ii], __fmul_rn(__fmul_rn(ws, ks[8 * ii]), ds));
+      for (int i4 = 0; i4 < KP / 4; i4++) {
+        const float4 k4 = ks[i4];
+        const float kv[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) S[4 * i4 + e] = __fadd_rn(S[4 * i4 + e], __fmul_rn(__fmul_rn(ws, kv[e]), ds));
+      }
     }
     __syncthreads();  // the staged rows are read before the next chunk's copies land
   }
 #pragma unroll
-  for (int ii = 0; ii < KP; ii++) base[(int64_t)(p + 8 * ii) * DV] = S[ii];
+  for (int ii = 0; ii < KP; ii++) base[(int64_t)(p * KP + ii) * DV] = S[ii];
 }
 
 // grid (rows): the gated RMSNorm of every value head of row t

@@ -488,7 +488,7 @@ void or_delta_step(const float* q, const float* k, const float* v, const float* 
  * states the algebra).  Same arithmetic as delta_head_step up to f32
  * rounding order; this restates the device's order exactly: key-dimension
  * dots sequential; U and W of delta = U - W S0 by forward substitution in s
- * order; W_t S0 and S0^T q in eight parts (part p: rows i = p mod 8)
+ * order; W_t S0 and S0^T q in eight parts (part p: rows p dk/8 .. (p+1) dk/8 - 1)
  * combined as
  * ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)), sums over s split s = p (mod 8) and
  * combined the same way, decays as exp of cumulative log-decay differences. */
@@ -545,7 +545,7 @@ static void delta_chunk(const float* q, const float* k, int ld_qk, const float* 
             for (int p = 0; p < 8; p++) {
                 float a1 = 0.f, a2 = 0.f;
                 for (int ii = 0; ii < kp; ii++) {
-                    int i = p + 8 * ii;
+                    int i = p * kp + ii;
                     a1 = a1 + S[i * dv + j] * Wk[t][i];
                     a2 = a2 + S[i * dv + j] * q[t * ld_qk + i];
                 }
