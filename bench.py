@@ -19,7 +19,11 @@ e2e        the same steps on the host clock through the C ABI (host tokens
 config     verify_us: one verification pass at k = 1, 2, 4, 8 (context 1024,
            drafts = the greedy continuation with 30% corrupted); ngram: the
            tiny model's n-gram-speculative decode at context 256; wide: the
-           tensor-core product at a 35B projection shape
+           tensor-core product at a 35B projection shape; wide_prefill: the
+           wide prefill pass (iq_forward) on the 35B shapes with Q8_0
+           weights, full 40 layers, 64 / 256 / 512 rows of seeded
+           uniform-random token ids over a 2048-token context, tok/s on the
+           device and through the C ABI
 roofline   the quantized GEMV (the dominant kernel): its weight bytes over its
            event-timed launches, against the measured HBM copy bandwidth
 cpu_baseline  the same MTP rounds through the CPU restatement of the
