@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(256) rows_argmax_kernel(const float* __restric
     b = merge(b, x, false);
   }
   b = block_best(b, false);
-  if (threadIdx.x == 0) out[t] = b.i;
+  if (threadIdx.x == 0) out[t] = b.i < 0 ? 0 : b.i;  // no finite logit: token 0, a valid id
 }
 
 // One CTA: final argmax per row, then accept and the authoritative token.
@@ -154,8 +154,9 @@ __global__ void __launch_bounds__(256) accept_kernel(HeadArgs a) {
     }
     b = block_best(b, scores);
     if (threadIdx.x == 0) {
-      am[t] = b.i;
-      a.argmax[t] = b.i;
+      const int bi = b.i < 0 ? 0 : b.i;  // no finite logit: token 0, a valid id
+      am[t] = bi;
+      a.argmax[t] = bi;
       if (scores) {
         a.scores[0] = b.v - b.v2;
         a.scores[1] = __fdiv_rn(1.f, b.se);

@@ -82,7 +82,12 @@ __device__ __forceinline__ void route_row_warp(const float* lg, int E, int topk,
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) den = __fadd_rn(den, __shfl_xor_sync(0xffffffffu, den, o));
 #pragma unroll
-    for (int i = 0; i < kPerLane; i++) p[i] = lane + 32 * i < E ? __fdiv_rn(p[i], den) : -1.f;
+    for (int i = 0; i < kPerLane; i++) {
+      p[i] = lane + 32 * i < E ? __fdiv_rn(p[i], den) : -1.f;
+      // a NaN probability (non-finite logits) ranks below every real one but
+      // above the taken marker, so the selection always names valid experts
+      if (p[i] != p[i]) p[i] = -0.5f;
+    }
     for (int r = 0; r < topk; r++) {
       float best = -1.f;
       int bi = 0x7fffffff;

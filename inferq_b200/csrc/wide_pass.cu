@@ -344,7 +344,11 @@ int wide_moe(iq_state* s, const Layer& L, int n) {
   // gathered row g*8+i is member i of group g
   std::vector<std::vector<int>> by_e(E);
   for (int r = 0; r < n; r++)
-    for (int q = 0; q < topk; q++) by_e[W.h_routes[r * topk + q]].push_back(r * topk + q);
+    for (int q = 0; q < topk; q++) {
+      const int e = W.h_routes[r * topk + q];
+      IQ_CHECK(e >= 0 && e < E, IQ_ESTATE, "wide pass: route %d of row %d names expert %d of %d", q, r, e, E);
+      by_e[e].push_back(r * topk + q);
+    }
   int groups = 0;
   for (int e = 0; e < E; e++) groups += (int)ceil_div((int64_t)by_e[e].size(), 8);
   const int ng_rows = 8 * groups;
