@@ -65,7 +65,7 @@ TOL = 2e-2          # logit tolerance: margins below it are listed
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -105,6 +105,15 @@ class Clocks:
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+
+    def wait_first(self, limit_s: float = 5.0):
+        """Block until the sampler has written its first row (so the timed
+        region that follows is covered), at most `limit_s`."""
+        t0 = time.perf_counter()
+        while self.proc is not None and time.perf_counter() - t0 < limit_s:
+            if self.path.exists() and self.path.read_text().strip():
+                return
+            time.sleep(0.02)
 
     def stop(self):
         if self.proc is None:
@@ -519,8 +528,9 @@ def main():
         stats.append(dict(loop.last))
         return toks
 
-    barrier()
     clocks = Clocks(local)
+    clocks.wait_first()
+    barrier()
     torch.cuda.nvtx.range_push("mtp_rounds")
     dev_s, wall, rounds = _timed(stream, round_, args.steps)
     torch.cuda.nvtx.range_pop()
@@ -625,4 +635,9 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    try:
+        main()
+    finally:
+        import torch.distributed as _dist
+        if _dist.is_available() and _dist.is_initialized():
+            _dist.destroy_process_group()
