@@ -10,6 +10,7 @@
 // the slot with the unit `depth` ahead.  Activations are staged into shared memory
 // once per change of input rows, not once per tile.
 #include <algorithm>
+#include <type_traits>
 #include <mutex>
 #include <cstdlib>
 #include <climits>
@@ -562,7 +563,10 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
     Frag f;
 #pragma unroll
     for (int i = 0; i < 4; i++) { f.acc[i] = 0.f; f.accm[i] = 0.f; }
-    if (ct.live() && ok) {
+    // the tile's units, with the dtype fixed per tile so each loop body holds
+    // only its own dtype's unpack and arithmetic
+    auto units = [&](auto dtc) {
+      constexpr int DT = decltype(dtc)::value;
       for (int b = ct.u0; b < ct.u1; b++, n++) {
         uint8_t* slot = ring + si * slot_bytes;
         if (!mbar_wait(&wbars[si], phase, wait_limit)) {
@@ -573,8 +577,8 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
           break;
         }
         WRegs cur;
-        load_slot(ct.dt, slot, b, gid, tig, cur);
-        compute_block(ct.dt, cur, bact, ac, ct.nb, b, tig, f);
+        load_slot(DT, slot, b, gid, tig, cur);
+        compute_block(DT, cur, bact, ac, ct.nb, b, tig, f);
         // refill the slot once the unit's words have been used: every lane's
         // reads of it have completed before lane 0 hands it to the copy engine
         __syncwarp();
@@ -588,6 +592,14 @@ __global__ void __launch_bounds__(kQmvThreads, 2) qmv_kernel(const QmvJob* jobs,
           si = 0;
           phase ^= 1u;
         }
+      }
+    };
+    if (ct.live() && ok) {
+      switch (ct.dt) {
+        case Q4_K: units(std::integral_constant<int, Q4_K>{}); break;
+        case Q5_K: units(std::integral_constant<int, Q5_K>{}); break;
+        case Q6_K: units(std::integral_constant<int, Q6_K>{}); break;
+        default: units(std::integral_constant<int, Q8_0>{}); break;
       }
     }
 
