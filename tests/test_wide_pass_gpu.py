@@ -50,6 +50,15 @@ def _mini_q80():
     return c
 
 
+def _tensors(cfg, seed):
+    """Seeded weights (generated on the device at 35B widths, then host copies
+    for the oracle)."""
+    if cfg.hidden_size >= 2048:
+        return [synth.Tensor(t.name, t.dtype, t.shape, t.data.cpu())
+                for t in synth.generate(cfg, seed=seed, device="cuda")]
+    return list(synth.generate(cfg, seed=seed))
+
+
 def _one_layer(cfg, kind):
     import dataclasses
     c = synth.Config(**{f.name: getattr(cfg, f.name) for f in dataclasses.fields(cfg)})
@@ -60,14 +69,24 @@ def _one_layer(cfg, kind):
     return c
 
 
-CASES = {"tiny": synth.tiny, "mini_wide": _mini_wide, "mini_q80": _mini_q80}
+def _35b_widths_q80():
+    """Four layers at the 35B widths (32 value / 16 key heads of 128, 256
+    experts top-8, hidden 2048), every matrix Q8_0, F32 router."""
+    c = synth.qwen36_35b()
+    c.name = "qwen3.6-35b-widths-4-layers-q8_0"
+    c.num_hidden_layers = 4
+    c.dtypes = {"default": Q.Q8_0, "router": Q.F32}
+    return c
+
+
+CASES = {"tiny": synth.tiny, "mini_wide": _mini_wide, "mini_q80": _mini_q80, "35b_widths": _35b_widths_q80}
 
 
 @pytest.fixture(scope="module", params=list(CASES))
 def pair(request, cuda):
     cfg = CASES[request.param]()
-    tensors = list(synth.generate(cfg, seed=31))
-    return cfg, Model(cfg, tensors), oracle.OracleModel(cfg, tensors)
+    tensors = _tensors(cfg, 31)
+    yield cfg, Model(cfg, tensors), oracle.OracleModel(cfg, tensors)
 
 
 def _oracle(om, prompt, order):
@@ -124,7 +143,7 @@ def test_wide_prefill_matches_the_oracle_per_layer(cuda, case, kind):
     amplifies a single flipped activation rounding; one layer keeps that
     from compounding)."""
     cfg = _one_layer(CASES[case](), kind)
-    tensors = list(synth.generate(cfg, seed=31))
+    tensors = _tensors(cfg, 31)
     _whole_model(cfg, Model(cfg, tensors), oracle.OracleModel(cfg, tensors), 200, 5, median=1e-4)
 
 
