@@ -170,6 +170,17 @@ struct MoeRouteArgs {
   int swiglu_down;  // 1: down jobs stage silu(g)*u from gu_out themselves (kActSwiGLU)
 };
 cudaError_t moe_route_launch(const MoeRouteArgs& a, const MoeRouteStatic& s, cudaStream_t st, bool pdl);
+// The F32 router (rows x cols, f32_matvec's arithmetic) and the routing in
+// one launch: y [k][ld] must be a.logits; `counter` is a device int that
+// starts at 0 (the launch leaves it at 0).
+struct RouterRouteArgs {
+  const float* w;  int rows, cols;
+  const float* x;  int ldx;
+  float* y;
+  int* counter;
+};
+cudaError_t router_route_launch(const RouterRouteArgs& r, const MoeRouteArgs& a, const MoeRouteStatic& s,
+                                cudaStream_t st, bool pdl);
 // Routes only (any number of rows): route_e / route_w [row][topk], the same
 // arithmetic as moe_route's per-row routing.
 cudaError_t moe_route_rows_launch(const float* logits, int ld, int rows, int E, int topk, int norm_topk,

@@ -85,7 +85,10 @@ struct Ctx {
   // GEMV ring slots per launch:
   // 1 MoE combine into the next RMSNorm, 2 gated norm + Q8_0 into the
   // DeltaNet kernel, 4 SwiGLU into the down GEMV, 8 RMSNorm + Q8_K into the
-  // f32 router, 16 output-projection quantization into the attention combine.
+  // f32 router, 16 output-projection quantization into the attention combine,
+  // 64 the f32 router and the routing kernel in one launch (off by default:
+  // 1% slower at k = 4 -- the routing then waits for the slowest router CTA,
+  // where as its own launch it overlaps the router's tail).
   int fuse;
   Ctx(iq_state* s_) : s(s_), m(s_->m), c(s_->m->cfg), st(s_->st), pdl(!s_->profiling && !getenv("IQ_NO_PDL")) {
     const char* f = getenv("IQ_FUSE");
@@ -292,6 +295,8 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   const bool q8k = needs(W.gate.dt, false) || needs(W.sh_gate.dt, false) || needs(W.router.dt, false);
   const bool q80 = needs(W.gate.dt, true) || needs(W.sh_gate.dt, true) || needs(W.router.dt, true);
   float* lg = s->logits_moe.as<float>();
+  bool fused_router = false;
+  const float* router_in = nullptr;
   if ((x.fuse & 8) && !W.router.present() && !q80 && !x.comb_pending && H % 256 == 0) {
     // f32 router: it normalizes the rows itself and writes their Q8_K form
     // for the expert matrices (one launch for norm, quantization and router)
@@ -312,6 +317,10 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
     ++x.s->launch_count;
     IQ_CUDA(f32_matvec(W.selector.p(), 1, H, rin, H, k, lg + E, E + 1, x.st, x.pdl, rnorm, c.rms_norm_eps));
     x.mark("moe.router");
+  } else if (x.fuse & 64) {
+    // F32 router fused with the routing kernel below (one launch)
+    fused_router = true;
+    router_in = rin;
   } else {
     ++x.s->launch_count;
     IQ_CUDA(f32_matvec(W.router_sel.p(), E + 1, H, rin, H, k, lg, E + 1, x.st, x.pdl, rnorm, c.rms_norm_eps));
@@ -390,7 +399,19 @@ int run_moe(Ctx& x, const Layer& L, const LayerRec& R, int k, int layer_index) {
   t.expert_lo = W.expert_lo;
   t.expert_hi = W.expert_hi;
   ++x.s->launch_count;
-  IQ_CUDA(moe_route_launch(a, t, x.st, x.pdl));
+  if (fused_router) {
+    RouterRouteArgs rr = {};
+    rr.w = W.router_sel.p();
+    rr.rows = E + 1;
+    rr.cols = H;
+    rr.x = router_in;
+    rr.ldx = H;
+    rr.y = lg;
+    rr.counter = cnt + 2;  // counts word 2: the fused router's finish counter
+    IQ_CUDA(router_route_launch(rr, a, t, x.st, x.pdl));
+  } else {
+    IQ_CUDA(moe_route_launch(a, t, x.st, x.pdl));
+  }
   x.mark("moe.route");
   // upper bounds on the dynamic job tables' tiles
   const int max_union = std::min(W.expert_hi - W.expert_lo, k * c.num_experts_per_tok);

@@ -8,6 +8,7 @@
 // row -> route order, multiply then add; shared expert times
 // sigmoid(x . selector) added after the routed sum).
 #include <cstddef>
+#include <mutex>
 #include "model_kernels.cuh"
 #include "devfns.cuh"
 
@@ -68,7 +69,8 @@ __device__ __forceinline__ void route_row_warp(const float* lg, int E, int topk,
 #pragma unroll
     for (int i = 0; i < kPerLane; i++) {
       const int e = lane + 32 * i;
-      p[i] = e < E ? lg[e] : -INFINITY;
+      // from L2 (the fused router's other CTAs wrote them during this launch)
+      p[i] = e < E ? __ldcg(lg + e) : -INFINITY;
       mx = fmaxf(mx, p[i]);
     }
 #pragma unroll
@@ -138,9 +140,7 @@ __global__ void __launch_bounds__(256) route_rows_kernel(const float* logits, in
 // [e*per, e*per+per), finds their rank in the ascending union with warp
 // ballots, and writes the gate, up and down jobs of its resident ones.
 template <int kPerLane>  // experts per lane: ceil(E / 32) rounded up to 8, 16 or 32
-__global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRouteStatic s) {
-  pdl_wait();
-  pdl_trigger();
+__device__ __forceinline__ void route_body(const MoeRouteArgs& a, const MoeRouteStatic& s) {
   __shared__ int sel_e[kMaxRows][16];
   __shared__ float sel_w[kMaxRows][16];
   __shared__ unsigned used[kMaxExperts / 32];
@@ -257,6 +257,82 @@ __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRoute
   }
 }
 
+template <int kPerLane>
+__global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a, MoeRouteStatic s) {
+  pdl_wait();
+  pdl_trigger();
+  route_body<kPerLane>(a, s);
+}
+
+// The F32 router and the routing in one launch: CTA b computes router rows
+// [8b, 8b+8) for the pass's rows with f32_matvec's arithmetic (lane l sums
+// the float4 at columns 4l + 128t in order of t with fused multiply-adds,
+// then the butterfly), and the last CTA to finish (device counter, reset by
+// that CTA) routes every row and writes the job tables as moe_route_kernel.
+template <int kPerLane>
+__global__ void __launch_bounds__(256) router_route_kernel(RouterRouteArgs r, MoeRouteArgs a, MoeRouteStatic s) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  const int c4 = r.cols / 4;
+  constexpr int kMaxPer = 32;  // float4 per lane: cols <= 4096
+  float4 wv[kMaxPer];
+  if (row < r.rows) {
+    const float4* wr = reinterpret_cast<const float4*>(r.w + (int64_t)row * r.cols);
+#pragma unroll
+    for (int j = 0; j < kMaxPer; j++)
+      if (lane + 32 * j < c4) wv[j] = __ldg(wr + lane + 32 * j);
+  }
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ float4 xs4[];  // [k][cols/4]
+  const int k = a.rows;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < k * c4; i += 256) {
+    const int rr = i / c4, c = i % c4;
+    xs4[i] = *reinterpret_cast<const float4*>(r.x + (int64_t)rr * r.ldx + 4 * c);
+  }
+  __syncthreads();
+  if (row < r.rows) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxPer; j++) {
+      if (lane + 32 * j >= c4) break;
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        if (i < k) {
+          const float4 xv = xs4[i * c4 + lane + 32 * j];
+          float t = acc[i];
+          t = fmaf(wv[j].x, xv.x, t);
+          t = fmaf(wv[j].y, xv.y, t);
+          t = fmaf(wv[j].z, xv.z, t);
+          t = fmaf(wv[j].w, xv.w, t);
+          acc[i] = t;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      if (i >= k) break;
+      float v = acc[i];
+#pragma unroll
+      for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+      if (lane == 0) r.y[(int64_t)i * a.logits_ld + row] = v;
+    }
+  }
+  // the last CTA to finish routes (every CTA's logits are visible to it)
+  __threadfence();
+  __syncthreads();
+  __shared__ int is_last;
+  if (threadIdx.x == 0) is_last = atomicAdd(r.counter, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  if (threadIdx.x == 0) *r.counter = 0;  // ready for the next launch
+  route_body<kPerLane>(a, s);
+}
+
 // One CTA per slot: silu(gate) * up (candle's elementwise silu,
 // g / (1 + exp(-g))), quantized for the down projection.
 template <int MAXB>
@@ -339,6 +415,30 @@ cudaError_t moe_route_launch(const MoeRouteArgs& a, const MoeRouteStatic& s, cud
   if (a.experts <= 256) return launch_pdl(moe_route_kernel<8>, dim3(1), dim3(256), 0, st, pdl, a, s);
   if (a.experts <= 512) return launch_pdl(moe_route_kernel<16>, dim3(1), dim3(256), 0, st, pdl, a, s);
   return launch_pdl(moe_route_kernel<32>, dim3(1), dim3(256), 0, st, pdl, a, s);
+}
+
+template <int kPerLane>
+cudaError_t launch_router_route(const RouterRouteArgs& r, const MoeRouteArgs& a, const MoeRouteStatic& s,
+                                cudaStream_t st, bool pdl) {
+  static std::mutex mu;
+  static bool done[64] = {};
+  const cudaError_t e = once_per_device(done, mu, [] {
+    return cudaFuncSetAttribute(router_route_kernel<kPerLane>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                8 * 4096 * 4);
+  });
+  if (e != cudaSuccess) return e;
+  return launch_pdl(router_route_kernel<kPerLane>, dim3((unsigned)ceil_div(r.rows, 8)), dim3(256),
+                    (size_t)a.rows * r.cols * sizeof(float), st, pdl, r, a, s);
+}
+
+cudaError_t router_route_launch(const RouterRouteArgs& r, const MoeRouteArgs& a, const MoeRouteStatic& s,
+                                cudaStream_t st, bool pdl) {
+  if (a.rows > kMaxRows || a.rows > 8 || a.experts > kMaxExperts || a.topk > 16 || r.cols % 4 || r.cols > 4096 ||
+      r.y != a.logits || !r.counter)
+    return cudaErrorInvalidValue;
+  if (a.experts <= 256) return launch_router_route<8>(r, a, s, st, pdl);
+  if (a.experts <= 512) return launch_router_route<16>(r, a, s, st, pdl);
+  return launch_router_route<32>(r, a, s, st, pdl);
 }
 
 cudaError_t moe_route_rows_launch(const float* logits, int ld, int rows, int E, int topk, int norm_topk,
