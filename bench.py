@@ -610,6 +610,9 @@ def main():
                    "verify_us": {k: v["verify_us"] for k, v in sweep.items()},
                    "verify_sweep": {"context": CTX, "drafts": "greedy continuation, 30% corrupted", **sweep},
                    "expert_union_mean_k4": float(union.mean()), "pass_bytes_k4": alg_bytes,
+                   "stage_us_k4": {name: round(v[1] / 3, 1) for name, v in sorted(prof.items(), key=lambda kv: -kv[1][1])},
+                   "stage_scope": "µs per k=4 verify pass per stage (CUDA events, stage profiler, PDL off); under "
+                                  "expert parallelism moe.exchange is the NCCL sum of the routed outputs",
                    "pass_roofline_k4": {"achieved_gbs": pass_gbs, "frac": pass_gbs / peak,
                                         "scope": "whole k=4 verify pass: algorithmic bytes / device-timed pass"},
                    "l2": "weights (23.6 GB) exceed L2; no flush needed",
