@@ -271,41 +271,32 @@ __global__ void __launch_bounds__(2 * DV) deltanet_kernel(DeltaNetArgs a) {
       const bool more = t + 1 < nb;
       const float4* k4 = reinterpret_cast<const float4*>(qk[t][1]);
       const float decay = more ? decay_s[t + 1] : 1.f;
+      // one instruction stream for both walkers (half the unrolled code):
+      // sv = S + k delta, S' = sv decay; the output walker sums
+      // (sv q) qscale, the prediction walker (S' n) * 1 -- multiplying by
+      // one is exact, so each sum is bitwise its own formula
+      const float4* w4 = reinterpret_cast<const float4*>(walker_o ? qk[t][0] : qk[more ? t + 1 : t][1]);
+      const float s2 = walker_o ? qscale : 1.f;
+      float acc = 0.f;
+#pragma unroll
+      for (int i4 = 0; i4 < DK / 4; i4++) {
+        const float4 kv = k4[i4], wv = w4[i4];
+        const float kk[4] = {kv.x, kv.y, kv.z, kv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const float sv = __fadd_rn(S[4 * i4 + e], __fmul_rn(kk[e], delta));
+          const float sn = __fmul_rn(sv, decay);
+          acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(walker_o ? sv : sn, ww[e]), s2));
+          S[4 * i4 + e] = sn;
+        }
+      }
       if (walker_o) {
-        const float4* q4 = reinterpret_cast<const float4*>(qk[t][0]);
-        float o = 0.f;
-#pragma unroll
-        for (int i4 = 0; i4 < DK / 4; i4++) {
-          const float4 kv = k4[i4], qv = q4[i4];
-          const float kk[4] = {kv.x, kv.y, kv.z, kv.w}, qq[4] = {qv.x, qv.y, qv.z, qv.w};
-#pragma unroll
-          for (int e = 0; e < 4; e++) {
-            const float sv = __fadd_rn(S[4 * i4 + e], __fmul_rn(kk[e], delta));
-            o = __fadd_rn(o, __fmul_rn(__fmul_rn(sv, qq[e]), qscale));
-            S[4 * i4 + e] = __fmul_rn(sv, decay);
-          }
-        }
-        if (gated) os[t][j] = o;
-        else a.out[(int64_t)(b0 + t) * a.out_ld + col] = o;
-      } else {
-        const float4* n4 = reinterpret_cast<const float4*>(qk[more ? t + 1 : t][1]);
-        float pn = 0.f;
-#pragma unroll
-        for (int i4 = 0; i4 < DK / 4; i4++) {
-          const float4 kv = k4[i4], nv = n4[i4];
-          const float kk[4] = {kv.x, kv.y, kv.z, kv.w}, nn[4] = {nv.x, nv.y, nv.z, nv.w};
-#pragma unroll
-          for (int e = 0; e < 4; e++) {
-            const float sv = __fmul_rn(__fadd_rn(S[4 * i4 + e], __fmul_rn(kk[e], delta)), decay);
-            pn = __fadd_rn(pn, __fmul_rn(sv, nn[e]));
-            S[4 * i4 + e] = sv;
-          }
-        }
-        if (more) {
-          const float dn = __fmul_rn(__fsub_rn(vs[t + 1][j], pn), beta_s[t + 1]);
-          dsm[t + 1][j] = dn;
-          if (fin) rec_head[(int64_t)(t + 1) * rec_stride + DK + j] = dn;
-        }
+        if (gated) os[t][j] = acc;
+        else a.out[(int64_t)(b0 + t) * a.out_ld + col] = acc;
+      } else if (more) {
+        const float dn = __fmul_rn(__fsub_rn(vs[t + 1][j], acc), beta_s[t + 1]);
+        dsm[t + 1][j] = dn;
+        if (fin) rec_head[(int64_t)(t + 1) * rec_stride + DK + j] = dn;
       }
       __syncthreads();
     }
