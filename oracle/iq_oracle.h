@@ -53,6 +53,9 @@ int or_qmatvec(int dtype, const void* w, int64_t rows, int64_t cols,
  * (src/sampling.rs:104-112).  Returns -1 when nothing is finite. */
 int64_t or_argmax(const float* v, int64_t n);
 
+/* the wide pass's chunked DeltaNet recurrence over <= 32 rows of one head */
+int or_delta_chunk(const float* q, const float* k, const float* v, const float* beta, const float* lg, int C, int dk,
+                   int dv, float* S, float* o);
 #ifdef __cplusplus
 }
 #endif

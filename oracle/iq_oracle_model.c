@@ -570,6 +570,16 @@ static void delta_chunk(const float* q, const float* k, int ld_qk, const float* 
         }
     }
 }
+/* The chunked form over C <= 32 rows of one value head, exported for the
+ * tests that compare it with the sequential rule: q, k [C][dk] (normalized),
+ * v [C][dv], beta and log-decay [C]; S [dk][dv] advanced in place; o [C][dv]. */
+int or_delta_chunk(const float* q, const float* k, const float* v, const float* beta, const float* lg, int C, int dk,
+                   int dv, float* S, float* o) {
+    if (C < 1 || C > CHUNK || dk % 8 || dv > 128 || dv < 1) return -1;
+    delta_chunk(q, k, dk, v, dv, beta, lg, C, dk, dv, S, o, dv);
+    return 0;
+}
+
 static int chunk_supported(const or_config* c) {
     int nk = c->linear_num_key_heads, nv = c->linear_num_value_heads, dk = c->linear_key_head_dim;
     int dv = c->linear_value_head_dim, K = c->linear_conv_kernel_dim;

@@ -141,6 +141,22 @@ def delta_step(q, k, v, g, beta, heads: int, key_dim: int, value_dim: int, state
     return out, st
 
 
+def delta_chunk(q, k, v, beta, log_decay, state):
+    """The wide pass's chunked recurrence over C <= 32 rows of one value head
+    (the device's order): q, k [C][dk], v [C][dv], beta and log-decay [C],
+    state [dk][dv]; returns (outputs [C][dv], new state)."""
+    q, k, v, beta, lg = map(_f32, (q, k, v, beta, log_decay))
+    C, dk = q.shape
+    dv = v.shape[1]
+    st = _f32(state).copy()
+    out = np.empty((C, dv), np.float32)
+    lib().or_delta_chunk.argtypes = [P, P, P, P, P, I32, I32, I32, P, P]
+    rc = lib().or_delta_chunk(_p(q), _p(k), _p(v), _p(beta), _p(lg), C, dk, dv, _p(st), _p(out))
+    if rc:
+        raise ValueError(f"or_delta_chunk: unsupported shape ({C}, {dk}, {dv})")
+    return out, st
+
+
 def route(logits, topk: int, norm_topk: bool = True):
     """top_k_routes for one row: (experts, weights)."""
     lg = _f32(logits)
