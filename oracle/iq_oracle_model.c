@@ -16,7 +16,8 @@
  * Every projection goes through or_qmatvec in the reference lane order.
  * A multi-row pass of the reference equals its rows run one at a time
  * (per-row matmuls, serial recurrence, causal attention), so the oracle
- * evaluates one row per step.
+ * evaluates passes of up to 8 rows, one row per step inside each (order 2:
+ * the wide pass's 512-row chunks).
  */
 #include "iq_oracle.h"
 #include <math.h>
@@ -117,10 +118,13 @@ static const float* getvec(const or_tensor* t, int n, const char* name) {
     return x ? (const float*)x->data : NULL;
 }
 
-/* Accumulation order of every projection: 0 = the reference's AVX2 lane
- * order (default), 1 = the device's block-chunk order of the 8-row passes,
- * 2 = the device order of the wide prefill pass (diagnostics that isolate
- * f32-order effects from everything else). */
+/* Accumulation orders: 0 = the reference's (AVX2 lane order of every
+ * projection, sequential sums; the default), 1 = the device's 8-row passes
+ * (block-chunk GEMV order, the device's RMSNorm sum), 2 = the device's wide
+ * prefill pass (dense blocks in one chunk, experts split as on the device,
+ * the device's RMSNorm sum, and passes of up to 512 rows whose DeltaNet rows
+ * before the final block of 8 run in the chunked form, delta_chunk).  1 and 2
+ * isolate f32-order effects from everything else in the parity tests. */
 static int g_order = 0;
 void or_set_gemv_order(int order) { g_order = order; }
 
