@@ -605,8 +605,6 @@ static void delta_rows(const or_model* m, const layer_t* L, lstate_t* st, const 
     float* ba = (float*)malloc((size_t)R * 2 * nv * 4);
     float* tmp = (float*)malloc((size_t)R * nv * 4);
     float* cv = (float*)malloc((size_t)conv_dim * 4);
-    float* qr = (float*)malloc((size_t)nv * dk * 4);
-    float* kr = (float*)malloc((size_t)nv * dk * 4);
     float* g = (float*)malloc((size_t)R * vd * 4);
     matvec_k(&L->qkv, x, R, proj);
     matvec_k(&L->z, x, R, z);
@@ -621,27 +619,14 @@ static void delta_rows(const or_model* m, const layer_t* L, lstate_t* st, const 
      * the chunked form (delta_chunk), the final block row by row */
     const int pre = (g_order == 2 && R > 8 && chunk_supported(c)) ? R - ((R - 1) % 8 + 1) : 0;
     float* oall = (float*)malloc((size_t)R * vd * 4);
-    float *cq = NULL, *ck = NULL, *cvv = NULL, *cb = NULL, *cl = NULL;
-    if (pre > 0) {
-        cq = (float*)malloc((size_t)pre * nv * dk * 4);
-        ck = (float*)malloc((size_t)pre * nv * dk * 4);
-        cvv = (float*)malloc((size_t)pre * vd * 4);
-        cb = (float*)malloc((size_t)pre * nv * 4);
-        cl = (float*)malloc((size_t)pre * nv * 4);
-    }
+    /* per row in order: conv step, L2 norms, beta and log-decay; each value
+     * head's inputs collected (q/k repeated per value head) */
+    float* cq = (float*)malloc((size_t)R * nv * dk * 4);
+    float* ck = (float*)malloc((size_t)R * nv * dk * 4);
+    float* cvv = (float*)malloc((size_t)R * vd * 4);
+    float* cb = (float*)malloc((size_t)R * nv * 4);
+    float* cl = (float*)malloc((size_t)R * nv * 4);
     for (int r = 0; r < R; r++) {
-        if (r == pre && pre > 0) {
-            for (int vh = 0; vh < nv; vh++) {
-                float bh[CHUNK], lh[CHUNK];
-                for (int c0 = 0; c0 < pre; c0 += CHUNK) {
-                    int C = pre - c0 < CHUNK ? pre - c0 : CHUNK;
-                    for (int t = 0; t < C; t++) { bh[t] = cb[(c0 + t) * nv + vh]; lh[t] = cl[(c0 + t) * nv + vh]; }
-                    delta_chunk(cq + (int64_t)c0 * nv * dk + vh * dk, ck + (int64_t)c0 * nv * dk + vh * dk, nv * dk,
-                                cvv + (int64_t)c0 * vd + vh * dv, vd, bh, lh, C, dk, dv,
-                                st->rec + (int64_t)vh * dk * dv, oall + (int64_t)c0 * vd + vh * dv, vd);
-                }
-            }
-        }
         const float* bar = ba + (int64_t)r * 2 * nv;
         or_conv_step(proj + (int64_t)r * conv_dim, L->conv_w, conv_dim, K, st->conv, cv);
         float* q = cv; float* k = cv + kd; const float* v = cv + 2 * kd;
@@ -649,31 +634,44 @@ static void delta_rows(const or_model* m, const layer_t* L, lstate_t* st, const 
             or_l2_normalize(q + kh * dk, dk);
             or_l2_normalize(k + kh * dk, dk);
         }
-        float q_scale = 1.f / sqrtf((float)dk);
         for (int kh = 0; kh < nk; kh++)
             for (int rep = 0; rep < ratio; rep++) {
                 int vh = or_value_head(kh, rep, nk, ratio, c->value_heads_tiled);
-                memcpy(qr + vh * dk, q + kh * dk, (size_t)dk * 4);
-                memcpy(kr + vh * dk, k + kh * dk, (size_t)dk * 4);
                 float b, al;
                 if (L->ba_fused) { int base = kh * 2 * ratio; b = bar[base + rep]; al = bar[base + ratio + rep]; }
                 else { b = bar[vh]; al = bar[nv + vh]; }
-                float beta = sigmoid_ref(b);
-                float gdec = L->ssm_a[vh] * softplus_ref(al + L->dt_bias[vh]);
-                if (r < pre) {
-                    memcpy(cq + ((int64_t)r * nv + vh) * dk, q + kh * dk, (size_t)dk * 4);
-                    memcpy(ck + ((int64_t)r * nv + vh) * dk, k + kh * dk, (size_t)dk * 4);
-                    memcpy(cvv + (int64_t)r * vd + vh * dv, v + vh * dv, (size_t)dv * 4);
-                    cb[r * nv + vh] = beta;
-                    cl[r * nv + vh] = gdec;
-                } else {
-                    delta_head_step(qr + vh * dk, kr + vh * dk, v + vh * dv, gdec, beta, dk, dv, q_scale,
-                                    st->rec + (int64_t)vh * dk * dv, oall + (int64_t)r * vd + vh * dv);
-                }
+                memcpy(cq + ((int64_t)r * nv + vh) * dk, q + kh * dk, (size_t)dk * 4);
+                memcpy(ck + ((int64_t)r * nv + vh) * dk, k + kh * dk, (size_t)dk * 4);
+                memcpy(cvv + (int64_t)r * vd + vh * dv, v + vh * dv, (size_t)dv * 4);
+                cb[r * nv + vh] = sigmoid_ref(b);
+                cl[r * nv + vh] = L->ssm_a[vh] * softplus_ref(al + L->dt_bias[vh]);
             }
-        if (st->snap_conv && r + 1 < R) {  /* entry state of the next row */
+        if (st->snap_conv && r + 1 < R)  /* entry state of the next row */
             memcpy(st->snap_conv[r], st->conv, (size_t)conv_dim * (K - 1) * 4);
-            memcpy(st->snap_rec[r], st->rec, (size_t)nv * dk * dv * 4);
+    }
+    /* the prefix of a wide pass in the chunked form, head by head */
+    for (int vh = 0; vh < nv && pre > 0; vh++) {
+        float bh[CHUNK], lh[CHUNK];
+        for (int c0 = 0; c0 < pre; c0 += CHUNK) {
+            int C = pre - c0 < CHUNK ? pre - c0 : CHUNK;
+            for (int t = 0; t < C; t++) { bh[t] = cb[(c0 + t) * nv + vh]; lh[t] = cl[(c0 + t) * nv + vh]; }
+            delta_chunk(cq + (int64_t)c0 * nv * dk + vh * dk, ck + (int64_t)c0 * nv * dk + vh * dk, nv * dk,
+                        cvv + (int64_t)c0 * vd + vh * dv, vd, bh, lh, C, dk, dv,
+                        st->rec + (int64_t)vh * dk * dv, oall + (int64_t)c0 * vd + vh * dv, vd);
+        }
+    }
+    /* the remaining rows with the delta rule; the heads are independent, so
+     * they run in parallel, each walking its rows in order */
+    const float q_scale = 1.f / sqrtf((float)dk);
+#pragma omp parallel for schedule(static)
+    for (int vh = 0; vh < nv; vh++) {
+        float* S = st->rec + (int64_t)vh * dk * dv;
+        for (int r = pre; r < R; r++) {
+            delta_head_step(cq + ((int64_t)r * nv + vh) * dk, ck + ((int64_t)r * nv + vh) * dk,
+                            cvv + (int64_t)r * vd + vh * dv, cl[r * nv + vh], cb[r * nv + vh], dk, dv, q_scale, S,
+                            oall + (int64_t)r * vd + vh * dv);
+            if (st->snap_rec && r + 1 < R)  /* this head's part of the next row's entry state */
+                memcpy(st->snap_rec[r] + (int64_t)vh * dk * dv, S, (size_t)dk * dv * 4);
         }
     }
     for (int r = 0; r < R; r++) {
@@ -692,7 +690,7 @@ static void delta_rows(const or_model* m, const layer_t* L, lstate_t* st, const 
     }
     free(oall); free(cq); free(ck); free(cvv); free(cb); free(cl);
     matvec_k(&L->out, g, R, out);
-    free(proj); free(z); free(ba); free(tmp); free(cv); free(qr); free(kr); free(g);
+    free(proj); free(z); free(ba); free(tmp); free(cv); free(g);
 }
 
 /* ----------------------------------------------------------- attention */
@@ -733,10 +731,14 @@ static void apply_rope(float* v, int64_t pos, int rd, double theta) {  /* :841-8
  * h / (nh / nkv).  q and gate of head h at qg + h*q_ld and + gate_off;
  * keys/values [positions][nkv][hd]; res [nh][hd]. */
 static void attend_row(const float* qg, int q_ld, int gate_off, const float* keys, const float* values, int nh, int nkv,
-                       int hd, int64_t positions, float* scores, float* res) {
+                       int hd, int64_t positions, float* scores_all, float* res) {
+    /* scores_all: nh rows of `positions` floats (one per head: the heads are
+     * independent and run in parallel, each in its own order) */
     const int G = nh / nkv;
     float scale = 1.f / sqrtf((float)hd);
+#pragma omp parallel for schedule(static)
     for (int h = 0; h < nh; h++) {
+        float* scores = scores_all + (int64_t)h * positions;
         const float* q = qg + (int64_t)h * q_ld;
         const float* gate = q + gate_off;
         int kvh = h / G;
@@ -765,7 +767,7 @@ void or_attend(const float* q, const float* gate, const float* keys, const float
                int64_t positions, float* out) {
     /* q and gate as [nh][hd] each: interleave into the layer's [q | gate] rows */
     float* qg = (float*)malloc((size_t)nh * 2 * hd * 4);
-    float* scores = (float*)malloc((size_t)(positions > 0 ? positions : 1) * 4);
+    float* scores = (float*)malloc((size_t)nh * (positions > 0 ? positions : 1) * 4);
     for (int h = 0; h < nh; h++) {
         memcpy(qg + (int64_t)h * 2 * hd, q + (int64_t)h * hd, (size_t)hd * 4);
         memcpy(qg + (int64_t)h * 2 * hd + hd, gate + (int64_t)h * hd, (size_t)hd * 4);
@@ -785,7 +787,7 @@ static void attn_rows(const or_model* m, const layer_t* L, lstate_t* st, int64_t
     float* kv = (float*)malloc((size_t)R * nkv * hd * 4);
     float* vv = (float*)malloc((size_t)R * nkv * hd * 4);
     float* res = (float*)malloc((size_t)R * nh * hd * 4);
-    float* scores = (float*)malloc((size_t)(pos + R) * 4);
+    float* scores = (float*)malloc((size_t)nh * (pos + R) * 4);
     matvec_k(&L->q, x, R, qg);
     matvec_k(&L->k, x, R, kv);
     matvec_k(&L->v, x, R, vv);
@@ -863,21 +865,39 @@ static void moe_rows(const or_model* m, const layer_t* L, const float* x, int R,
             if (experts_out) experts_out[r * topk + q] = rank[q];
         }
     }
-    for (int e = 0; e < E; e++) {
-        int n = 0;
-        for (int r = 0; r < R; r++)
-            for (int q = 0; q < topk; q++)
-                if (route_e[r * topk + q] == e) {
-                    memcpy(xs + (int64_t)n * H, x + (int64_t)r * H, (size_t)H * 4);
-                    slot_of[n++] = r * topk + q;
-                }
-        if (!n) continue;
-        matvec_nk(&L->gate, L->gate.p + (int64_t)e * F * or_row_bytes(L->gate.dt, L->gate.cols), F, xs, n, g, 1);
-        matvec_nk(&L->up, L->up.p + (int64_t)e * F * or_row_bytes(L->up.dt, L->up.cols), F, xs, n, u, 1);
-        for (int i = 0; i < n * F; i++) g[i] = (g[i] / (1.f + expf(-g[i]))) * u[i];
-        matvec_nk(&L->down, L->down.p + (int64_t)e * H * or_row_bytes(L->down.dt, L->down.cols), H, g, n, y, 1);
-        for (int i = 0; i < n; i++) memcpy(yslot + (int64_t)slot_of[i] * H, y + (int64_t)i * H, (size_t)H * 4);
+    /* the union's experts, one thread per expert (each expert's arithmetic is
+     * the same whichever thread runs it; the products inside run serially) */
+    int* used = (int*)malloc((size_t)E * sizeof(int));
+    int nu = 0;
+    for (int e = 0; e < E; e++)
+        for (int i = 0; i < R * topk; i++)
+            if (route_e[i] == e) { used[nu++] = e; break; }
+#pragma omp parallel
+    {
+        float* txs = (float*)malloc((size_t)R * topk * H * 4);
+        float* tg = (float*)malloc((size_t)R * topk * FF * 4);
+        float* tu = (float*)malloc((size_t)R * topk * FF * 4);
+        float* ty = (float*)malloc((size_t)R * topk * H * 4);
+        int* tslot = (int*)malloc((size_t)R * topk * sizeof(int));
+#pragma omp for schedule(dynamic, 1)
+        for (int ui = 0; ui < nu; ui++) {
+            const int e = used[ui];
+            int n = 0;
+            for (int r = 0; r < R; r++)
+                for (int q = 0; q < topk; q++)
+                    if (route_e[r * topk + q] == e) {
+                        memcpy(txs + (int64_t)n * H, x + (int64_t)r * H, (size_t)H * 4);
+                        tslot[n++] = r * topk + q;
+                    }
+            matvec_nk(&L->gate, L->gate.p + (int64_t)e * F * or_row_bytes(L->gate.dt, L->gate.cols), F, txs, n, tg, 1);
+            matvec_nk(&L->up, L->up.p + (int64_t)e * F * or_row_bytes(L->up.dt, L->up.cols), F, txs, n, tu, 1);
+            for (int i = 0; i < n * F; i++) tg[i] = (tg[i] / (1.f + expf(-tg[i]))) * tu[i];
+            matvec_nk(&L->down, L->down.p + (int64_t)e * H * or_row_bytes(L->down.dt, L->down.cols), H, tg, n, ty, 1);
+            for (int i = 0; i < n; i++) memcpy(yslot + (int64_t)tslot[i] * H, ty + (int64_t)i * H, (size_t)H * 4);
+        }
+        free(txs); free(tg); free(tu); free(ty); free(tslot);
     }
+    free(used);
     for (int r = 0; r < R; r++) {
         float* o = out + (int64_t)r * H;
         for (int i = 0; i < H; i++) o[i] = 0.f;
