@@ -6,17 +6,20 @@
  * Bitwise equal to the scalar restatements in iq_oracle_dot.c (ref_q4k,
  * ref_q6k, ref_q80): the same exact integer sums per 32-bit lane n (bytes
  * 4n..4n+3 of every 32-byte chunk), one fused multiply-add per lane and
- * block, the same horizontal sums.  Like the reference's tiled kernels
+ * block, the same horizontal sums (Q5_K: the one-chunk block order of
+ * ref_q5k).  Like the reference's tiled kernels
  * (src/qgemm.rs:175-397, 399-438), a weight block is decoded once for up to
- * eight input rows.  Used only when the CPU has AVX2 and FMA.
+ * eight input rows.  Used only when the CPU has AVX2, FMA and F16C.
  */
 #include "iq_oracle.h"
 #include <immintrin.h>
+#include <math.h>
 #include <string.h>
 
-#define AVX2 __attribute__((target("avx2,fma")))
+#define AVX2 __attribute__((target("avx2,fma,f16c")))
 
-static inline float f16f(const uint8_t* p) { return or_f16_to_f32((uint16_t)(p[0] | (p[1] << 8))); }
+/* f16 -> f32 with the F16C instruction (exact: every f16 value is an f32) */
+static inline AVX2 float f16f(const uint8_t* p) { return _cvtsh_ss((unsigned short)(p[0] | (p[1] << 8))); }
 static inline float hsum8f(const float a[8]) {
     float r0 = a[4] + a[0], r1 = a[5] + a[1], r2 = a[6] + a[2], r3 = a[7] + a[3];
     return (r0 + r2) + (r1 + r3);
@@ -34,12 +37,13 @@ static void scales_mins(const uint8_t* s, uint8_t sc[8], uint8_t mn[8]) {
 
 int or_have_avx2(void) {
     __builtin_cpu_init();
-    return __builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma");
+    return __builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma") && __builtin_cpu_supports("f16c");
 }
 
 /* Q4_K row against T <= 8 Q8_K input rows (blocks of 292 bytes: f32 d,
  * i8 qs[256], i16 bsums[16]); out[t]. */
-AVX2 void or_q4k_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, int T, float* out) {
+static inline __attribute__((always_inline)) AVX2 void q4k_rows_t(const uint8_t* w, int nb,
+                                                                 const uint8_t* const* xs, const int T, float* out) {
     const __m256i m4 = _mm256_set1_epi8(0xF);
     __m256 acc[8];
     __m128 accm[8];
@@ -86,7 +90,8 @@ AVX2 void or_q4k_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, i
 }
 
 /* Q6_K row (blocks of 210 bytes: ql[128], qh[64], i8 scales[16], f16 d). */
-AVX2 void or_q6k_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, int T, float* out) {
+static inline __attribute__((always_inline)) AVX2 void q6k_rows_t(const uint8_t* w, int nb,
+                                                                 const uint8_t* const* xs, const int T, float* out) {
     const __m256i m4 = _mm256_set1_epi8(0xF), m2 = _mm256_set1_epi8(3), m32s = _mm256_set1_epi8(32);
     __m256 acc[8];
     for (int t = 0; t < T; t++) acc[t] = _mm256_setzero_ps();
@@ -138,7 +143,8 @@ AVX2 void or_q6k_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, i
 
 /* Q8_0 row against Q8_0 input rows (blocks of 34 bytes: f16 d, i8 qs[32]);
  * lane n = sum of the products of elements 4n..4n+3, exact in i32. */
-AVX2 void or_q80_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, int T, float* out) {
+static inline __attribute__((always_inline)) AVX2 void q80_rows_t(const uint8_t* w, int nb,
+                                                                 const uint8_t* const* xs, const int T, float* out) {
     const __m256i perm = _mm256_setr_epi32(0, 1, 4, 5, 2, 3, 6, 7);
     __m256 acc[8];
     for (int t = 0; t < T; t++) acc[t] = _mm256_setzero_ps();
@@ -163,3 +169,74 @@ AVX2 void or_q80_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, i
         out[t] = hsum8f(a);
     }
 }
+
+/* Q5_K row (blocks of 176 bytes: f16 d, f16 dmin, scales[12], qh[32],
+ * qs[128]) against T <= 8 Q8_K input rows: per block the exact integers
+ * isum = sum_s sc[s] (q_s . y_s) and msum = sum_s mn[s] (bsum_{2s} +
+ * bsum_{2s+1}), then acc = fma(y.d d, isum, acc), accm = fma(y.d dmin,
+ * msum, accm), result acc - accm: bitwise the scalar form (ref_q5k, one
+ * chunk of the block order). */
+static inline __attribute__((always_inline)) AVX2 void q5k_rows_t(const uint8_t* w, int nb,
+                                                                 const uint8_t* const* xs, const int T, float* out) {
+    const __m256i m4 = _mm256_set1_epi8(0xF), m1 = _mm256_set1_epi8(1), ones = _mm256_set1_epi16(1);
+    float acc[8], accm[8];
+    for (int t = 0; t < T; t++) { acc[t] = 0.f; accm[t] = 0.f; }
+    for (int b = 0; b < nb; b++) {
+        const uint8_t* blk = w + 176 * b;
+        uint8_t sc[8], mn[8];
+        scales_mins(blk + 4, sc, mn);
+        const float xd = f16f(blk), xdmin = f16f(blk + 2);
+        const __m256i qh = _mm256_loadu_si256((const __m256i*)(blk + 16));
+        __m256i q[8];  /* the 5-bit weights of sub-block s as bytes */
+        for (int j = 0; j < 4; j++) {
+            const __m256i q4 = _mm256_loadu_si256((const __m256i*)(blk + 48 + 32 * j));
+            const __m256i lo = _mm256_and_si256(q4, m4), hi = _mm256_and_si256(_mm256_srli_epi16(q4, 4), m4);
+            const __m256i hb0 = _mm256_and_si256(_mm256_srli_epi16(qh, 2 * j), m1);
+            const __m256i hb1 = _mm256_and_si256(_mm256_srli_epi16(qh, 2 * j + 1), m1);
+            q[2 * j] = _mm256_or_si256(lo, _mm256_slli_epi16(hb0, 4));
+            q[2 * j + 1] = _mm256_or_si256(hi, _mm256_slli_epi16(hb1, 4));
+        }
+        for (int t = 0; t < T; t++) {
+            const uint8_t* y = xs[t] + 292 * b;
+            __m256i isv = _mm256_setzero_si256();
+            for (int s = 0; s < 8; s++) {
+                const __m256i yv = _mm256_loadu_si256((const __m256i*)(y + 4 + 32 * s));
+                const __m256i p = _mm256_madd_epi16(_mm256_maddubs_epi16(q[s], yv), ones);
+                isv = _mm256_add_epi32(isv, _mm256_mullo_epi32(p, _mm256_set1_epi32(sc[s])));
+            }
+            int32_t lanes[8];
+            _mm256_storeu_si256((__m256i*)lanes, isv);
+            int32_t isum = 0;
+            for (int i = 0; i < 8; i++) isum += lanes[i];
+            int16_t bs[16];
+            memcpy(bs, y + 260, 32);
+            int32_t msum = 0;
+            for (int s2 = 0; s2 < 8; s2++) msum += mn[s2] * (bs[2 * s2] + bs[2 * s2 + 1]);
+            float yd;
+            memcpy(&yd, y, 4);
+            acc[t] = fmaf(yd * xd, (float)isum, acc[t]);
+            accm[t] = fmaf(yd * xdmin, (float)msum, accm[t]);
+        }
+    }
+    for (int t = 0; t < T; t++) out[t] = acc[t] - accm[t];
+}
+
+/* Exported forms: T (the input rows, 1..8) made a constant per instance, so
+ * the per-row accumulators stay in registers (same operations, same order). */
+#define IQ_ROWS_DISPATCH(name)                                                                 \
+    AVX2 void or_##name##_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, int T, float* out) { \
+        switch (T) {                                                                           \
+            case 1: name##_rows_t(w, nb, xs, 1, out); break;                                   \
+            case 2: name##_rows_t(w, nb, xs, 2, out); break;                                   \
+            case 3: name##_rows_t(w, nb, xs, 3, out); break;                                   \
+            case 4: name##_rows_t(w, nb, xs, 4, out); break;                                   \
+            case 5: name##_rows_t(w, nb, xs, 5, out); break;                                   \
+            case 6: name##_rows_t(w, nb, xs, 6, out); break;                                   \
+            case 7: name##_rows_t(w, nb, xs, 7, out); break;                                   \
+            default: name##_rows_t(w, nb, xs, 8, out); break;                                  \
+        }                                                                                      \
+    }
+IQ_ROWS_DISPATCH(q4k)
+IQ_ROWS_DISPATCH(q6k)
+IQ_ROWS_DISPATCH(q80)
+IQ_ROWS_DISPATCH(q5k)

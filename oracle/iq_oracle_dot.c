@@ -194,6 +194,7 @@ int or_have_avx2(void);
 void or_q4k_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, int T, float* out);
 void or_q6k_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, int T, float* out);
 void or_q80_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, int T, float* out);
+void or_q5k_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, int T, float* out);
 static int g_force_scalar = 0;
 void or_force_scalar(int on) { g_force_scalar = on; }
 
@@ -280,7 +281,8 @@ int or_qmatvec(int dtype, const void* wv, int64_t rows, int64_t cols,
      * up to eight input rows (bitwise the scalar forms below) */
     static int avx2 = -1;
     if (avx2 < 0) avx2 = or_have_avx2();
-    if (order == 0 && avx2 && !g_force_scalar && (dtype == OR_Q4_K || dtype == OR_Q6_K || dtype == OR_Q8_0)) {
+    if (order == 0 && avx2 && !g_force_scalar &&
+        (dtype == OR_Q4_K || dtype == OR_Q5_K || dtype == OR_Q6_K || dtype == OR_Q8_0)) {
         #pragma omp parallel for schedule(static)
         for (int64_t r = 0; r < rows; r++) {
             const uint8_t* wr = w + r * rb;
@@ -291,6 +293,7 @@ int or_qmatvec(int dtype, const void* wv, int64_t rows, int64_t cols,
                 for (int t = 0; t < T; t++) xs[t] = xq + (i0 + t) * xbytes;
                 if (dtype == OR_Q4_K) or_q4k_rows_avx2(wr, nb, xs, T, o);
                 else if (dtype == OR_Q6_K) or_q6k_rows_avx2(wr, nb, xs, T, o);
+                else if (dtype == OR_Q5_K) or_q5k_rows_avx2(wr, nb, xs, T, o);
                 else or_q80_rows_avx2(wr, nb, xs, T, o);
                 for (int t = 0; t < T; t++) y[(i0 + t) * rows + r] = o[t];
             }

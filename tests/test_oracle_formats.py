@@ -68,7 +68,7 @@ def test_argmax_takes_the_last_max_and_skips_non_finite():
     assert oracle.argmax(np.array([np.nan], np.float32)) == -1
 
 
-@pytest.mark.parametrize("dtype", [12, 14, 8])
+@pytest.mark.parametrize("dtype", [12, 13, 14, 8])
 def test_avx2_reference_order_equals_the_scalar_restatement(dtype):
     """The oracle's AVX2 reference-order kernels (the CPU baseline's fast
     path) are bitwise its scalar restatement of src/qgemm.rs, for 1..11
