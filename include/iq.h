@@ -95,11 +95,12 @@ int iq_matrix_forward_device_noalloc(const iq_matrix* m, const float* x, int inp
 /* Wide form for many input rows at once, device buffers, enqueued on
  * `stream`.  The reference runs prefill through QuantizedMatrix::forward in
  * 512-row passes (src/runtime.rs:748-771, src/gguf.rs:406-456); this is that
- * call for Q8_0, Q4_K and Q6_K matrices on the tensor cores (other dtypes:
+ * call for Q8_0, Q4_K and Q6_K matrices on the tensor cores, and for Q5_K
+ * when the environment variable IQ_WIDE_Q5K is set (other dtypes:
  * IQ_EUNSUPPORTED); 1 <= input_rows <= 65535; y[i*rows + r] as above.
  * Arithmetic: input rows quantized as in iq_matrix_forward_device (Q8_0,
  * or Q8_K for the K-quants), exact integer block dots, one f32 FMA per
- * block (and per block min term for Q4_K) in ascending block order -- bitwise the
+ * block (and per block min term for Q4_K/Q5_K) in ascending block order -- bitwise the
  * narrow path's result whenever iq_qgemv_ksplit() is 1 for the shape.
  * Scratch (about 2 B per input element and per matrix element) is held per
  * thread between calls. */

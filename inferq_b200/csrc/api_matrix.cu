@@ -199,8 +199,9 @@ int iq_matrix_forward_device(const iq_matrix* m, const float* x, int input_rows,
 int iq_matrix_forward_wide(const iq_matrix* m, const float* x, int input_rows, float* y, void* stream) {
   clear_error();
   IQ_CHECK(m && x && y, IQ_EINVAL, "iq_matrix_forward_wide: null argument");
-  IQ_CHECK(m->dtype == Q8_0 || m->dtype == Q4_K || m->dtype == Q6_K, IQ_EUNSUPPORTED,
-           "the wide product takes Q8_0, Q4_K or Q6_K matrices, got dtype %d", m->dtype);
+  IQ_CHECK(m->dtype == Q8_0 || m->dtype == Q4_K || m->dtype == Q6_K || (m->dtype == Q5_K && wide_q5k_enabled()),
+           IQ_EUNSUPPORTED, "the wide product takes Q8_0, Q4_K or Q6_K matrices (Q5_K with IQ_WIDE_Q5K), got dtype %d",
+           m->dtype);
   IQ_CHECK(input_rows >= 1 && input_rows <= 65535, IQ_EINVAL, "expected 1..65535 input rows, got %d", input_rows);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (m->dtype == Q6_K) {
@@ -212,13 +213,14 @@ int iq_matrix_forward_wide(const iq_matrix* m, const float* x, int input_rows, f
                              sc, st));
     return IQ_OK;
   }
-  if (m->dtype == Q4_K) {
-    const size_t need = wide_q4k_scratch_bytes(m->rows, m->cols, input_rows, nullptr, nullptr);
+  if (m->dtype == Q4_K || m->dtype == Q5_K) {
+    const bool q5 = m->dtype == Q5_K;
+    const size_t need = wide_q4k_scratch_bytes(m->rows, m->cols, input_rows, nullptr, nullptr, q5);
     IQ_CUDA(scratch().wide_w.reserve(need));
     WideQ4kScratch sc;
-    wide_q4k_scratch_bytes(m->rows, m->cols, input_rows, &sc, scratch().wide_w.as<uint8_t>());
-    IQ_CUDA(wide_q4k_forward(m->base, m->rows, m->cols, m->row_bytes, x, (int)m->cols, input_rows, y, (int)m->rows,
-                             sc, st));
+    wide_q4k_scratch_bytes(m->rows, m->cols, input_rows, &sc, scratch().wide_w.as<uint8_t>(), q5);
+    IQ_CUDA((q5 ? wide_q5k_forward : wide_q4k_forward)(m->base, m->rows, m->cols, m->row_bytes, x, (int)m->cols,
+                                                       input_rows, y, (int)m->rows, sc, st));
     return IQ_OK;
   }
   IQ_CHECK(m->cols % 128 == 0, IQ_EINVAL, "the wide product needs cols %% 128 == 0, got %lld", (long long)m->cols);

@@ -57,16 +57,21 @@ cudaError_t bf16_matvec(const uint16_t* w, int rows, int cols, const float* x, i
 // wide_ldd(ntok) f32) and wx (rows x cols f16) are scratch.  cols % 128 == 0.
 int wide_ldd(int ntok);
 int* wide_timeout_flag();  // device flag: a wide-product wait gave up
-// Q4_K x Q8_K wide product (wide.cu); cols % 256 == 0.  Scratch carved from
-// one buffer by wide_q4k_scratch_bytes (base NULL: size only).
+// Q4_K / Q5_K x Q8_K wide product (wide.cu); cols % 256 == 0.  Scratch
+// carved from one buffer by wide_q4k_scratch_bytes (base NULL: size only;
+// q5: with the Q5_K centring tiles).
 struct WideQ4kScratch {
   __half* qx;
   float* dT;
   uint8_t* bm;
   __half* wx;
   uint8_t* am;
+  uint8_t* ac;  // Q5_K only
 };
-size_t wide_q4k_scratch_bytes(int64_t rows, int64_t cols, int ntok, WideQ4kScratch* sc, uint8_t* base);
+size_t wide_q4k_scratch_bytes(int64_t rows, int64_t cols, int ntok, WideQ4kScratch* sc, uint8_t* base,
+                              bool q5 = false);
+// The Q5_K wide product is enabled by the environment variable IQ_WIDE_Q5K.
+bool wide_q5k_enabled();
 // Q6_K x Q8_K wide product; cols % 256 == 0.
 struct WideQ6kScratch {
   __half* qx;
@@ -78,6 +83,8 @@ size_t wide_q6k_scratch_bytes(int64_t rows, int64_t cols, int ntok, WideQ6kScrat
 cudaError_t wide_q6k_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
                              int ldx, int ntok, float* y, int out_ld, const WideQ6kScratch& sc, cudaStream_t st);
 cudaError_t wide_q4k_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
+                             int ldx, int ntok, float* y, int out_ld, const WideQ4kScratch& sc, cudaStream_t st);
+cudaError_t wide_q5k_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
                              int ldx, int ntok, float* y, int out_ld, const WideQ4kScratch& sc, cudaStream_t st);
 cudaError_t wide_q80_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
                              int ldx, int ntok, float* y, int out_ld, __half* qx, float* dT, __half* wx,

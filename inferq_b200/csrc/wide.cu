@@ -432,6 +432,16 @@ constexpr int kQ4Stages = 2;
 constexpr int kQ4Side = 4, kQ4SideBytes = 2560, kQ4OffH = 256;  // input-row d (64 f32), then 16-B row headers
 constexpr int kQ4SmemBytes = kQ4Stages * kQ4StageBytes + kQ4Side * kQ4SideBytes + 1024;
 static_assert(kQ4StageBytes % 1024 == 0, "swizzled atoms stay 1024-byte aligned");
+// Q5_K, the same kernel: A = sc[s] * (q - 16), |.| <= 63 * 16, so each
+// half block stays below 128 * 1008 * 128 < 2^24 (exact), and one more
+// K=16 MMA forms the centring term c = sum_s sc[s] * bsum_s from
+// A_c = (sc[0..7], 64 * sc[0..7]) against the same B_m, exact below 2^22;
+// isum = a + b + 16 c, summed as integers.  The stage gains the 4 KB A_c
+// tile and TMEM holds four accumulators per block (two blocks: 512 columns).
+constexpr int kQ5OffAc = kQ4StageBytes, kQ5StageBytes = kQ4StageBytes + 4096;  // 106 KB
+constexpr int kQ5SmemBytes = kQ4Stages * kQ5StageBytes + kQ4Side * kQ4SideBytes + 1024;
+static_assert(kQ5StageBytes % 1024 == 0, "swizzled atoms stay 1024-byte aligned");
+static_assert(kQ5SmemBytes + 1024 <= 227 * 1024, "Q5_K stages and the 1 KB of static shared memory fit the opt-in");
 constexpr uint32_t kQ4Idesc = (1u << 4) | ((uint32_t)(kQ4Toks >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 
 __device__ __forceinline__ void mma_f16_n64(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
@@ -459,11 +469,16 @@ __host__ __device__ __forceinline__ int plain_off(int row, int half) {
   return (row >> 3) * 256 + half * 128 + (row & 7) * 16;
 }
 
+template <bool kQ5>
 __global__ void __launch_bounds__(kBoundThreads, 1)
     wide_q4k_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                     const __grid_constant__ CUtensorMap tm_d, const __grid_constant__ CUtensorMap tm_h,
-                    const uint8_t* __restrict__ am, const uint8_t* __restrict__ bm, int rows, int nb, int ntok,
-                    float* __restrict__ y, int out_ld, int* timeout_flag, int test_skip) {
+                    const uint8_t* __restrict__ am, const uint8_t* __restrict__ bm, const uint8_t* __restrict__ ac,
+                    int rows, int nb, int ntok, float* __restrict__ y, int out_ld, int* timeout_flag,
+                    int test_skip) {
+  constexpr int kStage = kQ5 ? kQ5StageBytes : kQ4StageBytes;
+  constexpr int kBlkBytes = kQ5 ? 176 : 144;        // device block bytes; its header starts it
+  constexpr uint32_t kBufCols = kQ5 ? 256u : 192u;  // TMEM columns per block buffer
   __shared__ __align__(8) uint64_t full_op[kQ4Stages], empty_op[kQ4Stages];
   __shared__ __align__(8) uint64_t full_side[kQ4Side], empty_side[kQ4Side];
   __shared__ __align__(8) uint64_t tfull[2], tempty[2], drained;
@@ -471,7 +486,7 @@ __global__ void __launch_bounds__(kBoundThreads, 1)
   __shared__ int abort_s;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (su32(smem_raw) & 1023)) & 1023);
-  uint8_t* side = smem + kQ4Stages * kQ4StageBytes;
+  uint8_t* side = smem + kQ4Stages * kStage;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tok0 = blockIdx.x * kQ4Toks, row0 = blockIdx.y * 128;
@@ -529,11 +544,28 @@ __global__ void __launch_bounds__(kBoundThreads, 1)
       }
       tc_after();
       uint32_t va[16], vb[16], vm[16];
-      tmem_ld16(lane_base + (uint32_t)(buf * 192), va);
-      tmem_ld16(lane_base + (uint32_t)(buf * 192 + 64), vb);
-      tmem_ld16(lane_base + (uint32_t)(buf * 192 + 128), vm);
-      tmem_wait16(va);
-      tmem_wait16(vb);
+      tmem_ld16(lane_base + buf * kBufCols, va);
+      tmem_ld16(lane_base + buf * kBufCols + 64u, vb);
+      if constexpr (kQ5) {
+        // isum = a + b + 16 c: exact integers (each below 2^24) summed as
+        // int32, then one rounding, as (float)isum in the block order
+        tmem_ld16(lane_base + buf * kBufCols + 192u, vm);
+        tmem_wait16(va);
+        tmem_wait16(vb);
+        tmem_wait16(vm);
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const int is = __float2int_rn(__uint_as_float(va[i])) + __float2int_rn(__uint_as_float(vb[i])) +
+                         16 * __float2int_rn(__uint_as_float(vm[i]));
+          va[i] = __float_as_uint(__int2float_rn(is));
+          vb[i] = 0u;  // +0.0f, so the sum below is isum itself
+        }
+      }
+      tmem_ld16(lane_base + buf * kBufCols + 128u, vm);
+      if constexpr (!kQ5) {
+        tmem_wait16(va);
+        tmem_wait16(vb);
+      }
       tmem_wait16(vm);
       tc_before();
       __syncwarp();
@@ -565,12 +597,13 @@ __global__ void __launch_bounds__(kBoundThreads, 1)
     // ------------------------------------------------------ TMA producer
     const uint8_t* am_tile = am + (int64_t)blockIdx.y * nb * 4096;
     const uint8_t* bm_tile = bm + (int64_t)blockIdx.x * nb * 2048;
+    const uint8_t* ac_tile = kQ5 ? ac + (int64_t)blockIdx.y * nb * 4096 : nullptr;
     int issued = 0;
     for (int it = 0; it < nb && !*abort_v; it++) {
       const int s = it % kQ4Stages, e = it % kQ4Side;
       if (it >= kQ4Stages && !bar_wait(&empty_op[s], ((it / kQ4Stages) + 1) & 1, lim)) { give_up(); break; }
-      uint8_t* st = smem + s * kQ4StageBytes;
-      bar_expect(&full_op[s], kQ4StageBytes);
+      uint8_t* st = smem + s * kStage;
+      bar_expect(&full_op[s], kStage);
 #pragma unroll
       for (int a = 0; a < 4; a++) {
         tma2d(st + a * kQ4AtomA, &tm_w, it * 256 + 64 * a, row0, &full_op[s]);
@@ -578,6 +611,7 @@ __global__ void __launch_bounds__(kBoundThreads, 1)
       }
       bulk_load(st + kQ4OffAm, am_tile + (int64_t)it * 4096, 4096, &full_op[s]);
       bulk_load(st + kQ4OffBm, bm_tile + (int64_t)it * 2048, 2048, &full_op[s]);
+      if constexpr (kQ5) bulk_load(st + kQ5OffAc, ac_tile + (int64_t)it * 4096, 4096, &full_op[s]);
       if (it >= kQ4Side && !bar_wait(&empty_side[e], ((it / kQ4Side) + 1) & 1, lim)) {
         issued = it + 1;
         give_up();
@@ -586,7 +620,7 @@ __global__ void __launch_bounds__(kBoundThreads, 1)
       uint8_t* sd = side + e * kQ4SideBytes;
       bar_expect(&full_side[e], kQ4OffH + 2048);
       tma2d(sd, &tm_d, tok0, it, &full_side[e]);
-      tma2d(sd + kQ4OffH, &tm_h, it * 144, row0, &full_side[e]);
+      tma2d(sd + kQ4OffH, &tm_h, it * kBlkBytes, row0, &full_side[e]);
       issued = it + 1;
     }
     if (*abort_v) {
@@ -609,8 +643,8 @@ __global__ void __launch_bounds__(kBoundThreads, 1)
         break;
       }
       tc_after();
-      const uint32_t a0 = su32(smem + s * kQ4StageBytes), b0 = a0 + kQ4OffB;
-      const uint32_t d0 = tmem + (uint32_t)(buf * 192);
+      const uint32_t a0 = su32(smem + s * kStage), b0 = a0 + kQ4OffB;
+      const uint32_t d0 = tmem + buf * kBufCols;
 #pragma unroll
       for (int kk = 0; kk < 16; kk++) {  // K steps of 16: halves 0..127 -> a, 128..255 -> b
         const uint32_t off_a = (uint32_t)((kk >> 2) * kQ4AtomA + (kk & 3) * 32);
@@ -619,6 +653,7 @@ __global__ void __launch_bounds__(kBoundThreads, 1)
                     (uint32_t)((kk & 7) != 0));
       }
       mma_f16_n64(d0 + 128u, plain_desc(a0 + kQ4OffAm), plain_desc(a0 + kQ4OffBm), 0u);
+      if constexpr (kQ5) mma_f16_n64(d0 + 192u, plain_desc(a0 + kQ5OffAc), plain_desc(a0 + kQ4OffBm), 0u);
       mma_commit(&tfull[buf]);
       mma_commit(&empty_op[s]);
     }
@@ -705,16 +740,26 @@ __global__ void wide_act_q8k_kernel(const float* __restrict__ x, int ldx, int co
 // 32j + 16h + 4tig + e) -> A = sc[s] * q as f16 (row-major) and the min
 // operand tiles (per 128 rows and block, core-matrix order: mn[0..7],
 // 64 * mn[0..7]).  One thread per 16-byte quant chunk.
+// Q5_K rows (the header, then qh' with byte tig*8 + h*4 + e holding GGUF
+// qh[16h + 4tig + e], then the Q4_K quant bytes): element 64j + i (i < 32)
+// takes bit 2j of qh[i] as its fifth bit, element 64j + 32 + i bit 2j+1;
+// A = sc[s] * (q - 16), and the centring tiles ac (sc[0..7], 64 * sc[0..7])
+// in the layout of the min tiles.
+template <bool kQ5>
 __global__ void wide_expand_q4k_kernel(const uint8_t* __restrict__ w, int64_t w_row_bytes, int rows, int cols,
-                                       __half* __restrict__ out, uint8_t* __restrict__ am) {
+                                       __half* __restrict__ out, uint8_t* __restrict__ am,
+                                       uint8_t* __restrict__ ac) {
   const int64_t id = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int nb = cols / 256;
   const int64_t r = id / (nb * 8);
   if (r >= rows) return;
   const int b = (int)(id / 8 % nb), c = (int)(id & 7), tig = c >> 1;
-  const uint8_t* blk = w + r * w_row_bytes + (int64_t)b * 144;
+  const uint8_t* blk = w + r * w_row_bytes + (int64_t)b * (kQ5 ? 176 : 144);
   const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));
-  const uint4 v = __ldg(reinterpret_cast<const uint4*>(blk + 16 + c * 16));
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(blk + (kQ5 ? 48 : 16) + c * 16));
+  uint2 qh = make_uint2(0u, 0u);
+  if constexpr (kQ5) qh = __ldg(reinterpret_cast<const uint2*>(blk + 16 + tig * 8));
+  constexpr int kCentre = kQ5 ? 16 : 0;
   // six-bit scales and mins as bytes: sc0-3, sc4-7, mn0-3, mn4-7
   const uint32_t s_lo = hdr.y & 0x3F3F3F3Fu, m_lo = hdr.z & 0x3F3F3F3Fu;
   const uint32_t s_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
@@ -731,8 +776,17 @@ __global__ void wide_expand_q4k_kernel(const uint8_t* __restrict__ w, int64_t w_
 #pragma unroll
     for (int e = 0; e < 4; e += 2) {
       const int b0 = (int)((wd[qw] >> (8 * e)) & 0xFF), b1 = (int)((wd[qw] >> (8 * (e + 1))) & 0xFF);
-      lo[e / 2] = __halves2half2(__int2half_rn(sc_lo * (b0 & 15)), __int2half_rn(sc_lo * (b1 & 15)));
-      hi[e / 2] = __halves2half2(__int2half_rn(sc_hi * (b0 >> 4)), __int2half_rn(sc_hi * (b1 >> 4)));
+      int l0 = b0 & 15, l1 = b1 & 15, h0 = b0 >> 4, h1 = b1 >> 4;
+      if constexpr (kQ5) {
+        const uint32_t qw32 = h ? qh.y : qh.x;
+        const uint32_t q0 = qw32 >> (8 * e + 2 * j), q1 = qw32 >> (8 * (e + 1) + 2 * j);
+        l0 |= (int)(q0 & 1) << 4;
+        l1 |= (int)(q1 & 1) << 4;
+        h0 |= (int)((q0 >> 1) & 1) << 4;
+        h1 |= (int)((q1 >> 1) & 1) << 4;
+      }
+      lo[e / 2] = __halves2half2(__int2half_rn(sc_lo * (l0 - kCentre)), __int2half_rn(sc_lo * (l1 - kCentre)));
+      hi[e / 2] = __halves2half2(__int2half_rn(sc_hi * (h0 - kCentre)), __int2half_rn(sc_hi * (h1 - kCentre)));
     }
     *reinterpret_cast<uint2*>(out + r * cols + k) =
         make_uint2(*reinterpret_cast<uint32_t*>(&lo[0]), *reinterpret_cast<uint32_t*>(&lo[1]));
@@ -747,6 +801,15 @@ __global__ void wide_expand_q4k_kernel(const uint8_t* __restrict__ w, int64_t w_
       const int mn = (int)(((s < 4 ? m_lo : m_hi) >> (8 * (s & 3))) & 0xFF);
       tile[plain_off(rr, 0) / 2 + s] = __int2half_rn(mn);
       tile[plain_off(rr, 1) / 2 + s] = __int2half_rn(64 * mn);
+    }
+    if constexpr (kQ5) {
+      __half* ct = reinterpret_cast<__half*>(ac + ((r / 128) * nb + b) * 4096);
+#pragma unroll
+      for (int s = 0; s < 8; s++) {
+        const int sc = (int)(((s < 4 ? s_lo : s_hi) >> (8 * (s & 3))) & 0xFF);
+        ct[plain_off(rr, 0) / 2 + s] = __int2half_rn(sc);
+        ct[plain_off(rr, 1) / 2 + s] = __int2half_rn(64 * sc);
+      }
     }
   }
 }
@@ -1043,21 +1106,23 @@ cudaError_t wide_q80_forward(const uint8_t* w, int64_t rows, int64_t cols, int64
   return cudaGetLastError();
 }
 
-cudaError_t wide_q4k_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
-                             int ldx, int ntok, float* y, int out_ld, const WideQ4kScratch& sc, cudaStream_t st) {
+template <bool kQ5>
+cudaError_t wide_qk_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
+                            int ldx, int ntok, float* y, int out_ld, const WideQ4kScratch& sc, cudaStream_t st) {
   if (cols % 256 || ntok < 1 || ntok > 65535 || rows < 1 || rows > INT32_MAX || ((uintptr_t)w & 15) ||
-      w_row_bytes % 16)
+      w_row_bytes % 16 || (kQ5 && !sc.ac))
     return cudaErrorInvalidValue;
   const int nb = (int)(cols / 256), ldd = wide_ldd(ntok);
   const int ttiles = (ntok + kQ4Toks - 1) / kQ4Toks, rtiles = (int)((rows + 127) / 128);
   cudaError_t e = cudaMemsetAsync(sc.bm, 0, (size_t)ttiles * nb * 2048, st);
   if (e == cudaSuccess) e = cudaMemsetAsync(sc.am, 0, (size_t)rtiles * nb * 4096, st);
+  if (e == cudaSuccess && kQ5) e = cudaMemsetAsync(sc.ac, 0, (size_t)rtiles * nb * 4096, st);
   if (e != cudaSuccess) return e;
   wide_act_q8k_kernel<<<dim3((unsigned)((nb + 7) / 8), (unsigned)ntok), 256, 0, st>>>(x, ldx, (int)cols, sc.qx,
                                                                                        sc.dT, ldd, sc.bm);
   const int64_t chunks = rows * nb * 8;
-  wide_expand_q4k_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(w, w_row_bytes, (int)rows, (int)cols,
-                                                                           sc.wx, sc.am);
+  wide_expand_q4k_kernel<kQ5><<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(w, w_row_bytes, (int)rows,
+                                                                                (int)cols, sc.wx, sc.am, sc.ac);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   alignas(64) CUtensorMap mw, mx, md, mh;
@@ -1072,20 +1137,31 @@ cudaError_t wide_q4k_forward(const uint8_t* w, int64_t rows, int64_t cols, int64
     return cudaErrorInvalidValue;
   static bool attr[64] = {};  // the shared-memory opt-in is per device
   static std::mutex mu;
+  constexpr int kSmem = kQ5 ? kQ5SmemBytes : kQ4SmemBytes;
   e = once_per_device(attr, mu, [] {
-    return cudaFuncSetAttribute(wide_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kQ4SmemBytes);
+    return cudaFuncSetAttribute(wide_q4k_kernel<kQ5>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   });
   if (e != cudaSuccess) return e;
   int* flag = wide_timeout_flag();
   if (!flag) return cudaErrorInvalidDevice;
   static const int test_skip = getenv("IQ_WIDE_TEST_TIMEOUT") ? 1 : 0;
   const dim3 grid((unsigned)ttiles, (unsigned)rtiles);
-  wide_q4k_kernel<<<grid, kThreads, kQ4SmemBytes, st>>>(mw, mx, md, mh, sc.am, sc.bm, (int)rows, nb, ntok, y, out_ld,
-                                                        flag, test_skip);
+  wide_q4k_kernel<kQ5><<<grid, kThreads, kSmem, st>>>(mw, mx, md, mh, sc.am, sc.bm, sc.ac, (int)rows, nb, ntok, y,
+                                                       out_ld, flag, test_skip);
   return cudaGetLastError();
 }
 
-size_t wide_q4k_scratch_bytes(int64_t rows, int64_t cols, int ntok, WideQ4kScratch* sc, uint8_t* base) {
+cudaError_t wide_q4k_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
+                             int ldx, int ntok, float* y, int out_ld, const WideQ4kScratch& sc, cudaStream_t st) {
+  return wide_qk_forward<false>(w, rows, cols, w_row_bytes, x, ldx, ntok, y, out_ld, sc, st);
+}
+
+cudaError_t wide_q5k_forward(const uint8_t* w, int64_t rows, int64_t cols, int64_t w_row_bytes, const float* x,
+                             int ldx, int ntok, float* y, int out_ld, const WideQ4kScratch& sc, cudaStream_t st) {
+  return wide_qk_forward<true>(w, rows, cols, w_row_bytes, x, ldx, ntok, y, out_ld, sc, st);
+}
+
+size_t wide_q4k_scratch_bytes(int64_t rows, int64_t cols, int ntok, WideQ4kScratch* sc, uint8_t* base, bool q5) {
   const int nb = (int)(cols / 256);
   const int ttiles = (ntok + kQ4Toks - 1) / kQ4Toks, rtiles = (int)((rows + 127) / 128);
   size_t off = 0;
@@ -1099,14 +1175,24 @@ size_t wide_q4k_scratch_bytes(int64_t rows, int64_t cols, int ntok, WideQ4kScrat
   uint8_t* bm = take((size_t)ttiles * nb * 2048);
   uint8_t* wx = take((size_t)rows * cols * 2);
   uint8_t* am = take((size_t)rtiles * nb * 4096);
+  uint8_t* ac = q5 ? take((size_t)rtiles * nb * 4096) : nullptr;
   if (sc) {
     sc->qx = reinterpret_cast<__half*>(qx);
     sc->dT = reinterpret_cast<float*>(dT);
     sc->bm = bm;
     sc->wx = reinterpret_cast<__half*>(wx);
     sc->am = am;
+    sc->ac = ac;
   }
   return off;
+}
+
+// Q5_K takes the Q4_K kernel's instance with the centred operand; it is
+// off unless IQ_WIDE_Q5K is set, until its bitwise test has passed on a
+// B200 (tests/test_wide_gpu.py runs it under that variable).
+bool wide_q5k_enabled() {
+  static const bool on = getenv("IQ_WIDE_Q5K") != nullptr;
+  return on;
 }
 
 size_t wide_q6k_scratch_bytes(int64_t rows, int64_t cols, int ntok, WideQ6kScratch* sc, uint8_t* base) {

@@ -112,7 +112,7 @@ __global__ void wide_commit_kernel(int* ctrl, int rows, int last) {
 }
 
 
-bool wide_dtype(int dt) { return dt == Q8_0 || dt == Q4_K || dt == Q6_K; }
+bool wide_dtype(int dt) { return dt == Q8_0 || dt == Q4_K || dt == Q6_K || (dt == Q5_K && wide_q5k_enabled()); }
 
 // y[t*ldy + r] = row r of w (rows [0, w.rows)) . x[t*ldx ..] for n input rows
 int wide_project(iq_state* s, const Weight& w, const float* x, int ldx, int n, float* y, int ldy) {
@@ -126,11 +126,13 @@ int wide_project(iq_state* s, const Weight& w, const float* x, int ldx, int n, f
     uint8_t* b = sc.as<uint8_t>();
     IQ_CUDA(wide_q80_forward(w.p(), w.rows, w.cols, w.row_bytes, x, ldx, n, y, ldy, reinterpret_cast<__half*>(b),
                              reinterpret_cast<float*>(b + qx), reinterpret_cast<__half*>(b + qx + dT), st));
-  } else if (w.dt == Q4_K) {
-    IQ_CUDA(sc.reserve(wide_q4k_scratch_bytes(w.rows, w.cols, n, nullptr, nullptr)));
+  } else if (w.dt == Q4_K || w.dt == Q5_K) {
+    const bool q5 = w.dt == Q5_K;
+    IQ_CUDA(sc.reserve(wide_q4k_scratch_bytes(w.rows, w.cols, n, nullptr, nullptr, q5)));
     WideQ4kScratch k;
-    wide_q4k_scratch_bytes(w.rows, w.cols, n, &k, sc.as<uint8_t>());
-    IQ_CUDA(wide_q4k_forward(w.p(), w.rows, w.cols, w.row_bytes, x, ldx, n, y, ldy, k, st));
+    wide_q4k_scratch_bytes(w.rows, w.cols, n, &k, sc.as<uint8_t>(), q5);
+    IQ_CUDA((q5 ? wide_q5k_forward : wide_q4k_forward)(w.p(), w.rows, w.cols, w.row_bytes, x, ldx, n, y, ldy, k,
+                                                       st));
   } else if (w.dt == Q6_K) {
     IQ_CUDA(sc.reserve(wide_q6k_scratch_bytes(w.rows, w.cols, n, nullptr, nullptr)));
     WideQ6kScratch k;

@@ -7,6 +7,8 @@ to give the integer block dots of src/qgemm.rs:369-397 (Q8_0 x Q8_0).  Its f32
 order is one FMA per block in ascending block order: bitwise the oracle's
 device order with one K chunk (oracle/iq_oracle_dot.c dev_block_chunks).
 """
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -117,11 +119,64 @@ def test_wide_kquant_at_full_width_equals_rows_run_alone(cuda, dt):
         assert torch.equal(m.forward_wide(x[i:i + 1])[0].view(torch.int32), y[i].view(torch.int32)), i
 
 
+Q5K = pytest.mark.skipif(not os.environ.get("IQ_WIDE_Q5K"),
+                         reason="the Q5_K wide product is enabled by IQ_WIDE_Q5K")
+
+
+def _q5k_extreme(rows, q):
+    """Q5_K rows whose every scale is 63, every min 0, every quant q, d = 1."""
+    blk = np.zeros(176, np.uint8)
+    blk[0:2] = np.frombuffer(np.float16(1.0).tobytes(), np.uint8)
+    blk[4:8] = 0xFF            # sc0-3 = 63, top bits of sc4-7 = 3
+    blk[12:16] = 0x0F          # sc4-7 low nibbles 15, mins 0
+    blk[16:48] = 0xFF if q & 16 else 0
+    blk[48:176] = (q & 15) * 0x11
+    return np.tile(blk, rows * 2)  # two blocks per row (512 columns)
+
+
+@Q5K
+@pytest.mark.parametrize("rows,cols,n", [
+    (128, 256, 1), (200, 512, 37), (128, 1024, 64), (300, 256, 129), (1000, 2048, 300),
+])
+def test_wide_q5k_matches_the_oracle_bitwise(cuda, rows, cols, n):
+    """Q5_K x Q8_K: the centred operand sc*(q-16) in half-block
+    accumulators, the centring term 16*sum sc*bsum from one more MMA, the
+    integers summed exactly: bitwise the one-chunk order."""
+    g = torch.Generator().manual_seed(rows + 5 * n)
+    w = Q.encode(torch.randn(rows, cols, generator=g) * 0.02, Q.Q5_K).numpy()
+    x = _inputs(n, cols, n + 2)
+    m = _lib.Matrix(Q.Q5_K, w, rows, cols)
+    got = m.forward_wide(torch.from_numpy(x).cuda()).cpu().numpy()
+    ref = oracle.qmatvec(Q.Q5_K, w, rows, cols, x, order=1, ksplit=1)
+    bad = np.argwhere(got.view(np.uint32) != ref.view(np.uint32))
+    assert len(bad) == 0, (len(bad), bad[:5], np.abs(got - ref).max())
+
+
+@Q5K
+@pytest.mark.parametrize("q", [0, 31, 16])
+def test_wide_q5k_is_exact_at_its_magnitude_bound(cuda, q):
+    """Every scale 63 and inputs of one sign (every Q8_K quant -128): each
+    half-block accumulator reaches 128 * 63 * 16 * 128, just below 2^24, and
+    the centring term 16 * 8 * 63 * 4096 exceeds it (q = 0: the exact block
+    sum is 0, which any rounding inside the accumulation would miss)."""
+    rows, cols = 128, 512
+    w = _q5k_extreme(rows, q)
+    x = np.ones((3, cols), np.float32)
+    x[1] *= -1.0
+    m = _lib.Matrix(Q.Q5_K, w, rows, cols)
+    got = m.forward_wide(torch.from_numpy(x).cuda()).cpu().numpy()
+    ref = oracle.qmatvec(Q.Q5_K, w, rows, cols, x, order=1, ksplit=1)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (got[:, :2], ref[:, :2])
+    if q == 0:
+        assert not ref.any()
+
+
 def test_wide_rejects_what_it_does_not_support(cuda):
     w = Q.encode(torch.randn(64, 256) * 0.02, Q.Q5_K).numpy()
     m = _lib.Matrix(Q.Q5_K, w, 64, 256)
-    with pytest.raises(_lib.IqError):
-        m.forward_wide(torch.zeros(4, 256, device="cuda"))
+    if not os.environ.get("IQ_WIDE_Q5K"):
+        with pytest.raises(_lib.IqError):
+            m.forward_wide(torch.zeros(4, 256, device="cuda"))
     w8 = _weights(64, 128, 1)
     m8 = _lib.Matrix(Q.Q8_0, w8, 64, 128)
     with pytest.raises(_lib.IqError):  # no input rows

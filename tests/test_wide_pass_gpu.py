@@ -80,6 +80,8 @@ def _35b_widths_q80():
 
 
 CASES = {"tiny": synth.tiny, "mini_wide": _mini_wide, "mini_q80": _mini_q80, "35b_widths": _35b_widths_q80}
+if os.environ.get("IQ_WIDE_Q5K"):  # the Q4_K_M mix itself: its attn_output is Q5_K
+    CASES["mini_q4km"] = synth.mini_35b
 
 
 @pytest.fixture(scope="module", params=list(CASES))
