@@ -194,6 +194,9 @@ int iq_model_create_ep(const iq_tensor_view* tensors, int n, const iq_config* cf
                        const void* nccl_unique_id, iq_model** out);
 /* 128 bytes: an NCCL unique id for iq_model_create_ep. */
 int iq_nccl_unique_id(void* out);
+/* The experts [*lo, *hi) that iq_model_create_ep keeps on `rank` of
+ * `world` (host only; IQ_EINVAL when num_experts does not divide). */
+int iq_ep_expert_range(int64_t num_experts, int rank, int world, int32_t* lo, int32_t* hi);
 void iq_model_destroy(iq_model* m);
 int iq_model_weight_bytes(const iq_model* m, int64_t* bytes);
 

@@ -125,9 +125,7 @@ struct Loader {
 int load_moe(const Loader& L, const iq_config& c, const std::string& p, int rank, int world, MoeWeights& m) {
   const int64_t E = c.num_experts, H = c.hidden_size, F = c.moe_intermediate_size;
   const int64_t Fs = c.shared_expert_intermediate_size;
-  IQ_CHECK(E % world == 0, IQ_EINVAL, "%lld experts do not divide over %d ranks", (long long)E, world);
-  m.expert_lo = (int)(E / world * rank);
-  m.expert_hi = (int)(E / world * (rank + 1));
+  TRY(iq_ep_expert_range(E, rank, world, &m.expert_lo, &m.expert_hi));
   const std::string rn = p + ".ffn_gate_inp.weight";
   const iq_tensor_view* rv = L.find(rn);
   if (!rv) return L.missing(rn);
@@ -304,6 +302,18 @@ int iq_model_create(const iq_tensor_view* tensors, int n, const iq_config* cfg, 
 int iq_model_create_ep(const iq_tensor_view* tensors, int n, const iq_config* cfg, int rank, int world,
                        const void* nccl_unique_id, iq_model** out) {
   return create(tensors, n, cfg, rank, world, nccl_unique_id, out);
+}
+
+int iq_ep_expert_range(int64_t num_experts, int rank, int world, int32_t* lo, int32_t* hi) {
+  clear_error();
+  IQ_CHECK(lo && hi, IQ_EINVAL, "iq_ep_expert_range: null argument");
+  IQ_CHECK(world >= 1 && rank >= 0 && rank < world, IQ_EINVAL, "invalid rank %d of %d", rank, world);
+  IQ_CHECK(num_experts > 0 && num_experts <= INT32_MAX && num_experts % world == 0, IQ_EINVAL,
+           "%lld experts do not divide over %d ranks", (long long)num_experts, world);
+  const int64_t per = num_experts / world;
+  *lo = (int32_t)(per * rank);
+  *hi = (int32_t)(per * (rank + 1));
+  return IQ_OK;
 }
 
 int iq_nccl_unique_id(void* out) {

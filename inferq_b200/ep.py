@@ -17,13 +17,19 @@ from . import _lib
 
 
 def expert_range(num_experts: int, rank: int, world: int) -> tuple[int, int]:
-    """Experts [lo, hi) resident on `rank` of `world`."""
+    """Experts [lo, hi) resident on `rank` of `world`: the loader's own rule
+    (iq_ep_expert_range, host only)."""
     if world < 1 or not 0 <= rank < world:
         raise ValueError(f"invalid rank {rank} of {world}")
     if num_experts % world:
         raise ValueError(f"{num_experts} experts do not divide over {world} ranks")
-    per = num_experts // world
-    return rank * per, (rank + 1) * per
+    L = _lib.lib()
+    L.iq_ep_expert_range.restype = ctypes.c_int
+    L.iq_ep_expert_range.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                     ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]
+    lo, hi = ctypes.c_int32(), ctypes.c_int32()
+    _lib.check(L.iq_ep_expert_range(num_experts, rank, world, ctypes.byref(lo), ctypes.byref(hi)))
+    return lo.value, hi.value
 
 
 def unique_id() -> bytes:

@@ -1,6 +1,7 @@
 """Host logic of expert parallelism, on CPU with world_size-2 gloo groups.
 
-* the expert ranges partition [0, E) exactly as the loader does;
+* the loader's expert ranges (iq_ep_expert_range, which the loader itself
+  calls) partition [0, E) into equal contiguous ranges;
 * rank 0's NCCL unique id reaches every rank intact;
 * the exchange's exactness: routed slots that are nonzero on their owner
   only, summed over the ranks, equal the owner's values bit for bit (the
@@ -68,16 +69,27 @@ def _exchange(rank, world, seed):
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
-def test_expert_ranges_partition_the_experts(world):
-    E = 256
+@pytest.mark.parametrize("E", [256, 512])
+def test_expert_ranges_partition_the_experts(world, E):
     covered = []
     for r in range(world):
         lo, hi = ep.expert_range(E, r, world)
-        assert hi - lo == E // world
+        assert (lo, hi) == (r * E // world, (r + 1) * E // world)
         covered.extend(range(lo, hi))
     assert covered == list(range(E))
     with pytest.raises(ValueError):
         ep.expert_range(10, 0, 4)
+    with pytest.raises(ValueError):
+        ep.expert_range(E, world, world)
+
+
+def test_the_library_refuses_what_does_not_divide():
+    import ctypes
+    from inferq_b200 import _lib
+    L = _lib.lib()
+    lo, hi = ctypes.c_int32(), ctypes.c_int32()
+    for E, r, w in ((10, 0, 4), (256, 2, 2), (256, -1, 2), (0, 0, 1)):
+        assert L.iq_ep_expert_range(ctypes.c_int64(E), r, w, ctypes.byref(lo), ctypes.byref(hi)) != 0
 
 
 def test_unique_id_reaches_every_rank():
