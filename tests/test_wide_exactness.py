@@ -73,3 +73,37 @@ def test_q6k_scale_split_is_exact_and_recombines_once():
     ref = exact.astype(np.float32)
     fma = (16.0 * hi.astype(np.float64) + lo.astype(np.float64)).astype(np.float32)  # f64 holds it exactly
     assert np.array_equal(fma.view(np.uint32), ref.view(np.uint32))
+
+
+def test_q5k_centred_operand_and_centring_term_are_exact():
+    """Q5_K: sc * q (q <= 31) reaches 1953 and a half block would pass 2^24,
+    so the operand is centred, A = sc * (q - 16); the centring term
+    c = sum_s sc[s] * bsum_s comes from (sc, 64 sc) x (bsum mod 64,
+    bsum div 64) and isum = a + b + 16 c as exact int32."""
+    sc, q = np.meshgrid(np.arange(64), np.arange(32))
+    assert _f16_exact(sc * q) and 128 * 1953 * 128 >= F24   # why it is centred
+    assert _f16_exact(sc * (q - 16))
+    assert 128 * 63 * 16 * 128 < F24                        # each half block
+    s = np.arange(64)
+    assert _f16_exact(s) and _f16_exact(64 * s)
+    assert 8 * 63 * 63 + 8 * (64 * 63) * 64 < F24            # the c accumulator
+    assert 256 * 63 * 31 * 128 < 2 ** 31                     # isum fits int32
+    # the decomposition itself, on random and on extreme blocks
+    rng = np.random.default_rng(2)
+    for trial in range(200):
+        if trial < 4:
+            qv = np.full(256, (0, 31, 16, 15)[trial])
+            scv = np.full(8, 63)
+            x = np.full(256, -128)
+        else:
+            qv = rng.integers(0, 32, 256)
+            scv = rng.integers(0, 64, 8)
+            x = rng.integers(-128, 128, 256)
+        a_op = np.repeat(scv, 32) * (qv - 16)
+        a, b = int((a_op[:128] * x[:128]).sum()), int((a_op[128:] * x[128:]).sum())
+        assert abs(a) < F24 and abs(b) < F24
+        bsum = x.reshape(8, 32).sum(axis=1)
+        lo = bsum & 63
+        hi = (bsum - lo) // 64
+        c = int((scv * lo).sum() + (64 * scv * hi).sum())
+        assert a + b + 16 * c == int((np.repeat(scv, 32) * qv * x).sum())
