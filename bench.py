@@ -23,7 +23,10 @@ config     verify_us: one verification pass at k = 1, 2, 4, 8 (context 1024,
            wide prefill pass (iq_forward) on the 35B shapes with Q8_0
            weights, full 40 layers, 64 / 256 / 512 rows of seeded
            uniform-random token ids over a 2048-token context, tok/s on the
-           device and through the C ABI
+           device and through the C ABI; ngram_80b: the Qwen3-Next-80B /
+           Coder-Next shapes (48 layers, 512 experts top-10, Q4_K_M mix) on
+           one GPU, n-gram-speculative decode at context 4096 with verify
+           passes of up to 8 rows (--no-80b skips it)
 roofline   the quantized GEMV (the dominant kernel): its weight bytes over its
            event-timed launches, against the measured HBM copy bandwidth
 cpu_baseline  the same MTP rounds through the CPU restatement of the
@@ -73,6 +76,7 @@ def parse():
                     help="with N > 1: N independent sequences (weak scaling) instead of one sequence with the "
                          "experts split over the ranks (expert parallelism, the default)")
     ap.add_argument("--sweep-steps", type=int, default=8, help="timed passes per k of the verify sweep")
+    ap.add_argument("--no-80b", action="store_true", help="skip the 80B-shapes n-gram leg (config.ngram_80b)")
     return ap.parse_args()
 
 
@@ -415,6 +419,52 @@ def ngram_tiny(steps, warmup):
             "us_per_step": dev / steps * 1e6}
 
 
+def ngram_80b(steps, warmup, ctx=4096, k=8):
+    """The Qwen3-Next-80B / Coder-Next shapes (48 layers, 512 experts top-10,
+    vocabulary 151936, Q4_K_M mix, seeded random-init weights) on one GPU:
+    greedy n-gram-speculative decode at context 4096 with verify passes of
+    up to k=8 rows; the prompt is a seeded 64-token pattern repeated to 4096
+    tokens.  The emitted sequence is checked against plain greedy."""
+    import torch
+    from inferq_b200 import synth
+    from inferq_b200.model import Model, State
+    from inferq_b200.speculative import NgramLoop
+    cfg = synth.coder_next_80b()
+    t0 = time.perf_counter()
+    model = Model(cfg, synth.generate(cfg, seed=0, device="cuda"))
+    build_s = time.perf_counter() - t0
+    try:
+        pattern = np.random.default_rng(80).integers(0, cfg.vocab_size, 64)
+        prompt = np.tile(pattern, ctx // 64)
+        n = (steps + warmup) * k + 8
+        greedy, _ = greedy_continuation(model, prompt, n)
+        loop = NgramLoop(State(model, len(prompt) + n + 16), k=k)
+        emitted = [loop.prefill(prompt)]
+        for _ in range(warmup):
+            emitted += loop.step()
+        stream = torch.cuda.ExternalStream(loop.state.stream())
+        drafted = []
+
+        def step():
+            toks = loop.step()
+            drafted.append(loop.last["drafted"])
+            return toks
+
+        dev, host, r = _timed(stream, step, steps)
+        for toks in r:
+            emitted += toks
+        assert emitted == greedy[:len(emitted)], "n-gram speculative output diverged from greedy (80B shapes)"
+        com = sum(len(t) for t in r)
+        return {"workload": f"{cfg.name}, full {cfg.num_hidden_layers} layers, prompt = 64-token pattern "
+                            f"x{ctx // 64} (ctx {ctx}), ngram drafts, verify width <= {k}",
+                "weights_gb": model.weight_bytes() / 1e9, "model_build_s": build_s,
+                "tok_s": com / dev, "e2e_tok_s": com / host, "committed_per_step": com / steps,
+                "verify_rows_per_step": 1 + float(np.mean(drafted)), "us_per_step": dev / steps * 1e6}
+    finally:
+        del model
+        torch.cuda.empty_cache()
+
+
 def cpu_mtp_rounds(cfg, steps: int, warmup: int):
     """The same MTP round on the host cores through the CPU restatement of
     the reference (oracle/: the reference-order quantized dots with AVX2 and
@@ -552,7 +602,7 @@ def main():
         committed_all = committed
     # ---- verify sweep (context 1024) and the GEMV stage profile at k=4
     sweep, union, prof, pos = verify_sweep(model, cfg, args.sweep_steps, max(2, args.warmup), barrier)
-    ngram = wide = prefill = None
+    ngram = wide = prefill = big = None
     if not ep_mode or world == 1:
         if rank == 0:
             try:
@@ -567,6 +617,11 @@ def main():
                 prefill = wide_prefill(max(3, args.steps // 4), 3)
             except Exception as e:
                 prefill = {"failed": str(e)}
+            if not args.no_80b:
+                try:
+                    big = ngram_80b(max(5, args.steps // 4), 3)
+                except Exception as e:
+                    big = {"failed": str(e)}
     if rank != 0:
         return
     per_seq = 1 if ep_mode else world
@@ -618,7 +673,7 @@ def main():
                    "l2": "weights (23.6 GB) exceed L2; no flush needed",
                    "parallelism": f"ep{world} (experts split, NCCL sum of routed outputs per MoE layer)"
                    if ep_mode else f"replicas x{world}",
-                   "ngram": ngram, "wide": wide, "wide_prefill": prefill},
+                   "ngram": ngram, "wide": wide, "wide_prefill": prefill, "ngram_80b": big},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak if achieved else None, "traffic": traffic, "peak_kind": peak_kind,
                      "traffic_scope": "DRAM bytes of the pass's GEMV launches: the ncu ratio of a 4-layer capture "
