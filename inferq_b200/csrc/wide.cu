@@ -49,6 +49,7 @@
 #include "layout.cuh"
 #include "kernels.cuh"
 #include "qmv.cuh"
+#include "wide_expand.cuh"
 
 namespace iq {
 namespace {
@@ -464,10 +465,6 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                "l"(src), "r"(bytes), "r"(su32(b))
                : "memory");
 }
-// Byte offset of (row, K half) in a core-matrix tile of the min operands.
-__host__ __device__ __forceinline__ int plain_off(int row, int half) {
-  return (row >> 3) * 256 + half * 128 + (row & 7) * 16;
-}
 
 template <bool kQ5>
 __global__ void __launch_bounds__(kBoundThreads, 1)
@@ -735,16 +732,10 @@ __global__ void wide_act_q8k_kernel(const float* __restrict__ x, int ldx, int co
   }
 }
 
-// Device-layout Q4_K rows (16-byte header d, dmin, 12 scale bytes; then the
-// 128 quant bytes, byte tig*32 + j*8 + h*4 + e holding GGUF byte
-// 32j + 16h + 4tig + e) -> A = sc[s] * q as f16 (row-major) and the min
-// operand tiles (per 128 rows and block, core-matrix order: mn[0..7],
-// 64 * mn[0..7]).  One thread per 16-byte quant chunk.
-// Q5_K rows (the header, then qh' with byte tig*8 + h*4 + e holding GGUF
-// qh[16h + 4tig + e], then the Q4_K quant bytes): element 64j + i (i < 32)
-// takes bit 2j of qh[i] as its fifth bit, element 64j + 32 + i bit 2j+1;
-// A = sc[s] * (q - 16), and the centring tiles ac (sc[0..7], 64 * sc[0..7])
-// in the layout of the min tiles.
+// Device-layout Q4_K / Q5_K rows -> the f16 operand A (row-major) and the
+// min (and, Q5_K, centring) operand tiles per 128 rows and block: one
+// thread per 16-byte quant chunk, the arithmetic in expand_qk_chunk
+// (wide_expand.cuh).
 template <bool kQ5>
 __global__ void wide_expand_q4k_kernel(const uint8_t* __restrict__ w, int64_t w_row_bytes, int rows, int cols,
                                        __half* __restrict__ out, uint8_t* __restrict__ am,
@@ -759,59 +750,9 @@ __global__ void wide_expand_q4k_kernel(const uint8_t* __restrict__ w, int64_t w_
   const uint4 v = __ldg(reinterpret_cast<const uint4*>(blk + (kQ5 ? 48 : 16) + c * 16));
   uint2 qh = make_uint2(0u, 0u);
   if constexpr (kQ5) qh = __ldg(reinterpret_cast<const uint2*>(blk + 16 + tig * 8));
-  constexpr int kCentre = kQ5 ? 16 : 0;
-  // six-bit scales and mins as bytes: sc0-3, sc4-7, mn0-3, mn4-7
-  const uint32_t s_lo = hdr.y & 0x3F3F3F3Fu, m_lo = hdr.z & 0x3F3F3F3Fu;
-  const uint32_t s_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
-  const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
-  const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int qw = 0; qw < 4; qw++) {
-    const int j = 2 * (c & 1) + (qw >> 1), h = qw & 1;
-    const int slo = 2 * j, shi = 2 * j + 1;
-    const int sc_lo = (int)(((slo < 4 ? s_lo : s_hi) >> (8 * (slo & 3))) & 0xFF);
-    const int sc_hi = (int)(((shi < 4 ? s_lo : s_hi) >> (8 * (shi & 3))) & 0xFF);
-    const int k = b * 256 + 64 * j + 16 * h + 4 * tig;
-    __half2 lo[2], hi[2];
-#pragma unroll
-    for (int e = 0; e < 4; e += 2) {
-      const int b0 = (int)((wd[qw] >> (8 * e)) & 0xFF), b1 = (int)((wd[qw] >> (8 * (e + 1))) & 0xFF);
-      int l0 = b0 & 15, l1 = b1 & 15, h0 = b0 >> 4, h1 = b1 >> 4;
-      if constexpr (kQ5) {
-        const uint32_t qw32 = h ? qh.y : qh.x;
-        const uint32_t q0 = qw32 >> (8 * e + 2 * j), q1 = qw32 >> (8 * (e + 1) + 2 * j);
-        l0 |= (int)(q0 & 1) << 4;
-        l1 |= (int)(q1 & 1) << 4;
-        h0 |= (int)((q0 >> 1) & 1) << 4;
-        h1 |= (int)((q1 >> 1) & 1) << 4;
-      }
-      lo[e / 2] = __halves2half2(__int2half_rn(sc_lo * (l0 - kCentre)), __int2half_rn(sc_lo * (l1 - kCentre)));
-      hi[e / 2] = __halves2half2(__int2half_rn(sc_hi * (h0 - kCentre)), __int2half_rn(sc_hi * (h1 - kCentre)));
-    }
-    *reinterpret_cast<uint2*>(out + r * cols + k) =
-        make_uint2(*reinterpret_cast<uint32_t*>(&lo[0]), *reinterpret_cast<uint32_t*>(&lo[1]));
-    *reinterpret_cast<uint2*>(out + r * cols + k + 32) =
-        make_uint2(*reinterpret_cast<uint32_t*>(&hi[0]), *reinterpret_cast<uint32_t*>(&hi[1]));
-  }
-  if (c == 0) {
-    __half* tile = reinterpret_cast<__half*>(am + ((r / 128) * nb + b) * 4096);
-    const int rr = (int)(r % 128);
-#pragma unroll
-    for (int s = 0; s < 8; s++) {
-      const int mn = (int)(((s < 4 ? m_lo : m_hi) >> (8 * (s & 3))) & 0xFF);
-      tile[plain_off(rr, 0) / 2 + s] = __int2half_rn(mn);
-      tile[plain_off(rr, 1) / 2 + s] = __int2half_rn(64 * mn);
-    }
-    if constexpr (kQ5) {
-      __half* ct = reinterpret_cast<__half*>(ac + ((r / 128) * nb + b) * 4096);
-#pragma unroll
-      for (int s = 0; s < 8; s++) {
-        const int sc = (int)(((s < 4 ? s_lo : s_hi) >> (8 * (s & 3))) & 0xFF);
-        ct[plain_off(rr, 0) / 2 + s] = __int2half_rn(sc);
-        ct[plain_off(rr, 1) / 2 + s] = __int2half_rn(64 * sc);
-      }
-    }
-  }
+  const int64_t tile = ((r / 128) * nb + b) * 4096;
+  expand_qk_chunk<kQ5>(hdr, v, qh, c, b, out + r * cols, reinterpret_cast<__half*>(am + tile),
+                       kQ5 ? reinterpret_cast<__half*>(ac + tile) : nullptr, (int)(r % 128));
 }
 
 // ----------------------------------------------------------------- Q6_K
