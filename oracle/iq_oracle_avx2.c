@@ -240,3 +240,38 @@ IQ_ROWS_DISPATCH(q4k)
 IQ_ROWS_DISPATCH(q6k)
 IQ_ROWS_DISPATCH(q80)
 IQ_ROWS_DISPATCH(q5k)
+
+/* The attention scan's two inner loops (quantized_attention.rs:155-178 and
+ * the value sum after it) eight lanes at a time, bitwise the scalar forms:
+ * dot8 keeps its eight lane partials as one vector (products and sums
+ * rounded separately, as the scalar build does), and the value sum is an
+ * independent sequential sum per output element d, so eight d run side by
+ * side in the same position order. */
+AVX2 float or_dot8_avx2(const float* a, const float* b, int n) {
+    __m256 acc = _mm256_setzero_ps();
+    const int full = n / 8 * 8;
+    for (int i = 0; i < full; i += 8)
+        acc = _mm256_add_ps(acc, _mm256_mul_ps(_mm256_loadu_ps(a + i), _mm256_loadu_ps(b + i)));
+    float lanes[8];
+    _mm256_storeu_ps(lanes, acc);
+    float total = 0.f;
+    for (int i = full; i < n; i++) total += a[i] * b[i];
+    for (int l = 0; l < 8; l++) total += lanes[l];
+    return total;
+}
+
+/* o[d] (zeroed by the caller) += (scores[p] / den) * v[p * stride + d] for p
+ * in order; scores is overwritten with the probabilities.  One pass over the
+ * value rows, o staying in L1. */
+AVX2 void or_attend_values_avx2(float* o, float* scores, float den, const float* v, int64_t positions,
+                                int64_t stride, int hd) {
+    for (int64_t p = 0; p < positions; p++) scores[p] = scores[p] / den;
+    const int full = hd / 8 * 8;
+    for (int64_t p = 0; p < positions; p++) {
+        const __m256 pb = _mm256_set1_ps(scores[p]);
+        const float* row = v + p * stride;
+        for (int d = 0; d < full; d += 8)
+            _mm256_storeu_ps(o + d, _mm256_add_ps(_mm256_loadu_ps(o + d), _mm256_mul_ps(pb, _mm256_loadu_ps(row + d))));
+        for (int d = full; d < hd; d++) o[d] += scores[p] * row[d];
+    }
+}

@@ -197,6 +197,7 @@ void or_q80_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, int T,
 void or_q5k_rows_avx2(const uint8_t* w, int nb, const uint8_t* const* xs, int T, float* out);
 static int g_force_scalar = 0;
 void or_force_scalar(int on) { g_force_scalar = on; }
+int or_scalar_forced(void) { return g_force_scalar; }
 
 static int block_bytes(int dtype) {
     return dtype == OR_Q4_K ? 144 : dtype == OR_Q5_K ? 176 : dtype == OR_Q6_K ? 210 : 34;

@@ -730,12 +730,22 @@ static void apply_rope(float* v, int64_t pos, int rd, double theta) {  /* :841-8
  * in position order, output times sigmoid(gate).  Query head h reads KV head
  * h / (nh / nkv).  q and gate of head h at qg + h*q_ld and + gate_off;
  * keys/values [positions][nkv][hd]; res [nh][hd]. */
+int or_have_avx2(void);
+int or_scalar_forced(void);
+float or_dot8_avx2(const float* a, const float* b, int n);
+void or_attend_values_avx2(float* o, float* scores, float den, const float* v, int64_t positions, int64_t stride,
+                           int hd);
+
 static void attend_row(const float* qg, int q_ld, int gate_off, const float* keys, const float* values, int nh, int nkv,
                        int hd, int64_t positions, float* scores_all, float* res) {
     /* scores_all: nh rows of `positions` floats (one per head: the heads are
-     * independent and run in parallel, each in its own order) */
+     * independent and run in parallel, each in its own order).  The AVX2
+     * forms of the two inner loops give the same bits (iq_oracle_avx2.c). */
     const int G = nh / nkv;
     float scale = 1.f / sqrtf((float)hd);
+    static int avx2 = -1;
+    if (avx2 < 0) avx2 = or_have_avx2();
+    const int vec = avx2 && !or_scalar_forced();
 #pragma omp parallel for schedule(static)
     for (int h = 0; h < nh; h++) {
         float* scores = scores_all + (int64_t)h * positions;
@@ -744,17 +754,22 @@ static void attend_row(const float* qg, int q_ld, int gate_off, const float* key
         int kvh = h / G;
         float mx = -INFINITY;
         for (int64_t p = 0; p < positions; p++) {
-            scores[p] = dot8(q, keys + (p * nkv + kvh) * hd, hd) * scale;
+            const float* kr = keys + (p * nkv + kvh) * hd;
+            scores[p] = (vec ? or_dot8_avx2(q, kr, hd) : dot8(q, kr, hd)) * scale;
             if (scores[p] > mx) mx = scores[p];
         }
         float den = 0.f;
         for (int64_t p = 0; p < positions; p++) { scores[p] = expf(scores[p] - mx); den += scores[p]; }
         float* o = res + (int64_t)h * hd;
         for (int d = 0; d < hd; d++) o[d] = 0.f;
-        for (int64_t p = 0; p < positions; p++) {
-            float prob = scores[p] / den;
-            const float* vr = values + (p * nkv + kvh) * hd;
-            for (int d = 0; d < hd; d++) o[d] += prob * vr[d];
+        if (vec) {
+            or_attend_values_avx2(o, scores, den, values + (int64_t)kvh * hd, positions, (int64_t)nkv * hd, hd);
+        } else {
+            for (int64_t p = 0; p < positions; p++) {
+                float prob = scores[p] / den;
+                const float* vr = values + (p * nkv + kvh) * hd;
+                for (int d = 0; d < hd; d++) o[d] += prob * vr[d];
+            }
         }
         for (int d = 0; d < hd; d++) o[d] *= sigmoid_ref(gate[d]);
     }

@@ -88,3 +88,24 @@ def test_avx2_reference_order_equals_the_scalar_restatement(dtype):
         finally:
             oracle.force_scalar(False)
         assert np.array_equal(fast.view(np.uint32), slow.view(np.uint32)), k
+
+
+@pytest.mark.parametrize("nh,nkv,hd,positions", [(16, 2, 256, 700), (8, 2, 72, 33), (4, 4, 64, 1)])
+def test_avx2_attention_scan_equals_the_scalar_restatement(nh, nkv, hd, positions):
+    """The oracle's AVX2 attention loops (dot8's eight lanes as one vector,
+    the value sum eight output elements at a time) are bitwise its scalar
+    restatement of src/qwen/quantized_attention.rs:155-178."""
+    if not oracle.have_avx2():
+        pytest.skip("no AVX2 on this CPU")
+    rng = np.random.default_rng(positions)
+    q = rng.standard_normal((nh, hd)).astype(np.float32)
+    gate = rng.standard_normal((nh, hd)).astype(np.float32)
+    keys = (3 * rng.standard_normal((positions, nkv, hd))).astype(np.float32)
+    values = rng.standard_normal((positions, nkv, hd)).astype(np.float32)
+    fast = oracle.attend(q, gate, keys, values, nh, nkv, hd)
+    oracle.force_scalar(True)
+    try:
+        slow = oracle.attend(q, gate, keys, values, nh, nkv, hd)
+    finally:
+        oracle.force_scalar(False)
+    assert np.array_equal(fast.view(np.uint32), slow.view(np.uint32))
