@@ -86,7 +86,7 @@ struct iq_state {
   // the wide prefill pass's buffers (allocated on its first use)
   struct Wide {
     iq::DevBuf hidden, xn, big, z, ba, o, y, kp, vp, logits, tokens, ctrl, lg, re, rw, xg, actg, gu, yg, ysh, gush,
-        map, jobs, argres, scratch, qbuf, part, cv, bl, dno, wyx, wym, wyew;
+        map, jobs, argres, scratch, qbuf, part, cv, bl, dno, wyx, wym, wyew, yslot;
     int attn_rows = 8;  // rows per attention slice of the chunk
     int32_t* h_routes = nullptr;  // pinned [rows][topk]
     std::vector<iq::QmvJob> job_table;

@@ -24,6 +24,7 @@
 // Q4_K, Q6_K) and the experts are resident on one GPU (wide_capable).
 #include <algorithm>
 #include <cstring>
+#include <nccl.h>
 #include "state.h"
 
 namespace iq {
@@ -342,6 +343,13 @@ int wide_moe(iq_state* s, const Layer& L, int n) {
   IQ_CUDA(cudaGetLastError());
   TRY_IQ(wide_project(s, M.sh_down, W.o.as<float>(), Fs, n, W.ysh.as<float>(), H));
   IQ_CUDA(cudaStreamSynchronize(st));
+  // Expert parallelism: this rank runs only the slots of its own experts
+  // [e_lo, e_hi) (its expert tensors hold just those); after the down
+  // projection every slot's output goes to a dense [slot][H] buffer, zero on
+  // the ranks that do not own it, and one sum over the ranks leaves each slot
+  // its owner's value (x + 0 = x), so the ordered combine is the one-GPU one.
+  const bool ep = s->m->ep_world > 1;
+  const int e_lo = ep ? M.expert_lo : 0, e_hi = ep ? M.expert_hi : E;
   // groups of at most 8 rows per expert, experts ascending, rows in order;
   // gathered row g*8+i is member i of group g
   std::vector<std::vector<int>> by_e(E);
@@ -349,7 +357,7 @@ int wide_moe(iq_state* s, const Layer& L, int n) {
     for (int q = 0; q < topk; q++) {
       const int e = W.h_routes[r * topk + q];
       IQ_CHECK(e >= 0 && e < E, IQ_ESTATE, "wide pass: route %d of row %d names expert %d of %d", q, r, e, E);
-      by_e[e].push_back(r * topk + q);
+      if (e >= e_lo && e < e_hi) by_e[e].push_back(r * topk + q);
     }
   int groups = 0;
   for (int e = 0; e < E; e++) groups += (int)ceil_div((int64_t)by_e[e].size(), 8);
@@ -363,17 +371,18 @@ int wide_moe(iq_state* s, const Layer& L, int n) {
   IQ_CUDA(W.gu.reserve((size_t)ng_rows * gu_ld * 4));
   IQ_CUDA(W.yg.reserve((size_t)ng_rows * H * 4));
   IQ_CUDA(W.jobs.reserve((size_t)3 * groups * sizeof(QmvJob)));
-  IQ_CUDA(W.map.reserve(((size_t)n * topk + ng_rows) * 4));
+  IQ_CUDA(W.map.reserve(((size_t)n * topk * (ep ? 2 : 1) + ng_rows) * 4));
   std::vector<int> gather((size_t)ng_rows, -1);  // source row per gathered slot (-1 padding)
-  W.map_host.assign((size_t)n * topk, 0);
+  W.map_host.assign((size_t)n * topk, ep ? -1 : 0);  // (EP: -1 for the slots of other ranks' experts)
   const int ks_gate = qmv_ksplit(M.gate.dt, F, H, true), ks_down = qmv_ksplit(M.down.dt, H, F, true);
   const int tg = (int)ceil_div(F, qmv_rows_per_cta(ks_gate)), td = (int)ceil_div(H, qmv_rows_per_cta(ks_down));
   std::vector<QmvJob>& jt = W.job_table;
   jt.clear();
   std::vector<QmvJob> down;
   int gt = 0, dtiles = 0, g = 0;
-  for (int e = 0; e < E; e++) {
+  for (int e = e_lo; e < e_hi; e++) {
     const std::vector<int>& sl = by_e[e];
+    const int64_t el = e - e_lo;  // the expert's index in this rank's tensors
     for (size_t g0 = 0; g0 < sl.size(); g0 += 8, g++) {
       const int ng = (int)std::min<size_t>(8, sl.size() - g0);
       const int base = 8 * g;
@@ -398,15 +407,15 @@ int wide_moe(iq_state* s, const Layer& L, int n) {
         j.rowmap[i] = (uint8_t)(i < ng ? i : 0);
         j.outrow[i] = (int16_t)(base + i);
       }
-      j.row_base = e * F;
-      j.w = M.gate.p() + (int64_t)e * F * M.gate.row_bytes;
+      j.row_base = (int)(el * F);
+      j.w = M.gate.p() + el * F * M.gate.row_bytes;
       j.tmap = M.gate.tmap();
       j.tmap_tail = M.gate.tmap_tail();
       j.out = W.gu.as<float>();
       j.tile0 = gt;
       jt.push_back(j);
       gt += tg;
-      j.w = M.up.p() + (int64_t)e * F * M.up.row_bytes;
+      j.w = M.up.p() + el * F * M.up.row_bytes;
       j.tmap = M.up.tmap();
       j.tmap_tail = M.up.tmap_tail();
       j.out = W.gu.as<float>() + F;
@@ -432,8 +441,8 @@ int wide_moe(iq_state* s, const Layer& L, int n) {
         d.rowmap[i] = (uint8_t)(i < ng ? i : 0);
         d.outrow[i] = (int16_t)(base + i);
       }
-      d.row_base = e * H;
-      d.w = M.down.p() + (int64_t)e * H * M.down.row_bytes;
+      d.row_base = (int)(el * H);
+      d.w = M.down.p() + el * H * M.down.row_bytes;
       d.tmap = M.down.tmap();
       d.tmap_tail = M.down.tmap_tail();
       d.tile0 = dtiles;
@@ -445,25 +454,48 @@ int wide_moe(iq_state* s, const Layer& L, int n) {
   for (auto& d : down) jt.push_back(d);
   int* d_map = W.map.as<int>();
   int* d_gather = d_map + (size_t)n * topk;
-  IQ_CUDA(cudaMemcpyAsync(W.jobs.p, jt.data(), jt.size() * sizeof(QmvJob), cudaMemcpyHostToDevice, st));
+  if (!jt.empty())
+    IQ_CUDA(cudaMemcpyAsync(W.jobs.p, jt.data(), jt.size() * sizeof(QmvJob), cudaMemcpyHostToDevice, st));
   IQ_CUDA(cudaMemcpyAsync(d_map, W.map_host.data(), (size_t)n * topk * 4, cudaMemcpyHostToDevice, st));
-  IQ_CUDA(cudaMemcpyAsync(d_gather, gather.data(), gather.size() * 4, cudaMemcpyHostToDevice, st));
+  if (ng_rows > 0)
+    IQ_CUDA(cudaMemcpyAsync(d_gather, gather.data(), gather.size() * 4, cudaMemcpyHostToDevice, st));
   // (host vectors stay alive until the stream synchronizes at the end of the chunk)
-  gather_rows_kernel<<<ng_rows, 256, 0, st>>>(W.xn.as<float>(), d_gather, ng_rows, H, W.xg.as<float>());
-  IQ_CUDA(cudaGetLastError());
-  PrepArgs pa = {};
-  pa.x = W.xg.as<float>();
-  pa.ldx = H;
-  pa.cols = H;
-  pa.inv_cols = (float)(1.0 / (double)H);
-  if (q80) { pa.q80 = W.actg.as<uint8_t>(); pa.q80_stride = arb; }
-  else { pa.q8k = W.actg.as<uint8_t>(); pa.q8k_stride = arb; }
-  IQ_CUDA(prep_rows(pa, ng_rows, st, false));
-  IQ_CUDA(qmv_launch(W.jobs.as<QmvJob>(), njobs, nullptr, gt, 8 * arb, st, false));
-  const int mid = (int)std::max(act_row_bytes_q8k(F), act_row_bytes_q80(F));
-  IQ_CUDA(qmv_launch(W.jobs.as<QmvJob>() + njobs, (int)down.size(), nullptr, dtiles, 8 * mid, st, false));
+  if (ng_rows > 0) {  // (zero only under expert parallelism: none of this rank's experts routed)
+    gather_rows_kernel<<<ng_rows, 256, 0, st>>>(W.xn.as<float>(), d_gather, ng_rows, H, W.xg.as<float>());
+    IQ_CUDA(cudaGetLastError());
+    PrepArgs pa = {};
+    pa.x = W.xg.as<float>();
+    pa.ldx = H;
+    pa.cols = H;
+    pa.inv_cols = (float)(1.0 / (double)H);
+    if (q80) { pa.q80 = W.actg.as<uint8_t>(); pa.q80_stride = arb; }
+    else { pa.q8k = W.actg.as<uint8_t>(); pa.q8k_stride = arb; }
+    IQ_CUDA(prep_rows(pa, ng_rows, st, false));
+    IQ_CUDA(qmv_launch(W.jobs.as<QmvJob>(), njobs, nullptr, gt, 8 * arb, st, false));
+    const int mid = (int)std::max(act_row_bytes_q8k(F), act_row_bytes_q80(F));
+    IQ_CUDA(qmv_launch(W.jobs.as<QmvJob>() + njobs, (int)down.size(), nullptr, dtiles, 8 * mid, st, false));
+  }
+  const int* comb_map = d_map;
+  const float* comb_y = W.yg.as<float>();
+  if (ep) {
+    const int slots = n * topk;
+    IQ_CUDA(W.yslot.reserve((size_t)slots * H * 4));
+    // slot s <- gathered row map[s] (zero where another rank owns the expert)
+    gather_rows_kernel<<<slots, 256, 0, st>>>(W.yg.as<float>(), d_map, slots, H, W.yslot.as<float>());
+    IQ_CUDA(cudaGetLastError());
+    const ncclResult_t r = ncclAllReduce(W.yslot.p, W.yslot.p, (size_t)slots * H, ncclFloat, ncclSum,
+                                         static_cast<ncclComm_t>(s->m->nccl_comm), st);
+    IQ_CHECK(r == ncclSuccess, IQ_ECUDA, "wide pass expert exchange (ncclAllReduce): %s", ncclGetErrorString(r));
+    std::vector<int> ident((size_t)slots);
+    for (int i = 0; i < slots; i++) ident[i] = i;
+    int* d_ident = d_gather + ng_rows;
+    // (pageable source: the call returns once `ident` has been staged)
+    IQ_CUDA(cudaMemcpyAsync(d_ident, ident.data(), (size_t)slots * 4, cudaMemcpyHostToDevice, st));
+    comb_map = d_ident;
+    comb_y = W.yslot.as<float>();
+  }
   const dim3 grid((unsigned)ceil_div(H, 256), (unsigned)n);
-  wide_combine_kernel<<<grid, 256, 0, st>>>(W.hidden.as<float>(), H, topk, d_map, W.yg.as<float>(), W.rw.as<float>(),
+  wide_combine_kernel<<<grid, 256, 0, st>>>(W.hidden.as<float>(), H, topk, comb_map, comb_y, W.rw.as<float>(),
                                             W.ysh.as<float>(), lg, E + 1, E);
   IQ_CUDA(cudaGetLastError());
   return IQ_OK;
@@ -558,7 +590,10 @@ int wide_chunk(iq_state* s, const uint32_t* tokens, int n, float* logits, float*
 }  // namespace
 
 bool wide_capable(const iq_model* m) {
-  if (m->ep_world > 1) return false;
+  // under expert parallelism only with IQ_WIDE_EP set, until its two-GPU
+  // test has passed on hardware (tests/test_ep_gpu.py sets it)
+  static const bool wide_ep = getenv("IQ_WIDE_EP") != nullptr;
+  if (m->ep_world > 1 && !wide_ep) return false;
   const iq_config& c = m->cfg;
   if (c.num_hidden_layers < 1 || c.num_experts_per_tok > 16 || c.hidden_size % 256) return false;
   auto ok = [](const Weight& w) { return wide_dtype(w.dt); };
